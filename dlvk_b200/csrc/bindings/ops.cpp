@@ -1,0 +1,396 @@
+// PyTorch bindings of the dlvk_b200 kernels (module dlvk_b200._C).
+// Every op launches on the current CUDA stream of the tensors' device, takes
+// strided views where the kernel supports them, and allocates outputs through
+// PyTorch's caching allocator (so the ops are CUDA-graph capturable).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "dlvk/kernels.h"
+#include "bind_common.h"
+
+namespace dlvk {
+namespace bind {
+
+DType to_dtype(const at::Tensor& t) {
+  switch (t.scalar_type()) {
+    case at::kFloat: return DType::F32;
+    case at::kBFloat16: return DType::BF16;
+    case at::kHalf: return DType::F16;
+    case at::kInt: return DType::I32;
+    case at::kChar: return DType::I8;
+    case at::kByte: return DType::U8;
+    case at::kLong: return DType::I64;
+    default: TORCH_CHECK(false, "dlvk: unsupported dtype ", t.scalar_type());
+  }
+}
+
+void check_cuda(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), "dlvk: ", name, " must be a CUDA tensor (the native kernels run on the GPU only)");
+}
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+namespace {
+
+// ---- elementwise ----
+at::Tensor unary_op(const at::Tensor& x, int64_t op, double a, double b, c10::optional<at::Tensor> out,
+                    c10::optional<at::ScalarType> out_dtype) {
+  check_cuda(x, "x");
+  c10::cuda::CUDAGuard g(x.device());
+  auto xc = x.contiguous();
+  at::Tensor y = out.has_value() ? *out : at::empty_like(xc, xc.options().dtype(out_dtype.value_or(xc.scalar_type())));
+  TORCH_CHECK(y.is_contiguous() && y.numel() == xc.numel(), "dlvk.unary: bad out");
+  unary(to_dtype(xc), to_dtype(y), xc.data_ptr(), y.data_ptr(), xc.numel(), (int)op, (float)a, (float)b, stream());
+  return y;
+}
+
+at::Tensor binary_op(const at::Tensor& x, const at::Tensor& y, int64_t op, c10::optional<at::Tensor> out) {
+  check_cuda(x, "x");
+  check_cuda(y, "y");
+  TORCH_CHECK(x.sizes() == y.sizes(), "dlvk.binary: shape mismatch ", x.sizes(), " vs ", y.sizes());
+  TORCH_CHECK(x.scalar_type() == y.scalar_type(), "dlvk.binary: dtype mismatch");
+  c10::cuda::CUDAGuard g(x.device());
+  auto xc = x.contiguous(), yc = y.contiguous();
+  at::Tensor z = out.has_value() ? *out : at::empty_like(xc);
+  TORCH_CHECK(z.is_contiguous() && z.numel() == xc.numel(), "dlvk.binary: bad out");
+  binary(to_dtype(xc), xc.data_ptr(), yc.data_ptr(), z.data_ptr(), xc.numel(), (int)op, stream());
+  return z;
+}
+
+at::Tensor bias_act_op(const at::Tensor& x, c10::optional<at::Tensor> bias, int64_t act) {
+  check_cuda(x, "x");
+  c10::cuda::CUDAGuard g(x.device());
+  auto xc = x.contiguous();
+  const int64_t cols = xc.size(-1), rows = xc.numel() / std::max<int64_t>(cols, 1);
+  at::Tensor out = at::empty_like(xc);
+  const void* bp = nullptr;
+  DType bdt = DType::F32;
+  at::Tensor bc;
+  if (bias.has_value()) {
+    bc = bias->contiguous();
+    TORCH_CHECK(bc.numel() == cols, "dlvk.bias_act: bias size");
+    bp = bc.data_ptr();
+    bdt = to_dtype(bc);
+  }
+  bias_act(to_dtype(xc), bdt, xc.data_ptr(), bp, out.data_ptr(), rows, cols, (int)act, stream());
+  return out;
+}
+
+// ---- reductions ----
+at::Tensor reduce_op(const at::Tensor& x, int64_t op, double scale) {
+  check_cuda(x, "x");
+  c10::cuda::CUDAGuard g(x.device());
+  auto xc = x.contiguous();
+  auto out = at::empty({}, xc.options().dtype(at::kFloat));
+  auto scratch = at::empty({reduce_scratch_floats()}, xc.options().dtype(at::kFloat));
+  reduce(to_dtype(xc), xc.data_ptr(), xc.numel(), (int)op, (float)scale, out.data_ptr<float>(),
+         scratch.data_ptr<float>(), stream());
+  return out;
+}
+
+at::Tensor colsum_op(const at::Tensor& x, double scale, c10::optional<at::Tensor> out, bool accumulate,
+                     c10::optional<at::ScalarType> out_dtype) {
+  check_cuda(x, "x");
+  c10::cuda::CUDAGuard g(x.device());
+  auto xc = x.contiguous();
+  const int64_t cols = xc.size(-1), rows = xc.numel() / std::max<int64_t>(cols, 1);
+  at::Tensor o = out.has_value() ? *out : at::empty({cols}, xc.options().dtype(out_dtype.value_or(at::kFloat)));
+  TORCH_CHECK(o.is_contiguous() && o.numel() == cols, "dlvk.colsum: bad out");
+  colsum(to_dtype(xc), to_dtype(o), xc.data_ptr(), rows, cols, (float)scale, o.data_ptr(), accumulate, stream());
+  return o;
+}
+
+at::Tensor rowsum_op(const at::Tensor& x, double scale) {
+  check_cuda(x, "x");
+  c10::cuda::CUDAGuard g(x.device());
+  auto xc = x.contiguous();
+  const int64_t cols = xc.size(-1), rows = xc.numel() / std::max<int64_t>(cols, 1);
+  auto o = at::empty({rows}, xc.options().dtype(at::kFloat));
+  rowsum(to_dtype(xc), xc.data_ptr(), rows, cols, (float)scale, o.data_ptr<float>(), stream());
+  return o;
+}
+
+at::Tensor transpose_op(const at::Tensor& x) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.dim() == 2 || x.dim() == 3, "dlvk.transpose: 2-D or batched 2-D");
+  c10::cuda::CUDAGuard g(x.device());
+  auto xc = x.contiguous();
+  const int64_t B = xc.dim() == 3 ? xc.size(0) : 1;
+  const int64_t R = xc.size(-2), Cc = xc.size(-1);
+  at::Tensor y = xc.dim() == 3 ? at::empty({B, Cc, R}, xc.options()) : at::empty({Cc, R}, xc.options());
+  transpose2d(to_dtype(xc), xc.data_ptr(), y.data_ptr(), B, R, Cc, stream());
+  return y;
+}
+
+at::Tensor permute4_op(const at::Tensor& x, std::vector<int64_t> perm) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.dim() == 4 && perm.size() == 4, "dlvk.permute4: 4-D");
+  c10::cuda::CUDAGuard g(x.device());
+  auto xc = x.contiguous();
+  int dims[4], p[4];
+  std::vector<int64_t> od(4);
+  for (int i = 0; i < 4; ++i) {
+    dims[i] = (int)xc.size(i);
+    p[i] = (int)perm[i];
+  }
+  for (int i = 0; i < 4; ++i) od[i] = xc.size(p[i]);
+  auto y = at::empty(od, xc.options());
+  permute4(to_dtype(xc), xc.data_ptr(), y.data_ptr(), dims, p, stream());
+  return y;
+}
+
+// ---- softmax / losses ----
+at::Tensor softmax_op(const at::Tensor& x, bool log_out) {
+  check_cuda(x, "x");
+  c10::cuda::CUDAGuard g(x.device());
+  auto xc = x.contiguous();
+  const int64_t cols = xc.size(-1), rows = xc.numel() / std::max<int64_t>(cols, 1);
+  auto y = at::empty_like(xc);
+  softmax(to_dtype(xc), xc.data_ptr(), y.data_ptr(), rows, cols, log_out, stream());
+  return y;
+}
+
+at::Tensor softmax_bwd_op(const at::Tensor& y, const at::Tensor& dy) {
+  check_cuda(y, "y");
+  c10::cuda::CUDAGuard g(y.device());
+  auto yc = y.contiguous(), dyc = dy.contiguous();
+  const int64_t cols = yc.size(-1), rows = yc.numel() / std::max<int64_t>(cols, 1);
+  auto dx = at::empty_like(yc);
+  softmax_bwd(to_dtype(yc), yc.data_ptr(), dyc.data_ptr(), dx.data_ptr(), rows, cols, stream());
+  return dx;
+}
+
+// Returns (loss_rows [rows] f32, dlogits or empty).  `target` is int32 labels
+// [rows] or f32 probabilities [rows, cols].  in_place writes dlogits over the
+// logits buffer.
+std::vector<at::Tensor> softmax_ce_op(const at::Tensor& logits, const at::Tensor& target, double grad_scale,
+                                      bool want_grad, bool in_place) {
+  check_cuda(logits, "logits");
+  c10::cuda::CUDAGuard g(logits.device());
+  TORCH_CHECK(logits.is_contiguous(), "dlvk.softmax_ce: logits must be contiguous");
+  const int64_t cols = logits.size(-1), rows = logits.numel() / std::max<int64_t>(cols, 1);
+  const int* labels = nullptr;
+  const float* probs = nullptr;
+  at::Tensor tc;
+  if (target.scalar_type() == at::kInt) {
+    tc = target.contiguous();
+    TORCH_CHECK(tc.numel() == rows, "dlvk.softmax_ce: labels size");
+    labels = tc.data_ptr<int>();
+  } else {
+    tc = target.to(at::kFloat).contiguous();
+    TORCH_CHECK(tc.numel() == rows * cols, "dlvk.softmax_ce: target size");
+    probs = tc.data_ptr<float>();
+  }
+  auto loss_rows = at::empty({rows}, logits.options().dtype(at::kFloat));
+  at::Tensor dl;
+  if (want_grad) dl = in_place ? logits : at::empty_like(logits);
+  softmax_cross_entropy(to_dtype(logits), logits.data_ptr(), labels, probs, loss_rows.data_ptr<float>(),
+                        want_grad ? dl.data_ptr() : nullptr, rows, cols, (float)grad_scale, stream());
+  return {loss_rows, want_grad ? dl : at::Tensor()};
+}
+
+at::Tensor sum_scalar_op(const at::Tensor& v, double scale) {
+  check_cuda(v, "v");
+  TORCH_CHECK(v.scalar_type() == at::kFloat && v.is_contiguous(), "dlvk.sum_scalar: f32 contiguous");
+  c10::cuda::CUDAGuard g(v.device());
+  auto out = at::empty({}, v.options());
+  sum_rows_to_scalar(v.data_ptr<float>(), v.numel(), (float)scale, out.data_ptr<float>(), stream());
+  return out;
+}
+
+std::vector<at::Tensor> pointwise_loss_op(const at::Tensor& p, const at::Tensor& t, int64_t kind, double loss_scale,
+                                          double grad_scale, bool want_grad) {
+  check_cuda(p, "p");
+  c10::cuda::CUDAGuard g(p.device());
+  auto pc = p.contiguous();
+  auto tc = t.to(at::kFloat).contiguous();
+  TORCH_CHECK(pc.numel() == tc.numel(), "dlvk.pointwise_loss: size mismatch");
+  auto out = at::empty({}, pc.options().dtype(at::kFloat));
+  auto scratch = at::empty({pointwise_loss_blocks(pc.numel())}, pc.options().dtype(at::kFloat));
+  at::Tensor grad = want_grad ? at::empty_like(pc) : at::Tensor();
+  pointwise_loss(to_dtype(pc), (int)kind, pc.data_ptr(), tc.data_ptr<float>(), pc.numel(), (float)loss_scale,
+                 (float)grad_scale, want_grad ? grad.data_ptr() : nullptr, out.data_ptr<float>(),
+                 scratch.data_ptr<float>(), stream());
+  return {out, grad};
+}
+
+// ---- GEMM ----
+// C = alpha * A @ B + beta * C + bias, act.  A: [M,K] or [b,M,K] (any strides
+// with one unit stride for the tensor-core path); B: [K,N] or [b,K,N].
+at::Tensor gemm_op(const at::Tensor& A, const at::Tensor& B, c10::optional<at::Tensor> bias, int64_t act,
+                   double alpha, double beta, c10::optional<at::Tensor> out, c10::optional<at::ScalarType> out_dtype,
+                   int64_t force_path, int64_t max_ctas) {
+  check_cuda(A, "A");
+  check_cuda(B, "B");
+  TORCH_CHECK(A.scalar_type() == B.scalar_type(), "dlvk.gemm: A and B must have the same dtype");
+  TORCH_CHECK(A.dim() == B.dim() && (A.dim() == 2 || A.dim() == 3), "dlvk.gemm: 2-D or 3-D operands");
+  c10::cuda::CUDAGuard g(A.device());
+  const bool batched = A.dim() == 3;
+  const int64_t batch = batched ? A.size(0) : 1;
+  TORCH_CHECK(!batched || B.size(0) == batch, "dlvk.gemm: batch mismatch");
+  const int64_t M = A.size(-2), K = A.size(-1), N = B.size(-1);
+  TORCH_CHECK(B.size(-2) == K, "dlvk.gemm: inner dims ", K, " vs ", B.size(-2));
+  at::Tensor C;
+  if (out.has_value()) {
+    C = *out;
+    TORCH_CHECK(C.size(-1) == N && C.size(-2) == M && C.stride(-1) == 1, "dlvk.gemm: bad out");
+  } else {
+    auto odt = out_dtype.value_or(A.scalar_type());
+    C = batched ? at::empty({batch, M, N}, A.options().dtype(odt)) : at::empty({M, N}, A.options().dtype(odt));
+    TORCH_CHECK(beta == 0.0, "dlvk.gemm: beta != 0 requires out");
+  }
+  GemmArgs a;
+  a.A = A.data_ptr();
+  a.B = B.data_ptr();
+  a.C = C.data_ptr();
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.sam = A.stride(-2);
+  a.sak = A.stride(-1);
+  a.sbk = B.stride(-2);
+  a.sbn = B.stride(-1);
+  a.ldc = C.stride(-2);
+  a.batch = batch;
+  a.batch_stride_a = batched ? A.stride(0) : 0;
+  a.batch_stride_b = batched ? B.stride(0) : 0;
+  a.batch_stride_c = batched ? C.stride(0) : 0;
+  a.alpha = (float)alpha;
+  a.beta = (float)beta;
+  at::Tensor bc;
+  if (bias.has_value()) {
+    bc = bias->contiguous();
+    TORCH_CHECK(bc.numel() == N, "dlvk.gemm: bias size");
+    a.bias = bc.data_ptr();
+    a.bias_dtype = (int)to_dtype(bc);
+  }
+  a.act = (int)act;
+  if (M == 0 || N == 0) return C;
+  if (K == 0) {
+    // Degenerate: C = beta*C + bias, act.  Rare; do it with ATen.
+    if (beta == 0.0) C.zero_();
+    else C.mul_(beta);
+    if (bias.has_value()) C.add_(bc.to(C.scalar_type()));
+    if (act == ACT_RELU) C.relu_();
+    return C;
+  }
+  const bool tc_ok = A.scalar_type() == at::kBFloat16 && gemm_tc_supported(a) &&
+                     (C.scalar_type() == at::kBFloat16 || C.scalar_type() == at::kFloat);
+  const bool use_tc = force_path == 1 ? true : (force_path == 2 ? false : tc_ok);
+  if (use_tc) {
+    TORCH_CHECK(tc_ok, "dlvk.gemm: tensor-core path requested but not applicable to these operands");
+    gemm_tc(to_dtype(C), a, stream(), device_error_word(), (int)max_ctas);
+  } else {
+    gemm_simt(to_dtype(A), to_dtype(C), a, stream());
+  }
+  return C;
+}
+
+bool gemm_tc_ok(const at::Tensor& A, const at::Tensor& B) {
+  if (A.scalar_type() != at::kBFloat16 || B.scalar_type() != at::kBFloat16) return false;
+  if (A.dim() != B.dim() || A.dim() < 2) return false;
+  GemmArgs a;
+  a.A = A.data_ptr();
+  a.B = B.data_ptr();
+  a.M = A.size(-2);
+  a.K = A.size(-1);
+  a.N = B.size(-1);
+  a.sam = A.stride(-2);
+  a.sak = A.stride(-1);
+  a.sbk = B.stride(-2);
+  a.sbn = B.stride(-1);
+  a.batch = A.dim() == 3 ? A.size(0) : 1;
+  a.batch_stride_a = A.dim() == 3 ? A.stride(0) : 0;
+  a.batch_stride_b = B.dim() == 3 ? B.stride(0) : 0;
+  return gemm_tc_supported(a);
+}
+
+// ---- optimizers ----
+void optim_advance_op(const at::Tensor& hyper) {
+  check_cuda(hyper, "hyper");
+  c10::cuda::CUDAGuard g(hyper.device());
+  optim_advance(reinterpret_cast<OptimHyper*>(hyper.data_ptr()), stream());
+}
+
+void optim_update_op(int64_t kind, const at::Tensor& hyper, const at::Tensor& p, const at::Tensor& grad,
+                     c10::optional<at::Tensor> m, c10::optional<at::Tensor> v, c10::optional<at::Tensor> p_bf16,
+                     double extra_scale) {
+  check_cuda(p, "p");
+  c10::cuda::CUDAGuard g(p.device());
+  TORCH_CHECK(p.scalar_type() == at::kFloat && p.is_contiguous(), "dlvk.optim_update: f32 contiguous params");
+  TORCH_CHECK(grad.is_contiguous() && grad.numel() == p.numel(), "dlvk.optim_update: grad");
+  float* mp = m.has_value() ? m->data_ptr<float>() : nullptr;
+  float* vp = v.has_value() ? v->data_ptr<float>() : nullptr;
+  if (kind == OPT_ADAM) TORCH_CHECK(mp && vp, "adam needs m and v");
+  if (kind == OPT_RMSPROP) TORCH_CHECK(vp, "rmsprop needs v");
+  __nv_bfloat16* pb = nullptr;
+  if (p_bf16.has_value()) {
+    TORCH_CHECK(p_bf16->scalar_type() == at::kBFloat16 && p_bf16->is_contiguous() && p_bf16->numel() == p.numel(),
+                "dlvk.optim_update: bf16 copy");
+    pb = reinterpret_cast<__nv_bfloat16*>(p_bf16->data_ptr());
+  }
+  optim_update((int)kind, reinterpret_cast<const OptimHyper*>(hyper.data_ptr()), p.data_ptr<float>(),
+               grad.data_ptr(), to_dtype(grad), mp, vp, pb, p.numel(), (float)extra_scale, stream());
+}
+
+void grad_stats_op(const at::Tensor& g, double scale, double max_norm, const at::Tensor& sumsq,
+                   c10::optional<at::Tensor> flag, c10::optional<at::Tensor> clip, bool accumulate,
+                   const at::Tensor& scratch) {
+  check_cuda(g, "g");
+  c10::cuda::CUDAGuard gd(g.device());
+  TORCH_CHECK(g.is_contiguous(), "grad_stats: contiguous grad");
+  TORCH_CHECK(scratch.numel() >= grad_stats_scratch_floats(), "grad_stats: scratch too small");
+  grad_stats(g.data_ptr(), to_dtype(g), g.numel(), (float)scale, (float)max_norm, sumsq.data_ptr<float>(),
+             flag.has_value() ? flag->data_ptr<int>() : nullptr, clip.has_value() ? clip->data_ptr<float>() : nullptr,
+             accumulate, scratch.data_ptr<float>(), stream());
+}
+
+void scaler_update_op(const at::Tensor& scale, const at::Tensor& good_steps, const at::Tensor& found_inf,
+                      double growth, double backoff, int64_t interval, double smin, double smax,
+                      c10::optional<at::Tensor> inv_scale) {
+  c10::cuda::CUDAGuard g(scale.device());
+  scaler_update(scale.data_ptr<float>(), good_steps.data_ptr<int>(), found_inf.data_ptr<int>(), (float)growth,
+                (float)backoff, (int)interval, (float)smin, (float)smax,
+                inv_scale.has_value() ? inv_scale->data_ptr<float>() : nullptr, stream());
+}
+
+int64_t optim_hyper_bytes() { return (int64_t)sizeof(OptimHyper); }
+
+}  // namespace
+
+void register_ops(py::module& m) {
+  m.def("unary", &unary_op, py::arg("x"), py::arg("op"), py::arg("a") = 0.0, py::arg("b") = 0.0,
+        py::arg("out") = py::none(), py::arg("out_dtype") = py::none());
+  m.def("binary", &binary_op, py::arg("x"), py::arg("y"), py::arg("op"), py::arg("out") = py::none());
+  m.def("bias_act", &bias_act_op, py::arg("x"), py::arg("bias") = py::none(), py::arg("act") = 6);
+  m.def("reduce", &reduce_op, py::arg("x"), py::arg("op") = 0, py::arg("scale") = 1.0);
+  m.def("colsum", &colsum_op, py::arg("x"), py::arg("scale") = 1.0, py::arg("out") = py::none(),
+        py::arg("accumulate") = false, py::arg("out_dtype") = py::none());
+  m.def("rowsum", &rowsum_op, py::arg("x"), py::arg("scale") = 1.0);
+  m.def("transpose", &transpose_op);
+  m.def("permute4", &permute4_op);
+  m.def("softmax", &softmax_op, py::arg("x"), py::arg("log") = false);
+  m.def("softmax_bwd", &softmax_bwd_op);
+  m.def("softmax_ce", &softmax_ce_op, py::arg("logits"), py::arg("target"), py::arg("grad_scale") = 1.0,
+        py::arg("want_grad") = true, py::arg("in_place") = false);
+  m.def("sum_scalar", &sum_scalar_op, py::arg("v"), py::arg("scale") = 1.0);
+  m.def("pointwise_loss", &pointwise_loss_op);
+  m.def("gemm", &gemm_op, py::arg("A"), py::arg("B"), py::arg("bias") = py::none(), py::arg("act") = 0,
+        py::arg("alpha") = 1.0, py::arg("beta") = 0.0, py::arg("out") = py::none(), py::arg("out_dtype") = py::none(),
+        py::arg("force_path") = 0, py::arg("max_ctas") = 0);
+  m.def("gemm_tc_ok", &gemm_tc_ok);
+  m.def("optim_advance", &optim_advance_op);
+  m.def("optim_update", &optim_update_op, py::arg("kind"), py::arg("hyper"), py::arg("p"), py::arg("grad"),
+        py::arg("m") = py::none(), py::arg("v") = py::none(), py::arg("p_bf16") = py::none(),
+        py::arg("extra_scale") = 1.0);
+  m.def("grad_stats", &grad_stats_op);
+  m.def("grad_stats_scratch_floats", &grad_stats_scratch_floats);
+  m.def("scaler_update", &scaler_update_op);
+  m.def("optim_hyper_bytes", &optim_hyper_bytes);
+  m.def("launch_count", []() { return (int64_t)launch_count(); });
+  m.def("read_device_error", [](bool clear) { return (int64_t)read_device_error(clear); }, py::arg("clear") = true);
+}
+
+}  // namespace bind
+}  // namespace dlvk

@@ -1,0 +1,10 @@
+// Registration hooks for binding groups that are filled in by other files.
+#include "bind_common.h"
+
+namespace dlvk {
+namespace bind {
+void register_runtime(py::module&) {}
+void register_nn(py::module&) {}
+void register_comm(py::module&) {}
+}  // namespace bind
+}  // namespace dlvk

@@ -1,0 +1,100 @@
+// General strided/batched GEMM on the CUDA cores (fp32 FFMA), used for fp32
+// mode and for shapes the tensor-core path cannot take (row pitches that are
+// not 16-byte multiples, tiny N such as the 128->10 classifier).
+//
+// Reference: shaders/matrix_multiply.comp:23-37 (one thread per output),
+// shaders/batch_matrix_multiply.comp:33-86 (16x16 shared tiles); dispatch in
+// src/tensor/tensor_ops.cpp:187-298.  Here: 64x64 block tile, 16-deep K
+// slices in shared memory, 4x4 register micro-tile per thread, fused
+// alpha/beta, bias and activation epilogue.
+#include "dlvk/common.h"
+#include "dlvk/kernels.h"
+
+namespace dlvk {
+namespace {
+
+constexpr int BM = 64, BN = 64, BK = 16;
+
+template <typename TA, typename TC>
+__global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs a) {
+  __shared__ float As[BK][BM + 4];
+  __shared__ float Bs[BK][BN + 4];
+  const int64_t bz = blockIdx.z;
+  const TA* A = reinterpret_cast<const TA*>(a.A) + bz * a.batch_stride_a;
+  const TA* B = reinterpret_cast<const TA*>(a.B) + bz * a.batch_stride_b;
+  TC* C = reinterpret_cast<TC*>(a.C) + bz * a.batch_stride_c;
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // 16 x 16 threads
+  float acc[4][4] = {};
+  for (int64_t k0 = 0; k0 < a.K; k0 += BK) {
+    // Load A tile (BM x BK) and B tile (BK x BN): 1024 elements each, 4 per thread.
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = threadIdx.x + i * 256;
+      // A: choose the mapping that keeps the contiguous dimension on threadIdx.
+      int mm, kk;
+      if (a.sak == 1) { kk = e % BK; mm = e / BK; } else { mm = e % BM; kk = e / BM; }
+      const int64_t gm = m0 + mm, gk = k0 + kk;
+      As[kk][mm] = (gm < a.M && gk < a.K) ? to_f32(A[gm * a.sam + gk * a.sak]) : 0.f;
+      int nn, kb;
+      if (a.sbn == 1) { nn = e % BN; kb = e / BN; } else { kb = e % BK; nn = e / BK; }
+      const int64_t gn = n0 + nn, gkb = k0 + kb;
+      Bs[kb][nn] = (gn < a.N && gkb < a.K) ? to_f32(B[gkb * a.sbk + gn * a.sbn]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      float av[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) av[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+  // Epilogue.
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t gm = m0 + ty * 4 + i;
+    if (gm >= a.M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t gn = n0 + tx * 4 + j;
+      if (gn >= a.N) continue;
+      float v = a.alpha * acc[i][j];
+      TC* cp = C + gm * a.ldc + gn;
+      if (a.beta != 0.f) v += a.beta * to_f32(*cp);
+      if (a.bias) {
+        v += (a.bias_dtype == (int)DType::F32) ? reinterpret_cast<const float*>(a.bias)[gn]
+                                               : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.bias)[gn]);
+      }
+      if (a.act == ACT_RELU) v = fmaxf(v, 0.f);
+      else if (a.act == ACT_GELU) v = 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
+      *cp = from_f32<TC>(v);
+    }
+  }
+}
+
+}  // namespace
+
+void gemm_simt(DType in_dt, DType out_dt, const GemmArgs& a, cudaStream_t s) {
+  if (a.M == 0 || a.N == 0) return;
+  dim3 grid((unsigned)((a.N + BN - 1) / BN), (unsigned)((a.M + BM - 1) / BM), (unsigned)a.batch);
+  if (in_dt == DType::F32 && out_dt == DType::F32)
+    gemm_simt_kernel<float, float><<<grid, 256, 0, s>>>(a);
+  else if (in_dt == DType::BF16 && out_dt == DType::BF16)
+    gemm_simt_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 256, 0, s>>>(a);
+  else if (in_dt == DType::BF16 && out_dt == DType::F32)
+    gemm_simt_kernel<__nv_bfloat16, float><<<grid, 256, 0, s>>>(a);
+  else if (in_dt == DType::F32 && out_dt == DType::BF16)
+    gemm_simt_kernel<float, __nv_bfloat16><<<grid, 256, 0, s>>>(a);
+  else
+    throw std::runtime_error("dlvk::gemm_simt: unsupported dtype combination");
+  DLVK_POST_LAUNCH();
+}
+
+}  // namespace dlvk

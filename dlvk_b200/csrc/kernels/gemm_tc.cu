@@ -1,0 +1,405 @@
+// Tensor-core GEMM for sm_100a: TMA -> shared-memory ring -> tcgen05.mma ->
+// TMEM accumulators -> fused epilogue.  Replaces the reference's
+// matrix_multiply.comp / batch_matrix_multiply.comp (shaders/, dispatched from
+// src/tensor/tensor_ops.cpp:187-298) for Dense forward/backward, attention
+// projections and the batched attention products.
+//
+// Design:
+//  * persistent kernel, one CTA per SM, 192 threads = 6 warps:
+//      warp 0      TMA producer (one lane) over a STAGES-deep smem ring
+//      warp 1      TMEM allocator + MMA issuer (one lane)
+//      warps 2..5  epilogue: tcgen05.ld 32x32b -> alpha/beta/bias/act -> global
+//  * tile 128 x BN x 64 (BN = 256 or 128), UMMA 128 x BN x 16 (kind::f16, bf16
+//    in, f32 accumulate), two TMEM accumulator buffers so the epilogue of tile
+//    i overlaps the main loop of tile i+1.
+//  * A may be K-major ([M,K] row-major) or M-major ([K,M] row-major); B may be
+//    K-major ([N,K]) or N-major ([K,N]).  Both are expressed through the TMA
+//    box shape and the UMMA descriptor major-ness, so no transpose kernels are
+//    ever needed for X*W, dY*W^T or X^T*dY.
+//  * TMA loads are plain (no cluster multicast).
+//  * every mbarrier wait is bounded (2 s) and reports through `err`.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <mutex>
+#include <unordered_map>
+
+#include "dlvk/common.h"
+#include "dlvk/kernels.h"
+#include "dlvk/sm100.h"
+
+namespace dlvk {
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // bf16 elements per 128-byte swizzle row
+
+struct TcParams {
+  int M, N, K, batch;
+  int tiles_m, tiles_n;
+  int a_mn, b_mn;
+  void* C;
+  int64_t ldc, bsc;
+  int out_f32;
+  int vec_ok;
+  float alpha, beta;
+  const void* bias;
+  int bias_f32;
+  int act;
+  uint32_t* err;
+};
+
+template <int BN>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ void tile_coords(int t, const TcParams& p, int& tm, int& tn, int& b) {
+  const int per_batch = p.tiles_m * p.tiles_n;
+  b = t / per_batch;
+  const int r = t - b * per_batch;
+  constexpr int GROUP_M = 8;
+  const int in_group = GROUP_M * p.tiles_n;
+  const int g = r / in_group;
+  const int first_m = g * GROUP_M;
+  const int gsz = min(p.tiles_m - first_m, GROUP_M);
+  const int rr = r - g * in_group;
+  tm = first_m + rr % gsz;
+  tn = rr / gsz;
+}
+
+__device__ __forceinline__ float act_apply(int act, float v) {
+  if (act == ACT_RELU) return fmaxf(v, 0.f);
+  if (act == ACT_GELU) return 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
+  return v;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, TcParams p) {
+  using C = Cfg<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_tiles = p.tiles_m * p.tiles_n * p.batch;
+  const int num_kb = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 128);
+    }
+    fence_barrier_init();
+    fence_proxy_async_smem();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+        int tm, tn, b;
+        tile_coords(t, p, tm, tn, b);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.err)) goto producer_done;
+          uint8_t* sA = smem + stage * C::STAGE_BYTES;
+          uint8_t* sB = sA + C::A_BYTES;
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          if (!p.a_mn) {
+            tma_load_3d(sA, &tmA, &full[stage], kb * BK, tm * BM, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_3d(sA + j * 8192, &tmA, &full[stage], tm * BM + j * 64, kb * BK, b);
+          }
+          if (!p.b_mn) {
+            tma_load_3d(sB, &tmB, &full[stage], kb * BK, tn * BN, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_3d(sB + j * 8192, &tmB, &full[stage], tn * BN + j * 64, kb * BK, b);
+          }
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc(1, 1, 1, p.a_mn != 0, p.b_mn != 0, BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.err)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t aBase = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t bBase = aBase + C::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = p.a_mn ? make_sw128_desc(aBase + k * 2048, 8192, 1024)
+                                       : make_sw128_desc(aBase + k * 32, 16, 1024);
+            const uint64_t bd = p.b_mn ? make_sw128_desc(bBase + k * 2048, 8192, 1024)
+                                       : make_sw128_desc(bBase + k * 32, 16, 1024);
+            mma_f16(d, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+    }
+  } else {
+    // Epilogue warps 2..5.  TMEM lane quarter accessible to a warp = warp % 4.
+    const int q = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      int tm, tn, b;
+      tile_coords(t, p, tm, tn, b);
+      if (!mbar_wait(&tfull[acc], acc_phase, p.err)) break;
+      tc_fence_after();
+      const int row = tm * BM + q * 32 + lane;
+      const bool row_ok = row < p.M;
+      const int64_t cbase = (int64_t)b * p.bsc + (int64_t)row * p.ldc;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
+        tmem_ld_wait();
+        const int n0 = tn * BN + c * 32;
+        if (!row_ok || n0 >= p.N) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+        const bool full_chunk = (n0 + 32 <= p.N);
+        if (p.beta != 0.f) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (n0 + j < p.N) {
+              const float old = p.out_f32 ? reinterpret_cast<const float*>(p.C)[cbase + n0 + j]
+                                          : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.C)[cbase + n0 + j]);
+              v[j] += p.beta * old;
+            }
+          }
+        }
+        if (p.bias) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (n0 + j < p.N)
+              v[j] += p.bias_f32 ? reinterpret_cast<const float*>(p.bias)[n0 + j]
+                                 : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.bias)[n0 + j]);
+          }
+        }
+        if (p.act != ACT_NONE) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = act_apply(p.act, v[j]);
+        }
+        if (p.out_f32) {
+          float* dst = reinterpret_cast<float*>(p.C) + cbase + n0;
+          if (full_chunk && p.vec_ok) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              reinterpret_cast<float4*>(dst)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < p.N) dst[j] = v[j];
+          }
+        } else {
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + cbase + n0;
+          if (full_chunk && p.vec_ok) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+              pk[j] = *reinterpret_cast<uint32_t*>(&h);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              reinterpret_cast<uint4*>(dst)[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < p.N) dst[j] = __float2bfloat16_rn(v[j]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side: tensor-map encoding through the driver entry point (no libcuda
+// link dependency), cached per device.
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    DLVK_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || ptr == nullptr)
+      throw std::runtime_error("dlvk: cuTensorMapEncodeTiled entry point unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 3-D bf16 tensor map: dims {d0 (contiguous), d1, d2}, strides in elements for
+// d1 and d2, box {64, box1, 1}, 128-byte swizzle, zero fill out of bounds.
+CUtensorMap make_tmap_bf16(const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1, uint64_t s2,
+                           uint32_t box1) {
+  CUtensorMap m;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1 * 2, s2 * 2};
+  cuuint32_t box[3] = {64, box1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("dlvk: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return m;
+}
+
+int sm_count() {
+  static int n[64] = {0};
+  int dev = 0;
+  DLVK_CUDA_CHECK(cudaGetDevice(&dev));
+  if (n[dev] == 0) DLVK_CUDA_CHECK(cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev));
+  return n[dev];
+}
+
+template <int BN>
+void launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, int max_ctas, cudaStream_t s) {
+  using C = Cfg<BN>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  DLVK_CUDA_CHECK(cudaGetDevice(&dev));
+  if (!attr_set[dev]) {
+    DLVK_CUDA_CHECK(cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    attr_set[dev] = true;
+  }
+  const int tiles = p.tiles_m * p.tiles_n * p.batch;
+  int grid = std::min(tiles, max_ctas > 0 ? max_ctas : sm_count());
+  gemm_tc_kernel<BN><<<grid, 192, C::SMEM, s>>>(ta, tb, p);
+  DLVK_POST_LAUNCH();
+}
+
+inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+bool gemm_tc_supported(const GemmArgs& a) {
+  const bool a_k = (a.sak == 1), a_m = (a.sam == 1) && !a_k;
+  const bool b_k = (a.sbk == 1), b_n = (a.sbn == 1) && !b_k;
+  if (!(a_k || a_m) || !(b_k || b_n)) return false;
+  const int64_t lda = a_k ? a.sam : a.sak;
+  const int64_t ldb = b_k ? a.sbn : a.sbk;
+  if ((lda * 2) % 16 || (ldb * 2) % 16) return false;
+  if (a.batch > 1 && ((a.batch_stride_a * 2) % 16 || (a.batch_stride_b * 2) % 16)) return false;
+  if (!al16(a.A) || !al16(a.B)) return false;
+  if (a.M < 1 || a.N < 16 || a.K < 1) return false;
+  if (a.M > (1LL << 31) - 1 || a.N > (1LL << 31) - 1 || a.K > (1LL << 31) - 1) return false;
+  return true;
+}
+
+void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int max_ctas) {
+  DLVK_CHECK(gemm_tc_supported(a), "gemm_tc: unsupported layout/alignment");
+  if (a.M == 0 || a.N == 0) return;
+  const bool a_k = (a.sak == 1);
+  const bool b_k = (a.sbk == 1);
+  const int BN = (a.N >= 256) ? 256 : 128;
+  const uint64_t batch = (uint64_t)a.batch;
+  CUtensorMap ta, tb;
+  if (a_k) {
+    const uint64_t bs = a.batch > 1 ? (uint64_t)a.batch_stride_a : (uint64_t)a.sam * (uint64_t)a.M;
+    ta = make_tmap_bf16(a.A, a.K, a.M, batch, a.sam, bs, BM);
+  } else {
+    const uint64_t bs = a.batch > 1 ? (uint64_t)a.batch_stride_a : (uint64_t)a.sak * (uint64_t)a.K;
+    ta = make_tmap_bf16(a.A, a.M, a.K, batch, a.sak, bs, 64);
+  }
+  if (b_k) {
+    const uint64_t bs = a.batch > 1 ? (uint64_t)a.batch_stride_b : (uint64_t)a.sbn * (uint64_t)a.N;
+    tb = make_tmap_bf16(a.B, a.K, a.N, batch, a.sbn, bs, BN);
+  } else {
+    const uint64_t bs = a.batch > 1 ? (uint64_t)a.batch_stride_b : (uint64_t)a.sbk * (uint64_t)a.K;
+    tb = make_tmap_bf16(a.B, a.N, a.K, batch, a.sbk, bs, 64);
+  }
+  TcParams p{};
+  p.M = (int)a.M;
+  p.N = (int)a.N;
+  p.K = (int)a.K;
+  p.batch = (int)a.batch;
+  p.tiles_m = (int)((a.M + BM - 1) / BM);
+  p.tiles_n = (int)((a.N + BN - 1) / BN);
+  p.a_mn = a_k ? 0 : 1;
+  p.b_mn = b_k ? 0 : 1;
+  p.C = a.C;
+  p.ldc = a.ldc;
+  p.bsc = a.batch_stride_c;
+  p.out_f32 = (out_dt == DType::F32);
+  const int esz = p.out_f32 ? 4 : 2;
+  p.vec_ok = al16(a.C) && ((a.ldc * esz) % 16 == 0) && ((a.batch_stride_c * esz) % 16 == 0);
+  p.alpha = a.alpha;
+  p.beta = a.beta;
+  p.bias = a.bias;
+  p.bias_f32 = (a.bias_dtype == (int)DType::F32);
+  p.act = a.act;
+  p.err = err;
+  if (BN == 256) launch_tc<256>(ta, tb, p, max_ctas, s);
+  else launch_tc<128>(ta, tb, p, max_ctas, s);
+}
+
+}  // namespace dlvk

@@ -1,0 +1,255 @@
+// Softmax, fused softmax + cross-entropy (forward and backward in one pass),
+// and the MSE / BCE losses.
+//
+// Reference: shaders/softmax.comp:23-67 (three dispatches: row max, exp+sum,
+// divide), shaders/cross_entropy_{forward,backward}.comp, shaders/mse_*.comp,
+// shaders/binary_cross_entropy_*.comp; host in src/loss/loss_functions.cpp
+// (CPU CE = -sum t*log(p+1e-8)/B, grad (p - t)/B at :127-160).
+// Here softmax is one kernel per row block, and softmax + CE produces the
+// per-row loss and dlogits = (softmax - target) * scale from the logits in a
+// single launch (the reference's softmax-backward-is-identity convention,
+// src/layers/activation.cpp:71-75, is only correct in this fused form).
+#include "dlvk/common.h"
+#include "dlvk/kernels.h"
+
+namespace dlvk {
+namespace {
+
+// Merge two (max, sum-of-exp) pairs.
+__device__ __forceinline__ void ms_merge(float& m, float& s, float m2, float s2) {
+  if (m2 > m) {
+    s = s * expf(m - m2) + s2;
+    m = m2;
+  } else if (m2 != -INFINITY) {
+    s = s + s2 * expf(m2 - m);
+  }
+}
+
+template <int THREADS>
+__device__ __forceinline__ void block_ms(float& m, float& s) {
+  __shared__ float sm_m[32], sm_s[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    ms_merge(m, s, m2, s2);
+  }
+  if (THREADS > 32) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) { sm_m[wid] = m; sm_s[wid] = s; }
+    __syncthreads();
+    m = -INFINITY;
+    s = 0.f;
+    for (int i = 0; i < THREADS / 32; ++i) ms_merge(m, s, sm_m[i], sm_s[i]);
+  }
+}
+
+template <int THREADS>
+__device__ __forceinline__ float block_sum_t(float v) {
+  __shared__ float sm[32];
+  v = warp_sum(v);
+  if (THREADS > 32) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) sm[wid] = v;
+    __syncthreads();
+    v = 0.f;
+    for (int i = 0; i < THREADS / 32; ++i) v += sm[i];
+  }
+  return v;
+}
+
+// One CTA (THREADS threads) per row.
+template <typename T, int THREADS>
+__global__ void __launch_bounds__(THREADS) softmax_rows_kernel(const T* __restrict__ x, T* __restrict__ y,
+                                                               int64_t cols, bool log_out) {
+  const int64_t r = blockIdx.x;
+  const T* xr = x + r * cols;
+  T* yr = y + r * cols;
+  float m = -INFINITY, s = 0.f;
+  for (int64_t c = threadIdx.x; c < cols; c += THREADS) {
+    const float v = to_f32(xr[c]);
+    ms_merge(m, s, v, 1.f);
+  }
+  block_ms<THREADS>(m, s);
+  const float inv = 1.f / s, lse = m + logf(s);
+  for (int64_t c = threadIdx.x; c < cols; c += THREADS) {
+    const float v = to_f32(xr[c]);
+    yr[c] = from_f32<T>(log_out ? v - lse : expf(v - m) * inv);
+  }
+}
+
+// dx = y * (dy - sum(dy * y))  (standard softmax Jacobian-vector product)
+template <typename T, int THREADS>
+__global__ void __launch_bounds__(THREADS) softmax_bwd_kernel(const T* __restrict__ y, const T* __restrict__ dy,
+                                                              T* __restrict__ dx, int64_t cols) {
+  const int64_t r = blockIdx.x;
+  float acc = 0.f;
+  for (int64_t c = threadIdx.x; c < cols; c += THREADS) acc += to_f32(y[r * cols + c]) * to_f32(dy[r * cols + c]);
+  acc = block_sum_t<THREADS>(acc);
+  for (int64_t c = threadIdx.x; c < cols; c += THREADS) {
+    const float yy = to_f32(y[r * cols + c]);
+    dx[r * cols + c] = from_f32<T>(yy * (to_f32(dy[r * cols + c]) - acc));
+  }
+}
+
+// Fused softmax + cross-entropy.  Targets are either class ids (labels, -1 =
+// ignored row) or a dense probability matrix `probs` [rows, cols].
+// loss_rows[r] = -sum_c t_c * log_softmax(x)_c
+// dlogits[r, c] = (softmax(x)_c - t_c) * grad_scale   (may alias x)
+template <typename T, int THREADS>
+__global__ void __launch_bounds__(THREADS) softmax_ce_kernel(const T* x, const int* __restrict__ labels,
+                                                             const float* __restrict__ probs,
+                                                             float* __restrict__ loss_rows, T* dlogits,
+                                                             int64_t cols, float grad_scale) {
+  const int64_t r = blockIdx.x;
+  const T* xr = x + r * cols;
+  float m = -INFINITY, s = 0.f;
+  for (int64_t c = threadIdx.x; c < cols; c += THREADS) ms_merge(m, s, to_f32(xr[c]), 1.f);
+  block_ms<THREADS>(m, s);
+  const float lse = m + logf(s), inv = 1.f / s;
+  const int label = labels ? labels[r] : -2;
+  float loss = 0.f;
+  if (labels) {
+    if (label >= 0 && label < cols && threadIdx.x == 0) loss = lse - to_f32(xr[label]);
+  } else {
+    float acc = 0.f;
+    for (int64_t c = threadIdx.x; c < cols; c += THREADS) {
+      const float t = probs[r * cols + c];
+      if (t != 0.f) acc += t * (lse - to_f32(xr[c]));
+    }
+    loss = acc;
+  }
+  loss = block_sum_t<THREADS>(loss);
+  if (threadIdx.x == 0 && loss_rows) loss_rows[r] = (labels && label < 0) ? 0.f : loss;
+  if (dlogits) {
+    T* dr = dlogits + r * cols;
+    const bool ignored = labels && label < 0;
+    for (int64_t c = threadIdx.x; c < cols; c += THREADS) {
+      const float p = expf(to_f32(xr[c]) - m) * inv;
+      const float t = labels ? (c == label ? 1.f : 0.f) : probs[r * cols + c];
+      dr[c] = from_f32<T>(ignored ? 0.f : (p - t) * grad_scale);
+    }
+  }
+}
+
+// Pointwise losses with a deterministic two-stage sum:
+//  MSE:  l = (p - t)^2,                      g = 2 (p - t) * gscale
+//  BCE:  l = -(t log p' + (1-t) log(1-p')),  p' = clamp(p, eps, 1-eps),
+//        g = (p' - t) / (p' (1 - p')) * gscale
+template <typename T>
+__global__ void pointwise_loss_kernel(int kind, const T* __restrict__ p, const float* __restrict__ t, int64_t n,
+                                      float gscale, T* __restrict__ grad, float* __restrict__ partial) {
+  __shared__ float sm[32];
+  float acc = 0.f;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float pv = to_f32(p[i]), tv = t[i];
+    float l, g;
+    if (kind == LOSS_MSE) {
+      const float d = pv - tv;
+      l = d * d;
+      g = 2.f * d * gscale;
+    } else {
+      const float eps = 1e-7f;
+      const float pc = fminf(fmaxf(pv, eps), 1.f - eps);
+      l = -(tv * logf(pc) + (1.f - tv) * logf(1.f - pc));
+      g = (pc - tv) / (pc * (1.f - pc)) * gscale;
+    }
+    acc += l;
+    if (grad) grad[i] = from_f32<T>(g);
+  }
+  acc = block_sum(acc, sm);
+  if (threadIdx.x == 0) partial[blockIdx.x] = acc;
+}
+
+__global__ void sum_partials_kernel(const float* __restrict__ part, int n, float scale, float* __restrict__ out) {
+  __shared__ float sm[32];
+  float acc = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) acc += part[i];
+  acc = block_sum(acc, sm);
+  if (threadIdx.x == 0) out[0] = acc * scale;
+}
+
+template <typename T>
+void launch_softmax(const void* x, void* y, int64_t rows, int64_t cols, bool log_out, cudaStream_t s) {
+  if (cols <= 64)
+    softmax_rows_kernel<T, 32><<<(unsigned)rows, 32, 0, s>>>((const T*)x, (T*)y, cols, log_out);
+  else if (cols <= 4096)
+    softmax_rows_kernel<T, 128><<<(unsigned)rows, 128, 0, s>>>((const T*)x, (T*)y, cols, log_out);
+  else
+    softmax_rows_kernel<T, 512><<<(unsigned)rows, 512, 0, s>>>((const T*)x, (T*)y, cols, log_out);
+}
+
+template <typename T>
+void launch_softmax_bwd(const void* y, const void* dy, void* dx, int64_t rows, int64_t cols, cudaStream_t s) {
+  if (cols <= 64)
+    softmax_bwd_kernel<T, 32><<<(unsigned)rows, 32, 0, s>>>((const T*)y, (const T*)dy, (T*)dx, cols);
+  else
+    softmax_bwd_kernel<T, 256><<<(unsigned)rows, 256, 0, s>>>((const T*)y, (const T*)dy, (T*)dx, cols);
+}
+
+template <typename T>
+void launch_ce(const void* x, const int* labels, const float* probs, float* loss_rows, void* dlogits, int64_t rows,
+               int64_t cols, float grad_scale, cudaStream_t s) {
+  if (cols <= 64)
+    softmax_ce_kernel<T, 32><<<(unsigned)rows, 32, 0, s>>>((const T*)x, labels, probs, loss_rows, (T*)dlogits, cols,
+                                                           grad_scale);
+  else if (cols <= 4096)
+    softmax_ce_kernel<T, 128><<<(unsigned)rows, 128, 0, s>>>((const T*)x, labels, probs, loss_rows, (T*)dlogits,
+                                                             cols, grad_scale);
+  else
+    softmax_ce_kernel<T, 512><<<(unsigned)rows, 512, 0, s>>>((const T*)x, labels, probs, loss_rows, (T*)dlogits,
+                                                             cols, grad_scale);
+}
+
+}  // namespace
+
+void softmax(DType dt, const void* x, void* y, int64_t rows, int64_t cols, bool log_out, cudaStream_t s) {
+  if (rows == 0) return;
+  if (dt == DType::F32) launch_softmax<float>(x, y, rows, cols, log_out, s);
+  else if (dt == DType::BF16) launch_softmax<__nv_bfloat16>(x, y, rows, cols, log_out, s);
+  else throw std::runtime_error("dlvk::softmax: unsupported dtype");
+  DLVK_POST_LAUNCH();
+}
+
+void softmax_bwd(DType dt, const void* y, const void* dy, void* dx, int64_t rows, int64_t cols, cudaStream_t s) {
+  if (rows == 0) return;
+  if (dt == DType::F32) launch_softmax_bwd<float>(y, dy, dx, rows, cols, s);
+  else if (dt == DType::BF16) launch_softmax_bwd<__nv_bfloat16>(y, dy, dx, rows, cols, s);
+  else throw std::runtime_error("dlvk::softmax_bwd: unsupported dtype");
+  DLVK_POST_LAUNCH();
+}
+
+void softmax_cross_entropy(DType dt, const void* logits, const int* labels, const float* probs, float* loss_rows,
+                           void* dlogits, int64_t rows, int64_t cols, float grad_scale, cudaStream_t s) {
+  if (rows == 0) return;
+  if (dt == DType::F32) launch_ce<float>(logits, labels, probs, loss_rows, dlogits, rows, cols, grad_scale, s);
+  else if (dt == DType::BF16)
+    launch_ce<__nv_bfloat16>(logits, labels, probs, loss_rows, dlogits, rows, cols, grad_scale, s);
+  else throw std::runtime_error("dlvk::softmax_cross_entropy: unsupported dtype");
+  DLVK_POST_LAUNCH();
+}
+
+int pointwise_loss_blocks(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>(296, (n + 1023) / 1024)); }
+
+void pointwise_loss(DType dt, int kind, const void* p, const float* t, int64_t n, float loss_scale, float grad_scale,
+                    void* grad, float* out, float* scratch, cudaStream_t s) {
+  const int blocks = pointwise_loss_blocks(n);
+  if (dt == DType::F32)
+    pointwise_loss_kernel<float><<<blocks, 256, 0, s>>>(kind, (const float*)p, t, n, grad_scale, (float*)grad, scratch);
+  else if (dt == DType::BF16)
+    pointwise_loss_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(kind, (const __nv_bfloat16*)p, t, n, grad_scale,
+                                                                (__nv_bfloat16*)grad, scratch);
+  else throw std::runtime_error("dlvk::pointwise_loss: unsupported dtype");
+  DLVK_POST_LAUNCH();
+  sum_partials_kernel<<<1, 512, 0, s>>>(scratch, blocks, loss_scale, out);
+  DLVK_POST_LAUNCH();
+}
+
+void sum_rows_to_scalar(const float* rows_vals, int64_t n, float scale, float* out, cudaStream_t s) {
+  sum_partials_kernel<<<1, 1024, 0, s>>>(rows_vals, (int)n, scale, out);
+  DLVK_POST_LAUNCH();
+}
+
+}  // namespace dlvk

@@ -1,0 +1,49 @@
+// CUDA device runtime pieces shared by all launchers: the launch counter, the
+// per-device error word used by bounded waits, and error formatting.
+// Replaces the reference's VulkanDevice error plumbing (bool returns + cerr,
+// src/core/vulkan_device.cpp, src/tensor/tensor_ops.cpp:1686-1709).
+#include <mutex>
+#include <string>
+
+#include "dlvk/common.h"
+#include "dlvk/kernels.h"
+
+namespace dlvk {
+
+namespace {
+std::atomic<uint64_t> g_launches{0};
+std::mutex g_err_mu;
+uint32_t* g_err_words[64] = {nullptr};
+}  // namespace
+
+uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
+void note_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+void throw_cuda(cudaError_t e, const char* what, const char* file, int line) {
+  throw std::runtime_error(std::string("dlvk CUDA error: ") + cudaGetErrorString(e) + " (" + what + ") at " + file +
+                           ":" + std::to_string(line));
+}
+
+uint32_t* device_error_word() {
+  int dev = 0;
+  DLVK_CUDA_CHECK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  if (g_err_words[dev] == nullptr) {
+    void* p = nullptr;
+    DLVK_CUDA_CHECK(cudaMalloc(&p, 256));
+    DLVK_CUDA_CHECK(cudaMemset(p, 0, 256));
+    DLVK_CUDA_CHECK(cudaDeviceSynchronize());
+    g_err_words[dev] = static_cast<uint32_t*>(p);
+  }
+  return g_err_words[dev];
+}
+
+uint32_t read_device_error(bool clear) {
+  uint32_t* w = device_error_word();
+  uint32_t v = 0;
+  DLVK_CUDA_CHECK(cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost));
+  if (clear && v) DLVK_CUDA_CHECK(cudaMemset(w, 0, sizeof(uint32_t)));
+  return v;
+}
+
+}  // namespace dlvk

@@ -1,0 +1,98 @@
+"""GEMM kernels (tcgen05 tensor-core path and the SIMT path) against a plain
+fp32 PyTorch reference of the same product."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _C():
+    from dlvk_b200 import _ext
+
+    return _ext.C()
+
+
+def _ref(a, b, bias=None, act=0, alpha=1.0):
+    c = alpha * (a.float() @ b.float())
+    if bias is not None:
+        c = c + bias.float()
+    if act == 1:
+        c = torch.relu(c)
+    return c
+
+
+def _check(out, ref, tol):
+    err = (out.float() - ref).abs().max().item()
+    scale = ref.abs().max().item() + 1e-6
+    assert err <= tol * scale, f"max err {err} (scale {scale})"
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 1024), (300, 200, 100), (1024, 1024, 1024),
+                                   (8192 // 4, 3072, 1024), (32, 128, 784), (129, 136, 72)])
+@pytest.mark.parametrize("a_t", [False, True])
+@pytest.mark.parametrize("b_t", [False, True])
+def test_gemm_tc_layouts(M, N, K, a_t, b_t):
+    C = _C()
+    torch.manual_seed(0)
+    dev = "cuda"
+    a = torch.randn(M, K, device=dev).bfloat16()
+    b = torch.randn(K, N, device=dev).bfloat16()
+    A = a.t().contiguous().t() if a_t else a  # M-major view when a_t
+    B = b.t().contiguous().t() if b_t else b  # K-major ([N,K] storage) when b_t
+    if not C.gemm_tc_ok(A, B):
+        pytest.skip("layout not eligible for the tensor-core path")
+    out = C.gemm(A, B, force_path=1)
+    torch.cuda.synchronize()
+    assert C.read_device_error(True) == 0
+    _check(out, _ref(a, b), 2e-2)
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_gemm_tc_epilogue(out_dtype):
+    C = _C()
+    torch.manual_seed(1)
+    M, N, K = 512, 384, 256
+    a = torch.randn(M, K, device="cuda").bfloat16()
+    b = torch.randn(K, N, device="cuda").bfloat16()
+    bias = torch.randn(N, device="cuda")
+    out = C.gemm(a, b, bias=bias, act=1, alpha=0.5, out_dtype=out_dtype, force_path=1)
+    _check(out, _ref(a, b, bias, 1, 0.5), 2e-2)
+    # beta accumulation into an f32 output (gradient accumulation)
+    acc = torch.randn(M, N, device="cuda")
+    ref = acc + a.float() @ b.float()
+    C.gemm(a, b, beta=1.0, out=acc, force_path=1)
+    _check(acc, ref, 2e-2)
+
+
+def test_gemm_tc_batched():
+    C = _C()
+    torch.manual_seed(2)
+    Bt, M, N, K = 6, 256, 192, 64
+    a = torch.randn(Bt, M, K, device="cuda").bfloat16()
+    b = torch.randn(Bt, K, N, device="cuda").bfloat16()
+    out = C.gemm(a, b, force_path=1, out_dtype=torch.float32)
+    _check(out, a.float() @ b.float(), 2e-2)
+    # Q K^T style: B given as a transposed view of [Bt, N, K]
+    kk = torch.randn(Bt, N, K, device="cuda").bfloat16()
+    out2 = C.gemm(a, kk.transpose(1, 2), force_path=1, out_dtype=torch.float32)
+    _check(out2, a.float() @ kk.float().transpose(1, 2), 2e-2)
+
+
+def test_gemm_tc_persistent_small_grid():
+    """Few CTAs loop over many tiles: exercises the TMEM double buffer and ring phases."""
+    C = _C()
+    a = torch.randn(2048, 512, device="cuda").bfloat16()
+    b = torch.randn(512, 1024, device="cuda").bfloat16()
+    out = C.gemm(a, b, force_path=1, max_ctas=3)
+    _check(out, _ref(a, b), 2e-2)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("M,N,K", [(32, 10, 128), (33, 47, 784), (257, 130, 65)])
+def test_gemm_simt(dtype, M, N, K):
+    C = _C()
+    a = torch.randn(M, K, device="cuda").to(dtype)
+    b = torch.randn(N, K, device="cuda").to(dtype).t()  # strided view
+    bias = torch.randn(N, device="cuda")
+    out = C.gemm(a, b, bias=bias, act=1, force_path=2, out_dtype=torch.float32)
+    _check(out, _ref(a, b, bias, 1), 1e-5 if dtype == torch.float32 else 1e-2)
