@@ -1,0 +1,318 @@
+"""Training-throughput benchmark (train samples/s, device-timed, max over ranks).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl ours|torch|reference]
+
+For N > 1 launch one process per GPU:
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \\
+        --master-port P bench.py --gpus N ...
+
+Workloads (synthetic data of the configuration's shapes, random-init weights):
+  transformer  Embedding 32000x1024, 12 encoder blocks (16 heads, d_ff 4096),
+               seq 512, batch 16 per GPU, next-token CE, Adam, bf16   [default]
+  wide_mlp     1024->4096, 4x4096 (BN, ReLU, Dropout 0.1), ->1000, batch 1024/GPU,
+               SGD-momentum 0.9, bf16
+  cnn          2xConv3x3(+ReLU, MaxPool) + 2xDense, 47 classes, batch 256/GPU, Adam, fp32
+  cnn_bf16     same, bf16
+  mlp          784->128->10, batch 32, Adam, fp32
+
+--impl ours       this framework (hand-written sm_100a kernels, CUDA-graph captured step,
+                  fused all-reduce + optimizer across GPUs)
+--impl torch      the same model in plain PyTorch (cuBLAS/cuDNN/SDPA, NCCL all-reduce +
+                  torch optimizer) -- the NCCL(+cuBLAS) comparison point
+--impl reference  the reference framework (prints why it cannot run here)
+
+Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+BASELINE_MS_BATCH1_FWD = 3.772  # published MLP forward (batch 1) of the reference
+
+REFERENCE_UNAVAILABLE = (
+    "reference is a C++/Vulkan-compute project with no Python package: offline pip install fails "
+    "('Neither setup.py nor pyproject.toml found'); it also does not compile as shipped "
+    "(src/core/memory_pool_manager.cpp missing) and no Vulkan stack exists on this box"
+)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="transformer",
+                    choices=["transformer", "wide_mlp", "cnn", "cnn_bf16", "mlp"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "torch", "reference"])
+    ap.add_argument("--no-graph", action="store_true", help="eager step instead of a captured CUDA graph")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--allreduce", default="nccl", choices=["fused", "nccl"],
+                    help="gradient path for N > 1 (ours): fused P2P all-reduce+optimizer or NCCL baseline")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.idx)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        mhz, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+# ---------------------------------------------------------------------------- distributed
+def init_dist(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus != world:
+        if world == 1 and args.gpus > 1:
+            raise SystemExit(f"--gpus {args.gpus} needs torchrun with {args.gpus} processes")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    return rank, local, world
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+_FLUSH = None
+
+
+def flush_l2():
+    global _FLUSH
+    if _FLUSH is None:
+        _FLUSH = torch.empty(64 << 20, dtype=torch.float32, device="cuda")  # 256 MB > 126 MB L2
+    _FLUSH.fill_(0.0)
+
+
+def metric_config(args, world, batch, seq):
+    cfg = {"model": args.config, "global_batch": batch * world, "per_gpu_batch": batch,
+           "parallelism": f"dp{world}", "l2": "flushed (256 MB write) between timed steps"}
+    if seq:
+        cfg["seq_len"] = seq
+    return cfg
+
+
+# ---------------------------------------------------------------------------- ours
+def run_ours(args, rank, local, world):
+    import dlvk_b200 as dl
+    from dlvk_b200 import _ext
+    from dlvk_b200.models import zoo
+    from dlvk_b200.training.step import TrainStep
+
+    C = _ext.C()
+    zc = zoo.CONFIGS[args.config]
+    name = "cnn" if args.config.startswith("cnn") else args.config
+    model = zoo.build(name, device=f"cuda:{local}", seed=0, dtype=zc.dtype)
+    opt = dl.Adam(1e-3) if zc.optimizer == "adam" else dl.SGD(0.01, momentum=0.9)
+    loss_fn = dl.CrossEntropyLoss()
+    seq = zc.seq_len
+    x_cpu, y_cpu = zoo.synthetic_batch(name, zc.batch, seed=1000 + rank, seq_len=seq or 512)
+    xs, ys = x_cpu.pin_memory(), y_cpu.pin_memory()
+
+    dp = None
+    if world > 1:
+        from dlvk_b200.parallel.data_parallel import DataParallel
+
+        dp = DataParallel(model, opt, mode=args.allreduce)
+    step = TrainStep(model, loss_fn, opt, dp=dp, graph=not args.no_graph)
+
+    # Device-side: inputs staged once into the step's static buffers.
+    step.stage(xs, ys)
+    for _ in range(args.warmup):
+        step.run_staged()
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    l0 = C.launch_count()
+    evs = []
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    for _ in range(args.steps):
+        flush_l2()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        step.run_staged()
+        e.record()
+        evs.append((s, e))
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    launches = C.launch_count() - l0 + step.graph_launches_per_step() * args.steps
+    clock = clocks.stop() if clocks else None
+    ms = sum(s.elapsed_time(e) for s, e in evs) / args.steps
+    ms = max_over_ranks(ms, world)
+    value = zc.batch * world / (ms / 1e3)
+
+    e2e = None
+    if not args.no_e2e:
+        # End to end through the public API: pinned host batch -> H2D -> step -> loss D2H.
+        for _ in range(2):
+            step(xs, ys).item()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(args.steps):
+            step(xs, ys).item()
+        e.record()
+        torch.cuda.synchronize()
+        ems = max_over_ranks(s.elapsed_time(e) / args.steps, world)
+        e2e = {"value": round(zc.batch * world / (ems / 1e3), 2), "unit": "samples/s",
+               "ms_per_step": round(ems, 4),
+               "h2d_bytes_per_step": int(xs.numel() * xs.element_size() + ys.numel() * ys.element_size()),
+               "d2h_bytes_per_step": 4}
+    out = {"metric": "train samples/s (device-timed, max/ranks)", "value": round(value, 2), "unit": "samples/s",
+           "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": zc.dtype, "data": "synthetic (shapes of the named config; random-init weights)",
+           "config": metric_config(args, world, zc.batch, seq), "impl": "ours",
+           "graph": not args.no_graph, "gpu_launches": int(launches), "e2e": e2e, "clocks": clock}
+    if dp is not None:
+        out["config"]["allreduce"] = dp.describe()
+        dp.close()
+    step.close()
+    return out
+
+
+# ---------------------------------------------------------------------------- torch baseline
+def run_torch(args, rank, local, world):
+    from dlvk_b200.bench.torch_models import build_torch
+
+    zc_name = args.config
+    model, opt, batch, seq, dtype, make_batch = build_torch(zc_name, local, rank)
+    if world > 1:
+        model = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local], bucket_cap_mb=64)
+    x, y = make_batch()
+    lossf = torch.nn.CrossEntropyLoss()
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16, enabled=(dtype == "bf16")):
+            out = model(x)
+            loss = lossf(out.reshape(-1, out.shape[-1]).float(), y.reshape(-1).long())
+        loss.backward()
+        opt.step()
+        return loss
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    evs = []
+    for _ in range(args.steps):
+        flush_l2()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        step()
+        e.record()
+        evs.append((s, e))
+    torch.cuda.synchronize()
+    barrier(world)
+    clock = clocks.stop() if clocks else None
+    ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in evs) / args.steps, world)
+    return {"metric": "train samples/s (device-timed, max/ranks)", "value": round(batch * world / (ms / 1e3), 2),
+            "unit": "samples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": dtype, "data": "synthetic", "config": metric_config(args, world, batch, seq),
+            "impl": "torch", "clocks": clock}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"impl": "reference", "unavailable": REFERENCE_UNAVAILABLE}), flush=True)
+        return 0
+    rank, local, world = init_dist(args)
+    try:
+        res = run_ours(args, rank, local, world) if args.impl == "ours" else run_torch(args, rank, local, world)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,48 @@
+"""Device timing helpers for the kernel micro-benchmarks (CUDA events on the
+launching stream, warm-up, L2 flush between timed iterations)."""
+from __future__ import annotations
+
+import json
+import torch
+
+_FLUSH = None
+
+
+def flush_l2(nbytes: int = 256 << 20) -> None:
+    """Overwrite a buffer larger than the 126 MB L2 so the next launch starts cold."""
+    global _FLUSH
+    if _FLUSH is None or _FLUSH.numel() * 4 < nbytes:
+        _FLUSH = torch.empty(nbytes // 4, dtype=torch.float32, device="cuda")
+    _FLUSH.fill_(1.0)
+
+
+def time_fn(fn, iters: int = 20, warmup: int = 3, flush: bool = True) -> float:
+    """Median device time of `fn()` in milliseconds."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        if flush:
+            flush_l2()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        times.append(s.elapsed_time(e))
+    times.sort()
+    return times[len(times) // 2]
+
+
+def measured_peaks() -> dict:
+    import os
+
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                        "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "fallback": True}

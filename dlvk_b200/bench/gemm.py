@@ -1,0 +1,69 @@
+"""GEMM micro-benchmark: the tcgen05 kernel against cuBLAS (torch.matmul) on
+the shapes of the transformer and wide-MLP training steps.
+
+    python -m dlvk_b200.bench.gemm [--shapes M,N,K ...] [--iters 20]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from dlvk_b200 import _ext
+from dlvk_b200.bench.common import measured_peaks, time_fn
+
+DEFAULT = [
+    # (M, N, K, a_major, b_major): 'k' = K-major, 'mn' = M/N-major
+    (8192, 3072, 1024, "k", "mn"),   # QKV projection  X @ W
+    (8192, 4096, 1024, "k", "mn"),   # FFN up
+    (8192, 1024, 4096, "k", "mn"),   # FFN down
+    (8192, 1024, 4096, "k", "k"),    # dX = dY @ W^T
+    (1024, 4096, 8192, "mn", "mn"),  # dW = X^T @ dY
+    (8192, 32000, 1024, "k", "mn"),  # vocab projection
+    (1024, 4096, 4096, "k", "mn"),   # wide MLP layer
+    (8192, 8192, 8192, "k", "mn"),
+]
+
+
+def make(M, N, K, am, bm):
+    a = torch.randn(M, K, device="cuda").bfloat16() if am == "k" else torch.randn(K, M, device="cuda").bfloat16().t()
+    b = torch.randn(K, N, device="cuda").bfloat16() if bm == "mn" else torch.randn(N, K, device="cuda").bfloat16().t()
+    return a, b
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--shapes", nargs="*", default=None)
+    ap.add_argument("--no-cublas", action="store_true")
+    ap.add_argument("--check", action="store_true")
+    args = ap.parse_args()
+    C = _ext.C()
+    shapes = DEFAULT
+    if args.shapes:
+        shapes = []
+        for s in args.shapes:
+            p = s.split(",")
+            shapes.append((int(p[0]), int(p[1]), int(p[2]), p[3] if len(p) > 3 else "k", p[4] if len(p) > 4 else "mn"))
+    peak = measured_peaks()["bf16_tflops"]
+    for (M, N, K, am, bm) in shapes:
+        a, b = make(M, N, K, am, bm)
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        flops = 2.0 * M * N * K
+        t_ours = time_fn(lambda: C.gemm(a, b, out=out, force_path=1), iters=args.iters)
+        rec = {"M": M, "N": N, "K": K, "a": am, "b": bm, "ours_ms": round(t_ours, 4),
+               "ours_tflops": round(flops / t_ours / 1e9, 1), "ours_frac_of_measured": round(flops / t_ours / 1e9 / peak, 3)}
+        if not args.no_cublas:
+            t_cb = time_fn(lambda: torch.matmul(a, b, out=out), iters=args.iters)
+            rec.update({"cublas_ms": round(t_cb, 4), "cublas_tflops": round(flops / t_cb / 1e9, 1),
+                        "speedup_vs_cublas": round(t_cb / t_ours, 3)})
+        if args.check:
+            ref = a.float() @ b.float()
+            C.gemm(a, b, out=out, force_path=1)
+            rec["max_rel_err"] = float((out.float() - ref).abs().max() / ref.abs().max())
+        print(json.dumps(rec), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -216,46 +216,62 @@ std::vector<at::Tensor> pointwise_loss_op(const at::Tensor& p, const at::Tensor&
 }
 
 // ---- GEMM ----
-// C = alpha * A @ B + beta * C + bias, act.  A: [M,K] or [b,M,K] (any strides
-// with one unit stride for the tensor-core path); B: [K,N] or [b,K,N].
-at::Tensor gemm_op(const at::Tensor& A, const at::Tensor& B, c10::optional<at::Tensor> bias, int64_t act,
-                   double alpha, double beta, c10::optional<at::Tensor> out, c10::optional<at::ScalarType> out_dtype,
-                   int64_t force_path, int64_t max_ctas) {
-  check_cuda(A, "A");
-  check_cuda(B, "B");
-  TORCH_CHECK(A.scalar_type() == B.scalar_type(), "dlvk.gemm: A and B must have the same dtype");
-  TORCH_CHECK(A.dim() == B.dim() && (A.dim() == 2 || A.dim() == 3), "dlvk.gemm: 2-D or 3-D operands");
-  c10::cuda::CUDAGuard g(A.device());
-  const bool batched = A.dim() == 3;
-  const int64_t batch = batched ? A.size(0) : 1;
-  TORCH_CHECK(!batched || B.size(0) == batch, "dlvk.gemm: batch mismatch");
-  const int64_t M = A.size(-2), K = A.size(-1), N = B.size(-1);
-  TORCH_CHECK(B.size(-2) == K, "dlvk.gemm: inner dims ", K, " vs ", B.size(-2));
-  at::Tensor C;
-  if (out.has_value()) {
-    C = *out;
-    TORCH_CHECK(C.size(-1) == N && C.size(-2) == M && C.stride(-1) == 1, "dlvk.gemm: bad out");
-  } else {
-    auto odt = out_dtype.value_or(A.scalar_type());
-    C = batched ? at::empty({batch, M, N}, A.options().dtype(odt)) : at::empty({M, N}, A.options().dtype(odt));
-    TORCH_CHECK(beta == 0.0, "dlvk.gemm: beta != 0 requires out");
-  }
+// C = act(alpha * A @ B + beta * C + bias + residual).  A: [M,K], [b,M,K] or
+// [b,b2,M,K] (any strides; one unit stride per operand for the tensor-core
+// path); B likewise [.., K, N].  Transposes and head splits are views.
+GemmArgs fill_args(const at::Tensor& A, const at::Tensor& B, const at::Tensor& C) {
   GemmArgs a;
+  const int nd = A.dim();
   a.A = A.data_ptr();
   a.B = B.data_ptr();
   a.C = C.data_ptr();
-  a.M = M;
-  a.N = N;
-  a.K = K;
+  a.M = A.size(-2);
+  a.K = A.size(-1);
+  a.N = B.size(-1);
   a.sam = A.stride(-2);
   a.sak = A.stride(-1);
   a.sbk = B.stride(-2);
   a.sbn = B.stride(-1);
   a.ldc = C.stride(-2);
-  a.batch = batch;
-  a.batch_stride_a = batched ? A.stride(0) : 0;
-  a.batch_stride_b = batched ? B.stride(0) : 0;
-  a.batch_stride_c = batched ? C.stride(0) : 0;
+  if (nd >= 3) {
+    a.batch = A.size(0);
+    a.batch_stride_a = A.stride(0);
+    a.batch_stride_b = B.stride(0);
+    a.batch_stride_c = C.stride(0);
+  }
+  if (nd == 4) {
+    a.batch2 = A.size(1);
+    a.batch2_stride_a = A.stride(1);
+    a.batch2_stride_b = B.stride(1);
+    a.batch2_stride_c = C.stride(1);
+  }
+  return a;
+}
+
+at::Tensor gemm_op(const at::Tensor& A, const at::Tensor& B, c10::optional<at::Tensor> bias, int64_t act,
+                   double alpha, double beta, c10::optional<at::Tensor> out, c10::optional<at::ScalarType> out_dtype,
+                   int64_t force_path, int64_t max_ctas, c10::optional<at::Tensor> residual) {
+  check_cuda(A, "A");
+  check_cuda(B, "B");
+  TORCH_CHECK(A.scalar_type() == B.scalar_type(), "dlvk.gemm: A and B must have the same dtype");
+  TORCH_CHECK(A.dim() == B.dim() && A.dim() >= 2 && A.dim() <= 4, "dlvk.gemm: 2-D, 3-D or 4-D operands");
+  c10::cuda::CUDAGuard g(A.device());
+  const int nd = A.dim();
+  for (int i = 0; i < nd - 2; ++i) TORCH_CHECK(A.size(i) == B.size(i), "dlvk.gemm: batch mismatch");
+  const int64_t M = A.size(-2), K = A.size(-1), N = B.size(-1);
+  TORCH_CHECK(B.size(-2) == K, "dlvk.gemm: inner dims ", K, " vs ", B.size(-2));
+  at::Tensor C;
+  if (out.has_value()) {
+    C = *out;
+    TORCH_CHECK(C.dim() == nd && C.size(-1) == N && C.size(-2) == M && C.stride(-1) == 1, "dlvk.gemm: bad out");
+  } else {
+    auto odt = out_dtype.value_or(A.scalar_type());
+    std::vector<int64_t> shp(A.sizes().begin(), A.sizes().end());
+    shp.back() = N;
+    C = at::empty(shp, A.options().dtype(odt));
+    TORCH_CHECK(beta == 0.0, "dlvk.gemm: beta != 0 requires out");
+  }
+  GemmArgs a = fill_args(A, B, C);
   a.alpha = (float)alpha;
   a.beta = (float)beta;
   at::Tensor bc;
@@ -265,13 +281,24 @@ at::Tensor gemm_op(const at::Tensor& A, const at::Tensor& B, c10::optional<at::T
     a.bias = bc.data_ptr();
     a.bias_dtype = (int)to_dtype(bc);
   }
+  if (residual.has_value()) {
+    const auto& R = *residual;
+    TORCH_CHECK(R.scalar_type() == C.scalar_type() && R.dim() == nd && R.size(-1) == N && R.size(-2) == M &&
+                    R.stride(-1) == 1,
+                "dlvk.gemm: residual must match the output's dtype/shape with unit column stride");
+    a.residual = R.data_ptr();
+    a.ldr = R.stride(-2);
+    if (nd >= 3) a.batch_stride_r = R.stride(0);
+    if (nd == 4) a.batch2_stride_r = R.stride(1);
+  }
   a.act = (int)act;
   if (M == 0 || N == 0) return C;
   if (K == 0) {
-    // Degenerate: C = beta*C + bias, act.  Rare; do it with ATen.
+    // Degenerate: C = act(beta*C + bias + residual).  Rare; do it with ATen.
     if (beta == 0.0) C.zero_();
     else C.mul_(beta);
     if (bias.has_value()) C.add_(bc.to(C.scalar_type()));
+    if (residual.has_value()) C.add_(*residual);
     if (act == ACT_RELU) C.relu_();
     return C;
   }
@@ -289,20 +316,8 @@ at::Tensor gemm_op(const at::Tensor& A, const at::Tensor& B, c10::optional<at::T
 
 bool gemm_tc_ok(const at::Tensor& A, const at::Tensor& B) {
   if (A.scalar_type() != at::kBFloat16 || B.scalar_type() != at::kBFloat16) return false;
-  if (A.dim() != B.dim() || A.dim() < 2) return false;
-  GemmArgs a;
-  a.A = A.data_ptr();
-  a.B = B.data_ptr();
-  a.M = A.size(-2);
-  a.K = A.size(-1);
-  a.N = B.size(-1);
-  a.sam = A.stride(-2);
-  a.sak = A.stride(-1);
-  a.sbk = B.stride(-2);
-  a.sbn = B.stride(-1);
-  a.batch = A.dim() == 3 ? A.size(0) : 1;
-  a.batch_stride_a = A.dim() == 3 ? A.stride(0) : 0;
-  a.batch_stride_b = B.dim() == 3 ? B.stride(0) : 0;
+  if (A.dim() != B.dim() || A.dim() < 2 || A.dim() > 4) return false;
+  GemmArgs a = fill_args(A, B, A);
   return gemm_tc_supported(a);
 }
 
@@ -378,7 +393,7 @@ void register_ops(py::module& m) {
   m.def("pointwise_loss", &pointwise_loss_op);
   m.def("gemm", &gemm_op, py::arg("A"), py::arg("B"), py::arg("bias") = py::none(), py::arg("act") = 0,
         py::arg("alpha") = 1.0, py::arg("beta") = 0.0, py::arg("out") = py::none(), py::arg("out_dtype") = py::none(),
-        py::arg("force_path") = 0, py::arg("max_ctas") = 0);
+        py::arg("force_path") = 0, py::arg("max_ctas") = 0, py::arg("residual") = py::none());
   m.def("gemm_tc_ok", &gemm_tc_ok);
   m.def("optim_advance", &optim_advance_op);
   m.def("optim_update", &optim_update_op, py::arg("kind"), py::arg("hyper"), py::arg("p"), py::arg("grad"),
@@ -388,6 +403,18 @@ void register_ops(py::module& m) {
   m.def("grad_stats_scratch_floats", &grad_stats_scratch_floats);
   m.def("scaler_update", &scaler_update_op);
   m.def("optim_hyper_bytes", &optim_hyper_bytes);
+  m.def("memset_zero", [](const at::Tensor& t) {
+    check_cuda(t, "t");
+    TORCH_CHECK(t.is_contiguous(), "memset_zero: contiguous tensor");
+    c10::cuda::CUDAGuard g(t.device());
+    DLVK_CUDA_CHECK(cudaMemsetAsync(t.data_ptr(), 0, t.numel() * t.element_size(), stream()));
+  });
+  m.def("counter_add", [](const at::Tensor& c, int64_t delta) {
+    check_cuda(c, "counter");
+    TORCH_CHECK(c.scalar_type() == at::kLong, "counter must be int64");
+    c10::cuda::CUDAGuard g(c.device());
+    counter_add(c.data_ptr<int64_t>(), delta, stream());
+  });
   m.def("launch_count", []() { return (int64_t)launch_count(); });
   m.def("read_device_error", [](bool clear) { return (int64_t)read_device_error(clear); }, py::arg("clear") = true);
 }

@@ -3,8 +3,8 @@
 
 namespace dlvk {
 namespace bind {
-void register_runtime(py::module&) {}
-void register_nn(py::module&) {}
+
+
 void register_comm(py::module&) {}
 }  // namespace bind
 }  // namespace dlvk

@@ -47,8 +47,10 @@ void sum_rows_to_scalar(const float* rows_vals, int64_t n, float scale, float* o
 
 // ---- GEMM -------------------------------------------------------------------
 enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU = 2 };
-// C[b](m, n) = alpha * sum_k A[b](m, k) * B[b](k, n) + beta * C[b](m, n) + bias[n], then act.
+// C[b](m, n) = act(alpha * sum_k A[b](m, k) * B[b](k, n) + beta * C[b](m, n) + bias[n] + R[b](m, n))
 // A(m,k) = A[m*sam + k*sak]; B(k,n) = B[k*sbk + n*sbn]; C(m,n) = C[m*ldc + n].
+// Batches are two-level: b = (bo, bi), bo < batch, bi < batch2, with
+// independent strides per level (e.g. (batch, head) of an attention tensor).
 struct GemmArgs {
   const void* A = nullptr;
   const void* B = nullptr;
@@ -56,10 +58,13 @@ struct GemmArgs {
   int64_t M = 0, N = 0, K = 0;
   int64_t sam = 0, sak = 0, sbk = 0, sbn = 0, ldc = 0;
   int64_t batch = 1, batch_stride_a = 0, batch_stride_b = 0, batch_stride_c = 0;
+  int64_t batch2 = 1, batch2_stride_a = 0, batch2_stride_b = 0, batch2_stride_c = 0;
   float alpha = 1.f, beta = 0.f;
   const void* bias = nullptr;
   int bias_dtype = 0;
   int act = ACT_NONE;
+  const void* residual = nullptr;  // same dtype as C, added before act
+  int64_t ldr = 0, batch_stride_r = 0, batch2_stride_r = 0;
 };
 void gemm_simt(DType in_dt, DType out_dt, const GemmArgs& a, cudaStream_t s);
 bool gemm_tc_supported(const GemmArgs& a);
@@ -94,8 +99,62 @@ void grad_stats(const void* g, DType g_dt, int64_t n, float scale, float max_nor
 void scaler_update(float* scale, int* good_steps, const int* found_inf, float growth, float backoff, int interval,
                    float smin, float smax, float* inv_scale, cudaStream_t s);
 
+// ---- convolution / pooling ---------------------------------------------------
+struct ConvDesc {
+  int N, Cin, H, W, Cout, KH, KW, stride, pad, Ho, Wo;
+};
+void conv2d_fwd(DType dt, const void* x, const void* w, const float* bias, void* y, const ConvDesc& d, bool relu,
+                cudaStream_t s);
+// relu_src (optional): the forward input of the preceding ReLU (or its output);
+// dx is zeroed where relu_src <= 0, fusing that activation's backward.
+void conv2d_dgrad(DType dt, const void* g, const void* w, void* dx, const void* relu_src, const ConvDesc& d,
+                  cudaStream_t s);
+int conv2d_wgrad_chunks(const ConvDesc& d);
+int64_t conv2d_wgrad_scratch_floats(const ConvDesc& d);
+void conv2d_wgrad(DType dt, const void* x, const void* g, float* dw, float* db, bool accumulate, const ConvDesc& d,
+                  float* scratch, cudaStream_t s);
+void maxpool2d_fwd(DType dt, const void* x, void* y, int32_t* idx, int64_t planes, int H, int W, int k, int stride,
+                   cudaStream_t s);
+void maxpool2d_bwd(DType dt, const void* g, const int32_t* idx, void* dx, int64_t planes, int H, int W, int k,
+                   int stride, cudaStream_t s);
+void avgpool2d_fwd(DType dt, const void* x, void* y, int64_t planes, int H, int W, int k, int stride, int pad,
+                   cudaStream_t s);
+void avgpool2d_bwd(DType dt, const void* g, void* dx, int64_t planes, int H, int W, int k, int stride, int pad,
+                   cudaStream_t s);
+
+// ---- normalisation / dropout / embedding -------------------------------------
+// Philox dropout stream: key = seed, counter = {element/4, stream, step}.
+struct DropoutDesc {
+  float p = 0.f;                  // drop probability (0 = disabled)
+  uint32_t stream = 0;            // distinct per dropout site
+  uint64_t seed = 0;
+  uint32_t step = 0;              // used when step_ptr is null
+  const int64_t* step_ptr = nullptr;  // device step counter (graph replays)
+};
+void batchnorm_fwd(DType dt, const void* x, const float* gamma, const float* beta, void* y, float* mean, float* rstd,
+                   float* run_mean, float* run_var, int N, int C, int S, float momentum, float eps, bool training,
+                   bool relu, const DropoutDesc& dd, cudaStream_t s);
+// scratch: 2*C floats
+void batchnorm_bwd(DType dt, const void* x, const void* dy, const float* mean, const float* rstd, const float* gamma,
+                   const float* beta, void* dx, float* dgamma, float* dbeta, bool accumulate, int N, int C, int S,
+                   bool relu, const DropoutDesc& dd, float* scratch, cudaStream_t s);
+void layernorm_fwd(DType dt, const void* x, const float* gamma, const float* beta, void* y, float* mean, float* rstd,
+                   int64_t rows, int D, float eps, cudaStream_t s);
+int layernorm_bwd_blocks(int64_t rows);
+int64_t layernorm_bwd_scratch_floats(int64_t rows, int D);
+void layernorm_bwd(DType dt, const void* x, const float* gamma, const float* mean, const float* rstd, const void* dy,
+                   void* dx, float* dgamma, float* dbeta, bool accumulate, int64_t rows, int D, float* scratch,
+                   cudaStream_t s);
+void dropout(DType dt, const void* x, void* y, int64_t n, const DropoutDesc& dd, cudaStream_t s);
+void embedding_fwd(DType dt, const int32_t* ids, const void* table, void* out, int64_t n, int64_t V, int D,
+                   cudaStream_t s);
+// dtable must be zeroed (or hold the gradient to accumulate into).
+void embedding_bwd(DType dt, const int32_t* ids, const void* dy, float* dtable, int64_t n, int64_t V, int D,
+                   cudaStream_t s);
+
 // ---- device error word -------------------------------------------------------
 uint32_t* device_error_word();     // per current device, zero-initialised
 uint32_t read_device_error(bool clear);
+void counter_add(int64_t* c, int64_t delta, cudaStream_t s);
 
 }  // namespace dlvk

@@ -20,9 +20,12 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs a) {
   __shared__ float As[BK][BM + 4];
   __shared__ float Bs[BK][BN + 4];
   const int64_t bz = blockIdx.z;
-  const TA* A = reinterpret_cast<const TA*>(a.A) + bz * a.batch_stride_a;
-  const TA* B = reinterpret_cast<const TA*>(a.B) + bz * a.batch_stride_b;
-  TC* C = reinterpret_cast<TC*>(a.C) + bz * a.batch_stride_c;
+  const int64_t bo = bz / a.batch2, bi = bz - bo * a.batch2;
+  const TA* A = reinterpret_cast<const TA*>(a.A) + bo * a.batch_stride_a + bi * a.batch2_stride_a;
+  const TA* B = reinterpret_cast<const TA*>(a.B) + bo * a.batch_stride_b + bi * a.batch2_stride_b;
+  TC* C = reinterpret_cast<TC*>(a.C) + bo * a.batch_stride_c + bi * a.batch2_stride_c;
+  const TC* R = a.residual ? reinterpret_cast<const TC*>(a.residual) + bo * a.batch_stride_r + bi * a.batch2_stride_r
+                           : nullptr;
   const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // 16 x 16 threads
   float acc[4][4] = {};
@@ -72,6 +75,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs a) {
         v += (a.bias_dtype == (int)DType::F32) ? reinterpret_cast<const float*>(a.bias)[gn]
                                                : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.bias)[gn]);
       }
+      if (R) v += to_f32(R[gm * a.ldr + gn]);
       if (a.act == ACT_RELU) v = fmaxf(v, 0.f);
       else if (a.act == ACT_GELU) v = 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
       *cp = from_f32<TC>(v);
@@ -83,7 +87,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs a) {
 
 void gemm_simt(DType in_dt, DType out_dt, const GemmArgs& a, cudaStream_t s) {
   if (a.M == 0 || a.N == 0) return;
-  dim3 grid((unsigned)((a.N + BN - 1) / BN), (unsigned)((a.M + BM - 1) / BM), (unsigned)a.batch);
+  dim3 grid((unsigned)((a.N + BN - 1) / BN), (unsigned)((a.M + BM - 1) / BM), (unsigned)(a.batch * a.batch2));
   if (in_dt == DType::F32 && out_dt == DType::F32)
     gemm_simt_kernel<float, float><<<grid, 256, 0, s>>>(a);
   else if (in_dt == DType::BF16 && out_dt == DType::BF16)

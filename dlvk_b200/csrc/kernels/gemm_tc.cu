@@ -36,11 +36,14 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // bf16 elements per 128-byte swizzle row
 
 struct TcParams {
-  int M, N, K, batch;
+  int M, N, K, batch;  // batch = number of (outer, inner) pairs
+  int batch2;          // inner batch count
   int tiles_m, tiles_n;
   int a_mn, b_mn;
   void* C;
-  int64_t ldc, bsc;
+  int64_t ldc, bsc, bsc2;
+  const void* R;       // residual (same dtype as C) or null
+  int64_t ldr, bsr, bsr2;
   int out_f32;
   int vec_ok;
   float alpha, beta;
@@ -62,7 +65,7 @@ struct Cfg {
 
 __device__ __forceinline__ void tile_coords(int t, const TcParams& p, int& tm, int& tn, int& b) {
   const int per_batch = p.tiles_m * p.tiles_n;
-  b = t / per_batch;
+  b = t / per_batch;  // combined batch index; (outer, inner) = (b / batch2, b % batch2)
   const int r = t - b * per_batch;
   constexpr int GROUP_M = 8;
   const int in_group = GROUP_M * p.tiles_n;
@@ -126,22 +129,25 @@ __global__ void __launch_bounds__(192, 1)
       for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
         int tm, tn, b;
         tile_coords(t, p, tm, tn, b);
+        const int bo = b / p.batch2, bi = b - bo * p.batch2;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.err)) goto producer_done;
           uint8_t* sA = smem + stage * C::STAGE_BYTES;
           uint8_t* sB = sA + C::A_BYTES;
           mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
           if (!p.a_mn) {
-            tma_load_3d(sA, &tmA, &full[stage], kb * BK, tm * BM, b);
+            tma_load_4d(sA, &tmA, &full[stage], kb * BK, tm * BM, bi, bo);
           } else {
 #pragma unroll
-            for (int j = 0; j < BM / 64; ++j) tma_load_3d(sA + j * 8192, &tmA, &full[stage], tm * BM + j * 64, kb * BK, b);
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_4d(sA + j * 8192, &tmA, &full[stage], tm * BM + j * 64, kb * BK, bi, bo);
           }
           if (!p.b_mn) {
-            tma_load_3d(sB, &tmB, &full[stage], kb * BK, tn * BN, b);
+            tma_load_4d(sB, &tmB, &full[stage], kb * BK, tn * BN, bi, bo);
           } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_3d(sB + j * 8192, &tmB, &full[stage], tn * BN + j * 64, kb * BK, b);
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_4d(sB + j * 8192, &tmB, &full[stage], tn * BN + j * 64, kb * BK, bi, bo);
           }
           if (++stage == C::STAGES) {
             stage = 0;
@@ -202,7 +208,9 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const int row = tm * BM + q * 32 + lane;
       const bool row_ok = row < p.M;
-      const int64_t cbase = (int64_t)b * p.bsc + (int64_t)row * p.ldc;
+      const int bo = b / p.batch2, bi = b - bo * p.batch2;
+      const int64_t cbase = (int64_t)bo * p.bsc + (int64_t)bi * p.bsc2 + (int64_t)row * p.ldc;
+      const int64_t rbase = (int64_t)bo * p.bsr + (int64_t)bi * p.bsr2 + (int64_t)row * p.ldr;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -230,6 +238,14 @@ __global__ void __launch_bounds__(192, 1)
             if (n0 + j < p.N)
               v[j] += p.bias_f32 ? reinterpret_cast<const float*>(p.bias)[n0 + j]
                                  : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.bias)[n0 + j]);
+          }
+        }
+        if (p.R) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (n0 + j < p.N)
+              v[j] += p.out_f32 ? reinterpret_cast<const float*>(p.R)[rbase + n0 + j]
+                                : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.R)[rbase + n0 + j]);
           }
         }
         if (p.act != ACT_NONE) {
@@ -297,16 +313,17 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 3-D bf16 tensor map: dims {d0 (contiguous), d1, d2}, strides in elements for
-// d1 and d2, box {64, box1, 1}, 128-byte swizzle, zero fill out of bounds.
-CUtensorMap make_tmap_bf16(const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1, uint64_t s2,
-                           uint32_t box1) {
+// 4-D bf16 tensor map: dims {d0 (contiguous), d1, inner batch, outer batch},
+// strides in elements, box {64, box1, 1, 1}, 128-byte swizzle, zero fill out
+// of bounds.
+CUtensorMap make_tmap_bf16(const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t d3, uint64_t s1,
+                           uint64_t s2, uint64_t s3, uint32_t box1) {
   CUtensorMap m;
-  cuuint64_t dims[3] = {d0, d1, d2};
-  cuuint64_t strides[2] = {s1 * 2, s2 * 2};
-  cuuint32_t box[3] = {64, box1, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+  cuuint64_t dims[4] = {d0, d1, d2, d3};
+  cuuint64_t strides[3] = {s1 * 2, s2 * 2, s3 * 2};
+  cuuint32_t box[4] = {64, box1, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw std::runtime_error("dlvk: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
@@ -349,6 +366,8 @@ bool gemm_tc_supported(const GemmArgs& a) {
   const int64_t ldb = b_k ? a.sbn : a.sbk;
   if ((lda * 2) % 16 || (ldb * 2) % 16) return false;
   if (a.batch > 1 && ((a.batch_stride_a * 2) % 16 || (a.batch_stride_b * 2) % 16)) return false;
+  if (a.batch2 > 1 && ((a.batch2_stride_a * 2) % 16 || (a.batch2_stride_b * 2) % 16)) return false;
+  if (a.batch * a.batch2 * ((a.M + 127) / 128) * ((a.N + 127) / 128) > (1LL << 31) - 1) return false;
   if (!al16(a.A) || !al16(a.B)) return false;
   if (a.M < 1 || a.N < 16 || a.K < 1) return false;
   if (a.M > (1LL << 31) - 1 || a.N > (1LL << 31) - 1 || a.K > (1LL << 31) - 1) return false;
@@ -361,27 +380,33 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
   const bool a_k = (a.sak == 1);
   const bool b_k = (a.sbk == 1);
   const int BN = (a.N >= 256) ? 256 : 128;
-  const uint64_t batch = (uint64_t)a.batch;
+  // Unused batch levels get a harmless stride (a multiple of 16 bytes).
+  auto pick = [](int64_t cnt, int64_t stride, uint64_t dflt) { return cnt > 1 ? (uint64_t)stride : dflt; };
   CUtensorMap ta, tb;
   if (a_k) {
-    const uint64_t bs = a.batch > 1 ? (uint64_t)a.batch_stride_a : (uint64_t)a.sam * (uint64_t)a.M;
-    ta = make_tmap_bf16(a.A, a.K, a.M, batch, a.sam, bs, BM);
+    const uint64_t d = (uint64_t)a.sam * (uint64_t)a.M;
+    ta = make_tmap_bf16(a.A, a.K, a.M, a.batch2, a.batch, a.sam, pick(a.batch2, a.batch2_stride_a, d),
+                        pick(a.batch, a.batch_stride_a, d), BM);
   } else {
-    const uint64_t bs = a.batch > 1 ? (uint64_t)a.batch_stride_a : (uint64_t)a.sak * (uint64_t)a.K;
-    ta = make_tmap_bf16(a.A, a.M, a.K, batch, a.sak, bs, 64);
+    const uint64_t d = (uint64_t)a.sak * (uint64_t)a.K;
+    ta = make_tmap_bf16(a.A, a.M, a.K, a.batch2, a.batch, a.sak, pick(a.batch2, a.batch2_stride_a, d),
+                        pick(a.batch, a.batch_stride_a, d), 64);
   }
   if (b_k) {
-    const uint64_t bs = a.batch > 1 ? (uint64_t)a.batch_stride_b : (uint64_t)a.sbn * (uint64_t)a.N;
-    tb = make_tmap_bf16(a.B, a.K, a.N, batch, a.sbn, bs, BN);
+    const uint64_t d = (uint64_t)a.sbn * (uint64_t)a.N;
+    tb = make_tmap_bf16(a.B, a.K, a.N, a.batch2, a.batch, a.sbn, pick(a.batch2, a.batch2_stride_b, d),
+                        pick(a.batch, a.batch_stride_b, d), BN);
   } else {
-    const uint64_t bs = a.batch > 1 ? (uint64_t)a.batch_stride_b : (uint64_t)a.sbk * (uint64_t)a.K;
-    tb = make_tmap_bf16(a.B, a.N, a.K, batch, a.sbk, bs, 64);
+    const uint64_t d = (uint64_t)a.sbk * (uint64_t)a.K;
+    tb = make_tmap_bf16(a.B, a.N, a.K, a.batch2, a.batch, a.sbk, pick(a.batch2, a.batch2_stride_b, d),
+                        pick(a.batch, a.batch_stride_b, d), 64);
   }
   TcParams p{};
   p.M = (int)a.M;
   p.N = (int)a.N;
   p.K = (int)a.K;
-  p.batch = (int)a.batch;
+  p.batch = (int)(a.batch * a.batch2);
+  p.batch2 = (int)a.batch2;
   p.tiles_m = (int)((a.M + BM - 1) / BM);
   p.tiles_n = (int)((a.N + BN - 1) / BN);
   p.a_mn = a_k ? 0 : 1;
@@ -389,9 +414,15 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
   p.C = a.C;
   p.ldc = a.ldc;
   p.bsc = a.batch_stride_c;
+  p.bsc2 = a.batch2_stride_c;
+  p.R = a.residual;
+  p.ldr = a.ldr;
+  p.bsr = a.batch_stride_r;
+  p.bsr2 = a.batch2_stride_r;
   p.out_f32 = (out_dt == DType::F32);
   const int esz = p.out_f32 ? 4 : 2;
-  p.vec_ok = al16(a.C) && ((a.ldc * esz) % 16 == 0) && ((a.batch_stride_c * esz) % 16 == 0);
+  p.vec_ok = al16(a.C) && ((a.ldc * esz) % 16 == 0) && ((a.batch_stride_c * esz) % 16 == 0) &&
+             ((a.batch2_stride_c * esz) % 16 == 0);
   p.alpha = a.alpha;
   p.beta = a.beta;
   p.bias = a.bias;

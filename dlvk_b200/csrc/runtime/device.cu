@@ -47,3 +47,17 @@ uint32_t read_device_error(bool clear) {
 }
 
 }  // namespace dlvk
+
+namespace dlvk {
+namespace {
+__global__ void counter_add_kernel(int64_t* c, int64_t delta) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) *c += delta;
+}
+}  // namespace
+
+// Device-side step counter bump (RNG step for dropout; captured into graphs).
+void counter_add(int64_t* c, int64_t delta, cudaStream_t s) {
+  counter_add_kernel<<<1, 32, 0, s>>>(c, delta);
+  DLVK_POST_LAUNCH();
+}
+}  // namespace dlvk

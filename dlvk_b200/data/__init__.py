@@ -1,0 +1,1 @@
+"""dlvk_b200 subpackage."""

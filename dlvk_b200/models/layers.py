@@ -1,0 +1,613 @@
+"""Layers with the reference's public surface.
+
+`ModernLayer` mirrors include/dlvk/layers/modern_layer.h:27-77 (forward,
+backward, clone, update_parameters, set_training, get_layer_info,
+save_weights/load_weights).  The legacy `Layer` names (DenseLayer,
+Conv2DLayer, ...; include/dlvk/layers/*.h) are the concrete classes here, and
+the adapter names of include/dlvk/layers/layer_adapters.h are aliases: both
+styles run the same kernels, so no adapter (and none of its deep copies) is
+needed.
+
+Weights are initialised from a seeded generator (the reference drew from
+std::random_device, e.g. src/layers/dense_layer.cpp:85-88) with the same
+distributions: Xavier-normal sigma = sqrt(2 / (fan_in + fan_out)).
+"""
+from __future__ import annotations
+
+import copy
+import enum
+import io
+import math
+import struct
+from dataclasses import dataclass
+from typing import List, Optional
+
+import torch
+
+from ..ops import core as K
+from ..ops import functional as Fn
+from ..ops import nn as NN
+from .params import Parameter, ParamStore
+from .. import runtime
+
+_GEN = torch.Generator().manual_seed(0)
+
+
+def manual_seed(seed: int) -> None:
+    """Seed the generator used for weight initialisation."""
+    _GEN.manual_seed(int(seed))
+
+
+def _normal(shape, std: float) -> torch.Tensor:
+    return torch.randn(*shape, generator=_GEN) * std
+
+
+@dataclass
+class LayerInfo:
+    type: str
+    output_shape_str: str = ""
+    parameter_count: int = 0
+    trainable: bool = False
+
+
+class ActivationType(enum.Enum):
+    ReLU = "relu"
+    Sigmoid = "sigmoid"
+    Tanh = "tanh"
+    Softmax = "softmax"
+    GELU = "gelu"
+    Linear = "linear"
+
+
+class ModernLayer:
+    """Base class.  Subclasses implement `_forward(x)` with autograd-tracked
+    ops and register parameters with `_param`."""
+
+    type_name = "Layer"
+
+    def __init__(self):
+        self._params: List[Parameter] = []
+        self._children: List["ModernLayer"] = []
+        self.training = True
+        self.track = True          # standalone use: cache input/output for backward()
+        self._last_in = None
+        self._last_out = None
+        self.device_ctx: Optional[runtime.CudaDevice] = None
+        self.compute_dtype = torch.float32
+        self._store: Optional[ParamStore] = None
+        self.output_shape = None
+
+    # -- parameters -----------------------------------------------------------
+    def _param(self, name: str, init: torch.Tensor, decay: bool = True) -> Parameter:
+        p = Parameter(f"{self.type_name.lower()}.{name}", init.shape, init, decay)
+        self._params.append(p)
+        return p
+
+    def _child(self, layer: "ModernLayer") -> "ModernLayer":
+        self._children.append(layer)
+        return layer
+
+    def parameters(self) -> List[Parameter]:
+        out = list(self._params)
+        for c in self._children:
+            out.extend(c.parameters())
+        return out
+
+    def parameter_count(self) -> int:
+        return sum(p.numel for p in self.parameters())
+
+    def bind_runtime(self, dev: runtime.CudaDevice, dtype) -> None:
+        """Attach the device context (RNG step counter, dtype) recursively."""
+        self.device_ctx = dev
+        self.compute_dtype = dtype
+        for c in self._children:
+            c.bind_runtime(dev, dtype)
+        self._on_bind()
+
+    def _on_bind(self) -> None:
+        pass
+
+    def to(self, device=None, dtype=torch.float32) -> "ModernLayer":
+        """Standalone placement: packs this layer's parameters into a private store."""
+        dev = runtime.get_device(device)
+        self.bind_runtime(dev, dtype)
+        if self.parameters():
+            self._store = ParamStore(self.parameters(), dev.device, dtype)
+        return self
+
+    def _ensure_placed(self, x: torch.Tensor) -> None:
+        if self.device_ctx is None:
+            self.to(x.device, x.dtype if x.is_floating_point() else torch.float32)
+
+    # -- ModernLayer API --------------------------------------------------------
+    def forward(self, x):
+        from ..tensor import Tensor as FacadeTensor
+
+        facade = isinstance(x, FacadeTensor)
+        if facade:
+            x = x.data
+        self._ensure_placed(x)
+        if self.track:
+            if x.is_floating_point() and not x.requires_grad:
+                x = x.detach().requires_grad_(True)
+            self._last_in = x
+        with torch.enable_grad() if self.track else _nullctx():
+            y = self._forward(x)
+        if self.track:
+            self._last_out = y
+        self.output_shape = tuple(y.shape)
+        return FacadeTensor.wrap(y) if facade else y
+
+    __call__ = forward
+
+    def _forward(self, x):  # pragma: no cover - abstract
+        raise NotImplementedError
+
+    def backward(self, grad_output):
+        """Gradient w.r.t. this layer's last input; parameter gradients land
+        in their grad buffers (reference ModernLayer::backward)."""
+        from ..tensor import Tensor as FacadeTensor
+
+        facade = isinstance(grad_output, FacadeTensor)
+        g = grad_output.data if facade else grad_output
+        if self._last_out is None:
+            raise RuntimeError("backward() called before forward()")
+        if self._store is not None:
+            self._store.zero_grad()
+        if self._last_in is not None and self._last_in.requires_grad:
+            (dx,) = torch.autograd.grad(self._last_out, self._last_in, g.to(self._last_out.dtype),
+                                        allow_unused=True)
+        else:
+            torch.autograd.backward(self._last_out, g.to(self._last_out.dtype))
+            dx = None
+        return FacadeTensor.wrap(dx) if (facade and dx is not None) else dx
+
+    def update_parameters(self, optimizer) -> None:
+        optimizer.update_parameters(self.parameters())
+
+    def set_training(self, training: bool) -> None:
+        self.training = bool(training)
+        for c in self._children:
+            c.set_training(training)
+
+    def get_layer_info(self) -> LayerInfo:
+        shp = "x".join(str(s) for s in self.output_shape) if self.output_shape else "?"
+        n = self.parameter_count()
+        return LayerInfo(self.type_name, shp, n, n > 0)
+
+    def clone(self) -> "ModernLayer":
+        c = copy.copy(self)
+        c.__dict__ = dict(self.__dict__)
+        c._params = []
+        mapping = {}
+        for p in self._params:
+            q = Parameter(p.name, p.shape, p.master.detach().cpu().clone(), p.decay)
+            mapping[id(p)] = q
+            c._params.append(q)
+        for k, v in list(c.__dict__.items()):
+            if isinstance(v, Parameter) and id(v) in mapping:
+                c.__dict__[k] = mapping[id(v)]
+        c._children = [ch.clone() for ch in self._children]
+        for k, v in list(c.__dict__.items()):
+            if isinstance(v, ModernLayer) and v in self._children:
+                c.__dict__[k] = c._children[self._children.index(v)]
+        for k in ("running_mean", "running_var"):
+            if k in c.__dict__ and isinstance(c.__dict__[k], torch.Tensor):
+                c.__dict__[k] = c.__dict__[k].detach().clone()
+        c._store = None
+        c.device_ctx = None
+        c._last_in = c._last_out = None
+        return c
+
+    # Weight stream format: u32 count, then per tensor u32 nbytes + raw fp32.
+    def state_tensors(self):
+        out = [(p.name, p.master) for p in self._params]
+        for c in self._children:
+            out.extend(c.state_tensors())
+        return out + self._buffers()
+
+    def _buffers(self):
+        return []
+
+    def save_weights(self, f) -> None:
+        ts = self.state_tensors()
+        f.write(struct.pack("<I", len(ts)))
+        for _, t in ts:
+            b = t.detach().float().contiguous().cpu().numpy().tobytes()
+            f.write(struct.pack("<Q", len(b)))
+            f.write(b)
+
+    def load_weights(self, f) -> None:
+        ts = self.state_tensors()
+        (n,) = struct.unpack("<I", f.read(4))
+        if n != len(ts):
+            raise ValueError(f"{self.type_name}: expected {len(ts)} tensors, file has {n}")
+        for _, t in ts:
+            (nb,) = struct.unpack("<Q", f.read(8))
+            src = torch.frombuffer(bytearray(f.read(nb)), dtype=torch.float32).reshape(t.shape)
+            t.copy_(src.to(t.device, t.dtype))
+        self._sync_values()
+
+    def _sync_values(self) -> None:
+        stores = {id(p.store): p.store for p in self.parameters() if p.store is not None}
+        for s in stores.values():
+            s.sync_value()
+
+    def summary_line(self) -> str:
+        info = self.get_layer_info()
+        return f"{info.type:<24}{info.output_shape_str:<24}{info.parameter_count:>12}"
+
+
+class _nullctx:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+# ============================================================== layers
+class DenseLayer(ModernLayer):
+    """y = x W + b, W [in, out] (src/layers/dense_layer.cpp:16-42)."""
+
+    type_name = "Dense"
+
+    def __init__(self, input_size: int, output_size: int, use_bias: bool = True, activation: Optional[str] = None,
+                 init_std: Optional[float] = None):
+        super().__init__()
+        self.input_size, self.output_size = int(input_size), int(output_size)
+        std = init_std if init_std is not None else math.sqrt(2.0 / (self.input_size + self.output_size))
+        self.weight = self._param("weight", _normal((self.input_size, self.output_size), std))
+        self.bias = self._param("bias", torch.zeros(self.output_size), decay=False) if use_bias else None
+        self.activation = activation
+        self._act = K.ACT_BY_NAME[activation]
+
+    def _forward(self, x, act=None, residual=None):
+        a = self._act if act is None else act
+        if x.dtype != self.compute_dtype:
+            x = x.to(self.compute_dtype)
+        return Fn.dense(x, self.weight, self.bias, a, residual)
+
+
+class Conv2DLayer(ModernLayer):
+    """NCHW convolution, weight [Cout, Cin, KH, KW] (src/layers/conv2d_layer.cpp)."""
+
+    type_name = "Conv2D"
+
+    def __init__(self, in_channels: int, out_channels: int, kernel_size: int, stride: int = 1, padding: int = 0,
+                 activation: Optional[str] = None, use_bias: bool = True):
+        super().__init__()
+        self.in_channels, self.out_channels = int(in_channels), int(out_channels)
+        self.kernel_size, self.stride, self.padding = int(kernel_size), int(stride), int(padding)
+        k2 = self.kernel_size * self.kernel_size
+        std = math.sqrt(2.0 / (self.in_channels * k2 + self.out_channels * k2))
+        self.weight = self._param("weight", _normal((self.out_channels, self.in_channels, self.kernel_size,
+                                                     self.kernel_size), std))
+        self.bias = self._param("bias", torch.zeros(self.out_channels), decay=False) if use_bias else None
+        self.relu = activation == "relu"
+
+    def _forward(self, x, relu=None):
+        if x.dtype != self.compute_dtype:
+            x = x.to(self.compute_dtype)
+        return Fn.Conv2dFn.apply(x, Fn._ANCHOR, self.weight, self.bias, self.stride, self.padding,
+                                 self.relu if relu is None else relu)
+
+
+class MaxPool2DLayer(ModernLayer):
+    type_name = "MaxPool2D"
+
+    def __init__(self, pool_size: int, stride: int = 0):
+        super().__init__()
+        self.pool_size = int(pool_size)
+        self.stride = int(stride) if stride else self.pool_size
+
+    def _forward(self, x):
+        return Fn.MaxPoolFn.apply(x, self.pool_size, self.stride)
+
+
+class AvgPool2DLayer(ModernLayer):
+    type_name = "AvgPool2D"
+
+    def __init__(self, pool_size: int, stride: int = 0, padding: int = 0):
+        super().__init__()
+        self.pool_size = int(pool_size)
+        self.stride = int(stride) if stride else self.pool_size
+        self.padding = int(padding)
+
+    def _forward(self, x):
+        return Fn.AvgPoolFn.apply(x, self.pool_size, self.stride, self.padding)
+
+
+class _BatchNormBase(ModernLayer):
+    """Training: biased batch variance, running = (1 - m) r + m batch, m = 0.1,
+    eps = 1e-5 (src/layers/batch_norm_layers.cpp:65-116); gamma = 1, beta = 0."""
+
+    def __init__(self, num_features: int, momentum: float = 0.1, eps: float = 1e-5, affine: bool = True):
+        super().__init__()
+        self.num_features = int(num_features)
+        self.momentum, self.eps = float(momentum), float(eps)
+        self.gamma = self._param("gamma", torch.ones(self.num_features), decay=False) if affine else None
+        self.beta = self._param("beta", torch.zeros(self.num_features), decay=False) if affine else None
+        self.running_mean = torch.zeros(self.num_features)
+        self.running_var = torch.ones(self.num_features)
+        self.fuse_relu = False
+        self.fuse_dropout = 0.0
+        self.dropout_stream = 0
+
+    def _on_bind(self):
+        dev = self.device_ctx.device
+        self.running_mean = self.running_mean.to(dev)
+        self.running_var = self.running_var.to(dev)
+        if not self.dropout_stream:
+            self.dropout_stream = self.device_ctx.next_stream_id()
+
+    def _buffers(self):
+        return [("running_mean", self.running_mean), ("running_var", self.running_var)]
+
+    def _forward(self, x, relu=False, p=0.0, stream=None):
+        cfg = dict(momentum=self.momentum, eps=self.eps, training=self.training, relu=relu, p=p if self.training else 0.0,
+                   stream=stream if stream is not None else self.dropout_stream, seed=self.device_ctx.seed,
+                   step_t=self.device_ctx.step_t)
+        return Fn.BatchNormFn.apply(x, Fn._ANCHOR, self.gamma, self.beta, self.running_mean, self.running_var, cfg)
+
+
+class BatchNorm1DLayer(_BatchNormBase):
+    type_name = "BatchNorm1D"
+
+
+class BatchNorm2DLayer(_BatchNormBase):
+    type_name = "BatchNorm2D"
+
+
+class DropoutLayer(ModernLayer):
+    """Inverted dropout with counter-based Philox masks (reproducible)."""
+
+    type_name = "Dropout"
+
+    def __init__(self, dropout_rate: float):
+        super().__init__()
+        self.rate = float(dropout_rate)
+        self.stream = 0
+
+    def _on_bind(self):
+        if not self.stream:
+            self.stream = self.device_ctx.next_stream_id()
+
+    def _forward(self, x):
+        if not self.training or self.rate <= 0.0:
+            return x
+        return Fn.DropoutFn.apply(x, self.rate, self.stream, self.device_ctx.seed, self.device_ctx.step_t)
+
+
+class ActivationLayer(ModernLayer):
+    type_name = "Activation"
+
+    def __init__(self, activation):
+        super().__init__()
+        if isinstance(activation, str):
+            activation = ActivationType(activation.lower())
+        self.activation = activation
+        self.type_name = activation.name
+
+    def _forward(self, x):
+        a = self.activation
+        if a == ActivationType.Softmax:
+            return Fn.SoftmaxFn.apply(x)
+        if a == ActivationType.Linear:
+            return x
+        return Fn.ActivationFn.apply(x, a.value)
+
+
+class FlattenLayer(ModernLayer):
+    type_name = "Flatten"
+
+    def _forward(self, x):
+        return x.reshape(x.shape[0], -1)
+
+
+class EmbeddingLayer(ModernLayer):
+    """Token embedding; ids outside [0, V) produce zeros
+    (shaders/embedding_lookup.comp:36-44)."""
+
+    type_name = "Embedding"
+
+    def __init__(self, num_embeddings: int, embedding_dim: int, init_std: float = 1.0):
+        super().__init__()
+        self.num_embeddings, self.embedding_dim = int(num_embeddings), int(embedding_dim)
+        self.weight = self._param("weight", _normal((self.num_embeddings, self.embedding_dim), init_std))
+        self._anchor = None
+
+    def forward(self, x):
+        from ..tensor import Tensor as FacadeTensor
+
+        facade = isinstance(x, FacadeTensor)
+        ids = x.data if facade else x
+        if self.device_ctx is None:
+            self.to(ids.device, torch.float32)
+        y = Fn.EmbeddingFn.apply(ids.to(torch.int32), self.weight, Fn._ANCHOR)
+        if self.track:
+            self._last_in, self._last_out = None, y
+        self.output_shape = tuple(y.shape)
+        return FacadeTensor.wrap(y) if facade else y
+
+    __call__ = forward
+
+    def _forward(self, x):
+        return self.forward(x)
+
+
+class LayerNormLayer(ModernLayer):
+    type_name = "LayerNorm"
+
+    def __init__(self, normalized_shape: int, eps: float = 1e-5):
+        super().__init__()
+        self.normalized_shape, self.eps = int(normalized_shape), float(eps)
+        self.gamma = self._param("gamma", torch.ones(self.normalized_shape), decay=False)
+        self.beta = self._param("beta", torch.zeros(self.normalized_shape), decay=False)
+
+    def _forward(self, x):
+        return Fn.LayerNormFn.apply(x, Fn._ANCHOR, self.gamma, self.beta, self.eps)
+
+
+class MultiHeadAttentionLayer(ModernLayer):
+    """softmax(Q K^T / sqrt(d)) V with x W_{q,k,v,o}, W [E, E], no biases
+    (src/layers/modern_layers.cpp:144-171).  Q, K and V come from one fused
+    [E, 3E] projection GEMM whose output the attention kernels read in place.
+    With `residual=True` the output projection adds its input (x + attn(x))
+    in the GEMM epilogue."""
+
+    type_name = "MultiHeadAttention"
+
+    def __init__(self, embed_dim: int, num_heads: int, dropout: float = 0.0, init_std: Optional[float] = None,
+                 residual: bool = False):
+        super().__init__()
+        if embed_dim % num_heads:
+            raise ValueError("embed_dim must be divisible by num_heads")
+        self.embed_dim, self.num_heads = int(embed_dim), int(num_heads)
+        self.head_dim = self.embed_dim // self.num_heads
+        std = init_std if init_std is not None else math.sqrt(2.0 / (2 * self.embed_dim))
+        self.w_qkv = self._param("w_qkv", _normal((self.embed_dim, 3 * self.embed_dim), std))
+        self.w_o = self._param("w_o", _normal((self.embed_dim, self.embed_dim), std))
+        self.dropout = float(dropout)
+        self.residual = residual
+
+    def _forward(self, x, residual_src=None):
+        B, S, E = x.shape
+        if x.dtype != self.compute_dtype:
+            x = x.to(self.compute_dtype)
+        qkv = Fn.dense(x, self.w_qkv, None)
+        att = Fn.AttentionFn.apply(qkv, B, S, self.num_heads, self.head_dim, 1.0 / math.sqrt(self.head_dim))
+        res = residual_src if residual_src is not None else (x if self.residual else None)
+        return Fn.dense(att, self.w_o, None, K.ACT_NONE, res)
+
+
+class PositionalEncodingLayer(ModernLayer):
+    """Adds the sinusoidal table PE[pos, 2i] = sin(pos / 10000^(2i/d)),
+    PE[pos, 2i+1] = cos(...) (src/layers/modern_layers.cpp:479-524)."""
+
+    type_name = "PositionalEncoding"
+
+    def __init__(self, d_model: int, max_len: int = 5000):
+        super().__init__()
+        self.d_model, self.max_len = int(d_model), int(max_len)
+        pos = torch.arange(self.max_len, dtype=torch.float32)[:, None]
+        div = torch.exp(torch.arange(0, self.d_model, 2, dtype=torch.float32) * (-math.log(10000.0) / self.d_model))
+        pe = torch.zeros(self.max_len, self.d_model)
+        pe[:, 0::2] = torch.sin(pos * div)
+        pe[:, 1::2] = torch.cos(pos * div)[:, : pe[:, 1::2].shape[1]]
+        self.table = pe
+        self._cache = {}
+
+    def _forward(self, x):
+        B, S, D = x.shape
+        key = (S, x.dtype, x.device)
+        if key not in self._cache:
+            self._cache[key] = self.table[:S].to(x.device, x.dtype).expand(B, S, D).contiguous()
+        pe = self._cache[key]
+        if pe.shape[0] != B:
+            pe = self.table[:S].to(x.device, x.dtype).expand(B, S, D).contiguous()
+            self._cache[key] = pe
+        return _AddConst.apply(x, pe)
+
+
+class _AddConst(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, c):
+        return K.binary(x.contiguous(), c, K.BIN_ADD)
+
+    @staticmethod
+    def backward(ctx, g):
+        return g, None
+
+
+class _ResidualAdd(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, a, b):
+        return K.binary(a.contiguous(), b.contiguous(), K.BIN_ADD)
+
+    @staticmethod
+    def backward(ctx, g):
+        return g, g
+
+
+class ResidualLayer(ModernLayer):
+    """y = x + f(x) (include/dlvk/layers/modern_layers.h:217-233)."""
+
+    type_name = "Residual"
+
+    def __init__(self, wrapped: ModernLayer):
+        super().__init__()
+        self.inner = self._child(wrapped)
+        self.inner.track = False
+
+    def _forward(self, x):
+        return _ResidualAdd.apply(x, self.inner._forward(x))
+
+
+class GlobalAvgPoolLayer(ModernLayer):
+    """[N, C, H, W] -> [N, C] mean over the spatial dims."""
+
+    type_name = "GlobalAvgPool"
+
+    def _forward(self, x):
+        N_, C, H, W = x.shape
+        return Fn.AvgPoolFn.apply(x, H, H, 0).reshape(N_, C) if H == W else x.float().mean((2, 3)).to(x.dtype)
+
+
+class TransformerEncoderLayer(ModernLayer):
+    """Pre-norm encoder block: x + MHA(LN(x)), then h + W2 relu(W1 LN(h))
+    (include/dlvk/layers/modern_layers.h:131-160).  Both residual adds are
+    fused into the output GEMMs' epilogues."""
+
+    type_name = "TransformerEncoder"
+
+    def __init__(self, d_model: int, nhead: int, dim_feedforward: int = 2048, dropout: float = 0.0,
+                 init_std: Optional[float] = None):
+        super().__init__()
+        self.d_model, self.nhead, self.dim_feedforward = int(d_model), int(nhead), int(dim_feedforward)
+        self.ln1 = self._child(LayerNormLayer(d_model))
+        self.attn = self._child(MultiHeadAttentionLayer(d_model, nhead, dropout, init_std))
+        self.ln2 = self._child(LayerNormLayer(d_model))
+        self.ff1 = self._child(DenseLayer(d_model, dim_feedforward, True, "relu", init_std))
+        self.ff2 = self._child(DenseLayer(dim_feedforward, d_model, True, None, init_std))
+        for c in self._children:
+            c.track = False
+
+    def _forward(self, x):
+        if x.dtype != self.compute_dtype:
+            x = x.to(self.compute_dtype)
+        h = self.attn._forward(self.ln1._forward(x), residual_src=x)
+        f = self.ff1._forward(self.ln2._forward(h))
+        return self.ff2._forward(f, residual=h)
+
+
+class GroupNormLayer(ModernLayer):
+    """Group norm over [N, C, *]: layer-norm statistics per (sample, group),
+    then a per-channel affine."""
+
+    type_name = "GroupNorm"
+
+    def __init__(self, num_groups: int, num_channels: int, eps: float = 1e-5):
+        super().__init__()
+        if num_channels % num_groups:
+            raise ValueError("num_channels must be divisible by num_groups")
+        self.num_groups, self.num_channels, self.eps = int(num_groups), int(num_channels), float(eps)
+        self.gamma = self._param("gamma", torch.ones(self.num_channels), decay=False)
+        self.beta = self._param("beta", torch.zeros(self.num_channels), decay=False)
+
+    def _forward(self, x):
+        N_, C = x.shape[:2]
+        xr = x.reshape(N_ * self.num_groups, -1)
+        y = Fn.LayerNormFn.apply(xr, Fn._ANCHOR, None, None, self.eps).reshape(x.shape)
+        return Fn.ChannelAffineFn.apply(y, Fn._ANCHOR, self.gamma, self.beta)
+
+
+# Reference adapter / legacy names (include/dlvk/layers/layer_adapters.h).
+DenseLayerAdapter = DenseLayer
+Conv2DLayerAdapter = Conv2DLayer
+MaxPool2DLayerAdapter = MaxPool2DLayer
+AvgPool2DLayerAdapter = AvgPool2DLayer
+BatchNorm1DLayerAdapter = BatchNorm1DLayer
+BatchNorm2DLayerAdapter = BatchNorm2DLayer
+DropoutLayerAdapter = DropoutLayer
+Layer = ModernLayer

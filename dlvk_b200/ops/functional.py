@@ -1,0 +1,304 @@
+"""Autograd functions over the native kernels.
+
+Parameters are not autograd leaves: each function writes dW/db straight into
+the parameter's slice of the flat gradient buffer (overwriting on the first
+write after ``zero_grad``, accumulating afterwards) and then fires the
+parameter's grad-ready hooks, which the data-parallel bucketer uses to start
+the fused all-reduce + optimizer of a bucket while backward continues.
+Autograd only tracks activations.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import core as K
+from . import nn as NN
+from .core import ACT_NONE, ACT_RELU, ACT_GELU
+
+
+def _flat2(t: torch.Tensor) -> torch.Tensor:
+    return t.reshape(-1, t.shape[-1])
+
+
+# Parameters are not autograd leaves, so every parametric function also takes
+# this grad-requiring anchor: it makes the op's output part of the autograd
+# graph even when the input activation does not require grad (first layer).
+_ANCHOR = torch.zeros((), requires_grad=True)
+
+
+def zero_(t: torch.Tensor) -> torch.Tensor:
+    if t.is_cuda:
+        K.N().memset_zero(t)
+    else:
+        t.zero_()
+    return t
+
+
+class DenseFn(torch.autograd.Function):
+    """y = act(x @ W + b [+ residual]); W stored [in, out] (reference layout,
+    src/layers/dense_layer.cpp:16-20)."""
+
+    @staticmethod
+    def forward(ctx, x, residual, anchor, W, b, act):
+        x2 = _flat2(x)
+        r2 = _flat2(residual) if residual is not None else None
+        y = K.gemm(x2, W.value, bias=b.value if b is not None else None, act=act, residual=r2)
+        ctx.W, ctx.b, ctx.act = W, b, act
+        ctx.has_res = residual is not None
+        ctx.save_for_backward(x2, y if act in (ACT_RELU,) else (x2 if act == ACT_GELU else None))
+        return y.reshape(*x.shape[:-1], W.shape[1])
+
+    @staticmethod
+    def backward(ctx, gy):
+        x2, saved = ctx.saved_tensors
+        W, b = ctx.W, ctx.b
+        g2 = _flat2(gy)
+        if g2.dtype != x2.dtype:
+            g2 = g2.to(x2.dtype)
+        if ctx.act == ACT_RELU:
+            g2 = K.binary(g2, saved, K.BIN_RELU_BWD)
+        elif ctx.act == ACT_GELU:
+            raise NotImplementedError("GELU-fused dense backward needs the pre-activation")
+        acc = W.take_accumulate_flag()
+        K.gemm(x2.t(), g2, out=W.grad, beta=1.0 if acc else 0.0)
+        if b is not None:
+            K.colsum(g2, out=b.grad, accumulate=b.take_accumulate_flag())
+        W.grad_ready()
+        if b is not None:
+            b.grad_ready()
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = K.gemm(g2, W.value.t()).reshape(*gy.shape[:-1], W.shape[0])
+        dres = gy if ctx.has_res and ctx.needs_input_grad[1] else None
+        return dx, dres, None, None, None, None
+
+
+def dense(x, W, b=None, act=ACT_NONE, residual=None):
+    return DenseFn.apply(x, residual, _ANCHOR, W, b, act)
+
+
+class ActivationFn(torch.autograd.Function):
+    """relu / sigmoid / tanh / gelu with the saved tensor the backward needs
+    (the reference passed zero dummies, src/layers/activation.cpp:51-69)."""
+
+    _FWD = {"relu": K.UN_RELU, "sigmoid": K.UN_SIGMOID, "tanh": K.UN_TANH, "gelu": K.UN_GELU}
+    _BWD = {"relu": K.BIN_RELU_BWD, "sigmoid": K.BIN_SIGMOID_BWD, "tanh": K.BIN_TANH_BWD, "gelu": K.BIN_GELU_BWD}
+
+    @staticmethod
+    def forward(ctx, x, kind):
+        y = K.unary(x, ActivationFn._FWD[kind])
+        ctx.kind = kind
+        ctx.save_for_backward(x if kind == "gelu" else y)
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        (s,) = ctx.saved_tensors
+        return K.binary(gy.contiguous(), s, ActivationFn._BWD[ctx.kind]), None
+
+
+class SoftmaxFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x):
+        y = K.softmax(x)
+        ctx.save_for_backward(y)
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        (y,) = ctx.saved_tensors
+        return K.softmax_bwd(y, gy.contiguous())
+
+
+class Conv2dFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, anchor, W, b, stride, pad, relu):
+        y = NN.conv2d_fwd(x.contiguous(), W.value, b.value if b is not None else None, stride, pad, relu)
+        ctx.W, ctx.b, ctx.stride, ctx.pad, ctx.relu = W, b, stride, pad, relu
+        ctx.xshape = tuple(x.shape)
+        ctx.save_for_backward(x, y if relu else None)
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, y = ctx.saved_tensors
+        g = gy.contiguous()
+        if g.dtype != x.dtype:
+            g = g.to(x.dtype)
+        if ctx.relu:
+            g = K.binary(g, y, K.BIN_RELU_BWD)
+        W, b = ctx.W, ctx.b
+        acc = W.take_accumulate_flag()
+        if b is not None:
+            b.take_accumulate_flag()
+        NN.conv2d_wgrad(x, g, W.grad, b.grad if b is not None else None, ctx.stride, ctx.pad, accumulate=acc)
+        W.grad_ready()
+        if b is not None:
+            b.grad_ready()
+        dx = NN.conv2d_dgrad(g, W.value, ctx.xshape, ctx.stride, ctx.pad) if ctx.needs_input_grad[0] else None
+        return dx, None, None, None, None, None, None
+
+
+class MaxPoolFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, k, stride):
+        y, idx = NN.maxpool_fwd(x.contiguous(), k, stride)
+        ctx.k, ctx.stride, ctx.hw = k, stride, (x.shape[2], x.shape[3])
+        ctx.save_for_backward(idx)
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        (idx,) = ctx.saved_tensors
+        return NN.maxpool_bwd(gy.contiguous(), idx, ctx.hw[0], ctx.hw[1], ctx.k, ctx.stride), None, None
+
+
+class AvgPoolFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, k, stride, pad):
+        ctx.k, ctx.stride, ctx.pad, ctx.hw = k, stride, pad, (x.shape[2], x.shape[3])
+        return NN.avgpool_fwd(x.contiguous(), k, stride, pad)
+
+    @staticmethod
+    def backward(ctx, gy):
+        return NN.avgpool_bwd(gy.contiguous(), ctx.hw[0], ctx.hw[1], ctx.k, ctx.stride, ctx.pad), None, None, None
+
+
+class BatchNormFn(torch.autograd.Function):
+    """Batch norm with optional fused ReLU and Philox dropout after it."""
+
+    @staticmethod
+    def forward(ctx, x, anchor, gamma, beta, run_mean, run_var, cfg):
+        y, mean, rstd = NN.batchnorm_fwd(x.contiguous(), gamma.value if gamma else None,
+                                         beta.value if beta else None, run_mean, run_var, cfg["momentum"],
+                                         cfg["eps"], cfg["training"], cfg["relu"], cfg["p"], cfg["stream"],
+                                         cfg["seed"], 0, cfg["step_t"])
+        ctx.gamma, ctx.beta, ctx.cfg = gamma, beta, cfg
+        ctx.save_for_backward(x, mean, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, mean, rstd = ctx.saved_tensors
+        gamma, beta, cfg = ctx.gamma, ctx.beta, ctx.cfg
+        acc = gamma.take_accumulate_flag() if gamma is not None else False
+        if beta is not None:
+            beta.take_accumulate_flag()
+        dx = NN.batchnorm_bwd(x.contiguous(), gy.contiguous().to(x.dtype), mean, rstd,
+                              gamma.value if gamma else None, beta.value if beta else None,
+                              gamma.grad if gamma else None, beta.grad if beta else None, acc, cfg["relu"],
+                              cfg["p"] if cfg["training"] else 0.0, cfg["stream"], cfg["seed"], 0, cfg["step_t"])
+        if gamma is not None:
+            gamma.grad_ready()
+        if beta is not None:
+            beta.grad_ready()
+        return dx, None, None, None, None, None, None
+
+
+class LayerNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, anchor, gamma, beta, eps):
+        y, mean, rstd = NN.layernorm_fwd(x.contiguous(), gamma.value if gamma else None,
+                                         beta.value if beta else None, eps)
+        ctx.gamma, ctx.beta = gamma, beta
+        ctx.save_for_backward(x, mean, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, mean, rstd = ctx.saved_tensors
+        gamma, beta = ctx.gamma, ctx.beta
+        acc = gamma.take_accumulate_flag() if gamma is not None else False
+        if beta is not None:
+            beta.take_accumulate_flag()
+        dx = NN.layernorm_bwd(x.contiguous(), gamma.value if gamma else None, mean, rstd,
+                              gy.contiguous().to(x.dtype), gamma.grad if gamma else None,
+                              beta.grad if beta else None, acc)
+        if gamma is not None:
+            gamma.grad_ready()
+        if beta is not None:
+            beta.grad_ready()
+        return dx, None, None, None, None
+
+
+class DropoutFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, p, stream, seed, step_t):
+        ctx.p, ctx.stream, ctx.seed, ctx.step_t = p, stream, seed, step_t
+        return NN.dropout(x.contiguous(), p, stream, seed, 0, step_t)
+
+    @staticmethod
+    def backward(ctx, gy):
+        return NN.dropout(gy.contiguous(), ctx.p, ctx.stream, ctx.seed, 0, ctx.step_t), None, None, None, None
+
+
+class EmbeddingFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, ids, table, anchor):
+        ctx.table = table
+        ctx.save_for_backward(ids)
+        return NN.embedding_fwd(ids, table.value)
+
+    @staticmethod
+    def backward(ctx, gy):
+        (ids,) = ctx.saved_tensors
+        T = ctx.table
+        if not T.take_accumulate_flag():
+            zero_(T.grad)
+        NN.embedding_bwd(ids, gy.contiguous(), T.grad)
+        T.grad_ready()
+        return None, None, None
+
+
+class AttentionFn(torch.autograd.Function):
+    """softmax(Q K^T * scale) V over a fused QKV buffer [B, S, 3*E]."""
+
+    @staticmethod
+    def forward(ctx, qkv, B, S, H, D, scale):
+        out, probs = NN.attention_fwd(qkv.contiguous(), B, S, H, D, scale)
+        ctx.dims = (B, S, H, D, scale)
+        ctx.save_for_backward(qkv, probs)
+        return out
+
+    @staticmethod
+    def backward(ctx, gout):
+        qkv, probs = ctx.saved_tensors
+        B, S, H, D, scale = ctx.dims
+        dqkv = NN.attention_bwd(qkv, probs, gout.contiguous().to(qkv.dtype), B, S, H, D, scale)
+        return dqkv, None, None, None, None, None
+
+
+def softmax_cross_entropy(logits: torch.Tensor, target: torch.Tensor, reduction_scale: float):
+    """Fused softmax + CE: returns (loss scalar tensor [f32], dlogits)."""
+    rows_loss, dl = K.softmax_ce(logits.detach().contiguous(), target, grad_scale=reduction_scale,
+                                 want_grad=True, in_place=False)
+    return K.sum_scalar(rows_loss, reduction_scale), dl
+
+
+class ChannelAffineFn(torch.autograd.Function):
+    """y = x * gamma[c] + beta[c] over [N, C, *] (group-norm affine)."""
+
+    @staticmethod
+    def forward(ctx, x, anchor, gamma, beta):
+        shape = [1, x.shape[1]] + [1] * (x.dim() - 2)
+        ctx.gamma, ctx.beta, ctx.shape = gamma, beta, shape
+        ctx.save_for_backward(x)
+        return (x.float() * gamma.value.reshape(shape) + beta.value.reshape(shape)).to(x.dtype)
+
+    @staticmethod
+    def backward(ctx, gy):
+        (x,) = ctx.saved_tensors
+        gamma, beta, shape = ctx.gamma, ctx.beta, ctx.shape
+        dims = [0] + list(range(2, x.dim()))
+        g = gy.float()
+        dg = (g * x.float()).sum(dims)
+        db = g.sum(dims)
+        for p, v in ((gamma, dg), (beta, db)):
+            if p.take_accumulate_flag():
+                p.grad.add_(v)
+            else:
+                p.grad.copy_(v)
+            p.grad_ready()
+        return (g * gamma.value.reshape(shape)).to(x.dtype), None, None, None

@@ -1,0 +1,88 @@
+"""Whole models on the GPU against the same models on the CPU reference path
+(identical seeded weights, identical Philox dropout masks)."""
+import pytest
+import torch
+
+import dlvk_b200 as dl
+from dlvk_b200.models import zoo
+
+pytestmark = pytest.mark.gpu
+
+
+def close(a, b, tol):
+    a, b = a.float().cpu(), b.float().cpu()
+    err = (a - b).abs().max().item()
+    scale = b.abs().max().item() + 1e-6
+    assert err <= tol * scale + 1e-7, f"max err {err}, scale {scale}"
+
+
+def _pair(builder, dtype_gpu, **kw):
+    mc = builder(device="cpu", dtype="fp32", seed=0, **kw)
+    mg = builder(device="cuda", dtype=dtype_gpu, seed=0, **kw)
+    mc.build()
+    mg.build()
+    assert torch.equal(mc.store.master, mg.store.master.cpu())
+    return mc, mg
+
+
+def _step_both(mc, mg, x, y, opt_c, opt_g, loss=None):
+    loss = loss or dl.CrossEntropyLoss()
+    lc = mc.train_step(x, y, loss, opt_c)
+    lg = mg.train_step(x, y, loss, opt_g)
+    return lc, lg
+
+
+def test_mlp_fp32_matches_cpu():
+    mc, mg = _pair(zoo.mlp, "fp32")
+    x, y = zoo.synthetic_batch("mlp", 32)
+    lc, lg = _step_both(mc, mg, x, y, dl.Adam(1e-3), dl.Adam(1e-3))
+    close(lg, lc, 1e-5)
+    close(mg.store.grad, mc.store.grad, 1e-4)
+    close(mg.store.master, mc.store.master, 1e-5)
+
+
+@pytest.mark.parametrize("dtype,tol", [("fp32", 1e-4), ("bf16", 5e-2)])
+def test_cnn_matches_cpu(dtype, tol):
+    mc, mg = _pair(zoo.small_cnn, dtype)
+    x, y = zoo.synthetic_batch("cnn", 16)
+    lc, lg = _step_both(mc, mg, x, y, dl.Adam(1e-3), dl.Adam(1e-3))
+    close(lg, lc, tol)
+    close(mg.store.grad, mc.store.grad, tol * 2)
+
+
+def test_wide_mlp_small_matches_cpu():
+    kw = dict(width=256, depth=2, d_in=128, n_out=100)
+    mc, mg = _pair(zoo.wide_mlp, "bf16", **kw)
+    x = torch.randn(64, 128)
+    y = torch.randint(0, 100, (64,), dtype=torch.int32)
+    lc, lg = _step_both(mc, mg, x, y, dl.SGD(0.01, 0.9), dl.SGD(0.01, 0.9))
+    close(lg, lc, 5e-2)
+    close(mg.store.grad, mc.store.grad, 1e-1)
+
+
+def test_transformer_small_matches_cpu():
+    kw = dict(vocab=512, d_model=128, layers=2, heads=2, d_ff=256)
+    mc, mg = _pair(zoo.transformer, "bf16", **kw)
+    x, y = zoo.synthetic_batch("transformer", 2, seq_len=64, vocab=512)
+    lc, lg = _step_both(mc, mg, x, y, dl.Adam(1e-3), dl.Adam(1e-3))
+    close(lg, lc, 3e-2)
+    close(mg.store.grad, mc.store.grad, 1e-1)
+
+
+def test_dlvk_roundtrip_gpu(tmp_path):
+    m = zoo.mlp(device="cuda", seed=1)
+    opt = dl.Adam(1e-3)
+    x, y = zoo.synthetic_batch("mlp", 32)
+    m.train_step(x, y, dl.CrossEntropyLoss(), opt)
+    p1 = tmp_path / "a.dlvk"
+    m.save_weights(str(p1), optimizer=opt)
+    m2 = zoo.mlp(device="cuda", seed=2)
+    opt2 = dl.Adam(1e-3)
+    m2.load_weights(str(p1), optimizer=opt2)
+    p2 = tmp_path / "b.dlvk"
+    m2.save_weights(str(p2), optimizer=opt2)
+    assert p1.read_bytes() == p2.read_bytes()
+    l1 = m.train_step(x, y, dl.CrossEntropyLoss(), opt)
+    l2 = m2.train_step(x, y, dl.CrossEntropyLoss(), opt2)
+    assert torch.equal(m.store.master, m2.store.master)
+    assert float(l1) == float(l2)
