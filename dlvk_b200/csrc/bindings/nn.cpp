@@ -196,16 +196,21 @@ std::vector<at::Tensor> layernorm_fwd_op(const at::Tensor& x, c10::optional<at::
 
 at::Tensor layernorm_bwd_op(const at::Tensor& x, c10::optional<at::Tensor> gamma, const at::Tensor& mean,
                             const at::Tensor& rstd, const at::Tensor& dy, c10::optional<at::Tensor> dgamma,
-                            c10::optional<at::Tensor> dbeta, bool accumulate) {
+                            c10::optional<at::Tensor> dbeta, bool accumulate, c10::optional<at::Tensor> dres) {
   check_cuda(x, "x");
   c10::cuda::CUDAGuard g(x.device());
   auto xc = x.contiguous(), dyc = dy.contiguous();
   const int64_t D = xc.size(-1), R = xc.numel() / std::max<int64_t>(D, 1);
   auto dx = at::empty_like(xc);
   auto scratch = at::empty({layernorm_bwd_scratch_floats(R, (int)D)}, xc.options().dtype(at::kFloat));
+  at::Tensor drc;
+  if (dres.has_value()) {
+    drc = dres->contiguous();
+    TORCH_CHECK(drc.scalar_type() == xc.scalar_type() && drc.numel() == xc.numel(), "dlvk.layernorm_bwd: dres");
+  }
   layernorm_bwd(to_dtype(xc), xc.data_ptr(), optf(gamma), mean.data_ptr<float>(), rstd.data_ptr<float>(),
                 dyc.data_ptr(), dx.data_ptr(), optfm(dgamma), optfm(dbeta), accumulate, R, (int)D,
-                scratch.data_ptr<float>(), stream());
+                scratch.data_ptr<float>(), stream(), dres.has_value() ? drc.data_ptr() : nullptr);
   return dx;
 }
 
@@ -266,7 +271,8 @@ void register_nn(py::module& m) {
         py::arg("step") = 0, py::arg("step_t") = py::none());
   m.def("layernorm_fwd", &layernorm_fwd_op, py::arg("x"), py::arg("gamma"), py::arg("beta"), py::arg("eps") = 1e-5);
   m.def("layernorm_bwd", &layernorm_bwd_op, py::arg("x"), py::arg("gamma"), py::arg("mean"), py::arg("rstd"),
-        py::arg("dy"), py::arg("dgamma"), py::arg("dbeta"), py::arg("accumulate") = false);
+        py::arg("dy"), py::arg("dgamma"), py::arg("dbeta"), py::arg("accumulate") = false,
+        py::arg("dres") = py::none());
   m.def("dropout", &dropout_op, py::arg("x"), py::arg("p"), py::arg("stream_id") = 0, py::arg("seed") = 0,
         py::arg("step") = 0, py::arg("step_t") = py::none());
   m.def("embedding_fwd", &embedding_fwd_op);

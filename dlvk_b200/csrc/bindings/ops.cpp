@@ -97,7 +97,10 @@ at::Tensor colsum_op(const at::Tensor& x, double scale, c10::optional<at::Tensor
   const int64_t cols = xc.size(-1), rows = xc.numel() / std::max<int64_t>(cols, 1);
   at::Tensor o = out.has_value() ? *out : at::empty({cols}, xc.options().dtype(out_dtype.value_or(at::kFloat)));
   TORCH_CHECK(o.is_contiguous() && o.numel() == cols, "dlvk.colsum: bad out");
-  colsum(to_dtype(xc), to_dtype(o), xc.data_ptr(), rows, cols, (float)scale, o.data_ptr(), accumulate, stream());
+  const int64_t ns = colsum_scratch_floats(rows, cols);
+  at::Tensor scratch = ns > 0 ? at::empty({ns}, xc.options().dtype(at::kFloat)) : at::Tensor();
+  colsum(to_dtype(xc), to_dtype(o), xc.data_ptr(), rows, cols, (float)scale, o.data_ptr(), accumulate,
+         ns > 0 ? scratch.data_ptr<float>() : nullptr, stream());
   return o;
 }
 
@@ -250,7 +253,8 @@ GemmArgs fill_args(const at::Tensor& A, const at::Tensor& B, const at::Tensor& C
 
 at::Tensor gemm_op(const at::Tensor& A, const at::Tensor& B, c10::optional<at::Tensor> bias, int64_t act,
                    double alpha, double beta, c10::optional<at::Tensor> out, c10::optional<at::ScalarType> out_dtype,
-                   int64_t force_path, int64_t max_ctas, c10::optional<at::Tensor> residual) {
+                   int64_t force_path, int64_t max_ctas, c10::optional<at::Tensor> residual,
+                   c10::optional<at::Tensor> relu_mask) {
   check_cuda(A, "A");
   check_cuda(B, "B");
   TORCH_CHECK(A.scalar_type() == B.scalar_type(), "dlvk.gemm: A and B must have the same dtype");
@@ -291,6 +295,16 @@ at::Tensor gemm_op(const at::Tensor& A, const at::Tensor& B, c10::optional<at::T
     if (nd >= 3) a.batch_stride_r = R.stride(0);
     if (nd == 4) a.batch2_stride_r = R.stride(1);
   }
+  if (relu_mask.has_value()) {
+    const auto& Mk = *relu_mask;
+    TORCH_CHECK(Mk.scalar_type() == C.scalar_type() && Mk.dim() == nd && Mk.size(-1) == N && Mk.size(-2) == M &&
+                    Mk.stride(-1) == 1,
+                "dlvk.gemm: relu_mask must match the output's dtype/shape with unit column stride");
+    a.relu_mask = Mk.data_ptr();
+    a.ldm = Mk.stride(-2);
+    if (nd >= 3) a.batch_stride_m = Mk.stride(0);
+    if (nd == 4) a.batch2_stride_m = Mk.stride(1);
+  }
   a.act = (int)act;
   if (M == 0 || N == 0) return C;
   if (K == 0) {
@@ -300,6 +314,7 @@ at::Tensor gemm_op(const at::Tensor& A, const at::Tensor& B, c10::optional<at::T
     if (bias.has_value()) C.add_(bc.to(C.scalar_type()));
     if (residual.has_value()) C.add_(*residual);
     if (act == ACT_RELU) C.relu_();
+    if (relu_mask.has_value()) C.mul_(relu_mask->gt(0));
     return C;
   }
   const bool tc_ok = A.scalar_type() == at::kBFloat16 && gemm_tc_supported(a) &&
@@ -393,7 +408,8 @@ void register_ops(py::module& m) {
   m.def("pointwise_loss", &pointwise_loss_op);
   m.def("gemm", &gemm_op, py::arg("A"), py::arg("B"), py::arg("bias") = py::none(), py::arg("act") = 0,
         py::arg("alpha") = 1.0, py::arg("beta") = 0.0, py::arg("out") = py::none(), py::arg("out_dtype") = py::none(),
-        py::arg("force_path") = 0, py::arg("max_ctas") = 0, py::arg("residual") = py::none());
+        py::arg("force_path") = 0, py::arg("max_ctas") = 0, py::arg("residual") = py::none(),
+        py::arg("relu_mask") = py::none());
   m.def("gemm_tc_ok", &gemm_tc_ok);
   m.def("optim_advance", &optim_advance_op);
   m.def("optim_update", &optim_update_op, py::arg("kind"), py::arg("hyper"), py::arg("p"), py::arg("grad"),

@@ -28,8 +28,10 @@ void bias_act(DType dt, DType dt_bias, const void* x, const void* bias, void* ou
 enum ReduceOp : int { RED_SUM = 0, RED_MAX = 1, RED_MIN = 2, RED_SUMSQ = 3, RED_ABSMAX = 4 };
 int reduce_scratch_floats();
 void reduce(DType dt, const void* x, int64_t n, int op, float scale, float* out, float* scratch, cudaStream_t s);
+// scratch: colsum_scratch_floats(rows, cols) floats (may be null: single pass)
+int64_t colsum_scratch_floats(int64_t rows, int64_t cols);
 void colsum(DType dt, DType dt_out, const void* x, int64_t rows, int64_t cols, float scale, void* out, bool accumulate,
-            cudaStream_t s);
+            float* scratch, cudaStream_t s);
 void rowsum(DType dt, const void* x, int64_t rows, int64_t cols, float scale, float* out, cudaStream_t s);
 void transpose2d(DType dt, const void* x, void* y, int64_t batch, int64_t rows, int64_t cols, cudaStream_t s);
 void permute4(DType dt, const void* x, void* y, const int* in_dims, const int* perm, cudaStream_t s);
@@ -65,6 +67,10 @@ struct GemmArgs {
   int act = ACT_NONE;
   const void* residual = nullptr;  // same dtype as C, added before act
   int64_t ldr = 0, batch_stride_r = 0, batch2_stride_r = 0;
+  // Optional mask source (same dtype and shape as C): the output is zeroed
+  // where mask <= 0.  Fuses the backward of a preceding ReLU into dX = dY W^T.
+  const void* relu_mask = nullptr;
+  int64_t ldm = 0, batch_stride_m = 0, batch2_stride_m = 0;
 };
 void gemm_simt(DType in_dt, DType out_dt, const GemmArgs& a, cudaStream_t s);
 bool gemm_tc_supported(const GemmArgs& a);
@@ -142,9 +148,11 @@ void layernorm_fwd(DType dt, const void* x, const float* gamma, const float* bet
                    int64_t rows, int D, float eps, cudaStream_t s);
 int layernorm_bwd_blocks(int64_t rows);
 int64_t layernorm_bwd_scratch_floats(int64_t rows, int D);
+// dres (optional, same dtype/shape as dx): a residual-branch gradient added
+// to dx, fusing the sum of the two gradients of a pre-norm block input.
 void layernorm_bwd(DType dt, const void* x, const float* gamma, const float* mean, const float* rstd, const void* dy,
                    void* dx, float* dgamma, float* dbeta, bool accumulate, int64_t rows, int D, float* scratch,
-                   cudaStream_t s);
+                   cudaStream_t s, const void* dres = nullptr);
 void dropout(DType dt, const void* x, void* y, int64_t n, const DropoutDesc& dd, cudaStream_t s);
 void embedding_fwd(DType dt, const int32_t* ids, const void* table, void* out, int64_t n, int64_t V, int D,
                    cudaStream_t s);

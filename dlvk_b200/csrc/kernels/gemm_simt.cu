@@ -26,6 +26,8 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs a) {
   TC* C = reinterpret_cast<TC*>(a.C) + bo * a.batch_stride_c + bi * a.batch2_stride_c;
   const TC* R = a.residual ? reinterpret_cast<const TC*>(a.residual) + bo * a.batch_stride_r + bi * a.batch2_stride_r
                            : nullptr;
+  const TC* Mk = a.relu_mask ? reinterpret_cast<const TC*>(a.relu_mask) + bo * a.batch_stride_m + bi * a.batch2_stride_m
+                             : nullptr;
   const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // 16 x 16 threads
   float acc[4][4] = {};
@@ -78,6 +80,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs a) {
       if (R) v += to_f32(R[gm * a.ldr + gn]);
       if (a.act == ACT_RELU) v = fmaxf(v, 0.f);
       else if (a.act == ACT_GELU) v = 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
+      if (Mk && !(to_f32(Mk[gm * a.ldm + gn]) > 0.f)) v = 0.f;
       *cp = from_f32<TC>(v);
     }
   }

@@ -44,6 +44,9 @@ struct TcParams {
   int64_t ldc, bsc, bsc2;
   const void* R;       // residual (same dtype as C) or null
   int64_t ldr, bsr, bsr2;
+  const void* Mk;      // ReLU mask source (same dtype as C) or null: out = 0 where Mk <= 0
+  int64_t ldm, bsm, bsm2;
+  int r_vec, m_vec;
   int out_f32;
   int vec_ok;
   float alpha, beta;
@@ -60,7 +63,8 @@ struct Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (BN == 256) ? 4 : 6;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int EPI_BYTES = 4 * 32 * 33 * 4;  // per-warp 32x33 fp32 staging
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + EPI_BYTES;
 };
 
 __device__ __forceinline__ void tile_coords(int t, const TcParams& p, int& tm, int& tn, int& b) {
@@ -83,6 +87,82 @@ __device__ __forceinline__ float act_apply(int act, float v) {
   return v;
 }
 
+template <typename T> __device__ __forceinline__ float ld_elem(const void* p, int64_t i) {
+  return to_f32(reinterpret_cast<const T*>(p)[i]);
+}
+
+// Loads VEC consecutive elements of type T (VEC * sizeof(T) == 16 when `vec`).
+template <typename T, int VEC>
+__device__ __forceinline__ void ld_vec(const void* base, int64_t off, int valid, bool vec, float* out) {
+  if (vec && valid == VEC) {
+    uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(base) + off);
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) out[k] = to_f32(e[k]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) out[k] = k < valid ? ld_elem<T>(base, off + k) : 0.f;
+  }
+}
+
+// Writes one staged 32x32 chunk: VEC columns per lane, 32/VEC lanes per row.
+template <typename T, int VEC>
+__device__ __forceinline__ void epi_store(const TcParams& p, const float* stg, int row0, int n0, int lane,
+                                          int64_t cb, int64_t rb, int64_t mb) {
+  constexpr int LPR = 32 / VEC;           // lanes per row
+  constexpr int RPP = 32 / LPR;           // rows per pass
+  const int cg = lane % LPR, rr = lane / LPR;
+  const int n = n0 + cg * VEC;
+  const int valid = max(0, min(VEC, p.N - n));
+#pragma unroll 1
+  for (int pass = 0; pass < 32 / RPP; ++pass) {
+    const int rl = pass * RPP + rr;
+    const int row = row0 + rl;
+    if (row >= p.M || valid == 0) continue;
+    float v[VEC];
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) v[k] = stg[rl * 33 + cg * VEC + k];
+    const int64_t ci = cb + (int64_t)row * p.ldc + n;
+    if (p.beta != 0.f) {
+      float o[VEC];
+      ld_vec<T, VEC>(p.C, ci, valid, p.vec_ok, o);
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) v[k] += p.beta * o[k];
+    }
+    if (p.bias) {
+#pragma unroll
+      for (int k = 0; k < VEC; ++k)
+        if (k < valid) v[k] += p.bias_f32 ? ld_elem<float>(p.bias, n + k) : ld_elem<__nv_bfloat16>(p.bias, n + k);
+    }
+    if (p.R) {
+      float o[VEC];
+      ld_vec<T, VEC>(p.R, rb + (int64_t)row * p.ldr + n, valid, p.r_vec, o);
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) v[k] += o[k];
+    }
+    if (p.act != ACT_NONE) {
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) v[k] = act_apply(p.act, v[k]);
+    }
+    if (p.Mk) {
+      float o[VEC];
+      ld_vec<T, VEC>(p.Mk, mb + (int64_t)row * p.ldm + n, valid, p.m_vec, o);
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) v[k] = o[k] > 0.f ? v[k] : 0.f;
+    }
+    T* dst = reinterpret_cast<T*>(p.C) + ci;
+    if (p.vec_ok && valid == VEC) {
+      uint4 u;
+      T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) e[k] = from_f32<T>(v[k]);
+      *reinterpret_cast<uint4*>(dst) = u;
+    } else {
+      for (int k = 0; k < valid; ++k) dst[k] = from_f32<T>(v[k]);
+    }
+  }
+}
+
 template <int BN>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, TcParams p) {
@@ -94,6 +174,7 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  float* epi = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES + 256);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_tiles = p.tiles_m * p.tiles_n * p.batch;
@@ -198,7 +279,11 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // Epilogue warps 2..5.  TMEM lane quarter accessible to a warp = warp % 4.
+    // Each 32x32 accumulator chunk is staged through shared memory so that
+    // every global access (C, beta*C, bias, residual, ReLU mask) is a
+    // coalesced 16-byte access along rows instead of one row per lane.
     const int q = warp & 3;
+    float* stg = epi + (warp - 2) * (32 * 33);
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
@@ -206,79 +291,25 @@ __global__ void __launch_bounds__(192, 1)
       tile_coords(t, p, tm, tn, b);
       if (!mbar_wait(&tfull[acc], acc_phase, p.err)) break;
       tc_fence_after();
-      const int row = tm * BM + q * 32 + lane;
-      const bool row_ok = row < p.M;
       const int bo = b / p.batch2, bi = b - bo * p.batch2;
-      const int64_t cbase = (int64_t)bo * p.bsc + (int64_t)bi * p.bsc2 + (int64_t)row * p.ldc;
-      const int64_t rbase = (int64_t)bo * p.bsr + (int64_t)bi * p.bsr2 + (int64_t)row * p.ldr;
+      const int64_t cb = (int64_t)bo * p.bsc + (int64_t)bi * p.bsc2;
+      const int64_t rb = (int64_t)bo * p.bsr + (int64_t)bi * p.bsr2;
+      const int64_t mb = (int64_t)bo * p.bsm + (int64_t)bi * p.bsm2;
+      const int row0 = tm * BM + q * 32;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
         tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) stg[lane * 33 + j] = __uint_as_float(r[j]) * p.alpha;
+        __syncwarp();
         const int n0 = tn * BN + c * 32;
-        if (!row_ok || n0 >= p.N) continue;
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
-        const bool full_chunk = (n0 + 32 <= p.N);
-        if (p.beta != 0.f) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (n0 + j < p.N) {
-              const float old = p.out_f32 ? reinterpret_cast<const float*>(p.C)[cbase + n0 + j]
-                                          : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.C)[cbase + n0 + j]);
-              v[j] += p.beta * old;
-            }
-          }
+        if (n0 < p.N && row0 < p.M) {
+          if (p.out_f32) epi_store<float, 4>(p, stg, row0, n0, lane, cb, rb, mb);
+          else epi_store<__nv_bfloat16, 8>(p, stg, row0, n0, lane, cb, rb, mb);
         }
-        if (p.bias) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (n0 + j < p.N)
-              v[j] += p.bias_f32 ? reinterpret_cast<const float*>(p.bias)[n0 + j]
-                                 : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.bias)[n0 + j]);
-          }
-        }
-        if (p.R) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (n0 + j < p.N)
-              v[j] += p.out_f32 ? reinterpret_cast<const float*>(p.R)[rbase + n0 + j]
-                                : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.R)[rbase + n0 + j]);
-          }
-        }
-        if (p.act != ACT_NONE) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = act_apply(p.act, v[j]);
-        }
-        if (p.out_f32) {
-          float* dst = reinterpret_cast<float*>(p.C) + cbase + n0;
-          if (full_chunk && p.vec_ok) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              reinterpret_cast<float4*>(dst)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-          } else {
-            for (int j = 0; j < 32; ++j)
-              if (n0 + j < p.N) dst[j] = v[j];
-          }
-        } else {
-          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + cbase + n0;
-          if (full_chunk && p.vec_ok) {
-            uint32_t pk[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-              pk[j] = *reinterpret_cast<uint32_t*>(&h);
-            }
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              reinterpret_cast<uint4*>(dst)[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-          } else {
-            for (int j = 0; j < 32; ++j)
-              if (n0 + j < p.N) dst[j] = __float2bfloat16_rn(v[j]);
-          }
-        }
+        __syncwarp();
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
@@ -377,6 +408,19 @@ bool gemm_tc_supported(const GemmArgs& a) {
 void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int max_ctas) {
   DLVK_CHECK(gemm_tc_supported(a), "gemm_tc: unsupported layout/alignment");
   if (a.M == 0 || a.N == 0) return;
+  // The tensor-map encoder is a driver call and needs a current context on
+  // this thread.  Threads that have only used the runtime through a "same
+  // device" cudaSetDevice shortcut (e.g. PyTorch's autograd workers) may not
+  // have one yet, so bind the primary context once per thread and device.
+  {
+    thread_local int bound_dev = -1;
+    int dev = 0;
+    DLVK_CUDA_CHECK(cudaGetDevice(&dev));
+    if (bound_dev != dev) {
+      DLVK_CUDA_CHECK(cudaSetDevice(dev));
+      bound_dev = dev;
+    }
+  }
   const bool a_k = (a.sak == 1);
   const bool b_k = (a.sbk == 1);
   const int BN = (a.N >= 256) ? 256 : 128;
@@ -419,10 +463,18 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
   p.ldr = a.ldr;
   p.bsr = a.batch_stride_r;
   p.bsr2 = a.batch2_stride_r;
+  p.Mk = a.relu_mask;
+  p.ldm = a.ldm;
+  p.bsm = a.batch_stride_m;
+  p.bsm2 = a.batch2_stride_m;
   p.out_f32 = (out_dt == DType::F32);
   const int esz = p.out_f32 ? 4 : 2;
   p.vec_ok = al16(a.C) && ((a.ldc * esz) % 16 == 0) && ((a.batch_stride_c * esz) % 16 == 0) &&
              ((a.batch2_stride_c * esz) % 16 == 0);
+  p.r_vec = a.residual && al16(a.residual) && ((a.ldr * esz) % 16 == 0) && ((a.batch_stride_r * esz) % 16 == 0) &&
+            ((a.batch2_stride_r * esz) % 16 == 0);
+  p.m_vec = a.relu_mask && al16(a.relu_mask) && ((a.ldm * esz) % 16 == 0) && ((a.batch_stride_m * esz) % 16 == 0) &&
+            ((a.batch2_stride_m * esz) % 16 == 0);
   p.alpha = a.alpha;
   p.beta = a.beta;
   p.bias = a.bias;

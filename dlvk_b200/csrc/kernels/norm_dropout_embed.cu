@@ -236,7 +236,7 @@ __global__ void ln_fwd_kernel(const T* __restrict__ x, const float* __restrict__
 template <typename T>
 __global__ void ln_bwd_kernel(const T* __restrict__ x, const float* __restrict__ gamma, const float* __restrict__ mean,
                               const float* __restrict__ rstd, const T* __restrict__ dy, T* __restrict__ dx,
-                              float* __restrict__ part, int64_t rows, int D) {
+                              float* __restrict__ part, int64_t rows, int D, const T* __restrict__ dres) {
   extern __shared__ float sp[];  // [warps][2*D]
   const int warps = blockDim.x >> 5, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* mine = sp + (int64_t)w * 2 * D;
@@ -261,13 +261,104 @@ __global__ void ln_bwd_kernel(const T* __restrict__ x, const float* __restrict__
     for (int d = lane; d < D; d += 32) {
       const float xh = (to_f32(xr[d]) - mu) * rs;
       const float gg = to_f32(gr[d]) * (gamma ? gamma[d] : 1.f);
-      dr[d] = from_f32<T>(rs * (gg - a - xh * b));
+      dr[d] = from_f32<T>(rs * (gg - a - xh * b) + (dres ? to_f32(dres[r * D + d]) : 0.f));
     }
   }
   __syncthreads();
   for (int d = threadIdx.x; d < 2 * D; d += blockDim.x) {
     float s = 0.f;
     for (int i = 0; i < warps; ++i) s += sp[(int64_t)i * 2 * D + d];
+    part[(int64_t)blockIdx.x * 2 * D + d] = s;
+  }
+}
+
+// Register-resident variant for D = 32 * NV * EPV: lane l owns the 16-byte
+// vectors l, l+32, ... of every row, so dgamma/dbeta partials stay in
+// registers across the rows of a warp; the 8 warps of a block then combine
+// them through shared memory in warp order and write one partial per block.
+template <typename T, int NV>
+__global__ void __launch_bounds__(256) ln_bwd_warp_kernel(const T* __restrict__ x, const float* __restrict__ gamma,
+                                                          const float* __restrict__ mean,
+                                                          const float* __restrict__ rstd, const T* __restrict__ dy,
+                                                          T* __restrict__ dx, float* __restrict__ part, int64_t rows,
+                                                          int D, const T* __restrict__ dres) {
+  constexpr int EPV = 16 / sizeof(T);
+  extern __shared__ float sp[];  // [8][2*D]
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float gam[NV][EPV], adg[NV][EPV], adb[NV][EPV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int k = 0; k < EPV; ++k) {
+      const int col = (lane + 32 * i) * EPV + k;
+      gam[i][k] = gamma ? gamma[col] : 1.f;
+      adg[i][k] = 0.f;
+      adb[i][k] = 0.f;
+    }
+  const float invD = 1.f / D;
+  for (int64_t r = (int64_t)blockIdx.x * 8 + w; r < rows; r += (int64_t)gridDim.x * 8) {
+    float xv[NV][EPV], gv[NV][EPV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const uint4 ux = reinterpret_cast<const uint4*>(x + r * D)[lane + 32 * i];
+      const uint4 ug = reinterpret_cast<const uint4*>(dy + r * D)[lane + 32 * i];
+      const T* ex = reinterpret_cast<const T*>(&ux);
+      const T* eg = reinterpret_cast<const T*>(&ug);
+#pragma unroll
+      for (int k = 0; k < EPV; ++k) {
+        xv[i][k] = to_f32(ex[k]);
+        gv[i][k] = to_f32(eg[k]);
+      }
+    }
+    const float mu = mean[r], rs = rstd[r];
+    float a = 0.f, b = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+#pragma unroll
+      for (int k = 0; k < EPV; ++k) {
+        const float xh = (xv[i][k] - mu) * rs;
+        xv[i][k] = xh;
+        const float gg = gv[i][k] * gam[i][k];
+        a += gg;
+        b += gg * xh;
+        adg[i][k] += gv[i][k] * xh;
+        adb[i][k] += gv[i][k];
+      }
+    a = warp_sum(a) * invD;
+    b = warp_sum(b) * invD;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      float add[EPV];
+      if (dres) {
+        const uint4 ur = reinterpret_cast<const uint4*>(dres + r * D)[lane + 32 * i];
+        const T* er = reinterpret_cast<const T*>(&ur);
+#pragma unroll
+        for (int k = 0; k < EPV; ++k) add[k] = to_f32(er[k]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < EPV; ++k) add[k] = 0.f;
+      }
+      uint4 o;
+      T* eo = reinterpret_cast<T*>(&o);
+#pragma unroll
+      for (int k = 0; k < EPV; ++k) eo[k] = from_f32<T>(rs * (gv[i][k] * gam[i][k] - a - xv[i][k] * b) + add[k]);
+      reinterpret_cast<uint4*>(dx + r * D)[lane + 32 * i] = o;
+    }
+  }
+  float* mine = sp + (int64_t)w * 2 * D;
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int k = 0; k < EPV; ++k) {
+      const int col = (lane + 32 * i) * EPV + k;
+      mine[col] = adg[i][k];
+      mine[D + col] = adb[i][k];
+    }
+  __syncthreads();
+  for (int d = threadIdx.x; d < 2 * D; d += blockDim.x) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += sp[(int64_t)i * 2 * D + d];
     part[(int64_t)blockIdx.x * 2 * D + d] = s;
   }
 }
@@ -395,8 +486,29 @@ int64_t layernorm_bwd_scratch_floats(int64_t rows, int D) { return (int64_t)laye
 
 void layernorm_bwd(DType dt, const void* x, const float* gamma, const float* mean, const float* rstd, const void* dy,
                    void* dx, float* dgamma, float* dbeta, bool accumulate, int64_t rows, int D, float* scratch,
-                   cudaStream_t s) {
+                   cudaStream_t s, const void* dres) {
   const int blocks = layernorm_bwd_blocks(rows);
+  {
+    // Register-resident path: D a multiple of 32 lanes x 16-byte vectors.
+    const int epv = dt == DType::F32 ? 4 : 8;
+    const int nv = (D % (32 * epv) == 0) ? D / (32 * epv) : 0;
+    const bool al = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dy) |
+                      reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(dres)) & 15) == 0;
+    const size_t smem = (size_t)8 * 2 * D * sizeof(float);
+    if (al && (nv == 1 || nv == 2 || nv == 4) && smem <= 200 * 1024) {
+      DLVK_DISPATCH_FB(dt, "layernorm_bwd", {
+        auto kern = nv == 1 ? ln_bwd_warp_kernel<T, 1> : (nv == 2 ? ln_bwd_warp_kernel<T, 2> : ln_bwd_warp_kernel<T, 4>);
+        if (smem > 48 * 1024)
+          DLVK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        kern<<<blocks, 256, smem, s>>>((const T*)x, gamma, mean, rstd, (const T*)dy, (T*)dx, scratch, rows, D,
+                                       (const T*)dres);
+      });
+      DLVK_POST_LAUNCH();
+      ln_bwd_final_kernel<<<(2 * D + 255) / 256, 256, 0, s>>>(scratch, blocks, D, dgamma, dbeta, accumulate ? 1 : 0);
+      DLVK_POST_LAUNCH();
+      return;
+    }
+  }
   int warps = 8;
   while (warps > 1 && (size_t)warps * 2 * D * sizeof(float) > 96 * 1024) warps >>= 1;
   const size_t smem = (size_t)warps * 2 * D * sizeof(float);
@@ -405,7 +517,7 @@ void layernorm_bwd(DType dt, const void* x, const float* gamma, const float* mea
     if (smem > 48 * 1024)
       DLVK_CUDA_CHECK(cudaFuncSetAttribute(ln_bwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     ln_bwd_kernel<T><<<blocks, warps * 32, smem, s>>>((const T*)x, gamma, mean, rstd, (const T*)dy, (T*)dx, scratch,
-                                                      rows, D);
+                                                      rows, D, (const T*)dres);
   });
   DLVK_POST_LAUNCH();
   ln_bwd_final_kernel<<<(2 * D + 255) / 256, 256, 0, s>>>(scratch, blocks, D, dgamma, dbeta, accumulate ? 1 : 0);

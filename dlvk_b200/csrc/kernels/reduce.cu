@@ -52,25 +52,46 @@ __global__ void reduce_final_kernel(const float* __restrict__ part, int nparts, 
 }
 
 // out[c] = scale * sum_r x[r, c]  (reduce_sum_axis0.comp).  Block = 32 x 8
-// threads; each block owns 32 columns and walks all rows in a fixed order.
+// threads owning 32 columns; blockIdx.y selects a chunk of rows.  With one
+// chunk the block writes the result, otherwise a per-chunk partial that
+// colsum_final_kernel sums in chunk order (deterministic).
 template <typename T, typename TO>
 __global__ void colsum_kernel(const T* __restrict__ x, int64_t rows, int64_t cols, float scale,
-                              TO* __restrict__ out, bool accumulate) {
+                              TO* __restrict__ out, bool accumulate, float* __restrict__ partial,
+                              int64_t rows_per_chunk) {
   __shared__ float sm[8][33];
   const int64_t c = blockIdx.x * 32 + threadIdx.x;
+  const int64_t r0 = blockIdx.y * rows_per_chunk;
+  const int64_t r1 = min(rows, r0 + rows_per_chunk);
   float acc = 0.f;
   if (c < cols)
-    for (int64_t r = threadIdx.y; r < rows; r += 8) acc += to_f32(x[r * cols + c]);
+    for (int64_t r = r0 + threadIdx.y; r < r1; r += 8) acc += to_f32(x[r * cols + c]);
   sm[threadIdx.y][threadIdx.x] = acc;
   __syncthreads();
   if (threadIdx.y == 0 && c < cols) {
     float s = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) s += sm[i][threadIdx.x];
+    if (gridDim.y > 1) {
+      partial[blockIdx.y * cols + c] = s;
+      return;
+    }
     s *= scale;
     if (accumulate) s += to_f32(out[c]);
     out[c] = from_f32<TO>(s);
   }
+}
+
+template <typename TO>
+__global__ void colsum_final_kernel(const float* __restrict__ partial, int chunks, int64_t cols, float scale,
+                                    TO* __restrict__ out, bool accumulate) {
+  const int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  float s = 0.f;
+  for (int k = 0; k < chunks; ++k) s += partial[k * cols + c];
+  s *= scale;
+  if (accumulate) s += to_f32(out[c]);
+  out[c] = from_f32<TO>(s);
 }
 
 // out[r] = scale * sum_c x[r, c]   (row sums, one warp per row)
@@ -147,20 +168,33 @@ void reduce(DType dt, const void* x, int64_t n, int op, float scale, float* out,
   DLVK_POST_LAUNCH();
 }
 
+int64_t colsum_scratch_floats(int64_t rows, int64_t cols) {
+  const int64_t chunks = std::min<int64_t>(64, std::max<int64_t>(1, rows / 256));
+  return chunks > 1 ? chunks * cols : 0;
+}
+
 void colsum(DType dt, DType dt_out, const void* x, int64_t rows, int64_t cols, float scale, void* out,
-            bool accumulate, cudaStream_t s) {
-  dim3 block(32, 8), grid((unsigned)((cols + 31) / 32));
-  if (dt == DType::F32 && dt_out == DType::F32)
-    colsum_kernel<float, float><<<grid, block, 0, s>>>((const float*)x, rows, cols, scale, (float*)out, accumulate);
-  else if (dt == DType::BF16 && dt_out == DType::F32)
-    colsum_kernel<__nv_bfloat16, float><<<grid, block, 0, s>>>((const __nv_bfloat16*)x, rows, cols, scale,
-                                                               (float*)out, accumulate);
-  else if (dt == DType::BF16 && dt_out == DType::BF16)
-    colsum_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, block, 0, s>>>(
-        (const __nv_bfloat16*)x, rows, cols, scale, (__nv_bfloat16*)out, accumulate);
-  else
-    throw std::runtime_error("dlvk::colsum: unsupported dtype");
-  DLVK_POST_LAUNCH();
+            bool accumulate, float* scratch, cudaStream_t s) {
+  int64_t chunks = scratch ? std::min<int64_t>(64, std::max<int64_t>(1, rows / 256)) : 1;
+  const int64_t rpc = (rows + chunks - 1) / std::max<int64_t>(chunks, 1);
+  chunks = std::max<int64_t>(1, (rows + rpc - 1) / std::max<int64_t>(rpc, 1));
+  dim3 block(32, 8), grid((unsigned)((cols + 31) / 32), (unsigned)chunks);
+#define DLVK_COLSUM(TI, TOUT)                                                                                   \
+  do {                                                                                                          \
+    colsum_kernel<TI, TOUT><<<grid, block, 0, s>>>((const TI*)x, rows, cols, scale, (TOUT*)out, accumulate, scratch, \
+                                                   rpc);                                                          \
+    DLVK_POST_LAUNCH();                                                                                          \
+    if (chunks > 1) {                                                                                            \
+      colsum_final_kernel<TOUT><<<(unsigned)((cols + 255) / 256), 256, 0, s>>>(scratch, (int)chunks, cols, scale,  \
+                                                                               (TOUT*)out, accumulate);          \
+      DLVK_POST_LAUNCH();                                                                                        \
+    }                                                                                                            \
+  } while (0)
+  if (dt == DType::F32 && dt_out == DType::F32) DLVK_COLSUM(float, float);
+  else if (dt == DType::BF16 && dt_out == DType::F32) DLVK_COLSUM(__nv_bfloat16, float);
+  else if (dt == DType::BF16 && dt_out == DType::BF16) DLVK_COLSUM(__nv_bfloat16, __nv_bfloat16);
+  else throw std::runtime_error("dlvk::colsum: unsupported dtype");
+#undef DLVK_COLSUM
 }
 
 void rowsum(DType dt, const void* x, int64_t rows, int64_t cols, float scale, float* out, cudaStream_t s) {

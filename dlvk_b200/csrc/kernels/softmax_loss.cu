@@ -103,13 +103,59 @@ __global__ void __launch_bounds__(THREADS) softmax_ce_kernel(const T* x, const i
                                                              const float* __restrict__ probs,
                                                              float* __restrict__ loss_rows, T* dlogits,
                                                              int64_t cols, float grad_scale) {
+  constexpr int EPV = 16 / sizeof(T);
   const int64_t r = blockIdx.x;
   const T* xr = x + r * cols;
+  // 16-byte vector path when the row is a whole number of aligned vectors.
+  const bool vec = (cols % EPV) == 0 && (reinterpret_cast<uintptr_t>(xr) & 15) == 0 &&
+                   (!dlogits || (reinterpret_cast<uintptr_t>(dlogits + r * cols) & 15) == 0);
   float m = -INFINITY, s = 0.f;
-  for (int64_t c = threadIdx.x; c < cols; c += THREADS) ms_merge(m, s, to_f32(xr[c]), 1.f);
+  if (vec) {
+    for (int64_t c8 = threadIdx.x; c8 < cols / EPV; c8 += THREADS) {
+      const uint4 u = reinterpret_cast<const uint4*>(xr)[c8];
+      const T* e = reinterpret_cast<const T*>(&u);
+      float v[EPV], lm = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < EPV; ++k) {
+        v[k] = to_f32(e[k]);
+        lm = fmaxf(lm, v[k]);
+      }
+      if (lm > m) {
+        s = (m == -INFINITY) ? 0.f : s * expf(m - lm);
+        m = lm;
+      }
+#pragma unroll
+      for (int k = 0; k < EPV; ++k) s += expf(v[k] - m);
+    }
+  } else {
+    for (int64_t c = threadIdx.x; c < cols; c += THREADS) ms_merge(m, s, to_f32(xr[c]), 1.f);
+  }
   block_ms<THREADS>(m, s);
   const float lse = m + logf(s), inv = 1.f / s;
   const int label = labels ? labels[r] : -2;
+  if (dlogits && vec && labels) {
+    // Loss first (thread 0 reads the label logit), then the gradient pass.
+    float loss = 0.f;
+    if (label >= 0 && label < cols && threadIdx.x == 0) loss = lse - to_f32(xr[label]);
+    loss = block_sum_t<THREADS>(loss);
+    if (threadIdx.x == 0 && loss_rows) loss_rows[r] = label < 0 ? 0.f : loss;
+    T* dr = dlogits + r * cols;
+    const float gs = label < 0 ? 0.f : grad_scale;
+    for (int64_t c8 = threadIdx.x; c8 < cols / EPV; c8 += THREADS) {
+      const uint4 u = reinterpret_cast<const uint4*>(xr)[c8];
+      const T* e = reinterpret_cast<const T*>(&u);
+      uint4 o;
+      T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+      for (int k = 0; k < EPV; ++k) {
+        const int64_t c = c8 * EPV + k;
+        const float p = expf(to_f32(e[k]) - m) * inv;
+        oe[k] = from_f32<T>((p - (c == label ? 1.f : 0.f)) * gs);
+      }
+      reinterpret_cast<uint4*>(dr)[c8] = o;
+    }
+    return;
+  }
   float loss = 0.f;
   if (labels) {
     if (label >= 0 && label < cols && threadIdx.x == 0) loss = lse - to_f32(xr[label]);
@@ -171,8 +217,132 @@ __global__ void sum_partials_kernel(const float* __restrict__ part, int n, float
   if (threadIdx.x == 0) out[0] = acc * scale;
 }
 
+// ---- warp-per-row kernels for rows that fit in registers --------------------
+// Each lane holds NV 16-byte vectors (EPV elements each) of the row; lane l
+// owns vectors l, l+32, ...  Requires cols == 32 * NV * EPV.
+template <typename T> struct V16 { static constexpr int EPV = 16 / sizeof(T); };
+
+template <typename T, int NV>
+__device__ __forceinline__ void row_load(const T* __restrict__ src, int lane, float (&v)[NV][16 / sizeof(T)]) {
+  constexpr int EPV = 16 / sizeof(T);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const uint4 u = reinterpret_cast<const uint4*>(src)[lane + 32 * i];
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int k = 0; k < EPV; ++k) v[i][k] = to_f32(e[k]);
+  }
+}
+template <typename T, int NV>
+__device__ __forceinline__ void row_store(T* __restrict__ dst, int lane, const float (&v)[NV][16 / sizeof(T)]) {
+  constexpr int EPV = 16 / sizeof(T);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    uint4 u;
+    T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+    for (int k = 0; k < EPV; ++k) e[k] = from_f32<T>(v[i][k]);
+    reinterpret_cast<uint4*>(dst)[lane + 32 * i] = u;
+  }
+}
+
+template <typename T, int NV>
+__global__ void __launch_bounds__(256) softmax_warp_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t rows,
+                                                           int cols, bool log_out) {
+  constexpr int EPV = 16 / sizeof(T);
+  const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  float v[NV][EPV];
+  row_load<T, NV>(x + r * cols, lane, v);
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int k = 0; k < EPV; ++k) m = fmaxf(m, v[i][k]);
+  m = warp_max(m);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int k = 0; k < EPV; ++k) {
+      const float e = expf(v[i][k] - m);
+      s += e;
+      if (!log_out) v[i][k] = e;
+    }
+  s = warp_sum(s);
+  if (log_out) {
+    const float lse = m + logf(s);
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+#pragma unroll
+      for (int k = 0; k < EPV; ++k) v[i][k] -= lse;
+  } else {
+    const float inv = 1.f / s;
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+#pragma unroll
+      for (int k = 0; k < EPV; ++k) v[i][k] *= inv;
+  }
+  row_store<T, NV>(y + r * cols, lane, v);
+}
+
+template <typename T, int NV>
+__global__ void __launch_bounds__(256) softmax_bwd_warp_kernel(const T* __restrict__ y, const T* __restrict__ dy,
+                                                               T* __restrict__ dx, int64_t rows, int cols) {
+  constexpr int EPV = 16 / sizeof(T);
+  const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  float a[NV][EPV], g[NV][EPV];
+  row_load<T, NV>(y + r * cols, lane, a);
+  row_load<T, NV>(dy + r * cols, lane, g);
+  float dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int k = 0; k < EPV; ++k) dot += a[i][k] * g[i][k];
+  dot = warp_sum(dot);
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int k = 0; k < EPV; ++k) g[i][k] = a[i][k] * (g[i][k] - dot);
+  row_store<T, NV>(dx + r * cols, lane, g);
+}
+
+// Dispatch to the warp kernels when cols == 32 * NV * EPV for NV in {1,2,4,8}
+// and the pointers are 16-byte aligned; returns false otherwise.
+template <typename T>
+bool try_softmax_warp(const void* x, void* y, int64_t rows, int64_t cols, bool log_out, cudaStream_t s) {
+  constexpr int EPV = 16 / sizeof(T);
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) return false;
+  const unsigned g = (unsigned)((rows + 7) / 8);
+  switch (cols / (32 * EPV) * ((cols % (32 * EPV)) == 0)) {
+    case 1: softmax_warp_kernel<T, 1><<<g, 256, 0, s>>>((const T*)x, (T*)y, rows, (int)cols, log_out); return true;
+    case 2: softmax_warp_kernel<T, 2><<<g, 256, 0, s>>>((const T*)x, (T*)y, rows, (int)cols, log_out); return true;
+    case 4: softmax_warp_kernel<T, 4><<<g, 256, 0, s>>>((const T*)x, (T*)y, rows, (int)cols, log_out); return true;
+    case 8: softmax_warp_kernel<T, 8><<<g, 256, 0, s>>>((const T*)x, (T*)y, rows, (int)cols, log_out); return true;
+    default: return false;
+  }
+}
+template <typename T>
+bool try_softmax_bwd_warp(const void* y, const void* dy, void* dx, int64_t rows, int64_t cols, cudaStream_t s) {
+  constexpr int EPV = 16 / sizeof(T);
+  if ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(dy) | reinterpret_cast<uintptr_t>(dx)) & 15)
+    return false;
+  const unsigned g = (unsigned)((rows + 7) / 8);
+  switch (cols / (32 * EPV) * ((cols % (32 * EPV)) == 0)) {
+    case 1: softmax_bwd_warp_kernel<T, 1><<<g, 256, 0, s>>>((const T*)y, (const T*)dy, (T*)dx, rows, (int)cols); return true;
+    case 2: softmax_bwd_warp_kernel<T, 2><<<g, 256, 0, s>>>((const T*)y, (const T*)dy, (T*)dx, rows, (int)cols); return true;
+    case 4: softmax_bwd_warp_kernel<T, 4><<<g, 256, 0, s>>>((const T*)y, (const T*)dy, (T*)dx, rows, (int)cols); return true;
+    case 8: softmax_bwd_warp_kernel<T, 8><<<g, 256, 0, s>>>((const T*)y, (const T*)dy, (T*)dx, rows, (int)cols); return true;
+    default: return false;
+  }
+}
+
 template <typename T>
 void launch_softmax(const void* x, void* y, int64_t rows, int64_t cols, bool log_out, cudaStream_t s) {
+  if (try_softmax_warp<T>(x, y, rows, cols, log_out, s)) return;
   if (cols <= 64)
     softmax_rows_kernel<T, 32><<<(unsigned)rows, 32, 0, s>>>((const T*)x, (T*)y, cols, log_out);
   else if (cols <= 4096)
@@ -183,6 +353,7 @@ void launch_softmax(const void* x, void* y, int64_t rows, int64_t cols, bool log
 
 template <typename T>
 void launch_softmax_bwd(const void* y, const void* dy, void* dx, int64_t rows, int64_t cols, cudaStream_t s) {
+  if (try_softmax_bwd_warp<T>(y, dy, dx, rows, cols, s)) return;
   if (cols <= 64)
     softmax_bwd_kernel<T, 32><<<(unsigned)rows, 32, 0, s>>>((const T*)y, (const T*)dy, (T*)dx, cols);
   else

@@ -262,11 +262,13 @@ class DenseLayer(ModernLayer):
         self.activation = activation
         self._act = K.ACT_BY_NAME[activation]
 
-    def _forward(self, x, act=None, residual=None):
+    def _forward(self, x, act=None, residual=None, mask_input=False, defer_relu=False):
         a = self._act if act is None else act
+        if x.dim() > 2 and x.shape[-1] != self.input_size:
+            x = x.reshape(x.shape[0], -1)
         if x.dtype != self.compute_dtype:
             x = x.to(self.compute_dtype)
-        return Fn.dense(x, self.weight, self.bias, a, residual)
+        return Fn.dense(x, self.weight, self.bias, a, residual, mask_input, defer_relu)
 
 
 class Conv2DLayer(ModernLayer):
@@ -576,9 +578,7 @@ class TransformerEncoderLayer(ModernLayer):
     def _forward(self, x):
         if x.dtype != self.compute_dtype:
             x = x.to(self.compute_dtype)
-        h = self.attn._forward(self.ln1._forward(x), residual_src=x)
-        f = self.ff1._forward(self.ln2._forward(h))
-        return self.ff2._forward(f, residual=h)
+        return Fn.TransformerBlockFn.apply(x.contiguous(), Fn._ANCHOR, self)
 
 
 class GroupNormLayer(ModernLayer):

@@ -162,8 +162,19 @@ class Sequential(Model):
             nxt = ls[i + 1] if i + 1 < len(ls) else None
             is_relu = isinstance(nxt, L.ActivationLayer) and nxt.activation == A.ReLU
             if isinstance(cur, L.DenseLayer) and is_relu and cur._act == K.ACT_NONE:
-                plan.append((lambda x, c=cur: c._forward(x, act=K.ACT_RELU), 2))
+                # Dense+ReLU feeding another Dense: the consumer's dX GEMM
+                # applies this ReLU's backward in its epilogue.
+                feeds_dense = i + 2 < len(ls) and isinstance(ls[i + 2], L.DenseLayer)
+                mask_in = bool(plan) and getattr(plan[-1][0], "relu_feeds_dense", False)
+                fn = (lambda x, c=cur, d=feeds_dense, m=mask_in:
+                      c._forward(x, act=K.ACT_RELU, mask_input=m, defer_relu=d))
+                fn.relu_feeds_dense = feeds_dense
+                plan.append((fn, 2))
                 i += 2
+                continue
+            if isinstance(cur, L.DenseLayer) and plan and getattr(plan[-1][0], "relu_feeds_dense", False):
+                plan.append((lambda x, c=cur: c._forward(x, mask_input=True), 1))
+                i += 1
                 continue
             if isinstance(cur, L.Conv2DLayer) and is_relu:
                 plan.append((lambda x, c=cur: c._forward(x, relu=True), 2))

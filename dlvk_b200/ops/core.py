@@ -168,13 +168,21 @@ def permute4(x: torch.Tensor, perm) -> torch.Tensor:
 
 # ---------------------------------------------------------------- GEMM
 def gemm(a: torch.Tensor, b: torch.Tensor, bias=None, act: int = ACT_NONE, alpha: float = 1.0, beta: float = 0.0,
-         out=None, out_dtype=None, residual=None) -> torch.Tensor:
-    """act(alpha * a @ b + beta * out + bias + residual).  a: [M,K], [B,M,K] or
-    [B,B2,M,K] (any strides), b likewise.  Transposes and head splits are
-    views; the tensor-core path is used whenever the layout allows it."""
+         out=None, out_dtype=None, residual=None, relu_mask=None) -> torch.Tensor:
+    """act(alpha * a @ b + beta * out + bias + residual), zeroed where
+    relu_mask <= 0.  a: [M,K], [B,M,K] or [B,B2,M,K] (any strides), b
+    likewise.  Transposes and head splits are views; the tensor-core path is
+    used whenever the layout allows it."""
     if native(a):
         return N().gemm(a, b, bias=bias, act=act, alpha=alpha, beta=beta, out=out, out_dtype=out_dtype,
-                        residual=residual)
+                        residual=residual, relu_mask=relu_mask)
+    if relu_mask is not None:
+        c = gemm(a, b, bias, act, alpha, beta, None, torch.float32, residual)
+        c = torch.where(relu_mask.float() > 0, c, torch.zeros_like(c))
+        if out is not None:
+            out.copy_(c)
+            return out
+        return c.to(out_dtype or a.dtype)
     c = alpha * torch.matmul(a.float(), b.float())
     if beta != 0.0 and out is not None:
         c = c + beta * out.float()

@@ -38,16 +38,26 @@ def zero_(t: torch.Tensor) -> torch.Tensor:
 
 class DenseFn(torch.autograd.Function):
     """y = act(x @ W + b [+ residual]); W stored [in, out] (reference layout,
-    src/layers/dense_layer.cpp:16-20)."""
+    src/layers/dense_layer.cpp:16-20).
+
+    fuse flags (set by the model's execution plan):
+      mask_input  x is the output of a ReLU consumed only here: the dX GEMM
+                  epilogue applies that ReLU's backward (zero where x <= 0);
+      defer_relu  this op's own ReLU backward is applied by its consumer.
+    """
 
     @staticmethod
-    def forward(ctx, x, residual, anchor, W, b, act):
+    def forward(ctx, x, residual, anchor, W, b, act, mask_input=False, defer_relu=False):
         x2 = _flat2(x)
         r2 = _flat2(residual) if residual is not None else None
-        y = K.gemm(x2, W.value, bias=b.value if b is not None else None, act=act, residual=r2)
+        y = K.gemm(x2, W.value, bias=b.master if b is not None else None, act=act, residual=r2)
         ctx.W, ctx.b, ctx.act = W, b, act
         ctx.has_res = residual is not None
-        ctx.save_for_backward(x2, y if act in (ACT_RELU,) else (x2 if act == ACT_GELU else None))
+        ctx.mask_input = mask_input
+        ctx.relu_here = act == ACT_RELU and not defer_relu
+        if act == ACT_GELU:
+            raise NotImplementedError("GELU is not fused into the dense GEMM")
+        ctx.save_for_backward(x2, y if ctx.relu_here else None)
         return y.reshape(*x.shape[:-1], W.shape[1])
 
     @staticmethod
@@ -57,10 +67,8 @@ class DenseFn(torch.autograd.Function):
         g2 = _flat2(gy)
         if g2.dtype != x2.dtype:
             g2 = g2.to(x2.dtype)
-        if ctx.act == ACT_RELU:
-            g2 = K.binary(g2, saved, K.BIN_RELU_BWD)
-        elif ctx.act == ACT_GELU:
-            raise NotImplementedError("GELU-fused dense backward needs the pre-activation")
+        if ctx.relu_here:
+            g2 = K.binary(g2.contiguous(), saved, K.BIN_RELU_BWD)
         acc = W.take_accumulate_flag()
         K.gemm(x2.t(), g2, out=W.grad, beta=1.0 if acc else 0.0)
         if b is not None:
@@ -70,13 +78,14 @@ class DenseFn(torch.autograd.Function):
             b.grad_ready()
         dx = None
         if ctx.needs_input_grad[0]:
-            dx = K.gemm(g2, W.value.t()).reshape(*gy.shape[:-1], W.shape[0])
+            dx = K.gemm(g2, W.value.t(), relu_mask=x2 if ctx.mask_input else None).reshape(*gy.shape[:-1],
+                                                                                          W.shape[0])
         dres = gy if ctx.has_res and ctx.needs_input_grad[1] else None
-        return dx, dres, None, None, None, None
+        return dx, dres, None, None, None, None, None, None
 
 
-def dense(x, W, b=None, act=ACT_NONE, residual=None):
-    return DenseFn.apply(x, residual, _ANCHOR, W, b, act)
+def dense(x, W, b=None, act=ACT_NONE, residual=None, mask_input=False, defer_relu=False):
+    return DenseFn.apply(x, residual, _ANCHOR, W, b, act, mask_input, defer_relu)
 
 
 class ActivationFn(torch.autograd.Function):
@@ -115,7 +124,7 @@ class SoftmaxFn(torch.autograd.Function):
 class Conv2dFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, anchor, W, b, stride, pad, relu):
-        y = NN.conv2d_fwd(x.contiguous(), W.value, b.value if b is not None else None, stride, pad, relu)
+        y = NN.conv2d_fwd(x.contiguous(), W.value, b.master if b is not None else None, stride, pad, relu)
         ctx.W, ctx.b, ctx.stride, ctx.pad, ctx.relu = W, b, stride, pad, relu
         ctx.xshape = tuple(x.shape)
         ctx.save_for_backward(x, y if relu else None)
@@ -171,8 +180,8 @@ class BatchNormFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, anchor, gamma, beta, run_mean, run_var, cfg):
-        y, mean, rstd = NN.batchnorm_fwd(x.contiguous(), gamma.value if gamma else None,
-                                         beta.value if beta else None, run_mean, run_var, cfg["momentum"],
+        y, mean, rstd = NN.batchnorm_fwd(x.contiguous(), gamma.master if gamma else None,
+                                         beta.master if beta else None, run_mean, run_var, cfg["momentum"],
                                          cfg["eps"], cfg["training"], cfg["relu"], cfg["p"], cfg["stream"],
                                          cfg["seed"], 0, cfg["step_t"])
         ctx.gamma, ctx.beta, ctx.cfg = gamma, beta, cfg
@@ -187,7 +196,7 @@ class BatchNormFn(torch.autograd.Function):
         if beta is not None:
             beta.take_accumulate_flag()
         dx = NN.batchnorm_bwd(x.contiguous(), gy.contiguous().to(x.dtype), mean, rstd,
-                              gamma.value if gamma else None, beta.value if beta else None,
+                              gamma.master if gamma else None, beta.master if beta else None,
                               gamma.grad if gamma else None, beta.grad if beta else None, acc, cfg["relu"],
                               cfg["p"] if cfg["training"] else 0.0, cfg["stream"], cfg["seed"], 0, cfg["step_t"])
         if gamma is not None:
@@ -200,8 +209,8 @@ class BatchNormFn(torch.autograd.Function):
 class LayerNormFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, anchor, gamma, beta, eps):
-        y, mean, rstd = NN.layernorm_fwd(x.contiguous(), gamma.value if gamma else None,
-                                         beta.value if beta else None, eps)
+        y, mean, rstd = NN.layernorm_fwd(x.contiguous(), gamma.master if gamma else None,
+                                         beta.master if beta else None, eps)
         ctx.gamma, ctx.beta = gamma, beta
         ctx.save_for_backward(x, mean, rstd)
         return y
@@ -213,7 +222,7 @@ class LayerNormFn(torch.autograd.Function):
         acc = gamma.take_accumulate_flag() if gamma is not None else False
         if beta is not None:
             beta.take_accumulate_flag()
-        dx = NN.layernorm_bwd(x.contiguous(), gamma.value if gamma else None, mean, rstd,
+        dx = NN.layernorm_bwd(x.contiguous(), gamma.master if gamma else None, mean, rstd,
                               gy.contiguous().to(x.dtype), gamma.grad if gamma else None,
                               beta.grad if beta else None, acc)
         if gamma is not None:
@@ -285,7 +294,7 @@ class ChannelAffineFn(torch.autograd.Function):
         shape = [1, x.shape[1]] + [1] * (x.dim() - 2)
         ctx.gamma, ctx.beta, ctx.shape = gamma, beta, shape
         ctx.save_for_backward(x)
-        return (x.float() * gamma.value.reshape(shape) + beta.value.reshape(shape)).to(x.dtype)
+        return (x.float() * gamma.master.reshape(shape) + beta.master.reshape(shape)).to(x.dtype)
 
     @staticmethod
     def backward(ctx, gy):
@@ -301,4 +310,85 @@ class ChannelAffineFn(torch.autograd.Function):
             else:
                 p.grad.copy_(v)
             p.grad_ready()
-        return (g * gamma.value.reshape(shape)).to(x.dtype), None, None, None
+        return (g * gamma.master.reshape(shape)).to(x.dtype), None, None, None
+
+
+class TransformerBlockFn(torch.autograd.Function):
+    """One pre-norm encoder block as a single autograd node:
+
+        h1 = LN1(x);  qkv = h1 Wqkv;  a = attn(qkv);  h = a Wo + x
+        h2 = LN2(h);  f = relu(h2 W1 + b1);           y = f W2 + b2 + h
+
+    Forward fuses both residual adds and the ReLU into GEMM epilogues.  The
+    hand-written backward fuses the ReLU backward into the dF GEMM epilogue
+    and both residual-gradient sums into the layer-norm backward kernels, so
+    a block's backward launches only this framework's kernels.
+    """
+
+    @staticmethod
+    def forward(ctx, x, anchor, blk):
+        B, S, E = x.shape
+        H, D = blk.attn.num_heads, blk.attn.head_dim
+        scale = 1.0 / math.sqrt(D)
+        ln1, ln2, at, f1, f2 = blk.ln1, blk.ln2, blk.attn, blk.ff1, blk.ff2
+        x2 = _flat2(x)
+        h1, m1, r1 = NN.layernorm_fwd(x2, ln1.gamma.master, ln1.beta.master, ln1.eps)
+        qkv = K.gemm(h1, at.w_qkv.value)
+        a, probs = NN.attention_fwd(qkv.reshape(B, S, 3 * E), B, S, H, D, scale)
+        a2 = _flat2(a)
+        h = K.gemm(a2, at.w_o.value, residual=x2)
+        h2, m2, r2 = NN.layernorm_fwd(h, ln2.gamma.master, ln2.beta.master, ln2.eps)
+        f = K.gemm(h2, f1.weight.value, bias=f1.bias.master, act=ACT_RELU)
+        y = K.gemm(f, f2.weight.value, bias=f2.bias.master, residual=h)
+        ctx.blk, ctx.dims = blk, (B, S, H, D, scale)
+        ctx.save_for_backward(x2, h1, m1, r1, qkv, probs, a2, h, h2, m2, r2, f)
+        return y.reshape(B, S, E)
+
+    @staticmethod
+    def backward(ctx, gy):
+        x2, h1, m1, r1, qkv, probs, a2, h, h2, m2, r2, f = ctx.saved_tensors
+        blk = ctx.blk
+        B, S, H, D, scale = ctx.dims
+        ln1, ln2, at, f1, f2 = blk.ln1, blk.ln2, blk.attn, blk.ff1, blk.ff2
+        g = _flat2(gy)
+        if g.dtype != x2.dtype:
+            g = g.to(x2.dtype)
+        g = g.contiguous()
+
+        def wgrad(p, a_t, grad):
+            K.gemm(a_t, grad, out=p.grad, beta=1.0 if p.take_accumulate_flag() else 0.0)
+
+        def bgrad(p, grad):
+            K.colsum(grad, out=p.grad, accumulate=p.take_accumulate_flag())
+
+        # FFN: y = f W2 + b2 + h
+        wgrad(f2.weight, f.t(), g)
+        bgrad(f2.bias, g)
+        f2.weight.grad_ready()
+        f2.bias.grad_ready()
+        df = K.gemm(g, f2.weight.value.t(), relu_mask=f)          # ReLU backward fused
+        wgrad(f1.weight, h2.t(), df)
+        bgrad(f1.bias, df)
+        f1.weight.grad_ready()
+        f1.bias.grad_ready()
+        dh2 = K.gemm(df, f1.weight.value.t())
+        acc = ln2.gamma.take_accumulate_flag()
+        ln2.beta.take_accumulate_flag()
+        dh = NN.layernorm_bwd(h, ln2.gamma.master, m2, r2, dh2, ln2.gamma.grad, ln2.beta.grad, acc, dres=g)
+        ln2.gamma.grad_ready()
+        ln2.beta.grad_ready()
+        # attention: h = a Wo + x
+        wgrad(at.w_o, a2.t(), dh)
+        at.w_o.grad_ready()
+        da = K.gemm(dh, at.w_o.value.t())
+        dqkv = NN.attention_bwd(qkv.reshape(B, S, -1), probs, da.reshape(B, S, -1), B, S, H, D, scale)
+        dqkv2 = _flat2(dqkv)
+        wgrad(at.w_qkv, h1.t(), dqkv2)
+        at.w_qkv.grad_ready()
+        dh1 = K.gemm(dqkv2, at.w_qkv.value.t())
+        acc = ln1.gamma.take_accumulate_flag()
+        ln1.beta.take_accumulate_flag()
+        dx = NN.layernorm_bwd(x2, ln1.gamma.master, m1, r1, dh1, ln1.gamma.grad, ln1.beta.grad, acc, dres=dh)
+        ln1.gamma.grad_ready()
+        ln1.beta.grad_ready()
+        return dx.reshape(B, S, -1), None, None

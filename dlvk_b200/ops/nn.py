@@ -162,9 +162,13 @@ def layernorm_fwd(x, gamma, beta, eps: float):
     return y.to(x.dtype), mean.reshape(-1), rstd.reshape(-1)
 
 
-def layernorm_bwd(x, gamma, mean, rstd, dy, dgamma, dbeta, accumulate: bool):
+def layernorm_bwd(x, gamma, mean, rstd, dy, dgamma, dbeta, accumulate: bool, dres=None):
+    """dx (+ dres, the gradient of a residual branch sharing the input)."""
     if native(x):
-        return N().layernorm_bwd(x, gamma, mean, rstd, dy, dgamma, dbeta, accumulate)
+        return N().layernorm_bwd(x, gamma, mean, rstd, dy, dgamma, dbeta, accumulate, dres)
+    if dres is not None:
+        out = layernorm_bwd(x, gamma, mean, rstd, dy, dgamma, dbeta, accumulate)
+        return (out.float() + dres.float()).to(x.dtype)
     D = x.shape[-1]
     xf = x.float().reshape(-1, D)
     g = dy.float().reshape(-1, D)
