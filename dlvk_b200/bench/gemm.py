@@ -38,6 +38,10 @@ def main():
     ap.add_argument("--shapes", nargs="*", default=None)
     ap.add_argument("--no-cublas", action="store_true")
     ap.add_argument("--check", action="store_true")
+    ap.add_argument("--bias", action="store_true", help="fp32 bias in the epilogue")
+    ap.add_argument("--relu", action="store_true", help="ReLU in the epilogue")
+    ap.add_argument("--residual", action="store_true", help="residual add in the epilogue")
+    ap.add_argument("--mask", action="store_true", help="ReLU-mask input in the epilogue")
     args = ap.parse_args()
     C = _ext.C()
     shapes = DEFAULT
@@ -51,8 +55,17 @@ def main():
         a, b = make(M, N, K, am, bm)
         out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
         flops = 2.0 * M * N * K
-        t_ours = time_fn(lambda: C.gemm(a, b, out=out, force_path=1), iters=args.iters)
-        rec = {"M": M, "N": N, "K": K, "a": am, "b": bm, "ours_ms": round(t_ours, 4),
+        kw = {}
+        if args.bias:
+            kw["bias"] = torch.randn(N, device="cuda")
+        if args.relu:
+            kw["act"] = 1
+        if args.residual:
+            kw["residual"] = torch.randn(M, N, device="cuda").bfloat16()
+        if args.mask:
+            kw["relu_mask"] = torch.randn(M, N, device="cuda").bfloat16()
+        t_ours = time_fn(lambda: C.gemm(a, b, out=out, force_path=1, **kw), iters=args.iters)
+        rec = {"M": M, "N": N, "K": K, "a": am, "b": bm, "epilogue": sorted(kw), "ours_ms": round(t_ours, 4),
                "ours_tflops": round(flops / t_ours / 1e9, 1), "ours_frac_of_measured": round(flops / t_ours / 1e9 / peak, 3)}
         if not args.no_cublas:
             t_cb = time_fn(lambda: torch.matmul(a, b, out=out), iters=args.iters)

@@ -76,7 +76,13 @@ void gemm_simt(DType in_dt, DType out_dt, const GemmArgs& a, cudaStream_t s);
 bool gemm_tc_supported(const GemmArgs& a);
 // bf16 inputs, bf16 or f32 output, tcgen05 tensor cores.  `err` is the
 // device error word; `max_ctas` caps the persistent grid (0 = #SMs).
-void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int max_ctas = 0);
+// Split-K: when the tile grid underfills the GPU, partial sums go to an fp32
+// `workspace` of gemm_tc_workspace_floats() floats (0 = no split chosen) and a
+// reduce kernel applies the epilogue.  With a null/small workspace the GEMM
+// runs unsplit.
+int64_t gemm_tc_workspace_floats(const GemmArgs& a, int max_ctas = 0);
+void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int max_ctas = 0,
+             float* workspace = nullptr, int64_t workspace_floats = 0);
 
 // ---- optimizers --------------------------------------------------------------
 enum OptKind : int { OPT_SGD = 0, OPT_ADAM = 1, OPT_RMSPROP = 2 };

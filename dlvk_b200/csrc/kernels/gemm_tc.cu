@@ -5,10 +5,10 @@
 // projections and the batched attention products.
 //
 // Design:
-//  * persistent kernel, one CTA per SM, 192 threads = 6 warps:
+//  * persistent kernel, one CTA per SM, 320 threads = 10 warps:
 //      warp 0      TMA producer (one lane) over a STAGES-deep smem ring
 //      warp 1      TMEM allocator + MMA issuer (one lane)
-//      warps 2..5  epilogue: tcgen05.ld 32x32b -> alpha/beta/bias/act -> global
+//      warps 2..9  epilogue: tcgen05.ld 32x32b -> alpha/beta/bias/act -> global
 //  * tile 128 x BN x 64 (BN = 256 or 128), UMMA 128 x BN x 16 (kind::f16, bf16
 //    in, f32 accumulate), two TMEM accumulator buffers so the epilogue of tile
 //    i overlaps the main loop of tile i+1.
@@ -54,6 +54,9 @@ struct TcParams {
   int bias_f32;
   int act;
   uint32_t* err;
+  int splits;          // split-K factor (1 = off); partials go to C (fp32 workspace)
+  int kb_per_split;
+  int64_t split_stride;  // elements between split slices of the workspace
 };
 
 template <int BN>
@@ -63,7 +66,7 @@ struct Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (BN == 256) ? 4 : 6;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int EPI_BYTES = 4 * 32 * 33 * 4;  // per-warp 32x33 fp32 staging
+  static constexpr int EPI_BYTES = 8 * 32 * 33 * 4;  // per-warp 32x33 fp32 staging
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + EPI_BYTES;
 };
 
@@ -81,10 +84,45 @@ __device__ __forceinline__ void tile_coords(int t, const TcParams& p, int& tm, i
   tn = rr / gsz;
 }
 
-__device__ __forceinline__ float act_apply(int act, float v) {
-  if (act == ACT_RELU) return fmaxf(v, 0.f);
-  if (act == ACT_GELU) return 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
-  return v;
+// Epilogue element loops below branch once per chunk, never per element: a
+// per-element select between activation or bias variants inside a fully
+// unrolled 32-wide loop is compiled to predicated code for every variant and
+// made the epilogue, not the tensor cores, the bottleneck.
+template <int VEC>
+__device__ __forceinline__ void apply_act(int act, float* v) {
+  if (act == ACT_RELU) {
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) v[k] = fmaxf(v[k], 0.f);
+  } else if (act == ACT_GELU) {
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) v[k] = 0.5f * v[k] * (1.f + erff(v[k] * 0.70710678118654752f));
+  }
+}
+
+template <int VEC>
+__device__ __forceinline__ void add_bias(const void* bias, bool f32, int n, int valid, float* v) {
+  if (f32) {
+    const float* b = reinterpret_cast<const float*>(bias) + n;
+    if (valid == VEC && (VEC % 4) == 0 && (reinterpret_cast<uintptr_t>(b) & 15) == 0) {
+#pragma unroll
+      for (int k = 0; k < VEC; k += 4) {
+        const float4 t = *reinterpret_cast<const float4*>(b + k);
+        v[k] += t.x;
+        v[k + 1] += t.y;
+        v[k + 2] += t.z;
+        v[k + 3] += t.w;
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < VEC; ++k)
+        if (k < valid) v[k] += b[k];
+    }
+  } else {
+    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(bias) + n;
+#pragma unroll
+    for (int k = 0; k < VEC; ++k)
+      if (k < valid) v[k] += __bfloat162float(b[k]);
+  }
 }
 
 template <typename T> __device__ __forceinline__ float ld_elem(const void* p, int64_t i) {
@@ -111,11 +149,65 @@ __device__ __forceinline__ void epi_store(const TcParams& p, const float* stg, i
                                           int64_t cb, int64_t rb, int64_t mb) {
   constexpr int LPR = 32 / VEC;           // lanes per row
   constexpr int RPP = 32 / LPR;           // rows per pass
+  constexpr int NP = 32 / RPP;            // passes
   const int cg = lane % LPR, rr = lane / LPR;
   const int n = n0 + cg * VEC;
   const int valid = max(0, min(VEC, p.N - n));
+  // Fast path: whole 16-byte vectors everywhere.  All global reads of the
+  // chunk (beta*C, residual, mask) are issued before any is consumed, so the
+  // chunk pays one memory latency instead of one per pass.
+  // Exactly one auxiliary input (beta*C, residual or mask) is prefetched.
+  const int naux = (p.beta != 0.f) + (p.R != nullptr) + (p.Mk != nullptr);
+  const bool fast = naux == 1 && valid == VEC && p.vec_ok && (!p.R || p.r_vec) && (!p.Mk || p.m_vec) &&
+                    row0 + 32 <= p.M;
+  if (fast) {
+    const T* abase;
+    int64_t aoff, ald;
+    if (p.beta != 0.f) {
+      abase = reinterpret_cast<const T*>(p.C); aoff = cb; ald = p.ldc;
+    } else if (p.R) {
+      abase = reinterpret_cast<const T*>(p.R); aoff = rb; ald = p.ldr;
+    } else {
+      abase = reinterpret_cast<const T*>(p.Mk); aoff = mb; ald = p.ldm;
+    }
+    uint4 av[NP];
+#pragma unroll
+    for (int ps = 0; ps < NP; ++ps)
+      av[ps] = *reinterpret_cast<const uint4*>(abase + aoff + (int64_t)(row0 + ps * RPP + rr) * ald + n);
+    float bv[VEC];
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) bv[k] = 0.f;
+    if (p.bias) add_bias<VEC>(p.bias, p.bias_f32, n, valid, bv);
+    const int mode = p.beta != 0.f ? 0 : (p.R ? 1 : 2);
+#pragma unroll
+    for (int ps = 0; ps < NP; ++ps) {
+      const int rl = ps * RPP + rr;
+      float v[VEC];
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) v[k] = stg[rl * 33 + cg * VEC + k] + bv[k];
+      const T* e = reinterpret_cast<const T*>(&av[ps]);
+      if (mode == 0) {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) v[k] += p.beta * to_f32(e[k]);
+      } else if (mode == 1) {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) v[k] += to_f32(e[k]);
+      }
+      apply_act<VEC>(p.act, v);
+      if (mode == 2) {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) v[k] = to_f32(e[k]) > 0.f ? v[k] : 0.f;
+      }
+      uint4 u;
+      T* eo = reinterpret_cast<T*>(&u);
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) eo[k] = from_f32<T>(v[k]);
+      *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.C) + cb + (int64_t)(row0 + rl) * p.ldc + n) = u;
+    }
+    return;
+  }
 #pragma unroll 1
-  for (int pass = 0; pass < 32 / RPP; ++pass) {
+  for (int pass = 0; pass < NP; ++pass) {
     const int rl = pass * RPP + rr;
     const int row = row0 + rl;
     if (row >= p.M || valid == 0) continue;
@@ -129,21 +221,14 @@ __device__ __forceinline__ void epi_store(const TcParams& p, const float* stg, i
 #pragma unroll
       for (int k = 0; k < VEC; ++k) v[k] += p.beta * o[k];
     }
-    if (p.bias) {
-#pragma unroll
-      for (int k = 0; k < VEC; ++k)
-        if (k < valid) v[k] += p.bias_f32 ? ld_elem<float>(p.bias, n + k) : ld_elem<__nv_bfloat16>(p.bias, n + k);
-    }
+    if (p.bias) add_bias<VEC>(p.bias, p.bias_f32, n, valid, v);
     if (p.R) {
       float o[VEC];
       ld_vec<T, VEC>(p.R, rb + (int64_t)row * p.ldr + n, valid, p.r_vec, o);
 #pragma unroll
       for (int k = 0; k < VEC; ++k) v[k] += o[k];
     }
-    if (p.act != ACT_NONE) {
-#pragma unroll
-      for (int k = 0; k < VEC; ++k) v[k] = act_apply(p.act, v[k]);
-    }
+    apply_act<VEC>(p.act, v);
     if (p.Mk) {
       float o[VEC];
       ld_vec<T, VEC>(p.Mk, mb + (int64_t)row * p.ldm + n, valid, p.m_vec, o);
@@ -164,7 +249,7 @@ __device__ __forceinline__ void epi_store(const TcParams& p, const float* stg, i
 }
 
 template <int BN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, TcParams p) {
   using C = Cfg<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -177,7 +262,8 @@ __global__ void __launch_bounds__(192, 1)
   float* epi = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES + 256);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int num_tiles = p.tiles_m * p.tiles_n * p.batch;
+  const int tiles_per_split = p.tiles_m * p.tiles_n * p.batch;
+  const int num_tiles = tiles_per_split * p.splits;  // work units
   const int num_kb = (p.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -187,7 +273,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 128);
+      mbar_init(&tempty[i], 256);
     }
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -209,9 +295,11 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
         int tm, tn, b;
-        tile_coords(t, p, tm, tn, b);
+        const int sp = t / tiles_per_split;
+        tile_coords(t - sp * tiles_per_split, p, tm, tn, b);
         const int bo = b / p.batch2, bi = b - bo * p.batch2;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int kb0 = sp * p.kb_per_split, kb1 = min(num_kb, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.err)) goto producer_done;
           uint8_t* sA = smem + stage * C::STAGE_BYTES;
           uint8_t* sB = sA + C::A_BYTES;
@@ -250,7 +338,9 @@ __global__ void __launch_bounds__(192, 1)
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * BN);
         bool ok = true;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int sp = t / tiles_per_split;
+        const int kb0 = sp * p.kb_per_split, kb1 = min(num_kb, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.err)) { ok = false; break; }
           tc_fence_after();
           const uint32_t aBase = smem_u32(smem + stage * C::STAGE_BYTES);
@@ -261,7 +351,7 @@ __global__ void __launch_bounds__(192, 1)
                                        : make_sw128_desc(aBase + k * 32, 16, 1024);
             const uint64_t bd = p.b_mn ? make_sw128_desc(bBase + k * 2048, 8192, 1024)
                                        : make_sw128_desc(bBase + k * 32, 16, 1024);
-            mma_f16(d, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            mma_f16(d, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           mma_commit(&empty[stage]);
           if (++stage == C::STAGES) {
@@ -278,38 +368,88 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    // Epilogue warps 2..5.  TMEM lane quarter accessible to a warp = warp % 4.
-    // Each 32x32 accumulator chunk is staged through shared memory so that
-    // every global access (C, beta*C, bias, residual, ReLU mask) is a
-    // coalesced 16-byte access along rows instead of one row per lane.
+    // Epilogue warps 2..9: two warps per TMEM lane quarter (warp % 4), each
+    // owning half of the tile's columns.  The TMEM load of the next 32-column
+    // chunk is issued before the current chunk is processed.  Plain epilogues
+    // (alpha, bias, activation) store straight from registers; with beta,
+    // residual or ReLU mask the chunk is staged through shared memory so that
+    // every extra global access is a coalesced 16-byte access along a row.
+    const int ew = warp - 2;
     const int q = warp & 3;
-    float* stg = epi + (warp - 2) * (32 * 33);
+    const int half = ew >> 2;
+    float* stg = epi + ew * (32 * 33);
+    const bool staged = (p.R != nullptr) || (p.Mk != nullptr) || (p.beta != 0.f);
+    constexpr int NCH = BN / 64;  // 32-column chunks per warp
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       int tm, tn, b;
-      tile_coords(t, p, tm, tn, b);
+      const int sp = t / tiles_per_split;
+      tile_coords(t - sp * tiles_per_split, p, tm, tn, b);
       if (!mbar_wait(&tfull[acc], acc_phase, p.err)) break;
       tc_fence_after();
       const int bo = b / p.batch2, bi = b - bo * p.batch2;
-      const int64_t cb = (int64_t)bo * p.bsc + (int64_t)bi * p.bsc2;
+      const int64_t cb = (int64_t)sp * p.split_stride + (int64_t)bo * p.bsc + (int64_t)bi * p.bsc2;
       const int64_t rb = (int64_t)bo * p.bsr + (int64_t)bi * p.bsr2;
       const int64_t mb = (int64_t)bo * p.bsm + (int64_t)bi * p.bsm2;
       const int row0 = tm * BM + q * 32;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
-        tmem_ld_wait();
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + half * NCH * 32);
+      uint32_t r[2][32];
+      tmem_ld32(tbase, r[0]);
+      tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) stg[lane * 33 + j] = __uint_as_float(r[j]) * p.alpha;
-        __syncwarp();
-        const int n0 = tn * BN + c * 32;
-        if (n0 < p.N && row0 < p.M) {
-          if (p.out_f32) epi_store<float, 4>(p, stg, row0, n0, lane, cb, rb, mb);
-          else epi_store<__nv_bfloat16, 8>(p, stg, row0, n0, lane, cb, rb, mb);
+      for (int i = 0; i < NCH; ++i) {
+        if (i + 1 < NCH) tmem_ld32(tbase + (uint32_t)((i + 1) * 32), r[(i + 1) & 1]);
+        const int n0 = tn * BN + (half * NCH + i) * 32;
+        if (staged) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) stg[lane * 33 + j] = __uint_as_float(r[i & 1][j]) * p.alpha;
+          __syncwarp();
+          if (n0 < p.N && row0 < p.M) {
+            if (p.out_f32) epi_store<float, 4>(p, stg, row0, n0, lane, cb, rb, mb);
+            else epi_store<__nv_bfloat16, 8>(p, stg, row0, n0, lane, cb, rb, mb);
+          }
+          __syncwarp();
+        } else {
+          const int row = row0 + lane;
+          if (row < p.M && n0 < p.N) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[i & 1][j]) * p.alpha;
+            if (p.bias) add_bias<32>(p.bias, p.bias_f32, n0, min(32, p.N - n0), v);
+            apply_act<32>(p.act, v);
+            const bool full = (n0 + 32 <= p.N) && p.vec_ok;
+            if (p.out_f32) {
+              float* dst = reinterpret_cast<float*>(p.C) + cb + (int64_t)row * p.ldc + n0;
+              if (full) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                  reinterpret_cast<float4*>(dst)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (n0 + j < p.N) dst[j] = v[j];
+              }
+            } else {
+              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + cb + (int64_t)row * p.ldc + n0;
+              if (full) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  uint4 u;
+                  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+                  for (int k = 0; k < 4; ++k) h[k] = __floats2bfloat162_rn(v[8 * j + 2 * k], v[8 * j + 2 * k + 1]);
+                  reinterpret_cast<uint4*>(dst)[j] = u;
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (n0 + j < p.N) dst[j] = __float2bfloat16_rn(v[j]);
+              }
+            }
+          }
         }
-        __syncwarp();
+        if (i + 1 < NCH) tmem_ld_wait();
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
@@ -379,13 +519,75 @@ void launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, 
     DLVK_CUDA_CHECK(cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_set[dev] = true;
   }
-  const int tiles = p.tiles_m * p.tiles_n * p.batch;
+  const int tiles = p.tiles_m * p.tiles_n * p.batch * p.splits;
   int grid = std::min(tiles, max_ctas > 0 ? max_ctas : sm_count());
-  gemm_tc_kernel<BN><<<grid, 192, C::SMEM, s>>>(ta, tb, p);
+  gemm_tc_kernel<BN><<<grid, 320, C::SMEM, s>>>(ta, tb, p);
   DLVK_POST_LAUNCH();
 }
 
 inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Split-K reduction: C = act(alpha * sum_s W[s] + beta * C + bias + R), masked.
+// W is the fp32 workspace [splits][batch][M][N]; summation is in split order
+// (deterministic).  One thread per output element.
+template <typename T>
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int64_t per_split, GemmArgs a) {
+  const int64_t MN = a.M * a.N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < per_split;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float acc = 0.f;
+    for (int s2 = 0; s2 < splits; ++s2) acc += ws[s2 * per_split + i];
+    const int64_t b = i / MN, r = i - b * MN;
+    const int64_t m = r / a.N, n = r - m * a.N;
+    const int64_t bo = b / a.batch2, bi = b - bo * a.batch2;
+    T* c = reinterpret_cast<T*>(a.C) + bo * a.batch_stride_c + bi * a.batch2_stride_c + m * a.ldc + n;
+    float v = a.alpha * acc;
+    if (a.beta != 0.f) v += a.beta * to_f32(*c);
+    if (a.bias)
+      v += a.bias_dtype == (int)DType::F32 ? reinterpret_cast<const float*>(a.bias)[n]
+                                           : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.bias)[n]);
+    if (a.residual)
+      v += to_f32(reinterpret_cast<const T*>(a.residual)[bo * a.batch_stride_r + bi * a.batch2_stride_r + m * a.ldr + n]);
+    if (a.act == ACT_RELU) v = fmaxf(v, 0.f);
+    else if (a.act == ACT_GELU) v = 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
+    if (a.relu_mask &&
+        !(to_f32(reinterpret_cast<const T*>(a.relu_mask)[bo * a.batch_stride_m + bi * a.batch2_stride_m + m * a.ldm + n]) >
+          0.f))
+      v = 0.f;
+    *c = from_f32<T>(v);
+  }
+}
+
+// Tile shape and split-K choice from a small time model: per-SM tensor rate
+// ~8 TFLOP/s at BN = 256 (15% less at BN = 128, which reloads A twice as
+// often per FLOP), whole waves of persistent CTAs, and for split-K the fp32
+// workspace write + read at ~5 TB/s plus one extra launch.
+void choose_tiling(const GemmArgs& a, int sms, int& BN, int& splits) {
+  const int64_t kbs = (a.K + BK - 1) / BK;
+  const int64_t tm = (a.M + BM - 1) / BM;
+  const double sm_flops = 8.1e12;
+  double best = 1e300;
+  BN = 256;
+  splits = 1;
+  for (int bn : {256, 128}) {
+    if (bn == 256 && a.N < 256) continue;
+    const double eff = bn == 256 ? 1.0 : 0.85;
+    const int64_t tiles = tm * ((a.N + bn - 1) / bn) * a.batch * a.batch2;
+    for (int sp : {1, 2, 3, 4, 6, 8}) {
+      if (sp > 1 && kbs / sp < 8) break;
+      const int64_t units = tiles * sp;
+      const int64_t waves = (units + sms - 1) / sms;
+      const double unit_s = (double)BM * bn * BK * 2.0 * ((kbs + sp - 1) / sp) / (sm_flops * eff);
+      double t = waves * unit_s;
+      if (sp > 1) t += (double)sp * a.M * a.N * a.batch * a.batch2 * 8.0 / 5e12 + 5e-6;
+      if (t < best * 0.97) {
+        best = t;
+        BN = bn;
+        splits = sp;
+      }
+    }
+  }
+}
 
 }  // namespace
 
@@ -405,7 +607,8 @@ bool gemm_tc_supported(const GemmArgs& a) {
   return true;
 }
 
-void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int max_ctas) {
+void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int max_ctas, float* workspace,
+             int64_t workspace_floats) {
   DLVK_CHECK(gemm_tc_supported(a), "gemm_tc: unsupported layout/alignment");
   if (a.M == 0 || a.N == 0) return;
   // The tensor-map encoder is a driver call and needs a current context on
@@ -423,7 +626,9 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
   }
   const bool a_k = (a.sak == 1);
   const bool b_k = (a.sbk == 1);
-  const int BN = (a.N >= 256) ? 256 : 128;
+  int BN = 256, splits = 1;
+  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits);
+  if (workspace == nullptr || workspace_floats < (int64_t)splits * a.M * a.N * a.batch * a.batch2) splits = 1;
   // Unused batch levels get a harmless stride (a multiple of 16 bytes).
   auto pick = [](int64_t cnt, int64_t stride, uint64_t dflt) { return cnt > 1 ? (uint64_t)stride : dflt; };
   CUtensorMap ta, tb;
@@ -481,8 +686,42 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
   p.bias_f32 = (a.bias_dtype == (int)DType::F32);
   p.act = a.act;
   p.err = err;
+  p.splits = splits;
+  p.kb_per_split = (int)(((a.K + BK - 1) / BK + splits - 1) / splits);
+  p.split_stride = 0;
+  if (splits > 1) {
+    // Partial accumulators go to the fp32 workspace; the reduce kernel
+    // applies alpha/beta/bias/residual/act/mask and writes C.
+    const int64_t per = a.M * a.N * a.batch * a.batch2;
+    p.C = workspace;
+    p.out_f32 = 1;
+    p.ldc = a.N;
+    p.bsc = a.M * a.N * a.batch2;
+    p.bsc2 = a.M * a.N;
+    p.split_stride = per;
+    p.vec_ok = al16(workspace) && (a.N % 4 == 0);
+    p.alpha = 1.f;
+    p.beta = 0.f;
+    p.bias = nullptr;
+    p.R = nullptr;
+    p.Mk = nullptr;
+    p.act = ACT_NONE;
+    if (BN == 256) launch_tc<256>(ta, tb, p, max_ctas, s);
+    else launch_tc<128>(ta, tb, p, max_ctas, s);
+    const int g = (int)std::min<int64_t>((per + 255) / 256, 148 * 16);
+    if (out_dt == DType::F32) splitk_reduce_kernel<float><<<g, 256, 0, s>>>(workspace, splits, per, a);
+    else splitk_reduce_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(workspace, splits, per, a);
+    DLVK_POST_LAUNCH();
+    return;
+  }
   if (BN == 256) launch_tc<256>(ta, tb, p, max_ctas, s);
   else launch_tc<128>(ta, tb, p, max_ctas, s);
+}
+
+int64_t gemm_tc_workspace_floats(const GemmArgs& a, int max_ctas) {
+  int BN = 256, splits = 1;
+  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits);
+  return splits > 1 ? (int64_t)splits * a.M * a.N * a.batch * a.batch2 : 0;
 }
 
 }  // namespace dlvk

@@ -363,12 +363,21 @@ __global__ void __launch_bounds__(256) ln_bwd_warp_kernel(const T* __restrict__ 
   }
 }
 
+// Sums the per-block partials: block (32 columns) x 8 row groups, combined in
+// a fixed order through shared memory.
 __global__ void ln_bwd_final_kernel(const float* __restrict__ part, int blocks, int D, float* __restrict__ dgamma,
                                     float* __restrict__ dbeta, int accumulate) {
-  const int d = blockIdx.x * blockDim.x + threadIdx.x;
-  if (d >= 2 * D) return;
+  __shared__ float sm[8][33];
+  const int d = blockIdx.x * 32 + threadIdx.x;
   float s = 0.f;
-  for (int b = 0; b < blocks; ++b) s += part[(int64_t)b * 2 * D + d];
+  if (d < 2 * D)
+    for (int b = threadIdx.y; b < blocks; b += 8) s += part[(int64_t)b * 2 * D + d];
+  sm[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y != 0 || d >= 2 * D) return;
+  s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s += sm[i][threadIdx.x];
   float* dst = d < D ? (dgamma ? dgamma + d : nullptr) : (dbeta ? dbeta + (d - D) : nullptr);
   if (dst) *dst = accumulate ? *dst + s : s;
 }
@@ -504,7 +513,7 @@ void layernorm_bwd(DType dt, const void* x, const float* gamma, const float* mea
                                        (const T*)dres);
       });
       DLVK_POST_LAUNCH();
-      ln_bwd_final_kernel<<<(2 * D + 255) / 256, 256, 0, s>>>(scratch, blocks, D, dgamma, dbeta, accumulate ? 1 : 0);
+      ln_bwd_final_kernel<<<(2 * D + 31) / 32, dim3(32, 8), 0, s>>>(scratch, blocks, D, dgamma, dbeta, accumulate ? 1 : 0);
       DLVK_POST_LAUNCH();
       return;
     }
@@ -520,7 +529,7 @@ void layernorm_bwd(DType dt, const void* x, const float* gamma, const float* mea
                                                       rows, D, (const T*)dres);
   });
   DLVK_POST_LAUNCH();
-  ln_bwd_final_kernel<<<(2 * D + 255) / 256, 256, 0, s>>>(scratch, blocks, D, dgamma, dbeta, accumulate ? 1 : 0);
+  ln_bwd_final_kernel<<<(2 * D + 31) / 32, dim3(32, 8), 0, s>>>(scratch, blocks, D, dgamma, dbeta, accumulate ? 1 : 0);
   DLVK_POST_LAUNCH();
 }
 

@@ -96,3 +96,49 @@ def test_gemm_simt(dtype, M, N, K):
     bias = torch.randn(N, device="cuda")
     out = C.gemm(a, b, bias=bias, act=1, force_path=2, out_dtype=torch.float32)
     _check(out, _ref(a, b, bias, 1), 1e-5 if dtype == torch.float32 else 1e-2)
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_gemm_tc_splitk_epilogues(out_dtype):
+    """Few output tiles and a long K select split-K (fp32 workspace + reduce)."""
+    C = _C()
+    torch.manual_seed(3)
+    M, N, K = 256, 384, 8192
+    a = torch.randn(K, M, device="cuda").bfloat16().t()       # M-major (like X^T in dW)
+    b = torch.randn(K, N, device="cuda").bfloat16()
+    bias = torch.randn(N, device="cuda")
+    res = torch.randn(M, N, device="cuda").to(out_dtype)
+    mask = torch.randn(M, N, device="cuda").to(out_dtype)
+    out = C.gemm(a, b, bias=bias, act=1, alpha=0.25, residual=res, relu_mask=mask, out_dtype=out_dtype, force_path=1)
+    ref = torch.relu(0.25 * (a.float() @ b.float()) + bias + res.float())
+    ref = torch.where(mask.float() > 0, ref, torch.zeros_like(ref))
+    _check(out, ref, 2e-2)
+    acc = torch.randn(M, N, device="cuda")
+    ref2 = acc + a.float() @ b.float()
+    C.gemm(a, b, beta=1.0, out=acc, force_path=1)
+    _check(acc, ref2, 2e-2)
+
+
+@pytest.mark.parametrize("epi", ["bias", "relu", "bias_relu", "residual", "mask"])
+def test_gemm_tc_epilogue_variants(epi):
+    C = _C()
+    torch.manual_seed(4)
+    M, N, K = 1000, 1040, 320
+    a = torch.randn(M, K, device="cuda").bfloat16()
+    b = torch.randn(K, N, device="cuda").bfloat16()
+    kw = {}
+    ref = a.float() @ b.float()
+    if "bias" in epi:
+        kw["bias"] = torch.randn(N, device="cuda")
+        ref = ref + kw["bias"]
+    if epi == "residual":
+        kw["residual"] = torch.randn(M, N, device="cuda").bfloat16()
+        ref = ref + kw["residual"].float()
+    if "relu" in epi:
+        kw["act"] = 1
+        ref = torch.relu(ref)
+    if epi == "mask":
+        kw["relu_mask"] = torch.randn(M, N, device="cuda").bfloat16()
+        ref = torch.where(kw["relu_mask"].float() > 0, ref, torch.zeros_like(ref))
+    out = C.gemm(a, b, force_path=1, **kw)
+    _check(out, ref, 2e-2)
