@@ -1,0 +1,116 @@
+// Bindings of the peer-memory communication layer.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "bind_common.h"
+#include "dlvk/comm.h"
+
+namespace dlvk {
+namespace bind {
+namespace {
+
+at::ScalarType scalar_of(int code) {
+  switch (code) {
+    case 0: return at::kFloat;
+    case 1: return at::kBFloat16;
+    case 3: return at::kInt;
+    case 6: return at::kLong;
+    default: TORCH_CHECK(false, "SymmetricBuffer.tensor: unsupported dtype code ", code);
+  }
+}
+
+struct PySym {
+  std::shared_ptr<SymmetricBuffer> buf;
+};
+
+// Arguments of one fused launch, gathered from tensors on the Python side.
+void fused_ar_op(std::shared_ptr<SymmetricBuffer> grads, std::shared_ptr<SymmetricBuffer> values,
+                 std::shared_ptr<SymmetricBuffer> flags, const at::Tensor& counters, int64_t bucket, int64_t start,
+                 int64_t end, const at::Tensor& master, c10::optional<at::Tensor> m, c10::optional<at::Tensor> v,
+                 const at::Tensor& hyper, int64_t kind, const at::Tensor& epoch, int64_t world, int64_t rank,
+                 bool one_shot, bool values_are_master, int64_t grad_code, int64_t value_code, int64_t ctas,
+                 double budget_s) {
+  c10::cuda::CUDAGuard g(master.device());
+  FusedARArgs a;
+  a.world = (int)world;
+  a.rank = (int)rank;
+  a.peer_grads = const_cast<const void* const*>(grads->device_ptrs());
+  a.peer_values = values->device_ptrs();
+  a.peer_flags = reinterpret_cast<uint32_t* const*>(flags->device_ptrs());
+  a.my_flags = static_cast<uint32_t*>(flags->local());
+  a.cta_counter = reinterpret_cast<unsigned int*>(counters.data_ptr<int>()) + bucket;
+  a.start = start;
+  a.end = end;
+  a.bucket = (int)bucket;
+  a.master = master.data_ptr<float>();
+  a.m = m.has_value() ? m->data_ptr<float>() : nullptr;
+  a.v = v.has_value() ? v->data_ptr<float>() : nullptr;
+  a.hyper = reinterpret_cast<const OptimHyper*>(hyper.data_ptr());
+  a.kind = (int)kind;
+  a.scale = 1.f / (float)world;
+  a.epoch_ptr = epoch.data_ptr<int64_t>();
+  a.one_shot = one_shot ? 1 : 0;
+  a.values_are_master = values_are_master ? 1 : 0;
+  a.err = device_error_word();
+  a.budget_ns = (uint64_t)(budget_s * 1e9);
+  fused_allreduce_optimizer(a, grad_code == 0 ? DType::F32 : DType::BF16, value_code == 0 ? DType::F32 : DType::BF16,
+                            (int)ctas, stream());
+}
+
+void p2p_allreduce_op(std::shared_ptr<SymmetricBuffer> data, std::shared_ptr<SymmetricBuffer> flags,
+                      const at::Tensor& counters, int64_t slot, int64_t start, int64_t end, const at::Tensor& epoch,
+                      int64_t world, int64_t rank, int64_t dtype_code, bool average, int64_t ctas, double budget_s) {
+  c10::cuda::CUDAGuard g(epoch.device());
+  FusedARArgs a;
+  a.world = (int)world;
+  a.rank = (int)rank;
+  a.peer_grads = const_cast<const void* const*>(data->device_ptrs());
+  a.peer_flags = reinterpret_cast<uint32_t* const*>(flags->device_ptrs());
+  a.my_flags = static_cast<uint32_t*>(flags->local());
+  a.cta_counter = reinterpret_cast<unsigned int*>(counters.data_ptr<int>()) + slot;
+  a.start = start;
+  a.end = end;
+  a.bucket = (int)slot;
+  a.epoch_ptr = epoch.data_ptr<int64_t>();
+  a.err = device_error_word();
+  a.budget_ns = (uint64_t)(budget_s * 1e9);
+  p2p_allreduce(a, dtype_code == 0 ? DType::F32 : DType::BF16, average, (int)ctas, stream());
+}
+
+}  // namespace
+
+void register_comm(py::module& m) {
+  auto c = m.def_submodule("comm", "NVLink peer-memory communication");
+  py::class_<SymmetricBuffer, std::shared_ptr<SymmetricBuffer>>(c, "SymmetricBuffer")
+      .def(py::init<int64_t, int>(), py::arg("bytes"), py::arg("device"))
+      .def("handle", [](const SymmetricBuffer& b) { return py::bytes(b.handle()); })
+      .def("open",
+           [](SymmetricBuffer& b, const std::vector<py::bytes>& hs, int rank) {
+             std::vector<std::string> v;
+             for (auto& h : hs) v.push_back(std::string(h));
+             b.open(v, rank);
+           })
+      .def("local_ptr", [](const SymmetricBuffer& b) { return (int64_t)(uintptr_t)b.local(); })
+      .def("nbytes", &SymmetricBuffer::bytes)
+      .def("tensor",
+           [](std::shared_ptr<SymmetricBuffer> b, int code, int64_t numel, int64_t byte_offset) {
+             auto st = scalar_of(code);
+             const int64_t esz = c10::elementSize(st);
+             TORCH_CHECK(byte_offset + numel * esz <= b->bytes(), "SymmetricBuffer.tensor: out of range");
+             auto opts = at::TensorOptions().dtype(st).device(at::kCUDA, b->device());
+             // The deleter keeps the buffer alive as long as any view exists.
+             return torch::from_blob(static_cast<char*>(b->local()) + byte_offset, {numel},
+                                     [b](void*) mutable { b.reset(); }, opts);
+           },
+           py::arg("dtype_code"), py::arg("numel"), py::arg("byte_offset") = 0);
+  c.def("fused_allreduce_optimizer", &fused_ar_op);
+  c.def("p2p_allreduce", &p2p_allreduce_op);
+  c.def("can_access_peer", [](int a, int b) {
+    int ok = 0;
+    DLVK_CUDA_CHECK(cudaDeviceCanAccessPeer(&ok, a, b));
+    return ok != 0;
+  });
+}
+
+}  // namespace bind
+}  // namespace dlvk

@@ -1,0 +1,281 @@
+// Data-parallel gradient all-reduce fused with the optimizer update, over
+// NVLink peer memory (P2P loads/stores through IPC-mapped buffers), plus the
+// plain P2P all-reduce used by the communication backend.
+//
+// Replaces the reference's RingAllReduce (src/deployment/ring_all_reduce.cpp:
+// 141-271: host-orchestrated "ring" whose transfer step records only a
+// pipeline barrier and whose add step is empty) and shaders/
+// ring_all_reduce_add.comp (never loaded by any host code).
+//
+// Protocol for one bucket [start, end) of the flat gradient buffer, epoch e
+// (a device counter bumped once per training step):
+//   1. ready:  every rank announces "my gradients of this bucket are final"
+//              by st.release.sys of e into flags[bucket][0][rank] on every
+//              peer, then all CTAs wait (ld.acquire.sys, bounded) until all
+//              ranks' ready flags equal e.
+//   2. reduce: two-shot -- rank r owns shard r: it sums the shard over all
+//              ranks in rank order (fp32, deterministic), scales by 1/world,
+//              applies the optimizer to its master/m/v and stores the new
+//              compute-dtype parameters into every rank's parameter buffer.
+//              one-shot (small buckets) -- every rank reduces the whole
+//              bucket itself and updates its own copy; no stores to peers.
+//   3. done:   the last CTA of the grid announces "finished reading your
+//              gradients / writing your parameters" to every peer and waits
+//              for all peers' done flags, so no rank starts its next step
+//              while a peer still reads its gradients or writes its params.
+// Every wait is bounded by a wall-clock budget; on expiry the kernel records
+// DLVK_ERR_PEER_TIMEOUT in the error word and returns.  No TMA and no
+// cluster multicast is used on peer memory.
+#include "dlvk/common.h"
+#include "dlvk/kernels.h"
+#include "dlvk/optim_math.h"
+#include "dlvk/comm.h"
+
+namespace dlvk {
+namespace {
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait until *flag == epoch.  Returns false (and records the timeout) after
+// budget_ns.
+__device__ bool wait_flag(const uint32_t* flag, uint32_t epoch, uint64_t budget_ns, uint32_t* err) {
+  if (ld_acquire_sys(flag) == epoch) return true;
+  const uint64_t t0 = gtimer();
+  while (true) {
+    if (ld_acquire_sys(flag) == epoch) return true;
+    if (gtimer() - t0 > budget_ns) {
+      atomicCAS(err, 0u, (uint32_t)DLVK_ERR_PEER_TIMEOUT);
+      return false;
+    }
+    __nanosleep(64);
+  }
+}
+
+__device__ __forceinline__ uint32_t* flag_slot(uint32_t* base, int bucket, int phase, int src, int world) {
+  return base + ((int64_t)bucket * 2 + phase) * world + src;
+}
+
+template <typename T> struct Pack;  // 16-byte packs
+template <> struct Pack<float> { static constexpr int N = 4; };
+template <> struct Pack<__nv_bfloat16> { static constexpr int N = 8; };
+
+template <typename T>
+__device__ __forceinline__ void load_pack(const T* p, float* out) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int k = 0; k < Pack<T>::N; ++k) out[k] = to_f32(e[k]);
+}
+
+// Phase 1 announce + wait.  All CTAs wait; CTA 0 announces.
+__device__ bool ready_barrier(const FusedARArgs& a, uint32_t epoch) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = 1;
+  __syncthreads();
+  if (blockIdx.x == 0 && threadIdx.x < a.world) {
+    __threadfence_system();
+    st_release_sys(flag_slot(a.peer_flags[threadIdx.x], a.bucket, 0, a.rank, a.world), epoch);
+  }
+  if (threadIdx.x < a.world) {
+    if (!wait_flag(flag_slot(a.my_flags, a.bucket, 0, threadIdx.x, a.world), epoch, a.budget_ns, a.err)) ok = 0;
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+// Phase 3: the last CTA to finish announces done and waits for all peers.
+__device__ void done_barrier(const FusedARArgs& a, uint32_t epoch) {
+  __shared__ int last;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) last = (atomicAdd(a.cta_counter, 1u) == gridDim.x - 1);
+  __syncthreads();
+  if (!last) return;
+  if (threadIdx.x < a.world) {
+    __threadfence_system();
+    st_release_sys(flag_slot(a.peer_flags[threadIdx.x], a.bucket, 1, a.rank, a.world), epoch);
+    wait_flag(flag_slot(a.my_flags, a.bucket, 1, threadIdx.x, a.world), epoch, a.budget_ns, a.err);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *a.cta_counter = 0u;
+}
+
+template <typename TG, typename TV>
+__global__ void __launch_bounds__(256, 5) fused_ar_opt_kernel(FusedARArgs a) {
+  const uint32_t epoch = (uint32_t)(*a.epoch_ptr);
+  if (!ready_barrier(a, epoch)) return;
+  const OptimHyper h = *a.hyper;
+  const float gs = a.scale * h.grad_scale;
+  constexpr int V = 4;  // elements per thread iteration (16 B of fp32 state)
+  const int64_t n = a.end - a.start;
+  int64_t lo = 0, hi = n;
+  if (!a.one_shot) {
+    const int64_t shard = ((n + a.world - 1) / a.world + 63) / 64 * 64;
+    lo = min(n, shard * a.rank);
+    hi = min(n, lo + shard);
+  }
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = lo + tid * V; i < hi; i += stride * V) {
+    const int64_t gi = a.start + i;
+    const int cnt = (int)min((int64_t)V, hi - i);
+    float g[V] = {0.f, 0.f, 0.f, 0.f};
+    if (cnt == V) {
+      for (int r = 0; r < a.world; ++r) {
+        const TG* src = reinterpret_cast<const TG*>(a.peer_grads[r]) + gi;
+        if (sizeof(TG) == 4) {
+          const float4 t = *reinterpret_cast<const float4*>(src);
+          g[0] += t.x; g[1] += t.y; g[2] += t.z; g[3] += t.w;
+        } else {
+          const uint2 t = *reinterpret_cast<const uint2*>(src);
+          const TG* e = reinterpret_cast<const TG*>(&t);
+#pragma unroll
+          for (int k = 0; k < V; ++k) g[k] += to_f32(e[k]);
+        }
+      }
+    } else {
+      for (int r = 0; r < a.world; ++r)
+#pragma unroll
+        for (int k = 0; k < V; ++k)
+          if (k < cnt) g[k] += to_f32(reinterpret_cast<const TG*>(a.peer_grads[r])[gi + k]);
+    }
+    float w[V], m[V], v[V];
+    TV out[V];
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      if (k < cnt) {
+        w[k] = a.master[gi + k];
+        m[k] = a.m ? a.m[gi + k] : 0.f;
+        v[k] = a.v ? a.v[gi + k] : 0.f;
+        opt_apply(a.kind, h, w[k], g[k] * gs, m[k], v[k]);
+        a.master[gi + k] = w[k];
+        if (a.m) a.m[gi + k] = m[k];
+        if (a.v) a.v[gi + k] = v[k];
+        out[k] = from_f32<TV>(w[k]);
+      }
+    }
+    if (a.values_are_master) {
+      // fp32 mode: the master is the compute copy; peers still need it.
+      if (!a.one_shot)
+        for (int r = 0; r < a.world; ++r)
+          if (r != a.rank)
+#pragma unroll
+            for (int k = 0; k < V; ++k)
+              if (k < cnt) reinterpret_cast<TV*>(a.peer_values[r])[gi + k] = out[k];
+    } else {
+      const int targets_lo = a.one_shot ? a.rank : 0;
+      const int targets_hi = a.one_shot ? a.rank + 1 : a.world;
+      for (int r = targets_lo; r < targets_hi; ++r) {
+        TV* dst = reinterpret_cast<TV*>(a.peer_values[r]) + gi;
+        if (cnt == V && sizeof(TV) == 2) {
+          uint2 u;
+          TV* e = reinterpret_cast<TV*>(&u);
+#pragma unroll
+          for (int k = 0; k < V; ++k) e[k] = out[k];
+          *reinterpret_cast<uint2*>(dst) = u;
+        } else {
+#pragma unroll
+          for (int k = 0; k < V; ++k)
+            if (k < cnt) dst[k] = out[k];
+        }
+      }
+    }
+  }
+  done_barrier(a, epoch);
+}
+
+// Plain two-shot sum all-reduce of [start, end) of a symmetric buffer, in
+// place: reduce my shard over all ranks (rank order), store the sum into every
+// rank's buffer.  Same flag protocol as the fused kernel.
+template <typename T>
+__global__ void __launch_bounds__(256, 5) p2p_allreduce_kernel(FusedARArgs a, int average) {
+  const uint32_t epoch = (uint32_t)(*a.epoch_ptr);
+  if (!ready_barrier(a, epoch)) return;
+  constexpr int V = Pack<T>::N;
+  const int64_t n = a.end - a.start;
+  const int64_t shard = ((n + a.world - 1) / a.world + 63) / 64 * 64;
+  const int64_t lo = min(n, shard * a.rank), hi = min(n, lo + shard);
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const float sc = average ? 1.f / a.world : 1.f;
+  for (int64_t i = lo + tid * V; i < hi; i += stride * V) {
+    const int64_t gi = a.start + i;
+    const int cnt = (int)min((int64_t)V, hi - i);
+    float acc[V];
+#pragma unroll
+    for (int k = 0; k < V; ++k) acc[k] = 0.f;
+    for (int r = 0; r < a.world; ++r) {
+      const T* src = reinterpret_cast<const T*>(a.peer_grads[r]) + gi;
+      if (cnt == V) {
+        float t[V];
+        load_pack<T>(src, t);
+#pragma unroll
+        for (int k = 0; k < V; ++k) acc[k] += t[k];
+      } else {
+#pragma unroll
+        for (int k = 0; k < V; ++k)
+          if (k < cnt) acc[k] += to_f32(src[k]);
+      }
+    }
+    uint4 u;
+    T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+    for (int k = 0; k < V; ++k) e[k] = from_f32<T>(acc[k] * sc);
+    // Write back only after every rank has read this shard: the sum goes to a
+    // separate region first would need a second buffer; instead each rank
+    // writes its own shard's sum to all ranks, which no rank reads again.
+    for (int r = 0; r < a.world; ++r) {
+      T* dst = reinterpret_cast<T*>(const_cast<void*>(a.peer_grads[r])) + gi;
+      if (cnt == V) *reinterpret_cast<uint4*>(dst) = u;
+      else
+#pragma unroll
+        for (int k = 0; k < V; ++k)
+          if (k < cnt) dst[k] = e[k];
+    }
+  }
+  done_barrier(a, epoch);
+}
+
+}  // namespace
+
+void fused_allreduce_optimizer(const FusedARArgs& a, DType grad_dt, DType value_dt, int ctas, cudaStream_t s) {
+  const int64_t n = a.end - a.start;
+  if (n <= 0) return;
+  DLVK_CHECK(a.world <= 512, "fused all-reduce: world size too large");
+  const int64_t work = a.one_shot ? n : (n + a.world - 1) / a.world;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ctas, (work / 4 + 255) / 256));
+  if (grad_dt == DType::F32 && value_dt == DType::BF16)
+    fused_ar_opt_kernel<float, __nv_bfloat16><<<grid, 256, 0, s>>>(a);
+  else if (grad_dt == DType::F32 && value_dt == DType::F32)
+    fused_ar_opt_kernel<float, float><<<grid, 256, 0, s>>>(a);
+  else if (grad_dt == DType::BF16 && value_dt == DType::BF16)
+    fused_ar_opt_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 256, 0, s>>>(a);
+  else
+    throw std::runtime_error("fused all-reduce: unsupported grad/value dtypes");
+  DLVK_POST_LAUNCH();
+}
+
+void p2p_allreduce(const FusedARArgs& a, DType dt, bool average, int ctas, cudaStream_t s) {
+  const int64_t n = a.end - a.start;
+  if (n <= 0) return;
+  const int64_t work = (n + a.world - 1) / a.world;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ctas, (work / 8 + 255) / 256));
+  if (dt == DType::F32) p2p_allreduce_kernel<float><<<grid, 256, 0, s>>>(a, average ? 1 : 0);
+  else if (dt == DType::BF16) p2p_allreduce_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(a, average ? 1 : 0);
+  else throw std::runtime_error("p2p all-reduce: unsupported dtype");
+  DLVK_POST_LAUNCH();
+}
+
+}  // namespace dlvk

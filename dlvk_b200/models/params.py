@@ -98,6 +98,23 @@ class ParamStore:
         p.grad = self.grad[sl].view(p.shape)
         p.store = self
 
+    def rebind(self, grad: torch.Tensor = None, value: torch.Tensor = None, master: torch.Tensor = None) -> None:
+        """Move the flat buffers into caller-provided storage (e.g. peer-mapped
+        memory for the fused all-reduce), copying current contents."""
+        if master is not None:
+            master.copy_(self.master)
+            if self.value is self.master:
+                self.value = master
+            self.master = master
+        if grad is not None:
+            grad.copy_(self.grad)
+            self.grad = grad
+        if value is not None and self.value is not self.master:
+            value.copy_(self.value)
+            self.value = value
+        for p in self.order:
+            self._bind(p)
+
     def sync_value(self) -> None:
         """Refresh the compute-dtype mirror from the fp32 master."""
         if self.value is not self.master:

@@ -73,13 +73,15 @@ class DenseFn(torch.autograd.Function):
         K.gemm(x2.t(), g2, out=W.grad, beta=1.0 if acc else 0.0)
         if b is not None:
             K.colsum(g2, out=b.grad, accumulate=b.take_accumulate_flag())
-        W.grad_ready()
-        if b is not None:
-            b.grad_ready()
         dx = None
         if ctx.needs_input_grad[0]:
             dx = K.gemm(g2, W.value.t(), relu_mask=x2 if ctx.mask_input else None).reshape(*gy.shape[:-1],
                                                                                           W.shape[0])
+        # Hooks fire only after the last read of W in this backward: a
+        # data-parallel bucket may update W in place as soon as it is ready.
+        W.grad_ready()
+        if b is not None:
+            b.grad_ready()
         dres = gy if ctx.has_res and ctx.needs_input_grad[1] else None
         return dx, dres, None, None, None, None, None, None
 
@@ -143,10 +145,10 @@ class Conv2dFn(torch.autograd.Function):
         if b is not None:
             b.take_accumulate_flag()
         NN.conv2d_wgrad(x, g, W.grad, b.grad if b is not None else None, ctx.stride, ctx.pad, accumulate=acc)
+        dx = NN.conv2d_dgrad(g, W.value, ctx.xshape, ctx.stride, ctx.pad) if ctx.needs_input_grad[0] else None
         W.grad_ready()
         if b is not None:
             b.grad_ready()
-        dx = NN.conv2d_dgrad(g, W.value, ctx.xshape, ctx.stride, ctx.pad) if ctx.needs_input_grad[0] else None
         return dx, None, None, None, None, None, None
 
 
@@ -364,31 +366,24 @@ class TransformerBlockFn(torch.autograd.Function):
         # FFN: y = f W2 + b2 + h
         wgrad(f2.weight, f.t(), g)
         bgrad(f2.bias, g)
-        f2.weight.grad_ready()
-        f2.bias.grad_ready()
         df = K.gemm(g, f2.weight.value.t(), relu_mask=f)          # ReLU backward fused
         wgrad(f1.weight, h2.t(), df)
         bgrad(f1.bias, df)
-        f1.weight.grad_ready()
-        f1.bias.grad_ready()
         dh2 = K.gemm(df, f1.weight.value.t())
         acc = ln2.gamma.take_accumulate_flag()
         ln2.beta.take_accumulate_flag()
         dh = NN.layernorm_bwd(h, ln2.gamma.master, m2, r2, dh2, ln2.gamma.grad, ln2.beta.grad, acc, dres=g)
-        ln2.gamma.grad_ready()
-        ln2.beta.grad_ready()
         # attention: h = a Wo + x
         wgrad(at.w_o, a2.t(), dh)
-        at.w_o.grad_ready()
         da = K.gemm(dh, at.w_o.value.t())
         dqkv = NN.attention_bwd(qkv.reshape(B, S, -1), probs, da.reshape(B, S, -1), B, S, H, D, scale)
         dqkv2 = _flat2(dqkv)
         wgrad(at.w_qkv, h1.t(), dqkv2)
-        at.w_qkv.grad_ready()
         dh1 = K.gemm(dqkv2, at.w_qkv.value.t())
         acc = ln1.gamma.take_accumulate_flag()
         ln1.beta.take_accumulate_flag()
         dx = NN.layernorm_bwd(x2, ln1.gamma.master, m1, r1, dh1, ln1.gamma.grad, ln1.beta.grad, acc, dres=dh)
-        ln1.gamma.grad_ready()
-        ln1.beta.grad_ready()
+        # All of the block's parameter reads are enqueued: release its buckets.
+        for p in (f2.weight, f2.bias, f1.weight, f1.bias, ln2.gamma, ln2.beta, at.w_o, at.w_qkv, ln1.gamma, ln1.beta):
+            p.grad_ready()
         return dx.reshape(B, S, -1), None, None

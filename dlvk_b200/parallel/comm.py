@@ -1,0 +1,224 @@
+"""Communication backends (reference `CommunicationBackend`,
+include/dlvk/deployment/multi_gpu_trainer.h:222-266: initialize, all_reduce,
+broadcast, all_gather, reduce_scatter, finalize).
+
+* `NcclBackend` -- torch.distributed over NCCL (the comparison baseline; also
+  gloo on CPU for tests).
+* `NvlinkBackend` -- this framework's own kernels over NVLink peer memory
+  (symmetric IPC-mapped buffers, P2P loads/stores, bounded flag waits).
+* `FusedAllReduceOptimizer` -- the data-parallel gradient path: one kernel per
+  bucket that reduces peers' gradients and applies the optimizer (comm.cu).
+"""
+from __future__ import annotations
+
+import enum
+import os
+from typing import List, Optional
+
+import torch
+import torch.distributed as dist
+
+from .. import _ext
+from ..ops import core as K
+
+
+class GradientSyncStrategy(enum.Enum):
+    """Reference enum (multi_gpu_trainer.h:212-217); only AllReduce is
+    implemented, as in the reference's intent."""
+    AllReduce = 0
+    ParameterServer = 1
+    HierarchicalReduce = 2
+    AsyncUpdate = 3
+
+
+def _codes(dt: torch.dtype) -> int:
+    return {torch.float32: 0, torch.bfloat16: 1, torch.int32: 3, torch.int64: 6}[dt]
+
+
+MAX_BUCKETS = 4096
+BUDGET_S = float(os.environ.get("DLVK_PEER_TIMEOUT_S", "10"))
+
+
+def _exchange(handle: bytes, group=None) -> List[bytes]:
+    world = dist.get_world_size(group)
+    out = [None] * world
+    dist.all_gather_object(out, handle, group=group)
+    return out
+
+
+def make_symmetric(nbytes: int, device: torch.device, group=None):
+    """Allocate and map a SymmetricBuffer on every rank (collective)."""
+    C = _ext.C()
+    buf = C.comm.SymmetricBuffer(int(nbytes), device.index)
+    handles = _exchange(buf.handle(), group)
+    buf.open(handles, dist.get_rank(group))
+    return buf
+
+
+class FusedAllReduceOptimizer:
+    """Per-bucket fused gradient all-reduce + optimizer update.
+
+    The model's flat gradient buffer and compute-dtype parameter buffer are
+    moved into symmetric peer-mapped memory.  Buckets smaller than
+    `one_shot_bytes` are reduced redundantly on every rank (one round); larger
+    ones two-shot (each rank reduces and updates 1/world of the bucket and
+    writes the new parameters to all ranks), so optimizer state is touched
+    only by the shard owner.
+    """
+
+    def __init__(self, store, optimizer, world: int, rank: int, group=None,
+                 one_shot_bytes: Optional[int] = None, ctas: Optional[int] = None):
+        if optimizer.clip_norm is not None:
+            raise ValueError("global-norm clipping is not supported with the fused all-reduce optimizer")
+        self.C = _ext.C()
+        self.store, self.opt = store, optimizer
+        self.world, self.rank, self.group = world, rank, group
+        dev = store.device
+        self.dev = dev
+        n = store.numel
+        self.grad_buf = make_symmetric(n * 4, dev, group)
+        self.bf16 = store.value is not store.master
+        if self.bf16:
+            self.value_buf = make_symmetric(n * 2, dev, group)
+            store.rebind(grad=self.grad_buf.tensor(0, n, 0), value=self.value_buf.tensor(1, n, 0))
+        else:
+            self.value_buf = make_symmetric(n * 4, dev, group)
+            store.rebind(grad=self.grad_buf.tensor(0, n, 0), master=self.value_buf.tensor(0, n, 0))
+        self.flag_buf = make_symmetric(MAX_BUCKETS * 2 * world * 4, dev, group)
+        self.counters = torch.zeros(MAX_BUCKETS, dtype=torch.int32, device=dev)
+        self.epoch = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.one_shot_bytes = one_shot_bytes if one_shot_bytes is not None else int(
+            os.environ.get("DLVK_ONE_SHOT_BYTES", str(2 << 20)))
+        self.ctas = ctas or int(os.environ.get("DLVK_AR_CTAS", "32"))
+        self.st = optimizer.state(store)
+        self._bucket_ids = {}
+        torch.cuda.synchronize(dev)
+        dist.barrier(group)
+
+    def begin_step(self) -> None:
+        self.C.counter_add(self.epoch, 1)
+
+    def reduce_update(self, start: int, end: int) -> None:
+        key = (start, end)
+        if key not in self._bucket_ids:
+            if len(self._bucket_ids) >= MAX_BUCKETS:
+                raise RuntimeError("too many buckets")
+            self._bucket_ids[key] = len(self._bucket_ids)
+        b = self._bucket_ids[key]
+        one_shot = (end - start) * 4 <= self.one_shot_bytes
+        st = self.st
+        self.C.comm.fused_allreduce_optimizer(
+            self.grad_buf, self.value_buf, self.flag_buf, self.counters, b, start, end, self.store.master,
+            st.m, st.v, st.hyper, self.opt.kind, self.epoch, self.world, self.rank, one_shot, not self.bf16,
+            0, 1 if self.bf16 else 0, self.ctas, BUDGET_S)
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.dev)
+
+
+class CommunicationBackend:
+    """Interface of the reference (multi_gpu_trainer.h:222-234)."""
+
+    def initialize(self, device_ids=None) -> bool:
+        raise NotImplementedError
+
+    def all_reduce(self, tensors, average: bool = False) -> bool:
+        raise NotImplementedError
+
+    def broadcast(self, tensor, root: int = 0) -> bool:
+        raise NotImplementedError
+
+    def all_gather(self, tensor) -> List[torch.Tensor]:
+        raise NotImplementedError
+
+    def reduce_scatter(self, tensor) -> torch.Tensor:
+        raise NotImplementedError
+
+    def finalize(self) -> None:
+        pass
+
+
+class NcclBackend(CommunicationBackend):
+    """torch.distributed collectives (NCCL on GPUs, gloo on CPU)."""
+
+    def __init__(self, group=None):
+        self.group = group
+
+    def initialize(self, device_ids=None) -> bool:
+        return dist.is_initialized()
+
+    def all_reduce(self, tensors, average: bool = False) -> bool:
+        if isinstance(tensors, torch.Tensor):
+            tensors = [tensors]
+        w = dist.get_world_size(self.group)
+        for t in tensors:
+            dist.all_reduce(t, group=self.group)
+            if average:
+                t.div_(w)
+        return True
+
+    def broadcast(self, tensor, root: int = 0) -> bool:
+        dist.broadcast(tensor, root, group=self.group)
+        return True
+
+    def all_gather(self, tensor) -> List[torch.Tensor]:
+        out = [torch.empty_like(tensor) for _ in range(dist.get_world_size(self.group))]
+        dist.all_gather(out, tensor, group=self.group)
+        return out
+
+    def reduce_scatter(self, tensor) -> torch.Tensor:
+        w = dist.get_world_size(self.group)
+        chunks = list(tensor.chunk(w))
+        out = torch.empty_like(chunks[dist.get_rank(self.group)])
+        dist.reduce_scatter(out, chunks, group=self.group)
+        return out
+
+
+class NvlinkBackend(CommunicationBackend):
+    """All-reduce through this framework's P2P kernel over a symmetric staging
+    buffer (sized on first use); other collectives through NCCL."""
+
+    def __init__(self, group=None, capacity_bytes: int = 256 << 20):
+        self.group = group
+        self.capacity = capacity_bytes
+        self.buf = None
+        self.flags = None
+        self.nccl = NcclBackend(group)
+
+    def initialize(self, device_ids=None) -> bool:
+        if not dist.is_initialized():
+            return False
+        dev = torch.device("cuda", torch.cuda.current_device())
+        w = dist.get_world_size(self.group)
+        self.world, self.rank = w, dist.get_rank(self.group)
+        self.buf = make_symmetric(self.capacity, dev, self.group)
+        self.flags = make_symmetric(2 * w * 4 * 4, dev, self.group)
+        self.counters = torch.zeros(4, dtype=torch.int32, device=dev)
+        self.epoch = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.C = _ext.C()
+        return True
+
+    def all_reduce(self, tensors, average: bool = False) -> bool:
+        if isinstance(tensors, torch.Tensor):
+            tensors = [tensors]
+        for t in tensors:
+            nb = t.numel() * t.element_size()
+            if nb > self.capacity or t.dtype not in (torch.float32, torch.bfloat16):
+                self.nccl.all_reduce([t], average)
+                continue
+            view = self.buf.tensor(_codes(t.dtype), t.numel(), 0)
+            view.copy_(t.reshape(-1))
+            self.C.counter_add(self.epoch, 1)
+            self.C.comm.p2p_allreduce(self.buf, self.flags, self.counters, 0, 0, t.numel(), self.epoch, self.world,
+                                      self.rank, _codes(t.dtype), average, 64, BUDGET_S)
+            t.reshape(-1).copy_(view)
+        return True
+
+    def broadcast(self, tensor, root: int = 0) -> bool:
+        return self.nccl.broadcast(tensor, root)
+
+    def all_gather(self, tensor):
+        return self.nccl.all_gather(tensor)
+
+    def reduce_scatter(self, tensor):
+        return self.nccl.reduce_scatter(tensor)

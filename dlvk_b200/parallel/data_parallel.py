@@ -52,7 +52,7 @@ class DataParallel:
         self.rank = dist.get_rank(group)
         self.store = model.store
         self.dev = model.dev
-        self.comm_stream = self.dev.comm_stream
+        self.comm_stream = self.dev.comm_stream if self.dev.is_cuda else None
         self.mode = mode
         self.buckets = self._make_buckets(bucket_mb)
         self._bucket_of = {}
@@ -68,7 +68,8 @@ class DataParallel:
         # make every replica start from rank 0's parameters
         dist.broadcast(self.store.master, 0, group=group)
         self.store.sync_value()
-        torch.cuda.synchronize()
+        if self.dev.is_cuda:
+            torch.cuda.synchronize(self.dev.device)
 
     def _make_buckets(self, bucket_mb: float) -> List[Bucket]:
         limit = int(bucket_mb * (1 << 20) / 4)
@@ -102,16 +103,22 @@ class DataParallel:
         if b.pending == 0:
             self._launch(b)
 
+    def _reduce_bucket(self, b: Bucket) -> None:
+        if self.fused is not None:
+            self.fused.reduce_update(b.start, b.end)
+        else:
+            g = self.store.grad[b.start:b.end]
+            dist.all_reduce(g, group=self.group)
+            self.opt.update_range(self.store, b.start, b.end, extra_scale=1.0 / self.world)
+
     def _launch(self, b: Bucket) -> None:
+        if not self.dev.is_cuda:
+            self._reduce_bucket(b)
+            return
         cur = torch.cuda.current_stream()
         self.comm_stream.wait_stream(cur)
         with torch.cuda.stream(self.comm_stream):
-            if self.fused is not None:
-                self.fused.reduce_update(b.start, b.end)
-            else:
-                g = self.store.grad[b.start:b.end]
-                dist.all_reduce(g, group=self.group)
-                self.opt.update_range(self.store, b.start, b.end, extra_scale=1.0 / self.world)
+            self._reduce_bucket(b)
 
     def finish_step(self) -> None:
         # Buckets whose params got no gradient hook call (unused params) are
@@ -120,7 +127,34 @@ class DataParallel:
             if b.pending > 0:
                 b.pending = 0
                 self._launch(b)
-        torch.cuda.current_stream().wait_stream(self.comm_stream)
+        if self.dev.is_cuda:
+            torch.cuda.current_stream().wait_stream(self.comm_stream)
+
+    def consolidate(self) -> None:
+        """Make every rank's fp32 master and optimizer state complete (two-shot
+        buckets update them only on the shard owner).  Call before saving a
+        checkpoint; collective."""
+        if self.fused is None:
+            return
+        st = self.opt.state(self.store)
+        w = self.world
+        for b in self.buckets:
+            n = b.numel
+            if n * 4 <= self.fused.one_shot_bytes:
+                continue
+            shard = ((n + w - 1) // w + 63) // 64 * 64
+            for buf in (self.store.master, st.m, st.v):
+                if buf is None:
+                    continue
+                full = torch.zeros(shard * w, dtype=buf.dtype, device=buf.device)
+                lo = min(n, shard * self.rank)
+                hi = min(n, lo + shard)
+                mine = torch.zeros(shard, dtype=buf.dtype, device=buf.device)
+                mine[: hi - lo].copy_(buf[b.start + lo:b.start + hi])
+                dist.all_gather_into_tensor(full, mine, group=self.group)
+                buf[b.start:b.end].copy_(full[:n])
+        if self.dev.is_cuda:
+            torch.cuda.synchronize(self.dev.device)
 
     def close(self) -> None:
         if self.fused is not None:

@@ -1,0 +1,109 @@
+"""Data-parallel self-test: N ranks train a model on disjoint shards of one
+batch; the result must equal single-process training on the whole batch.
+
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \\
+        --master-port P -m dlvk_b200.parallel.selftest --mode fused --model mlp
+
+Each rank checks its parameters against a reference it computes itself on
+the full batch (same seed, same initial weights), prints one JSON line and
+exits non-zero on mismatch.  Works on CPU with gloo (mode nccl) as well.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--mode", default="fused", choices=["fused", "nccl"])
+    ap.add_argument("--model", default="mlp", choices=["mlp", "transformer"])
+    ap.add_argument("--dtype", default="fp32")
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--bucket-mb", type=float, default=0.05)
+    ap.add_argument("--one-shot-bytes", type=int, default=None)
+    ap.add_argument("--cpu", action="store_true")
+    ap.add_argument("--tol", type=float, default=None)
+    args = ap.parse_args()
+
+    import dlvk_b200 as dl
+    from dlvk_b200.models import zoo
+    from dlvk_b200.parallel.data_parallel import DataParallel
+    from dlvk_b200.training.step import TrainStep
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.cpu:
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
+        device = "cpu"
+    else:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
+                                device_id=torch.device("cuda", local))
+        device = f"cuda:{local}"
+    if args.one_shot_bytes is not None:
+        os.environ["DLVK_ONE_SHOT_BYTES"] = str(args.one_shot_bytes)
+
+    def build(dev):
+        if args.model == "mlp":
+            return zoo.mlp(device=dev, dtype=args.dtype, seed=0)
+        return zoo.transformer(device=dev, dtype=args.dtype, seed=0, vocab=256, d_model=128, layers=2, heads=2,
+                               d_ff=256)
+
+    per = 8
+    g = torch.Generator().manual_seed(123)
+    if args.model == "mlp":
+        X = torch.rand(per * world, 784, generator=g)
+        Y = torch.randint(0, 10, (per * world,), generator=g, dtype=torch.int32)
+    else:
+        toks = torch.randint(0, 256, (per * world, 33), generator=g, dtype=torch.int32)
+        X, Y = toks[:, :-1].contiguous(), toks[:, 1:].contiguous()
+
+    # reference: one process, full batch (mean over all rows == DP mean of shard means)
+    ref = build(device)
+    ref_opt = dl.Adam(1e-2)
+    ref_step = TrainStep(ref, dl.CrossEntropyLoss(), ref_opt, graph=False)
+    for _ in range(args.steps):
+        ref_step(X, Y)
+
+    model = build(device)
+    opt = dl.Adam(1e-2)
+    dp = DataParallel(model, opt, mode=args.mode, bucket_mb=args.bucket_mb)
+    step = TrainStep(model, dl.CrossEntropyLoss(), opt, dp=dp, graph=False)
+    xs, ys = X[rank * per:(rank + 1) * per].contiguous(), Y[rank * per:(rank + 1) * per].contiguous()
+    for _ in range(args.steps):
+        loss = step(xs, ys)
+    dp.consolidate()
+    if not args.cpu:
+        torch.cuda.synchronize()
+    err_word = 0
+    if not args.cpu:
+        from dlvk_b200 import _ext
+
+        err_word = int(_ext.C().read_device_error(True))
+    a = model.store.value.float()
+    b = ref.store.value.float()
+    diff = float((a - b).abs().max())
+    scale = float(b.abs().max())
+    tol = args.tol if args.tol is not None else (2e-4 if args.dtype == "fp32" else 2e-2)
+    ok = diff <= tol * scale and err_word == 0
+    mdiff = float((model.store.master - ref.store.master).abs().max())
+    res = {"rank": rank, "world": world, "mode": args.mode, "model": args.model, "dtype": args.dtype,
+           "max_param_diff": diff, "param_scale": scale, "master_diff": mdiff, "device_error": err_word,
+           "buckets": dp.describe()["buckets"], "ok": ok, "loss": float(loss)}
+    print(json.dumps(res), flush=True)
+    dp.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0 if ok else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())
