@@ -55,7 +55,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "torch", "reference"])
     ap.add_argument("--no-graph", action="store_true", help="eager step instead of a captured CUDA graph")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--allreduce", default="nccl", choices=["fused", "nccl"],
+    ap.add_argument("--allreduce", default="fused", choices=["fused", "nccl"],
                     help="gradient path for N > 1 (ours): fused P2P all-reduce+optimizer or NCCL baseline")
     return ap.parse_args()
 

@@ -1,0 +1,117 @@
+"""Gradient all-reduce + Adam sweep (one process per GPU):
+
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \\
+        --master-port P -m dlvk_b200.bench.allreduce [--dtype fp32|bf16]
+
+For every bucket size (4 KB .. 1 GB of fp32 gradients) it times, on the
+device (CUDA events, max over ranks):
+  fused  this framework's one-kernel P2P all-reduce + Adam (comm.cu)
+  nccl   NCCL all-reduce followed by this framework's Adam kernel
+and reports bus bandwidth (2 (N-1)/N * bytes / t, the all-reduce convention)
+and the fused kernel's fraction of its roofline: max(bytes over NVLink per
+direction / 770 GB/s, local HBM bytes / measured HBM bandwidth).
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+
+import torch
+import torch.distributed as dist
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--dtype", default="bf16", choices=["fp32", "bf16"], help="parameter (compute) dtype")
+    ap.add_argument("--min-kb", type=int, default=4)
+    ap.add_argument("--max-mb", type=int, default=1024)
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--nvlink-gbs", type=float, default=770.0)
+    args = ap.parse_args()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    rank, world = dist.get_rank(), dist.get_world_size()
+    import dlvk_b200 as dl
+    from dlvk_b200 import _ext
+    from dlvk_b200.bench.common import measured_peaks
+    from dlvk_b200.models.params import Parameter, ParamStore
+    from dlvk_b200.parallel.comm import FusedAllReduceOptimizer
+
+    C = _ext.C()
+    hbm = measured_peaks()["hbm_gbs"] * 1e9
+    dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float32
+    nmax = args.max_mb * (1 << 20) // 4
+    g = torch.Generator().manual_seed(rank)
+    p = Parameter("w", (nmax,), torch.randn(nmax, generator=g) * 0.02)
+    store = ParamStore([p], f"cuda:{local}", dtype)
+    opt = dl.Adam(1e-3)
+    fused = FusedAllReduceOptimizer(store, opt, world, rank)
+    store.grad.normal_(0, 1e-3)
+    st = opt.state(store)
+    sizes = []
+    n = max(64, args.min_kb * 1024 // 4)
+    while n <= nmax:
+        sizes.append(n // 64 * 64)
+        n *= 4
+
+    def time_it(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(args.iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([s.elapsed_time(e) / args.iters], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item()) / 1e3
+
+    for n in sizes:
+        def fused_step():
+            fused.begin_step()
+            opt.advance(store)
+            fused.reduce_update(0, n)
+
+        def nccl_step():
+            gr = store.grad[:n]
+            dist.all_reduce(gr)
+            opt.advance(store)
+            opt.update_range(store, 0, n, extra_scale=1.0 / world)
+
+        tf = time_it(fused_step)
+        tn = time_it(nccl_step)
+        gbytes = n * 4
+        vbytes = n * (2 if dtype == torch.bfloat16 else 4)
+        one_shot = gbytes <= fused.one_shot_bytes
+        if one_shot:
+            link = (world - 1) * gbytes
+            local_b = gbytes + n * 4 * 5 + vbytes
+        else:
+            link = (world - 1) / world * (gbytes + vbytes)
+            local_b = (gbytes + n * 4 * 5 + vbytes) / world
+        roof = max(link / (args.nvlink_gbs * 1e9), local_b / hbm)
+        bus = 2 * (world - 1) / world * gbytes
+        if rank == 0:
+            print(json.dumps({"world": world, "bucket_bytes": gbytes, "param_dtype": args.dtype,
+                              "algo": "one-shot" if one_shot else "two-shot",
+                              "fused_us": round(tf * 1e6, 1), "nccl_plus_adam_us": round(tn * 1e6, 1),
+                              "fused_bus_gbs": round(bus / tf / 1e9, 1), "nccl_bus_gbs": round(bus / tn / 1e9, 1),
+                              "fused_roofline_us": round(roof * 1e6, 1),
+                              "fused_frac_of_roofline": round(roof / tf, 3),
+                              "speedup_vs_nccl_plus_adam": round(tn / tf, 3)}), flush=True)
+    err = C.read_device_error(True)
+    if rank == 0:
+        print(json.dumps({"device_error": int(err)}))
+    fused.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -112,95 +112,155 @@ __device__ void done_barrier(const FusedARArgs& a, uint32_t epoch) {
   if (threadIdx.x == 0) *a.cta_counter = 0u;
 }
 
-template <typename TG, typename TV>
-__global__ void __launch_bounds__(256, 5) fused_ar_opt_kernel(FusedARArgs a) {
+template <typename T> __device__ __forceinline__ float4 load4(const T* base, int64_t vi);
+template <> __device__ __forceinline__ float4 load4<float>(const float* base, int64_t vi) {
+  return reinterpret_cast<const float4*>(base)[vi];
+}
+template <> __device__ __forceinline__ float4 load4<__nv_bfloat16>(const __nv_bfloat16* base, int64_t vi) {
+  const uint2 u = reinterpret_cast<const uint2*>(base)[vi];
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+  const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+template <typename T> __device__ __forceinline__ void store4(T* base, int64_t vi, const float4& v);
+template <> __device__ __forceinline__ void store4<float>(float* base, int64_t vi, const float4& v) {
+  reinterpret_cast<float4*>(base)[vi] = v;
+}
+template <> __device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* base, int64_t vi, const float4& v) {
+  uint2 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+  h[0] = __floats2bfloat162_rn(v.x, v.y);
+  h[1] = __floats2bfloat162_rn(v.z, v.w);
+  reinterpret_cast<uint2*>(base)[vi] = u;
+}
+
+// Bucket and shard boundaries are multiples of 64 elements (parameter
+// offsets in the flat buffers are 256-byte aligned), so the loops below work
+// on whole 4-element vectors.  With the world size W a template parameter,
+// every peer's U gradient vectors and the local optimizer state of an
+// iteration are all issued before the first is consumed, keeping enough bytes
+// in flight to cover NVLink latency.  W = 0 is the runtime-world fallback.
+template <typename TG, typename TV, int W, int U>
+__global__ void __launch_bounds__(128, 6) fused_ar_opt_kernel(FusedARArgs a) {
   const uint32_t epoch = (uint32_t)(*a.epoch_ptr);
   if (!ready_barrier(a, epoch)) return;
   const OptimHyper h = *a.hyper;
   const float gs = a.scale * h.grad_scale;
-  constexpr int V = 4;  // elements per thread iteration (16 B of fp32 state)
+  const int world = W > 0 ? W : a.world;
   const int64_t n = a.end - a.start;
   int64_t lo = 0, hi = n;
   if (!a.one_shot) {
-    const int64_t shard = ((n + a.world - 1) / a.world + 63) / 64 * 64;
+    const int64_t shard = ((n + world - 1) / world + 63) / 64 * 64;
     lo = min(n, shard * a.rank);
     hi = min(n, lo + shard);
   }
+  const int64_t base = a.start + lo;  // element offset of this rank's range
+  const int64_t nvec = (hi - lo) / 4;
   const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = lo + tid * V; i < hi; i += stride * V) {
-    const int64_t gi = a.start + i;
-    const int cnt = (int)min((int64_t)V, hi - i);
-    float g[V] = {0.f, 0.f, 0.f, 0.f};
-    if (cnt == V) {
-      for (int r = 0; r < a.world; ++r) {
-        const TG* src = reinterpret_cast<const TG*>(a.peer_grads[r]) + gi;
-        if (sizeof(TG) == 4) {
-          const float4 t = *reinterpret_cast<const float4*>(src);
-          g[0] += t.x; g[1] += t.y; g[2] += t.z; g[3] += t.w;
-        } else {
-          const uint2 t = *reinterpret_cast<const uint2*>(src);
-          const TG* e = reinterpret_cast<const TG*>(&t);
+  float* mst = a.master + base;
+  float* mm = a.m ? a.m + base : nullptr;
+  float* vv = a.v ? a.v + base : nullptr;
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int64_t v0 = tid; v0 < nvec; v0 += stride * U) {
+    float4 g[U], w[U], m4[U], v4[U];
+    if (W > 0) {
+      float4 t[W > 0 ? W : 1][U];
 #pragma unroll
-          for (int k = 0; k < V; ++k) g[k] += to_f32(e[k]);
+      for (int r = 0; r < (W > 0 ? W : 1); ++r) {
+        const TG* src = reinterpret_cast<const TG*>(a.peer_grads[r]) + base;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t vi = v0 + u * stride;
+          t[r][u] = vi < nvec ? load4<TG>(src, vi) : z4;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t vi = v0 + u * stride;
+        w[u] = vi < nvec ? reinterpret_cast<const float4*>(mst)[vi] : z4;
+        m4[u] = (mm && vi < nvec) ? reinterpret_cast<const float4*>(mm)[vi] : z4;
+        v4[u] = (vv && vi < nvec) ? reinterpret_cast<const float4*>(vv)[vi] : z4;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        g[u] = z4;
+#pragma unroll
+        for (int r = 0; r < (W > 0 ? W : 1); ++r) {  // rank order: deterministic
+          g[u].x += t[r][u].x;
+          g[u].y += t[r][u].y;
+          g[u].z += t[r][u].z;
+          g[u].w += t[r][u].w;
         }
       }
     } else {
-      for (int r = 0; r < a.world; ++r)
 #pragma unroll
-        for (int k = 0; k < V; ++k)
-          if (k < cnt) g[k] += to_f32(reinterpret_cast<const TG*>(a.peer_grads[r])[gi + k]);
-    }
-    float w[V], m[V], v[V];
-    TV out[V];
+      for (int u = 0; u < U; ++u) g[u] = z4;
+      for (int r = 0; r < world; ++r) {
+        const TG* src = reinterpret_cast<const TG*>(a.peer_grads[r]) + base;
+        float4 t[U];
 #pragma unroll
-    for (int k = 0; k < V; ++k) {
-      if (k < cnt) {
-        w[k] = a.master[gi + k];
-        m[k] = a.m ? a.m[gi + k] : 0.f;
-        v[k] = a.v ? a.v[gi + k] : 0.f;
-        opt_apply(a.kind, h, w[k], g[k] * gs, m[k], v[k]);
-        a.master[gi + k] = w[k];
-        if (a.m) a.m[gi + k] = m[k];
-        if (a.v) a.v[gi + k] = v[k];
-        out[k] = from_f32<TV>(w[k]);
+        for (int u = 0; u < U; ++u) {
+          const int64_t vi = v0 + u * stride;
+          t[u] = vi < nvec ? load4<TG>(src, vi) : z4;
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          g[u].x += t[u].x;
+          g[u].y += t[u].y;
+          g[u].z += t[u].z;
+          g[u].w += t[u].w;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t vi = v0 + u * stride;
+        w[u] = vi < nvec ? reinterpret_cast<const float4*>(mst)[vi] : z4;
+        m4[u] = (mm && vi < nvec) ? reinterpret_cast<const float4*>(mm)[vi] : z4;
+        v4[u] = (vv && vi < nvec) ? reinterpret_cast<const float4*>(vv)[vi] : z4;
       }
     }
-    if (a.values_are_master) {
-      // fp32 mode: the master is the compute copy; peers still need it.
-      if (!a.one_shot)
-        for (int r = 0; r < a.world; ++r)
-          if (r != a.rank)
 #pragma unroll
-            for (int k = 0; k < V; ++k)
-              if (k < cnt) reinterpret_cast<TV*>(a.peer_values[r])[gi + k] = out[k];
-    } else {
-      const int targets_lo = a.one_shot ? a.rank : 0;
-      const int targets_hi = a.one_shot ? a.rank + 1 : a.world;
-      for (int r = targets_lo; r < targets_hi; ++r) {
-        TV* dst = reinterpret_cast<TV*>(a.peer_values[r]) + gi;
-        if (cnt == V && sizeof(TV) == 2) {
-          uint2 u;
-          TV* e = reinterpret_cast<TV*>(&u);
-#pragma unroll
-          for (int k = 0; k < V; ++k) e[k] = out[k];
-          *reinterpret_cast<uint2*>(dst) = u;
-        } else {
-#pragma unroll
-          for (int k = 0; k < V; ++k)
-            if (k < cnt) dst[k] = out[k];
-        }
+    for (int u = 0; u < U; ++u) {
+      const int64_t vi = v0 + u * stride;
+      if (vi >= nvec) continue;
+      opt_apply(a.kind, h, w[u].x, g[u].x * gs, m4[u].x, v4[u].x);
+      opt_apply(a.kind, h, w[u].y, g[u].y * gs, m4[u].y, v4[u].y);
+      opt_apply(a.kind, h, w[u].z, g[u].z * gs, m4[u].z, v4[u].z);
+      opt_apply(a.kind, h, w[u].w, g[u].w * gs, m4[u].w, v4[u].w);
+      reinterpret_cast<float4*>(mst)[vi] = w[u];
+      if (mm) reinterpret_cast<float4*>(mm)[vi] = m4[u];
+      if (vv) reinterpret_cast<float4*>(vv)[vi] = v4[u];
+      if (a.values_are_master) {
+        // fp32 mode: the master is the compute copy; peers still need it.
+        if (!a.one_shot)
+          for (int r = 0; r < world; ++r)
+            if (r != a.rank) store4<float>(reinterpret_cast<float*>(a.peer_values[r]) + base, vi, w[u]);
+      } else {
+        const int r0 = a.one_shot ? a.rank : 0, r1 = a.one_shot ? a.rank + 1 : world;
+        for (int r = r0; r < r1; ++r) store4<TV>(reinterpret_cast<TV*>(a.peer_values[r]) + base, vi, w[u]);
       }
     }
   }
   done_barrier(a, epoch);
 }
 
+template <typename TG, typename TV>
+void launch_fused(const FusedARArgs& a, int grid, cudaStream_t s) {
+  switch (a.world) {
+    case 1: fused_ar_opt_kernel<TG, TV, 1, 2><<<grid, 128, 0, s>>>(a); break;
+    case 2: fused_ar_opt_kernel<TG, TV, 2, 2><<<grid, 128, 0, s>>>(a); break;
+    case 4: fused_ar_opt_kernel<TG, TV, 4, 1><<<grid, 128, 0, s>>>(a); break;
+    case 8: fused_ar_opt_kernel<TG, TV, 8, 1><<<grid, 128, 0, s>>>(a); break;
+    default: fused_ar_opt_kernel<TG, TV, 0, 2><<<grid, 128, 0, s>>>(a); break;
+  }
+}
+
 // Plain two-shot sum all-reduce of [start, end) of a symmetric buffer, in
 // place: reduce my shard over all ranks (rank order), store the sum into every
 // rank's buffer.  Same flag protocol as the fused kernel.
 template <typename T>
-__global__ void __launch_bounds__(256, 5) p2p_allreduce_kernel(FusedARArgs a, int average) {
+__global__ void __launch_bounds__(128, 8) p2p_allreduce_kernel(FusedARArgs a, int average) {
   const uint32_t epoch = (uint32_t)(*a.epoch_ptr);
   if (!ready_barrier(a, epoch)) return;
   constexpr int V = Pack<T>::N;
@@ -254,16 +314,13 @@ void fused_allreduce_optimizer(const FusedARArgs& a, DType grad_dt, DType value_
   const int64_t n = a.end - a.start;
   if (n <= 0) return;
   DLVK_CHECK(a.world <= 512, "fused all-reduce: world size too large");
+  DLVK_CHECK(a.start % 64 == 0 && n % 64 == 0, "fused all-reduce: bucket must be 64-element aligned");
   const int64_t work = a.one_shot ? n : (n + a.world - 1) / a.world;
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ctas, (work / 4 + 255) / 256));
-  if (grad_dt == DType::F32 && value_dt == DType::BF16)
-    fused_ar_opt_kernel<float, __nv_bfloat16><<<grid, 256, 0, s>>>(a);
-  else if (grad_dt == DType::F32 && value_dt == DType::F32)
-    fused_ar_opt_kernel<float, float><<<grid, 256, 0, s>>>(a);
-  else if (grad_dt == DType::BF16 && value_dt == DType::BF16)
-    fused_ar_opt_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 256, 0, s>>>(a);
-  else
-    throw std::runtime_error("fused all-reduce: unsupported grad/value dtypes");
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ctas, (work / 16 + 127) / 128));
+  if (grad_dt == DType::F32 && value_dt == DType::BF16) launch_fused<float, __nv_bfloat16>(a, grid, s);
+  else if (grad_dt == DType::F32 && value_dt == DType::F32) launch_fused<float, float>(a, grid, s);
+  else if (grad_dt == DType::BF16 && value_dt == DType::BF16) launch_fused<__nv_bfloat16, __nv_bfloat16>(a, grid, s);
+  else throw std::runtime_error("fused all-reduce: unsupported grad/value dtypes");
   DLVK_POST_LAUNCH();
 }
 
@@ -271,9 +328,9 @@ void p2p_allreduce(const FusedARArgs& a, DType dt, bool average, int ctas, cudaS
   const int64_t n = a.end - a.start;
   if (n <= 0) return;
   const int64_t work = (n + a.world - 1) / a.world;
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ctas, (work / 8 + 255) / 256));
-  if (dt == DType::F32) p2p_allreduce_kernel<float><<<grid, 256, 0, s>>>(a, average ? 1 : 0);
-  else if (dt == DType::BF16) p2p_allreduce_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(a, average ? 1 : 0);
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ctas, (work / 8 + 127) / 128));
+  if (dt == DType::F32) p2p_allreduce_kernel<float><<<grid, 128, 0, s>>>(a, average ? 1 : 0);
+  else if (dt == DType::BF16) p2p_allreduce_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(a, average ? 1 : 0);
   else throw std::runtime_error("p2p all-reduce: unsupported dtype");
   DLVK_POST_LAUNCH();
 }

@@ -89,7 +89,7 @@ class FusedAllReduceOptimizer:
         self.epoch = torch.zeros(1, dtype=torch.int64, device=dev)
         self.one_shot_bytes = one_shot_bytes if one_shot_bytes is not None else int(
             os.environ.get("DLVK_ONE_SHOT_BYTES", str(2 << 20)))
-        self.ctas = ctas or int(os.environ.get("DLVK_AR_CTAS", "32"))
+        self.ctas = ctas or int(os.environ.get("DLVK_AR_CTAS", "296"))
         self.st = optimizer.state(store)
         self._bucket_ids = {}
         torch.cuda.synchronize(dev)

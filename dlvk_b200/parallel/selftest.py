@@ -30,6 +30,9 @@ def main() -> int:
     ap.add_argument("--one-shot-bytes", type=int, default=None)
     ap.add_argument("--cpu", action="store_true")
     ap.add_argument("--tol", type=float, default=None)
+    ap.add_argument("--opt", default="adam", choices=["adam", "sgd"],
+                    help="sgd keeps bf16 rounding differences linear; Adam maps near-zero "
+                         "gradients of either sign to +-lr on its first step")
     args = ap.parse_args()
 
     import dlvk_b200 as dl
@@ -68,13 +71,14 @@ def main() -> int:
 
     # reference: one process, full batch (mean over all rows == DP mean of shard means)
     ref = build(device)
-    ref_opt = dl.Adam(1e-2)
+    make_opt = (lambda: dl.Adam(1e-2)) if args.opt == "adam" else (lambda: dl.SGD(0.05, momentum=0.9))
+    ref_opt = make_opt()
     ref_step = TrainStep(ref, dl.CrossEntropyLoss(), ref_opt, graph=False)
     for _ in range(args.steps):
         ref_step(X, Y)
 
     model = build(device)
-    opt = dl.Adam(1e-2)
+    opt = make_opt()
     dp = DataParallel(model, opt, mode=args.mode, bucket_mb=args.bucket_mb)
     step = TrainStep(model, dl.CrossEntropyLoss(), opt, dp=dp, graph=False)
     xs, ys = X[rank * per:(rank + 1) * per].contiguous(), Y[rank * per:(rank + 1) * per].contiguous()

@@ -13,19 +13,20 @@ def _need(n):
         pytest.skip(f"needs {n} GPUs")
 
 
-@pytest.mark.parametrize("model,dtype,oneshot", [("mlp", "fp32", 1 << 30), ("mlp", "fp32", 0),
-                                                 ("transformer", "bf16", 1 << 30), ("transformer", "bf16", 0),
-                                                 ("transformer", "fp32", 0)])
-def test_fused_dp_matches_full_batch(model, dtype, oneshot):
+@pytest.mark.parametrize("model,dtype,oneshot,opt", [("mlp", "fp32", 1 << 30, "adam"), ("mlp", "fp32", 0, "adam"),
+                                                     ("transformer", "bf16", 1 << 30, "sgd"),
+                                                     ("transformer", "bf16", 0, "sgd"),
+                                                     ("transformer", "fp32", 0, "adam")])
+def test_fused_dp_matches_full_batch(model, dtype, oneshot, opt):
     _need(2)
     rc, lines, log = run_selftest(2, ["--mode", "fused", "--model", model, "--dtype", dtype,
-                                      "--one-shot-bytes", str(oneshot)])
+                                      "--one-shot-bytes", str(oneshot), "--opt", opt])
     assert rc == 0, log[-4000:]
     assert len(lines) == 2 and all(l["ok"] for l in lines), lines
 
 
 def test_nccl_dp_matches_full_batch():
     _need(2)
-    rc, lines, log = run_selftest(2, ["--mode", "nccl", "--model", "transformer", "--dtype", "bf16"])
+    rc, lines, log = run_selftest(2, ["--mode", "nccl", "--model", "transformer", "--dtype", "bf16", "--opt", "sgd"])
     assert rc == 0, log[-4000:]
     assert all(l["ok"] for l in lines), lines
