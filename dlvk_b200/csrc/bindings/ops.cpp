@@ -369,14 +369,15 @@ void optim_update_op(int64_t kind, const at::Tensor& hyper, const at::Tensor& p,
 
 void grad_stats_op(const at::Tensor& g, double scale, double max_norm, const at::Tensor& sumsq,
                    c10::optional<at::Tensor> flag, c10::optional<at::Tensor> clip, bool accumulate,
-                   const at::Tensor& scratch) {
+                   const at::Tensor& scratch, c10::optional<at::Tensor> scale_dev) {
   check_cuda(g, "g");
   c10::cuda::CUDAGuard gd(g.device());
   TORCH_CHECK(g.is_contiguous(), "grad_stats: contiguous grad");
   TORCH_CHECK(scratch.numel() >= grad_stats_scratch_floats(), "grad_stats: scratch too small");
   grad_stats(g.data_ptr(), to_dtype(g), g.numel(), (float)scale, (float)max_norm, sumsq.data_ptr<float>(),
              flag.has_value() ? flag->data_ptr<int>() : nullptr, clip.has_value() ? clip->data_ptr<float>() : nullptr,
-             accumulate, scratch.data_ptr<float>(), stream());
+             accumulate, scratch.data_ptr<float>(), stream(),
+             scale_dev.has_value() ? scale_dev->data_ptr<float>() : nullptr);
 }
 
 void scaler_update_op(const at::Tensor& scale, const at::Tensor& good_steps, const at::Tensor& found_inf,
@@ -418,7 +419,53 @@ void register_ops(py::module& m) {
   m.def("optim_update", &optim_update_op, py::arg("kind"), py::arg("hyper"), py::arg("p"), py::arg("grad"),
         py::arg("m") = py::none(), py::arg("v") = py::none(), py::arg("p_bf16") = py::none(),
         py::arg("extra_scale") = 1.0);
-  m.def("grad_stats", &grad_stats_op);
+  m.def("grad_stats", &grad_stats_op, py::arg("g"), py::arg("scale"), py::arg("max_norm"), py::arg("sumsq"),
+        py::arg("flag"), py::arg("clip"), py::arg("accumulate"), py::arg("scratch"), py::arg("scale_dev") = py::none());
+  m.def("step_metrics", [](const at::Tensor& logits, c10::optional<at::Tensor> labels, c10::optional<at::Tensor> probs,
+                           c10::optional<at::Tensor> loss, c10::optional<at::Tensor> loss_sum,
+                           c10::optional<at::Tensor> correct, double loss_weight) {
+    check_cuda(logits, "logits");
+    TORCH_CHECK(logits.is_contiguous() && logits.dim() >= 1, "step_metrics: contiguous logits");
+    const int cols = (int)logits.size(-1);
+    const int64_t rows = cols ? logits.numel() / cols : 0;
+    const int* lp = nullptr;
+    const float* pp = nullptr;
+    if (labels.has_value()) {
+      TORCH_CHECK(labels->scalar_type() == at::kInt && labels->numel() == rows, "step_metrics: int32 labels [rows]");
+      lp = labels->data_ptr<int>();
+    }
+    if (probs.has_value()) {
+      TORCH_CHECK(probs->scalar_type() == at::kFloat && probs->numel() == rows * cols && probs->is_contiguous(),
+                  "step_metrics: fp32 probs [rows, cols]");
+      pp = probs->data_ptr<float>();
+    }
+    c10::cuda::CUDAGuard g(logits.device());
+    step_metrics(to_dtype(logits), logits.data_ptr(), rows, cols, lp, pp,
+                 loss.has_value() ? loss->data_ptr<float>() : nullptr,
+                 loss_sum.has_value() ? loss_sum->data_ptr<float>() : nullptr,
+                 correct.has_value() ? reinterpret_cast<unsigned long long*>(correct->data_ptr<int64_t>()) : nullptr,
+                 (float)loss_weight, stream());
+  }, py::arg("logits"), py::arg("labels") = py::none(), py::arg("probs") = py::none(), py::arg("loss") = py::none(),
+     py::arg("loss_sum") = py::none(), py::arg("correct") = py::none(), py::arg("loss_weight") = 1.0);
+  m.def("scale_by_device_scalar", [](const at::Tensor& x, const at::Tensor& s) {
+    check_cuda(x, "x");
+    TORCH_CHECK(x.is_contiguous() && s.scalar_type() == at::kFloat && s.is_cuda(), "scale_by_device_scalar: args");
+    c10::cuda::CUDAGuard g(x.device());
+    scale_by_device_scalar(to_dtype(x), x.data_ptr(), x.numel(), s.data_ptr<float>(), stream());
+  });
+  m.def("regularize", [](const at::Tensor& w, const at::Tensor& g, double l1, double l2, double ll1, double ll2,
+                         c10::optional<at::Tensor> loss_out, c10::optional<at::Tensor> gscale) {
+    check_cuda(w, "w");
+    check_cuda(g, "g");
+    TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous() && g.is_contiguous() && g.numel() == w.numel(),
+                "regularize: w fp32 contiguous, g same numel");
+    c10::cuda::CUDAGuard gd(w.device());
+    regularize(w.data_ptr<float>(), g.data_ptr(), to_dtype(g), w.numel(), (float)l1, (float)l2, (float)ll1, (float)ll2,
+               loss_out.has_value() ? loss_out->data_ptr<float>() : nullptr, stream(),
+               gscale.has_value() ? gscale->data_ptr<float>() : nullptr);
+  }, py::arg("w"), py::arg("g"), py::arg("l1"), py::arg("l2"), py::arg("ll1"), py::arg("ll2"),
+     py::arg("loss_out") = py::none(),
+     py::arg("gscale") = py::none());
   m.def("grad_stats_scratch_floats", &grad_stats_scratch_floats);
   m.def("scaler_update", &scaler_update_op);
   m.def("optim_hyper_bytes", &optim_hyper_bytes);

@@ -1,5 +1,7 @@
 // Bindings of the host C++ runtime: `.dlvk` I/O and the CPU oracle.
 #include "bind_common.h"
+#include "dlvk/data.h"
+#include "dlvk/export.h"
 #include "dlvk/io.h"
 #include "dlvk/oracle.h"
 
@@ -41,7 +43,145 @@ std::vector<io::TensorRecord> py_to_records(const py::list& recs) {
 
 }  // namespace
 
+void cpu_contig(const at::Tensor& t, const char* what) {
+  TORCH_CHECK(!t.is_cuda() && t.is_contiguous(), "dlvk.data: ", what, " must be a contiguous CPU tensor");
+}
+
+void register_data(py::module& m) {
+  auto d = m.def_submodule("data", "native batch assembly (gather into pinned buffers, IDX files)");
+  d.def("gather_rows", [](const at::Tensor& src, const at::Tensor& idx, at::Tensor& dst, int threads) {
+    cpu_contig(src, "src");
+    cpu_contig(idx, "idx");
+    cpu_contig(dst, "dst");
+    TORCH_CHECK(idx.scalar_type() == at::kLong, "dlvk.data: idx must be int64");
+    TORCH_CHECK(src.dim() >= 1 && dst.size(0) >= idx.numel(), "dlvk.data: dst too small");
+    const int64_t rows = src.size(0);
+    const int64_t row_bytes = rows ? src.nbytes() / rows : 0;
+    TORCH_CHECK(dst.nbytes() >= (size_t)(idx.numel() * row_bytes), "dlvk.data: dst bytes");
+    py::gil_scoped_release nogil;
+    data::gather_rows(static_cast<const uint8_t*>(src.data_ptr()), rows, row_bytes, idx.data_ptr<int64_t>(),
+                      idx.numel(), static_cast<uint8_t*>(dst.data_ptr()), threads);
+  }, py::arg("src"), py::arg("idx"), py::arg("dst"), py::arg("threads") = 4);
+  d.def("gather_u8_to_f32", [](const at::Tensor& src, const at::Tensor& idx, at::Tensor& dst, double scale,
+                               double shift, int threads) {
+    cpu_contig(src, "src");
+    cpu_contig(idx, "idx");
+    cpu_contig(dst, "dst");
+    TORCH_CHECK(src.scalar_type() == at::kByte && dst.scalar_type() == at::kFloat && idx.scalar_type() == at::kLong,
+                "dlvk.data: gather_u8_to_f32 wants u8 src, f32 dst, int64 idx");
+    const int64_t rows = src.size(0);
+    const int64_t row = rows ? src.numel() / rows : 0;
+    TORCH_CHECK(dst.numel() >= idx.numel() * row, "dlvk.data: dst too small");
+    py::gil_scoped_release nogil;
+    data::gather_u8_to_f32(src.data_ptr<uint8_t>(), rows, row, idx.data_ptr<int64_t>(), idx.numel(),
+                           dst.data_ptr<float>(), (float)scale, (float)shift, threads);
+  }, py::arg("src"), py::arg("idx"), py::arg("dst"), py::arg("scale") = 1.0, py::arg("shift") = 0.0,
+     py::arg("threads") = 4);
+  d.def("gather_labels", [](const at::Tensor& labels, const at::Tensor& idx, int classes,
+                            c10::optional<at::Tensor> ids_out, c10::optional<at::Tensor> one_hot_out) {
+    cpu_contig(labels, "labels");
+    cpu_contig(idx, "idx");
+    TORCH_CHECK(labels.scalar_type() == at::kInt && idx.scalar_type() == at::kLong, "dlvk.data: labels i32, idx i64");
+    int32_t* ip = nullptr;
+    float* op = nullptr;
+    if (ids_out.has_value()) {
+      cpu_contig(*ids_out, "ids_out");
+      TORCH_CHECK(ids_out->scalar_type() == at::kInt && ids_out->numel() >= idx.numel(), "dlvk.data: ids_out");
+      ip = ids_out->data_ptr<int32_t>();
+    }
+    if (one_hot_out.has_value()) {
+      cpu_contig(*one_hot_out, "one_hot_out");
+      TORCH_CHECK(one_hot_out->scalar_type() == at::kFloat && one_hot_out->numel() >= idx.numel() * classes,
+                  "dlvk.data: one_hot_out");
+      op = one_hot_out->data_ptr<float>();
+    }
+    return data::gather_labels(labels.data_ptr<int32_t>(), labels.numel(), idx.data_ptr<int64_t>(), idx.numel(),
+                               classes, ip, op);
+  }, py::arg("labels"), py::arg("idx"), py::arg("classes"), py::arg("ids_out") = py::none(),
+     py::arg("one_hot_out") = py::none());
+  d.def("permutation", [](int64_t n, uint64_t seed, uint64_t epoch) {
+    auto p = data::permutation(n, seed, epoch);
+    auto t = at::empty({n}, at::TensorOptions().dtype(at::kLong));
+    if (n) std::memcpy(t.data_ptr<int64_t>(), p.data(), sizeof(int64_t) * (size_t)n);
+    return t;
+  });
+  d.def("read_idx", [](const std::string& path) {
+    auto f = data::read_idx(path);
+    return py::make_tuple(f.type_code, f.dims, py::bytes(f.data));
+  });
+  d.def("write_idx", [](const std::string& path, int code, const std::vector<int64_t>& dims, const std::string& raw) {
+    data::write_idx(path, code, dims, raw);
+  });
+}
+
+std::vector<exportfmt::Tensor> py_to_ex(const py::list& recs) {
+  std::vector<exportfmt::Tensor> out;
+  for (auto item : recs) {
+    auto tup = item.cast<py::tuple>();
+    exportfmt::Tensor t;
+    t.name = tup[0].cast<std::string>();
+    t.dtype = tup[1].cast<std::string>();
+    t.shape = tup[2].cast<std::vector<int64_t>>();
+    t.data = tup[3].cast<std::string>();
+    out.push_back(std::move(t));
+  }
+  return out;
+}
+
+py::list ex_to_py(const std::vector<exportfmt::Tensor>& ts) {
+  py::list l;
+  for (const auto& t : ts) l.append(py::make_tuple(t.name, t.dtype, t.shape, py::bytes(t.data)));
+  return l;
+}
+
+void register_export(py::module& m) {
+  auto e = m.def_submodule("export", "SafeTensors / GGUF v3 containers (C++)");
+  e.def("encode_safetensors", [](const py::list& recs, const std::vector<std::pair<std::string, std::string>>& meta) {
+    return py::bytes(exportfmt::encode_safetensors(py_to_ex(recs), meta));
+  });
+  e.def("decode_safetensors", [](const std::string& blob) {
+    std::vector<exportfmt::Tensor> ts;
+    std::vector<std::pair<std::string, std::string>> meta;
+    exportfmt::decode_safetensors(blob, ts, meta);
+    return py::make_tuple(ex_to_py(ts), meta);
+  });
+  // kvs: list of (key, type, value) with value str / int / float / bool
+  e.def("encode_gguf", [](const py::list& recs, const py::list& kvs, uint32_t alignment) {
+    std::vector<exportfmt::KV> kv;
+    for (auto item : kvs) {
+      auto tup = item.cast<py::tuple>();
+      exportfmt::KV k;
+      k.key = tup[0].cast<std::string>();
+      k.type = tup[1].cast<uint32_t>();
+      if (k.type == 8) k.s = tup[2].cast<std::string>();
+      else if (k.type == 6) k.f = tup[2].cast<double>();
+      else if (k.type == 11) k.i = tup[2].cast<int64_t>();
+      else k.u = tup[2].cast<uint64_t>();
+      kv.push_back(std::move(k));
+    }
+    return py::bytes(exportfmt::encode_gguf(py_to_ex(recs), kv, alignment));
+  }, py::arg("recs"), py::arg("kvs"), py::arg("alignment") = 32);
+  e.def("decode_gguf", [](const std::string& blob) {
+    std::vector<exportfmt::Tensor> ts;
+    std::vector<exportfmt::KV> kv;
+    exportfmt::decode_gguf(blob, ts, kv);
+    py::list kl;
+    for (const auto& k : kv) {
+      py::object v;
+      if (k.type == 4 || k.type == 10) v = py::int_(k.u);
+      else if (k.type == 7) v = py::bool_(k.u != 0);
+      else if (k.type == 11) v = py::int_(k.i);
+      else if (k.type == 6) v = py::float_(k.f);
+      else v = py::str(k.s);
+      kl.append(py::make_tuple(k.key, k.type, v));
+    }
+    return py::make_tuple(ex_to_py(ts), kl);
+  });
+}
+
 void register_runtime(py::module& m) {
+  register_data(m);
+  register_export(m);
   auto io_m = m.def_submodule("io", ".dlvk file format (C++)");
   io_m.def("save_v2", [](const std::string& path, const std::string& meta, const py::list& recs) {
     io::save_v2(path, meta, py_to_records(recs));

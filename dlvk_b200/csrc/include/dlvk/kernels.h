@@ -84,6 +84,19 @@ int64_t gemm_tc_workspace_floats(const GemmArgs& a, int max_ctas = 0);
 void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int max_ctas = 0,
              float* workspace = nullptr, int64_t workspace_floats = 0);
 
+// ---- int8 ----------------------------------------------------------------------
+// q[r, :] = round(x[r, :] / s[r]), s[r] = max|x[r, :]| / 127 (symmetric, per row).
+void quantize_rows_int8(DType dt, const void* x, int64_t rows, int64_t cols, int64_t ldx, int8_t* q, int64_t ldq,
+                        float* scale, cudaStream_t s);
+bool gemm_i8_tc_supported(const void* A, const void* Bt, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb);
+// C = act(sum_k A[m,k] Bt[n,k] * sa[m] * sb[n] + bias[n]); A [M,K], Bt [N,K] int8.
+void gemm_i8_tc(const int8_t* A, const int8_t* Bt, const float* sa, const float* sb, const float* bias, int act,
+                void* C, DType out_dt, int64_t ldc, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                cudaStream_t s, uint32_t* err);
+void gemm_i8_simt(const int8_t* A, const int8_t* Bt, const float* sa, const float* sb, const float* bias, int act,
+                  void* C, DType out_dt, int64_t ldc, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                  cudaStream_t s);
+
 // ---- optimizers --------------------------------------------------------------
 enum OptKind : int { OPT_SGD = 0, OPT_ADAM = 1, OPT_RMSPROP = 2 };
 // Device-resident optimizer hyper-parameters (one per optimizer instance).
@@ -107,7 +120,16 @@ void optim_update(int kind, const OptimHyper* h_dev, float* p, const void* g, DT
                   __nv_bfloat16* p_bf16, int64_t n, float extra_scale, cudaStream_t s);
 int grad_stats_scratch_floats();
 void grad_stats(const void* g, DType g_dt, int64_t n, float scale, float max_norm, float* sumsq_out, int* flag,
-                float* clip_out, bool accumulate, float* scratch, cudaStream_t s);
+                float* clip_out, bool accumulate, float* scratch, cudaStream_t s, const float* scale_ptr = nullptr);
+// x[i] *= *s (s on the device: a loss scale that a captured graph re-reads).
+void scale_by_device_scalar(DType dt, void* x, int64_t n, const float* s, cudaStream_t st);
+// Fused L1/L2 regularisation over [n) flat parameters:
+//   g += k * (l1 * sign(w) + l2 * w);  *loss_out += ll1 * |w| + 0.5 * ll2 * w^2 (if loss_out),
+// with k = *gscale (a loss scale still applied to g) or 1.  The loss
+// coefficients differ from the gradient ones for weight decay, which has a
+// gradient term and no loss term.
+void regularize(const float* w, void* g, DType g_dt, int64_t n, float l1, float l2, float ll1, float ll2,
+                float* loss_out, cudaStream_t s, const float* gscale = nullptr);
 void scaler_update(float* scale, int* good_steps, const int* found_inf, float growth, float backoff, int interval,
                    float smin, float smax, float* inv_scale, cudaStream_t s);
 
@@ -170,5 +192,59 @@ void embedding_bwd(DType dt, const int32_t* ids, const void* dy, float* dtable, 
 uint32_t* device_error_word();     // per current device, zero-initialised
 uint32_t read_device_error(bool clear);
 void counter_add(int64_t* c, int64_t delta, cudaStream_t s);
+
+// Per-step training metrics on the device: *loss_sum += *loss * loss_weight and
+// *correct += #rows whose logits argmax equals the label (labels: int ids, or
+// probs: target rows whose argmax is the class).  Either may be null.
+void step_metrics(DType dt, const void* logits, int64_t rows, int cols, const int* labels, const float* probs,
+                  const float* loss, float* loss_sum, unsigned long long* correct, float loss_weight, cudaStream_t s);
+
+// ---- recurrent cells (rnn.cu); kind 0 RNN-tanh, 1 LSTM, 2 GRU ---------------
+// Every pointer addresses B rows with its own row stride (elements).
+struct RnnCellFwd {
+  int kind = 0;
+  int64_t B = 0;
+  int H = 0;
+  const void* a = nullptr; int64_t lda = 0;        // pre-activations (GRU: input side) [B, G*H]
+  const void* hg = nullptr; int64_t ldhg = 0;      // GRU hidden side h W_hh^T + b_hh [B, 3H]
+  const void* h_prev = nullptr; int64_t ldhp = 0;  // GRU h_{t-1}
+  const float* c_prev = nullptr; int64_t ldcp = 0; // LSTM c_{t-1} (null = 0)
+  void* h_out = nullptr; int64_t ldo = 0;
+  void* h_copy = nullptr; int64_t ldcopy = 0;      // optional second copy of h_t
+  float* c_out = nullptr; int64_t ldco = 0;        // LSTM c_t
+  float* saved = nullptr; int64_t lds = 0;         // LSTM (i,f,g,o) / GRU (r,z,n,hn) [B, 4H]
+};
+struct RnnCellBwd {
+  int kind = 0;
+  int64_t B = 0;
+  int H = 0;
+  const void* dh = nullptr; int64_t lddh = 0;
+  const float* dc_next = nullptr; int64_t lddcn = 0;
+  const void* h_t = nullptr; int64_t ldht = 0;
+  const void* h_prev = nullptr; int64_t ldhp = 0;
+  const float* c_t = nullptr; int64_t ldct = 0;
+  const float* c_prev = nullptr; int64_t ldcp = 0;
+  const float* saved = nullptr; int64_t lds = 0;
+  void* dA = nullptr; int64_t ldda = 0;
+  void* dAh = nullptr; int64_t lddah = 0;
+  float* dc_prev = nullptr; int64_t lddcp = 0;
+  const void* dy_prev = nullptr; int64_t lddyp = 0;
+  void* resid = nullptr; int64_t ldres = 0;
+};
+void rnn_cell_fwd(const RnnCellFwd& p, DType dt, cudaStream_t s);
+void rnn_cell_bwd(const RnnCellBwd& p, DType dt, cudaStream_t s);
+
+// ---- batched image transforms (augment.cu), fp32 [N, C, H, W] ---------------
+// theta: [N, 6] output->input maps (sx = t0*x + t1*y + t2, sy = t3*x + t4*y + t5);
+// mode 0 nearest-floor, 1 nearest-round, 2 bilinear.
+void image_affine_sample(const float* x, float* y, int N, int C, int H, int W, int OH, int OW, const float* theta,
+                         int mode, float fill, cudaStream_t s);
+// kind 0 contrast (params [N,2]: factor, -), 1 standardise, 2 min-max (params [N,2]: lo, hi).
+void image_per_sample_stats(const float* x, float* y, int64_t N, int64_t len, int kind, const float* params,
+                            bool clamp01, cudaStream_t s);
+void image_channel_affine(const float* x, float* y, int64_t N, int C, int64_t HW, const float* mean,
+                          const float* inv_std, const float* sample_add, bool clamp01, cudaStream_t s);
+void image_gaussian_noise(const float* x, float* y, int64_t n, float sigma, uint64_t seed, uint32_t stream,
+                          cudaStream_t s);
 
 }  // namespace dlvk

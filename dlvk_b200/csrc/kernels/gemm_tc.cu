@@ -57,6 +57,9 @@ struct TcParams {
   int splits;          // split-K factor (1 = off); partials go to C (fp32 workspace)
   int kb_per_split;
   int64_t split_stride;  // elements between split slices of the workspace
+  int i8;                  // 1: int8 x int8 -> int32 (kind::i8), K-major operands
+  const float* row_scale;  // int8 dequantisation: per-row (A) and per-column (B) scales
+  const float* col_scale;
 };
 
 template <int BN>
@@ -264,7 +267,8 @@ __global__ void __launch_bounds__(320, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_per_split = p.tiles_m * p.tiles_n * p.batch;
   const int num_tiles = tiles_per_split * p.splits;  // work units
-  const int num_kb = (p.K + BK - 1) / BK;
+  const int bke = p.i8 ? 2 * BK : BK;  // elements per 128-byte k-block
+  const int num_kb = (p.K + bke - 1) / bke;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -305,14 +309,14 @@ __global__ void __launch_bounds__(320, 1)
           uint8_t* sB = sA + C::A_BYTES;
           mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
           if (!p.a_mn) {
-            tma_load_4d(sA, &tmA, &full[stage], kb * BK, tm * BM, bi, bo);
+            tma_load_4d(sA, &tmA, &full[stage], kb * bke, tm * BM, bi, bo);
           } else {
 #pragma unroll
             for (int j = 0; j < BM / 64; ++j)
               tma_load_4d(sA + j * 8192, &tmA, &full[stage], tm * BM + j * 64, kb * BK, bi, bo);
           }
           if (!p.b_mn) {
-            tma_load_4d(sB, &tmB, &full[stage], kb * BK, tn * BN, bi, bo);
+            tma_load_4d(sB, &tmB, &full[stage], kb * bke, tn * BN, bi, bo);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
@@ -328,7 +332,8 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = make_idesc(1, 1, 1, p.a_mn != 0, p.b_mn != 0, BM, BN);
+      const uint32_t idesc = p.i8 ? make_idesc(2, 1, 1, false, false, BM, BN)
+                                  : make_idesc(1, 1, 1, p.a_mn != 0, p.b_mn != 0, BM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -351,7 +356,8 @@ __global__ void __launch_bounds__(320, 1)
                                        : make_sw128_desc(aBase + k * 32, 16, 1024);
             const uint64_t bd = p.b_mn ? make_sw128_desc(bBase + k * 2048, 8192, 1024)
                                        : make_sw128_desc(bBase + k * 32, 16, 1024);
-            mma_f16(d, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+            if (p.i8) mma_i8(d, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+            else mma_f16(d, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           mma_commit(&empty[stage]);
           if (++stage == C::STAGES) {
@@ -416,6 +422,18 @@ __global__ void __launch_bounds__(320, 1)
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[i & 1][j]) * p.alpha;
+            if (p.i8) {
+              // int32 accumulators -> real values: alpha * acc * row_scale * col_scale
+              const float rs = p.alpha * p.row_scale[row];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = (float)(int)r[i & 1][j] * rs;
+              float cs[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) cs[j] = 0.f;
+              add_bias<32>(p.col_scale, true, n0, min(32, p.N - n0), cs);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] *= cs[j];
+            }
             if (p.bias) add_bias<32>(p.bias, p.bias_f32, n0, min(32, p.N - n0), v);
             apply_act<32>(p.act, v);
             const bool full = (n0 + 32 <= p.N) && p.vec_ok;
@@ -487,14 +505,15 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // 4-D bf16 tensor map: dims {d0 (contiguous), d1, inner batch, outer batch},
 // strides in elements, box {64, box1, 1, 1}, 128-byte swizzle, zero fill out
 // of bounds.
-CUtensorMap make_tmap_bf16(const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t d3, uint64_t s1,
-                           uint64_t s2, uint64_t s3, uint32_t box1) {
+CUtensorMap make_tmap(const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t d3, uint64_t s1, uint64_t s2,
+                      uint64_t s3, uint32_t box1, bool i8) {
   CUtensorMap m;
   cuuint64_t dims[4] = {d0, d1, d2, d3};
-  cuuint64_t strides[3] = {s1 * 2, s2 * 2, s3 * 2};
-  cuuint32_t box[4] = {64, box1, 1, 1};
+  const uint64_t esz = i8 ? 1 : 2;
+  cuuint64_t strides[3] = {s1 * esz, s2 * esz, s3 * esz};
+  cuuint32_t box[4] = {i8 ? 128u : 64u, box1, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+  CUresult r = encode_fn()(&m, i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw std::runtime_error("dlvk: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
@@ -634,21 +653,21 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
   CUtensorMap ta, tb;
   if (a_k) {
     const uint64_t d = (uint64_t)a.sam * (uint64_t)a.M;
-    ta = make_tmap_bf16(a.A, a.K, a.M, a.batch2, a.batch, a.sam, pick(a.batch2, a.batch2_stride_a, d),
-                        pick(a.batch, a.batch_stride_a, d), BM);
+    ta = make_tmap(a.A, a.K, a.M, a.batch2, a.batch, a.sam, pick(a.batch2, a.batch2_stride_a, d),
+                        pick(a.batch, a.batch_stride_a, d), BM, false);
   } else {
     const uint64_t d = (uint64_t)a.sak * (uint64_t)a.K;
-    ta = make_tmap_bf16(a.A, a.M, a.K, a.batch2, a.batch, a.sak, pick(a.batch2, a.batch2_stride_a, d),
-                        pick(a.batch, a.batch_stride_a, d), 64);
+    ta = make_tmap(a.A, a.M, a.K, a.batch2, a.batch, a.sak, pick(a.batch2, a.batch2_stride_a, d),
+                        pick(a.batch, a.batch_stride_a, d), 64, false);
   }
   if (b_k) {
     const uint64_t d = (uint64_t)a.sbn * (uint64_t)a.N;
-    tb = make_tmap_bf16(a.B, a.K, a.N, a.batch2, a.batch, a.sbn, pick(a.batch2, a.batch2_stride_b, d),
-                        pick(a.batch, a.batch_stride_b, d), BN);
+    tb = make_tmap(a.B, a.K, a.N, a.batch2, a.batch, a.sbn, pick(a.batch2, a.batch2_stride_b, d),
+                        pick(a.batch, a.batch_stride_b, d), BN, false);
   } else {
     const uint64_t d = (uint64_t)a.sbk * (uint64_t)a.K;
-    tb = make_tmap_bf16(a.B, a.N, a.K, a.batch2, a.batch, a.sbk, pick(a.batch2, a.batch2_stride_b, d),
-                        pick(a.batch, a.batch_stride_b, d), 64);
+    tb = make_tmap(a.B, a.N, a.K, a.batch2, a.batch, a.sbk, pick(a.batch2, a.batch2_stride_b, d),
+                        pick(a.batch, a.batch_stride_b, d), 64, false);
   }
   TcParams p{};
   p.M = (int)a.M;
@@ -722,6 +741,62 @@ int64_t gemm_tc_workspace_floats(const GemmArgs& a, int max_ctas) {
   int BN = 256, splits = 1;
   choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits);
   return splits > 1 ? (int64_t)splits * a.M * a.N * a.batch * a.batch2 : 0;
+}
+
+}  // namespace dlvk
+
+namespace dlvk {
+
+bool gemm_i8_tc_supported(const void* A, const void* Bt, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb) {
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  return al(A) && al(Bt) && K % 16 == 0 && lda % 16 == 0 && ldb % 16 == 0 && M >= 1 && N >= 16 && K >= 16 &&
+         M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31);
+}
+
+// int8 x int8 -> int32 on the tensor cores (tcgen05.mma kind::i8), both
+// operands K-major (A [M,K], Bt [N,K]), dequantised in the epilogue:
+// C = act(acc * row_scale[m] * col_scale[n] + bias[n]).
+void gemm_i8_tc(const int8_t* A, const int8_t* Bt, const float* row_scale, const float* col_scale, const float* bias,
+                int act, void* C, DType out_dt, int64_t ldc, int64_t M, int64_t N, int64_t K, int64_t lda,
+                int64_t ldb, cudaStream_t s, uint32_t* err) {
+  DLVK_CHECK(gemm_i8_tc_supported(A, Bt, M, N, K, lda, ldb), "gemm_i8_tc: unsupported shape/alignment");
+  {
+    thread_local int bound_dev = -1;
+    int dev = 0;
+    DLVK_CUDA_CHECK(cudaGetDevice(&dev));
+    if (bound_dev != dev) {
+      DLVK_CUDA_CHECK(cudaSetDevice(dev));
+      bound_dev = dev;
+    }
+  }
+  const int BN = N >= 256 ? 256 : 128;
+  CUtensorMap ta = make_tmap(A, K, M, 1, 1, lda, lda * M, lda * M, BM, true);
+  CUtensorMap tb = make_tmap(Bt, K, N, 1, 1, ldb, ldb * N, ldb * N, BN, true);
+  TcParams p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.batch = 1;
+  p.batch2 = 1;
+  p.tiles_m = (int)((M + BM - 1) / BM);
+  p.tiles_n = (int)((N + BN - 1) / BN);
+  p.C = C;
+  p.ldc = ldc;
+  p.out_f32 = out_dt == DType::F32;
+  const int esz = p.out_f32 ? 4 : 2;
+  p.vec_ok = ((reinterpret_cast<uintptr_t>(C) & 15u) == 0) && ((ldc * esz) % 16 == 0);
+  p.alpha = 1.f;
+  p.bias = bias;
+  p.bias_f32 = 1;
+  p.act = act;
+  p.err = err;
+  p.splits = 1;
+  p.kb_per_split = (int)((K + 2 * BK - 1) / (2 * BK));
+  p.i8 = 1;
+  p.row_scale = row_scale;
+  p.col_scale = col_scale;
+  if (BN == 256) launch_tc<256>(ta, tb, p, 0, s);
+  else launch_tc<128>(ta, tb, p, 0, s);
 }
 
 }  // namespace dlvk

@@ -18,6 +18,8 @@ namespace {
 
 __global__ void advance_kernel(OptimHyper* h) {
   if (threadIdx.x == 0 && blockIdx.x == 0) {
+    // A step that a loss scaler skips (non-finite gradients) does not count.
+    if (h->skip_flag_ptr && *h->skip_flag_ptr) return;
     h->step += 1;
     const float t = (float)h->step;
     if (h->bias_correction) {
@@ -154,11 +156,13 @@ __global__ void grad_stats_partial(const TG* __restrict__ g, int64_t n, float* _
   }
 }
 
-// Final: out[0] = total sum of squares * scale^2, flag = any non-finite,
+// Final: out[0] = total sum of squares * scale^2 (scale times *scale_ptr when
+// given, e.g. a loss scaler's device-resident 1/scale), flag = any non-finite,
 // clip = min(1, max_norm / (sqrt(sumsq) + 1e-6)) (if max_norm > 0).
 __global__ void grad_stats_final(const float* __restrict__ part_sq, const int* __restrict__ part_bad, int nparts,
-                                 float scale, float max_norm, float* __restrict__ sumsq_out, int* __restrict__ flag,
-                                 float* __restrict__ clip_out, int accumulate) {
+                                 float scale, const float* __restrict__ scale_ptr, float max_norm,
+                                 float* __restrict__ sumsq_out, int* __restrict__ flag, float* __restrict__ clip_out,
+                                 int accumulate) {
   __shared__ float sm[32];
   float acc = 0.f;
   int bad = 0;
@@ -169,6 +173,7 @@ __global__ void grad_stats_final(const float* __restrict__ part_sq, const int* _
   acc = block_sum(acc, sm);
   bad = __syncthreads_or(bad);
   if (threadIdx.x == 0) {
+    if (scale_ptr) scale *= *scale_ptr;
     float tot = acc * scale * scale;
     if (accumulate) tot += *sumsq_out;
     *sumsq_out = tot;
@@ -228,7 +233,7 @@ void optim_update(int kind, const OptimHyper* h_dev, float* p, const void* g, DT
 int grad_stats_scratch_floats() { return 2 * 1024; }
 
 void grad_stats(const void* g, DType g_dt, int64_t n, float scale, float max_norm, float* sumsq_out, int* flag,
-                float* clip_out, bool accumulate, float* scratch, cudaStream_t s) {
+                float* clip_out, bool accumulate, float* scratch, cudaStream_t s, const float* scale_ptr) {
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(1024, (n + 4095) / 4096));
   float* part_sq = scratch;
   int* part_bad = reinterpret_cast<int*>(scratch + 1024);
@@ -239,7 +244,7 @@ void grad_stats(const void* g, DType g_dt, int64_t n, float scale, float max_nor
   else
     throw std::runtime_error("dlvk::grad_stats: unsupported dtype");
   DLVK_POST_LAUNCH();
-  grad_stats_final<<<1, 1024, 0, s>>>(part_sq, part_bad, blocks, scale, max_norm, sumsq_out, flag, clip_out,
+  grad_stats_final<<<1, 1024, 0, s>>>(part_sq, part_bad, blocks, scale, scale_ptr, max_norm, sumsq_out, flag, clip_out,
                                       accumulate ? 1 : 0);
   DLVK_POST_LAUNCH();
 }

@@ -201,9 +201,11 @@ class ModernLayer:
 
     # Weight stream format: u32 count, then per tensor u32 nbytes + raw fp32.
     def state_tensors(self):
+        """(name, tensor) of parameters and buffers; a child's names carry its
+        index ("<j>.<name>") so two children of one type stay distinct."""
         out = [(p.name, p.master) for p in self._params]
-        for c in self._children:
-            out.extend(c.state_tensors())
+        for j, c in enumerate(self._children):
+            out.extend((f"{j}.{n}", t) for n, t in c.state_tensors())
         return out + self._buffers()
 
     def _buffers(self):
@@ -600,6 +602,150 @@ class GroupNormLayer(ModernLayer):
         xr = x.reshape(N_ * self.num_groups, -1)
         y = Fn.LayerNormFn.apply(xr, Fn._ANCHOR, None, None, self.eps).reshape(x.shape)
         return Fn.ChannelAffineFn.apply(y, Fn._ANCHOR, self.gamma, self.beta)
+
+
+class _RecurrentBase(ModernLayer):
+    """Shared parameters and state of RNN / LSTM / GRU (weights [G*H, I] and
+    [G*H, H], biases [G*H], Xavier-uniform init with bound sqrt(6/(fan_in +
+    fan_out)), src/layers/recurrent_layers.cpp:70-100).  Input [B, T, I];
+    output [B, T, H] (or the last step [B, H] with return_sequences=False).
+    Each forward starts from the stored initial state (zeros unless set);
+    the final states are kept for `get_hidden_state` / `get_cell_state`."""
+
+    cell = "rnn"
+
+    def __init__(self, input_size: int, hidden_size: int, return_sequences: bool = True, reverse: bool = False,
+                 use_bias: bool = True):
+        super().__init__()
+        from ..ops.rnn import GATES, KINDS
+
+        self.kind = KINDS[self.cell]
+        self.input_size, self.hidden_size = int(input_size), int(hidden_size)
+        self.return_sequences = bool(return_sequences)
+        self.reverse = bool(reverse)
+        G = GATES[self.kind]
+        gh = G * self.hidden_size
+        b_ih = math.sqrt(6.0 / (self.input_size + self.hidden_size))
+        b_hh = math.sqrt(6.0 / (2 * self.hidden_size))
+        self.w_ih = self._param("weight_ih", (torch.rand(gh, self.input_size) * 2 - 1) * b_ih)
+        self.w_hh = self._param("weight_hh", (torch.rand(gh, self.hidden_size) * 2 - 1) * b_hh)
+        if use_bias:
+            bias = torch.zeros(gh)
+            if self.kind == 1:
+                bias[self.hidden_size:2 * self.hidden_size] = 1.0  # forget gate
+            self.b_ih = self._param("bias_ih", bias, decay=False)
+            self.b_hh = self._param("bias_hh", torch.zeros(gh), decay=False)
+        else:
+            self.b_ih = self.b_hh = None
+        self.h0 = None
+        self.c0 = None
+        self.hidden_state = None
+        self.cell_state = None
+
+    def _directions(self):
+        return [self], [self.reverse]
+
+    def _forward(self, x):
+        from ..ops.rnn import RecurrentFn
+
+        if x.dtype != self.compute_dtype:
+            x = x.to(self.compute_dtype)
+        cells, revs = self._directions()
+        states = [(c.h0, c.c0) for c in cells]
+        y = RecurrentFn.apply(x.contiguous(), Fn._ANCHOR, cells, revs, states)
+        H = self.hidden_size
+        last = y[:, -1] if not self.reverse else y[:, 0]
+        self.hidden_state = last.detach()[..., :H]
+        if self.return_sequences:
+            return y
+        return last
+
+    # reference state API
+    def reset_hidden_state(self):
+        self.h0 = None
+        self.c0 = None
+        self.hidden_state = self.cell_state = None
+
+    reset_states = reset_hidden_state
+
+    def get_hidden_state(self):
+        return self.hidden_state
+
+    def set_hidden_state(self, h):
+        self.h0 = h
+
+    def get_cell_state(self):
+        return self.cell_state
+
+    def set_states(self, h, c):
+        self.h0, self.c0 = h, c
+
+
+class RNNLayer(_RecurrentBase):
+    """h_t = tanh(x_t W_ih^T + b_ih + h_{t-1} W_hh^T + b_hh)."""
+
+    type_name = "RNN"
+    cell = "rnn"
+
+
+class LSTMLayer(_RecurrentBase):
+    """i,f,g,o = split(x W_ih^T + h W_hh^T + b); c = f c + i g; h = o tanh(c)."""
+
+    type_name = "LSTM"
+    cell = "lstm"
+
+
+class GRULayer(_RecurrentBase):
+    """r,z = sigma(...); n = tanh(x W_in^T + b_in + r (h W_hn^T + b_hn));
+    h = (1 - z) n + z h."""
+
+    type_name = "GRU"
+    cell = "gru"
+
+
+class BidirectionalRNN(ModernLayer):
+    """Forward and time-reversed copies of one cell type; output [B, T, 2H]
+    (both directions write their half in place)."""
+
+    type_name = "Bidirectional"
+
+    def __init__(self, cell_type, input_size: int, hidden_size: int, return_sequences: bool = True):
+        super().__init__()
+        if isinstance(cell_type, str):
+            cell_type = {"rnn": RNNLayer, "lstm": LSTMLayer, "gru": GRULayer}[cell_type.lower()]
+        self.cell = cell_type.cell
+        self.input_size, self.hidden_size = int(input_size), int(hidden_size)
+        self.return_sequences = bool(return_sequences)
+        self.fwd = self._child(cell_type(input_size, hidden_size))
+        self.bwd = self._child(cell_type(input_size, hidden_size, reverse=True))
+        for c in self._children:
+            c.track = False
+
+    def _forward(self, x):
+        from ..ops.rnn import RecurrentFn
+
+        if x.dtype != self.compute_dtype:
+            x = x.to(self.compute_dtype)
+        cells = [self.fwd, self.bwd]
+        y = RecurrentFn.apply(x.contiguous(), Fn._ANCHOR, cells, [False, True],
+                              [(c.h0, c.c0) for c in cells])
+        if self.return_sequences:
+            return y
+        H = self.hidden_size
+        # last step of the forward direction, first step of the reverse one
+        return torch.cat([y[:, -1, :H], y[:, 0, H:]], -1)
+
+
+def BiLSTM(input_size: int, hidden_size: int, **kw):
+    return BidirectionalRNN(LSTMLayer, input_size, hidden_size, **kw)
+
+
+def BiGRU(input_size: int, hidden_size: int, **kw):
+    return BidirectionalRNN(GRULayer, input_size, hidden_size, **kw)
+
+
+def BiRNN(input_size: int, hidden_size: int, **kw):
+    return BidirectionalRNN(RNNLayer, input_size, hidden_size, **kw)
 
 
 # Reference adapter / legacy names (include/dlvk/layers/layer_adapters.h).

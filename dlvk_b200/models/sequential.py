@@ -32,6 +32,34 @@ def resolve_dtype(dtype) -> torch.dtype:
     return _DTYPES[str(dtype).lower()]
 
 
+_CONFIG_KEYS = ("input_size", "output_size", "in_channels", "out_channels", "kernel_size", "stride", "padding",
+                "pool_size", "num_features", "rate", "num_embeddings", "embedding_dim", "normalized_shape",
+                "embed_dim", "num_heads", "d_model", "nhead", "dim_feedforward", "max_len", "eps", "momentum",
+                "num_groups", "num_channels", "residual", "hidden_size", "num_layers", "return_sequences",
+                "bidirectional", "cell", "reverse")
+
+
+def layer_config(layer) -> dict:
+    """Constructor arguments of one layer as a JSON-able dict."""
+    d = {"type": layer.type_name}
+    for k in _CONFIG_KEYS:
+        v = getattr(layer, k, None)
+        if isinstance(v, (int, float, bool, str)):
+            d[k] = v
+    if isinstance(layer, L.ActivationLayer):
+        d["type"] = "Activation"
+        d["activation"] = layer.activation.value
+    if hasattr(layer, "bias") and hasattr(layer, "weight"):
+        d["use_bias"] = layer.bias is not None
+    if isinstance(layer, L.DenseLayer):
+        d["activation"] = layer.activation
+    if isinstance(layer, L.Conv2DLayer):
+        d["activation"] = "relu" if layer.relu else None
+    if isinstance(layer, L.ResidualLayer):
+        d["inner"] = layer_config(layer.inner)
+    return d
+
+
 class Model:
     """Abstract model interface (include/dlvk/model/model.h:15-26)."""
 
@@ -134,6 +162,18 @@ class Sequential(Model):
 
     def add_positional_encoding(self, d_model: int, max_len: int = 5000):
         return self.add(L.PositionalEncodingLayer(d_model, max_len))
+
+    def add_rnn(self, input_size: int, hidden_size: int, return_sequences: bool = True):
+        return self.add(L.RNNLayer(input_size, hidden_size, return_sequences))
+
+    def add_lstm(self, input_size: int, hidden_size: int, return_sequences: bool = True):
+        return self.add(L.LSTMLayer(input_size, hidden_size, return_sequences))
+
+    def add_gru(self, input_size: int, hidden_size: int, return_sequences: bool = True):
+        return self.add(L.GRULayer(input_size, hidden_size, return_sequences))
+
+    def add_bidirectional(self, cell: str, input_size: int, hidden_size: int, return_sequences: bool = True):
+        return self.add(L.BidirectionalRNN(cell, input_size, hidden_size, return_sequences))
 
     # ----------------------------------------------------------- build
     def build(self) -> "Sequential":
@@ -288,16 +328,9 @@ class Sequential(Model):
         return out
 
     def architecture(self) -> list:
-        arch = []
-        for layer in self.m_layers:
-            d = {"type": layer.type_name}
-            for k in ("input_size", "output_size", "in_channels", "out_channels", "kernel_size", "stride", "padding",
-                      "pool_size", "num_features", "rate", "num_embeddings", "embedding_dim", "normalized_shape",
-                      "embed_dim", "num_heads", "d_model", "nhead", "dim_feedforward"):
-                if hasattr(layer, k):
-                    d[k] = getattr(layer, k)
-            arch.append(d)
-        return arch
+        """Per-layer constructor arguments (enough to rebuild the model with
+        `models.builder.model_from_architecture`)."""
+        return [layer_config(layer) for layer in self.m_layers]
 
     def save_weights(self, filepath: str, optimizer=None, extra_meta: Optional[dict] = None):
         from ..utils import dlvk_io

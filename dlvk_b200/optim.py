@@ -60,6 +60,7 @@ class Optimizer:
         self.clip_norm: Optional[float] = None
         self.clip_value: Optional[float] = None
         self._states: Dict[int, _State] = {}
+        self._scaler = None  # a GradientScaler attached to this optimizer's hyper blocks
 
     # ---------------------------------------------------------------- API
     def get_learning_rate(self) -> float:
@@ -88,13 +89,20 @@ class Optimizer:
     def advance(self, store) -> None:
         """Advance the step counter (and bias corrections) for `store`."""
         st = self.state(store)
-        st.step += 1
         if st.cuda:
+            st.step += 1  # host mirror; the device counter skips overflowed steps
             K.N().optim_advance(st.hyper)
+        elif not self._cpu_skip():
+            st.step += 1
 
     def prepare_grads(self, store) -> None:
         """Global-norm clipping coefficient and value clipping (device side)."""
         st = self.state(store)
+        scaled = self._scaler is not None and self._scaler.enabled
+        if scaled and self.clip_value is not None:
+            raise ValueError("value clipping is not defined on loss-scaled gradients; use clip_norm")
+        if scaled:
+            return  # the scaler computed the overflow flag and the clip coefficient
         if self.clip_value is not None:
             g = store.grad
             if st.cuda:
@@ -123,6 +131,10 @@ class Optimizer:
         if st.cuda:
             K.N().optim_update(self.kind, st.hyper, p, g, m, v, pb, extra_scale)
         else:
+            if self._cpu_skip():
+                return
+            if self._scaler is not None and self._scaler.enabled:
+                extra_scale = extra_scale * float(self._scaler.inv_scale)
             self._cpu_update(st, p, g.float() * extra_scale * float(st.clip), m, v)
             if pb is not None:
                 pb.copy_(p)
@@ -144,6 +156,10 @@ class Optimizer:
             self.prepare_grads(store)
             for p in ps:
                 self.update_range(store, p.offset, p.offset + p.numel)
+
+    def _cpu_skip(self) -> bool:
+        sc = self._scaler
+        return sc is not None and sc.enabled and bool(int(sc.found_inf))
 
     # ---------------------------------------------------------------- CPU reference update
     def _cpu_update(self, st, p, g, m, v):
@@ -181,7 +197,8 @@ class Optimizer:
 
     def state_meta(self, store) -> dict:
         st = self.state(store)
-        return {"type": type(self).__name__, "step": st.step, "lr": self.lr, "beta1": self.beta1,
+        step = int(read_hyper(st.hyper)["step"]) if st.hyper is not None else st.step
+        return {"type": type(self).__name__, "step": step, "lr": self.lr, "beta1": self.beta1,
                 "beta2": self.beta2, "eps": self.eps, "momentum": self.momentum, "alpha": self.alpha,
                 "weight_decay": self.weight_decay, "bias_correction": self.bias_correction}
 

@@ -1,0 +1,5 @@
+"""Model optimisation: int8 quantisation, pruning, distillation, inference
+preparation and benchmarking (reference include/dlvk/optimization/
+model_optimizer.h)."""
+from .model_optimizer import (QuantizationType, QuantizationConfig, PruningConfig, ONNXConfig, OptimizationStats,
+                              ModelOptimizer, QuantizedDenseLayer)

@@ -19,14 +19,33 @@ from typing import Optional
 import torch
 
 from .. import _ext
+from ..ops import core as K
 
 
 class TrainStep:
-    def __init__(self, model, loss_fn, optimizer, dp=None, graph: bool = True, warmup_eager: int = 2):
+    """`scaler` (a GradientScaler) adds device-side dynamic loss scaling,
+    `regularizer` (a RegularizationManager) adds fused L1/L2 penalty
+    gradients, `metrics=True` accumulates loss x batch and the number of
+    correct argmax predictions into device counters (`epoch_metrics()` reads
+    and resets them) -- all inside the captured graph."""
+
+    def __init__(self, model, loss_fn, optimizer, dp=None, graph: bool = True, warmup_eager: int = 2,
+                 scaler=None, regularizer=None, metrics: bool = False):
         self.model = model.build()
         self.loss_fn = loss_fn
         self.opt = optimizer
         self.dp = dp
+        if dp is not None and (scaler is not None or regularizer is not None):
+            raise ValueError("with DataParallel use the optimizer's weight_decay; loss scaling and "
+                             "regularizers act on local gradients after the bucket all-reduce has started")
+        self.scaler = scaler if (scaler is not None and scaler.enabled) else None
+        self.regularizer = regularizer
+        self.metrics = bool(metrics)
+        dev = model.dev.device
+        self.loss_sum = torch.zeros(1, dtype=torch.float32, device=dev) if metrics else None
+        self.correct = torch.zeros(1, dtype=torch.int64, device=dev) if metrics else None
+        self.samples = 0
+        self.rows = 0
         self.use_graph = bool(graph) and model.dev.is_cuda
         self.warmup_eager = warmup_eager
         self.x = None
@@ -47,23 +66,74 @@ class TrainStep:
         fused = getattr(self.loss_fn, "fuses_softmax", False) and m.has_trailing_softmax()
         out = m.forward_logits(self.x) if fused else m.forward(self.x)
         loss, dout = self.loss_fn.value_and_grad(out, self.y, from_logits=fused)
+        if self.metrics:
+            self._record_metrics(out, loss)
+        if self.scaler is not None:
+            self.scaler.scale_grad_output(dout)
         torch.autograd.backward(out, dout)
         m.store.finish_backward()
+        if self.regularizer is not None:
+            self.regularizer.apply_to_store(m.store, self.scaler.scale if self.scaler is not None else None)
         if self.dp is not None:
             self.dp.finish_step()
         else:
+            if self.scaler is not None:
+                self.scaler.unscale_gradients(self.opt, m.store)
             self.opt.step(m)
+            if self.scaler is not None:
+                self.scaler.update()
         return loss
+
+    def _record_metrics(self, out, loss):
+        rows = out.numel() // out.shape[-1]
+        classify = out.shape[-1] > 1
+        y = self.y
+        if out.is_cuda:
+            labels = probs = None
+            if classify:
+                if y.is_floating_point() and y.numel() == out.numel():
+                    probs = y.reshape(rows, -1)
+                elif not y.is_floating_point():
+                    labels = y.reshape(rows)
+            K.N().step_metrics(out.detach().contiguous(), labels, probs, loss.reshape(1), self.loss_sum,
+                               self.correct if classify else None, float(self.x.shape[0]))
+        else:
+            self.loss_sum += loss.detach().float().reshape(1) * self.x.shape[0]
+            if classify:
+                pred = out.detach().reshape(rows, -1).float().argmax(-1)
+                lab = y.reshape(rows, -1).argmax(-1) if y.is_floating_point() else y.reshape(rows).long()
+                self.correct += (pred == lab).sum()
+
+    def epoch_metrics(self, reset: bool = True):
+        """(mean loss per sample, accuracy per predicted row, samples) since
+        the last reset; one D2H read."""
+        if not self.metrics:
+            raise RuntimeError("TrainStep(metrics=True) is required")
+        vals = torch.stack([self.loss_sum.double().reshape(()), self.correct.double().reshape(())]).cpu()
+        out = (float(vals[0]) / max(self.samples, 1), float(vals[1]) / max(self.rows, 1), self.samples)
+        if reset:
+            self.loss_sum.zero_()
+            self.correct.zero_()
+            self.samples = 0
+            self.rows = 0
+        return out
 
     # ---------------------------------------------------------------- staging
     def stage(self, x: torch.Tensor, y: torch.Tensor) -> None:
         """Copy a (pinned) host batch into the step's static device buffers."""
         dev = self.model.dev.device
+        if not y.is_floating_point() and y.dtype != torch.int32:
+            y = y.to(torch.int32)  # class ids: the fused loss and metrics read int32
         if self.x is None:
             self.x = torch.empty(x.shape, dtype=x.dtype, device=dev)
             self.y = torch.empty(y.shape, dtype=y.dtype, device=dev)
         if tuple(x.shape) != tuple(self.x.shape) or tuple(y.shape) != tuple(self.y.shape):
             raise ValueError("TrainStep: batch shape changed; create a new TrainStep for a new shape")
+        self.samples += int(x.shape[0]) if x.dim() else 1
+        if y.is_floating_point():
+            self.rows += y.numel() // y.shape[-1] if y.dim() > 1 else y.numel()
+        else:
+            self.rows += y.numel()
         self.x.copy_(x, non_blocking=True)
         self.y.copy_(y, non_blocking=True)
 

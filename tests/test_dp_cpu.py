@@ -25,8 +25,25 @@ def run_selftest(nproc, extra, timeout=240):
            "--master-addr", "127.0.0.1", f"--master-port={_port()}", "-m", "dlvk_b200.parallel.selftest"] + extra
     env = dict(os.environ, PYTHONPATH=ROOT + os.pathsep + os.environ.get("PYTHONPATH", ""))
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, cwd=ROOT, env=env)
-    lines = [json.loads(l) for l in r.stdout.splitlines() if l.startswith("{")]
-    return r.returncode, lines, r.stdout + r.stderr
+    return r.returncode, parse_objects(r.stdout), r.stdout + r.stderr
+
+
+def parse_objects(text):
+    """Every JSON object in `text` that carries an "ok" key (rank outputs
+    can interleave on the shared pipe, so lines are not trusted)."""
+    dec, out, i = json.JSONDecoder(), [], 0
+    while True:
+        i = text.find("{", i)
+        if i < 0:
+            return out
+        try:
+            obj, end = dec.raw_decode(text, i)
+        except json.JSONDecodeError:
+            i += 1
+            continue
+        if isinstance(obj, dict) and "ok" in obj:
+            out.append(obj)
+        i = end
 
 
 @pytest.mark.parametrize("model", ["mlp", "transformer"])
