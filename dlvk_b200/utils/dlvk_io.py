@@ -112,3 +112,13 @@ def _load_v1_weights(model, tens) -> None:
     if d.bias is not None:
         d.bias.master.copy_(b.reshape(d.bias.shape).to(d.bias.master.device))
     model.store.sync_value()
+
+
+def decode(blob: bytes):
+    """Like `load` for an in-memory `.dlvk` blob."""
+    version, variant, meta_json, recs = _ext.C().io.decode(blob)
+    try:
+        meta = json.loads(meta_json) if meta_json else {}
+    except json.JSONDecodeError:
+        meta = {"raw": meta_json}
+    return version, variant, meta, {r[0]: record_tensor(r) for r in recs}
