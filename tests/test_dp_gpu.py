@@ -30,3 +30,22 @@ def test_nccl_dp_matches_full_batch():
     rc, lines, log = run_selftest(2, ["--mode", "nccl", "--model", "transformer", "--dtype", "bf16", "--opt", "sgd"])
     assert rc == 0, log[-4000:]
     assert all(l["ok"] for l in lines), lines
+
+
+@pytest.mark.parametrize("extra", [[], ["--nccl"]])
+def test_multi_gpu_trainer_api(extra):
+    """MultiGPUTrainer + RingAllReduce (P2P kernel) on 2 GPUs."""
+    import os
+    import subprocess
+    import sys
+
+    from test_dp_cpu import ROOT, _port, parse_objects
+
+    _need(2)
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2", "--master-addr",
+           "127.0.0.1", f"--master-port={_port()}", "-m", "dlvk_b200.deployment.selftest"] + extra
+    env = dict(os.environ, PYTHONPATH=ROOT + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=300, cwd=ROOT, env=env)
+    res = parse_objects(r.stdout)
+    assert r.returncode == 0, (r.stdout + r.stderr)[-3000:]
+    assert len(res) == 2 and all(o["ok"] for o in res), res
