@@ -448,8 +448,55 @@ void register_rnn(py::module& m) {
      py::arg("dy_prev"), py::arg("resid"));
 }
 
+void bf16c(const at::Tensor& t, const char* what) {
+  check_cuda(t, what);
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16 && t.is_contiguous(), "dlvk.flash_attn: ", what,
+              " must be contiguous bf16");
+}
+
+void register_attention(py::module& m) {
+  m.def("flash_attn_supported", [](int64_t B, int64_t S, int64_t H, int64_t D, const at::Tensor& qkv) {
+    return qkv.is_cuda() && qkv.scalar_type() == at::kBFloat16 && qkv.is_contiguous() &&
+           flash_attention_supported(B, S, H, D, qkv.data_ptr());
+  });
+  m.def("flash_attn_fwd", [](const at::Tensor& qkv, int64_t B, int64_t S, int64_t H, double scale,
+                             int64_t max_ctas) {
+    bf16c(qkv, "qkv");
+    TORCH_CHECK(qkv.numel() == B * S * 3 * H * 64, "dlvk.flash_attn_fwd: qkv must be [B, S, 3*H*64]");
+    c10::cuda::CUDAGuard g(qkv.device());
+    auto out = at::empty({B, S, H * 64}, qkv.options());
+    auto lse = at::empty({B, H, S}, qkv.options().dtype(at::kFloat));
+    flash_attention_fwd(reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),
+                        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), lse.data_ptr<float>(), (int)B, (int)S,
+                        (int)H, (float)scale, stream(), device_error_word(), (int)max_ctas);
+    return py::make_tuple(out, lse);
+  }, py::arg("qkv"), py::arg("B"), py::arg("S"), py::arg("H"), py::arg("scale"), py::arg("max_ctas") = 0);
+  m.def("flash_attn_bwd", [](const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& dout,
+                             const at::Tensor& lse, int64_t B, int64_t S, int64_t H, double scale, int64_t max_ctas) {
+    bf16c(qkv, "qkv");
+    bf16c(out, "out");
+    bf16c(dout, "dout");
+    check_cuda(lse, "lse");
+    TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.numel() == B * H * S && lse.is_contiguous(),
+                "dlvk.flash_attn_bwd: lse [B, H, S] fp32");
+    TORCH_CHECK(out.numel() == B * S * H * 64 && dout.numel() == out.numel(), "dlvk.flash_attn_bwd: out/dout shape");
+    c10::cuda::CUDAGuard g(qkv.device());
+    auto dqkv = at::empty({B, S, 3 * H * 64}, qkv.options());
+    auto delta = at::empty({B, H, S}, lse.options());
+    auto acc = at::empty({B * S, H * 64}, lse.options());
+    flash_attention_bwd(reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),
+                        reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()),
+                        reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), lse.data_ptr<float>(),
+                        delta.data_ptr<float>(), acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()),
+                        (int)B, (int)S, (int)H, (float)scale, stream(), device_error_word(), (int)max_ctas);
+    return dqkv;
+  }, py::arg("qkv"), py::arg("out"), py::arg("dout"), py::arg("lse"), py::arg("B"), py::arg("S"), py::arg("H"),
+     py::arg("scale"), py::arg("max_ctas") = 0);
+}
+
 void register_nn(py::module& m) {
   register_image(m);
+  register_attention(m);
   register_rnn(m);
   m.def("quantize_rows", &quantize_rows_op);
   m.def("gemm_i8", &gemm_i8_op, py::arg("qa"), py::arg("qbt"), py::arg("sa"), py::arg("sb"),

@@ -199,6 +199,17 @@ void counter_add(int64_t* c, int64_t delta, cudaStream_t s);
 void step_metrics(DType dt, const void* logits, int64_t rows, int cols, const int* labels, const float* probs,
                   const float* loss, float* loss_sum, unsigned long long* correct, float loss_weight, cudaStream_t s);
 
+// ---- fused attention on tcgen05 (attention_tc.cu): head dim 64, S % 128 == 0 --
+// qkv: [B, S, 3, H, 64] bf16; out: [B, S, H*64] bf16; lse: [B, H, S] fp32 (log2 units).
+bool flash_attention_supported(int64_t B, int64_t S, int64_t H, int64_t D, const void* qkv);
+void flash_attention_fwd(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* lse, int B, int S, int H, float scale,
+                         cudaStream_t s, uint32_t* err, int max_ctas = 0);
+// dqkv: [B, S, 3, H, 64] bf16 (fully written); delta: [B, H, S] and dq_acc:
+// [B*S, H*64] fp32 scratch.
+void flash_attention_bwd(const __nv_bfloat16* qkv, const __nv_bfloat16* out, const __nv_bfloat16* dout,
+                         const float* lse, float* delta, float* dq_acc, __nv_bfloat16* dqkv, int B, int S, int H,
+                         float scale, cudaStream_t s, uint32_t* err, int max_ctas = 0);
+
 // ---- recurrent cells (rnn.cu); kind 0 RNN-tanh, 1 LSTM, 2 GRU ---------------
 // Every pointer addresses B rows with its own row stride (elements).
 struct RnnCellFwd {

@@ -1,0 +1,710 @@
+// Fused multi-head attention on the 5th-generation tensor cores (tcgen05),
+// forward and backward, for head dim 64 and sequence lengths that are a
+// multiple of 128 (non-causal, no mask: the encoder attention of the
+// reference's MultiHeadAttentionLayer, include/dlvk/layers/modern_layers.h:
+// 75-129; its shader shaders/multi_head_attention.comp:33-114 never
+// normalised the softmax).
+//
+// Q, K and V are read in place from the fused QKV projection output
+// [B, S, 3, H, 64] (bf16) through one 2-D TMA map over [B*S, 3*H*64].
+//
+// Forward (flash_fwd_kernel): persistent CTAs walk (batch, head, 128-query
+// tile) items.  Warp 0 issues TMA loads (Q double-buffered, K/V in a
+// 3-stage ring), warp 1 issues tcgen05.mma (S = Q K^T into one of two TMEM
+// score buffers; O += P V into a TMEM accumulator), warps 2..5 own one
+// query row per thread: they read the score row from TMEM, keep the online
+// max / sum in the log2 domain, rescale O in TMEM only when a row's max grew
+// by more than 2^8 (warp-uniform decision, since tcgen05.ld/st are
+// warp-collective), write P (bf16) into shared memory in the 128-byte
+// swizzled K-major layout the next MMA reads, and finally normalise O and
+// store it with the row's log-sum-exp (log2 units) for the backward pass.
+//
+// Backward (flash_bwd_kernel): persistent CTAs walk (batch, head, 128-key
+// tile) items with K and V resident.  For each query tile the MMA warp
+// computes S^T = K Q^T and dP^T = V dO^T into TMEM; warps 2..5 (one key row
+// per thread) rebuild P^T = exp2(S^T c - lse) and dS^T = P^T (dP^T - delta)
+// into shared memory; the MMA warp then accumulates dV += P^T dO and
+// dK += dS^T Q in TMEM and computes dQ = dS K reading the same dS^T tile as
+// an MN-major operand.  The dQ tile goes through shared memory to the
+// global fp32 accumulator with TMA bulk reduce-add; dK / dV are written to
+// the fused gradient buffer [B, S, 3, H, 64] when the key tile is done.
+//
+// Every mbarrier wait is bounded (mbar_wait: error word + early exit).
+#include <cuda.h>
+
+#include "dlvk/common.h"
+#include "dlvk/kernels.h"
+#include "dlvk/sm100.h"
+#include "dlvk/tmap.h"
+
+namespace dlvk {
+namespace {
+using namespace sm100;
+
+constexpr int FT = 128;                  // query / key tile
+constexpr int FD = 64;                   // head dim
+constexpr int TILE = FT * FD * 2;        // one bf16 [128 x 64] tile, 16 KB
+constexpr int KV_STAGES = 3;
+
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Byte offset of 16-byte chunk `c` (8 bf16, c in 0..15) of row `r` in a
+// [128 x 128] bf16 K-major operand stored as two 128-byte-swizzled
+// [128 x 64] sub-tiles (the layout TMA SWIZZLE_128B produces).
+__device__ __forceinline__ uint32_t sw_off(int r, int c) {
+  return (uint32_t)((c >> 3) * 16384 + (r >> 3) * 1024 + (r & 7) * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+// Bounded wait whose outcome is the same in every lane of the warp (the
+// warp-collective tcgen05.ld / st that follow need all 32 lanes).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
+  const bool ok = mbar_wait(bar, parity, err);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// Bounded barrier among the 128 compute threads on an mbarrier of count 128
+// (bar.sync has no timeout; this gives up with the error word set).
+__device__ __forceinline__ bool group_sync(uint64_t* bar, uint32_t& phase, uint32_t* err) {
+  mbar_arrive(bar);
+  const bool ok = mbar_wait(bar, phase, err);
+  phase ^= 1u;
+  return __all_sync(0xffffffffu, ok);
+}
+
+struct FwdP {
+  __nv_bfloat16* out;
+  float* lse;
+  int B, S, H, E;
+  float c;  // softmax scale * log2(e)
+  uint32_t* err;
+};
+
+// Shared memory: Q x2 | (K, V) x KV_STAGES | P (32 KB) | barriers.
+constexpr int FWD_SMEM = 2 * TILE + KV_STAGES * 2 * TILE + 2 * TILE + 256 + 1024;
+
+__global__ void __launch_bounds__(192, 1) flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, FwdP p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sKV = smem + 2 * TILE;
+  uint8_t* sP = sKV + KV_STAGES * 2 * TILE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * TILE);
+  uint64_t* q_full = bars;         // 2
+  uint64_t* q_empty = bars + 2;    // 2
+  uint64_t* kv_full = bars + 4;    // 3
+  uint64_t* kv_empty = bars + 7;   // 3
+  uint64_t* s_full = bars + 10;    // 2
+  uint64_t* s_empty = bars + 12;   // 2
+  uint64_t* p_full = bars + 14;
+  uint64_t* pv_done = bars + 15;
+  uint64_t* o_empty = bars + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nt = p.S / FT;
+  const int items = p.B * p.H * nt;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 4);
+    }
+    for (int i = 0; i < KV_STAGES; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(pv_done, 1);
+    mbar_init(o_empty, 4);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;  // S0: cols 0..127, S1: 128..255, O: 256..319
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tm);
+      int it = 0;
+      int kvs = 0;
+      uint32_t kvph = 0;
+      for (int item = blockIdx.x; item < items; item += gridDim.x, ++it) {
+        const int qt = item % nt, bh = item / nt, h = bh % p.H, b = bh / p.H;
+        const int qs = it & 1;
+        if (!mbar_wait(&q_empty[qs], ((it >> 1) & 1) ^ 1u, p.err)) break;
+        mbar_arrive_expect_tx(&q_full[qs], TILE);
+        tma_load_2d(sQ + qs * TILE, &tm, &q_full[qs], h * FD, b * p.S + qt * FT);
+        bool ok = true;
+        for (int j = 0; j < nt; ++j) {
+          if (!mbar_wait(&kv_empty[kvs], kvph ^ 1u, p.err)) { ok = false; break; }
+          uint8_t* k = sKV + kvs * 2 * TILE;
+          mbar_arrive_expect_tx(&kv_full[kvs], 2 * TILE);
+          tma_load_2d(k, &tm, &kv_full[kvs], p.E + h * FD, b * p.S + j * FT);
+          tma_load_2d(k + TILE, &tm, &kv_full[kvs], 2 * p.E + h * FD, b * p.S + j * FT);
+          if (++kvs == KV_STAGES) {
+            kvs = 0;
+            kvph ^= 1u;
+          }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_s = make_idesc(1, 1, 1, false, false, 128, 128);
+      const uint32_t id_o = make_idesc(1, 1, 1, false, true, 128, 64);
+      int it = 0, kvs = 0, sb = 0;
+      uint32_t kvph = 0, sph = 0, pph = 0, oph = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < items && ok; item += gridDim.x, ++it) {
+        const int qs = it & 1;
+        if (!mbar_wait(&q_full[qs], (it >> 1) & 1, p.err)) break;
+        const uint32_t qa = smem_u32(sQ + qs * TILE);
+        int prev = 0;
+        for (int j = 0; j <= nt; ++j) {
+          if (j < nt) {
+            if (!mbar_wait(&kv_full[kvs], kvph, p.err) || !mbar_wait(&s_empty[sb], sph ^ 1u, p.err)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t ka = smem_u32(sKV + kvs * 2 * TILE);
+#pragma unroll
+            for (int k = 0; k < FD / 16; ++k)
+              mma_f16(tbase + (uint32_t)(sb * 128), make_sw128_desc(qa + k * 32, 16, 1024),
+                      make_sw128_desc(ka + k * 32, 16, 1024), id_s, k ? 1u : 0u);
+            mma_commit(&s_full[sb]);
+            if (j == nt - 1) mma_commit(&q_empty[qs]);
+          }
+          if (j > 0) {
+            if (j == 1) {
+              if (!mbar_wait(o_empty, oph ^ 1u, p.err)) { ok = false; break; }
+              oph ^= 1u;
+            }
+            if (!mbar_wait(p_full, pph, p.err)) { ok = false; break; }
+            pph ^= 1u;
+            tc_fence_after();
+            const uint32_t va = smem_u32(sKV + prev * 2 * TILE + TILE);
+            const uint32_t pa = smem_u32(sP);
+#pragma unroll
+            for (int k = 0; k < FT / 16; ++k)
+              mma_f16(tbase + 256, make_sw128_desc(pa + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024),
+                      make_sw128_desc(va + k * 2048, 16384, 1024), id_o, (j > 1 || k > 0) ? 1u : 0u);
+            mma_commit(&kv_empty[prev]);
+            mma_commit(pv_done);
+          }
+          if (j < nt) {
+            prev = kvs;
+            if (++kvs == KV_STAGES) {
+              kvs = 0;
+              kvph ^= 1u;
+            }
+            if (++sb == 2) {
+              sb = 0;
+              sph ^= 1u;
+            }
+          }
+        }
+      }
+    }
+  } else {
+    // Softmax warps: warp w reads TMEM lanes 32*(w%4) .. +31 (row = query).
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    int sb = 0;
+    uint32_t sph = 0, pvph = 0;
+    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+      const int qt = item % nt, bh = item / nt, h = bh % p.H, b = bh / p.H;
+      float m = -INFINITY, l = 0.f;
+      bool ok = true;
+      for (int j = 0; j < nt; ++j) {
+        if (!warp_wait(&s_full[sb], sph, p.err)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t sr[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(tbase + lane_off + (uint32_t)(sb * 128 + c * 32), sr[c]);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty[sb]);
+        if (++sb == 2) {
+          sb = 0;
+          sph ^= 1u;
+        }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(sr[c][i]));
+        mx *= p.c;
+        const bool need = mx > m + 8.f;  // lazy rescale: keep the old reference max while it is within 2^8
+        const float m_new = need ? mx : m;
+        const float alpha = need ? exp2f(m - m_new) : 1.f;
+        if (j > 0) {
+          // PV of the previous tile must be done before O is rescaled or P rewritten.
+          if (!warp_wait(pv_done, pvph, p.err)) { ok = false; break; }
+          pvph ^= 1u;
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              uint32_t o[32];
+              const uint32_t ta = tbase + lane_off + 256u + (uint32_t)(c * 32);
+              tmem_ld32(ta, o);
+              tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+              tmem_st32(ta, o);
+            }
+            tmem_st_wait();
+          }
+        }
+        l *= alpha;
+        m = m_new;
+        float sum = 0.f;
+        uint8_t* prow = sP;
+#pragma unroll
+        for (int ch = 0; ch < 16; ++ch) {
+          float e[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            e[i] = exp2f(fmaf(__uint_as_float(sr[ch >> 2][(ch & 3) * 8 + i]), p.c, -m));
+            sum += e[i];
+          }
+          uint4 v;
+          v.x = pack2(e[0], e[1]);
+          v.y = pack2(e[2], e[3]);
+          v.z = pack2(e[4], e[5]);
+          v.w = pack2(e[6], e[7]);
+          *reinterpret_cast<uint4*>(prow + sw_off(row, ch)) = v;
+        }
+        l += sum;
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full);
+      }
+      if (!ok) break;
+      if (!warp_wait(pv_done, pvph, p.err)) break;
+      pvph ^= 1u;
+      tc_fence_after();
+      uint32_t o0[32], o1[32];
+      tmem_ld32(tbase + lane_off + 256u, o0);
+      tmem_ld32(tbase + lane_off + 288u, o1);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(o_empty);
+      const float inv = 1.f / l;
+      const int64_t grow = (int64_t)b * p.S + (int64_t)qt * FT + row;
+      uint4* dst = reinterpret_cast<uint4*>(p.out + grow * p.E + h * FD);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t* src = c < 4 ? &o0[c * 8] : &o1[(c - 4) * 8];
+        uint4 v;
+        v.x = pack2(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
+        v.y = pack2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
+        v.z = pack2(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
+        v.w = pack2(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
+        dst[c] = v;
+      }
+      p.lse[((int64_t)b * p.H + h) * p.S + (int64_t)qt * FT + row] = m + log2f(l);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+// ---------------------------------------------------------------- backward
+struct BwdP {
+  const float* lse;    // [B, H, S] log2 units
+  const float* delta;  // [B, H, S] rowsum(dO * O)
+  __nv_bfloat16* dqkv; // [B, S, 3E]
+  int B, S, H, E;
+  float c;             // scale * log2(e)
+  float scale;
+  uint32_t* err;
+};
+
+// Shared memory: K | V | (Q, dO) x2 | P^T (32 KB) | dS^T (32 KB) | dQ staging
+// (2 x 16 KB fp32, 128-byte swizzled) | lse x2 | delta x2 | barriers.
+constexpr int BWD_SMEM = 2 * TILE + 2 * 2 * TILE + 2 * TILE + 2 * TILE + 2 * TILE + 4 * 128 * 4 + 256 + 1024;
+
+__device__ __forceinline__ void tma_reduce_add_2d(const void* tmap, const void* src, int x, int y) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+      "r"(smem_u32(src)), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__global__ void __launch_bounds__(192, 1) flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv,
+                                                           const __grid_constant__ CUtensorMap tm_do,
+                                                           const __grid_constant__ CUtensorMap tm_dq, BwdP p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = smem + TILE;
+  uint8_t* sQD = smem + 2 * TILE;            // stage s: Q at s*2*TILE, dO at +TILE
+  uint8_t* sPT = smem + 6 * TILE;            // 32 KB
+  uint8_t* sDS = smem + 8 * TILE;            // 32 KB
+  uint8_t* sDQ = smem + 10 * TILE;           // 32 KB fp32 staging
+  float* sLse = reinterpret_cast<float*>(smem + 12 * TILE);   // [2][128]
+  float* sDel = sLse + 256;                                   // [2][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDel + 256);
+  uint64_t* kv_full = bars;
+  uint64_t* kv_empty = bars + 1;
+  uint64_t* qd_full = bars + 2;   // 2
+  uint64_t* qd_empty = bars + 4;  // 2
+  uint64_t* st_full = bars + 6;
+  uint64_t* ds_full = bars + 7;
+  uint64_t* dq_full = bars + 8;
+  uint64_t* dq_free = bars + 9;
+  uint64_t* kv_done = bars + 10;   // dK, dV accumulated for the item
+  uint64_t* kv_read = bars + 11;   // dK, dV read out of TMEM
+  uint64_t* cw_bar = bars + 12;    // compute-warp group barrier (128 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nt = p.S / FT;
+  const int items = p.B * p.H * nt;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(kv_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qd_full[i], 1);
+      mbar_init(&qd_empty[i], 1);
+    }
+    mbar_init(st_full, 1);
+    mbar_init(ds_full, 4);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 4);
+    mbar_init(kv_done, 1);
+    mbar_init(kv_read, 4);
+    mbar_init(cw_bar, 128);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  // TMEM: S^T 0..127, dP^T 128..255, dV 256..319, dK 320..383, dQ 384..447
+  const uint32_t tbase = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tm_qkv);
+      prefetch_tmap(&tm_do);
+      int it = 0, qs = 0;
+      uint32_t qph = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < items && ok; item += gridDim.x, ++it) {
+        const int kt = item % nt, bh = item / nt, h = bh % p.H, b = bh / p.H;
+        if (!mbar_wait(kv_empty, (it & 1) ^ 1u, p.err)) break;
+        mbar_arrive_expect_tx(kv_full, 2 * TILE);
+        tma_load_2d(sK, &tm_qkv, kv_full, p.E + h * FD, b * p.S + kt * FT);
+        tma_load_2d(sV, &tm_qkv, kv_full, 2 * p.E + h * FD, b * p.S + kt * FT);
+        for (int i = 0; i < nt; ++i) {
+          if (!mbar_wait(&qd_empty[qs], qph ^ 1u, p.err)) { ok = false; break; }
+          uint8_t* d = sQD + qs * 2 * TILE;
+          mbar_arrive_expect_tx(&qd_full[qs], 2 * TILE);
+          tma_load_2d(d, &tm_qkv, &qd_full[qs], h * FD, b * p.S + i * FT);
+          tma_load_2d(d + TILE, &tm_do, &qd_full[qs], h * FD, b * p.S + i * FT);
+          if (++qs == 2) {
+            qs = 0;
+            qph ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_st = make_idesc(1, 1, 1, false, false, 128, 128);  // S^T, dP^T: K-major A and B
+      const uint32_t id_kv = make_idesc(1, 1, 1, false, true, 128, 64);    // dV, dK: K-major A, MN-major B
+      const uint32_t id_q = make_idesc(1, 1, 1, true, true, 128, 64);      // dQ: MN-major A and B
+      int it = 0, qs = 0;
+      uint32_t qph = 0, dsph = 0, dqph = 0;
+      bool ok = true;
+      const uint32_t ka = smem_u32(sK), va = smem_u32(sV), pta = smem_u32(sPT), dsa = smem_u32(sDS);
+      for (int item = blockIdx.x; item < items && ok; item += gridDim.x, ++it) {
+        if (!mbar_wait(kv_full, it & 1, p.err)) break;
+        if (!mbar_wait(kv_read, (it & 1) ^ 1u, p.err)) break;  // previous item's dK / dV read out
+        for (int i = 0; i < nt; ++i) {
+          if (!mbar_wait(&qd_full[qs], qph, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t qa = smem_u32(sQD + qs * 2 * TILE), doa = qa + TILE;
+#pragma unroll
+          for (int k = 0; k < FD / 16; ++k) {
+            mma_f16(tbase, make_sw128_desc(ka + k * 32, 16, 1024), make_sw128_desc(qa + k * 32, 16, 1024), id_st,
+                    k ? 1u : 0u);
+            mma_f16(tbase + 128, make_sw128_desc(va + k * 32, 16, 1024), make_sw128_desc(doa + k * 32, 16, 1024),
+                    id_st, k ? 1u : 0u);
+          }
+          mma_commit(st_full);
+          if (!mbar_wait(ds_full, dsph, p.err)) { ok = false; break; }
+          dsph ^= 1u;
+          if (!mbar_wait(dq_free, dqph ^ 1u, p.err)) { ok = false; break; }
+          dqph ^= 1u;
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < FT / 16; ++k) {
+            const uint32_t koff = (uint32_t)((k >> 2) * 16384 + (k & 3) * 32);
+            // dV += P^T dO, dK += dS^T Q: A K-major [keys x queries], B = dO / Q as MN-major [queries x d]
+            mma_f16(tbase + 256, make_sw128_desc(pta + koff, 16, 1024), make_sw128_desc(doa + k * 2048, 16384, 1024),
+                    id_kv, (i > 0 || k > 0) ? 1u : 0u);
+            mma_f16(tbase + 320, make_sw128_desc(dsa + koff, 16, 1024), make_sw128_desc(qa + k * 2048, 16384, 1024),
+                    id_kv, (i > 0 || k > 0) ? 1u : 0u);
+            // dQ = dS K: A = dS^T tile read MN-major (M = queries in 64-wide chunks 16 KB apart), B = K MN-major
+            mma_f16(tbase + 384, make_sw128_desc(dsa + k * 2048, 16384, 1024),
+                    make_sw128_desc(ka + k * 2048, 16384, 1024), id_q, k > 0 ? 1u : 0u);
+          }
+          mma_commit(dq_full);
+          mma_commit(&qd_empty[qs]);
+          if (++qs == 2) {
+            qs = 0;
+            qph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(kv_empty);
+        mma_commit(kv_done);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // key row (S^T, dP^T, dK, dV) or query row (dQ)
+    const int tid = threadIdx.x - 64;     // 0..127
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    uint32_t stph = 0, dqph = 0, cwph = 0;
+    int it = 0, ib = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < items && ok; item += gridDim.x, ++it) {
+      const int kt = item % nt, bh = item / nt, h = bh % p.H, b = bh / p.H;
+      const int64_t lbase = ((int64_t)b * p.H + h) * p.S;
+      for (int i = 0; i < nt; ++i, ib ^= 1) {
+        sLse[ib * 128 + tid] = p.lse[lbase + i * FT + tid];
+        sDel[ib * 128 + tid] = p.delta[lbase + i * FT + tid];
+        if (!group_sync(cw_bar, cwph, p.err)) { ok = false; break; }
+        if (!warp_wait(st_full, stph, p.err)) { ok = false; break; }
+        stph ^= 1u;
+        tc_fence_after();
+        const float* L = sLse + ib * 128;
+        const float* Dl = sDel + ib * 128;
+#pragma unroll 1
+        for (int cb = 0; cb < 4; ++cb) {  // 32 query columns at a time
+          uint32_t s[32], dp[32];
+          tmem_ld32(tbase + lane_off + (uint32_t)(cb * 32), s);
+          tmem_ld32(tbase + lane_off + 128u + (uint32_t)(cb * 32), dp);
+          tmem_ld_wait();
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {  // 8 queries per 16-byte chunk
+            float pt[8], ds[8];
+#pragma unroll
+            for (int i8 = 0; i8 < 8; ++i8) {
+              const int qi = cb * 32 + q4 * 8 + i8;
+              pt[i8] = exp2f(fmaf(__uint_as_float(s[q4 * 8 + i8]), p.c, -L[qi]));
+              ds[i8] = pt[i8] * (__uint_as_float(dp[q4 * 8 + i8]) - Dl[qi]);
+            }
+            const int ch = cb * 4 + q4;
+            uint4 a, d;
+            a.x = pack2(pt[0], pt[1]); a.y = pack2(pt[2], pt[3]); a.z = pack2(pt[4], pt[5]); a.w = pack2(pt[6], pt[7]);
+            d.x = pack2(ds[0], ds[1]); d.y = pack2(ds[2], ds[3]); d.z = pack2(ds[4], ds[5]); d.w = pack2(ds[6], ds[7]);
+            *reinterpret_cast<uint4*>(sPT + sw_off(row, ch)) = a;
+            *reinterpret_cast<uint4*>(sDS + sw_off(row, ch)) = d;
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ds_full);
+        // dQ tile (row = query): TMEM -> swizzled fp32 staging -> TMA reduce-add.
+        if (!warp_wait(dq_full, dqph, p.err)) { ok = false; break; }
+        dqph ^= 1u;
+        tc_fence_after();
+        uint32_t q0[32], q1[32];
+        tmem_ld32(tbase + lane_off + 384u, q0);
+        tmem_ld32(tbase + lane_off + 416u, q1);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_free);
+        if (tid == 0) bulk_wait_read0();  // the previous reduce has read the staging buffer
+        if (!group_sync(cw_bar, cwph, p.err)) { ok = false; break; }
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const uint32_t* src = half ? q1 : q0;
+          uint8_t* base = sDQ + half * 16384 + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            uint4 v = make_uint4(src[c * 4], src[c * 4 + 1], src[c * 4 + 2], src[c * 4 + 3]);
+            *reinterpret_cast<uint4*>(base + ((c ^ (row & 7)) << 4)) = v;
+          }
+        }
+        fence_proxy_async_smem();
+        if (!group_sync(cw_bar, cwph, p.err)) { ok = false; break; }
+        if (tid == 0) {
+          const int y = b * p.S + i * FT;
+          tma_reduce_add_2d(&tm_dq, sDQ, h * FD, y);
+          tma_reduce_add_2d(&tm_dq, sDQ + 16384, h * FD + 32, y);
+          bulk_commit();
+        }
+      }
+      if (!ok) break;
+      // dK (scaled) and dV of this key tile -> the fused gradient buffer.
+      if (!warp_wait(kv_done, it & 1, p.err)) break;
+      tc_fence_after();
+      const int64_t grow = (int64_t)b * p.S + (int64_t)kt * FT + row;
+#pragma unroll
+      for (int w2 = 0; w2 < 2; ++w2) {  // 0: dV (cols 256..), 1: dK (cols 320..)
+        uint32_t a0[32], a1[32];
+        tmem_ld32(tbase + lane_off + 256u + (uint32_t)(w2 * 64), a0);
+        tmem_ld32(tbase + lane_off + 288u + (uint32_t)(w2 * 64), a1);
+        tmem_ld_wait();
+        const float sc = w2 ? p.scale : 1.f;
+        uint4* dst = reinterpret_cast<uint4*>(p.dqkv + grow * 3 * p.E + (w2 ? p.E : 2 * p.E) + h * FD);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint32_t* s = c < 4 ? &a0[c * 8] : &a1[(c - 4) * 8];
+          uint4 v;
+          v.x = pack2(__uint_as_float(s[0]) * sc, __uint_as_float(s[1]) * sc);
+          v.y = pack2(__uint_as_float(s[2]) * sc, __uint_as_float(s[3]) * sc);
+          v.z = pack2(__uint_as_float(s[4]) * sc, __uint_as_float(s[5]) * sc);
+          v.w = pack2(__uint_as_float(s[6]) * sc, __uint_as_float(s[7]) * sc);
+          dst[c] = v;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(kv_read);
+    }
+    if (tid == 0) bulk_wait0();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+// delta[b, h, q] = sum_d dO[b, q, h, d] * O[b, q, h, d]; one warp per (b, q, h).
+__global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
+                                  float* __restrict__ delta, int B, int S, int H) {
+  const int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t total = (int64_t)B * S * H;
+  if (w >= total) return;
+  const int h = (int)(w % H);
+  const int64_t bq = w / H;
+  const int q = (int)(bq % S), b = (int)(bq / S);
+  const __nv_bfloat162* a = reinterpret_cast<const __nv_bfloat162*>(o + w * FD) + lane;
+  const __nv_bfloat162* d = reinterpret_cast<const __nv_bfloat162*>(dout + w * FD) + lane;
+  const float2 x = __bfloat1622float2(*a), y = __bfloat1622float2(*d);
+  const float v = warp_sum(x.x * y.x + x.y * y.y);
+  if (lane == 0) delta[((int64_t)b * H + h) * S + q] = v;
+}
+
+// dqkv[:, :, 0] = bf16(dq_acc * scale)
+__global__ void attn_dq_finish_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dqkv, int64_t rows,
+                                      int E, float scale) {
+  const int64_t n4 = rows * E / 4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = reinterpret_cast<const float4*>(acc)[i];
+    const int64_t e = i * 4;
+    const int64_t r = e / E, c = e % E;
+    uint2 o;
+    o.x = pack2(v.x * scale, v.y * scale);
+    o.y = pack2(v.z * scale, v.w * scale);
+    *reinterpret_cast<uint2*>(dqkv + r * 3 * E + c) = o;
+  }
+}
+
+}  // namespace
+
+bool flash_attention_supported(int64_t B, int64_t S, int64_t H, int64_t D, const void* qkv) {
+  return D == FD && S % FT == 0 && S > 0 && B > 0 && H > 0 && (reinterpret_cast<uintptr_t>(qkv) & 15u) == 0 &&
+         B * S < (1LL << 31) && 3 * H * D < (1LL << 31);
+}
+
+void flash_attention_fwd(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* lse, int B, int S, int H, float scale,
+                         cudaStream_t s, uint32_t* err, int max_ctas) {
+  DLVK_CHECK(flash_attention_supported(B, S, H, FD, qkv), "flash_attention_fwd: unsupported shape");
+  tmap::bind_context();
+  const int E = H * FD;
+  CUtensorMap tm = tmap::bf16_2d_sw128(qkv, (uint64_t)3 * E, (uint64_t)B * S, (uint64_t)3 * E, FT);
+  FwdP p{out, lse, B, S, H, E, scale * 1.4426950408889634f, err};
+  static bool attr = false;
+  if (!attr) {
+    DLVK_CUDA_CHECK(cudaFuncSetAttribute(flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM));
+    attr = true;
+  }
+  const int items = B * H * (S / FT);
+  int grid = std::min(items, max_ctas > 0 ? max_ctas : tmap::sm_count());
+  flash_fwd_kernel<<<grid, 192, FWD_SMEM, s>>>(tm, p);
+  DLVK_POST_LAUNCH();
+}
+
+void flash_attention_bwd(const __nv_bfloat16* qkv, const __nv_bfloat16* out, const __nv_bfloat16* dout,
+                         const float* lse, float* delta, float* dq_acc, __nv_bfloat16* dqkv, int B, int S, int H,
+                         float scale, cudaStream_t s, uint32_t* err, int max_ctas) {
+  DLVK_CHECK(flash_attention_supported(B, S, H, FD, qkv), "flash_attention_bwd: unsupported shape");
+  tmap::bind_context();
+  const int E = H * FD;
+  const int64_t rows = (int64_t)B * S;
+  {
+    const int64_t threads = rows * H * 32;
+    attn_delta_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(out, dout, delta, B, S, H);
+    DLVK_POST_LAUNCH();
+  }
+  DLVK_CUDA_CHECK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * E, s));
+  CUtensorMap tq = tmap::bf16_2d_sw128(qkv, (uint64_t)3 * E, (uint64_t)rows, (uint64_t)3 * E, FT);
+  CUtensorMap td = tmap::bf16_2d_sw128(dout, (uint64_t)E, (uint64_t)rows, (uint64_t)E, FT);
+  CUtensorMap tdq;
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)E, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)E * 4};
+    cuuint32_t box[2] = {32u, (cuuint32_t)FT};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = tmap::encode_fn()(&tdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dq_acc, dims, strides, box, estr,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("dlvk: dq tensor map failed (" + std::to_string((int)r) + ")");
+  }
+  BwdP p{lse, delta, dqkv, B, S, H, E, scale * 1.4426950408889634f, scale, err};
+  static bool attr = false;
+  if (!attr) {
+    DLVK_CUDA_CHECK(cudaFuncSetAttribute(flash_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM));
+    attr = true;
+  }
+  const int items = B * H * (S / FT);
+  const int grid = std::min(items, max_ctas > 0 ? max_ctas : tmap::sm_count());
+  flash_bwd_kernel<<<grid, 192, BWD_SMEM, s>>>(tq, td, tdq, p);
+  DLVK_POST_LAUNCH();
+  const int64_t n4 = rows * E / 4;
+  attn_dq_finish_kernel<<<(unsigned)std::min<int64_t>((n4 + 255) / 256, 148 * 16), 256, 0, s>>>(dq_acc, dqkv, rows, E,
+                                                                                                 scale);
+  DLVK_POST_LAUNCH();
+}
+
+}  // namespace dlvk

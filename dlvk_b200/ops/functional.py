@@ -270,14 +270,14 @@ class AttentionFn(torch.autograd.Function):
     def forward(ctx, qkv, B, S, H, D, scale):
         out, probs = NN.attention_fwd(qkv.contiguous(), B, S, H, D, scale)
         ctx.dims = (B, S, H, D, scale)
-        ctx.save_for_backward(qkv, probs)
+        ctx.save_for_backward(qkv, probs, out)
         return out
 
     @staticmethod
     def backward(ctx, gout):
-        qkv, probs = ctx.saved_tensors
+        qkv, probs, out = ctx.saved_tensors
         B, S, H, D, scale = ctx.dims
-        dqkv = NN.attention_bwd(qkv, probs, gout.contiguous().to(qkv.dtype), B, S, H, D, scale)
+        dqkv = NN.attention_bwd(qkv, probs, gout.contiguous().to(qkv.dtype), B, S, H, D, scale, out=out)
         return dqkv, None, None, None, None, None
 
 
@@ -376,7 +376,7 @@ class TransformerBlockFn(torch.autograd.Function):
         # attention: h = a Wo + x
         wgrad(at.w_o, a2.t(), dh)
         da = K.gemm(dh, at.w_o.value.t())
-        dqkv = NN.attention_bwd(qkv.reshape(B, S, -1), probs, da.reshape(B, S, -1), B, S, H, D, scale)
+        dqkv = NN.attention_bwd(qkv.reshape(B, S, -1), probs, da.reshape(B, S, -1), B, S, H, D, scale, out=a2)
         dqkv2 = _flat2(dqkv)
         wgrad(at.w_qkv, h1.t(), dqkv2)
         dh1 = K.gemm(dqkv2, at.w_qkv.value.t())

@@ -212,10 +212,23 @@ def embedding_bwd(ids, dy, dtable):
 
 
 # ---------------------------------------------------------------- attention
+def flash_ok(qkv, B: int, S: int, H: int, D: int) -> bool:
+    """The fused tcgen05 attention kernels apply: bf16, head dim 64, S a
+    multiple of 128 (DLVK_FLASH_ATTN=0 disables them)."""
+    import os
+
+    return (native(qkv) and qkv.dtype == torch.bfloat16 and os.environ.get("DLVK_FLASH_ATTN", "1") != "0"
+            and N().flash_attn_supported(B, S, H, D, qkv))
+
+
 def attention_fwd(qkv, B: int, S: int, H: int, D: int, scale: float):
     """Multi-head attention over a fused QKV buffer [B, S, 3, H, D] (the QKV
-    GEMM's natural output).  Returns (out [B, S, H*D], probs [B, H, S, S])."""
+    GEMM's natural output).  Returns (out [B, S, H*D], aux) where aux is the
+    per-row log-sum-exp [B, H, S] (fp32, log2 units) on the fused tensor-core
+    path, or the probabilities [B, H, S, S] on the GEMM + softmax path."""
     E = H * D
+    if flash_ok(qkv, B, S, H, D):
+        return N().flash_attn_fwd(qkv.contiguous(), B, S, H, scale)
     if native(qkv):
         base = qkv.reshape(-1)
         o0 = base.storage_offset()
@@ -236,9 +249,16 @@ def attention_fwd(qkv, B: int, S: int, H: int, D: int, scale: float):
     return o.transpose(1, 2).reshape(B, S, E).to(qkv.dtype), probs
 
 
-def attention_bwd(qkv, probs, dout, B: int, S: int, H: int, D: int, scale: float):
-    """Gradient of attention_fwd w.r.t. the fused QKV buffer: [B, S, 3*H*D]."""
+def attention_bwd(qkv, probs, dout, B: int, S: int, H: int, D: int, scale: float, out=None):
+    """Gradient of attention_fwd w.r.t. the fused QKV buffer: [B, S, 3*H*D].
+    `probs` is attention_fwd's aux output; the fused path (aux = lse) also
+    needs the forward output `out`."""
     E = H * D
+    if probs.dim() == 3 and probs.dtype == torch.float32 and native(qkv):
+        if out is None:
+            raise ValueError("attention_bwd on the fused path needs the forward output")
+        return N().flash_attn_bwd(qkv.contiguous(), out.reshape(B, S, E).contiguous(),
+                                  dout.reshape(B, S, E).contiguous(), probs, B, S, H, scale)
     if native(qkv):
         base = qkv.reshape(-1)
         o0 = base.storage_offset()
