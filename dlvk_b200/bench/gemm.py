@@ -42,6 +42,8 @@ def main():
     ap.add_argument("--relu", action="store_true", help="ReLU in the epilogue")
     ap.add_argument("--residual", action="store_true", help="residual add in the epilogue")
     ap.add_argument("--mask", action="store_true", help="ReLU-mask input in the epilogue")
+    ap.add_argument("--compare-single", action="store_true",
+                    help="also time the single-CTA kernel (CTA-pair variant switched off)")
     args = ap.parse_args()
     C = _ext.C()
     shapes = DEFAULT
@@ -67,6 +69,13 @@ def main():
         t_ours = time_fn(lambda: C.gemm(a, b, out=out, force_path=1, **kw), iters=args.iters)
         rec = {"M": M, "N": N, "K": K, "a": am, "b": bm, "epilogue": sorted(kw), "ours_ms": round(t_ours, 4),
                "ours_tflops": round(flops / t_ours / 1e9, 1), "ours_frac_of_measured": round(flops / t_ours / 1e9 / peak, 3)}
+        if args.compare_single:
+            C.gemm_set_pair(False)
+            try:
+                t_1 = time_fn(lambda: C.gemm(a, b, out=out, force_path=1, **kw), iters=args.iters)
+            finally:
+                C.gemm_set_pair(True)
+            rec.update({"single_cta_ms": round(t_1, 4), "single_cta_tflops": round(flops / t_1 / 1e9, 1)})
         if not args.no_cublas:
             t_cb = time_fn(lambda: torch.matmul(a, b, out=out), iters=args.iters)
             rec.update({"cublas_ms": round(t_cb, 4), "cublas_tflops": round(flops / t_cb / 1e9, 1),

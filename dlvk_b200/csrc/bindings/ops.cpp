@@ -419,6 +419,8 @@ void register_ops(py::module& m) {
   m.def("optim_update", &optim_update_op, py::arg("kind"), py::arg("hyper"), py::arg("p"), py::arg("grad"),
         py::arg("m") = py::none(), py::arg("v") = py::none(), py::arg("p_bf16") = py::none(),
         py::arg("extra_scale") = 1.0);
+  m.def("gemm_set_pair", [](bool on) { gemm_tc_set_pair(on); });
+  m.def("gemm_pair_enabled", []() { return gemm_tc_pair_enabled(); });
   m.def("grad_stats", &grad_stats_op, py::arg("g"), py::arg("scale"), py::arg("max_norm"), py::arg("sumsq"),
         py::arg("flag"), py::arg("clip"), py::arg("accumulate"), py::arg("scratch"), py::arg("scale_dev") = py::none());
   m.def("step_metrics", [](const at::Tensor& logits, c10::optional<at::Tensor> labels, c10::optional<at::Tensor> probs,

@@ -81,6 +81,10 @@ bool gemm_tc_supported(const GemmArgs& a);
 // reduce kernel applies the epilogue.  With a null/small workspace the GEMM
 // runs unsplit.
 int64_t gemm_tc_workspace_floats(const GemmArgs& a, int max_ctas = 0);
+// CTA-pair (tcgen05 cta_group::2, 256 x 256 tiles) variant for unsplit bf16
+// GEMMs with M >= 256; on by default (DLVK_GEMM_PAIR=0 turns it off).
+bool gemm_tc_pair_enabled();
+void gemm_tc_set_pair(bool on);
 void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int max_ctas = 0,
              float* workspace = nullptr, int64_t workspace_floats = 0);
 

@@ -20,6 +20,7 @@
 //  * every mbarrier wait is bounded (2 s) and reports through `err`.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
@@ -62,12 +63,14 @@ struct TcParams {
   const float* col_scale;
 };
 
-template <int BN>
+// PAIR: a 2-CTA cluster shares one 256 x BN tile (tcgen05 cta_group::2);
+// each CTA stages its 128 rows of A and its BN/2 columns of B.
+template <int BN, bool PAIR = false>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int STAGES = PAIR ? 6 : ((BN == 256) ? 4 : 6);
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int EPI_BYTES = 8 * 32 * 33 * 4;  // per-warp 32x33 fp32 staging
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + EPI_BYTES;
@@ -251,10 +254,10 @@ __device__ __forceinline__ void epi_store(const TcParams& p, const float* stg, i
   }
 }
 
-template <int BN>
+template <int BN, bool PAIR = false>
 __global__ void __launch_bounds__(320, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, TcParams p) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, PAIR>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
@@ -269,6 +272,12 @@ __global__ void __launch_bounds__(320, 1)
   const int num_tiles = tiles_per_split * p.splits;  // work units
   const int bke = p.i8 ? 2 * BK : BK;  // elements per 128-byte k-block
   const int num_kb = (p.K + bke - 1) / bke;
+  // With PAIR the two CTAs of a cluster walk the same tiles; `rank` selects
+  // the 128-row half of A / the BN/2-column half of B this CTA stages.
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int t0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int tstep = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  constexpr int TILE_M = PAIR ? 2 * BM : BM;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -277,7 +286,9 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 256);
+      // PAIR: one arrival per epilogue warp of both CTAs (the leader's barrier
+      // is the one the MMA warp waits on); otherwise one per epilogue thread.
+      mbar_init(&tempty[i], PAIR ? 16 : 256);
     }
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -285,16 +296,57 @@ __global__ void __launch_bounds__(320, 1)
     prefetch_tmap(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync();  // the peer's barriers are initialised before any remote signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {
+    if (lane == 0 && PAIR) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = t0; t < num_tiles; t += tstep) {
+        int tm, tn, b;
+        tile_coords(t, p, tm, tn, b);
+        const int bo = b / p.batch2, bi = b - bo * p.batch2;
+        const int arow = tm * TILE_M + (int)rank * BM;
+        const int bcol = tn * BN + (int)rank * (BN / 2);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.err)) goto producer_done_pair;
+          uint8_t* sA = smem + stage * C::STAGE_BYTES;
+          uint8_t* sB = sA + C::A_BYTES;
+          const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);  // the leader's full barrier
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+          if (!p.a_mn) {
+            tma_load_4d_pair(sA, &tmA, fb, kb * BK, arow, bi, bo);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_4d_pair(sA + j * 8192, &tmA, fb, arow + j * 64, kb * BK, bi, bo);
+          }
+          if (!p.b_mn) {
+            tma_load_4d_pair(sB, &tmB, fb, kb * BK, bcol, bi, bo);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j)
+              tma_load_4d_pair(sB + j * 8192, &tmB, fb, bcol + j * 64, kb * BK, bi, bo);
+          }
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    producer_done_pair:;
+    } else if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
@@ -331,7 +383,52 @@ __global__ void __launch_bounds__(320, 1)
     producer_done:;
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && PAIR) {
+      if (rank == 0) {
+        // M = 256 across the pair; B descriptors describe this CTA's BN/2
+        // columns (the peer's half sits at the same offsets in its smem).
+        const uint32_t idesc = make_idesc(1, 1, 1, p.a_mn != 0, p.b_mn != 0, 2 * BM, BN);
+        int stage = 0;
+        uint32_t phase = 0;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int t = t0; t < num_tiles; t += tstep) {
+          if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.err)) break;
+          tc_fence_after();
+          const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+          bool ok = true;
+          for (int kb = 0; kb < num_kb; ++kb) {
+            if (!mbar_wait(&full[stage], phase, p.err)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t aBase = smem_u32(smem + stage * C::STAGE_BYTES);
+            const uint32_t bBase = aBase + C::A_BYTES;
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) {
+              const uint64_t ad = p.a_mn ? make_sw128_desc(aBase + k * 2048, 8192, 1024)
+                                         : make_sw128_desc(aBase + k * 32, 16, 1024);
+              const uint64_t bd = p.b_mn ? make_sw128_desc(bBase + k * 2048, 8192, 1024)
+                                         : make_sw128_desc(bBase + k * 32, 16, 1024);
+              mma_f16_pair(d, ad, bd, idesc, (kb != 0 || k != 0) ? 1u : 0u);
+            }
+            const uint32_t eb = smem_u32(&empty[stage]);
+            mma_commit_pair(eb);
+            mma_commit_pair(mapa_shared(eb, 1));
+            if (++stage == C::STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+          if (!ok) break;
+          const uint32_t fb = smem_u32(&tfull[acc]);
+          mma_commit_pair(fb);
+          mma_commit_pair(mapa_shared(fb, 1));
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1u;
+          }
+        }
+      }
+    } else if (lane == 0) {
       const uint32_t idesc = p.i8 ? make_idesc(2, 1, 1, false, false, BM, BN)
                                   : make_idesc(1, 1, 1, p.a_mn != 0, p.b_mn != 0, BM, BN);
       int stage = 0;
@@ -388,7 +485,7 @@ __global__ void __launch_bounds__(320, 1)
     constexpr int NCH = BN / 64;  // 32-column chunks per warp
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+    for (int t = t0; t < num_tiles; t += tstep) {
       int tm, tn, b;
       const int sp = t / tiles_per_split;
       tile_coords(t - sp * tiles_per_split, p, tm, tn, b);
@@ -398,7 +495,7 @@ __global__ void __launch_bounds__(320, 1)
       const int64_t cb = (int64_t)sp * p.split_stride + (int64_t)bo * p.bsc + (int64_t)bi * p.bsc2;
       const int64_t rb = (int64_t)bo * p.bsr + (int64_t)bi * p.bsr2;
       const int64_t mb = (int64_t)bo * p.bsm + (int64_t)bi * p.bsm2;
-      const int row0 = tm * BM + q * 32;
+      const int row0 = tm * TILE_M + (int)rank * BM + q * 32;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + half * NCH * 32);
       uint32_t r[2][32];
       tmem_ld32(tbase, r[0]);
@@ -470,7 +567,12 @@ __global__ void __launch_bounds__(320, 1)
         if (i + 1 < NCH) tmem_ld_wait();
       }
       tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      if (PAIR) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+      } else {
+        mbar_arrive(&tempty[acc]);
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
@@ -479,9 +581,11 @@ __global__ void __launch_bounds__(320, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync();  // no CTA leaves while its peer may still signal its barriers
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if (PAIR) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+    else tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
 }
 
@@ -541,6 +645,40 @@ void launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, 
   const int tiles = p.tiles_m * p.tiles_n * p.batch * p.splits;
   int grid = std::min(tiles, max_ctas > 0 ? max_ctas : sm_count());
   gemm_tc_kernel<BN><<<grid, 320, C::SMEM, s>>>(ta, tb, p);
+  DLVK_POST_LAUNCH();
+}
+
+// 2-CTA clusters sharing 256 x 256 tiles (cta_group::2).  The persistent
+// grid is as many pairs as can be resident at once.
+void launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, int max_ctas, cudaStream_t s) {
+  using C = Cfg<256, true>;
+  static int max_pairs[64] = {0};
+  int dev = 0;
+  DLVK_CUDA_CHECK(cudaGetDevice(&dev));
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(320, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (max_pairs[dev] == 0) {
+    DLVK_CUDA_CHECK(
+        cudaFuncSetAttribute(gemm_tc_kernel<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    cfg.gridDim = dim3(2 * 74, 1, 1);
+    int n = 0;
+    DLVK_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<256, true>, &cfg));
+    max_pairs[dev] = std::max(1, n);
+  }
+  const int tiles = p.tiles_m * p.tiles_n * p.batch;
+  int pairs = std::min(tiles, max_pairs[dev]);
+  if (max_ctas > 0) pairs = std::max(1, std::min(pairs, max_ctas / 2));
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  DLVK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<256, true>, ta, tb, p));
   DLVK_POST_LAUNCH();
 }
 
@@ -648,6 +786,9 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
   int BN = 256, splits = 1;
   choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits);
   if (workspace == nullptr || workspace_floats < (int64_t)splits * a.M * a.N * a.batch * a.batch2) splits = 1;
+  // The CTA-pair kernel (256 x 256 tiles, half the B traffic per CTA) takes
+  // every bf16 GEMM the single-CTA model would run unsplit with 256-wide tiles.
+  const bool pair = gemm_tc_pair_enabled() && splits == 1 && BN == 256 && a.M >= 256 && max_ctas != 1;
   // Unused batch levels get a harmless stride (a multiple of 16 bytes).
   auto pick = [](int64_t cnt, int64_t stride, uint64_t dflt) { return cnt > 1 ? (uint64_t)stride : dflt; };
   CUtensorMap ta, tb;
@@ -663,7 +804,7 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
   if (b_k) {
     const uint64_t d = (uint64_t)a.sbn * (uint64_t)a.N;
     tb = make_tmap(a.B, a.K, a.N, a.batch2, a.batch, a.sbn, pick(a.batch2, a.batch2_stride_b, d),
-                        pick(a.batch, a.batch_stride_b, d), BN, false);
+                        pick(a.batch, a.batch_stride_b, d), pair ? BN / 2 : BN, false);
   } else {
     const uint64_t d = (uint64_t)a.sbk * (uint64_t)a.K;
     tb = make_tmap(a.B, a.N, a.K, a.batch2, a.batch, a.sbk, pick(a.batch2, a.batch2_stride_b, d),
@@ -675,7 +816,7 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
   p.K = (int)a.K;
   p.batch = (int)(a.batch * a.batch2);
   p.batch2 = (int)a.batch2;
-  p.tiles_m = (int)((a.M + BM - 1) / BM);
+  p.tiles_m = (int)((a.M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM));
   p.tiles_n = (int)((a.N + BN - 1) / BN);
   p.a_mn = a_k ? 0 : 1;
   p.b_mn = b_k ? 0 : 1;
@@ -733,9 +874,23 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
     DLVK_POST_LAUNCH();
     return;
   }
-  if (BN == 256) launch_tc<256>(ta, tb, p, max_ctas, s);
+  if (pair) launch_tc_pair(ta, tb, p, max_ctas, s);
+  else if (BN == 256) launch_tc<256>(ta, tb, p, max_ctas, s);
   else launch_tc<128>(ta, tb, p, max_ctas, s);
 }
+
+namespace {
+int& pair_flag() {
+  static int f = [] {
+    const char* e = std::getenv("DLVK_GEMM_PAIR");
+    return (e && e[0] == '0') ? 0 : 1;
+  }();
+  return f;
+}
+}  // namespace
+
+bool gemm_tc_pair_enabled() { return pair_flag() != 0; }
+void gemm_tc_set_pair(bool on) { pair_flag() = on ? 1 : 0; }
 
 int64_t gemm_tc_workspace_floats(const GemmArgs& a, int max_ctas) {
   int BN = 256, splits = 1;

@@ -142,3 +142,48 @@ def test_gemm_tc_epilogue_variants(epi):
         ref = torch.where(kw["relu_mask"].float() > 0, ref, torch.zeros_like(ref))
     out = C.gemm(a, b, force_path=1, **kw)
     _check(out, ref, 2e-2)
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (512, 768, 320), (1000, 520, 1024), (4096, 4096, 512)])
+@pytest.mark.parametrize("a_t", [False, True])
+@pytest.mark.parametrize("b_t", [False, True])
+@pytest.mark.parametrize("epi", ["none", "bias_relu", "residual"])
+def test_gemm_tc_pair_matches_single(M, N, K, a_t, b_t, epi):
+    """The CTA-pair (cta_group::2) kernel against the single-CTA kernel and
+    the fp32 reference."""
+    C = _C()
+    torch.manual_seed(3)
+    a = torch.randn(M, K, device="cuda").bfloat16()
+    b = torch.randn(K, N, device="cuda").bfloat16()
+    A = a.t().contiguous().t() if a_t else a
+    B = b.t().contiguous().t() if b_t else b
+    kw = {}
+    ref = a.float() @ b.float()
+    if epi == "bias_relu":
+        kw = dict(bias=torch.randn(N, device="cuda"), act=1)
+        ref = torch.relu(ref + kw["bias"])
+    elif epi == "residual":
+        kw = dict(residual=torch.randn(M, N, device="cuda").bfloat16())
+        ref = ref + kw["residual"].float()
+    outs = []
+    for on in (True, False):
+        C.gemm_set_pair(on)
+        try:
+            outs.append(C.gemm(A, B, force_path=1, **kw))
+        finally:
+            C.gemm_set_pair(True)
+    torch.cuda.synchronize()
+    assert C.read_device_error(True) == 0
+    _check(outs[0], ref, 2e-2)
+    _check(outs[1], ref, 2e-2)
+    assert (outs[0].float() - outs[1].float()).abs().max().item() <= 2e-2 * (ref.abs().max().item() + 1e-6)
+
+
+def test_gemm_tc_pair_persistent_one_pair():
+    C = _C()
+    a = torch.randn(4096, 512, device="cuda").bfloat16()
+    b = torch.randn(512, 2048, device="cuda").bfloat16()
+    out = C.gemm(a, b, force_path=1, max_ctas=2)  # one CTA pair walks all 128 tiles
+    torch.cuda.synchronize()
+    assert C.read_device_error(True) == 0
+    _check(out, _ref(a, b), 2e-2)
