@@ -52,12 +52,18 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="transformer",
                     choices=["transformer", "wide_mlp", "cnn", "cnn_bf16", "mlp"])
+    ap.add_argument("--config-file", default=None,
+                    help="JSON workload file (dlvk_b200/bench/configs/*.json); its 'config' selects the workload")
     ap.add_argument("--impl", default="ours", choices=["ours", "torch", "reference"])
     ap.add_argument("--no-graph", action="store_true", help="eager step instead of a captured CUDA graph")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--allreduce", default="fused", choices=["fused", "nccl"],
                     help="gradient path for N > 1 (ours): fused P2P all-reduce+optimizer or NCCL baseline")
-    return ap.parse_args()
+    a = ap.parse_args()
+    if a.config_file:
+        with open(a.config_file) as f:
+            a.config = json.load(f)["config"]
+    return a
 
 
 # ---------------------------------------------------------------------------- clocks

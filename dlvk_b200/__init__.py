@@ -25,3 +25,18 @@ from .losses import LossFunction, CrossEntropyLoss, MeanSquaredError, BinaryCros
 # The reference spells the device class VulkanDevice; this framework's device
 # runtime is CUDA.
 VulkanDevice = CudaDevice
+
+from .models.layers import (RNNLayer, LSTMLayer, GRULayer, BidirectionalRNN, BiLSTM, BiGRU, BiRNN)
+from .models.builder import model_from_architecture, load_model_file
+from .training import (TrainStep, ModelTrainer, Trainer, create_trainer, TrainingMetrics, TrainingCallback,
+                       ProgressCallback, ModelCheckpoint, EarlyStopping, EarlyStoppingCallback, ReduceLROnPlateau,
+                       CSVLogger, PrecisionMode, GradientScaler, MixedPrecisionContext, AutocastContext,
+                       MixedPrecisionTrainer, RegularizationManager, L1Regularizer, L2Regularizer,
+                       ElasticNetRegularizer, WeightDecayRegularizer, AdvancedDropout, AdvancedTrainer,
+                       AdvancedTrainingConfig, create_advanced_trainer, ModelSerializer, ModelVersioning,
+                       CheckpointManager)
+from . import data, export, deployment, optimization, training, parallel
+from .data import DataLoader, MnistDataset, Dataset, TransformDataset
+from .export import ModelExportManager, ModelFormat
+from .optimization.model_optimizer import ModelOptimizer, QuantizationConfig, PruningConfig
+from .deployment import ModelInferenceEngine, ModelServingServer, MultiGPUTrainer, MultiGPUDeviceManager

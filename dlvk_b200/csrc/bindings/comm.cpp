@@ -105,6 +105,14 @@ void register_comm(py::module& m) {
            py::arg("dtype_code"), py::arg("numel"), py::arg("byte_offset") = 0);
   c.def("fused_allreduce_optimizer", &fused_ar_op);
   c.def("p2p_allreduce", &p2p_allreduce_op);
+  c.def("wait_flag_probe", [](const at::Tensor& flag, int64_t epoch, double budget_s) {
+    TORCH_CHECK(flag.is_cuda() && flag.scalar_type() == at::kInt && flag.numel() >= 1, "wait_flag_probe: int32 flag");
+    c10::cuda::CUDAGuard g(flag.device());
+    auto res = at::zeros({1}, flag.options());
+    wait_flag_probe(reinterpret_cast<const uint32_t*>(flag.data_ptr<int>()), (uint32_t)epoch,
+                    (uint64_t)(budget_s * 1e9), device_error_word(), res.data_ptr<int>(), stream());
+    return res;
+  });
   c.def("can_access_peer", [](int a, int b) {
     int ok = 0;
     DLVK_CUDA_CHECK(cudaDeviceCanAccessPeer(&ok, a, b));

@@ -67,4 +67,10 @@ class SymmetricBuffer {
   void** dev_ptrs_ = nullptr;
 };
 
+// Failure-detection probe: waits (bounded by budget_ns) for *flag == epoch
+// with the all-reduce kernels' wait; result[0] = 1 if seen, 0 on timeout
+// (the timeout is also recorded in `err` as DLVK_ERR_PEER_TIMEOUT).
+void wait_flag_probe(const uint32_t* flag, uint32_t epoch, uint64_t budget_ns, uint32_t* err, int* result,
+                     cudaStream_t s);
+
 }  // namespace dlvk

@@ -335,4 +335,20 @@ void p2p_allreduce(const FusedARArgs& a, DType dt, bool average, int ctas, cudaS
   DLVK_POST_LAUNCH();
 }
 
+namespace {
+// One block waiting on `flag` for `epoch` through the same bounded wait the
+// all-reduce kernels use; result[0] = 1 on success, 0 on timeout.
+__global__ void wait_flag_probe_kernel(const uint32_t* flag, uint32_t epoch, uint64_t budget_ns, uint32_t* err,
+                                       int* result) {
+  const bool ok = wait_flag(flag, epoch, budget_ns, err);
+  if (threadIdx.x == 0) result[0] = ok ? 1 : 0;
+}
+}  // namespace
+
+void wait_flag_probe(const uint32_t* flag, uint32_t epoch, uint64_t budget_ns, uint32_t* err, int* result,
+                     cudaStream_t s) {
+  wait_flag_probe_kernel<<<1, 32, 0, s>>>(flag, epoch, budget_ns, err, result);
+  DLVK_POST_LAUNCH();
+}
+
 }  // namespace dlvk

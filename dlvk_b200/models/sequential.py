@@ -252,10 +252,16 @@ class Sequential(Model):
         if self._plan is None:
             self._plan = self._make_plan()
         consumed = 0
+        from ..utils.profiling import NVTX_LAYERS, nvtx_range
+
         for fn, n in self._plan:
             if upto is not None and consumed + n > upto:
                 break
-            x = fn(x)
+            if NVTX_LAYERS:
+                with nvtx_range("+".join(l.type_name for l in self.m_layers[consumed:consumed + n])):
+                    x = fn(x)
+            else:
+                x = fn(x)
             for layer in self.m_layers[consumed:consumed + n]:
                 layer.output_shape = tuple(x.shape)
             consumed += n

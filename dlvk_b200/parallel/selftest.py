@@ -29,6 +29,10 @@ def main() -> int:
     ap.add_argument("--bucket-mb", type=float, default=0.05)
     ap.add_argument("--one-shot-bytes", type=int, default=None)
     ap.add_argument("--cpu", action="store_true")
+    ap.add_argument("--fail-rank", type=int, default=-1,
+                    help="fault injection on the host: this rank exits between steps")
+    ap.add_argument("--fail-step", type=int, default=1)
+    ap.add_argument("--pg-timeout", type=float, default=60.0)
     ap.add_argument("--tol", type=float, default=None)
     ap.add_argument("--opt", default="adam", choices=["adam", "sgd"],
                     help="sgd keeps bf16 rounding differences linear; Adam maps near-zero "
@@ -44,11 +48,11 @@ def main() -> int:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.cpu:
-        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=args.pg_timeout))
         device = "cpu"
     else:
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=args.pg_timeout),
                                 device_id=torch.device("cuda", local))
         device = f"cuda:{local}"
     if args.one_shot_bytes is not None:
@@ -82,8 +86,17 @@ def main() -> int:
     dp = DataParallel(model, opt, mode=args.mode, bucket_mb=args.bucket_mb)
     step = TrainStep(model, dl.CrossEntropyLoss(), opt, dp=dp, graph=False)
     xs, ys = X[rank * per:(rank + 1) * per].contiguous(), Y[rank * per:(rank + 1) * per].contiguous()
-    for _ in range(args.steps):
-        loss = step(xs, ys)
+    for it in range(args.steps):
+        if rank == args.fail_rank and it == args.fail_step:
+            # leaves between steps: nothing of this rank is in flight
+            print(json.dumps({"rank": rank, "injected_exit": it}), flush=True)
+            os._exit(3)
+        try:
+            loss = step(xs, ys)
+        except Exception as e:  # a peer left: the collective fails instead of hanging
+            print(json.dumps({"rank": rank, "peer_failure_detected": True, "step": it,
+                              "error": type(e).__name__}), flush=True)
+            os._exit(4)
     dp.consolidate()
     if not args.cpu:
         torch.cuda.synchronize()
