@@ -355,7 +355,10 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-__global__ void __launch_bounds__(192, 1) flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv,
+constexpr int BWD_COMPUTE_WARPS = 8;  // two per TMEM lane quarter
+constexpr int BWD_THREADS = 64 + 32 * BWD_COMPUTE_WARPS;
+
+__global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv,
                                                            const __grid_constant__ CUtensorMap tm_do,
                                                            const __grid_constant__ CUtensorMap tm_dq, BwdP p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -379,7 +382,7 @@ __global__ void __launch_bounds__(192, 1) flash_bwd_kernel(const __grid_constant
   uint64_t* dq_free = bars + 9;
   uint64_t* kv_done = bars + 10;   // dK, dV accumulated for the item
   uint64_t* kv_read = bars + 11;   // dK, dV read out of TMEM
-  uint64_t* cw_bar = bars + 12;    // compute-warp group barrier (128 arrivals)
+  uint64_t* cw_bar = bars + 12;    // compute-warp group barrier (one arrival per compute thread)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -394,12 +397,12 @@ __global__ void __launch_bounds__(192, 1) flash_bwd_kernel(const __grid_constant
       mbar_init(&qd_empty[i], 1);
     }
     mbar_init(st_full, 1);
-    mbar_init(ds_full, 4);
+    mbar_init(ds_full, BWD_COMPUTE_WARPS);
     mbar_init(dq_full, 1);
-    mbar_init(dq_free, 4);
+    mbar_init(dq_free, BWD_COMPUTE_WARPS);
     mbar_init(kv_done, 1);
-    mbar_init(kv_read, 4);
-    mbar_init(cw_bar, 128);
+    mbar_init(kv_read, BWD_COMPUTE_WARPS);
+    mbar_init(cw_bar, 32 * BWD_COMPUTE_WARPS);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -492,19 +495,32 @@ __global__ void __launch_bounds__(192, 1) flash_bwd_kernel(const __grid_constant
       }
     }
   } else {
+    // Compute warps 2..9: warp w reads TMEM lanes 32*(w%4).. (row = key for
+    // S^T, dP^T, dK, dV; query for dQ); `hf` selects which half of the
+    // columns (queries of S^T / dP^T, dQ columns, dV vs dK) it handles.
     const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;  // key row (S^T, dP^T, dK, dV) or query row (dQ)
-    const int tid = threadIdx.x - 64;     // 0..127
+    const int hf = (warp - 2) >> 2;
+    const int row = quarter * 32 + lane;
+    const int tid = threadIdx.x - 64;     // 0..255
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     uint32_t stph = 0, dqph = 0, cwph = 0;
     int it = 0, ib = 0;
     bool ok = true;
+    // Each thread carries one lse (tid < 128) or delta (tid >= 128) value of
+    // the next query tile, loaded one iteration ahead.
+    auto fetch = [&](int item_, int i_) -> float {
+      if (item_ >= items) return 0.f;
+      const int bh_ = item_ / nt, h_ = bh_ % p.H, b_ = bh_ / p.H;
+      const int64_t base = ((int64_t)b_ * p.H + h_) * p.S + (int64_t)i_ * FT + (tid & 127);
+      return tid < 128 ? p.lse[base] : p.delta[base];
+    };
+    float cur = fetch(blockIdx.x, 0);
     for (int item = blockIdx.x; item < items && ok; item += gridDim.x, ++it) {
       const int kt = item % nt, bh = item / nt, h = bh % p.H, b = bh / p.H;
-      const int64_t lbase = ((int64_t)b * p.H + h) * p.S;
       for (int i = 0; i < nt; ++i, ib ^= 1) {
-        sLse[ib * 128 + tid] = p.lse[lbase + i * FT + tid];
-        sDel[ib * 128 + tid] = p.delta[lbase + i * FT + tid];
+        const float nxt = (i + 1 < nt) ? fetch(item, i + 1) : fetch(item + gridDim.x, 0);
+        (tid < 128 ? sLse : sDel)[ib * 128 + (tid & 127)] = cur;
+        cur = nxt;
         if (!group_sync(cw_bar, cwph, p.err)) { ok = false; break; }
         if (!warp_wait(st_full, stph, p.err)) { ok = false; break; }
         stph ^= 1u;
@@ -512,7 +528,8 @@ __global__ void __launch_bounds__(192, 1) flash_bwd_kernel(const __grid_constant
         const float* L = sLse + ib * 128;
         const float* Dl = sDel + ib * 128;
 #pragma unroll 1
-        for (int cb = 0; cb < 4; ++cb) {  // 32 query columns at a time
+        for (int cq = 0; cq < 2; ++cq) {  // 32 query columns at a time, this warp's half
+          const int cb = hf * 2 + cq;
           uint32_t s[32], dp[32];
           tmem_ld32(tbase + lane_off + (uint32_t)(cb * 32), s);
           tmem_ld32(tbase + lane_off + 128u + (uint32_t)(cb * 32), dp);
@@ -527,37 +544,35 @@ __global__ void __launch_bounds__(192, 1) flash_bwd_kernel(const __grid_constant
               ds[i8] = pt[i8] * (__uint_as_float(dp[q4 * 8 + i8]) - Dl[qi]);
             }
             const int ch = cb * 4 + q4;
-            uint4 a, d;
-            a.x = pack2(pt[0], pt[1]); a.y = pack2(pt[2], pt[3]); a.z = pack2(pt[4], pt[5]); a.w = pack2(pt[6], pt[7]);
-            d.x = pack2(ds[0], ds[1]); d.y = pack2(ds[2], ds[3]); d.z = pack2(ds[4], ds[5]); d.w = pack2(ds[6], ds[7]);
-            *reinterpret_cast<uint4*>(sPT + sw_off(row, ch)) = a;
-            *reinterpret_cast<uint4*>(sDS + sw_off(row, ch)) = d;
+            uint4 a4, d4;
+            a4.x = pack2(pt[0], pt[1]); a4.y = pack2(pt[2], pt[3]); a4.z = pack2(pt[4], pt[5]); a4.w = pack2(pt[6], pt[7]);
+            d4.x = pack2(ds[0], ds[1]); d4.y = pack2(ds[2], ds[3]); d4.z = pack2(ds[4], ds[5]); d4.w = pack2(ds[6], ds[7]);
+            *reinterpret_cast<uint4*>(sPT + sw_off(row, ch)) = a4;
+            *reinterpret_cast<uint4*>(sDS + sw_off(row, ch)) = d4;
           }
         }
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(ds_full);
-        // dQ tile (row = query): TMEM -> swizzled fp32 staging -> TMA reduce-add.
+        // dQ tile (row = query): this warp's 32 columns -> swizzled fp32 staging
+        // sub-tile `hf` -> TMA reduce-add.
         if (!warp_wait(dq_full, dqph, p.err)) { ok = false; break; }
         dqph ^= 1u;
         tc_fence_after();
-        uint32_t q0[32], q1[32];
-        tmem_ld32(tbase + lane_off + 384u, q0);
-        tmem_ld32(tbase + lane_off + 416u, q1);
+        uint32_t qv[32];
+        tmem_ld32(tbase + lane_off + 384u + (uint32_t)(hf * 32), qv);
         tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(dq_free);
         if (tid == 0) bulk_wait_read0();  // the previous reduce has read the staging buffer
         if (!group_sync(cw_bar, cwph, p.err)) { ok = false; break; }
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const uint32_t* src = half ? q1 : q0;
-          uint8_t* base = sDQ + half * 16384 + (row >> 3) * 1024 + (row & 7) * 128;
+        {
+          uint8_t* base = sDQ + hf * 16384 + (row >> 3) * 1024 + (row & 7) * 128;
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
-            uint4 v = make_uint4(src[c * 4], src[c * 4 + 1], src[c * 4 + 2], src[c * 4 + 3]);
+            uint4 v = make_uint4(qv[c * 4], qv[c * 4 + 1], qv[c * 4 + 2], qv[c * 4 + 3]);
             *reinterpret_cast<uint4*>(base + ((c ^ (row & 7)) << 4)) = v;
           }
         }
@@ -571,26 +586,25 @@ __global__ void __launch_bounds__(192, 1) flash_bwd_kernel(const __grid_constant
         }
       }
       if (!ok) break;
-      // dK (scaled) and dV of this key tile -> the fused gradient buffer.
+      // dV (hf = 0) or dK (hf = 1, scaled) of this key tile -> the fused gradient buffer.
       if (!warp_wait(kv_done, it & 1, p.err)) break;
       tc_fence_after();
       const int64_t grow = (int64_t)b * p.S + (int64_t)kt * FT + row;
-#pragma unroll
-      for (int w2 = 0; w2 < 2; ++w2) {  // 0: dV (cols 256..), 1: dK (cols 320..)
+      {
         uint32_t a0[32], a1[32];
-        tmem_ld32(tbase + lane_off + 256u + (uint32_t)(w2 * 64), a0);
-        tmem_ld32(tbase + lane_off + 288u + (uint32_t)(w2 * 64), a1);
+        tmem_ld32(tbase + lane_off + 256u + (uint32_t)(hf * 64), a0);
+        tmem_ld32(tbase + lane_off + 288u + (uint32_t)(hf * 64), a1);
         tmem_ld_wait();
-        const float sc = w2 ? p.scale : 1.f;
-        uint4* dst = reinterpret_cast<uint4*>(p.dqkv + grow * 3 * p.E + (w2 ? p.E : 2 * p.E) + h * FD);
+        const float sc = hf ? p.scale : 1.f;
+        uint4* dst = reinterpret_cast<uint4*>(p.dqkv + grow * 3 * p.E + (hf ? p.E : 2 * p.E) + h * FD);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          const uint32_t* s = c < 4 ? &a0[c * 8] : &a1[(c - 4) * 8];
+          const uint32_t* sv = c < 4 ? &a0[c * 8] : &a1[(c - 4) * 8];
           uint4 v;
-          v.x = pack2(__uint_as_float(s[0]) * sc, __uint_as_float(s[1]) * sc);
-          v.y = pack2(__uint_as_float(s[2]) * sc, __uint_as_float(s[3]) * sc);
-          v.z = pack2(__uint_as_float(s[4]) * sc, __uint_as_float(s[5]) * sc);
-          v.w = pack2(__uint_as_float(s[6]) * sc, __uint_as_float(s[7]) * sc);
+          v.x = pack2(__uint_as_float(sv[0]) * sc, __uint_as_float(sv[1]) * sc);
+          v.y = pack2(__uint_as_float(sv[2]) * sc, __uint_as_float(sv[3]) * sc);
+          v.z = pack2(__uint_as_float(sv[4]) * sc, __uint_as_float(sv[5]) * sc);
+          v.w = pack2(__uint_as_float(sv[6]) * sc, __uint_as_float(sv[7]) * sc);
           dst[c] = v;
         }
       }
@@ -608,21 +622,37 @@ __global__ void __launch_bounds__(192, 1) flash_bwd_kernel(const __grid_constant
   }
 }
 
-// delta[b, h, q] = sum_d dO[b, q, h, d] * O[b, q, h, d]; one warp per (b, q, h).
+// delta[b, h, q] = sum_d dO[b, q, h, d] * O[b, q, h, d]; one thread per
+// (b, q, h) row of 64 with 16-byte loads (consecutive threads read
+// consecutive rows).
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
                                   float* __restrict__ delta, int B, int S, int H) {
-  const int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
   const int64_t total = (int64_t)B * S * H;
-  if (w >= total) return;
-  const int h = (int)(w % H);
-  const int64_t bq = w / H;
-  const int q = (int)(bq % S), b = (int)(bq / S);
-  const __nv_bfloat162* a = reinterpret_cast<const __nv_bfloat162*>(o + w * FD) + lane;
-  const __nv_bfloat162* d = reinterpret_cast<const __nv_bfloat162*>(dout + w * FD) + lane;
-  const float2 x = __bfloat1622float2(*a), y = __bfloat1622float2(*d);
-  const float v = warp_sum(x.x * y.x + x.y * y.y);
-  if (lane == 0) delta[((int64_t)b * H + h) * S + q] = v;
+  for (int64_t w = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; w < total; w += (int64_t)gridDim.x * blockDim.x) {
+    const uint4* a = reinterpret_cast<const uint4*>(o + w * FD);
+    const uint4* d = reinterpret_cast<const uint4*>(dout + w * FD);
+    uint4 av[8], dv[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      av[c] = a[c];
+      dv[c] = d[c];
+    }
+    float acc = 0.f;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const __nv_bfloat162* x = reinterpret_cast<const __nv_bfloat162*>(&av[c]);
+      const __nv_bfloat162* y = reinterpret_cast<const __nv_bfloat162*>(&dv[c]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 xf = __bfloat1622float2(x[k]), yf = __bfloat1622float2(y[k]);
+        acc = fmaf(xf.x, yf.x, fmaf(xf.y, yf.y, acc));
+      }
+    }
+    const int h = (int)(w % H);
+    const int64_t bq = w / H;
+    const int q = (int)(bq % S), b = (int)(bq / S);
+    delta[((int64_t)b * H + h) * S + q] = acc;
+  }
 }
 
 // dqkv[:, :, 0] = bf16(dq_acc * scale)
@@ -673,8 +703,9 @@ void flash_attention_bwd(const __nv_bfloat16* qkv, const __nv_bfloat16* out, con
   const int E = H * FD;
   const int64_t rows = (int64_t)B * S;
   {
-    const int64_t threads = rows * H * 32;
-    attn_delta_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(out, dout, delta, B, S, H);
+    const int64_t n = rows * H;
+    attn_delta_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 148 * 8), 256, 0, s>>>(out, dout, delta, B, S,
+                                                                                            H);
     DLVK_POST_LAUNCH();
   }
   DLVK_CUDA_CHECK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * E, s));
@@ -699,7 +730,7 @@ void flash_attention_bwd(const __nv_bfloat16* qkv, const __nv_bfloat16* out, con
   }
   const int items = B * H * (S / FT);
   const int grid = std::min(items, max_ctas > 0 ? max_ctas : tmap::sm_count());
-  flash_bwd_kernel<<<grid, 192, BWD_SMEM, s>>>(tq, td, tdq, p);
+  flash_bwd_kernel<<<grid, BWD_THREADS, BWD_SMEM, s>>>(tq, td, tdq, p);
   DLVK_POST_LAUNCH();
   const int64_t n4 = rows * E / 4;
   attn_dq_finish_kernel<<<(unsigned)std::min<int64_t>((n4 + 255) / 256, 148 * 16), 256, 0, s>>>(dq_acc, dqkv, rows, E,
