@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the Blackwell (sm_100a) primitives used by the
-// tensor-core kernels: mbarriers, TMA tiled loads (never multicast), TMEM
+// tensor-core kernels: mbarriers, plain single-destination TMA tiled loads, TMEM
 // allocation, tcgen05.mma / commit / ld and the UMMA shared-memory and
 // instruction descriptors.
 //
@@ -77,7 +77,7 @@ __device__ __forceinline__ bool device_error_set(const uint32_t* err) {
 }
 
 // TMA tiled loads (global -> this CTA's shared memory), completion counted on
-// `bar` in bytes.  Plain, non-multicast form only.
+// `bar` in bytes.  Plain single-destination form only.
 __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_t* bar, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
@@ -235,7 +235,7 @@ __device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t cluster_a
 }
 // TMA tiled load into this CTA's shared memory whose completion is counted
 // on an mbarrier that may live in the peer CTA of the pair (`bar_cluster`,
-// a shared::cluster address).  Plain, non-multicast form.
+// a shared::cluster address).  Plain single-destination form.
 __device__ __forceinline__ void tma_load_4d_pair(void* dst, const void* tmap, uint32_t bar_cluster, int x, int y, int z,
                                                  int w) {
   asm volatile(

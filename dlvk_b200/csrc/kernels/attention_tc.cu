@@ -537,11 +537,16 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4) {  // 8 queries per 16-byte chunk
             float pt[8], ds[8];
+            // per-query lse / delta: two 16-byte broadcast loads each
+            const float4* L4 = reinterpret_cast<const float4*>(L + cb * 32 + q4 * 8);
+            const float4* D4 = reinterpret_cast<const float4*>(Dl + cb * 32 + q4 * 8);
+            const float4 la = L4[0], lb = L4[1], da = D4[0], db = D4[1];
+            const float lv[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
+            const float dv[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
 #pragma unroll
             for (int i8 = 0; i8 < 8; ++i8) {
-              const int qi = cb * 32 + q4 * 8 + i8;
-              pt[i8] = exp2f(fmaf(__uint_as_float(s[q4 * 8 + i8]), p.c, -L[qi]));
-              ds[i8] = pt[i8] * (__uint_as_float(dp[q4 * 8 + i8]) - Dl[qi]);
+              pt[i8] = exp2f(fmaf(__uint_as_float(s[q4 * 8 + i8]), p.c, -lv[i8]));
+              ds[i8] = pt[i8] * (__uint_as_float(dp[q4 * 8 + i8]) - dv[i8]);
             }
             const int ch = cb * 4 + q4;
             uint4 a4, d4;

@@ -24,8 +24,8 @@
 //              for all peers' done flags, so no rank starts its next step
 //              while a peer still reads its gradients or writes its params.
 // Every wait is bounded by a wall-clock budget; on expiry the kernel records
-// DLVK_ERR_PEER_TIMEOUT in the error word and returns.  No TMA and no
-// cluster multicast is used on peer memory.
+// DLVK_ERR_PEER_TIMEOUT in the error word and returns.  Peer memory is only
+// read with plain per-thread loads (no TMA).
 #include "dlvk/common.h"
 #include "dlvk/kernels.h"
 #include "dlvk/optim_math.h"

@@ -16,7 +16,7 @@
 //    K-major ([N,K]) or N-major ([K,N]).  Both are expressed through the TMA
 //    box shape and the UMMA descriptor major-ness, so no transpose kernels are
 //    ever needed for X*W, dY*W^T or X^T*dY.
-//  * TMA loads are plain (no cluster multicast).
+//  * TMA loads are plain single-destination loads.
 //  * every mbarrier wait is bounded (2 s) and reports through `err`.
 #include <cuda.h>
 #include <cudaTypedefs.h>

@@ -230,6 +230,66 @@ __global__ void ln_fwd_kernel(const T* __restrict__ x, const float* __restrict__
   }
 }
 
+// Register-resident variant: one warp per row, D = 32 lanes x NV vectors of
+// 16 bytes; exact two-pass mean / variance from registers, 16-byte loads and
+// stores, gamma / beta as float4.
+template <typename T, int NV>
+__global__ void ln_fwd_vec_kernel(const T* __restrict__ x, const float* __restrict__ gamma,
+                                  const float* __restrict__ beta, T* __restrict__ y, float* __restrict__ mean,
+                                  float* __restrict__ rstd, int64_t rows, int D, float eps) {
+  constexpr int EPV = 16 / sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + r * D);
+    float v[NV][EPV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const uint4 u = xr[k * 32 + lane];
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int j = 0; j < EPV; ++j) v[k][j] = to_f32(e[j]);
+    }
+    float a = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+#pragma unroll
+      for (int j = 0; j < EPV; ++j) a += v[k][j];
+    const float mu = warp_sum(a) / D;
+    float b = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+#pragma unroll
+      for (int j = 0; j < EPV; ++j) {
+        const float d0 = v[k][j] - mu;
+        b += d0 * d0;
+      }
+    const float rs = rsqrtf(warp_sum(b) / D + eps);
+    uint4* yr = reinterpret_cast<uint4*>(y + r * D);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int d0 = (k * 32 + lane) * EPV;
+      float gv[EPV], bv[EPV];
+#pragma unroll
+      for (int j = 0; j < EPV; j += 4) {
+        const float4 g4 = gamma ? *reinterpret_cast<const float4*>(gamma + d0 + j) : make_float4(1.f, 1.f, 1.f, 1.f);
+        const float4 b4 = beta ? *reinterpret_cast<const float4*>(beta + d0 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+        gv[j] = g4.x; gv[j + 1] = g4.y; gv[j + 2] = g4.z; gv[j + 3] = g4.w;
+        bv[j] = b4.x; bv[j + 1] = b4.y; bv[j + 2] = b4.z; bv[j + 3] = b4.w;
+      }
+      uint4 u;
+      T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+      for (int j = 0; j < EPV; ++j) e[j] = from_f32<T>((v[k][j] - mu) * rs * gv[j] + bv[j]);
+      yr[k * 32 + lane] = u;
+    }
+    if (lane == 0) {
+      if (mean) mean[r] = mu;
+      if (rstd) rstd[r] = rs;
+    }
+  }
+}
+
 // dx per row (one warp per row, grid-stride over rows with a fixed grid);
 // each block accumulates dgamma/dbeta partials for its rows in shared memory
 // and writes them to part[block][2*D].  Fixed order => deterministic.
@@ -484,6 +544,20 @@ void batchnorm_bwd(DType dt, const void* x, const void* dy, const float* mean, c
 
 void layernorm_fwd(DType dt, const void* x, const float* gamma, const float* beta, void* y, float* mean, float* rstd,
                    int64_t rows, int D, float eps, cudaStream_t s) {
+  const int epv = dt == DType::F32 ? 4 : 8;
+  const int nv = (D % (32 * epv) == 0) ? D / (32 * epv) : 0;
+  const bool al = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
+                    reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) & 15) == 0;
+  if (al && (nv == 1 || nv == 2 || nv == 4 || nv == 8)) {
+    const unsigned g = (unsigned)std::max<int64_t>(1, std::min<int64_t>((rows + 7) / 8, 148 * 8));
+    DLVK_DISPATCH_FB(dt, "layernorm_fwd", {
+      auto kern = nv == 1 ? ln_fwd_vec_kernel<T, 1>
+                          : (nv == 2 ? ln_fwd_vec_kernel<T, 2> : (nv == 4 ? ln_fwd_vec_kernel<T, 4> : ln_fwd_vec_kernel<T, 8>));
+      kern<<<g, 256, 0, s>>>((const T*)x, gamma, beta, (T*)y, mean, rstd, rows, D, eps);
+    });
+    DLVK_POST_LAUNCH();
+    return;
+  }
   const unsigned g = (unsigned)((rows + 7) / 8);
   DLVK_DISPATCH_FB(dt, "layernorm_fwd", ln_fwd_kernel<T><<<g, 256, 0, s>>>((const T*)x, gamma, beta, (T*)y, mean, rstd,
                                                                             rows, D, eps));

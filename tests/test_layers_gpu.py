@@ -166,5 +166,5 @@ def test_attention(dtype):
     close(out, ref, tol)
     g = torch.randn(B, S, E, device="cuda")
     ref.backward(g)
-    dqkv = NN.attention_bwd(qkv, probs, g.to(dtype), B, S, H, D, scale)
+    dqkv = NN.attention_bwd(qkv, probs, g.to(dtype), B, S, H, D, scale, out=out)
     close(dqkv, x.grad.reshape(B, S, 3 * E), tol * 3)
