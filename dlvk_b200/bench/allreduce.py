@@ -4,12 +4,21 @@
         --master-port P -m dlvk_b200.bench.allreduce [--dtype fp32|bf16]
 
 For every bucket size (4 KB .. 1 GB of fp32 gradients) it times, on the
-device (CUDA events, max over ranks):
-  fused  this framework's one-kernel P2P all-reduce + Adam (comm.cu)
+device (CUDA events around a CUDA graph of --iters steps, max over ranks):
+  fused  this framework's one-kernel all-reduce + Adam (comm.cu), in the form
+         the optimizer picks (LL one-shot for small buckets, pull two-shot,
+         or push two-shot with --algo push); LL sizes also time the pull
+         one-shot form, and --pull-ctas times two-shot at other grid sizes
   nccl   NCCL all-reduce followed by this framework's Adam kernel
 and reports bus bandwidth (2 (N-1)/N * bytes / t, the all-reduce convention)
-and the fused kernel's fraction of its roofline: max(bytes over NVLink per
-direction / 770 GB/s, local HBM bytes / measured HBM bandwidth).
+and the fused kernel's fraction of its roofline, max(bytes over NVLink per
+direction / 770 GB/s, local HBM bytes / measured HBM bandwidth), with
+  ll        NVLink 2 (N-1) * G;               HBM G + 2 (N-1) G + 24 n + V
+  one-shot  NVLink (N-1) * G;                 HBM N*G + 24 n + V
+  two-shot  NVLink (N-1)/N * (G + V);         HBM G + 24 n/N + V (pull),
+                                              G (1 + 2 (N-1)/N) + 24 n/N + V (push)
+for n elements, G = 4 n gradient bytes, V parameter bytes and 24 n/N the
+fp32 master, m and v read and written by the shard owner.
 """
 from __future__ import annotations
 
@@ -29,6 +38,9 @@ def main():
     ap.add_argument("--max-mb", type=int, default=1024)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--nvlink-gbs", type=float, default=770.0)
+    ap.add_argument("--pull-ctas", default="", help="comma list: also time the pull form at these grid sizes")
+    ap.add_argument("--algo", default=None, choices=["auto", "pull", "push"], help="two-shot form (DLVK_AR_ALGO)")
+    ap.add_argument("--no-graph", dest="graph", action="store_false", help="time eager launches, not a CUDA graph")
     args = ap.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -48,7 +60,7 @@ def main():
     p = Parameter("w", (nmax,), torch.randn(nmax, generator=g) * 0.02)
     store = ParamStore([p], f"cuda:{local}", dtype)
     opt = dl.Adam(1e-3)
-    fused = FusedAllReduceOptimizer(store, opt, world, rank)
+    fused = FusedAllReduceOptimizer(store, opt, world, rank, algo=args.algo)
     store.grad.normal_(0, 1e-3)
     st = opt.state(store)
     sizes = []
@@ -62,21 +74,34 @@ def main():
             fn()
         torch.cuda.synchronize()
         dist.barrier()
+        graph = None
+        if args.graph:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(args.iters):
+                    fn()
+            graph.replay()  # untimed: the first replay uploads the graph
+            torch.cuda.synchronize()
+            dist.barrier()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        for _ in range(args.iters):
-            fn()
+        if graph is not None:
+            graph.replay()
+        else:
+            for _ in range(args.iters):
+                fn()
         e.record()
         torch.cuda.synchronize()
         t = torch.tensor([s.elapsed_time(e) / args.iters], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        del graph
         return float(t.item()) / 1e3
 
     for n in sizes:
-        def fused_step():
+        def fused_step(algo_override=None, ctas=None):
             fused.begin_step()
             opt.advance(store)
-            fused.reduce_update(0, n)
+            fused.reduce_update(0, n, algo=algo_override, ctas=ctas)
 
         def nccl_step():
             gr = store.grad[:n]
@@ -84,27 +109,44 @@ def main():
             opt.advance(store)
             opt.update_range(store, 0, n, extra_scale=1.0 / world)
 
+        algo = fused.algorithm(0, n)
         tf = time_it(fused_step)
+        tpull = time_it(lambda: fused_step("pull")) if algo == "push" else None
+        toneshot = time_it(lambda: fused_step("one-shot")) if algo == "ll" else None
+        tpull_ctas = {}
+        if algo in ("push", "pull") and args.pull_ctas:
+            for c in (int(v) for v in args.pull_ctas.split(",")):
+                tpull_ctas[c] = time_it(lambda: fused_step("pull", c))
         tn = time_it(nccl_step)
         gbytes = n * 4
         vbytes = n * (2 if dtype == torch.bfloat16 else 4)
-        one_shot = gbytes <= fused.one_shot_bytes
-        if one_shot:
+        state = 24 * n
+        if algo == "ll":  # every rank stores 8 bytes per gradient to every peer
+            link = (world - 1) * 2 * gbytes
+            local_b = gbytes + (world - 1) * 2 * gbytes + state + vbytes
+        elif algo == "one-shot":
             link = (world - 1) * gbytes
-            local_b = gbytes + n * 4 * 5 + vbytes
+            local_b = world * gbytes + state + vbytes
         else:
             link = (world - 1) / world * (gbytes + vbytes)
-            local_b = (gbytes + n * 4 * 5 + vbytes) / world
+            local_b = gbytes * (1 + (2 * (world - 1) / world if algo == "push" else 0)) + state / world + vbytes
         roof = max(link / (args.nvlink_gbs * 1e9), local_b / hbm)
         bus = 2 * (world - 1) / world * gbytes
         if rank == 0:
-            print(json.dumps({"world": world, "bucket_bytes": gbytes, "param_dtype": args.dtype,
-                              "algo": "one-shot" if one_shot else "two-shot",
-                              "fused_us": round(tf * 1e6, 1), "nccl_plus_adam_us": round(tn * 1e6, 1),
-                              "fused_bus_gbs": round(bus / tf / 1e9, 1), "nccl_bus_gbs": round(bus / tn / 1e9, 1),
-                              "fused_roofline_us": round(roof * 1e6, 1),
-                              "fused_frac_of_roofline": round(roof / tf, 3),
-                              "speedup_vs_nccl_plus_adam": round(tn / tf, 3)}), flush=True)
+            row = {"world": world, "bucket_bytes": gbytes, "param_dtype": args.dtype, "algo": algo,
+                   "timing": "cuda-graph" if args.graph else "eager",
+                   "fused_us": round(tf * 1e6, 1), "nccl_plus_adam_us": round(tn * 1e6, 1),
+                   "fused_bus_gbs": round(bus / tf / 1e9, 1), "nccl_bus_gbs": round(bus / tn / 1e9, 1),
+                   "fused_roofline_us": round(roof * 1e6, 1),
+                   "fused_frac_of_roofline": round(roof / tf, 3),
+                   "speedup_vs_nccl_plus_adam": round(tn / tf, 3)}
+            if tpull is not None:
+                row["pull_us"] = round(tpull * 1e6, 1)
+            if toneshot is not None:
+                row["pull_one_shot_us"] = round(toneshot * 1e6, 1)
+            for c, t in tpull_ctas.items():
+                row[f"pull_{c}ctas_us"] = round(t * 1e6, 1)
+            print(json.dumps(row), flush=True)
     err = C.read_device_error(True)
     if rank == 0:
         print(json.dumps({"device_error": int(err)}))

@@ -57,6 +57,88 @@ void fused_ar_op(std::shared_ptr<SymmetricBuffer> grads, std::shared_ptr<Symmetr
                             (int)ctas, stream());
 }
 
+// Push two-shot variant: `recv` holds world-1 slots of recv_slot gradient
+// elements; `cflags` is the [PUSH_MAX_BUCKETS][PUSH_MAX_CHUNKS][world] table.
+void fused_ar_push_op(std::shared_ptr<SymmetricBuffer> grads, std::shared_ptr<SymmetricBuffer> values,
+                      std::shared_ptr<SymmetricBuffer> flags, std::shared_ptr<SymmetricBuffer> recv,
+                      std::shared_ptr<SymmetricBuffer> cflags, const at::Tensor& counters, int64_t bucket,
+                      int64_t cbucket, int64_t start, int64_t end, int64_t recv_off, int64_t recv_slot,
+                      const at::Tensor& master, c10::optional<at::Tensor> m, c10::optional<at::Tensor> v,
+                      const at::Tensor& hyper, int64_t kind, const at::Tensor& epoch, int64_t world, int64_t rank,
+                      bool values_are_master, int64_t grad_code, int64_t value_code, int64_t ctas,
+                      double budget_s) {
+  c10::cuda::CUDAGuard g(master.device());
+  const int64_t gsz = grad_code == 0 ? 4 : 2;
+  TORCH_CHECK((world - 1) * recv_slot * gsz <= recv->bytes(), "push all-reduce: receive buffer too small");
+  TORCH_CHECK((int64_t)PUSH_MAX_BUCKETS * PUSH_MAX_CHUNKS * world * 4 <= cflags->bytes(),
+              "push all-reduce: chunk-flag buffer too small");
+  FusedARArgs a;
+  a.world = (int)world;
+  a.rank = (int)rank;
+  a.peer_grads = const_cast<const void* const*>(grads->device_ptrs());
+  a.peer_values = values->device_ptrs();
+  a.peer_flags = reinterpret_cast<uint32_t* const*>(flags->device_ptrs());
+  a.my_flags = static_cast<uint32_t*>(flags->local());
+  a.cta_counter = reinterpret_cast<unsigned int*>(counters.data_ptr<int>()) + bucket;
+  a.start = start;
+  a.end = end;
+  a.bucket = (int)bucket;
+  a.master = master.data_ptr<float>();
+  a.m = m.has_value() ? m->data_ptr<float>() : nullptr;
+  a.v = v.has_value() ? v->data_ptr<float>() : nullptr;
+  a.hyper = reinterpret_cast<const OptimHyper*>(hyper.data_ptr());
+  a.kind = (int)kind;
+  a.scale = 1.f / (float)world;
+  a.epoch_ptr = epoch.data_ptr<int64_t>();
+  a.values_are_master = values_are_master ? 1 : 0;
+  a.err = device_error_word();
+  a.budget_ns = (uint64_t)(budget_s * 1e9);
+  a.peer_recv = recv->device_ptrs();
+  a.my_recv = recv->local();
+  a.recv_off = recv_off;
+  a.recv_slot = recv_slot;
+  a.peer_cflags = reinterpret_cast<uint32_t* const*>(cflags->device_ptrs());
+  a.my_cflags = static_cast<uint32_t*>(cflags->local());
+  a.cbucket = (int)cbucket;
+  const int64_t n = end - start;
+  a.chunk = push_chunk_elems(((n + world - 1) / world + 63) / 64 * 64, (int)ctas);
+  fused_allreduce_optimizer_push(a, grad_code == 0 ? DType::F32 : DType::BF16,
+                                 value_code == 0 ? DType::F32 : DType::BF16, stream());
+}
+
+// LL one-shot variant: `ll` holds [2][world-1][ll_cap] 8-byte words.
+void fused_ar_ll_op(std::shared_ptr<SymmetricBuffer> grads, std::shared_ptr<SymmetricBuffer> values,
+                    std::shared_ptr<SymmetricBuffer> ll, int64_t start, int64_t end, int64_t ll_off, int64_t ll_cap,
+                    const at::Tensor& master, c10::optional<at::Tensor> m, c10::optional<at::Tensor> v,
+                    const at::Tensor& hyper, int64_t kind, const at::Tensor& epoch, int64_t world, int64_t rank,
+                    bool values_are_master, int64_t value_code, int64_t ctas, double budget_s) {
+  c10::cuda::CUDAGuard g(master.device());
+  TORCH_CHECK(2 * (world - 1) * ll_cap * 8 <= ll->bytes(), "LL all-reduce: buffer too small");
+  FusedARArgs a;
+  a.world = (int)world;
+  a.rank = (int)rank;
+  a.peer_grads = const_cast<const void* const*>(grads->device_ptrs());
+  a.peer_values = values->device_ptrs();
+  a.start = start;
+  a.end = end;
+  a.master = master.data_ptr<float>();
+  a.m = m.has_value() ? m->data_ptr<float>() : nullptr;
+  a.v = v.has_value() ? v->data_ptr<float>() : nullptr;
+  a.hyper = reinterpret_cast<const OptimHyper*>(hyper.data_ptr());
+  a.kind = (int)kind;
+  a.scale = 1.f / (float)world;
+  a.epoch_ptr = epoch.data_ptr<int64_t>();
+  a.one_shot = 1;
+  a.values_are_master = values_are_master ? 1 : 0;
+  a.err = device_error_word();
+  a.budget_ns = (uint64_t)(budget_s * 1e9);
+  a.peer_ll = ll->device_ptrs();
+  a.my_ll = ll->local();
+  a.ll_off = ll_off;
+  a.ll_cap = ll_cap;
+  fused_allreduce_optimizer_ll(a, value_code == 0 ? DType::F32 : DType::BF16, (int)ctas, stream());
+}
+
 void p2p_allreduce_op(std::shared_ptr<SymmetricBuffer> data, std::shared_ptr<SymmetricBuffer> flags,
                       const at::Tensor& counters, int64_t slot, int64_t start, int64_t end, const at::Tensor& epoch,
                       int64_t world, int64_t rank, int64_t dtype_code, bool average, int64_t ctas, double budget_s) {
@@ -104,6 +186,10 @@ void register_comm(py::module& m) {
            },
            py::arg("dtype_code"), py::arg("numel"), py::arg("byte_offset") = 0);
   c.def("fused_allreduce_optimizer", &fused_ar_op);
+  c.def("fused_allreduce_optimizer_push", &fused_ar_push_op);
+  c.def("fused_allreduce_optimizer_ll", &fused_ar_ll_op);
+  c.attr("PUSH_MAX_BUCKETS") = PUSH_MAX_BUCKETS;
+  c.attr("PUSH_MAX_CHUNKS") = PUSH_MAX_CHUNKS;
   c.def("p2p_allreduce", &p2p_allreduce_op);
   c.def("wait_flag_probe", [](const at::Tensor& flag, int64_t epoch, double budget_s) {
     TORCH_CHECK(flag.is_cuda() && flag.scalar_type() == at::kInt && flag.numel() >= 1, "wait_flag_probe: int32 flag");

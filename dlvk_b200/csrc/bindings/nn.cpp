@@ -47,6 +47,23 @@ DropoutDesc drop_desc(double p, int64_t stream_id, int64_t seed, int64_t step, c
   return dd;
 }
 
+// NCHW -> NHWC copy of a bf16 activation (one batched 2-D transpose).
+at::Tensor to_nhwc(const at::Tensor& x) {
+  auto y = at::empty({x.size(0), x.size(2), x.size(3), x.size(1)}, x.options());
+  transpose2d(DType::BF16, x.data_ptr(), y.data_ptr(), x.size(0), x.size(1), x.size(2) * x.size(3), stream());
+  return y;
+}
+
+at::Tensor pack_conv_weights(const at::Tensor& w, const ConvDesc& d, bool dgrad) {
+  const int64_t rows = dgrad ? d.Cin : d.Cout;
+  const int64_t cols = conv_pack_cols((int64_t)d.KH * d.KW * (dgrad ? d.Cout : d.Cin));
+  auto wp = at::empty({rows, cols}, w.options().dtype(at::kBFloat16));
+  conv_pack_weights(to_dtype(w), w.data_ptr(), reinterpret_cast<__nv_bfloat16*>(wp.data_ptr()), d, dgrad, stream());
+  return wp;
+}
+
+const __nv_bfloat16* bf(const at::Tensor& t) { return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr()); }
+
 at::Tensor conv2d_fwd_op(const at::Tensor& x, const at::Tensor& w, c10::optional<at::Tensor> bias, int64_t stride,
                          int64_t pad, bool relu) {
   check_cuda(x, "x");
@@ -54,6 +71,12 @@ at::Tensor conv2d_fwd_op(const at::Tensor& x, const at::Tensor& w, c10::optional
   auto xc = x.contiguous(), wc = w.contiguous().to(x.scalar_type());
   auto d = conv_desc(xc, wc, stride, pad);
   auto y = at::empty({d.N, d.Cout, d.Ho, d.Wo}, xc.options());
+  if (conv2d_tc_supported(to_dtype(xc), d)) {
+    auto xn = to_nhwc(xc);
+    auto wp = pack_conv_weights(wc, d, false);
+    conv2d_igemm(bf(xn), bf(wp), d, false, optf(bias), relu, nullptr, y.data_ptr(), false, stream());
+    return y;
+  }
   conv2d_fwd(to_dtype(xc), xc.data_ptr(), wc.data_ptr(), optf(bias), y.data_ptr(), d, relu, stream());
   return y;
 }
@@ -73,6 +96,12 @@ at::Tensor conv2d_dgrad_op(const at::Tensor& gy, const at::Tensor& w, std::vecto
     TORCH_CHECK(rsc.scalar_type() == gc.scalar_type() && rsc.numel() == dx.numel(), "dlvk.conv2d_dgrad: relu_src");
     rs = rsc.data_ptr();
   }
+  if (conv2d_tc_supported(to_dtype(gc), d)) {
+    auto gn = to_nhwc(gc);
+    auto wp = pack_conv_weights(wc, d, true);
+    conv2d_igemm(bf(gn), bf(wp), d, true, nullptr, false, rs, dx.data_ptr(), false, stream());
+    return dx;
+  }
   conv2d_dgrad(to_dtype(gc), gc.data_ptr(), wc.data_ptr(), dx.data_ptr(), rs, d, stream());
   return dx;
 }
@@ -84,6 +113,20 @@ void conv2d_wgrad_op(const at::Tensor& x, const at::Tensor& gy, const at::Tensor
   auto xc = x.contiguous(), gc = gy.contiguous().to(x.scalar_type());
   TORCH_CHECK(dw.scalar_type() == at::kFloat && dw.is_contiguous(), "dlvk.conv2d_wgrad: f32 contiguous dw");
   auto d = conv_desc(xc, dw, stride, pad);
+  if (conv2d_tc_supported(to_dtype(xc), d)) {
+    TORCH_CHECK(gc.size(2) == d.Ho && gc.size(3) == d.Wo, "dlvk.conv2d_wgrad: grad shape");
+    auto xn = to_nhwc(xc);
+    auto gn = to_nhwc(gc);
+    auto ws = at::empty({conv2d_wgrad_tc_ws_floats(d)}, xc.options().dtype(at::kFloat));
+    conv2d_wgrad_tc(bf(xn), bf(gn), d, ws.data_ptr<float>(), dw.data_ptr<float>(), accumulate, stream());
+    if (db.has_value()) {
+      const int64_t P = (int64_t)d.N * d.Ho * d.Wo;
+      auto cs = at::empty({std::max<int64_t>(1, colsum_scratch_floats(P, d.Cout))}, ws.options());
+      colsum(DType::BF16, DType::F32, gn.data_ptr(), P, d.Cout, 1.f, db->data_ptr<float>(), accumulate,
+             cs.data_ptr<float>(), stream());
+    }
+    return;
+  }
   auto scratch = at::empty({conv2d_wgrad_scratch_floats(d)}, xc.options().dtype(at::kFloat));
   conv2d_wgrad(to_dtype(xc), xc.data_ptr(), gc.data_ptr(), dw.data_ptr<float>(), optfm(db), accumulate, d,
                scratch.data_ptr<float>(), stream());
@@ -508,6 +551,8 @@ void register_nn(py::module& m) {
         py::arg("pad") = 0, py::arg("relu_src") = py::none());
   m.def("conv2d_wgrad", &conv2d_wgrad_op, py::arg("x"), py::arg("gy"), py::arg("dw"), py::arg("db") = py::none(),
         py::arg("stride") = 1, py::arg("pad") = 0, py::arg("accumulate") = false);
+  m.def("conv_tc_set_mode", &conv_tc_set_mode, "0 auto, 1 tensor-core implicit GEMM whenever supported, 2 never");
+  m.def("conv_tc_get_mode", &conv_tc_get_mode);
   m.def("maxpool_fwd", &maxpool_fwd_op);
   m.def("maxpool_bwd", &maxpool_bwd_op);
   m.def("avgpool_fwd", &avgpool_fwd_op);

@@ -3,6 +3,7 @@
 // all-reduce + optimizer kernel (comm.cu).
 #pragma once
 #include <cuda_runtime.h>
+#include <algorithm>
 #include <cstdint>
 #include <string>
 #include <vector>
@@ -32,12 +33,52 @@ struct FusedARArgs {
   int values_are_master = 0;
   uint32_t* err = nullptr;
   uint64_t budget_ns = 5000000000ull;
+  // Push two-shot (fused_allreduce_optimizer_push): every rank stores the
+  // gradient slices it does not own into the owners' receive buffers, so all
+  // NVLink traffic is stores and every reduction read is local.
+  void* const* peer_recv = nullptr;         // device array [world]: receive buffer of every rank
+  const void* my_recv = nullptr;
+  int64_t recv_off = 0;                     // element offset of this bucket's shard inside one slot
+  int64_t recv_slot = 0;                    // elements per slot; a rank has world-1 slots
+  uint32_t* const* peer_cflags = nullptr;   // device array [world]: chunk-flag table of every rank
+  uint32_t* my_cflags = nullptr;
+  int cbucket = 0;                          // row of this bucket in the chunk-flag table
+  int64_t chunk = 0;                        // elements of each rank's shard handled by one CTA
+  // LL one-shot (fused_allreduce_optimizer_ll): [2 parities][world-1 slots]
+  // [ll_cap] 8-byte {fp32 gradient, epoch} words in every rank's ll buffer.
+  void* const* peer_ll = nullptr;
+  const void* my_ll = nullptr;
+  int64_t ll_off = 0;                       // element offset of this bucket inside a slot
+  int64_t ll_cap = 0;                       // elements per slot
 };
+
+// Chunk-flag table of the push two-shot kernel: [PUSH_MAX_BUCKETS]
+// [PUSH_MAX_CHUNKS][world] uint32 epochs; one entry per (CTA, sub-chunk).
+constexpr int PUSH_MAX_BUCKETS = 128;
+constexpr int PUSH_MAX_CHUNKS = 2048;
+constexpr int PUSH_SUB = 2;  // sub-chunks per CTA
+// Elements of each rank's shard handled by one CTA when the kernel runs
+// `ctas` CTAs: a multiple of 1024, at least 2048, and at most
+// PUSH_MAX_CHUNKS / PUSH_SUB CTAs.
+inline int64_t push_chunk_elems(int64_t shard, int ctas) {
+  const int64_t g = std::max<int64_t>(1, std::min<int64_t>(ctas, PUSH_MAX_CHUNKS / PUSH_SUB));
+  const int64_t c = (shard + g - 1) / g;
+  return std::max<int64_t>(2048, (c + 1023) / 1024 * 1024);
+}
 
 void fused_allreduce_optimizer(const FusedARArgs& a, DType grad_dt, DType value_dt, int ctas, cudaStream_t s);
 // Generic in-place sum (or mean) all-reduce of [start, end) of the symmetric
 // buffer whose per-rank bases are a.peer_grads.
 void p2p_allreduce(const FusedARArgs& a, DType dt, bool average, int ctas, cudaStream_t s);
+// One-shot low-latency variant for small buckets: every rank stores its
+// gradients, each fp32 value paired with the step epoch in one 8-byte word,
+// into every peer's LL buffer; receivers poll the words themselves (no
+// flags, fences or barriers) and every rank updates the whole bucket.
+// Requires fp32 gradients; peer_ll, my_ll, ll_off and ll_cap must be set.
+void fused_allreduce_optimizer_ll(const FusedARArgs& a, DType value_dt, int ctas, cudaStream_t s);
+// Two-shot push variant of fused_allreduce_optimizer (peer_recv, my_recv,
+// recv_off, recv_slot, peer_cflags, my_cflags and cbucket must be set).
+void fused_allreduce_optimizer_push(const FusedARArgs& a, DType grad_dt, DType value_dt, cudaStream_t s);
 
 // A device allocation that every rank of the node can address: cudaMalloc +
 // cudaIpcGetMemHandle here, cudaIpcOpenMemHandle of the peers' handles there.

@@ -147,6 +147,23 @@ void conv2d_fwd(DType dt, const void* x, const void* w, const float* bias, void*
 // dx is zeroed where relu_src <= 0, fusing that activation's backward.
 void conv2d_dgrad(DType dt, const void* g, const void* w, void* dx, const void* relu_src, const ConvDesc& d,
                   cudaStream_t s);
+// Implicit-GEMM tcgen05 convolution (conv_tc.cu), bf16 with channel counts
+// that are multiples of 8.  Activations are gathered from NHWC copies; the
+// outputs (y, dx) are written NCHW.
+bool conv2d_tc_supported(DType dt, const ConvDesc& d);
+void conv_tc_set_mode(int mode);  // 0 auto (large convolutions), 1 whenever supported, 2 never
+int conv_tc_get_mode();
+int64_t conv_pack_cols(int64_t k);  // packed weight row length for K = KH*KW*channels
+// [OC][C][KH][KW] -> bf16 [OC][conv_pack_cols(KH*KW*C)] (forward) or
+// [C][conv_pack_cols(KH*KW*OC)] (dgrad), taps outer and channels inner.
+void conv_pack_weights(DType wdt, const void* w, __nv_bfloat16* out, const ConvDesc& d, bool dgrad, cudaStream_t s);
+// forward: src = X (NHWC), out = Y (NCHW); dgrad: src = dY (NHWC), out = dX
+// (NCHW), `mask` zeroes dX where the preceding ReLU was inactive.
+void conv2d_igemm(const __nv_bfloat16* src_nhwc, const __nv_bfloat16* wpack, const ConvDesc& d, bool dgrad,
+                  const float* bias, bool relu, const void* mask, void* out, bool out_f32, cudaStream_t s);
+int64_t conv2d_wgrad_tc_ws_floats(const ConvDesc& d);
+void conv2d_wgrad_tc(const __nv_bfloat16* x_nhwc, const __nv_bfloat16* dy_nhwc, const ConvDesc& d, float* ws,
+                     float* dw, bool accumulate, cudaStream_t s);
 int conv2d_wgrad_chunks(const ConvDesc& d);
 int64_t conv2d_wgrad_scratch_floats(const ConvDesc& d);
 void conv2d_wgrad(DType dt, const void* x, const void* g, float* dw, float* db, bool accumulate, const ConvDesc& d,

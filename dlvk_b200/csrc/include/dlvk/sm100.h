@@ -186,6 +186,18 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// cp.async (Ampere-style, per-thread 16-byte global -> shared copies):
+// `src_bytes` < 16 zero-fills the rest (0 = all zeros, nothing read).
+__device__ __forceinline__ void cp_async_16(uint32_t dst_smem, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst_smem), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // UMMA shared-memory descriptor for a SWIZZLE_128B tile.
 //  K-major : rows of 128 B (64 bf16 along K), 8-row atoms 1024 B apart
 //            (SBO = 1024, LBO unused).

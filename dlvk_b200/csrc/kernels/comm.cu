@@ -308,6 +308,265 @@ __global__ void __launch_bounds__(128, 8) p2p_allreduce_kernel(FusedARArgs a, in
   done_barrier(a, epoch);
 }
 
+// Push two-shot: CTA c of every rank handles chunk c of every rank's shard,
+// as PUSH_SUB sub-chunks.
+//   A. push:   for each sub-chunk s and each peer k (starting at rank+1, so
+//              the ranks' stores spread over all peers), store my gradients
+//              of sub-chunk s of chunk c of k's shard into k's receive slot
+//              for me, fence, and set k's flag [cbucket][c][s][rank] = epoch.
+//   B. reduce: for each sub-chunk, wait (bounded) for the flags of all
+//              peers; sum it over the ranks in rank order (my own gradients
+//              for my rank, the receive slots for the others), apply the
+//              optimizer and store the new parameters into every rank's
+//              buffer.  The stores of the last sub-chunks drain over NVLink
+//              while the first ones are reduced.
+//   C. done:   as in the pull kernels.
+// There is no global ready barrier: stream order makes my gradients final
+// before the kernel starts, and an owner waits only for the sub-chunks it
+// reduces.  All NVLink traffic is stores and every load is local.  The grid
+// is sized to be resident at once (one wave), so the waits never depend on
+// a CTA that has not been scheduled.
+template <typename TG, typename TV, int W, int U>
+__global__ void __launch_bounds__(256, 2) fused_push_ar_opt_kernel(FusedARArgs a) {
+  const uint32_t epoch = (uint32_t)(*a.epoch_ptr);
+  const int world = W > 0 ? W : a.world;
+  const int me = a.rank;
+  const int64_t n = a.end - a.start;
+  const int64_t shard = ((n + world - 1) / world + 63) / 64 * 64;
+  const int64_t c0 = (int64_t)blockIdx.x * a.chunk;
+  const int64_t sub = ((a.chunk + PUSH_SUB - 1) / PUSH_SUB + 63) / 64 * 64;
+  const int nt = blockDim.x;
+  // [lo, lo + len) of rank k's shard covered by sub-chunk s of this CTA.
+  auto sub_range = [&](int k, int s, int64_t& lo) -> int64_t {
+    const int64_t klen = min(n, shard * (k + 1)) - min(n, shard * k);
+    const int64_t cend = min(klen, c0 + a.chunk);
+    lo = c0 + s * sub;
+    return max((int64_t)0, min(cend, lo + sub) - lo);
+  };
+  auto flag_at = [&](uint32_t* base, int s, int src) {
+    return base + ((int64_t)a.cbucket * PUSH_MAX_CHUNKS + (int64_t)blockIdx.x * PUSH_SUB + s) * world + src;
+  };
+
+  // A. push my slices of the peers' shards.
+  for (int s = 0; s < PUSH_SUB; ++s) {
+    for (int d = 1; d < world; ++d) {
+      const int k = (me + d) % world;
+      int64_t lo;
+      const int64_t len = sub_range(k, s, lo);
+      if (len <= 0) continue;
+      const int slot = (me - k - 1 + world) % world;
+      const uint4* src =
+          reinterpret_cast<const uint4*>(reinterpret_cast<const TG*>(a.peer_grads[me]) + a.start + shard * k + lo);
+      uint4* dst =
+          reinterpret_cast<uint4*>(reinterpret_cast<TG*>(a.peer_recv[k]) + slot * a.recv_slot + a.recv_off + lo);
+      const int64_t nv = len * (int64_t)sizeof(TG) / 16;
+      constexpr int UA = 4;
+      for (int64_t i = threadIdx.x; i < nv; i += (int64_t)nt * UA) {
+        uint4 t[UA];
+#pragma unroll
+        for (int u = 0; u < UA; ++u) {
+          const int64_t j = i + (int64_t)u * nt;
+          if (j < nv) t[u] = src[j];
+        }
+#pragma unroll
+        for (int u = 0; u < UA; ++u) {
+          const int64_t j = i + (int64_t)u * nt;
+          if (j < nv) dst[j] = t[u];
+        }
+      }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < world && (int)threadIdx.x != me) st_release_sys(flag_at(a.peer_cflags[threadIdx.x], s, me), epoch);
+  }
+
+  // B. per sub-chunk: wait for the peers' slices, reduce, update, store.
+  __shared__ int ok;
+  const OptimHyper h = *a.hyper;
+  const float gs = a.scale * h.grad_scale;
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s = 0; s < PUSH_SUB; ++s) {
+    if (threadIdx.x == 0) ok = 1;
+    __syncthreads();
+    if (threadIdx.x < world && (int)threadIdx.x != me)
+      if (!wait_flag(flag_at(a.my_cflags, s, threadIdx.x), epoch, a.budget_ns, a.err)) ok = 0;
+    __syncthreads();
+    if (!ok) break;
+    int64_t lo;
+    const int64_t nvec = sub_range(me, s, lo) / 4;
+    const int64_t base = a.start + shard * me + lo;  // element offset in the flat buffers
+    float* mst = a.master + base;
+    float* mm = a.m ? a.m + base : nullptr;
+    float* vv = a.v ? a.v + base : nullptr;
+    const TG* own = reinterpret_cast<const TG*>(a.peer_grads[me]) + base;
+    const TG* recv = reinterpret_cast<const TG*>(a.my_recv) + a.recv_off + lo;
+    for (int64_t v0 = threadIdx.x; v0 < nvec; v0 += (int64_t)nt * U) {
+      float4 g[U], w[U], m4[U], v4[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) g[u] = z4;
+      auto add_rank = [&](int r) {
+        const TG* src = r == me ? own : recv + (int64_t)((r - me - 1 + world) % world) * a.recv_slot;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t vi = v0 + (int64_t)u * nt;
+          const float4 t = vi < nvec ? load4<TG>(src, vi) : z4;
+          g[u].x += t.x;
+          g[u].y += t.y;
+          g[u].z += t.z;
+          g[u].w += t.w;
+        }
+      };
+      if constexpr (W > 0) {
+#pragma unroll
+        for (int r = 0; r < W; ++r) add_rank(r);  // rank order: deterministic
+      } else {
+        for (int r = 0; r < world; ++r) add_rank(r);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t vi = v0 + (int64_t)u * nt;
+        w[u] = vi < nvec ? reinterpret_cast<const float4*>(mst)[vi] : z4;
+        m4[u] = (mm && vi < nvec) ? reinterpret_cast<const float4*>(mm)[vi] : z4;
+        v4[u] = (vv && vi < nvec) ? reinterpret_cast<const float4*>(vv)[vi] : z4;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t vi = v0 + (int64_t)u * nt;
+        if (vi >= nvec) continue;
+        opt_apply(a.kind, h, w[u].x, g[u].x * gs, m4[u].x, v4[u].x);
+        opt_apply(a.kind, h, w[u].y, g[u].y * gs, m4[u].y, v4[u].y);
+        opt_apply(a.kind, h, w[u].z, g[u].z * gs, m4[u].z, v4[u].z);
+        opt_apply(a.kind, h, w[u].w, g[u].w * gs, m4[u].w, v4[u].w);
+        reinterpret_cast<float4*>(mst)[vi] = w[u];
+        if (mm) reinterpret_cast<float4*>(mm)[vi] = m4[u];
+        if (vv) reinterpret_cast<float4*>(vv)[vi] = v4[u];
+        for (int d = 0; d < world; ++d) {
+          const int r = (me + 1 + d) % world;
+          if (a.values_are_master) {
+            if (r != me) store4<float>(reinterpret_cast<float*>(a.peer_values[r]) + base, vi, w[u]);
+          } else {
+            store4<TV>(reinterpret_cast<TV*>(a.peer_values[r]) + base, vi, w[u]);
+          }
+        }
+      }
+    }
+  }
+  done_barrier(a, epoch);
+}
+
+// LL one-shot.  Element pair i of the bucket travels as two 8-byte words
+// {value bits, epoch}; a 64-bit aligned store is single-copy atomic, so a
+// reader that sees the epoch also sees the value.  Words live in
+// [parity = epoch & 1][slot][ll_off + i]; a writer can reuse a parity only
+// two epochs later, after its own next kernel, which needs this rank's next
+// words, which this rank sends only after finishing the current kernel.
+__device__ __forceinline__ void st_ll2(void* p, float a, float b, uint32_t e) {
+  const uint64_t w0 = (uint64_t)__float_as_uint(a) | ((uint64_t)e << 32);
+  const uint64_t w1 = (uint64_t)__float_as_uint(b) | ((uint64_t)e << 32);
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(w0), "l"(w1) : "memory");
+}
+__device__ __forceinline__ void ld_ll2(const void* p, uint64_t& w0, uint64_t& w1) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(p) : "memory");
+}
+
+template <typename TV, int W>
+__global__ void __launch_bounds__(128) fused_ll_ar_opt_kernel(FusedARArgs a) {
+  const uint32_t epoch = (uint32_t)(*a.epoch_ptr);
+  const int world = W > 0 ? W : a.world;
+  const int me = a.rank;
+  const int64_t npair = (a.end - a.start) / 2;
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t par = (int64_t)(epoch & 1u) * (world - 1);
+  const float* grad = reinterpret_cast<const float*>(a.peer_grads[me]) + a.start;
+  // 1. send
+  for (int64_t i = tid; i < npair; i += stride) {
+    const float2 g = reinterpret_cast<const float2*>(grad)[i];
+    for (int d = 1; d < world; ++d) {
+      const int k = (me + d) % world;
+      const int slot = (me - k - 1 + world) % world;
+      uint64_t* dst = reinterpret_cast<uint64_t*>(a.peer_ll[k]) + (par + slot) * a.ll_cap + a.ll_off + 2 * i;
+      st_ll2(dst, g.x, g.y, epoch);
+    }
+  }
+  // 2. receive, reduce in rank order, update
+  const OptimHyper h = *a.hyper;
+  const float gs = a.scale * h.grad_scale;
+  const uint64_t* ll = reinterpret_cast<const uint64_t*>(a.my_ll);
+  bool alive = true;
+  for (int64_t i = tid; i < npair; i += stride) {
+    const float2 own = reinterpret_cast<const float2*>(grad)[i];
+    float s0 = 0.f, s1 = 0.f;
+    for (int r = 0; r < world; ++r) {
+      if (r == me) {
+        s0 += own.x;
+        s1 += own.y;
+        continue;
+      }
+      const uint64_t* src = ll + (par + (r - me - 1 + world) % world) * a.ll_cap + a.ll_off + 2 * i;
+      uint64_t w0 = 0, w1 = 0;
+      if (alive) {
+        ld_ll2(src, w0, w1);
+        if ((uint32_t)(w0 >> 32) != epoch || (uint32_t)(w1 >> 32) != epoch) {
+          const uint64_t t0 = gtimer();
+          uint32_t it = 0;
+          while (true) {
+            ld_ll2(src, w0, w1);
+            if ((uint32_t)(w0 >> 32) == epoch && (uint32_t)(w1 >> 32) == epoch) break;
+            if ((++it & 63u) == 0 && gtimer() - t0 > a.budget_ns) {
+              atomicCAS(a.err, 0u, (uint32_t)DLVK_ERR_PEER_TIMEOUT);
+              alive = false;
+              w0 = w1 = 0;
+              break;
+            }
+          }
+        }
+      }
+      s0 += __uint_as_float((uint32_t)w0);
+      s1 += __uint_as_float((uint32_t)w1);
+    }
+    if (!alive) continue;
+    const int64_t e0 = a.start + 2 * i;
+    float w[2] = {a.master[e0], a.master[e0 + 1]};
+    float m2[2] = {0.f, 0.f}, v2[2] = {0.f, 0.f};
+    if (a.m) {
+      m2[0] = a.m[e0];
+      m2[1] = a.m[e0 + 1];
+    }
+    if (a.v) {
+      v2[0] = a.v[e0];
+      v2[1] = a.v[e0 + 1];
+    }
+    opt_apply(a.kind, h, w[0], s0 * gs, m2[0], v2[0]);
+    opt_apply(a.kind, h, w[1], s1 * gs, m2[1], v2[1]);
+    a.master[e0] = w[0];
+    a.master[e0 + 1] = w[1];
+    if (a.m) {
+      a.m[e0] = m2[0];
+      a.m[e0 + 1] = m2[1];
+    }
+    if (a.v) {
+      a.v[e0] = v2[0];
+      a.v[e0 + 1] = v2[1];
+    }
+    if (!a.values_are_master) {
+      TV* out = reinterpret_cast<TV*>(a.peer_values[me]) + e0;
+      out[0] = from_f32<TV>(w[0]);
+      out[1] = from_f32<TV>(w[1]);
+    }
+  }
+}
+
+template <typename TG, typename TV>
+void launch_push(const FusedARArgs& a, int grid, cudaStream_t s) {
+  switch (a.world) {
+    case 2: fused_push_ar_opt_kernel<TG, TV, 2, 2><<<grid, 256, 0, s>>>(a); break;
+    case 4: fused_push_ar_opt_kernel<TG, TV, 4, 2><<<grid, 256, 0, s>>>(a); break;
+    case 8: fused_push_ar_opt_kernel<TG, TV, 8, 1><<<grid, 256, 0, s>>>(a); break;
+    default: fused_push_ar_opt_kernel<TG, TV, 0, 1><<<grid, 256, 0, s>>>(a); break;
+  }
+}
+
 }  // namespace
 
 void fused_allreduce_optimizer(const FusedARArgs& a, DType grad_dt, DType value_dt, int ctas, cudaStream_t s) {
@@ -321,6 +580,53 @@ void fused_allreduce_optimizer(const FusedARArgs& a, DType grad_dt, DType value_
   else if (grad_dt == DType::F32 && value_dt == DType::F32) launch_fused<float, float>(a, grid, s);
   else if (grad_dt == DType::BF16 && value_dt == DType::BF16) launch_fused<__nv_bfloat16, __nv_bfloat16>(a, grid, s);
   else throw std::runtime_error("fused all-reduce: unsupported grad/value dtypes");
+  DLVK_POST_LAUNCH();
+}
+
+void fused_allreduce_optimizer_ll(const FusedARArgs& a, DType value_dt, int ctas, cudaStream_t s) {
+  const int64_t n = a.end - a.start;
+  if (n <= 0) return;
+  DLVK_CHECK(a.world >= 2 && a.world <= 64, "LL all-reduce: world size must be in [2, 64]");
+  DLVK_CHECK(a.start % 64 == 0 && n % 64 == 0, "LL all-reduce: bucket must be 64-element aligned");
+  DLVK_CHECK(a.peer_ll && a.my_ll && a.ll_off % 2 == 0 && a.ll_off + n <= a.ll_cap, "LL all-reduce: buffer");
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ctas, (n / 2 + 127) / 128));
+  auto launch = [&](auto tv) {
+    using TV = decltype(tv);
+    switch (a.world) {
+      case 2: fused_ll_ar_opt_kernel<TV, 2><<<grid, 128, 0, s>>>(a); break;
+      case 4: fused_ll_ar_opt_kernel<TV, 4><<<grid, 128, 0, s>>>(a); break;
+      case 8: fused_ll_ar_opt_kernel<TV, 8><<<grid, 128, 0, s>>>(a); break;
+      default: fused_ll_ar_opt_kernel<TV, 0><<<grid, 128, 0, s>>>(a); break;
+    }
+  };
+  if (value_dt == DType::BF16) launch(__nv_bfloat16{});
+  else if (value_dt == DType::F32) launch(float{});
+  else throw std::runtime_error("LL all-reduce: unsupported value dtype");
+  DLVK_POST_LAUNCH();
+}
+
+void fused_allreduce_optimizer_push(const FusedARArgs& a, DType grad_dt, DType value_dt, cudaStream_t s) {
+  const int64_t n = a.end - a.start;
+  if (n <= 0) return;
+  DLVK_CHECK(a.world >= 2 && a.world <= 64, "push all-reduce: world size must be in [2, 64]");
+  DLVK_CHECK(a.start % 64 == 0 && n % 64 == 0, "push all-reduce: bucket must be 64-element aligned");
+  DLVK_CHECK(a.cbucket >= 0 && a.cbucket < PUSH_MAX_BUCKETS, "push all-reduce: chunk-flag row out of range");
+  DLVK_CHECK(a.peer_recv && a.my_recv && a.peer_cflags && a.my_cflags, "push all-reduce: buffers not set");
+  const int64_t shard = ((n + a.world - 1) / a.world + 63) / 64 * 64;
+  DLVK_CHECK(a.chunk >= 2048 && a.chunk % 1024 == 0, "push all-reduce: bad chunk size");
+  DLVK_CHECK(a.recv_off % 64 == 0 && a.recv_off + shard <= a.recv_slot, "push all-reduce: receive slot overflow");
+  const int grid = (int)((shard + a.chunk - 1) / a.chunk);
+  DLVK_CHECK((int64_t)grid * PUSH_SUB <= PUSH_MAX_CHUNKS, "push all-reduce: too many chunks");
+  // One wave: every CTA must be resident at once (CTA c waits on the peers'
+  // CTA c only, but a CTA that cannot be scheduled would stall its chunk).
+  int dev = 0, sms = 0;
+  DLVK_CUDA_CHECK(cudaGetDevice(&dev));
+  DLVK_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  DLVK_CHECK(grid <= 2 * sms, "push all-reduce: grid larger than one wave");
+  if (grad_dt == DType::F32 && value_dt == DType::BF16) launch_push<float, __nv_bfloat16>(a, grid, s);
+  else if (grad_dt == DType::F32 && value_dt == DType::F32) launch_push<float, float>(a, grid, s);
+  else if (grad_dt == DType::BF16 && value_dt == DType::BF16) launch_push<__nv_bfloat16, __nv_bfloat16>(a, grid, s);
+  else throw std::runtime_error("push all-reduce: unsupported grad/value dtypes");
   DLVK_POST_LAUNCH();
 }
 

@@ -342,66 +342,78 @@ __global__ void __launch_bounds__(256) ln_bwd_warp_kernel(const T* __restrict__ 
                                                           const float* __restrict__ rstd, const T* __restrict__ dy,
                                                           T* __restrict__ dx, float* __restrict__ part, int64_t rows,
                                                           int D, const T* __restrict__ dres) {
+  // One warp per row, the row held in registers; the next row's x, dy (and
+  // residual gradient) are loaded before the current row is processed, so
+  // two rows per warp are in flight.
   constexpr int EPV = 16 / sizeof(T);
-  extern __shared__ float sp[];  // [8][2*D]
+  extern __shared__ float sp[];  // [8][2*D] partials, then gamma [D]
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float gam[NV][EPV], adg[NV][EPV], adb[NV][EPV];
+  float* sgam = sp + 16 * D;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) sgam[d] = gamma ? gamma[d] : 1.f;
+  __syncthreads();
+  float adg[NV][EPV], adb[NV][EPV];
 #pragma unroll
   for (int i = 0; i < NV; ++i)
 #pragma unroll
     for (int k = 0; k < EPV; ++k) {
-      const int col = (lane + 32 * i) * EPV + k;
-      gam[i][k] = gamma ? gamma[col] : 1.f;
       adg[i][k] = 0.f;
       adb[i][k] = 0.f;
     }
   const float invD = 1.f / D;
-  for (int64_t r = (int64_t)blockIdx.x * 8 + w; r < rows; r += (int64_t)gridDim.x * 8) {
-    float xv[NV][EPV], gv[NV][EPV];
+  const int64_t step = (int64_t)gridDim.x * 8;
+  int64_t r = (int64_t)blockIdx.x * 8 + w;
+  uint4 nx[NV], ng[NV], nr[NV];
+  auto fetch = [&](int64_t row) {
+    if (row >= rows) return;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      const uint4 ux = reinterpret_cast<const uint4*>(x + r * D)[lane + 32 * i];
-      const uint4 ug = reinterpret_cast<const uint4*>(dy + r * D)[lane + 32 * i];
-      const T* ex = reinterpret_cast<const T*>(&ux);
-      const T* eg = reinterpret_cast<const T*>(&ug);
+      nx[i] = reinterpret_cast<const uint4*>(x + row * D)[lane + 32 * i];
+      ng[i] = reinterpret_cast<const uint4*>(dy + row * D)[lane + 32 * i];
+      if (dres) nr[i] = reinterpret_cast<const uint4*>(dres + row * D)[lane + 32 * i];
+    }
+  };
+  fetch(r);
+  for (; r < rows; r += step) {
+    uint4 cx[NV], cg[NV], cr[NV];  // current row, raw; nx/ng/nr take the next one
 #pragma unroll
-      for (int k = 0; k < EPV; ++k) {
-        xv[i][k] = to_f32(ex[k]);
-        gv[i][k] = to_f32(eg[k]);
-      }
+    for (int i = 0; i < NV; ++i) {
+      cx[i] = nx[i];
+      cg[i] = ng[i];
+      cr[i] = nr[i];
     }
     const float mu = mean[r], rs = rstd[r];
+    fetch(r + step);
     float a = 0.f, b = 0.f;
 #pragma unroll
-    for (int i = 0; i < NV; ++i)
+    for (int i = 0; i < NV; ++i) {
+      const T* ex = reinterpret_cast<const T*>(&cx[i]);
+      const T* eg = reinterpret_cast<const T*>(&cg[i]);
 #pragma unroll
       for (int k = 0; k < EPV; ++k) {
-        const float xh = (xv[i][k] - mu) * rs;
-        xv[i][k] = xh;
-        const float gg = gv[i][k] * gam[i][k];
+        const float xh = (to_f32(ex[k]) - mu) * rs;
+        const float g = to_f32(eg[k]);
+        const float gg = g * sgam[(lane + 32 * i) * EPV + k];
         a += gg;
         b += gg * xh;
-        adg[i][k] += gv[i][k] * xh;
-        adb[i][k] += gv[i][k];
+        adg[i][k] += g * xh;
+        adb[i][k] += g;
       }
+    }
     a = warp_sum(a) * invD;
     b = warp_sum(b) * invD;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      float add[EPV];
-      if (dres) {
-        const uint4 ur = reinterpret_cast<const uint4*>(dres + r * D)[lane + 32 * i];
-        const T* er = reinterpret_cast<const T*>(&ur);
-#pragma unroll
-        for (int k = 0; k < EPV; ++k) add[k] = to_f32(er[k]);
-      } else {
-#pragma unroll
-        for (int k = 0; k < EPV; ++k) add[k] = 0.f;
-      }
+      const T* ex = reinterpret_cast<const T*>(&cx[i]);
+      const T* eg = reinterpret_cast<const T*>(&cg[i]);
+      const T* er = reinterpret_cast<const T*>(&cr[i]);
       uint4 o;
       T* eo = reinterpret_cast<T*>(&o);
 #pragma unroll
-      for (int k = 0; k < EPV; ++k) eo[k] = from_f32<T>(rs * (gv[i][k] * gam[i][k] - a - xv[i][k] * b) + add[k]);
+      for (int k = 0; k < EPV; ++k) {
+        const float xh = (to_f32(ex[k]) - mu) * rs;
+        const float v = rs * (to_f32(eg[k]) * sgam[(lane + 32 * i) * EPV + k] - a - xh * b);
+        eo[k] = from_f32<T>(dres ? v + to_f32(er[k]) : v);
+      }
       reinterpret_cast<uint4*>(dx + r * D)[lane + 32 * i] = o;
     }
   }
@@ -423,21 +435,31 @@ __global__ void __launch_bounds__(256) ln_bwd_warp_kernel(const T* __restrict__ 
   }
 }
 
-// Sums the per-block partials: block (32 columns) x 8 row groups, combined in
-// a fixed order through shared memory.
-__global__ void ln_bwd_final_kernel(const float* __restrict__ part, int blocks, int D, float* __restrict__ dgamma,
-                                    float* __restrict__ dbeta, int accumulate) {
-  __shared__ float sm[8][33];
+// Sums the per-block partials: block = 32 columns x 16 row groups, each
+// thread with four independent accumulators, combined in a fixed order
+// through shared memory.
+__global__ void __launch_bounds__(512) ln_bwd_final_kernel(const float* __restrict__ part, int blocks, int D,
+                                                           float* __restrict__ dgamma, float* __restrict__ dbeta,
+                                                           int accumulate) {
+  __shared__ float sm[16][33];
   const int d = blockIdx.x * 32 + threadIdx.x;
-  float s = 0.f;
-  if (d < 2 * D)
-    for (int b = threadIdx.y; b < blocks; b += 8) s += part[(int64_t)b * 2 * D + d];
-  sm[threadIdx.y][threadIdx.x] = s;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  if (d < 2 * D) {
+    int b = threadIdx.y;
+    for (; b + 48 < blocks; b += 64) {
+      s0 += part[(int64_t)b * 2 * D + d];
+      s1 += part[(int64_t)(b + 16) * 2 * D + d];
+      s2 += part[(int64_t)(b + 32) * 2 * D + d];
+      s3 += part[(int64_t)(b + 48) * 2 * D + d];
+    }
+    for (; b < blocks; b += 16) s0 += part[(int64_t)b * 2 * D + d];
+  }
+  sm[threadIdx.y][threadIdx.x] = (s0 + s1) + (s2 + s3);
   __syncthreads();
   if (threadIdx.y != 0 || d >= 2 * D) return;
-  s = 0.f;
+  float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) s += sm[i][threadIdx.x];
+  for (int i = 0; i < 16; ++i) s += sm[i][threadIdx.x];
   float* dst = d < D ? (dgamma ? dgamma + d : nullptr) : (dbeta ? dbeta + (d - D) : nullptr);
   if (dst) *dst = accumulate ? *dst + s : s;
 }
@@ -564,7 +586,7 @@ void layernorm_fwd(DType dt, const void* x, const float* gamma, const float* bet
   DLVK_POST_LAUNCH();
 }
 
-int layernorm_bwd_blocks(int64_t rows) { return (int)std::max<int64_t>(1, std::min<int64_t>(148 * 2, (rows + 7) / 8)); }
+int layernorm_bwd_blocks(int64_t rows) { return (int)std::max<int64_t>(1, std::min<int64_t>(148, (rows + 7) / 8)); }
 int64_t layernorm_bwd_scratch_floats(int64_t rows, int D) { return (int64_t)layernorm_bwd_blocks(rows) * 2 * D; }
 
 void layernorm_bwd(DType dt, const void* x, const float* gamma, const float* mean, const float* rstd, const void* dy,
@@ -577,7 +599,7 @@ void layernorm_bwd(DType dt, const void* x, const float* gamma, const float* mea
     const int nv = (D % (32 * epv) == 0) ? D / (32 * epv) : 0;
     const bool al = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dy) |
                       reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(dres)) & 15) == 0;
-    const size_t smem = (size_t)8 * 2 * D * sizeof(float);
+    const size_t smem = (size_t)(8 * 2 + 1) * D * sizeof(float);
     if (al && (nv == 1 || nv == 2 || nv == 4) && smem <= 200 * 1024) {
       DLVK_DISPATCH_FB(dt, "layernorm_bwd", {
         auto kern = nv == 1 ? ln_bwd_warp_kernel<T, 1> : (nv == 2 ? ln_bwd_warp_kernel<T, 2> : ln_bwd_warp_kernel<T, 4>);
@@ -587,7 +609,7 @@ void layernorm_bwd(DType dt, const void* x, const float* gamma, const float* mea
                                        (const T*)dres);
       });
       DLVK_POST_LAUNCH();
-      ln_bwd_final_kernel<<<(2 * D + 31) / 32, dim3(32, 8), 0, s>>>(scratch, blocks, D, dgamma, dbeta, accumulate ? 1 : 0);
+      ln_bwd_final_kernel<<<(2 * D + 31) / 32, dim3(32, 16), 0, s>>>(scratch, blocks, D, dgamma, dbeta, accumulate ? 1 : 0);
       DLVK_POST_LAUNCH();
       return;
     }
@@ -603,7 +625,7 @@ void layernorm_bwd(DType dt, const void* x, const float* gamma, const float* mea
                                                       rows, D, (const T*)dres);
   });
   DLVK_POST_LAUNCH();
-  ln_bwd_final_kernel<<<(2 * D + 31) / 32, dim3(32, 8), 0, s>>>(scratch, blocks, D, dgamma, dbeta, accumulate ? 1 : 0);
+  ln_bwd_final_kernel<<<(2 * D + 31) / 32, dim3(32, 16), 0, s>>>(scratch, blocks, D, dgamma, dbeta, accumulate ? 1 : 0);
   DLVK_POST_LAUNCH();
 }
 

@@ -9,6 +9,8 @@
 // per-row loss and dlogits = (softmax - target) * scale from the logits in a
 // single launch (the reference's softmax-backward-is-identity convention,
 // src/layers/activation.cpp:71-75, is only correct in this fused form).
+#include <type_traits>
+
 #include "dlvk/common.h"
 #include "dlvk/kernels.h"
 
@@ -177,6 +179,91 @@ __global__ void __launch_bounds__(THREADS) softmax_ce_kernel(const T* x, const i
       const float t = labels ? (c == label ? 1.f : 0.f) : probs[r * cols + c];
       dr[c] = from_f32<T>(ignored ? 0.f : (p - t) * grad_scale);
     }
+  }
+}
+
+// Register-resident fused softmax + CE for bf16 rows of up to 512 x 8 x NV
+// class-id-targeted columns (the 32000-way vocabulary fits with NV = 8): the
+// row is read from memory once, each logit is exponentiated once, and the
+// gradient is written from the kept exponentials -- one read and one write of
+// the logits instead of two reads, and half the exponentials.  dlogits may
+// alias x: every thread writes only vectors it has already loaded, and only
+// after the block-wide reductions.
+template <int NV>
+__global__ void __launch_bounds__(512, 1) softmax_ce_reg_kernel(const __nv_bfloat16* x, const int* __restrict__ labels,
+                                                                float* __restrict__ loss_rows,
+                                                                __nv_bfloat16* dlogits, int64_t cols,
+                                                                float grad_scale) {
+  constexpr int THREADS = 512;
+  __shared__ float red[32];
+  const int64_t r = blockIdx.x;
+  const __nv_bfloat16* xr = x + r * cols;
+  const int nvec = (int)(cols / 8);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  uint4 raw[NV];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int v = threadIdx.x + i * THREADS;
+    if (v < nvec) {
+      raw[i] = reinterpret_cast<const uint4*>(xr)[v];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(h[k]);
+        mx = fmaxf(mx, fmaxf(f.x, f.y));
+      }
+    }
+  }
+  const int label = labels[r];
+  const float xl = (label >= 0 && label < cols) ? __bfloat162float(xr[label]) : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) red[wid] = mx;
+  __syncthreads();
+  mx = lane < THREADS / 32 ? red[lane] : -INFINITY;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float e[NV][8];
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int v = threadIdx.x + i * THREADS;
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (v < nvec) {
+        const float2 f = __bfloat1622float2(h[k]);
+        e[i][2 * k] = __expf(f.x - mx);
+        e[i][2 * k + 1] = __expf(f.y - mx);
+        sum += e[i][2 * k] + e[i][2 * k + 1];
+      }
+    }
+  }
+  sum = warp_sum(sum);
+  __syncthreads();  // every warp has read red[] (the maximum)
+  if (lane == 0) red[wid] = sum;
+  __syncthreads();
+  sum = lane < THREADS / 32 ? red[lane] : 0.f;
+  sum = warp_sum(sum);
+  const float inv = 1.f / sum;
+  if (threadIdx.x == 0 && loss_rows) loss_rows[r] = label < 0 ? 0.f : mx + logf(sum) - xl;
+  const float gs = label < 0 ? 0.f : grad_scale;
+  __nv_bfloat16* dr = dlogits + r * cols;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int v = threadIdx.x + i * THREADS;
+    if (v >= nvec) continue;
+    uint4 o;
+    __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int c = v * 8 + 2 * k;
+      const float g0 = (e[i][2 * k] * inv - (c == label ? 1.f : 0.f)) * gs;
+      const float g1 = (e[i][2 * k + 1] * inv - (c + 1 == label ? 1.f : 0.f)) * gs;
+      oh[k] = __floats2bfloat162_rn(g0, g1);
+    }
+    reinterpret_cast<uint4*>(dr)[v] = o;
   }
 }
 
@@ -363,6 +450,18 @@ void launch_softmax_bwd(const void* y, const void* dy, void* dx, int64_t rows, i
 template <typename T>
 void launch_ce(const void* x, const int* labels, const float* probs, float* loss_rows, void* dlogits, int64_t rows,
                int64_t cols, float grad_scale, cudaStream_t s) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dlogits)) & 15) == 0;
+    if (labels && dlogits && aligned && cols % 8 == 0 && cols > 4096 && cols <= 512 * 8 * 8) {
+      const int64_t per = (cols / 8 + 511) / 512;  // 16-byte vectors per thread
+      const auto* xb = (const __nv_bfloat16*)x;
+      auto* db = (__nv_bfloat16*)dlogits;
+      if (per <= 2) softmax_ce_reg_kernel<2><<<(unsigned)rows, 512, 0, s>>>(xb, labels, loss_rows, db, cols, grad_scale);
+      else if (per <= 4) softmax_ce_reg_kernel<4><<<(unsigned)rows, 512, 0, s>>>(xb, labels, loss_rows, db, cols, grad_scale);
+      else softmax_ce_reg_kernel<8><<<(unsigned)rows, 512, 0, s>>>(xb, labels, loss_rows, db, cols, grad_scale);
+      return;
+    }
+  }
   if (cols <= 64)
     softmax_ce_kernel<T, 32><<<(unsigned)rows, 32, 0, s>>>((const T*)x, labels, probs, loss_rows, (T*)dlogits, cols,
                                                            grad_scale);

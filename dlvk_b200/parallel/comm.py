@@ -60,14 +60,35 @@ class FusedAllReduceOptimizer:
 
     The model's flat gradient buffer and compute-dtype parameter buffer are
     moved into symmetric peer-mapped memory.  Buckets smaller than
-    `one_shot_bytes` are reduced redundantly on every rank (one round); larger
-    ones two-shot (each rank reduces and updates 1/world of the bucket and
-    writes the new parameters to all ranks), so optimizer state is touched
-    only by the shard owner.
+    `one_shot_bytes` are reduced redundantly on every rank (one round,
+    "one-shot"); larger ones two-shot: each rank reduces and updates 1/world
+    of the bucket and writes the new parameters to all ranks, so optimizer
+    state is touched only by the shard owner.
+
+    One-shot buckets run as "ll" while the LL buffer has room: every rank
+    stores its gradients, each value paired with the step epoch in one
+    8-byte word, straight into the peers' LL buffers, and receivers poll the
+    words themselves -- one NVLink crossing, no flags or barriers -- else as
+    "one-shot" (pull, with ready/done flags).  Two-shot comes in two forms:
+
+    * "pull" (default): the owner loads the peers' slices over NVLink with
+      6 CTAs of 128 threads per SM, enough loads in flight to cover NVLink
+      latency; no extra memory.
+    * "push": every rank first stores the gradient slices it does not own
+      into the owners' receive buffers, so NVLink carries only stores and the
+      reduction reads local memory.  Needs a receive buffer of `recv_factor`
+      x (gradient bytes / world) per peer slot.  Measured slower than pull on
+      two B200s at every size from 4 MB to 1 GB (its push, fence and reduce
+      phases serialise per CTA), so it is opt-in.
+
+    `algo` ("auto", "push", "pull"; env DLVK_AR_ALGO) picks the two-shot
+    form; "auto" is pull.  The one-shot threshold defaults to 4 MB / world
+    of gradients: LL traffic grows with (world - 1) x 8 bytes per gradient.
     """
 
     def __init__(self, store, optimizer, world: int, rank: int, group=None,
-                 one_shot_bytes: Optional[int] = None, ctas: Optional[int] = None):
+                 one_shot_bytes: Optional[int] = None, ctas: Optional[int] = None, algo: Optional[str] = None,
+                 recv_factor: Optional[float] = None):
         if optimizer.clip_norm is not None:
             raise ValueError("global-norm clipping is not supported with the fused all-reduce optimizer")
         self.C = _ext.C()
@@ -88,29 +109,113 @@ class FusedAllReduceOptimizer:
         self.counters = torch.zeros(MAX_BUCKETS, dtype=torch.int32, device=dev)
         self.epoch = torch.zeros(1, dtype=torch.int64, device=dev)
         self.one_shot_bytes = one_shot_bytes if one_shot_bytes is not None else int(
-            os.environ.get("DLVK_ONE_SHOT_BYTES", str(2 << 20)))
-        self.ctas = ctas or int(os.environ.get("DLVK_AR_CTAS", "296"))
+            os.environ.get("DLVK_ONE_SHOT_BYTES", str((4 << 20) // max(world, 1))))
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        self.ctas = ctas or int(os.environ.get("DLVK_AR_CTAS", str(6 * sms)))
+        self.push_ctas = int(os.environ.get("DLVK_PUSH_CTAS", str(2 * sms)))
         self.st = optimizer.state(store)
         self._bucket_ids = {}
+        self.algo = algo or os.environ.get("DLVK_AR_ALGO", "auto")
+        if self.algo not in ("auto", "push", "pull"):
+            raise ValueError(f"unknown all-reduce algorithm {self.algo!r}")
+        self._ll = {}  # (start, end) -> LL offset
+        self._ll_used = 0
+        self.ll = None
+        self.ll_cap = 0
+        if world > 1 and os.environ.get("DLVK_AR_LL", "1") != "0":
+            self.ll_cap = (min(n, self.one_shot_bytes // 4 * 4, int(os.environ.get("DLVK_LL_CAP", str(1 << 22))))
+                           + 63) // 64 * 64
+            self.ll = make_symmetric(2 * (world - 1) * self.ll_cap * 8, dev, group)
+        self._push = {}  # (start, end) -> (flag-table row, receive offset)
+        self._recv_used = 0
+        self.recv = self.cflags = None
+        if world > 1 and self.algo == "push":
+            f = recv_factor if recv_factor is not None else float(os.environ.get("DLVK_PUSH_RECV_FACTOR", "2"))
+            per = -(-n // world)
+            self.recv_slot = (int(f * per) + 64 * self.C.comm.PUSH_MAX_BUCKETS + 63) // 64 * 64
+            self.recv = make_symmetric((world - 1) * self.recv_slot * 4, dev, group)
+            self.cflags = make_symmetric(self.C.comm.PUSH_MAX_BUCKETS * self.C.comm.PUSH_MAX_CHUNKS * world * 4,
+                                         dev, group)
         torch.cuda.synchronize(dev)
         dist.barrier(group)
+
+    def _push_slot(self, start: int, end: int):
+        """(flag-table row, receive offset) of a push bucket, or None when the
+        receive buffer or the flag table is full (the bucket then runs pull)."""
+        key = (start, end)
+        if key in self._push:
+            return self._push[key]
+        if self.recv is None or len(self._push) >= self.C.comm.PUSH_MAX_BUCKETS:
+            return None
+        shard = ((end - start + self.world - 1) // self.world + 63) // 64 * 64
+        if self._recv_used + shard > self.recv_slot:
+            return None
+        self._push[key] = (len(self._push), self._recv_used)
+        self._recv_used += shard
+        return self._push[key]
+
+    def _ll_slot(self, start: int, end: int):
+        key = (start, end)
+        if key in self._ll:
+            return self._ll[key]
+        if self.ll is None or self._ll_used + (end - start) > self.ll_cap:
+            return None
+        self._ll[key] = self._ll_used
+        self._ll_used += end - start
+        return self._ll[key]
+
+    def algorithm(self, start: int, end: int) -> str:
+        """The form the bucket [start, end) runs as: ll, one-shot, push or pull."""
+        if (end - start) * 4 <= self.one_shot_bytes or self.world == 1:
+            if self.world > 1 and self._ll_slot(start, end) is not None:
+                return "ll"
+            return "one-shot"
+        if self.algo == "push":
+            if self._push_slot(start, end) is not None:
+                return "push"
+            raise RuntimeError("push all-reduce: receive buffer or flag table full")
+        return "pull"
 
     def begin_step(self) -> None:
         self.C.counter_add(self.epoch, 1)
 
-    def reduce_update(self, start: int, end: int) -> None:
+    def reduce_update(self, start: int, end: int, algo: Optional[str] = None, ctas: Optional[int] = None) -> None:
+        """Launch the fused all-reduce + update of [start, end) on the current
+        stream.  `algo` = "pull" forces the pull two-shot form for a bucket
+        that would run push, "one-shot" the pull one-shot form for one that
+        would run ll, and `ctas` overrides the grid size (both for
+        comparisons)."""
         key = (start, end)
         if key not in self._bucket_ids:
             if len(self._bucket_ids) >= MAX_BUCKETS:
                 raise RuntimeError("too many buckets")
             self._bucket_ids[key] = len(self._bucket_ids)
         b = self._bucket_ids[key]
-        one_shot = (end - start) * 4 <= self.one_shot_bytes
+        chosen = self.algorithm(start, end)
+        if algo == "pull" and chosen == "push":
+            chosen = "pull"
+        if algo == "one-shot" and chosen == "ll":
+            chosen = "one-shot"
+        algo = chosen
         st = self.st
+        if algo == "ll":
+            self.C.comm.fused_allreduce_optimizer_ll(
+                self.grad_buf, self.value_buf, self.ll, start, end, self._ll[key], self.ll_cap, self.store.master,
+                st.m, st.v, st.hyper, self.opt.kind, self.epoch, self.world, self.rank, not self.bf16,
+                1 if self.bf16 else 0, ctas or self.ctas, BUDGET_S)
+            return
+        if algo == "push":
+            row, off = self._push[key]
+            self.C.comm.fused_allreduce_optimizer_push(
+                self.grad_buf, self.value_buf, self.flag_buf, self.recv, self.cflags, self.counters, b, row, start,
+                end, off, self.recv_slot, self.store.master, st.m, st.v, st.hyper, self.opt.kind, self.epoch,
+                self.world, self.rank, not self.bf16, 0, 1 if self.bf16 else 0, ctas or self.push_ctas, BUDGET_S)
+            return
+        one_shot = algo == "one-shot"
         self.C.comm.fused_allreduce_optimizer(
             self.grad_buf, self.value_buf, self.flag_buf, self.counters, b, start, end, self.store.master,
             st.m, st.v, st.hyper, self.opt.kind, self.epoch, self.world, self.rank, one_shot, not self.bf16,
-            0, 1 if self.bf16 else 0, self.ctas, BUDGET_S)
+            0, 1 if self.bf16 else 0, ctas or self.ctas, BUDGET_S)
 
     def close(self) -> None:
         torch.cuda.synchronize(self.dev)

@@ -140,7 +140,7 @@ class DataParallel:
         w = self.world
         for b in self.buckets:
             n = b.numel
-            if n * 4 <= self.fused.one_shot_bytes:
+            if self.fused.algorithm(b.start, b.end) in ("ll", "one-shot"):
                 continue
             shard = ((n + w - 1) // w + 63) // 64 * 64
             for buf in (self.store.master, st.m, st.v):

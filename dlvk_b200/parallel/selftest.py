@@ -28,6 +28,8 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--bucket-mb", type=float, default=0.05)
     ap.add_argument("--one-shot-bytes", type=int, default=None)
+    ap.add_argument("--ll", type=int, default=1, help="0: small buckets use the pull one-shot form, not LL")
+    ap.add_argument("--algo", default=None, choices=["auto", "push", "pull"], help="two-shot form of the fused path")
     ap.add_argument("--cpu", action="store_true")
     ap.add_argument("--fail-rank", type=int, default=-1,
                     help="fault injection on the host: this rank exits between steps")
@@ -57,6 +59,9 @@ def main() -> int:
         device = f"cuda:{local}"
     if args.one_shot_bytes is not None:
         os.environ["DLVK_ONE_SHOT_BYTES"] = str(args.one_shot_bytes)
+    if args.algo is not None:
+        os.environ["DLVK_AR_ALGO"] = args.algo
+    os.environ["DLVK_AR_LL"] = str(args.ll)
 
     def build(dev):
         if args.model == "mlp":

@@ -13,14 +13,20 @@ def _need(n):
         pytest.skip(f"needs {n} GPUs")
 
 
-@pytest.mark.parametrize("model,dtype,oneshot,opt", [("mlp", "fp32", 1 << 30, "adam"), ("mlp", "fp32", 0, "adam"),
-                                                     ("transformer", "bf16", 1 << 30, "sgd"),
-                                                     ("transformer", "bf16", 0, "sgd"),
-                                                     ("transformer", "fp32", 0, "adam")])
-def test_fused_dp_matches_full_batch(model, dtype, oneshot, opt):
+@pytest.mark.parametrize("model,dtype,oneshot,opt,algo", [("mlp", "fp32", 1 << 30, "adam", "auto"),
+                                                          ("mlp", "fp32", 1 << 30, "adam", "noll"),
+                                                          ("transformer", "bf16", 1 << 30, "sgd", "noll"),
+                                                          ("mlp", "fp32", 0, "adam", "push"),
+                                                          ("mlp", "fp32", 0, "adam", "pull"),
+                                                          ("transformer", "bf16", 1 << 30, "sgd", "auto"),
+                                                          ("transformer", "bf16", 0, "sgd", "push"),
+                                                          ("transformer", "bf16", 0, "sgd", "pull"),
+                                                          ("transformer", "fp32", 0, "adam", "push")])
+def test_fused_dp_matches_full_batch(model, dtype, oneshot, opt, algo):
     _need(2)
+    extra = ["--ll", "0"] if algo == "noll" else ["--algo", algo]
     rc, lines, log = run_selftest(2, ["--mode", "fused", "--model", model, "--dtype", dtype,
-                                      "--one-shot-bytes", str(oneshot), "--opt", opt])
+                                      "--one-shot-bytes", str(oneshot), "--opt", opt] + extra)
     assert rc == 0, log[-4000:]
     assert len(lines) == 2 and all(l["ok"] for l in lines), lines
 

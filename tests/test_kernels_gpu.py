@@ -66,6 +66,26 @@ def test_softmax_ce(cols, dtype):
     torch.testing.assert_close(sm.float(), torch.softmax(x.float(), -1), atol=tol, rtol=tol * 10)
 
 
+@pytest.mark.parametrize("cols", [8000, 32000])
+def test_softmax_ce_vocab_inplace_ignored(cols):
+    """bf16 vocabulary-sized rows (register-resident kernel), gradient written
+    over the logits, one ignored row."""
+    C = _C()
+    rows = 19
+    x = (torch.randn(rows, cols, device="cuda") * 3).bfloat16()
+    lab = torch.randint(0, cols, (rows,), device="cuda", dtype=torch.int32)
+    lab[3] = -1
+    xf = x.float().requires_grad_(True)
+    keep = lab >= 0
+    ref = torch.nn.functional.cross_entropy(xf, lab.long().clamp(min=0), reduction="none") * keep
+    ref.sum().backward()
+    loss_rows, dl = C.softmax_ce(x, lab, 1.0, in_place=True)
+    assert dl.data_ptr() == x.data_ptr()
+    torch.testing.assert_close(loss_rows, ref.detach(), atol=0.2, rtol=2e-2)
+    torch.testing.assert_close(dl.float(), xf.grad, atol=2e-2, rtol=0.2)
+    assert float(dl[3].float().abs().max()) == 0.0
+
+
 def test_softmax_bwd_and_losses():
     C = _C()
     x = torch.randn(64, 100, device="cuda", requires_grad=True)

@@ -115,6 +115,10 @@ def test_layernorm(dtype):
     close(dx, xr.grad, tol * 2)
     close(dgam, gr.grad, tol * 2)
     close(dbet, br.grad, tol * 2)
+    dres = torch.randn_like(yr).to(dtype)
+    dx2 = C.layernorm_bwd(x, gamma, mean, rstd, g, dgam, dbet, True, dres)
+    close(dx2, xr.grad + dres.float(), tol * 2)
+    close(dgam, 2 * gr.grad, tol * 2)
 
 
 def test_dropout_matches_cpu_oracle():
