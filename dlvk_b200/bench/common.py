@@ -17,22 +17,28 @@ def flush_l2(nbytes: int = 256 << 20) -> None:
 
 
 def time_fn(fn, iters: int = 20, warmup: int = 3, flush: bool = True) -> float:
-    """Median device time of `fn()` in milliseconds."""
+    """Median device time of `fn()` in milliseconds.
+
+    Every timed iteration is enqueued before any is waited on, behind a
+    ~2 ms spin kernel, so the host runs ahead of the GPU and the events
+    bracket device work only (no host launch latency between them).  With
+    `flush`, a 256 MB write before each iteration starts it with a cold L2.
+    """
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
-    times = []
-    for _ in range(iters):
+    if flush:
+        flush_l2()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    torch.cuda._sleep(4_000_000)
+    for s, e in ev:
         if flush:
             flush_l2()
-        s = torch.cuda.Event(enable_timing=True)
-        e = torch.cuda.Event(enable_timing=True)
         s.record()
         fn()
         e.record()
-        e.synchronize()
-        times.append(s.elapsed_time(e))
-    times.sort()
+    torch.cuda.synchronize()
+    times = sorted(s.elapsed_time(e) for s, e in ev)
     return times[len(times) // 2]
 
 

@@ -41,7 +41,8 @@ def main():
     db = torch.zeros(D, device="cuda")
     rows = []
 
-    def report(name, t, nbytes):
+    def report(name, t_ms, nbytes):
+        t = t_ms * 1e-3
         rows.append({"kernel": name, "us": round(t * 1e6, 2), "gbs": round(nbytes / t / 1e9, 1),
                      "frac_of_measured_hbm": round(nbytes / t / hbm, 3)})
 

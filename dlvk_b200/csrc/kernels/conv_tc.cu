@@ -180,6 +180,9 @@ __global__ void __launch_bounds__(IG_THREADS, 1)
           if (!p.transposed) {
             sh = bh + dh;
             sw = bw + dw;
+          } else if (p.stride == 1) {  // uniform branch: no division on the common path
+            sh = bh - dh;
+            sw = bw - dw;
           } else {
             const int th = bh - dh, tw = bw - dw;
             ok = ok && th >= 0 && tw >= 0 && (th % p.stride) == 0 && (tw % p.stride) == 0;
