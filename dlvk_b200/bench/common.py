@@ -9,11 +9,13 @@ _FLUSH = None
 
 
 def flush_l2(nbytes: int = 256 << 20) -> None:
-    """Overwrite a buffer larger than the 126 MB L2 so the next launch starts cold."""
+    """Evict L2 (126 MB on B200) by reading a larger buffer, so the next
+    launch starts cold.  A read leaves clean lines behind; a write would leave
+    dirty ones whose write-back the timed kernel would then pay for."""
     global _FLUSH
     if _FLUSH is None or _FLUSH.numel() * 4 < nbytes:
-        _FLUSH = torch.empty(nbytes // 4, dtype=torch.float32, device="cuda")
-    _FLUSH.fill_(1.0)
+        _FLUSH = torch.zeros(nbytes // 4, dtype=torch.float32, device="cuda")
+    _FLUSH.amax()
 
 
 def time_fn(fn, iters: int = 20, warmup: int = 3, flush: bool = True) -> float:

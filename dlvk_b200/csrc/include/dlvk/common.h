@@ -11,6 +11,7 @@
 #include <stdexcept>
 #include <string>
 #include <atomic>
+#include <utility>
 
 namespace dlvk {
 
@@ -55,8 +56,39 @@ void note_launch(uint64_t n = 1);
     DLVK_CUDA_CHECK(cudaGetLastError());                                         \
   } while (0)
 
+namespace dlvk {
+// Programmatic dependent launch (sm_90+).  A kernel launched through
+// launch_pdl() may begin (prologue: barrier init, TMEM allocation, tensor-map
+// prefetch) while the previous kernel in the stream is still finishing; it
+// must execute pdl_wait() before its first access to global memory, which
+// returns once the previous grid has completed and its writes are visible.
+// The persistent tensor-core kernels call pdl_trigger() when a CTA has
+// finished its work, so their successor's prologue overlaps the tail.
+// Opt-in with DLVK_PDL=1; otherwise the launches are ordinary
+// stream-serialised ones and the waits return at once.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  DLVK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+}
+}  // namespace dlvk
+
 #ifdef __CUDACC__
 namespace dlvk {
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ float to_f32(float x) { return x; }
 __device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }

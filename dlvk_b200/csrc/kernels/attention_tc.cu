@@ -131,6 +131,7 @@ __global__ void __launch_bounds__(192, 1) flash_fwd_kernel(const __grid_constant
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;  // S0: cols 0..127, S1: 128..255, O: 256..319
+  pdl_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -324,6 +325,7 @@ __global__ void __launch_bounds__(192, 1) flash_fwd_kernel(const __grid_constant
   }
   tc_fence_before();
   __syncthreads();
+  pdl_trigger();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tbase, 512);
@@ -414,6 +416,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
   tc_fence_after();
   // TMEM: S^T 0..127, dP^T 128..255, dV 256..319, dK 320..383, dQ 384..447
   const uint32_t tbase = *tmem_slot;
+  pdl_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -621,6 +624,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
   }
   tc_fence_before();
   __syncthreads();
+  pdl_trigger();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tbase, 512);
@@ -632,6 +636,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
 // consecutive rows).
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
                                   float* __restrict__ delta, int B, int S, int H) {
+  pdl_wait();
   const int64_t total = (int64_t)B * S * H;
   for (int64_t w = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; w < total; w += (int64_t)gridDim.x * blockDim.x) {
     const uint4* a = reinterpret_cast<const uint4*>(o + w * FD);
@@ -663,6 +668,7 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __n
 // dqkv[:, :, 0] = bf16(dq_acc * scale)
 __global__ void attn_dq_finish_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dqkv, int64_t rows,
                                       int E, float scale) {
+  pdl_wait();
   const int64_t n4 = rows * E / 4;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
     const float4 v = reinterpret_cast<const float4*>(acc)[i];
@@ -696,7 +702,7 @@ void flash_attention_fwd(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* ls
   }
   const int items = B * H * (S / FT);
   int grid = std::min(items, max_ctas > 0 ? max_ctas : tmap::sm_count());
-  flash_fwd_kernel<<<grid, 192, FWD_SMEM, s>>>(tm, p);
+  launch_pdl(flash_fwd_kernel, dim3(grid), dim3(192), FWD_SMEM, s, tm, p);
   DLVK_POST_LAUNCH();
 }
 
@@ -709,8 +715,8 @@ void flash_attention_bwd(const __nv_bfloat16* qkv, const __nv_bfloat16* out, con
   const int64_t rows = (int64_t)B * S;
   {
     const int64_t n = rows * H;
-    attn_delta_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 148 * 8), 256, 0, s>>>(out, dout, delta, B, S,
-                                                                                            H);
+    launch_pdl(attn_delta_kernel, dim3((unsigned)std::min<int64_t>((n + 255) / 256, 148 * 8)), dim3(256), 0, s, out,
+               dout, delta, B, S, H);
     DLVK_POST_LAUNCH();
   }
   DLVK_CUDA_CHECK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * E, s));
@@ -735,11 +741,11 @@ void flash_attention_bwd(const __nv_bfloat16* qkv, const __nv_bfloat16* out, con
   }
   const int items = B * H * (S / FT);
   const int grid = std::min(items, max_ctas > 0 ? max_ctas : tmap::sm_count());
-  flash_bwd_kernel<<<grid, BWD_THREADS, BWD_SMEM, s>>>(tq, td, tdq, p);
+  launch_pdl(flash_bwd_kernel, dim3(grid), dim3(BWD_THREADS), BWD_SMEM, s, tq, td, tdq, p);
   DLVK_POST_LAUNCH();
   const int64_t n4 = rows * E / 4;
-  attn_dq_finish_kernel<<<(unsigned)std::min<int64_t>((n4 + 255) / 256, 148 * 16), 256, 0, s>>>(dq_acc, dqkv, rows, E,
-                                                                                                 scale);
+  launch_pdl(attn_dq_finish_kernel, dim3((unsigned)std::min<int64_t>((n4 + 255) / 256, 148 * 16)), dim3(256), 0, s,
+             (const float*)dq_acc, dqkv, rows, E, scale);
   DLVK_POST_LAUNCH();
 }
 

@@ -309,6 +309,7 @@ __global__ void __launch_bounds__(320, 1)
   if (PAIR) cluster_sync();  // the peer's barriers are initialised before any remote signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the previous kernel's outputs (our operands) are complete from here on
 
   if (warp == 0) {
     if (lane == 0 && PAIR) {
@@ -316,11 +317,13 @@ __global__ void __launch_bounds__(320, 1)
       uint32_t phase = 0;
       for (int t = t0; t < num_tiles; t += tstep) {
         int tm, tn, b;
-        tile_coords(t, p, tm, tn, b);
+        const int sp = t / tiles_per_split;
+        tile_coords(t - sp * tiles_per_split, p, tm, tn, b);
         const int bo = b / p.batch2, bi = b - bo * p.batch2;
         const int arow = tm * TILE_M + (int)rank * BM;
         const int bcol = tn * BN + (int)rank * (BN / 2);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int kb0 = sp * p.kb_per_split, kb1 = min(num_kb, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.err)) goto producer_done_pair;
           uint8_t* sA = smem + stage * C::STAGE_BYTES;
           uint8_t* sB = sA + C::A_BYTES;
@@ -397,7 +400,9 @@ __global__ void __launch_bounds__(320, 1)
           tc_fence_after();
           const uint32_t d = tmem_base + (uint32_t)(acc * BN);
           bool ok = true;
-          for (int kb = 0; kb < num_kb; ++kb) {
+          const int sp = t / tiles_per_split;
+          const int kb0 = sp * p.kb_per_split, kb1 = min(num_kb, kb0 + p.kb_per_split);
+          for (int kb = kb0; kb < kb1; ++kb) {
             if (!mbar_wait(&full[stage], phase, p.err)) { ok = false; break; }
             tc_fence_after();
             const uint32_t aBase = smem_u32(smem + stage * C::STAGE_BYTES);
@@ -408,7 +413,7 @@ __global__ void __launch_bounds__(320, 1)
                                          : make_sw128_desc(aBase + k * 32, 16, 1024);
               const uint64_t bd = p.b_mn ? make_sw128_desc(bBase + k * 2048, 8192, 1024)
                                          : make_sw128_desc(bBase + k * 32, 16, 1024);
-              mma_f16_pair(d, ad, bd, idesc, (kb != 0 || k != 0) ? 1u : 0u);
+              mma_f16_pair(d, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
             }
             const uint32_t eb = smem_u32(&empty[stage]);
             mma_commit_pair(eb);
@@ -582,6 +587,7 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_before();
   __syncthreads();
   if (PAIR) cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+  pdl_trigger();             // this CTA's work is done: the next kernel may start launching
   if (warp == 1) {
     tc_fence_after();
     if (PAIR) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
@@ -644,7 +650,7 @@ void launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, 
   }
   const int tiles = p.tiles_m * p.tiles_n * p.batch * p.splits;
   int grid = std::min(tiles, max_ctas > 0 ? max_ctas : sm_count());
-  gemm_tc_kernel<BN><<<grid, 320, C::SMEM, s>>>(ta, tb, p);
+  launch_pdl(gemm_tc_kernel<BN, false>, dim3(grid), dim3(320), C::SMEM, s, ta, tb, p);
   DLVK_POST_LAUNCH();
 }
 
@@ -656,16 +662,18 @@ void launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams
   int dev = 0;
   DLVK_CUDA_CHECK(cudaGetDevice(&dev));
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.blockDim = dim3(320, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = s;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 1;  // occupancy query: cluster shape only
   if (max_pairs[dev] == 0) {
     DLVK_CUDA_CHECK(
         cudaFuncSetAttribute(gemm_tc_kernel<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
@@ -674,10 +682,11 @@ void launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams
     DLVK_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<256, true>, &cfg));
     max_pairs[dev] = std::max(1, n);
   }
-  const int tiles = p.tiles_m * p.tiles_n * p.batch;
+  const int tiles = p.tiles_m * p.tiles_n * p.batch * p.splits;
   int pairs = std::min(tiles, max_pairs[dev]);
   if (max_ctas > 0) pairs = std::max(1, std::min(pairs, max_ctas / 2));
   cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.numAttrs = 2;
   DLVK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<256, true>, ta, tb, p));
   DLVK_POST_LAUNCH();
 }
@@ -719,28 +728,44 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
 // ~8 TFLOP/s at BN = 256 (15% less at BN = 128, which reloads A twice as
 // often per FLOP), whole waves of persistent CTAs, and for split-K the fp32
 // workspace write + read at ~5 TB/s plus one extra launch.
-void choose_tiling(const GemmArgs& a, int sms, int& BN, int& splits) {
+// Picks the tile shape, the split-K factor and whether the CTA-pair kernel
+// runs, by a wave model: time = waves x (per-unit MMA time at an efficiency
+// measured for that tile shape) + the split-K partial traffic.  Pair units
+// are 256 x 256 tiles on sms/2 pairs (about 1.2x the single-CTA 128 x 256
+// rate on B200); single units are 128 x BN on sms CTAs.
+void choose_tiling(const GemmArgs& a, int sms, int& BN, int& splits, bool& pair) {
   const int64_t kbs = (a.K + BK - 1) / BK;
-  const int64_t tm = (a.M + BM - 1) / BM;
   const double sm_flops = 8.1e12;
   double best = 1e300;
   BN = 256;
   splits = 1;
-  for (int bn : {256, 128}) {
-    if (bn == 256 && a.N < 256) continue;
-    const double eff = bn == 256 ? 1.0 : 0.85;
-    const int64_t tiles = tm * ((a.N + bn - 1) / bn) * a.batch * a.batch2;
+  pair = false;
+  const bool pair_ok = gemm_tc_pair_enabled() && a.M >= 256 && sms >= 2;
+  struct Cand {
+    bool pair;
+    int bn;
+    double eff;
+  };
+  const Cand cands[] = {{true, 256, 1.2}, {false, 256, 1.0}, {false, 128, 0.85}};
+  for (const Cand& c : cands) {
+    if (c.pair && !pair_ok) continue;
+    if (c.bn == 256 && a.N < 256) continue;
+    const int64_t tile_m = c.pair ? 2 * BM : BM;
+    const int64_t tiles = ((a.M + tile_m - 1) / tile_m) * ((a.N + c.bn - 1) / c.bn) * a.batch * a.batch2;
+    const int64_t slots = c.pair ? sms / 2 : sms;
     for (int sp : {1, 2, 3, 4, 6, 8}) {
       if (sp > 1 && kbs / sp < 8) break;
       const int64_t units = tiles * sp;
-      const int64_t waves = (units + sms - 1) / sms;
-      const double unit_s = (double)BM * bn * BK * 2.0 * ((kbs + sp - 1) / sp) / (sm_flops * eff);
+      const int64_t waves = (units + slots - 1) / slots;
+      const double unit_s = (double)tile_m * c.bn * BK * 2.0 * ((kbs + sp - 1) / sp) /
+                            (sm_flops * (c.pair ? 2 : 1) * c.eff);
       double t = waves * unit_s;
       if (sp > 1) t += (double)sp * a.M * a.N * a.batch * a.batch2 * 8.0 / 5e12 + 5e-6;
       if (t < best * 0.97) {
         best = t;
-        BN = bn;
+        BN = c.bn;
         splits = sp;
+        pair = c.pair;
       }
     }
   }
@@ -784,11 +809,10 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
   const bool a_k = (a.sak == 1);
   const bool b_k = (a.sbk == 1);
   int BN = 256, splits = 1;
-  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits);
+  bool pair = false;
+  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits, pair);
   if (workspace == nullptr || workspace_floats < (int64_t)splits * a.M * a.N * a.batch * a.batch2) splits = 1;
-  // The CTA-pair kernel (256 x 256 tiles, half the B traffic per CTA) takes
-  // every bf16 GEMM the single-CTA model would run unsplit with 256-wide tiles.
-  const bool pair = gemm_tc_pair_enabled() && splits == 1 && BN == 256 && a.M >= 256 && max_ctas != 1;
+  pair = pair && max_ctas != 1;
   // Unused batch levels get a harmless stride (a multiple of 16 bytes).
   auto pick = [](int64_t cnt, int64_t stride, uint64_t dflt) { return cnt > 1 ? (uint64_t)stride : dflt; };
   CUtensorMap ta, tb;
@@ -866,7 +890,8 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
     p.R = nullptr;
     p.Mk = nullptr;
     p.act = ACT_NONE;
-    if (BN == 256) launch_tc<256>(ta, tb, p, max_ctas, s);
+    if (pair) launch_tc_pair(ta, tb, p, max_ctas, s);
+    else if (BN == 256) launch_tc<256>(ta, tb, p, max_ctas, s);
     else launch_tc<128>(ta, tb, p, max_ctas, s);
     const int g = (int)std::min<int64_t>((per + 255) / 256, 148 * 16);
     if (out_dt == DType::F32) splitk_reduce_kernel<float><<<g, 256, 0, s>>>(workspace, splits, per, a);
@@ -894,7 +919,8 @@ void gemm_tc_set_pair(bool on) { pair_flag() = on ? 1 : 0; }
 
 int64_t gemm_tc_workspace_floats(const GemmArgs& a, int max_ctas) {
   int BN = 256, splits = 1;
-  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits);
+  bool pair = false;
+  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits, pair);
   return splits > 1 ? (int64_t)splits * a.M * a.N * a.batch * a.batch2 : 0;
 }
 

@@ -16,6 +16,7 @@
 // masks on every replay.
 #include "dlvk/common.h"
 #include "dlvk/kernels.h"
+#include "dlvk/sm100.h"
 
 namespace dlvk {
 namespace {
@@ -234,54 +235,58 @@ __global__ void ln_fwd_kernel(const T* __restrict__ x, const float* __restrict__
 // 16 bytes; exact two-pass mean / variance from registers, 16-byte loads and
 // stores, gamma / beta as float4.
 template <typename T, int NV>
-__global__ void ln_fwd_vec_kernel(const T* __restrict__ x, const float* __restrict__ gamma,
-                                  const float* __restrict__ beta, T* __restrict__ y, float* __restrict__ mean,
-                                  float* __restrict__ rstd, int64_t rows, int D, float eps) {
+__global__ void __launch_bounds__(256, 4) ln_fwd_vec_kernel(const T* __restrict__ x, const float* __restrict__ gamma,
+                                                            const float* __restrict__ beta, T* __restrict__ y,
+                                                            float* __restrict__ mean, float* __restrict__ rstd,
+                                                            int64_t rows, int D, float eps) {
+  // One warp per row; the row stays in registers as raw 16-byte vectors and
+  // is converted on each of the three passes (mean, variance, output), which
+  // keeps registers low enough for four blocks (32 warps) per SM.
+  pdl_wait();
   constexpr int EPV = 16 / sizeof(T);
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+    uint4 u[NV];
     const uint4* xr = reinterpret_cast<const uint4*>(x + r * D);
-    float v[NV][EPV];
 #pragma unroll
-    for (int k = 0; k < NV; ++k) {
-      const uint4 u = xr[k * 32 + lane];
-      const T* e = reinterpret_cast<const T*>(&u);
-#pragma unroll
-      for (int j = 0; j < EPV; ++j) v[k][j] = to_f32(e[j]);
-    }
+    for (int k = 0; k < NV; ++k) u[k] = xr[k * 32 + lane];
     float a = 0.f;
 #pragma unroll
-    for (int k = 0; k < NV; ++k)
+    for (int k = 0; k < NV; ++k) {
+      const T* e = reinterpret_cast<const T*>(&u[k]);
 #pragma unroll
-      for (int j = 0; j < EPV; ++j) a += v[k][j];
+      for (int j = 0; j < EPV; ++j) a += to_f32(e[j]);
+    }
     const float mu = warp_sum(a) / D;
     float b = 0.f;
 #pragma unroll
-    for (int k = 0; k < NV; ++k)
+    for (int k = 0; k < NV; ++k) {
+      const T* e = reinterpret_cast<const T*>(&u[k]);
 #pragma unroll
       for (int j = 0; j < EPV; ++j) {
-        const float d0 = v[k][j] - mu;
+        const float d0 = to_f32(e[j]) - mu;
         b += d0 * d0;
       }
+    }
     const float rs = rsqrtf(warp_sum(b) / D + eps);
     uint4* yr = reinterpret_cast<uint4*>(y + r * D);
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int d0 = (k * 32 + lane) * EPV;
-      float gv[EPV], bv[EPV];
+      const T* e = reinterpret_cast<const T*>(&u[k]);
+      uint4 o;
+      T* eo = reinterpret_cast<T*>(&o);
 #pragma unroll
       for (int j = 0; j < EPV; j += 4) {
         const float4 g4 = gamma ? *reinterpret_cast<const float4*>(gamma + d0 + j) : make_float4(1.f, 1.f, 1.f, 1.f);
         const float4 b4 = beta ? *reinterpret_cast<const float4*>(beta + d0 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
-        gv[j] = g4.x; gv[j + 1] = g4.y; gv[j + 2] = g4.z; gv[j + 3] = g4.w;
-        bv[j] = b4.x; bv[j + 1] = b4.y; bv[j + 2] = b4.z; bv[j + 3] = b4.w;
+        eo[j] = from_f32<T>((to_f32(e[j]) - mu) * rs * g4.x + b4.x);
+        eo[j + 1] = from_f32<T>((to_f32(e[j + 1]) - mu) * rs * g4.y + b4.y);
+        eo[j + 2] = from_f32<T>((to_f32(e[j + 2]) - mu) * rs * g4.z + b4.z);
+        eo[j + 3] = from_f32<T>((to_f32(e[j + 3]) - mu) * rs * g4.w + b4.w);
       }
-      uint4 u;
-      T* e = reinterpret_cast<T*>(&u);
-#pragma unroll
-      for (int j = 0; j < EPV; ++j) e[j] = from_f32<T>((v[k][j] - mu) * rs * gv[j] + bv[j]);
-      yr[k * 32 + lane] = u;
+      yr[k * 32 + lane] = o;
     }
     if (lane == 0) {
       if (mean) mean[r] = mu;
@@ -435,12 +440,128 @@ __global__ void __launch_bounds__(256) ln_bwd_warp_kernel(const T* __restrict__ 
   }
 }
 
+// Deep-pipelined variant for bf16 rows of 256 x NV elements (D = 1024 with
+// NV = 4): each warp streams its rows through a 3-slot shared-memory ring
+// with cp.async (x, dy and the residual gradient of three rows in flight per
+// warp, 8 warps and one CTA per SM), reading the row back from shared memory
+// in both passes, so registers hold only the dgamma / dbeta accumulators.
+// Every lane reads back only the 16-byte vectors it copied itself, so
+// cp.async.wait_group alone orders the copy before the read.
+template <int NV, bool RES>
+__global__ void __launch_bounds__(256, 1) ln_bwd_ring_kernel(const __nv_bfloat16* __restrict__ x,
+                                                             const float* __restrict__ gamma,
+                                                             const float* __restrict__ mean,
+                                                             const float* __restrict__ rstd,
+                                                             const __nv_bfloat16* __restrict__ dy,
+                                                             __nv_bfloat16* __restrict__ dx, float* __restrict__ part,
+                                                             int64_t rows, int D,
+                                                             const __nv_bfloat16* __restrict__ dres) {
+  constexpr int EPV = 8, RING = 3, NT = RES ? 3 : 2, RV = NV * 32;  // 16-byte vectors per tensor row
+  pdl_wait();
+  extern __shared__ uint4 sring[];                                   // [8][RING][NT][RV]
+  float* sgam = reinterpret_cast<float*>(sring + 8 * RING * NT * RV);
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) sgam[d] = gamma ? gamma[d] : 1.f;
+  __syncthreads();
+  uint4* ring = sring + (size_t)w * RING * NT * RV;
+  const int64_t step = (int64_t)gridDim.x * 8;
+  const int64_t r0 = (int64_t)blockIdx.x * 8 + w;
+  auto issue = [&](int64_t row, int slot) {
+    if (row < rows) {
+      uint4* b = ring + slot * NT * RV;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int v = lane + 32 * i;
+        sm100::cp_async_16(sm100::smem_u32(b + v), reinterpret_cast<const uint4*>(x + row * D) + v, 16);
+        sm100::cp_async_16(sm100::smem_u32(b + RV + v), reinterpret_cast<const uint4*>(dy + row * D) + v, 16);
+        if (RES)
+          sm100::cp_async_16(sm100::smem_u32(b + 2 * RV + v), reinterpret_cast<const uint4*>(dres + row * D) + v, 16);
+      }
+    }
+    sm100::cp_async_commit();  // empty groups keep the count aligned
+  };
+#pragma unroll
+  for (int k = 0; k < RING; ++k) issue(r0 + k * step, k);
+  float adg[NV][EPV], adb[NV][EPV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int k = 0; k < EPV; ++k) adg[i][k] = adb[i][k] = 0.f;
+  const float invD = 1.f / D;
+  int slot = 0;
+  for (int64_t r = r0; r < rows; r += step) {
+    sm100::cp_async_wait<RING - 1>();
+    const uint4* b = ring + slot * NT * RV;
+    const float mu = mean[r], rs = rstd[r];
+    float a = 0.f, bb = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const uint4 ux = b[lane + 32 * i], ug = b[RV + lane + 32 * i];
+      const __nv_bfloat16* ex = reinterpret_cast<const __nv_bfloat16*>(&ux);
+      const __nv_bfloat16* eg = reinterpret_cast<const __nv_bfloat16*>(&ug);
+#pragma unroll
+      for (int k = 0; k < EPV; ++k) {
+        const float xh = (__bfloat162float(ex[k]) - mu) * rs;
+        const float g = __bfloat162float(eg[k]);
+        const float gg = g * sgam[(lane + 32 * i) * EPV + k];
+        a += gg;
+        bb += gg * xh;
+        adg[i][k] += g * xh;
+        adb[i][k] += g;
+      }
+    }
+    a = warp_sum(a) * invD;
+    bb = warp_sum(bb) * invD;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const uint4 ux = b[lane + 32 * i], ug = b[RV + lane + 32 * i];
+      uint4 ur = make_uint4(0, 0, 0, 0);
+      if (RES) ur = b[2 * RV + lane + 32 * i];
+      const __nv_bfloat16* ex = reinterpret_cast<const __nv_bfloat16*>(&ux);
+      const __nv_bfloat16* eg = reinterpret_cast<const __nv_bfloat16*>(&ug);
+      const __nv_bfloat16* er = reinterpret_cast<const __nv_bfloat16*>(&ur);
+      uint4 o;
+      __nv_bfloat16* eo = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+      for (int k = 0; k < EPV; ++k) {
+        const float xh = (__bfloat162float(ex[k]) - mu) * rs;
+        float v = rs * (__bfloat162float(eg[k]) * sgam[(lane + 32 * i) * EPV + k] - a - xh * bb);
+        if (RES) v += __bfloat162float(er[k]);
+        eo[k] = __float2bfloat16_rn(v);
+      }
+      reinterpret_cast<uint4*>(dx + r * D)[lane + 32 * i] = o;
+    }
+    issue(r + RING * step, slot);  // this lane has read its vectors of the slot
+    slot = slot + 1 == RING ? 0 : slot + 1;
+  }
+  sm100::cp_async_wait<0>();
+  __syncthreads();
+  float* sp = reinterpret_cast<float*>(sring);  // the ring is free: [8][2*D] partials
+  float* mine = sp + (int64_t)w * 2 * D;
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int k = 0; k < EPV; ++k) {
+      const int col = (lane + 32 * i) * EPV + k;
+      mine[col] = adg[i][k];
+      mine[D + col] = adb[i][k];
+    }
+  __syncthreads();
+  for (int d = threadIdx.x; d < 2 * D; d += blockDim.x) {
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc += sp[(int64_t)i * 2 * D + d];
+    part[(int64_t)blockIdx.x * 2 * D + d] = acc;
+  }
+}
+
 // Sums the per-block partials: block = 32 columns x 16 row groups, each
 // thread with four independent accumulators, combined in a fixed order
 // through shared memory.
 __global__ void __launch_bounds__(512) ln_bwd_final_kernel(const float* __restrict__ part, int blocks, int D,
                                                            float* __restrict__ dgamma, float* __restrict__ dbeta,
                                                            int accumulate) {
+  pdl_wait();
   __shared__ float sm[16][33];
   const int d = blockIdx.x * 32 + threadIdx.x;
   float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
@@ -571,11 +692,11 @@ void layernorm_fwd(DType dt, const void* x, const float* gamma, const float* bet
   const bool al = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
                     reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) & 15) == 0;
   if (al && (nv == 1 || nv == 2 || nv == 4 || nv == 8)) {
-    const unsigned g = (unsigned)std::max<int64_t>(1, std::min<int64_t>((rows + 7) / 8, 148 * 8));
+    const unsigned g = (unsigned)std::max<int64_t>(1, std::min<int64_t>((rows + 7) / 8, 148 * 4));
     DLVK_DISPATCH_FB(dt, "layernorm_fwd", {
       auto kern = nv == 1 ? ln_fwd_vec_kernel<T, 1>
                           : (nv == 2 ? ln_fwd_vec_kernel<T, 2> : (nv == 4 ? ln_fwd_vec_kernel<T, 4> : ln_fwd_vec_kernel<T, 8>));
-      kern<<<g, 256, 0, s>>>((const T*)x, gamma, beta, (T*)y, mean, rstd, rows, D, eps);
+      launch_pdl(kern, dim3(g), dim3(256), 0, s, (const T*)x, gamma, beta, (T*)y, mean, rstd, rows, D, eps);
     });
     DLVK_POST_LAUNCH();
     return;
@@ -593,6 +714,35 @@ void layernorm_bwd(DType dt, const void* x, const float* gamma, const float* mea
                    void* dx, float* dgamma, float* dbeta, bool accumulate, int64_t rows, int D, float* scratch,
                    cudaStream_t s, const void* dres) {
   const int blocks = layernorm_bwd_blocks(rows);
+  if (dt == DType::BF16 && D % 256 == 0 && (D / 256 == 4 || D / 256 == 2 || D / 256 == 1)) {
+    const bool al = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dy) |
+                      reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(dres)) & 15) == 0;
+    const int nv = D / 256;
+    const int nt = dres ? 3 : 2;
+    const size_t ring = (size_t)8 * 3 * nt * nv * 32 * 16;  // reused for the [8][2D] fp32 partials
+    const size_t smem = ring + (size_t)D * 4;
+    if (al && ring >= (size_t)8 * 2 * D * 4 && smem <= 200 * 1024) {
+      auto launch = [&](auto kern) {
+        DLVK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        launch_pdl(kern, dim3(blocks), dim3(256), smem, s, (const __nv_bfloat16*)x, gamma, mean, rstd,
+                   (const __nv_bfloat16*)dy, (__nv_bfloat16*)dx, scratch, rows, D, (const __nv_bfloat16*)dres);
+      };
+      if (dres) {
+        if (nv == 4) launch(ln_bwd_ring_kernel<4, true>);
+        else if (nv == 2) launch(ln_bwd_ring_kernel<2, true>);
+        else launch(ln_bwd_ring_kernel<1, true>);
+      } else {
+        if (nv == 4) launch(ln_bwd_ring_kernel<4, false>);
+        else if (nv == 2) launch(ln_bwd_ring_kernel<2, false>);
+        else launch(ln_bwd_ring_kernel<1, false>);
+      }
+      DLVK_POST_LAUNCH();
+      launch_pdl(ln_bwd_final_kernel, dim3((2 * D + 31) / 32), dim3(32, 16), 0, s, (const float*)scratch, blocks, D,
+                 dgamma, dbeta, accumulate ? 1 : 0);
+      DLVK_POST_LAUNCH();
+      return;
+    }
+  }
   {
     // Register-resident path: D a multiple of 32 lanes x 16-byte vectors.
     const int epv = dt == DType::F32 ? 4 : 8;

@@ -184,17 +184,20 @@ __global__ void __launch_bounds__(THREADS) softmax_ce_kernel(const T* x, const i
 
 // Register-resident fused softmax + CE for bf16 rows of up to 512 x 8 x NV
 // class-id-targeted columns (the 32000-way vocabulary fits with NV = 8): the
-// row is read from memory once, each logit is exponentiated once, and the
-// gradient is written from the kept exponentials -- one read and one write of
-// the logits instead of two reads, and half the exponentials.  dlogits may
-// alias x: every thread writes only vectors it has already loaded, and only
-// after the block-wide reductions.
+// row is read from memory once into registers (raw bf16, 4 bytes per two
+// logits), then max, sum of exponentials and the gradient are computed from
+// the registers, recomputing each exponential for the gradient rather than
+// keeping 64 floats per thread.  That keeps the kernel at two 512-thread
+// blocks per SM, so one block's loads overlap the other's reductions.
+// dlogits may alias x: every thread writes only vectors it has already
+// loaded, and only after the block-wide reductions.
 template <int NV>
-__global__ void __launch_bounds__(512, 1) softmax_ce_reg_kernel(const __nv_bfloat16* x, const int* __restrict__ labels,
+__global__ void __launch_bounds__(512, 2) softmax_ce_reg_kernel(const __nv_bfloat16* x, const int* __restrict__ labels,
                                                                 float* __restrict__ loss_rows,
                                                                 __nv_bfloat16* dlogits, int64_t cols,
                                                                 float grad_scale) {
   constexpr int THREADS = 512;
+  pdl_wait();
   __shared__ float red[32];
   const int64_t r = blockIdx.x;
   const __nv_bfloat16* xr = x + r * cols;
@@ -205,8 +208,14 @@ __global__ void __launch_bounds__(512, 1) softmax_ce_reg_kernel(const __nv_bfloa
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int v = threadIdx.x + i * THREADS;
+    if (v < nvec) raw[i] = reinterpret_cast<const uint4*>(xr)[v];
+  }
+  const int label = labels[r];
+  const float xl = (label >= 0 && label < cols) ? __bfloat162float(xr[label]) : 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int v = threadIdx.x + i * THREADS;
     if (v < nvec) {
-      raw[i] = reinterpret_cast<const uint4*>(xr)[v];
       const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -215,8 +224,6 @@ __global__ void __launch_bounds__(512, 1) softmax_ce_reg_kernel(const __nv_bfloa
       }
     }
   }
-  const int label = labels[r];
-  const float xl = (label >= 0 && label < cols) ? __bfloat162float(xr[label]) : 0.f;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if (lane == 0) red[wid] = mx;
@@ -224,19 +231,16 @@ __global__ void __launch_bounds__(512, 1) softmax_ce_reg_kernel(const __nv_bfloa
   mx = lane < THREADS / 32 ? red[lane] : -INFINITY;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  float e[NV][8];
   float sum = 0.f;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int v = threadIdx.x + i * THREADS;
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
+    if (v < nvec) {
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      if (v < nvec) {
+      for (int k = 0; k < 4; ++k) {
         const float2 f = __bfloat1622float2(h[k]);
-        e[i][2 * k] = __expf(f.x - mx);
-        e[i][2 * k + 1] = __expf(f.y - mx);
-        sum += e[i][2 * k] + e[i][2 * k + 1];
+        sum += __expf(f.x - mx) + __expf(f.y - mx);
       }
     }
   }
@@ -254,13 +258,15 @@ __global__ void __launch_bounds__(512, 1) softmax_ce_reg_kernel(const __nv_bfloa
   for (int i = 0; i < NV; ++i) {
     const int v = threadIdx.x + i * THREADS;
     if (v >= nvec) continue;
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
     uint4 o;
     __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int c = v * 8 + 2 * k;
-      const float g0 = (e[i][2 * k] * inv - (c == label ? 1.f : 0.f)) * gs;
-      const float g1 = (e[i][2 * k + 1] * inv - (c + 1 == label ? 1.f : 0.f)) * gs;
+      const float2 f = __bfloat1622float2(h[k]);
+      const float g0 = (__expf(f.x - mx) * inv - (c == label ? 1.f : 0.f)) * gs;
+      const float g1 = (__expf(f.y - mx) * inv - (c + 1 == label ? 1.f : 0.f)) * gs;
       oh[k] = __floats2bfloat162_rn(g0, g1);
     }
     reinterpret_cast<uint4*>(dr)[v] = o;
@@ -456,9 +462,8 @@ void launch_ce(const void* x, const int* labels, const float* probs, float* loss
       const int64_t per = (cols / 8 + 511) / 512;  // 16-byte vectors per thread
       const auto* xb = (const __nv_bfloat16*)x;
       auto* db = (__nv_bfloat16*)dlogits;
-      if (per <= 2) softmax_ce_reg_kernel<2><<<(unsigned)rows, 512, 0, s>>>(xb, labels, loss_rows, db, cols, grad_scale);
-      else if (per <= 4) softmax_ce_reg_kernel<4><<<(unsigned)rows, 512, 0, s>>>(xb, labels, loss_rows, db, cols, grad_scale);
-      else softmax_ce_reg_kernel<8><<<(unsigned)rows, 512, 0, s>>>(xb, labels, loss_rows, db, cols, grad_scale);
+      auto kern = per <= 2 ? softmax_ce_reg_kernel<2> : (per <= 4 ? softmax_ce_reg_kernel<4> : softmax_ce_reg_kernel<8>);
+      launch_pdl(kern, dim3((unsigned)rows), dim3(512), 0, s, xb, labels, loss_rows, db, cols, grad_scale);
       return;
     }
   }

@@ -109,7 +109,7 @@ class ModernLayer:
 
     def to(self, device=None, dtype=torch.float32) -> "ModernLayer":
         """Standalone placement: packs this layer's parameters into a private store."""
-        dev = runtime.get_device(device)
+        dev = runtime.ModelContext(runtime.get_device(device))
         self.bind_runtime(dev, dtype)
         if self.parameters():
             self._store = ParamStore(self.parameters(), dev.device, dtype)

@@ -90,7 +90,9 @@ class Model:
 
 class Sequential(Model):
     def __init__(self, device=None, dtype="fp32", seed: Optional[int] = None):
-        self.dev = device if isinstance(device, runtime.CudaDevice) else runtime.get_device(device)
+        base = device if isinstance(device, runtime.CudaDevice) else runtime.get_device(device)
+        # A private RNG context: dropout masks depend on this model alone.
+        self.dev = runtime.ModelContext(base, seed if seed is not None else 0)
         self.dtype = resolve_dtype(dtype)
         self.m_layers: List[L.ModernLayer] = []
         self.is_training = True

@@ -98,6 +98,62 @@ class CudaDevice:
         return f"CudaDevice({self.device})"
 
 
+class ModelContext(CudaDevice):
+    """A model's view of its device: its own Philox seed, dropout stream ids
+    and device step counter, so the dropout masks of a model depend only on
+    that model (seed, order of its dropout sites, its own step count) and not
+    on how many other models the process has built or trained on the same
+    device.  Streams, queries and everything else are the shared device's."""
+
+    def __init__(self, base: CudaDevice, seed: int = 0):
+        self._base = base.base if isinstance(base, ModelContext) else base
+        self.device = self._base.device
+        self.seed = int(seed)
+        self._stream_ids = 0
+        self._step_t = None
+
+    @property
+    def base(self) -> CudaDevice:
+        return self._base
+
+    @property
+    def compute_stream(self):
+        return self._base.compute_stream
+
+    @property
+    def comm_stream(self):
+        return self._base.comm_stream
+
+    @property
+    def _initialized(self) -> bool:
+        return self._base._initialized
+
+    def initialize(self) -> bool:
+        ok = self._base.initialize()
+        if self._step_t is None:
+            self._step_t = torch.zeros(1, dtype=torch.int64, device=self.device)
+        return ok
+
+    @property
+    def step_t(self):
+        if self._step_t is None:
+            self.initialize()
+        return self._step_t
+
+    def advance_step(self, delta: int = 1) -> None:
+        self.initialize()
+        if self.is_cuda:
+            _ext.C().counter_add(self._step_t, int(delta))
+        else:
+            self._step_t += int(delta)
+
+    def cleanup(self) -> None:
+        self._base.cleanup()
+
+    def __repr__(self) -> str:
+        return f"ModelContext({self.device}, seed={self.seed})"
+
+
 _lock = threading.Lock()
 _devices: Dict[str, CudaDevice] = {}
 

@@ -187,3 +187,23 @@ def test_gemm_tc_pair_persistent_one_pair():
     torch.cuda.synchronize()
     assert C.read_device_error(True) == 0
     _check(out, _ref(a, b), 2e-2)
+
+
+@pytest.mark.parametrize("M,N", [(1024, 1024), (512, 3072), (2048, 512)])
+def test_gemm_tc_pair_splitk_wgrad_shapes(M, N):
+    """Weight-gradient shapes (few output tiles, K = 8192 tokens, both
+    operands M/N-major) take split-K on the CTA-pair kernel; with beta = 1 the
+    reduce accumulates into the existing gradient."""
+    C = _C()
+    torch.manual_seed(5)
+    K = 8192
+    a = torch.randn(K, M, device="cuda").bfloat16().t()  # X^T
+    b = torch.randn(K, N, device="cuda").bfloat16()      # dY
+    out = C.gemm(a, b, out_dtype=torch.float32, force_path=1)
+    _check(out, a.float() @ b.float(), 2e-2)
+    acc = torch.randn(M, N, device="cuda")
+    ref = acc + a.float() @ b.float()
+    C.gemm(a, b, beta=1.0, out=acc, force_path=1)
+    torch.cuda.synchronize()
+    assert C.read_device_error(True) == 0
+    _check(acc, ref, 2e-2)

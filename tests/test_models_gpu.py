@@ -55,8 +55,12 @@ def test_cnn_matches_cpu(dtype, tol):
 def test_wide_mlp_small_matches_cpu():
     kw = dict(width=256, depth=2, d_in=128, n_out=100)
     mc, mg = _pair(zoo.wide_mlp, "bf16", **kw)
-    x = torch.randn(64, 128)
-    y = torch.randint(0, 100, (64,), dtype=torch.int32)
+    # Seeded: with batch 64 a BatchNorm channel of near-zero batch variance
+    # multiplies bf16 rounding noise by its 1/std, so an unlucky unseeded draw
+    # can exceed any fixed tolerance on both paths alike.
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(64, 128, generator=g)
+    y = torch.randint(0, 100, (64,), dtype=torch.int32, generator=g)
     lc, lg = _step_both(mc, mg, x, y, dl.SGD(0.01, 0.9), dl.SGD(0.01, 0.9))
     close(lg, lc, 5e-2)
     close(mg.store.grad, mc.store.grad, 1e-1)
