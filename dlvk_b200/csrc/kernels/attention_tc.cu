@@ -58,6 +58,28 @@ __device__ __forceinline__ uint32_t sw_off(int r, int c) {
   return (uint32_t)((c >> 3) * 16384 + (r >> 3) * 1024 + (r & 7) * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
 
+// Phase timestamps for kernel development: compiled in only with
+// DLVK_ATTN_TRACE defined (a standalone harness reads g_attn_trace).
+#ifdef DLVK_ATTN_TRACE
+__device__ unsigned long long g_attn_trace[8192];
+#define ATTN_TRACE(cond, slot)                                              \
+  do {                                                                      \
+    if ((cond) && blockIdx.x == 0 && (slot) < 8192) g_attn_trace[(slot)] = clock64(); \
+  } while (0)
+#else
+#define ATTN_TRACE(cond, slot) \
+  do {                         \
+  } while (0)
+#endif
+
+// 2^x with the hardware approximation (ex2.approx.ftz: flushes denormal
+// results to zero, which bf16 probabilities cannot represent anyway).
+__device__ __forceinline__ float hw_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Bounded wait whose outcome is the same in every lane of the warp (the
 // warp-collective tcgen05.ld / st that follow need all 32 lanes).
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
@@ -230,7 +252,10 @@ __global__ void __launch_bounds__(192, 1) flash_fwd_kernel(const __grid_constant
       float m = -INFINITY, l = 0.f;
       bool ok = true;
       for (int j = 0; j < nt; ++j) {
+        const int tslot = (((item - (int)blockIdx.x) / (int)gridDim.x) * nt + j) * 8;
+        ATTN_TRACE(threadIdx.x == 64, tslot + 0);
         if (!warp_wait(&s_full[sb], sph, p.err)) { ok = false; break; }
+        ATTN_TRACE(threadIdx.x == 64, tslot + 1);
         tc_fence_after();
         uint32_t sr[4][32];
 #pragma unroll
@@ -239,22 +264,45 @@ __global__ void __launch_bounds__(192, 1) flash_fwd_kernel(const __grid_constant
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_empty[sb]);
+        ATTN_TRACE(threadIdx.x == 64, tslot + 2);
         if (++sb == 2) {
           sb = 0;
           sph ^= 1u;
         }
-        float mx = -INFINITY;
+        // Row max and (below) row sum as 8 independent partials: one thread
+        // owns the row, so a single 128-long dependency chain would leave the
+        // warp waiting on each step's latency.
+        float mp[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mp[k] = -INFINITY;
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(sr[c][i]));
+          for (int i = 0; i < 32; ++i) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(sr[c][i]));
+        float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
         mx *= p.c;
         const bool need = mx > m + 8.f;  // lazy rescale: keep the old reference max while it is within 2^8
         const float m_new = need ? mx : m;
-        const float alpha = need ? exp2f(m - m_new) : 1.f;
+        const float alpha = need ? hw_exp2(m - m_new) : 1.f;
+        // Exponentials first, into the S registers: this MUFU-heavy part
+        // overlaps the previous tile's PV product on the tensor cores; only
+        // the P write and the O rescale wait for that product.
+        float sp8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) sp8[k] = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float e = hw_exp2(fmaf(__uint_as_float(sr[c][i]), p.c, -m_new));
+            sp8[i & 7] += e;
+            sr[c][i] = __float_as_uint(e);
+          }
+        ATTN_TRACE(threadIdx.x == 64, tslot + 3);
         if (j > 0) {
           // PV of the previous tile must be done before O is rescaled or P rewritten.
           if (!warp_wait(pv_done, pvph, p.err)) { ok = false; break; }
+          ATTN_TRACE(threadIdx.x == 64, tslot + 4);
           pvph ^= 1u;
           tc_fence_after();
           if (__any_sync(0xffffffffu, need)) {
@@ -271,30 +319,25 @@ __global__ void __launch_bounds__(192, 1) flash_fwd_kernel(const __grid_constant
             tmem_st_wait();
           }
         }
-        l *= alpha;
+        ATTN_TRACE(threadIdx.x == 64, tslot + 5);
+        l = l * alpha + (((sp8[0] + sp8[1]) + (sp8[2] + sp8[3])) + ((sp8[4] + sp8[5]) + (sp8[6] + sp8[7])));
         m = m_new;
-        float sum = 0.f;
         uint8_t* prow = sP;
 #pragma unroll
         for (int ch = 0; ch < 16; ++ch) {
-          float e[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            e[i] = exp2f(fmaf(__uint_as_float(sr[ch >> 2][(ch & 3) * 8 + i]), p.c, -m));
-            sum += e[i];
-          }
+          const uint32_t* e = &sr[ch >> 2][(ch & 3) * 8];
           uint4 v;
-          v.x = pack2(e[0], e[1]);
-          v.y = pack2(e[2], e[3]);
-          v.z = pack2(e[4], e[5]);
-          v.w = pack2(e[6], e[7]);
+          v.x = pack2(__uint_as_float(e[0]), __uint_as_float(e[1]));
+          v.y = pack2(__uint_as_float(e[2]), __uint_as_float(e[3]));
+          v.z = pack2(__uint_as_float(e[4]), __uint_as_float(e[5]));
+          v.w = pack2(__uint_as_float(e[6]), __uint_as_float(e[7]));
           *reinterpret_cast<uint4*>(prow + sw_off(row, ch)) = v;
         }
-        l += sum;
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full);
+        ATTN_TRACE(threadIdx.x == 64, tslot + 6);
       }
       if (!ok) break;
       if (!warp_wait(pv_done, pvph, p.err)) break;
@@ -457,7 +500,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
         if (!mbar_wait(kv_full, it & 1, p.err)) break;
         if (!mbar_wait(kv_read, (it & 1) ^ 1u, p.err)) break;  // previous item's dK / dV read out
         for (int i = 0; i < nt; ++i) {
+          ATTN_TRACE(true, 4096 + (it * nt + i) * 16 + 12);
           if (!mbar_wait(&qd_full[qs], qph, p.err)) { ok = false; break; }
+          ATTN_TRACE(true, 4096 + (it * nt + i) * 16 + 13);
           tc_fence_after();
           const uint32_t qa = smem_u32(sQD + qs * 2 * TILE), doa = qa + TILE;
 #pragma unroll
@@ -468,9 +513,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
                     id_st, k ? 1u : 0u);
           }
           mma_commit(st_full);
+          ATTN_TRACE(true, 4096 + (it * nt + i) * 16 + 8);
           if (!mbar_wait(ds_full, dsph, p.err)) { ok = false; break; }
+          ATTN_TRACE(true, 4096 + (it * nt + i) * 16 + 9);
           dsph ^= 1u;
           if (!mbar_wait(dq_free, dqph ^ 1u, p.err)) { ok = false; break; }
+          ATTN_TRACE(true, 4096 + (it * nt + i) * 16 + 10);
           dqph ^= 1u;
           tc_fence_after();
 #pragma unroll
@@ -486,6 +534,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
                     make_sw128_desc(ka + k * 2048, 16384, 1024), id_q, k > 0 ? 1u : 0u);
           }
           mma_commit(dq_full);
+          ATTN_TRACE(true, 4096 + (it * nt + i) * 16 + 11);
           mma_commit(&qd_empty[qs]);
           if (++qs == 2) {
             qs = 0;
@@ -521,11 +570,15 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
     for (int item = blockIdx.x; item < items && ok; item += gridDim.x, ++it) {
       const int kt = item % nt, bh = item / nt, h = bh % p.H, b = bh / p.H;
       for (int i = 0; i < nt; ++i, ib ^= 1) {
+        const int bslot = 4096 + (it * nt + i) * 16;
+        ATTN_TRACE(threadIdx.x == 64, bslot + 0);
         const float nxt = (i + 1 < nt) ? fetch(item, i + 1) : fetch(item + gridDim.x, 0);
         (tid < 128 ? sLse : sDel)[ib * 128 + (tid & 127)] = cur;
         cur = nxt;
         if (!group_sync(cw_bar, cwph, p.err)) { ok = false; break; }
+        ATTN_TRACE(threadIdx.x == 64, bslot + 1);
         if (!warp_wait(st_full, stph, p.err)) { ok = false; break; }
+        ATTN_TRACE(threadIdx.x == 64, bslot + 2);
         stph ^= 1u;
         tc_fence_after();
         const float* L = sLse + ib * 128;
@@ -548,7 +601,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
             const float dv[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
 #pragma unroll
             for (int i8 = 0; i8 < 8; ++i8) {
-              pt[i8] = exp2f(fmaf(__uint_as_float(s[q4 * 8 + i8]), p.c, -lv[i8]));
+              pt[i8] = hw_exp2(fmaf(__uint_as_float(s[q4 * 8 + i8]), p.c, -lv[i8]));
               ds[i8] = pt[i8] * (__uint_as_float(dp[q4 * 8 + i8]) - dv[i8]);
             }
             const int ch = cb * 4 + q4;
@@ -563,9 +616,11 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(ds_full);
+        ATTN_TRACE(threadIdx.x == 64, bslot + 3);
         // dQ tile (row = query): this warp's 32 columns -> swizzled fp32 staging
         // sub-tile `hf` -> TMA reduce-add.
         if (!warp_wait(dq_full, dqph, p.err)) { ok = false; break; }
+        ATTN_TRACE(threadIdx.x == 64, bslot + 4);
         dqph ^= 1u;
         tc_fence_after();
         uint32_t qv[32];
@@ -574,8 +629,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(dq_free);
+        ATTN_TRACE(threadIdx.x == 64, bslot + 5);
         if (tid == 0) bulk_wait_read0();  // the previous reduce has read the staging buffer
         if (!group_sync(cw_bar, cwph, p.err)) { ok = false; break; }
+        ATTN_TRACE(threadIdx.x == 64, bslot + 6);
         {
           uint8_t* base = sDQ + hf * 16384 + (row >> 3) * 1024 + (row & 7) * 128;
 #pragma unroll
@@ -586,6 +643,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
         }
         fence_proxy_async_smem();
         if (!group_sync(cw_bar, cwph, p.err)) { ok = false; break; }
+        ATTN_TRACE(threadIdx.x == 64, bslot + 7);
         if (tid == 0) {
           const int y = b * p.S + i * FT;
           tma_reduce_add_2d(&tm_dq, sDQ, h * FD, y);

@@ -61,6 +61,7 @@ struct TcParams {
   int i8;                  // 1: int8 x int8 -> int32 (kind::i8), K-major operands
   const float* row_scale;  // int8 dequantisation: per-row (A) and per-column (B) scales
   const float* col_scale;
+  int tma_c;               // 1: plain epilogue stores C through per-warp smem boxes + TMA
 };
 
 // PAIR: a 2-CTA cluster shares one 256 x BN tile (tcgen05 cta_group::2);
@@ -72,9 +73,35 @@ struct Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = PAIR ? 6 : ((BN == 256) ? 4 : 6);
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int EPI_BYTES = 8 * 32 * 33 * 4;  // per-warp 32x33 fp32 staging
+  // per-warp 32x33 fp32 staging; also holds the TMA-store boxes (8 x 4 KB
+  // from the next 1024-byte boundary)
+  static constexpr int EPI_BYTES = 8 * 32 * 33 * 4;
+  static_assert(EPI_BYTES >= 768 + 8 * 4096, "epilogue smem too small for the TMA-store boxes");
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + EPI_BYTES;
 };
+
+// Wait-time accounting for kernel development: compiled in only with
+// DLVK_GEMM_TRACE defined (a standalone harness reads g_gemm_trace):
+// per CTA, cycles spent waiting on each barrier class.
+#ifdef DLVK_GEMM_TRACE
+__device__ unsigned long long g_gemm_trace[148 * 16];
+#define GEMM_T0() const long long _gt0 = clock64()
+#define GEMM_ACC(slot) atomicAdd(&g_gemm_trace[blockIdx.x * 16 + (slot)], (unsigned long long)(clock64() - _gt0))
+#define GEMM_STAMP(cond, slot)                                                              \
+  do {                                                                                      \
+    if (cond) g_gemm_trace[blockIdx.x * 16 + (slot)] = (unsigned long long)clock64();       \
+  } while (0)
+#else
+#define GEMM_STAMP(cond, slot) \
+  do {                         \
+  } while (0)
+#define GEMM_T0() \
+  do {            \
+  } while (0)
+#define GEMM_ACC(slot) \
+  do {                 \
+  } while (0)
+#endif
 
 __device__ __forceinline__ void tile_coords(int t, const TcParams& p, int& tm, int& tn, int& b) {
   const int per_batch = p.tiles_m * p.tiles_n;
@@ -256,8 +283,10 @@ __device__ __forceinline__ void epi_store(const TcParams& p, const float* stg, i
 
 template <int BN, bool PAIR = false>
 __global__ void __launch_bounds__(320, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, TcParams p) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, TcParams p) {
   using C = Cfg<BN, PAIR>;
+  GEMM_STAMP(threadIdx.x == 0, 4);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
@@ -310,6 +339,7 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait();  // the previous kernel's outputs (our operands) are complete from here on
+  GEMM_STAMP(threadIdx.x == 0, 5);
 
   if (warp == 0) {
     if (lane == 0 && PAIR) {
@@ -324,7 +354,11 @@ __global__ void __launch_bounds__(320, 1)
         const int bcol = tn * BN + (int)rank * (BN / 2);
         const int kb0 = sp * p.kb_per_split, kb1 = min(num_kb, kb0 + p.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, p.err)) goto producer_done_pair;
+          {
+            GEMM_T0();
+            if (!mbar_wait(&empty[stage], phase ^ 1u, p.err)) goto producer_done_pair;
+            GEMM_ACC(0);
+          }
           uint8_t* sA = smem + stage * C::STAGE_BYTES;
           uint8_t* sB = sA + C::A_BYTES;
           const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);  // the leader's full barrier
@@ -359,7 +393,11 @@ __global__ void __launch_bounds__(320, 1)
         const int bo = b / p.batch2, bi = b - bo * p.batch2;
         const int kb0 = sp * p.kb_per_split, kb1 = min(num_kb, kb0 + p.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, p.err)) goto producer_done;
+          {
+            GEMM_T0();
+            if (!mbar_wait(&empty[stage], phase ^ 1u, p.err)) goto producer_done;
+            GEMM_ACC(0);
+          }
           uint8_t* sA = smem + stage * C::STAGE_BYTES;
           uint8_t* sB = sA + C::A_BYTES;
           mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
@@ -396,14 +434,20 @@ __global__ void __launch_bounds__(320, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int t = t0; t < num_tiles; t += tstep) {
-          if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.err)) break;
+          {
+            GEMM_T0();
+            if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.err)) break;
+            GEMM_ACC(1);
+          }
           tc_fence_after();
           const uint32_t d = tmem_base + (uint32_t)(acc * BN);
           bool ok = true;
           const int sp = t / tiles_per_split;
           const int kb0 = sp * p.kb_per_split, kb1 = min(num_kb, kb0 + p.kb_per_split);
           for (int kb = kb0; kb < kb1; ++kb) {
+            GEMM_T0();
             if (!mbar_wait(&full[stage], phase, p.err)) { ok = false; break; }
+            GEMM_ACC(2);
             tc_fence_after();
             const uint32_t aBase = smem_u32(smem + stage * C::STAGE_BYTES);
             const uint32_t bBase = aBase + C::A_BYTES;
@@ -441,14 +485,20 @@ __global__ void __launch_bounds__(320, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.err)) break;
+        {
+          GEMM_T0();
+          if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.err)) break;
+          GEMM_ACC(1);
+        }
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * BN);
         bool ok = true;
         const int sp = t / tiles_per_split;
         const int kb0 = sp * p.kb_per_split, kb1 = min(num_kb, kb0 + p.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
+          GEMM_T0();
           if (!mbar_wait(&full[stage], phase, p.err)) { ok = false; break; }
+          GEMM_ACC(2);
           tc_fence_after();
           const uint32_t aBase = smem_u32(smem + stage * C::STAGE_BYTES);
           const uint32_t bBase = aBase + C::A_BYTES;
@@ -488,13 +538,19 @@ __global__ void __launch_bounds__(320, 1)
     float* stg = epi + ew * (32 * 33);
     const bool staged = (p.R != nullptr) || (p.Mk != nullptr) || (p.beta != 0.f);
     constexpr int NCH = BN / 64;  // 32-column chunks per warp
-    int acc = 0;
+    int acc = 0, ecount = 0;
     uint32_t acc_phase = 0;
     for (int t = t0; t < num_tiles; t += tstep) {
       int tm, tn, b;
       const int sp = t / tiles_per_split;
       tile_coords(t - sp * tiles_per_split, p, tm, tn, b);
-      if (!mbar_wait(&tfull[acc], acc_phase, p.err)) break;
+      {
+        GEMM_T0();
+        if (!mbar_wait(&tfull[acc], acc_phase, p.err)) break;
+        if (threadIdx.x == 64) GEMM_ACC(3);
+        GEMM_STAMP(threadIdx.x == 64 && g_gemm_trace[blockIdx.x * 16 + 6] == 0, 6);
+        GEMM_STAMP(threadIdx.x == 64, 7);
+      }
       tc_fence_after();
       const int bo = b / p.batch2, bi = b - bo * p.batch2;
       const int64_t cb = (int64_t)sp * p.split_stride + (int64_t)bo * p.bsc + (int64_t)bi * p.bsc2;
@@ -518,6 +574,59 @@ __global__ void __launch_bounds__(320, 1)
             else epi_store<__nv_bfloat16, 8>(p, stg, row0, n0, lane, cb, rb, mb);
           }
           __syncwarp();
+        } else if (p.tma_c) {
+          // Row `lane` of this warp's 32 x 32 box goes to smem; one lane
+          // stores the box with TMA (rows >= M / columns >= N are clipped).
+          // Two boxes alternate for bf16 (one for fp32), so the store of
+          // chunk i overlaps the conversion of chunk i+1.
+          if (n0 < p.N) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[i & 1][j]) * p.alpha;
+            if (p.bias) add_bias<32>(p.bias, p.bias_f32, n0, min(32, p.N - n0), v);
+            apply_act<32>(p.act, v);
+            // 1024-byte aligned 4 KB slot per warp (the swizzled box layout is
+            // defined on aligned addresses): two bf16 boxes or one fp32 box.
+            uint8_t* box = reinterpret_cast<uint8_t*>(
+                               (reinterpret_cast<uintptr_t>(epi) + 1023) & ~uintptr_t(1023)) +
+                           ew * 4096 + (p.out_f32 ? 0 : (ecount & 1) * 2048);
+            if (lane == 0) {
+              if (p.out_f32) bulk_wait_group_read<0>();
+              else bulk_wait_group_read<1>();
+            }
+            __syncwarp();
+            // The box map uses the 128-byte (fp32 rows) / 64-byte (bf16 rows)
+            // swizzle, which the TMA unit applies to shared-memory address
+            // bits: XOR the 16-byte chunk index with address bits 7..9 (7..8).
+            const uint32_t bb = smem_u32(box);
+            if (p.out_f32) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const uint32_t a = bb + (uint32_t)lane * 128u + (uint32_t)j * 16u;
+                st_shared_v4(a ^ (((a >> 7) & 7u) << 4), __float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]),
+                             __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3]));
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                uint32_t w[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  const __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * j + 2 * k], v[8 * j + 2 * k + 1]);
+                  w[k] = *reinterpret_cast<const uint32_t*>(&h);
+                }
+                const uint32_t a = bb + (uint32_t)lane * 64u + (uint32_t)j * 16u;
+                st_shared_v4(a ^ (((a >> 7) & 3u) << 4), w[0], w[1], w[2], w[3]);
+              }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmC, box, n0, row0);
+              bulk_commit_group();
+            }
+            ++ecount;
+          }
         } else {
           const int row = row0 + lane;
           if (row < p.M && n0 < p.N) {
@@ -583,10 +692,16 @@ __global__ void __launch_bounds__(320, 1)
         acc_phase ^= 1u;
       }
     }
+    if (p.tma_c && lane == 0) bulk_wait_group_read<0>();  // the boxes' smem is read before the CTA exits
   }
+  GEMM_STAMP(threadIdx.x == 64, 9);
+  GEMM_STAMP(threadIdx.x == 32, 11);
+  GEMM_STAMP(threadIdx.x == 0, 12);
   tc_fence_before();
   __syncthreads();
+  GEMM_STAMP(threadIdx.x == 64, 8);
   if (PAIR) cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+  GEMM_STAMP(threadIdx.x == 64, 10);
   pdl_trigger();             // this CTA's work is done: the next kernel may start launching
   if (warp == 1) {
     tc_fence_after();
@@ -639,7 +754,8 @@ int sm_count() {
 }
 
 template <int BN>
-void launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, int max_ctas, cudaStream_t s) {
+void launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const TcParams& p, int max_ctas,
+               cudaStream_t s) {
   using C = Cfg<BN>;
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -650,13 +766,14 @@ void launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, 
   }
   const int tiles = p.tiles_m * p.tiles_n * p.batch * p.splits;
   int grid = std::min(tiles, max_ctas > 0 ? max_ctas : sm_count());
-  launch_pdl(gemm_tc_kernel<BN, false>, dim3(grid), dim3(320), C::SMEM, s, ta, tb, p);
+  launch_pdl(gemm_tc_kernel<BN, false>, dim3(grid), dim3(320), C::SMEM, s, ta, tb, tc, p);
   DLVK_POST_LAUNCH();
 }
 
 // 2-CTA clusters sharing 256 x 256 tiles (cta_group::2).  The persistent
 // grid is as many pairs as can be resident at once.
-void launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, int max_ctas, cudaStream_t s) {
+void launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const TcParams& p,
+                    int max_ctas, cudaStream_t s) {
   using C = Cfg<256, true>;
   static int max_pairs[64] = {0};
   int dev = 0;
@@ -687,7 +804,7 @@ void launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams
   if (max_ctas > 0) pairs = std::max(1, std::min(pairs, max_ctas / 2));
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.numAttrs = 2;
-  DLVK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<256, true>, ta, tb, p));
+  DLVK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<256, true>, ta, tb, tc, p));
   DLVK_POST_LAUNCH();
 }
 
@@ -788,6 +905,17 @@ bool gemm_tc_supported(const GemmArgs& a) {
   if (a.M > (1LL << 31) - 1 || a.N > (1LL << 31) - 1 || a.K > (1LL << 31) - 1) return false;
   return true;
 }
+
+namespace {
+// DLVK_GEMM_TMA_STORE=0 keeps the register-direct epilogue stores.
+bool tma_c_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("DLVK_GEMM_TMA_STORE");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+}  // namespace
 
 void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int max_ctas, float* workspace,
              int64_t workspace_floats) {
@@ -890,18 +1018,33 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
     p.R = nullptr;
     p.Mk = nullptr;
     p.act = ACT_NONE;
-    if (pair) launch_tc_pair(ta, tb, p, max_ctas, s);
-    else if (BN == 256) launch_tc<256>(ta, tb, p, max_ctas, s);
-    else launch_tc<128>(ta, tb, p, max_ctas, s);
+    if (pair) launch_tc_pair(ta, tb, ta, p, max_ctas, s);
+    else if (BN == 256) launch_tc<256>(ta, tb, ta, p, max_ctas, s);
+    else launch_tc<128>(ta, tb, ta, p, max_ctas, s);
     const int g = (int)std::min<int64_t>((per + 255) / 256, 148 * 16);
     if (out_dt == DType::F32) splitk_reduce_kernel<float><<<g, 256, 0, s>>>(workspace, splits, per, a);
     else splitk_reduce_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(workspace, splits, per, a);
     DLVK_POST_LAUNCH();
     return;
   }
-  if (pair) launch_tc_pair(ta, tb, p, max_ctas, s);
-  else if (BN == 256) launch_tc<256>(ta, tb, p, max_ctas, s);
-  else launch_tc<128>(ta, tb, p, max_ctas, s);
+  // Plain epilogues of unbatched GEMMs store C with TMA from per-warp
+  // 32 x 32 boxes: one async bulk store per box instead of each lane writing
+  // its own row (32 scattered 16-byte stores per warp instruction).
+  CUtensorMap tc = ta;
+  if (p.R == nullptr && p.Mk == nullptr && p.beta == 0.f && p.batch == 1 && !p.i8 && p.vec_ok && tma_c_enabled()) {
+    cuuint64_t dims[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
+    cuuint64_t strides[1] = {(cuuint64_t)a.ldc * (uint64_t)esz};
+    cuuint32_t box[2] = {32u, 32u};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode_fn()(&tc, p.out_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                             a.C, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             p.out_f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r == CUDA_SUCCESS) p.tma_c = 1;
+  }
+  if (pair) launch_tc_pair(ta, tb, tc, p, max_ctas, s);
+  else if (BN == 256) launch_tc<256>(ta, tb, tc, p, max_ctas, s);
+  else launch_tc<128>(ta, tb, tc, p, max_ctas, s);
 }
 
 namespace {
@@ -915,6 +1058,7 @@ int& pair_flag() {
 }  // namespace
 
 bool gemm_tc_pair_enabled() { return pair_flag() != 0; }
+
 void gemm_tc_set_pair(bool on) { pair_flag() = on ? 1 : 0; }
 
 int64_t gemm_tc_workspace_floats(const GemmArgs& a, int max_ctas) {
@@ -976,8 +1120,8 @@ void gemm_i8_tc(const int8_t* A, const int8_t* Bt, const float* row_scale, const
   p.i8 = 1;
   p.row_scale = row_scale;
   p.col_scale = col_scale;
-  if (BN == 256) launch_tc<256>(ta, tb, p, 0, s);
-  else launch_tc<128>(ta, tb, p, 0, s);
+  if (BN == 256) launch_tc<256>(ta, tb, ta, p, 0, s);
+  else launch_tc<128>(ta, tb, ta, p, 0, s);
 }
 
 }  // namespace dlvk
