@@ -196,6 +196,11 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, 
                "r"(smem_u32(src)), "r"(x), "r"(y)
                : "memory");
 }
+__device__ __forceinline__ void tma_store_5d(const void* tmap, const void* src, int x, int y, int z, int w, int v) {
+  asm volatile("cp.async.bulk.tensor.5d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5, %6}], [%1];" ::"l"(tmap),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(v)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until at most N bulk groups still read their shared-memory source.
 template <int N>

@@ -21,6 +21,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <unordered_map>
 
@@ -622,7 +623,7 @@ __global__ void __launch_bounds__(320, 1)
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              tma_store_2d(&tmC, box, n0, row0);
+              tma_store_5d(&tmC, box, n0, row0, bi, bo, sp);
               bulk_commit_group();
             }
             ++ecount;
@@ -915,6 +916,36 @@ bool tma_c_enabled() {
   }();
   return on;
 }
+// Plain epilogues (alpha, bias, activation; split-K partials included) store
+// C with TMA from per-warp 32 x 32 boxes: one async bulk store per box
+// instead of each lane writing its own row (32 scattered 16-byte stores per
+// warp instruction).  The map is 5-D {N, M, inner batch, outer batch, split}
+// with the epilogue's strides; sets p.tma_c when it applies.
+CUtensorMap make_c_map(TcParams& p, int64_t M, int64_t N) {
+  CUtensorMap tc;
+  std::memset(&tc, 0, sizeof(tc));
+  p.tma_c = 0;
+  if (p.R != nullptr || p.Mk != nullptr || p.beta != 0.f || p.i8 || !p.vec_ok || !tma_c_enabled()) return tc;
+  const uint64_t esz = p.out_f32 ? 4 : 2;
+  auto pick = [&](int64_t cnt, int64_t stride) -> uint64_t {
+    return cnt > 1 ? (uint64_t)stride * esz : (uint64_t)M * (uint64_t)p.ldc * esz;
+  };
+  const int64_t batch_outer = p.batch / p.batch2;
+  cuuint64_t dims[5] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)p.batch2, (cuuint64_t)batch_outer,
+                        (cuuint64_t)p.splits};
+  cuuint64_t strides[4] = {(cuuint64_t)p.ldc * esz, pick(p.batch2, p.bsc2), pick(batch_outer, p.bsc),
+                           pick(p.splits, p.split_stride)};
+  for (uint64_t st : strides)
+    if (st == 0 || st % 16 != 0 || st >= (1ull << 40)) return tc;
+  cuuint32_t box[5] = {32u, 32u, 1u, 1u, 1u};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = encode_fn()(&tc, p.out_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, p.C,
+                           dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           p.out_f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                           CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r == CUDA_SUCCESS) p.tma_c = 1;
+  return tc;
+}
 }  // namespace
 
 void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int max_ctas, float* workspace,
@@ -1018,30 +1049,17 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
     p.R = nullptr;
     p.Mk = nullptr;
     p.act = ACT_NONE;
-    if (pair) launch_tc_pair(ta, tb, ta, p, max_ctas, s);
-    else if (BN == 256) launch_tc<256>(ta, tb, ta, p, max_ctas, s);
-    else launch_tc<128>(ta, tb, ta, p, max_ctas, s);
+    const CUtensorMap tc = make_c_map(p, a.M, a.N);
+    if (pair) launch_tc_pair(ta, tb, tc, p, max_ctas, s);
+    else if (BN == 256) launch_tc<256>(ta, tb, tc, p, max_ctas, s);
+    else launch_tc<128>(ta, tb, tc, p, max_ctas, s);
     const int g = (int)std::min<int64_t>((per + 255) / 256, 148 * 16);
     if (out_dt == DType::F32) splitk_reduce_kernel<float><<<g, 256, 0, s>>>(workspace, splits, per, a);
     else splitk_reduce_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(workspace, splits, per, a);
     DLVK_POST_LAUNCH();
     return;
   }
-  // Plain epilogues of unbatched GEMMs store C with TMA from per-warp
-  // 32 x 32 boxes: one async bulk store per box instead of each lane writing
-  // its own row (32 scattered 16-byte stores per warp instruction).
-  CUtensorMap tc = ta;
-  if (p.R == nullptr && p.Mk == nullptr && p.beta == 0.f && p.batch == 1 && !p.i8 && p.vec_ok && tma_c_enabled()) {
-    cuuint64_t dims[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
-    cuuint64_t strides[1] = {(cuuint64_t)a.ldc * (uint64_t)esz};
-    cuuint32_t box[2] = {32u, 32u};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = encode_fn()(&tc, p.out_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                             a.C, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                             p.out_f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
-                             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r == CUDA_SUCCESS) p.tma_c = 1;
-  }
+  const CUtensorMap tc = make_c_map(p, a.M, a.N);
   if (pair) launch_tc_pair(ta, tb, tc, p, max_ctas, s);
   else if (BN == 256) launch_tc<256>(ta, tb, tc, p, max_ctas, s);
   else launch_tc<128>(ta, tb, tc, p, max_ctas, s);
