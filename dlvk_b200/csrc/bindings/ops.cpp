@@ -348,7 +348,7 @@ void optim_advance_op(const at::Tensor& hyper) {
 
 void optim_update_op(int64_t kind, const at::Tensor& hyper, const at::Tensor& p, const at::Tensor& grad,
                      c10::optional<at::Tensor> m, c10::optional<at::Tensor> v, c10::optional<at::Tensor> p_bf16,
-                     double extra_scale) {
+                     double extra_scale, int64_t max_ctas) {
   check_cuda(p, "p");
   c10::cuda::CUDAGuard g(p.device());
   TORCH_CHECK(p.scalar_type() == at::kFloat && p.is_contiguous(), "dlvk.optim_update: f32 contiguous params");
@@ -364,7 +364,7 @@ void optim_update_op(int64_t kind, const at::Tensor& hyper, const at::Tensor& p,
     pb = reinterpret_cast<__nv_bfloat16*>(p_bf16->data_ptr());
   }
   optim_update((int)kind, reinterpret_cast<const OptimHyper*>(hyper.data_ptr()), p.data_ptr<float>(),
-               grad.data_ptr(), to_dtype(grad), mp, vp, pb, p.numel(), (float)extra_scale, stream());
+               grad.data_ptr(), to_dtype(grad), mp, vp, pb, p.numel(), (float)extra_scale, stream(), (int)max_ctas);
 }
 
 void grad_stats_op(const at::Tensor& g, double scale, double max_norm, const at::Tensor& sumsq,
@@ -418,7 +418,7 @@ void register_ops(py::module& m) {
   m.def("optim_advance", &optim_advance_op);
   m.def("optim_update", &optim_update_op, py::arg("kind"), py::arg("hyper"), py::arg("p"), py::arg("grad"),
         py::arg("m") = py::none(), py::arg("v") = py::none(), py::arg("p_bf16") = py::none(),
-        py::arg("extra_scale") = 1.0);
+        py::arg("extra_scale") = 1.0, py::arg("max_ctas") = 0);
   m.def("gemm_set_pair", [](bool on) { gemm_tc_set_pair(on); });
   m.def("gemm_pair_enabled", []() { return gemm_tc_pair_enabled(); });
   m.def("grad_stats", &grad_stats_op, py::arg("g"), py::arg("scale"), py::arg("max_norm"), py::arg("sumsq"),

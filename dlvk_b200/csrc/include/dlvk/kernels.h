@@ -120,8 +120,9 @@ struct OptimHyper {
   const int* skip_flag_ptr;    // optional device flag: skip the update when set
 };
 void optim_advance(OptimHyper* h_dev, cudaStream_t s);
+// max_ctas > 0 caps the grid (an update overlapped with other kernels).
 void optim_update(int kind, const OptimHyper* h_dev, float* p, const void* g, DType g_dt, float* m, float* v,
-                  __nv_bfloat16* p_bf16, int64_t n, float extra_scale, cudaStream_t s);
+                  __nv_bfloat16* p_bf16, int64_t n, float extra_scale, cudaStream_t s, int max_ctas = 0);
 int grad_stats_scratch_floats();
 void grad_stats(const void* g, DType g_dt, int64_t n, float scale, float max_norm, float* sumsq_out, int* flag,
                 float* clip_out, bool accumulate, float* scratch, cudaStream_t s, const float* scale_ptr = nullptr);

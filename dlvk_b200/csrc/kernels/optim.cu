@@ -217,9 +217,9 @@ void optim_advance(OptimHyper* h_dev, cudaStream_t s) {
 }
 
 void optim_update(int kind, const OptimHyper* h_dev, float* p, const void* g, DType g_dt, float* m, float* v,
-                  __nv_bfloat16* p_bf16, int64_t n, float extra_scale, cudaStream_t s) {
+                  __nv_bfloat16* p_bf16, int64_t n, float extra_scale, cudaStream_t s, int max_ctas) {
   if (n == 0) return;
-  const int grid = update_grid(n);
+  const int grid = max_ctas > 0 ? std::min(update_grid(n), max_ctas) : update_grid(n);
   if (g_dt == DType::F32)
     update_kernel<float><<<grid, 256, 0, s>>>(kind, h_dev, p, (const float*)g, m, v, p_bf16, n, extra_scale);
   else if (g_dt == DType::BF16)

@@ -120,8 +120,9 @@ class Optimizer:
                 st.clip.fill_(min(1.0, self.clip_norm / (norm + 1e-6)))
 
     def update_range(self, store, start: int, end: int, grad: Optional[torch.Tensor] = None,
-                     extra_scale: float = 1.0) -> None:
-        """Apply the update to flat elements [start, end)."""
+                     extra_scale: float = 1.0, max_ctas: int = 0) -> None:
+        """Apply the update to flat elements [start, end); `max_ctas` caps
+        the kernel's grid (an update running beside other kernels)."""
         st = self.state(store)
         g = store.grad[start:end] if grad is None else grad
         p = store.master[start:end]
@@ -129,7 +130,7 @@ class Optimizer:
         v = st.v[start:end] if st.v is not None else None
         pb = store.value[start:end] if store.value is not store.master else None
         if st.cuda:
-            K.N().optim_update(self.kind, st.hyper, p, g, m, v, pb, extra_scale)
+            K.N().optim_update(self.kind, st.hyper, p, g, m, v, pb, extra_scale, max_ctas)
         else:
             if self._cpu_skip():
                 return

@@ -92,3 +92,28 @@ def test_dlvk_roundtrip_gpu(tmp_path):
     l2 = m2.train_step(x, y, dl.CrossEntropyLoss(), opt2)
     assert torch.equal(m.store.master, m2.store.master)
     assert float(l1) == float(l2)
+
+
+def test_overlapped_update_matches_default_step():
+    """The one-GPU optimizer update run per bucket beside backward (side stream,
+    capped grid, inside the captured graph) gives the default path's weights."""
+    kw = dict(vocab=512, d_model=128, layers=2, heads=2, d_ff=256)
+    ma = zoo.transformer(device="cuda", seed=0, **kw).build()
+    mb = zoo.transformer(device="cuda", seed=0, **kw).build()
+    x, y = zoo.synthetic_batch("transformer", 4, seq_len=64, vocab=512)
+    sa = dl.TrainStep(ma, dl.CrossEntropyLoss(), dl.Adam(1e-3), overlap_update=False)
+    auto = dl.TrainStep(mb, dl.CrossEntropyLoss(), dl.Adam(1e-3), overlap_update=True)
+    assert auto.dp is not None and auto.dp.describe()["mode"] == "overlapped-update"
+    auto.close()
+    from dlvk_b200.training.overlap import OverlappedUpdate
+
+    ov = OverlappedUpdate(mb, dl.Adam(1e-3), bucket_mb=0.25)
+    assert len(ov.buckets) > 2
+    sb = dl.TrainStep(mb, dl.CrossEntropyLoss(), ov.opt, dp=ov)
+    for _ in range(5):
+        la, lb = sa(x, y), sb(x, y)
+    close(torch.as_tensor(lb), torch.as_tensor(la), 1e-2)
+    close(mb.store.master, ma.store.master, 1e-2)
+    sa.close()
+    sb.close()
+    ov.close()

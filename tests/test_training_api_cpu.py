@@ -214,3 +214,27 @@ def test_persistence(tmp_path):
     ser = T.ModelSerializer(T.SerializationFormat.DLVK_JSON)
     ser.save(m, str(tmp_path / "m.json"))
     assert torch.equal(ser.load(str(tmp_path / "m.json")).forward(x), m.forward(x))
+
+
+def test_overlapped_update_matches_step_after_backward():
+    """Per-bucket updates driven by the grad-ready hooks give the same weights
+    as one optimizer step after backward."""
+    from dlvk_b200.training.overlap import OverlappedUpdate
+    from dlvk_b200.training.step import TrainStep
+
+    x, y = clusters(64)
+    y = y.to(torch.int32)
+    ma, mb = mlp(), mlp()
+    ov = OverlappedUpdate(mb, O.Adam(1e-2), bucket_mb=0.001)
+    assert len(ov.buckets) > 1
+    sa = TrainStep(ma, Lo.CrossEntropyLoss(), O.Adam(1e-2))
+    sb = TrainStep(mb, Lo.CrossEntropyLoss(), ov.opt, dp=ov)
+    for _ in range(4):
+        la, lb = sa(x, y), sb(x, y)
+    assert torch.allclose(torch.as_tensor(la), torch.as_tensor(lb), atol=1e-6)
+    assert torch.allclose(ma.store.master, mb.store.master, atol=1e-6)
+    ov.close()
+    clipped = O.Adam(1e-2)
+    clipped.set_gradient_clipping(max_norm=1.0)
+    with pytest.raises(ValueError):
+        OverlappedUpdate(mlp(), clipped)
