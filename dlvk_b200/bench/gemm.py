@@ -42,6 +42,9 @@ def main():
     ap.add_argument("--relu", action="store_true", help="ReLU in the epilogue")
     ap.add_argument("--residual", action="store_true", help="residual add in the epilogue")
     ap.add_argument("--mask", action="store_true", help="ReLU-mask input in the epilogue")
+    ap.add_argument("--out-f32", action="store_true",
+                    help="fp32 output, as for weight gradients (cuBLAS still writes bf16)")
+    ap.add_argument("--beta", type=float, default=0.0, help="accumulate: C = A B + beta C")
     ap.add_argument("--compare-single", action="store_true",
                     help="also time the single-CTA kernel (CTA-pair variant switched off)")
     args = ap.parse_args()
@@ -55,7 +58,8 @@ def main():
     peak = measured_peaks()["bf16_tflops"]
     for (M, N, K, am, bm) in shapes:
         a, b = make(M, N, K, am, bm)
-        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        out = torch.zeros(M, N, device="cuda", dtype=torch.float32 if args.out_f32 else torch.bfloat16)
+        out_cb = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
         flops = 2.0 * M * N * K
         kw = {}
         if args.bias:
@@ -66,8 +70,11 @@ def main():
             kw["residual"] = torch.randn(M, N, device="cuda").bfloat16()
         if args.mask:
             kw["relu_mask"] = torch.randn(M, N, device="cuda").bfloat16()
+        if args.beta:
+            kw["beta"] = args.beta
         t_ours = time_fn(lambda: C.gemm(a, b, out=out, force_path=1, **kw), iters=args.iters)
-        rec = {"M": M, "N": N, "K": K, "a": am, "b": bm, "epilogue": sorted(kw), "ours_ms": round(t_ours, 4),
+        rec = {"M": M, "N": N, "K": K, "a": am, "b": bm, "epilogue": sorted(kw), "out": str(out.dtype)[6:],
+               "ours_ms": round(t_ours, 4),
                "ours_tflops": round(flops / t_ours / 1e9, 1), "ours_frac_of_measured": round(flops / t_ours / 1e9 / peak, 3)}
         if args.compare_single:
             C.gemm_set_pair(False)
@@ -77,7 +84,7 @@ def main():
                 C.gemm_set_pair(True)
             rec.update({"single_cta_ms": round(t_1, 4), "single_cta_tflops": round(flops / t_1 / 1e9, 1)})
         if not args.no_cublas:
-            t_cb = time_fn(lambda: torch.matmul(a, b, out=out), iters=args.iters)
+            t_cb = time_fn(lambda: torch.matmul(a, b, out=out_cb), iters=args.iters)
             rec.update({"cublas_ms": round(t_cb, 4), "cublas_tflops": round(flops / t_cb / 1e9, 1),
                         "speedup_vs_cublas": round(t_cb / t_ours, 3)})
         if args.check:

@@ -198,9 +198,10 @@ std::vector<at::Tensor> batchnorm_fwd_op(const at::Tensor& x, c10::optional<at::
     rstd = at::rsqrt(*run_var + eps);  // tiny [C] vector
   }
   auto dd = drop_desc(training ? p : 0.0, stream_id, seed, step, step_t);
+  auto scratch = at::empty({batchnorm_scratch_floats(N, C, S)}, xc.options().dtype(at::kFloat));
   batchnorm_fwd(to_dtype(xc), xc.data_ptr(), optf(gamma), optf(beta), y.data_ptr(), mean.data_ptr<float>(),
                 rstd.data_ptr<float>(), training ? optfm(run_mean) : nullptr, training ? optfm(run_var) : nullptr, N,
-                C, S, (float)momentum, (float)eps, training, relu, dd, stream());
+                C, S, (float)momentum, (float)eps, training, relu, dd, scratch.data_ptr<float>(), stream());
   return {y, mean, rstd};
 }
 
@@ -215,7 +216,7 @@ at::Tensor batchnorm_bwd_op(const at::Tensor& x, const at::Tensor& dy, const at:
   const int N = (int)xc.size(0), C = (int)xc.size(1);
   const int S = (int)(xc.numel() / std::max<int64_t>(1, (int64_t)N * C));
   auto dx = at::empty_like(xc);
-  auto scratch = at::empty({2 * C}, xc.options().dtype(at::kFloat));
+  auto scratch = at::empty({batchnorm_scratch_floats(N, C, S)}, xc.options().dtype(at::kFloat));
   auto dd = drop_desc(p, stream_id, seed, step, step_t);
   batchnorm_bwd(to_dtype(xc), xc.data_ptr(), dyc.data_ptr(), mean.data_ptr<float>(), rstd.data_ptr<float>(),
                 optf(gamma), optf(beta), dx.data_ptr(), optfm(dgamma), optfm(dbeta), accumulate, N, C, S, relu, dd,

@@ -322,7 +322,7 @@ at::Tensor gemm_op(const at::Tensor& A, const at::Tensor& B, c10::optional<at::T
   const bool use_tc = force_path == 1 ? true : (force_path == 2 ? false : tc_ok);
   if (use_tc) {
     TORCH_CHECK(tc_ok, "dlvk.gemm: tensor-core path requested but not applicable to these operands");
-    const int64_t wsf = gemm_tc_workspace_floats(a, (int)max_ctas);
+    const int64_t wsf = gemm_tc_workspace_floats(a, (int)max_ctas, to_dtype(C));
     at::Tensor ws = wsf > 0 ? at::empty({wsf}, A.options().dtype(at::kFloat)) : at::Tensor();
     gemm_tc(to_dtype(C), a, stream(), device_error_word(), (int)max_ctas, wsf > 0 ? ws.data_ptr<float>() : nullptr,
             wsf);

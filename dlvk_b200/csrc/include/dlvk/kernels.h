@@ -77,10 +77,11 @@ bool gemm_tc_supported(const GemmArgs& a);
 // bf16 inputs, bf16 or f32 output, tcgen05 tensor cores.  `err` is the
 // device error word; `max_ctas` caps the persistent grid (0 = #SMs).
 // Split-K: when the tile grid underfills the GPU, partial sums go to an fp32
-// `workspace` of gemm_tc_workspace_floats() floats (0 = no split chosen) and a
+// `workspace` of gemm_tc_workspace_floats() floats (0 = none needed) and a
 // reduce kernel applies the epilogue.  With a null/small workspace the GEMM
-// runs unsplit.
-int64_t gemm_tc_workspace_floats(const GemmArgs& a, int max_ctas = 0);
+// runs unsplit.  An fp32 C with a linear epilogue (alpha, beta 0 or 1) needs
+// no workspace: the partials are added into C by TMA reduces.
+int64_t gemm_tc_workspace_floats(const GemmArgs& a, int max_ctas = 0, DType out_dt = DType::BF16);
 // CTA-pair (tcgen05 cta_group::2, 256 x 256 tiles) variant for unsplit bf16
 // GEMMs with M >= 256; on by default (DLVK_GEMM_PAIR=0 turns it off).
 bool gemm_tc_pair_enabled();
@@ -187,10 +188,11 @@ struct DropoutDesc {
   uint32_t step = 0;              // used when step_ptr is null
   const int64_t* step_ptr = nullptr;  // device step counter (graph replays)
 };
+// scratch (both passes): batchnorm_scratch_floats(N, C, S) floats.
+int64_t batchnorm_scratch_floats(int N, int C, int S);
 void batchnorm_fwd(DType dt, const void* x, const float* gamma, const float* beta, void* y, float* mean, float* rstd,
                    float* run_mean, float* run_var, int N, int C, int S, float momentum, float eps, bool training,
-                   bool relu, const DropoutDesc& dd, cudaStream_t s);
-// scratch: 2*C floats
+                   bool relu, const DropoutDesc& dd, float* scratch, cudaStream_t s);
 void batchnorm_bwd(DType dt, const void* x, const void* dy, const float* mean, const float* rstd, const float* gamma,
                    const float* beta, void* dx, float* dgamma, float* dbeta, bool accumulate, int N, int C, int S,
                    bool relu, const DropoutDesc& dd, float* scratch, cudaStream_t s);

@@ -201,6 +201,16 @@ __device__ __forceinline__ void tma_store_5d(const void* tmap, const void* src, 
                "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(v)
                : "memory");
 }
+// Element-wise atomic add of a shared-memory box into global memory
+// (performed by L2); the box layout and map are those of tma_store_5d.
+__device__ __forceinline__ void tma_reduce_add_5d(const void* tmap, const void* src, int x, int y, int z, int w,
+                                                  int v) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.5d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4, %5, %6}], [%1];" ::"l"(
+          tmap),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(v)
+      : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until at most N bulk groups still read their shared-memory source.
 template <int N>

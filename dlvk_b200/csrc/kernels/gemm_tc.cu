@@ -62,7 +62,8 @@ struct TcParams {
   int i8;                  // 1: int8 x int8 -> int32 (kind::i8), K-major operands
   const float* row_scale;  // int8 dequantisation: per-row (A) and per-column (B) scales
   const float* col_scale;
-  int tma_c;               // 1: plain epilogue stores C through per-warp smem boxes + TMA
+  int tma_c;               // 1: plain epilogue stores C through per-warp smem boxes + TMA;
+                           // 2: same boxes, added into fp32 C (split-K partials reduced in L2)
 };
 
 // PAIR: a 2-CTA cluster shares one 256 x BN tile (tcgen05 cta_group::2);
@@ -623,7 +624,8 @@ __global__ void __launch_bounds__(320, 1)
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              tma_store_5d(&tmC, box, n0, row0, bi, bo, sp);
+              if (p.tma_c == 2) tma_reduce_add_5d(&tmC, box, n0, row0, bi, bo, 0);
+              else tma_store_5d(&tmC, box, n0, row0, bi, bo, sp);
               bulk_commit_group();
             }
             ++ecount;
@@ -851,7 +853,10 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
 // measured for that tile shape) + the split-K partial traffic.  Pair units
 // are 256 x 256 tiles on sms/2 pairs (about 1.2x the single-CTA 128 x 256
 // rate on B200); single units are 128 x BN on sms CTAs.
-void choose_tiling(const GemmArgs& a, int sms, int& BN, int& splits, bool& pair) {
+// With `red` (split_red_ok) the partials are added into C by the epilogue's
+// TMA reduce in L2 (plus a clear of C when beta = 0) instead of the workspace
+// round trip and the reduce launch.
+void choose_tiling(const GemmArgs& a, int sms, int& BN, int& splits, bool& pair, bool red = false) {
   const int64_t kbs = (a.K + BK - 1) / BK;
   const double sm_flops = 8.1e12;
   double best = 1e300;
@@ -878,7 +883,11 @@ void choose_tiling(const GemmArgs& a, int sms, int& BN, int& splits, bool& pair)
       const double unit_s = (double)tile_m * c.bn * BK * 2.0 * ((kbs + sp - 1) / sp) /
                             (sm_flops * (c.pair ? 2 : 1) * c.eff);
       double t = waves * unit_s;
-      if (sp > 1) t += (double)sp * a.M * a.N * a.batch * a.batch2 * 8.0 / 5e12 + 5e-6;
+      if (sp > 1) {
+        const double mn = (double)a.M * a.N * a.batch * a.batch2;
+        t += red ? sp * mn * 4.0 / 8e12 + (a.beta == 0.f ? mn * 4.0 / 5e12 + 2e-6 : 0.0)
+                 : sp * mn * 8.0 / 5e12 + 5e-6;
+      }
       if (t < best * 0.97) {
         best = t;
         BN = c.bn;
@@ -889,6 +898,35 @@ void choose_tiling(const GemmArgs& a, int sms, int& BN, int& splits, bool& pair)
   }
 }
 
+}  // namespace
+
+namespace {
+// DLVK_GEMM_TMA_STORE=0 keeps the register-direct epilogue stores.
+bool tma_c_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("DLVK_GEMM_TMA_STORE");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+// DLVK_GEMM_SPLITK_RED=0 keeps split-K on the workspace + reduce-kernel path,
+// whose summation order is fixed (bitwise reproducible run to run).
+bool split_red_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("DLVK_GEMM_SPLITK_RED");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+// Split-K partials can be added straight into C: fp32 C without batching,
+// an epilogue that is linear in the accumulator (alpha only; beta 0 or 1),
+// and the alignment the fp32 C map needs.
+bool split_red_ok(DType out_dt, const GemmArgs& a) {
+  return split_red_enabled() && tma_c_enabled() && out_dt == DType::F32 && a.batch == 1 && a.batch2 == 1 &&
+         (a.beta == 0.f || a.beta == 1.f) && a.bias == nullptr && a.residual == nullptr &&
+         a.relu_mask == nullptr && a.act == ACT_NONE && al16(a.C) && (a.ldc * 4) % 16 == 0 &&
+         a.ldc * 4 < (1LL << 40) && a.N % 4 == 0;
+}
 }  // namespace
 
 bool gemm_tc_supported(const GemmArgs& a) {
@@ -908,20 +946,12 @@ bool gemm_tc_supported(const GemmArgs& a) {
 }
 
 namespace {
-// DLVK_GEMM_TMA_STORE=0 keeps the register-direct epilogue stores.
-bool tma_c_enabled() {
-  static const bool on = [] {
-    const char* e = std::getenv("DLVK_GEMM_TMA_STORE");
-    return !(e && e[0] == '0');
-  }();
-  return on;
-}
 // Plain epilogues (alpha, bias, activation; split-K partials included) store
 // C with TMA from per-warp 32 x 32 boxes: one async bulk store per box
 // instead of each lane writing its own row (32 scattered 16-byte stores per
 // warp instruction).  The map is 5-D {N, M, inner batch, outer batch, split}
 // with the epilogue's strides; sets p.tma_c when it applies.
-CUtensorMap make_c_map(TcParams& p, int64_t M, int64_t N) {
+CUtensorMap make_c_map(TcParams& p, int64_t M, int64_t N, bool reduce = false) {
   CUtensorMap tc;
   std::memset(&tc, 0, sizeof(tc));
   p.tma_c = 0;
@@ -931,10 +961,11 @@ CUtensorMap make_c_map(TcParams& p, int64_t M, int64_t N) {
     return cnt > 1 ? (uint64_t)stride * esz : (uint64_t)M * (uint64_t)p.ldc * esz;
   };
   const int64_t batch_outer = p.batch / p.batch2;
+  const int64_t slices = reduce ? 1 : p.splits;  // reduce: every split adds into the one C
   cuuint64_t dims[5] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)p.batch2, (cuuint64_t)batch_outer,
-                        (cuuint64_t)p.splits};
+                        (cuuint64_t)slices};
   cuuint64_t strides[4] = {(cuuint64_t)p.ldc * esz, pick(p.batch2, p.bsc2), pick(batch_outer, p.bsc),
-                           pick(p.splits, p.split_stride)};
+                           pick(slices, p.split_stride)};
   for (uint64_t st : strides)
     if (st == 0 || st % 16 != 0 || st >= (1ull << 40)) return tc;
   cuuint32_t box[5] = {32u, 32u, 1u, 1u, 1u};
@@ -943,7 +974,7 @@ CUtensorMap make_c_map(TcParams& p, int64_t M, int64_t N) {
                            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                            p.out_f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r == CUDA_SUCCESS) p.tma_c = 1;
+  if (r == CUDA_SUCCESS) p.tma_c = reduce ? 2 : 1;
   return tc;
 }
 }  // namespace
@@ -969,8 +1000,10 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
   const bool b_k = (a.sbk == 1);
   int BN = 256, splits = 1;
   bool pair = false;
-  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits, pair);
-  if (workspace == nullptr || workspace_floats < (int64_t)splits * a.M * a.N * a.batch * a.batch2) splits = 1;
+  const bool red = split_red_ok(out_dt, a);
+  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits, pair, red);
+  if (!red && (workspace == nullptr || workspace_floats < (int64_t)splits * a.M * a.N * a.batch * a.batch2))
+    splits = 1;
   pair = pair && max_ctas != 1;
   // Unused batch levels get a harmless stride (a multiple of 16 bytes).
   auto pick = [](int64_t cnt, int64_t stride, uint64_t dflt) { return cnt > 1 ? (uint64_t)stride : dflt; };
@@ -1032,6 +1065,25 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
   p.splits = splits;
   p.kb_per_split = (int)(((a.K + BK - 1) / BK + splits - 1) / splits);
   p.split_stride = 0;
+  if (splits > 1 && red) {
+    // Every split's epilogue adds alpha * partial into C with a TMA reduce;
+    // C starts from zero (beta = 0) or from its old value (beta = 1).
+    p.beta = 0.f;  // the epilogue itself never reads C
+    const CUtensorMap tc = make_c_map(p, a.M, a.N, true);
+    if (p.tma_c == 2) {
+      if (a.beta == 0.f)
+        DLVK_CUDA_CHECK(cudaMemset2DAsync(a.C, (size_t)a.ldc * 4, 0, (size_t)a.N * 4, (size_t)a.M, s));
+      if (pair) launch_tc_pair(ta, tb, tc, p, max_ctas, s);
+      else if (BN == 256) launch_tc<256>(ta, tb, tc, p, max_ctas, s);
+      else launch_tc<128>(ta, tb, tc, p, max_ctas, s);
+      return;
+    }
+    // The map was refused: run unsplit.
+    p.beta = a.beta;
+    splits = 1;
+    p.splits = 1;
+    p.kb_per_split = (int)((a.K + BK - 1) / BK);
+  }
   if (splits > 1) {
     // Partial accumulators go to the fp32 workspace; the reduce kernel
     // applies alpha/beta/bias/residual/act/mask and writes C.
@@ -1079,7 +1131,8 @@ bool gemm_tc_pair_enabled() { return pair_flag() != 0; }
 
 void gemm_tc_set_pair(bool on) { pair_flag() = on ? 1 : 0; }
 
-int64_t gemm_tc_workspace_floats(const GemmArgs& a, int max_ctas) {
+int64_t gemm_tc_workspace_floats(const GemmArgs& a, int max_ctas, DType out_dt) {
+  if (split_red_ok(out_dt, a)) return 0;
   int BN = 256, splits = 1;
   bool pair = false;
   choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits, pair);

@@ -37,166 +37,418 @@ __device__ __forceinline__ uint32_t read_step(const DropoutDesc& d) {
 }
 
 // ------------------------------------------------------------------ batch norm
-// Column statistics of x viewed as [N, C, S]; one thread block of 256 threads
-// per group of channels.  S == 1 (BatchNorm1D): 64 channels per block, rows
-// strided over 4 thread rows.  S > 1: one block per channel.
-// Uses shifted sums (shift = first element) for a stable variance.
+// Scalar fallbacks of the element-wise passes (odd totals, unaligned
+// tensors); same coefficients and masks as the 8-wide kernels.
 template <typename T>
-__global__ void bn_stats_kernel(const T* __restrict__ x, int N, int C, int S, float* __restrict__ mean,
-                                float* __restrict__ rstd, float* __restrict__ run_mean, float* __restrict__ run_var,
-                                float momentum, float eps) {
-  if (S == 1) {
-    __shared__ float s1[4][64], s2[4][64];
-    const int cl = threadIdx.x & 63, rg = threadIdx.x >> 6;
-    const int c = blockIdx.x * 64 + cl;
-    float a = 0.f, b = 0.f, shift = 0.f;
-    if (c < C) {
-      shift = to_f32(x[c]);
-      for (int n = rg; n < N; n += 4) {
-        const float v = to_f32(x[(int64_t)n * C + c]) - shift;
-        a += v;
-        b += v * v;
-      }
-    }
-    s1[rg][cl] = a;
-    s2[rg][cl] = b;
-    __syncthreads();
-    if (rg == 0 && c < C) {
-      a = s1[0][cl] + s1[1][cl] + s1[2][cl] + s1[3][cl];
-      b = s2[0][cl] + s2[1][cl] + s2[2][cl] + s2[3][cl];
-      const float m1 = a / N;
-      const float var = fmaxf(b / N - m1 * m1, 0.f);
-      const float mu = m1 + shift;
-      mean[c] = mu;
-      rstd[c] = rsqrtf(var + eps);
-      if (run_mean) run_mean[c] = (1.f - momentum) * run_mean[c] + momentum * mu;
-      if (run_var) run_var[c] = (1.f - momentum) * run_var[c] + momentum * var;
-    }
-  } else {
-    __shared__ float sm[32];
-    const int c = blockIdx.x;
-    const float shift = to_f32(x[(int64_t)c * S]);
-    float a = 0.f, b = 0.f;
-    const int64_t cnt = (int64_t)N * S;
-    for (int64_t i = threadIdx.x; i < cnt; i += blockDim.x) {
-      const int64_t n = i / S, sp = i - n * S;
-      const float v = to_f32(x[(n * C + c) * S + sp]) - shift;
-      a += v;
-      b += v * v;
-    }
-    a = block_sum(a, sm);
-    b = block_sum(b, sm);
-    if (threadIdx.x == 0) {
-      const float m1 = a / cnt;
-      const float var = fmaxf(b / cnt - m1 * m1, 0.f);
-      const float mu = m1 + shift;
-      mean[c] = mu;
-      rstd[c] = rsqrtf(var + eps);
-      if (run_mean) run_mean[c] = (1.f - momentum) * run_mean[c] + momentum * mu;
-      if (run_var) run_var[c] = (1.f - momentum) * run_var[c] + momentum * var;
-    }
-  }
-}
-
-// y = dropout(relu(gamma * (x - mean) * rstd + beta))
-template <typename T>
-__global__ void bn_apply_kernel(const T* __restrict__ x, const float* __restrict__ mean, const float* __restrict__ rstd,
-                                const float* __restrict__ gamma, const float* __restrict__ beta, T* __restrict__ y,
-                                int64_t total, int C, int S, int relu, DropoutDesc dd) {
+__global__ void bn_apply_kernel(const T* __restrict__ x, const float* __restrict__ scale,
+                                const float* __restrict__ shift, T* __restrict__ y, int64_t total, int C, int S,
+                                int relu, DropoutDesc dd) {
   const uint32_t step = read_step(dd);
   const float inv_keep = dd.p > 0.f ? 1.f / (1.f - dd.p) : 1.f;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int c = (int)((i / S) % C);
-    float v = (to_f32(x[i]) - mean[c]) * rstd[c] * (gamma ? gamma[c] : 1.f) + (beta ? beta[c] : 0.f);
+    float v = fmaf(to_f32(x[i]), scale[c], shift[c]);
     if (relu) v = fmaxf(v, 0.f);
     if (dd.p > 0.f) v = keep_elem(i, dd, step) ? v * inv_keep : 0.f;
     y[i] = from_f32<T>(v);
   }
 }
 
-// Gradient w.r.t. the normalised pre-activation, undoing dropout and ReLU.
 template <typename T>
-__device__ __forceinline__ float bn_upstream(const T* dy, const T* x, int64_t i, int c, const float* mean,
-                                             const float* rstd, const float* gamma, const float* beta, int relu,
-                                             const DropoutDesc& dd, uint32_t step, float inv_keep, float& xhat) {
-  xhat = (to_f32(x[i]) - mean[c]) * rstd[c];
-  float g = to_f32(dy[i]);
-  if (dd.p > 0.f) g = keep_elem(i, dd, step) ? g * inv_keep : 0.f;
-  if (relu) {
-    const float pre = xhat * (gamma ? gamma[c] : 1.f) + (beta ? beta[c] : 0.f);
-    if (!(pre > 0.f)) g = 0.f;
-  }
-  return g;
-}
-
-// Per-channel sums: sg[c] = sum g, sgx[c] = sum g * xhat.  Same layouts as
-// bn_stats_kernel.  Writes dbeta/dgamma (optionally accumulating).
-template <typename T>
-__global__ void bn_bwd_reduce_kernel(const T* __restrict__ x, const T* __restrict__ dy, const float* __restrict__ mean,
-                                     const float* __restrict__ rstd, const float* __restrict__ gamma,
-                                     const float* __restrict__ beta, int N, int C, int S, int relu, DropoutDesc dd,
-                                     float* __restrict__ sg_out, float* __restrict__ sgx_out,
-                                     float* __restrict__ dgamma, float* __restrict__ dbeta, int accumulate) {
-  const uint32_t step = read_step(dd);
-  const float inv_keep = dd.p > 0.f ? 1.f / (1.f - dd.p) : 1.f;
-  float a = 0.f, b = 0.f;
-  int c;
-  if (S == 1) {
-    __shared__ float s1[4][64], s2[4][64];
-    const int cl = threadIdx.x & 63, rg = threadIdx.x >> 6;
-    c = blockIdx.x * 64 + cl;
-    if (c < C) {
-      for (int n = rg; n < N; n += 4) {
-        float xh;
-        const int64_t i = (int64_t)n * C + c;
-        const float g = bn_upstream(dy, x, i, c, mean, rstd, gamma, beta, relu, dd, step, inv_keep, xh);
-        a += g;
-        b += g * xh;
-      }
-    }
-    s1[rg][cl] = a;
-    s2[rg][cl] = b;
-    __syncthreads();
-    if (rg != 0 || c >= C) return;
-    a = s1[0][cl] + s1[1][cl] + s1[2][cl] + s1[3][cl];
-    b = s2[0][cl] + s2[1][cl] + s2[2][cl] + s2[3][cl];
-  } else {
-    __shared__ float sm[32];
-    c = blockIdx.x;
-    const int64_t cnt = (int64_t)N * S;
-    for (int64_t k = threadIdx.x; k < cnt; k += blockDim.x) {
-      const int64_t n = k / S, sp = k - n * S;
-      const int64_t i = (n * C + c) * S + sp;
-      float xh;
-      const float g = bn_upstream(dy, x, i, c, mean, rstd, gamma, beta, relu, dd, step, inv_keep, xh);
-      a += g;
-      b += g * xh;
-    }
-    a = block_sum(a, sm);
-    b = block_sum(b, sm);
-    if (threadIdx.x != 0) return;
-  }
-  sg_out[c] = a;
-  sgx_out[c] = b;
-  if (dbeta) dbeta[c] = accumulate ? dbeta[c] + a : a;
-  if (dgamma) dgamma[c] = accumulate ? dgamma[c] + b : b;
-}
-
-// dx = gamma * rstd * (g - sg / M - xhat * sgx / M)
-template <typename T>
-__global__ void bn_bwd_apply_kernel(const T* __restrict__ x, const T* __restrict__ dy, const float* __restrict__ mean,
-                                    const float* __restrict__ rstd, const float* __restrict__ gamma,
-                                    const float* __restrict__ beta, const float* __restrict__ sg,
-                                    const float* __restrict__ sgx, T* __restrict__ dx, int64_t total, int C, int S,
-                                    int relu, DropoutDesc dd, float inv_count) {
+__global__ void bn_bwd_apply_kernel(const T* __restrict__ x, const T* __restrict__ dy, const float* __restrict__ A,
+                                    const float* __restrict__ B, const float* __restrict__ D,
+                                    const float* __restrict__ shift, T* __restrict__ dx, int64_t total, int C, int S,
+                                    int relu, DropoutDesc dd) {
   const uint32_t step = read_step(dd);
   const float inv_keep = dd.p > 0.f ? 1.f / (1.f - dd.p) : 1.f;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int c = (int)((i / S) % C);
-    float xh;
-    const float g = bn_upstream(dy, x, i, c, mean, rstd, gamma, beta, relu, dd, step, inv_keep, xh);
-    const float v = (gamma ? gamma[c] : 1.f) * rstd[c] * (g - sg[c] * inv_count - xh * sgx[c] * inv_count);
-    dx[i] = from_f32<T>(v);
+    const float xv = to_f32(x[i]);
+    float g = to_f32(dy[i]);
+    if (dd.p > 0.f) g = keep_elem(i, dd, step) ? g * inv_keep : 0.f;
+    if (relu && !(fmaf(xv, A[c], shift[c]) > 0.f)) g = 0.f;
+    dx[i] = from_f32<T>(fmaf(A[c], g, fmaf(B[c], xv, D[c])));
+  }
+}
+
+// ---- BatchNorm, wide grids ---------------------------------------------------
+// The reductions run in two passes: per-chunk partial sums over a 2-D grid
+// (channel group x row chunk), then one thread per channel adds the chunks.
+// The element-wise passes move 8 elements per thread (16-byte bf16 accesses)
+// and draw the dropout mask one Philox block per 4 elements.
+
+// Keep flags of elements i0 .. i0+7 (i0 a multiple of 4): the same mask as
+// keep_elem() element by element.
+__device__ __forceinline__ void keep8(int64_t i0, const DropoutDesc& d, uint32_t step, bool k[8]) {
+  const uint4 r0 = philox_block((uint64_t)i0 >> 2, d.stream, step, d.seed);
+  const uint4 r1 = philox_block(((uint64_t)i0 >> 2) + 1, d.stream, step, d.seed);
+  k[0] = u01(r0.x) >= d.p; k[1] = u01(r0.y) >= d.p; k[2] = u01(r0.z) >= d.p; k[3] = u01(r0.w) >= d.p;
+  k[4] = u01(r1.x) >= d.p; k[5] = u01(r1.y) >= d.p; k[6] = u01(r1.z) >= d.p; k[7] = u01(r1.w) >= d.p;
+}
+__device__ __forceinline__ void load8(const float* p, float v[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float v[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = __bfloat1622float2(h[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void store8(float* p, const float v[8]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float v[8]) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+constexpr int BN_GROUP = 256;  // channels per block when S == 1 (8 per thread, 32 threads)
+
+// Pass 1.  MODE 0 (statistics): a = sum(x - x0), b = sum((x - x0)^2) with x0
+// the channel's first element (shifted sums keep the variance stable).
+// MODE 1 (backward): a = sum(g), b = sum(g * xhat), g the upstream gradient
+// through dropout and ReLU.  Grid (groups, chunks); `per` is rows per chunk
+// when S == 1 (a group is BN_GROUP channels, 8 row lanes per block) and
+// elements of the channel per chunk when S > 1 (a group is one channel).
+// Output: part[chunk * C + c] (a) and part[(chunks + chunk) * C + c] (b).
+template <typename T, int MODE>
+__global__ void __launch_bounds__(256) bn_partial_kernel(const T* __restrict__ x, const T* __restrict__ dy,
+                                                         const float* __restrict__ mean,
+                                                         const float* __restrict__ rstd,
+                                                         const float* __restrict__ gamma,
+                                                         const float* __restrict__ beta, int N, int C, int S,
+                                                         int64_t per, int relu, DropoutDesc dd, int vec,
+                                                         float* __restrict__ part) {
+  const uint32_t step = MODE == 1 ? read_step(dd) : 0u;
+  const float inv_keep = dd.p > 0.f ? 1.f / (1.f - dd.p) : 1.f;
+  const int chunk = blockIdx.y, chunks = gridDim.y;
+  if (S == 1) {
+    __shared__ float sa[8][BN_GROUP + 1], sb[8][BN_GROUP + 1];
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    const int c0 = blockIdx.x * BN_GROUP + tx * 8;
+    float a[8], b[8], k0[8], k1[8], k2[8], k3[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = min(c0 + j, C - 1);
+      a[j] = b[j] = 0.f;
+      if (MODE == 0) {
+        k0[j] = to_f32(x[c]);
+      } else {
+        k0[j] = mean[c];
+        k1[j] = rstd[c];
+        k2[j] = (gamma ? gamma[c] : 1.f) * k1[j];      // the forward's scale
+        k3[j] = (beta ? beta[c] : 0.f) - k0[j] * k2[j];  // and shift
+      }
+    }
+    const int64_t n0 = (int64_t)chunk * per, n1 = min((int64_t)N, n0 + per);
+    if (c0 < C) {
+#pragma unroll 2
+      for (int64_t n = n0 + ty; n < n1; n += 8) {
+        const int64_t i0 = n * C + c0;
+        float xv[8], gv[8];
+        bool keep[8];
+        if (vec) {
+          load8(x + i0, xv);
+          if (MODE == 1) {
+            load8(dy + i0, gv);
+            if (dd.p > 0.f) keep8(i0, dd, step, keep);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const bool in = c0 + j < C;
+            xv[j] = in ? to_f32(x[i0 + j]) : 0.f;
+            if (MODE == 1) {
+              gv[j] = in ? to_f32(dy[i0 + j]) : 0.f;
+              keep[j] = dd.p > 0.f && in ? keep_elem(i0 + j, dd, step) : true;
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (c0 + j >= C) continue;
+          if (MODE == 0) {
+            const float v = xv[j] - k0[j];
+            a[j] += v;
+            b[j] += v * v;
+          } else {
+            const float xh = (xv[j] - k0[j]) * k1[j];
+            float g = gv[j];
+            if (dd.p > 0.f) g = keep[j] ? g * inv_keep : 0.f;
+            if (relu && !(fmaf(xv[j], k2[j], k3[j]) > 0.f)) g = 0.f;
+            a[j] += g;
+            b[j] += g * xh;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      sa[ty][tx * 8 + j] = a[j];
+      sb[ty][tx * 8 + j] = b[j];
+    }
+    __syncthreads();
+    const int cl = threadIdx.x, c = blockIdx.x * BN_GROUP + cl;
+    if (c < C) {
+      float ra = 0.f, rb = 0.f;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        ra += sa[r][cl];
+        rb += sb[r][cl];
+      }
+      part[(int64_t)chunk * C + c] = ra;
+      part[(int64_t)(chunks + chunk) * C + c] = rb;
+    }
+  } else {
+    __shared__ float sm[32];
+    const int c = blockIdx.x;
+    const int64_t cnt = (int64_t)N * S;
+    const int64_t k0 = (int64_t)chunk * per, k1 = min(cnt, k0 + per);
+    float sh = 0.f, mu = 0.f, rs = 0.f, sc = 1.f, sf = 0.f;
+    if (MODE == 0) {
+      sh = to_f32(x[(int64_t)c * S]);
+    } else {
+      mu = mean[c];
+      rs = rstd[c];
+      sc = (gamma ? gamma[c] : 1.f) * rs;
+      sf = (beta ? beta[c] : 0.f) - mu * sc;
+    }
+    float a = 0.f, b = 0.f;
+    for (int64_t k = k0 + threadIdx.x; k < k1; k += blockDim.x) {
+      const int64_t n = k / S, sp = k - n * S;
+      const int64_t i = (n * C + c) * S + sp;
+      if (MODE == 0) {
+        const float v = to_f32(x[i]) - sh;
+        a += v;
+        b += v * v;
+      } else {
+        const float xv = to_f32(x[i]);
+        const float xh = (xv - mu) * rs;
+        float g = to_f32(dy[i]);
+        if (dd.p > 0.f) g = keep_elem(i, dd, step) ? g * inv_keep : 0.f;
+        if (relu && !(fmaf(xv, sc, sf) > 0.f)) g = 0.f;
+        a += g;
+        b += g * xh;
+      }
+    }
+    a = block_sum(a, sm);
+    b = block_sum(b, sm);
+    if (threadIdx.x == 0) {
+      part[(int64_t)chunk * C + c] = a;
+      part[(int64_t)(chunks + chunk) * C + c] = b;
+    }
+  }
+}
+
+// Per-channel coefficients of the element-wise passes, so that every element
+// costs one fma per term:
+//   forward   pre = fma(x, scale, shift), scale = gamma * rstd,
+//             shift = beta - mean * scale;  y = dropout(relu(pre))
+//   backward  dx = A * g + B * x + D with g the masked upstream gradient,
+//             A = gamma * rstd, B = -A * rstd * sgx / M,
+//             D = -A * sg / M - B * mean  (the ReLU test reuses pre).
+// Scratch layout (floats): [scale | shift | A | B | D | sg | sgx | partials].
+struct BnCoef {
+  float* scale;
+  float* shift;
+  float* A;
+  float* B;
+  float* D;
+  float* sg;
+  float* sgx;
+  float* part;
+};
+__host__ __device__ inline BnCoef bn_coef(float* scratch, int C) {
+  return BnCoef{scratch, scratch + C, scratch + 2 * (int64_t)C, scratch + 3 * (int64_t)C, scratch + 4 * (int64_t)C,
+                scratch + 5 * (int64_t)C, scratch + 6 * (int64_t)C, scratch + 7 * (int64_t)C};
+}
+
+// Sum of the chunk partials of 32 channels per block, 8 lanes per channel.
+__device__ __forceinline__ bool bn_sum_chunks(const float* __restrict__ part, int chunks, int C, float& a, float& b) {
+  __shared__ float sa[8][33], sb[8][33];
+  const int cl = threadIdx.x & 31, ly = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + cl;
+  a = 0.f;
+  b = 0.f;
+  if (c < C)
+    for (int k = ly; k < chunks; k += 8) {
+      a += part[(int64_t)k * C + c];
+      b += part[(int64_t)(chunks + k) * C + c];
+    }
+  sa[ly][cl] = a;
+  sb[ly][cl] = b;
+  __syncthreads();
+  if (ly != 0 || c >= C) return false;
+#pragma unroll
+  for (int r = 1; r < 8; ++r) {
+    a += sa[r][cl];
+    b += sb[r][cl];
+  }
+  return true;
+}
+
+// Pass 2 of the statistics: mean, rstd, the running averages and the forward
+// coefficients.  The running variance tracks the population (divide-by-count)
+// variance, as the reference's layer does (src/layers/batch_norm_layers.cpp:
+// 79-90).
+template <typename T>
+__global__ void __launch_bounds__(256) bn_stats_finalize_kernel(const float* __restrict__ part, int chunks,
+                                                                const T* __restrict__ x, int C, int S, int64_t count,
+                                                                float* __restrict__ mean, float* __restrict__ rstd,
+                                                                float* __restrict__ run_mean,
+                                                                float* __restrict__ run_var, float momentum, float eps,
+                                                                const float* __restrict__ gamma,
+                                                                const float* __restrict__ beta, BnCoef co) {
+  float a, b;
+  if (!bn_sum_chunks(part, chunks, C, a, b)) return;
+  const int c = blockIdx.x * 32 + (threadIdx.x & 31);
+  const float m1 = a / (float)count;
+  const float var = fmaxf(b / (float)count - m1 * m1, 0.f);
+  const float mu = m1 + to_f32(x[(int64_t)c * S]);
+  const float rs = rsqrtf(var + eps);
+  mean[c] = mu;
+  rstd[c] = rs;
+  if (run_mean) run_mean[c] = (1.f - momentum) * run_mean[c] + momentum * mu;
+  if (run_var) run_var[c] = (1.f - momentum) * run_var[c] + momentum * var;
+  const float sc = (gamma ? gamma[c] : 1.f) * rs;
+  co.scale[c] = sc;
+  co.shift[c] = (beta ? beta[c] : 0.f) - mu * sc;
+}
+
+// Forward coefficients from given statistics (inference: running stats).
+__global__ void bn_coef_kernel(const float* __restrict__ mean, const float* __restrict__ rstd,
+                               const float* __restrict__ gamma, const float* __restrict__ beta, int C, BnCoef co) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const float sc = (gamma ? gamma[c] : 1.f) * rstd[c];
+  co.scale[c] = sc;
+  co.shift[c] = (beta ? beta[c] : 0.f) - mean[c] * sc;
+}
+
+// Pass 2 of the backward reduction: sg, sgx, the parameter gradients and the
+// backward coefficients.
+__global__ void __launch_bounds__(256) bn_bwd_finalize_kernel(const float* __restrict__ part, int chunks, int C,
+                                                              const float* __restrict__ mean,
+                                                              const float* __restrict__ rstd,
+                                                              const float* __restrict__ gamma,
+                                                              const float* __restrict__ beta, float inv_count,
+                                                              float* __restrict__ dgamma, float* __restrict__ dbeta,
+                                                              int accumulate, BnCoef co) {
+  float a, b;
+  if (!bn_sum_chunks(part, chunks, C, a, b)) return;
+  const int c = blockIdx.x * 32 + (threadIdx.x & 31);
+  co.sg[c] = a;
+  co.sgx[c] = b;
+  if (dbeta) dbeta[c] = accumulate ? dbeta[c] + a : a;
+  if (dgamma) dgamma[c] = accumulate ? dgamma[c] + b : b;
+  const float rs = rstd[c], A = (gamma ? gamma[c] : 1.f) * rs;
+  const float B = -A * rs * b * inv_count;
+  co.A[c] = A;
+  co.B[c] = B;
+  co.D[c] = -A * a * inv_count - B * mean[c];
+  co.shift[c] = (beta ? beta[c] : 0.f) - mean[c] * A;
+}
+
+// Channel of element i0 and its position inside the channel's S run.
+__device__ __forceinline__ void bn_chan(int64_t i0, int C, int S, int& c, int& sp) {
+  if (S == 1) {
+    c = (int)(i0 % C);
+    sp = 0;
+  } else {
+    const int64_t q = i0 / S;
+    sp = (int)(i0 - q * S);
+    c = (int)(q % C);
+  }
+}
+__device__ __forceinline__ void bn_next(int C, int S, int& c, int& sp) {
+  if (++sp >= S) {
+    sp = 0;
+    if (++c == C) c = 0;
+  }
+}
+// Coefficients of the 8 elements from i0: one pair of float4 loads per array
+// when the 8 elements are 8 consecutive channels (S == 1, C % 8 == 0).
+template <int NA>
+__device__ __forceinline__ void bn_coef8(const float* const (&arr)[NA], int64_t i0, int C, int S, bool chan8,
+                                         float (&o)[NA][8]) {
+  if (chan8) {
+    const int c0 = (int)(i0 % C);
+#pragma unroll
+    for (int a = 0; a < NA; ++a) load8(arr[a] + c0, o[a]);
+  } else {
+    int c, sp;
+    bn_chan(i0, C, S, c, sp);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int a = 0; a < NA; ++a) o[a][j] = arr[a][c];
+      bn_next(C, S, c, sp);
+    }
+  }
+}
+
+// y = dropout(relu(x * scale + shift)), 8 elements per thread (total % 8 == 0,
+// 16-byte aligned x and y).
+template <typename T>
+__global__ void bn_apply_vec_kernel(const T* __restrict__ x, BnCoef co, T* __restrict__ y, int64_t total, int C,
+                                    int S, int relu, DropoutDesc dd) {
+  const uint32_t step = read_step(dd);
+  const float inv_keep = dd.p > 0.f ? 1.f / (1.f - dd.p) : 1.f;
+  const bool chan8 = S == 1 && (C & 7) == 0;
+  const float* const arr[2] = {co.scale, co.shift};
+  const int64_t n8 = total >> 3;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n8; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i0 = t << 3;
+    float v[8], k[2][8];
+    bool keep[8];
+    load8(x + i0, v);
+    bn_coef8<2>(arr, i0, C, S, chan8, k);
+    if (dd.p > 0.f) keep8(i0, dd, step, keep);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float o = fmaf(v[j], k[0][j], k[1][j]);
+      if (relu) o = fmaxf(o, 0.f);
+      if (dd.p > 0.f) o = keep[j] ? o * inv_keep : 0.f;
+      v[j] = o;
+    }
+    store8(y + i0, v);
+  }
+}
+
+// dx = A * g + B * x + D, 8 elements per thread.
+template <typename T>
+__global__ void bn_bwd_apply_vec_kernel(const T* __restrict__ x, const T* __restrict__ dy, BnCoef co,
+                                        T* __restrict__ dx, int64_t total, int C, int S, int relu, DropoutDesc dd) {
+  const uint32_t step = read_step(dd);
+  const float inv_keep = dd.p > 0.f ? 1.f / (1.f - dd.p) : 1.f;
+  const bool chan8 = S == 1 && (C & 7) == 0;
+  const float* const arr[4] = {co.A, co.B, co.D, co.shift};
+  const int64_t n8 = total >> 3;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n8; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i0 = t << 3;
+    float xv[8], gv[8], k[4][8];
+    bool keep[8];
+    load8(x + i0, xv);
+    load8(dy + i0, gv);
+    bn_coef8<4>(arr, i0, C, S, chan8, k);
+    if (dd.p > 0.f) keep8(i0, dd, step, keep);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float g = gv[j];
+      if (dd.p > 0.f) g = keep[j] ? g * inv_keep : 0.f;
+      if (relu && !(fmaf(xv[j], k[0][j], k[3][j]) > 0.f)) g = 0.f;
+      xv[j] = fmaf(k[0][j], g, fmaf(k[1][j], xv[j], k[2][j]));
+    }
+    store8(dx + i0, xv);
   }
 }
 
@@ -653,35 +905,87 @@ inline unsigned grid1d(int64_t n) { return (unsigned)std::max<int64_t>(1, std::m
 
 }  // namespace
 
+namespace {
+// Row chunks of the BatchNorm reductions: about four blocks per SM.
+void bn_grid(int N, int C, int S, unsigned& groups, unsigned& chunks, int64_t& per) {
+  if (S == 1) {
+    groups = (unsigned)((C + BN_GROUP - 1) / BN_GROUP);
+    const int64_t want = std::max<int64_t>(1, (4 * 148 + (int64_t)groups - 1) / groups);
+    const int64_t ch = std::min<int64_t>(std::min<int64_t>(want, std::max<int64_t>(1, N / 8)), 1024);
+    per = (N + ch - 1) / ch;
+    chunks = (unsigned)((N + per - 1) / per);
+  } else {
+    groups = (unsigned)C;
+    const int64_t cnt = (int64_t)N * S;
+    const int64_t want = std::max<int64_t>(1, (4 * 148 + C - 1) / C);
+    const int64_t ch = std::min<int64_t>(std::min<int64_t>(want, std::max<int64_t>(1, cnt / 2048)), 1024);
+    per = (cnt + ch - 1) / ch;
+    chunks = (unsigned)((cnt + per - 1) / per);
+  }
+}
+bool al16p(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+}  // namespace
+
+int64_t batchnorm_scratch_floats(int N, int C, int S) {
+  unsigned groups, chunks;
+  int64_t per;
+  bn_grid(N, C, S, groups, chunks, per);
+  return 7 * (int64_t)C + 2 * (int64_t)chunks * C;
+}
+
 void batchnorm_fwd(DType dt, const void* x, const float* gamma, const float* beta, void* y, float* mean, float* rstd,
                    float* run_mean, float* run_var, int N, int C, int S, float momentum, float eps, bool training,
-                   bool relu, const DropoutDesc& dd, cudaStream_t s) {
+                   bool relu, const DropoutDesc& dd, float* scratch, cudaStream_t s) {
+  const BnCoef co = bn_coef(scratch, C);
   if (training) {
-    const unsigned g = S == 1 ? (unsigned)((C + 63) / 64) : (unsigned)C;
-    DLVK_DISPATCH_FB(dt, "batchnorm_fwd", bn_stats_kernel<T><<<g, 256, 0, s>>>(
-        (const T*)x, N, C, S, mean, rstd, run_mean, run_var, momentum, eps));
+    unsigned groups, chunks;
+    int64_t per;
+    bn_grid(N, C, S, groups, chunks, per);
+    const int vec = (S == 1 && C % 8 == 0 && al16p(x)) ? 1 : 0;
+    DLVK_DISPATCH_FB(dt, "batchnorm_fwd", bn_partial_kernel<T, 0><<<dim3(groups, chunks), 256, 0, s>>>(
+        (const T*)x, nullptr, nullptr, nullptr, nullptr, nullptr, N, C, S, per, 0, DropoutDesc{}, vec, co.part));
     DLVK_POST_LAUNCH();
+    DLVK_DISPATCH_FB(dt, "batchnorm_fwd", bn_stats_finalize_kernel<T><<<(C + 31) / 32, 256, 0, s>>>(
+        co.part, (int)chunks, (const T*)x, C, S, (int64_t)N * S, mean, rstd, run_mean, run_var, momentum, eps,
+        gamma, beta, co));
+  } else {
+    bn_coef_kernel<<<(C + 255) / 256, 256, 0, s>>>(mean, rstd, gamma, beta, C, co);
   }
+  DLVK_POST_LAUNCH();
   const int64_t total = (int64_t)N * C * S;
-  DLVK_DISPATCH_FB(dt, "batchnorm_fwd", bn_apply_kernel<T><<<grid1d(total), 256, 0, s>>>(
-      (const T*)x, mean, rstd, gamma, beta, (T*)y, total, C, S, relu ? 1 : 0, dd));
+  if (total % 8 == 0 && al16p(x) && al16p(y) && al16p(scratch) && C % 4 == 0) {
+    DLVK_DISPATCH_FB(dt, "batchnorm_fwd", bn_apply_vec_kernel<T><<<grid1d(total / 8), 256, 0, s>>>(
+        (const T*)x, co, (T*)y, total, C, S, relu ? 1 : 0, dd));
+  } else {
+    DLVK_DISPATCH_FB(dt, "batchnorm_fwd", bn_apply_kernel<T><<<grid1d(total), 256, 0, s>>>(
+        (const T*)x, co.scale, co.shift, (T*)y, total, C, S, relu ? 1 : 0, dd));
+  }
   DLVK_POST_LAUNCH();
 }
 
 void batchnorm_bwd(DType dt, const void* x, const void* dy, const float* mean, const float* rstd, const float* gamma,
                    const float* beta, void* dx, float* dgamma, float* dbeta, bool accumulate, int N, int C, int S,
                    bool relu, const DropoutDesc& dd, float* scratch, cudaStream_t s) {
-  float* sg = scratch;
-  float* sgx = scratch + C;
-  const unsigned g = S == 1 ? (unsigned)((C + 63) / 64) : (unsigned)C;
-  DLVK_DISPATCH_FB(dt, "batchnorm_bwd", bn_bwd_reduce_kernel<T><<<g, 256, 0, s>>>(
-      (const T*)x, (const T*)dy, mean, rstd, gamma, beta, N, C, S, relu ? 1 : 0, dd, sg, sgx, dgamma, dbeta,
-      accumulate ? 1 : 0));
+  const BnCoef co = bn_coef(scratch, C);
+  unsigned groups, chunks;
+  int64_t per;
+  bn_grid(N, C, S, groups, chunks, per);
+  const int vec = (S == 1 && C % 8 == 0 && al16p(x) && al16p(dy)) ? 1 : 0;
+  DLVK_DISPATCH_FB(dt, "batchnorm_bwd", bn_partial_kernel<T, 1><<<dim3(groups, chunks), 256, 0, s>>>(
+      (const T*)x, (const T*)dy, mean, rstd, gamma, beta, N, C, S, per, relu ? 1 : 0, dd, vec, co.part));
+  DLVK_POST_LAUNCH();
+  const float inv_count = 1.f / (float)((int64_t)N * S);
+  bn_bwd_finalize_kernel<<<(C + 31) / 32, 256, 0, s>>>(co.part, (int)chunks, C, mean, rstd, gamma, beta, inv_count,
+                                                        dgamma, dbeta, accumulate ? 1 : 0, co);
   DLVK_POST_LAUNCH();
   const int64_t total = (int64_t)N * C * S;
-  DLVK_DISPATCH_FB(dt, "batchnorm_bwd", bn_bwd_apply_kernel<T><<<grid1d(total), 256, 0, s>>>(
-      (const T*)x, (const T*)dy, mean, rstd, gamma, beta, sg, sgx, (T*)dx, total, C, S, relu ? 1 : 0, dd,
-      1.f / (float)((int64_t)N * S)));
+  if (total % 8 == 0 && al16p(x) && al16p(dy) && al16p(dx) && al16p(scratch) && C % 4 == 0) {
+    DLVK_DISPATCH_FB(dt, "batchnorm_bwd", bn_bwd_apply_vec_kernel<T><<<grid1d(total / 8), 256, 0, s>>>(
+        (const T*)x, (const T*)dy, co, (T*)dx, total, C, S, relu ? 1 : 0, dd));
+  } else {
+    DLVK_DISPATCH_FB(dt, "batchnorm_bwd", bn_bwd_apply_kernel<T><<<grid1d(total), 256, 0, s>>>(
+        (const T*)x, (const T*)dy, co.A, co.B, co.D, co.shift, (T*)dx, total, C, S, relu ? 1 : 0, dd));
+  }
   DLVK_POST_LAUNCH();
 }
 

@@ -207,3 +207,27 @@ def test_gemm_tc_pair_splitk_wgrad_shapes(M, N):
     torch.cuda.synchronize()
     assert C.read_device_error(True) == 0
     _check(acc, ref, 2e-2)
+
+
+@pytest.mark.parametrize("M,N", [(1000, 1000), (384, 2056)])
+def test_gemm_tc_splitk_reduce_into_strided_fp32(M, N):
+    """Split-K partials added into an fp32 output that is a column window of a
+    wider buffer (ragged M and N, alpha != 1): the columns outside the window
+    and the rows' padding stay untouched, beta = 0 overwrites, beta = 1 adds."""
+    C = _C()
+    torch.manual_seed(6)
+    K = 8192
+    a = torch.randn(K, M, device="cuda").bfloat16().t()
+    b = torch.randn(K, N, device="cuda").bfloat16()
+    big = torch.full((M, N + 68), 7.0, device="cuda")
+    out = big[:, 4:4 + N]
+    ref = 0.5 * (a.float() @ b.float())
+    C.gemm(a, b, alpha=0.5, out=out, force_path=1)
+    torch.cuda.synchronize()
+    assert C.read_device_error(True) == 0
+    _check(out, ref, 2e-2)
+    assert torch.all(big[:, :4] == 7.0) and torch.all(big[:, 4 + N:] == 7.0)
+    C.gemm(a, b, alpha=0.5, beta=1.0, out=out, force_path=1)
+    torch.cuda.synchronize()
+    _check(out, 2 * ref, 2e-2)
+    assert torch.all(big[:, :4] == 7.0) and torch.all(big[:, 4 + N:] == 7.0)

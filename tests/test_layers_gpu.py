@@ -67,17 +67,21 @@ def test_pooling():
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("shape", [(256, 300), (64, 8, 5, 5)])
-def test_batchnorm_relu_dropout(dtype, shape):
+@pytest.mark.parametrize("shape,p", [((256, 300), 0.1), ((64, 8, 5, 5), 0.0), ((1024, 4096), 0.1), ((24, 64), 0.1),
+                                     ((16, 16, 14, 14), 0.1), ((7, 10, 3), 0.0)])
+def test_batchnorm_relu_dropout(dtype, shape, p):
+    """Covers the wide-grid reductions (several channel groups and row
+    chunks), 8-wide element passes with channel wrap-around (S = 1 and S > 1)
+    and the scalar fallbacks (C % 8 != 0, odd totals)."""
     from dlvk_b200.ops import nn as NN
 
     C = _C()
-    x = torch.randn(*shape, device="cuda").to(dtype)
+    torch.manual_seed(sum(shape))
+    x = (torch.randn(*shape, device="cuda") * 2 + 1).to(dtype)
     Cn = shape[1]
     gamma = torch.rand(Cn, device="cuda") + 0.5
     beta = torch.randn(Cn, device="cuda") * 0.1
     rm, rv = torch.zeros(Cn, device="cuda"), torch.ones(Cn, device="cuda")
-    p = 0.1 if len(shape) == 2 else 0.0
     y, mean, rstd = C.batchnorm_fwd(x, gamma, beta, rm, rv, 0.1, 1e-5, True, True, p, 3, 7, 5, None)
     rm_c, rv_c = torch.zeros(Cn), torch.ones(Cn)
     yr, mr, sr = NN.batchnorm_fwd(x.cpu(), gamma.cpu(), beta.cpu(), rm_c, rv_c, 0.1, 1e-5, True, True, p, 3, 7, 5)
@@ -85,6 +89,9 @@ def test_batchnorm_relu_dropout(dtype, shape):
     close(y, yr, tol)
     close(rm, rm_c, 1e-4)
     close(rv, rv_c, 1e-4)
+    ye, _, _ = C.batchnorm_fwd(x, gamma, beta, rm, rv, 0.1, 1e-5, False, True, p, 3, 7, 5, None)
+    yer, _, _ = NN.batchnorm_fwd(x.cpu(), gamma.cpu(), beta.cpu(), rm_c, rv_c, 0.1, 1e-5, False, True, p, 3, 7, 5)
+    close(ye, yer, tol)
     g = torch.randn(*shape, device="cuda").to(dtype)
     dg, dbt = torch.zeros(Cn, device="cuda"), torch.zeros(Cn, device="cuda")
     dx = C.batchnorm_bwd(x, g, mean, rstd, gamma, beta, dg, dbt, False, True, p, 3, 7, 5, None)
@@ -93,6 +100,10 @@ def test_batchnorm_relu_dropout(dtype, shape):
     close(dx, dxr, tol * 2)
     close(dg, dg_c, tol * 2)
     close(dbt, db_c, tol * 2)
+    # accumulate = True adds onto the existing parameter gradients
+    C.batchnorm_bwd(x, g, mean, rstd, gamma, beta, dg, dbt, True, True, p, 3, 7, 5, None)
+    close(dg, 2 * dg_c, tol * 2)
+    close(dbt, 2 * db_c, tol * 2)
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
