@@ -45,10 +45,13 @@ def main():
     ap.add_argument("--out-f32", action="store_true",
                     help="fp32 output, as for weight gradients (cuBLAS still writes bf16)")
     ap.add_argument("--beta", type=float, default=0.0, help="accumulate: C = A B + beta C")
+    ap.add_argument("--wide", type=int, default=1,
+                    help="256 x 512 pair tile: 0 never, 1 when the tiling model picks it, 2 whenever it applies")
     ap.add_argument("--compare-single", action="store_true",
                     help="also time the single-CTA kernel (CTA-pair variant switched off)")
     args = ap.parse_args()
     C = _ext.C()
+    C.gemm_set_wide(args.wide)
     shapes = DEFAULT
     if args.shapes:
         shapes = []
@@ -74,6 +77,7 @@ def main():
             kw["beta"] = args.beta
         t_ours = time_fn(lambda: C.gemm(a, b, out=out, force_path=1, **kw), iters=args.iters)
         rec = {"M": M, "N": N, "K": K, "a": am, "b": bm, "epilogue": sorted(kw), "out": str(out.dtype)[6:],
+               "plan": list(C.gemm_plan(a, b, args.out_f32)),
                "ours_ms": round(t_ours, 4),
                "ours_tflops": round(flops / t_ours / 1e9, 1), "ours_frac_of_measured": round(flops / t_ours / 1e9 / peak, 3)}
         if args.compare_single:

@@ -420,6 +420,17 @@ void register_ops(py::module& m) {
         py::arg("m") = py::none(), py::arg("v") = py::none(), py::arg("p_bf16") = py::none(),
         py::arg("extra_scale") = 1.0, py::arg("max_ctas") = 0);
   m.def("gemm_set_pair", [](bool on) { gemm_tc_set_pair(on); });
+  m.def("gemm_set_wide", [](int64_t mode) { gemm_tc_set_wide((int)mode); });
+  m.def(
+      "gemm_plan",
+      [](const at::Tensor& A, const at::Tensor& B, bool out_f32, int64_t max_ctas) {
+        GemmArgs a = fill_args(A, B, A);
+        a.ldc = B.size(-1);
+        int bn = 0, sp = 0, pr = 0;
+        gemm_tc_plan(out_f32 ? DType::F32 : DType::BF16, a, (int)max_ctas, &bn, &sp, &pr);
+        return py::make_tuple(bn, sp, pr != 0);
+      },
+      py::arg("A"), py::arg("B"), py::arg("out_f32") = false, py::arg("max_ctas") = 0);
   m.def("gemm_pair_enabled", []() { return gemm_tc_pair_enabled(); });
   m.def("grad_stats", &grad_stats_op, py::arg("g"), py::arg("scale"), py::arg("max_norm"), py::arg("sumsq"),
         py::arg("flag"), py::arg("clip"), py::arg("accumulate"), py::arg("scratch"), py::arg("scale_dev") = py::none());

@@ -86,6 +86,13 @@ int64_t gemm_tc_workspace_floats(const GemmArgs& a, int max_ctas = 0, DType out_
 // GEMMs with M >= 256; on by default (DLVK_GEMM_PAIR=0 turns it off).
 bool gemm_tc_pair_enabled();
 void gemm_tc_set_pair(bool on);
+// 256 x 512 CTA-pair tile (two N = 256 MMAs per k-step, one TMEM buffer) for
+// long-K GEMMs with few tiles.  Mode 0 never, 1 when the tiling model picks
+// it (default; DLVK_GEMM_WIDE sets the initial mode), 2 whenever it applies.
+void gemm_tc_set_wide(int mode);
+// The tiling the model picks for these operands: tile N (128/256/512), the
+// split-K factor, and whether the CTA-pair kernel runs.
+void gemm_tc_plan(DType out_dt, const GemmArgs& a, int max_ctas, int* bn, int* splits, int* pair);
 void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int max_ctas = 0,
              float* workspace = nullptr, int64_t workspace_floats = 0);
 

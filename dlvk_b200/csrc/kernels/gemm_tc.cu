@@ -69,17 +69,27 @@ struct TcParams {
 // PAIR: a 2-CTA cluster shares one 256 x BN tile (tcgen05 cta_group::2);
 // each CTA stages its 128 rows of A and its BN/2 columns of B.
 template <int BN, bool PAIR = false>
+// BN = 512 (PAIR only): the tile is two N = 256 MMAs per k-step; each CTA
+// stages two 128-column B sub-blocks, and the 512 accumulator columns fill
+// TMEM, so there is one accumulator buffer instead of two.
 struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = PAIR ? 6 : ((BN == 256) ? 4 : 6);
-  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int STAGES = PAIR ? (BN == 512 ? 4 : 6) : ((BN == 256) ? 4 : 6);
+  static constexpr int ACCS = 2 * BN <= 512 ? 2 : 1;      // TMEM accumulator buffers
+  static constexpr int TMEM_COLS = ACCS * BN;
+  static constexpr int MMA_N = BN > 256 ? 256 : BN;        // N of one tcgen05.mma
+  static constexpr int NSUB = BN / MMA_N;                  // MMAs per k-step
+  static constexpr int SUB_B_BYTES = B_BYTES / NSUB;       // B bytes per sub-block
+  static_assert(!(BN == 512) || PAIR, "the 512-column tile is a CTA-pair tile");
   // per-warp 32x33 fp32 staging; also holds the TMA-store boxes (8 x 4 KB
   // from the next 1024-byte boundary)
   static constexpr int EPI_BYTES = 8 * 32 * 33 * 4;
   static_assert(EPI_BYTES >= 768 + 8 * 4096, "epilogue smem too small for the TMA-store boxes");
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + EPI_BYTES;
+  static_assert(SMEM <= 232448, "shared memory above the per-block limit");
+  static_assert(STAGES * STAGE_BYTES / 8 >= 4096, "last-tile epilogue needs a 4 KB box per warp");
 };
 
 // Wait-time accounting for kernel development: compiled in only with
@@ -353,7 +363,8 @@ __global__ void __launch_bounds__(320, 1)
         tile_coords(t - sp * tiles_per_split, p, tm, tn, b);
         const int bo = b / p.batch2, bi = b - bo * p.batch2;
         const int arow = tm * TILE_M + (int)rank * BM;
-        const int bcol = tn * BN + (int)rank * (BN / 2);
+        // sub-block j of this CTA: columns tn*BN + j*MMA_N + rank*MMA_N/2 + [0, MMA_N/2)
+        const int bcol = tn * BN + (int)rank * (C::MMA_N / 2);
         const int kb0 = sp * p.kb_per_split, kb1 = min(num_kb, kb0 + p.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
           {
@@ -371,12 +382,17 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
             for (int j = 0; j < BM / 64; ++j) tma_load_4d_pair(sA + j * 8192, &tmA, fb, arow + j * 64, kb * BK, bi, bo);
           }
-          if (!p.b_mn) {
-            tma_load_4d_pair(sB, &tmB, fb, kb * BK, bcol, bi, bo);
-          } else {
 #pragma unroll
-            for (int j = 0; j < BN / 128; ++j)
-              tma_load_4d_pair(sB + j * 8192, &tmB, fb, bcol + j * 64, kb * BK, bi, bo);
+          for (int sub = 0; sub < C::NSUB; ++sub) {
+            uint8_t* sBs = sB + sub * C::SUB_B_BYTES;
+            const int col = bcol + sub * C::MMA_N;
+            if (!p.b_mn) {
+              tma_load_4d_pair(sBs, &tmB, fb, kb * BK, col, bi, bo);
+            } else {
+#pragma unroll
+              for (int j = 0; j < C::MMA_N / 128; ++j)
+                tma_load_4d_pair(sBs + j * 8192, &tmB, fb, col + j * 64, kb * BK, bi, bo);
+            }
           }
           if (++stage == C::STAGES) {
             stage = 0;
@@ -430,7 +446,7 @@ __global__ void __launch_bounds__(320, 1)
       if (rank == 0) {
         // M = 256 across the pair; B descriptors describe this CTA's BN/2
         // columns (the peer's half sits at the same offsets in its smem).
-        const uint32_t idesc = make_idesc(1, 1, 1, p.a_mn != 0, p.b_mn != 0, 2 * BM, BN);
+        const uint32_t idesc = make_idesc(1, 1, 1, p.a_mn != 0, p.b_mn != 0, 2 * BM, C::MMA_N);
         int stage = 0;
         uint32_t phase = 0;
         int acc = 0;
@@ -457,9 +473,13 @@ __global__ void __launch_bounds__(320, 1)
             for (int k = 0; k < BK / 16; ++k) {
               const uint64_t ad = p.a_mn ? make_sw128_desc(aBase + k * 2048, 8192, 1024)
                                          : make_sw128_desc(aBase + k * 32, 16, 1024);
-              const uint64_t bd = p.b_mn ? make_sw128_desc(bBase + k * 2048, 8192, 1024)
-                                         : make_sw128_desc(bBase + k * 32, 16, 1024);
-              mma_f16_pair(d, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+#pragma unroll
+              for (int sub = 0; sub < C::NSUB; ++sub) {
+                const uint32_t bs = bBase + sub * C::SUB_B_BYTES;
+                const uint64_t bd = p.b_mn ? make_sw128_desc(bs + k * 2048, 8192, 1024)
+                                           : make_sw128_desc(bs + k * 32, 16, 1024);
+                mma_f16_pair(d + (uint32_t)(sub * C::MMA_N), ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+              }
             }
             const uint32_t eb = smem_u32(&empty[stage]);
             mma_commit_pair(eb);
@@ -473,7 +493,7 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t fb = smem_u32(&tfull[acc]);
           mma_commit_pair(fb);
           mma_commit_pair(mapa_shared(fb, 1));
-          if (++acc == 2) {
+          if (++acc == C::ACCS) {
             acc = 0;
             acc_phase ^= 1u;
           }
@@ -521,7 +541,7 @@ __global__ void __launch_bounds__(320, 1)
         }
         if (!ok) break;
         mma_commit(&tfull[acc]);
-        if (++acc == 2) {
+        if (++acc == C::ACCS) {
           acc = 0;
           acc_phase ^= 1u;
         }
@@ -542,10 +562,19 @@ __global__ void __launch_bounds__(320, 1)
     constexpr int NCH = BN / 64;  // 32-column chunks per warp
     int acc = 0, ecount = 0;
     uint32_t acc_phase = 0;
+    // TMA-store boxes (4 KB): one slot per warp in the epilogue area, so each
+    // box waits for the store issued before it.  A CTA's last tile has the
+    // whole stage area to itself (every stage has been consumed by the MMAs
+    // and no load is left), so there each warp gets 1/8 of it and issues its
+    // boxes without waiting.
+    constexpr int WREG = (C::STAGES * C::STAGE_BYTES / 8) & ~1023;
     for (int t = t0; t < num_tiles; t += tstep) {
       int tm, tn, b;
       const int sp = t / tiles_per_split;
       tile_coords(t - sp * tiles_per_split, p, tm, tn, b);
+      const bool last_tile = t + tstep >= num_tiles;
+      int tcount = 0;  // boxes of this tile issued by this warp
+
       {
         GEMM_T0();
         if (!mbar_wait(&tfull[acc], acc_phase, p.err)) break;
@@ -561,10 +590,13 @@ __global__ void __launch_bounds__(320, 1)
       const int row0 = tm * TILE_M + (int)rank * BM + q * 32;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + half * NCH * 32);
       uint32_t r[2][32];
+      uint8_t* box = nullptr;  // the TMA-store box being filled
       tmem_ld32(tbase, r[0]);
       tmem_ld_wait();
+      GEMM_STAMP(threadIdx.x == 64 && last_tile, 13);
 #pragma unroll
       for (int i = 0; i < NCH; ++i) {
+        if (i == 1) GEMM_STAMP(threadIdx.x == 64 && last_tile, 15);
         if (i + 1 < NCH) tmem_ld32(tbase + (uint32_t)((i + 1) * 32), r[(i + 1) & 1]);
         const int n0 = tn * BN + (half * NCH + i) * 32;
         if (staged) {
@@ -577,34 +609,43 @@ __global__ void __launch_bounds__(320, 1)
           }
           __syncwarp();
         } else if (p.tma_c) {
-          // Row `lane` of this warp's 32 x 32 box goes to smem; one lane
-          // stores the box with TMA (rows >= M / columns >= N are clipped).
-          // Two boxes alternate for bf16 (one for fp32), so the store of
-          // chunk i overlaps the conversion of chunk i+1.
-          if (n0 < p.N) {
+          // Row `lane` of this warp's box goes to smem and one lane stores the
+          // box with TMA (rows >= M / columns >= N are clipped).  fp32: one
+          // 32 x 32 box (128-byte rows) per chunk.  bf16: chunks i, i+1 fill
+          // the two halves of one 32 x 64 box, so every box row is a whole
+          // 128-byte line and there is one store (and one proxy fence) per two
+          // chunks.
+          const bool bf = !p.out_f32;
+          const bool opens = !bf || (i & 1) == 0;
+          const int nbox = bf ? n0 - (i & 1) * 32 : n0;  // the box's first column
+          if (nbox < p.N) {
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[i & 1][j]) * p.alpha;
-            if (p.bias) add_bias<32>(p.bias, p.bias_f32, n0, min(32, p.N - n0), v);
+            if (p.bias && n0 < p.N) add_bias<32>(p.bias, p.bias_f32, n0, min(32, p.N - n0), v);
             apply_act<32>(p.act, v);
-            // 1024-byte aligned 4 KB slot per warp (the swizzled box layout is
-            // defined on aligned addresses): two bf16 boxes or one fp32 box.
-            uint8_t* box = reinterpret_cast<uint8_t*>(
-                               (reinterpret_cast<uintptr_t>(epi) + 1023) & ~uintptr_t(1023)) +
-                           ew * 4096 + (p.out_f32 ? 0 : (ecount & 1) * 2048);
-            if (lane == 0) {
-              if (p.out_f32) bulk_wait_group_read<0>();
-              else bulk_wait_group_read<1>();
+            // Boxes start on 1024-byte boundaries (the swizzled box layout is
+            // defined on aligned addresses).
+            if (opens) {
+              if (last_tile) {
+                const int nslot = WREG / 4096;
+                box = smem + ew * WREG + (tcount % nslot) * 4096;
+                if (tcount > 0 && tcount % nslot == 0 && lane == 0) bulk_wait_group_read<0>();
+              } else {
+                box = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(epi) + 1023) & ~uintptr_t(1023)) +
+                      ew * 4096;
+                if (lane == 0) bulk_wait_group_read<0>();
+              }
+              __syncwarp();
             }
-            __syncwarp();
-            // The box map uses the 128-byte (fp32 rows) / 64-byte (bf16 rows)
-            // swizzle, which the TMA unit applies to shared-memory address
-            // bits: XOR the 16-byte chunk index with address bits 7..9 (7..8).
-            const uint32_t bb = smem_u32(box);
-            if (p.out_f32) {
+            // The box map uses the 128-byte swizzle, which the TMA unit applies
+            // to shared-memory address bits: XOR the 16-byte chunk index with
+            // address bits 7..9.
+            const uint32_t bb = smem_u32(box) + (uint32_t)lane * 128u;
+            if (!bf) {
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
-                const uint32_t a = bb + (uint32_t)lane * 128u + (uint32_t)j * 16u;
+                const uint32_t a = bb + (uint32_t)j * 16u;
                 st_shared_v4(a ^ (((a >> 7) & 7u) << 4), __float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]),
                              __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3]));
               }
@@ -617,18 +658,21 @@ __global__ void __launch_bounds__(320, 1)
                   const __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * j + 2 * k], v[8 * j + 2 * k + 1]);
                   w[k] = *reinterpret_cast<const uint32_t*>(&h);
                 }
-                const uint32_t a = bb + (uint32_t)lane * 64u + (uint32_t)j * 16u;
-                st_shared_v4(a ^ (((a >> 7) & 3u) << 4), w[0], w[1], w[2], w[3]);
+                const uint32_t a = bb + (uint32_t)((i & 1) * 4 + j) * 16u;
+                st_shared_v4(a ^ (((a >> 7) & 7u) << 4), w[0], w[1], w[2], w[3]);
               }
             }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              if (p.tma_c == 2) tma_reduce_add_5d(&tmC, box, n0, row0, bi, bo, 0);
-              else tma_store_5d(&tmC, box, n0, row0, bi, bo, sp);
-              bulk_commit_group();
+            if (!bf || (i & 1)) {
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                if (p.tma_c == 2) tma_reduce_add_5d(&tmC, box, nbox, row0, bi, bo, 0);
+                else tma_store_5d(&tmC, box, nbox, row0, bi, bo, sp);
+                bulk_commit_group();
+              }
+              ++ecount;
+              ++tcount;
             }
-            ++ecount;
           }
         } else {
           const int row = row0 + lane;
@@ -683,6 +727,7 @@ __global__ void __launch_bounds__(320, 1)
         }
         if (i + 1 < NCH) tmem_ld_wait();
       }
+      GEMM_STAMP(threadIdx.x == 64 && last_tile, 14);
       tc_fence_before();
       if (PAIR) {
         __syncwarp();
@@ -690,7 +735,7 @@ __global__ void __launch_bounds__(320, 1)
       } else {
         mbar_arrive(&tempty[acc]);
       }
-      if (++acc == 2) {
+      if (++acc == C::ACCS) {
         acc = 0;
         acc_phase ^= 1u;
       }
@@ -773,11 +818,12 @@ void launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& 
   DLVK_POST_LAUNCH();
 }
 
-// 2-CTA clusters sharing 256 x 256 tiles (cta_group::2).  The persistent
+// 2-CTA clusters sharing 256 x BN tiles (cta_group::2).  The persistent
 // grid is as many pairs as can be resident at once.
+template <int BN>
 void launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const TcParams& p,
                     int max_ctas, cudaStream_t s) {
-  using C = Cfg<256, true>;
+  using C = Cfg<BN, true>;
   static int max_pairs[64] = {0};
   int dev = 0;
   DLVK_CUDA_CHECK(cudaGetDevice(&dev));
@@ -796,10 +842,10 @@ void launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensor
   cfg.numAttrs = 1;  // occupancy query: cluster shape only
   if (max_pairs[dev] == 0) {
     DLVK_CUDA_CHECK(
-        cudaFuncSetAttribute(gemm_tc_kernel<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        cudaFuncSetAttribute(gemm_tc_kernel<BN, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     cfg.gridDim = dim3(2 * 74, 1, 1);
     int n = 0;
-    DLVK_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<256, true>, &cfg));
+    DLVK_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<BN, true>, &cfg));
     max_pairs[dev] = std::max(1, n);
   }
   const int tiles = p.tiles_m * p.tiles_n * p.batch * p.splits;
@@ -807,7 +853,7 @@ void launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensor
   if (max_ctas > 0) pairs = std::max(1, std::min(pairs, max_ctas / 2));
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.numAttrs = 2;
-  DLVK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<256, true>, ta, tb, tc, p));
+  DLVK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, true>, ta, tb, tc, p));
   DLVK_POST_LAUNCH();
 }
 
@@ -853,10 +899,21 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
 // measured for that tile shape) + the split-K partial traffic.  Pair units
 // are 256 x 256 tiles on sms/2 pairs (about 1.2x the single-CTA 128 x 256
 // rate on B200); single units are 128 x BN on sms CTAs.
+// The 256 x 512 pair tile: 0 never, 1 when the model picks it (default),
+// 2 whenever it applies (measurement).  DLVK_GEMM_WIDE or gemm_tc_set_wide.
+int& wide_flag() {
+  static int f = [] {
+    const char* e = std::getenv("DLVK_GEMM_WIDE");
+    return e ? std::atoi(e) : 1;
+  }();
+  return f;
+}
+bool gemm_tc_wide_enabled() { return wide_flag() != 0; }
 // With `red` (split_red_ok) the partials are added into C by the epilogue's
 // TMA reduce in L2 (plus a clear of C when beta = 0) instead of the workspace
 // round trip and the reduce launch.
-void choose_tiling(const GemmArgs& a, int sms, int& BN, int& splits, bool& pair, bool red = false) {
+void choose_tiling(const GemmArgs& a, int sms, int& BN, int& splits, bool& pair, bool red = false,
+                   bool out_f32 = false) {
   const int64_t kbs = (a.K + BK - 1) / BK;
   const double sm_flops = 8.1e12;
   double best = 1e300;
@@ -869,9 +926,17 @@ void choose_tiling(const GemmArgs& a, int sms, int& BN, int& splits, bool& pair,
     int bn;
     double eff;
   };
-  const Cand cands[] = {{true, 256, 1.2}, {false, 256, 1.0}, {false, 128, 0.85}};
+  // The 256 x 512 pair tile moves 25% fewer L2 bytes per FLOP than 256 x 256
+  // (the mainloop of the latter waits on L2 ~25% of the time), but its single
+  // TMEM buffer leaves every tile's epilogue exposed.
+  // Measured per-SM rates relative to the single-CTA tile: the wide tile
+  // gains with K (1.3 at K = 4096, 1.55 from K = 8192 on).
+  const double wide_eff = kbs >= 128 ? 1.55 : 1.3;
+  const Cand cands[] = {{true, 512, wide_eff}, {true, 256, 1.2}, {false, 256, 1.0}, {false, 128, 0.85}};
   for (const Cand& c : cands) {
     if (c.pair && !pair_ok) continue;
+    if (c.bn == 512 && (!gemm_tc_wide_enabled() || a.N < 512)) continue;
+    if (c.bn != 512 && wide_flag() == 2 && pair_ok && a.N >= 512 && best < 1e300) continue;
     if (c.bn == 256 && a.N < 256) continue;
     const int64_t tile_m = c.pair ? 2 * BM : BM;
     const int64_t tiles = ((a.M + tile_m - 1) / tile_m) * ((a.N + c.bn - 1) / c.bn) * a.batch * a.batch2;
@@ -882,7 +947,11 @@ void choose_tiling(const GemmArgs& a, int sms, int& BN, int& splits, bool& pair,
       const int64_t waves = (units + slots - 1) / slots;
       const double unit_s = (double)tile_m * c.bn * BK * 2.0 * ((kbs + sp - 1) / sp) /
                             (sm_flops * (c.pair ? 2 : 1) * c.eff);
-      double t = waves * unit_s;
+      // Epilogue of one CTA's 128 x BN block (measured last-tile epilogue:
+      // ~5K cycles for 128 x 256 bf16, ~3x that for 128 x 512), exposed once
+      // at the end, or after every wave without a second accumulator buffer.
+      const double epi_s = 128.0 * c.bn * ((out_f32 || sp > 1) ? 4.0 : 2.0) / (c.bn == 512 ? 10e9 : 17e9);
+      double t = waves * unit_s + (c.bn == 512 ? waves : 1) * epi_s;
       if (sp > 1) {
         const double mn = (double)a.M * a.N * a.batch * a.batch2;
         t += red ? sp * mn * 4.0 / 8e12 + (a.beta == 0.f ? mn * 4.0 / 5e12 + 2e-6 : 0.0)
@@ -968,11 +1037,11 @@ CUtensorMap make_c_map(TcParams& p, int64_t M, int64_t N, bool reduce = false) {
                            pick(slices, p.split_stride)};
   for (uint64_t st : strides)
     if (st == 0 || st % 16 != 0 || st >= (1ull << 40)) return tc;
-  cuuint32_t box[5] = {32u, 32u, 1u, 1u, 1u};
+  cuuint32_t box[5] = {p.out_f32 ? 32u : 64u, 32u, 1u, 1u, 1u};  // 128-byte rows
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   CUresult r = encode_fn()(&tc, p.out_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, p.C,
                            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                           p.out_f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                           CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r == CUDA_SUCCESS) p.tma_c = reduce ? 2 : 1;
   return tc;
@@ -1001,7 +1070,7 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
   int BN = 256, splits = 1;
   bool pair = false;
   const bool red = split_red_ok(out_dt, a);
-  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits, pair, red);
+  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits, pair, red, out_dt == DType::F32);
   if (!red && (workspace == nullptr || workspace_floats < (int64_t)splits * a.M * a.N * a.batch * a.batch2))
     splits = 1;
   pair = pair && max_ctas != 1;
@@ -1020,7 +1089,7 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
   if (b_k) {
     const uint64_t d = (uint64_t)a.sbn * (uint64_t)a.N;
     tb = make_tmap(a.B, a.K, a.N, a.batch2, a.batch, a.sbn, pick(a.batch2, a.batch2_stride_b, d),
-                        pick(a.batch, a.batch_stride_b, d), pair ? BN / 2 : BN, false);
+                        pick(a.batch, a.batch_stride_b, d), pair ? 128 : BN, false);
   } else {
     const uint64_t d = (uint64_t)a.sbk * (uint64_t)a.K;
     tb = make_tmap(a.B, a.N, a.K, a.batch2, a.batch, a.sbk, pick(a.batch2, a.batch2_stride_b, d),
@@ -1073,7 +1142,8 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
     if (p.tma_c == 2) {
       if (a.beta == 0.f)
         DLVK_CUDA_CHECK(cudaMemset2DAsync(a.C, (size_t)a.ldc * 4, 0, (size_t)a.N * 4, (size_t)a.M, s));
-      if (pair) launch_tc_pair(ta, tb, tc, p, max_ctas, s);
+      if (pair && BN == 512) launch_tc_pair<512>(ta, tb, tc, p, max_ctas, s);
+    else if (pair) launch_tc_pair<256>(ta, tb, tc, p, max_ctas, s);
       else if (BN == 256) launch_tc<256>(ta, tb, tc, p, max_ctas, s);
       else launch_tc<128>(ta, tb, tc, p, max_ctas, s);
       return;
@@ -1102,7 +1172,8 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
     p.Mk = nullptr;
     p.act = ACT_NONE;
     const CUtensorMap tc = make_c_map(p, a.M, a.N);
-    if (pair) launch_tc_pair(ta, tb, tc, p, max_ctas, s);
+    if (pair && BN == 512) launch_tc_pair<512>(ta, tb, tc, p, max_ctas, s);
+    else if (pair) launch_tc_pair<256>(ta, tb, tc, p, max_ctas, s);
     else if (BN == 256) launch_tc<256>(ta, tb, tc, p, max_ctas, s);
     else launch_tc<128>(ta, tb, tc, p, max_ctas, s);
     const int g = (int)std::min<int64_t>((per + 255) / 256, 148 * 16);
@@ -1112,7 +1183,8 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
     return;
   }
   const CUtensorMap tc = make_c_map(p, a.M, a.N);
-  if (pair) launch_tc_pair(ta, tb, tc, p, max_ctas, s);
+  if (pair && BN == 512) launch_tc_pair<512>(ta, tb, tc, p, max_ctas, s);
+  else if (pair) launch_tc_pair<256>(ta, tb, tc, p, max_ctas, s);
   else if (BN == 256) launch_tc<256>(ta, tb, tc, p, max_ctas, s);
   else launch_tc<128>(ta, tb, tc, p, max_ctas, s);
 }
@@ -1131,11 +1203,22 @@ bool gemm_tc_pair_enabled() { return pair_flag() != 0; }
 
 void gemm_tc_set_pair(bool on) { pair_flag() = on ? 1 : 0; }
 
+void gemm_tc_set_wide(int mode) { wide_flag() = mode; }
+
+void gemm_tc_plan(DType out_dt, const GemmArgs& a, int max_ctas, int* bn, int* splits, int* pair) {
+  int BN = 256, sp = 1;
+  bool pr = false;
+  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, sp, pr, split_red_ok(out_dt, a), out_dt == DType::F32);
+  *bn = BN;
+  *splits = sp;
+  *pair = (pr && max_ctas != 1) ? 1 : 0;
+}
+
 int64_t gemm_tc_workspace_floats(const GemmArgs& a, int max_ctas, DType out_dt) {
   if (split_red_ok(out_dt, a)) return 0;
   int BN = 256, splits = 1;
   bool pair = false;
-  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits, pair);
+  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits, pair, false, out_dt == DType::F32);
   return splits > 1 ? (int64_t)splits * a.M * a.N * a.batch * a.batch2 : 0;
 }
 

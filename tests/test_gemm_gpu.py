@@ -231,3 +231,76 @@ def test_gemm_tc_splitk_reduce_into_strided_fp32(M, N):
     torch.cuda.synchronize()
     _check(out, 2 * ref, 2e-2)
     assert torch.all(big[:, :4] == 7.0) and torch.all(big[:, 4 + N:] == 7.0)
+
+
+def _wide(C, mode):
+    C.gemm_set_wide(mode)
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 1024, 256), (1000, 1000, 320), (768, 1536, 1024)])
+@pytest.mark.parametrize("a_t", [False, True])
+@pytest.mark.parametrize("b_t", [False, True])
+@pytest.mark.parametrize("epi", ["none", "bias_relu", "residual", "mask"])
+def test_gemm_tc_wide_pair_tile(M, N, K, a_t, b_t, epi):
+    """The 256 x 512 CTA-pair tile (two N = 256 MMAs per k-step, one TMEM
+    buffer), forced on, against the fp32 reference and the 256-wide tile."""
+    C = _C()
+    torch.manual_seed(7)
+    a = torch.randn(M, K, device="cuda").bfloat16()
+    b = torch.randn(K, N, device="cuda").bfloat16()
+    A = a.t().contiguous().t() if a_t else a
+    B = b.t().contiguous().t() if b_t else b
+    kw = {}
+    ref = a.float() @ b.float()
+    if epi == "bias_relu":
+        kw = dict(bias=torch.randn(N, device="cuda"), act=1)
+        ref = torch.relu(ref + kw["bias"])
+    elif epi == "residual":
+        kw = dict(residual=torch.randn(M, N, device="cuda").bfloat16())
+        ref = ref + kw["residual"].float()
+    elif epi == "mask":
+        kw = dict(relu_mask=torch.randn(M, N, device="cuda").bfloat16())
+        ref = torch.where(kw["relu_mask"].float() > 0, ref, torch.zeros_like(ref))
+    try:
+        _wide(C, 2)
+        assert C.gemm_plan(A, B)[0] == 512
+        wide = C.gemm(A, B, force_path=1, **kw)
+        _wide(C, 0)
+        assert C.gemm_plan(A, B)[0] != 512
+        narrow = C.gemm(A, B, force_path=1, **kw)
+    finally:
+        _wide(C, 1)
+    torch.cuda.synchronize()
+    assert C.read_device_error(True) == 0
+    _check(wide, ref, 2e-2)
+    _check(narrow, ref, 2e-2)
+
+
+def test_gemm_tc_wide_pair_tile_splitk_batched_persistent():
+    """Wide tile with split-K partials added into fp32 C, with 4-D batching,
+    and with one CTA pair walking 16 tiles through its single TMEM buffer."""
+    C = _C()
+    torch.manual_seed(8)
+    try:
+        _wide(C, 2)
+        a = torch.randn(8192, 1024, device="cuda").bfloat16().t()     # M-major, like X^T
+        b = torch.randn(8192, 1024, device="cuda").bfloat16()
+        plan = C.gemm_plan(a, b, True)
+        assert plan[0] == 512 and plan[1] > 1
+        out = C.gemm(a, b, out_dtype=torch.float32, force_path=1)
+        _check(out, a.float() @ b.float(), 2e-2)
+        acc = torch.randn(1024, 1024, device="cuda")
+        ref = acc + a.float() @ b.float()
+        C.gemm(a, b, beta=1.0, out=acc, force_path=1)
+        _check(acc, ref, 2e-2)
+        x = torch.randn(2, 3, 512, 128, device="cuda").bfloat16()
+        w = torch.randn(2, 3, 128, 1024, device="cuda").bfloat16()
+        _check(C.gemm(x, w, force_path=1, out_dtype=torch.float32), x.float() @ w.float(), 2e-2)
+        a2 = torch.randn(1024, 384, device="cuda").bfloat16()
+        b2 = torch.randn(384, 4096, device="cuda").bfloat16()
+        assert C.gemm_plan(a2, b2, False, 2)[0] == 512
+        _check(C.gemm(a2, b2, force_path=1, max_ctas=2), a2.float() @ b2.float(), 2e-2)
+    finally:
+        _wide(C, 1)
+    torch.cuda.synchronize()
+    assert C.read_device_error(True) == 0
