@@ -1,11 +1,13 @@
 """Memory-bound kernel micro-benchmark at the transformer config's shapes
 (8192 rows = batch 16 x seq 512, d_model 1024, vocab 32000, bf16): LayerNorm
 forward and backward (with the residual gradient), fused softmax +
-cross-entropy, bias-gradient column sums and the Adam update, each as
-achieved GB/s of its algorithmic bytes and the fraction of the measured HBM
-copy bandwidth.  CUDA-event timed, L2 flushed between launches.
+cross-entropy, bias-gradient column sums and the Adam update, plus the
+wide-MLP config's BatchNorm1D (+ ReLU + dropout 0.1) forward and backward on
+[1024, 4096]; each as achieved GB/s of its algorithmic bytes and the fraction
+of the measured HBM copy bandwidth.  CUDA-event timed, L2 flushed between
+launches.
 
-    python -m dlvk_b200.bench.kernels [--rows 8192 --d 1024 --vocab 32000]
+    python -m dlvk_b200.bench.kernels [--rows 8192 --d 1024 --vocab 32000] [--only bn]
 """
 from __future__ import annotations
 
@@ -24,6 +26,7 @@ def main():
     ap.add_argument("--vocab", type=int, default=32000)
     ap.add_argument("--params", type=int, default=185_000_000)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--only", default=None, choices=["bn"], help="bn: only the BatchNorm rows")
     a = ap.parse_args()
     import dlvk_b200 as dl
     from dlvk_b200.models.params import Parameter, ParamStore
@@ -46,6 +49,27 @@ def main():
         rows.append({"kernel": name, "us": round(t * 1e6, 2), "gbs": round(nbytes / t / 1e9, 1),
                      "frac_of_measured_hbm": round(nbytes / t / hbm, 3)})
 
+    def want(g):
+        return a.only is None or a.only == g
+
+    if want("bn"):
+        bx = torch.randn(1024, 4096, device="cuda").bfloat16()
+        bg = torch.randn(1024, 4096, device="cuda").bfloat16()
+        bgam, bbet = torch.rand(4096, device="cuda") + 0.5, torch.randn(4096, device="cuda") * 0.1
+        rmean, rvar = torch.zeros(4096, device="cuda"), torch.ones(4096, device="cuda")
+        dgb, dbb = torch.zeros(4096, device="cuda"), torch.zeros(4096, device="cuda")
+        _, bm, bs = NN.batchnorm_fwd(bx, bgam, bbet, rmean, rvar, 0.1, 1e-5, True, True, 0.1, 3, 7, 5)
+        n = bx.numel()
+        report("batchnorm1d_fwd+relu+dropout [1024,4096]",
+               time_fn(lambda: NN.batchnorm_fwd(bx, bgam, bbet, rmean, rvar, 0.1, 1e-5, True, True, 0.1, 3, 7, 5),
+                       a.iters), 2 * n * 2)  # read x, write y (the second read of x hits L2)
+        report("batchnorm1d_bwd+relu+dropout [1024,4096]",
+               time_fn(lambda: NN.batchnorm_bwd(bx, bg, bm, bs, bgam, bbet, dgb, dbb, False, True, 0.1, 3, 7, 5),
+                       a.iters), 3 * n * 2)  # read x and dy, write dx
+    if a.only == "bn":
+        for r in rows:
+            print(json.dumps(r), flush=True)
+        return
     y, mean, rstd = NN.layernorm_fwd(x, gamma, beta, 1e-5)
     report("layernorm_fwd", time_fn(lambda: NN.layernorm_fwd(x, gamma, beta, 1e-5), a.iters), 2 * R * D * 2 + R * 8)
     report("layernorm_bwd+dres", time_fn(lambda: NN.layernorm_bwd(x, gamma, mean, rstd, dy, dg, db, False, dres),

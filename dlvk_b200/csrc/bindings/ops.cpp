@@ -254,7 +254,8 @@ GemmArgs fill_args(const at::Tensor& A, const at::Tensor& B, const at::Tensor& C
 at::Tensor gemm_op(const at::Tensor& A, const at::Tensor& B, c10::optional<at::Tensor> bias, int64_t act,
                    double alpha, double beta, c10::optional<at::Tensor> out, c10::optional<at::ScalarType> out_dtype,
                    int64_t force_path, int64_t max_ctas, c10::optional<at::Tensor> residual,
-                   c10::optional<at::Tensor> relu_mask) {
+                   c10::optional<at::Tensor> relu_mask, c10::optional<at::Tensor> colsum_out,
+                   double colsum_scale, bool colsum_accumulate) {
   check_cuda(A, "A");
   check_cuda(B, "B");
   TORCH_CHECK(A.scalar_type() == B.scalar_type(), "dlvk.gemm: A and B must have the same dtype");
@@ -320,6 +321,18 @@ at::Tensor gemm_op(const at::Tensor& A, const at::Tensor& B, c10::optional<at::T
   const bool tc_ok = A.scalar_type() == at::kBFloat16 && gemm_tc_supported(a) &&
                      (C.scalar_type() == at::kBFloat16 || C.scalar_type() == at::kFloat);
   const bool use_tc = force_path == 1 ? true : (force_path == 2 ? false : tc_ok);
+  // colsum_out[n] (+)= colsum_scale * sum over rows of the output: fused into
+  // the tensor-core epilogue where its layout allows, else a column-sum pass.
+  at::Tensor cs_part;
+  if (colsum_out.has_value()) {
+    TORCH_CHECK(colsum_out->scalar_type() == at::kFloat && colsum_out->is_contiguous() && colsum_out->numel() == N &&
+                    colsum_out->device() == C.device() && nd == 2,
+                "dlvk.gemm: colsum_out must be a contiguous fp32 [N] tensor on the output's device (2-D GEMM)");
+    if (use_tc && tc_ok && gemm_tc_colsum_ok(to_dtype(C), a)) {
+      cs_part = at::empty({(M + 31) / 32 * N}, A.options().dtype(at::kFloat));
+      a.colsum = cs_part.data_ptr<float>();
+    }
+  }
   if (use_tc) {
     TORCH_CHECK(tc_ok, "dlvk.gemm: tensor-core path requested but not applicable to these operands");
     const int64_t wsf = gemm_tc_workspace_floats(a, (int)max_ctas, to_dtype(C));
@@ -328,6 +341,18 @@ at::Tensor gemm_op(const at::Tensor& A, const at::Tensor& B, c10::optional<at::T
             wsf);
   } else {
     gemm_simt(to_dtype(A), to_dtype(C), a, stream());
+  }
+  if (colsum_out.has_value()) {
+    if (a.colsum != nullptr) {
+      colsum_partials(a.colsum, (M + 31) / 32, N, (float)colsum_scale, colsum_out->data_ptr<float>(),
+                      colsum_accumulate, stream());
+    } else {
+      TORCH_CHECK(C.stride(-2) == N, "dlvk.gemm: colsum_out with a strided output needs the fused path");
+      const int64_t ns = colsum_scratch_floats(M, N);
+      at::Tensor scr = ns > 0 ? at::empty({ns}, A.options().dtype(at::kFloat)) : at::Tensor();
+      colsum(to_dtype(C), DType::F32, C.data_ptr(), M, N, (float)colsum_scale, colsum_out->data_ptr<float>(),
+             colsum_accumulate, ns > 0 ? scr.data_ptr<float>() : nullptr, stream());
+    }
   }
   return C;
 }
@@ -413,7 +438,8 @@ void register_ops(py::module& m) {
   m.def("gemm", &gemm_op, py::arg("A"), py::arg("B"), py::arg("bias") = py::none(), py::arg("act") = 0,
         py::arg("alpha") = 1.0, py::arg("beta") = 0.0, py::arg("out") = py::none(), py::arg("out_dtype") = py::none(),
         py::arg("force_path") = 0, py::arg("max_ctas") = 0, py::arg("residual") = py::none(),
-        py::arg("relu_mask") = py::none());
+        py::arg("relu_mask") = py::none(), py::arg("colsum_out") = py::none(), py::arg("colsum_scale") = 1.0,
+        py::arg("colsum_accumulate") = false);
   m.def("gemm_tc_ok", &gemm_tc_ok);
   m.def("optim_advance", &optim_advance_op);
   m.def("optim_update", &optim_update_op, py::arg("kind"), py::arg("hyper"), py::arg("p"), py::arg("grad"),

@@ -28,6 +28,9 @@ void bias_act(DType dt, DType dt_bias, const void* x, const void* bias, void* ou
 enum ReduceOp : int { RED_SUM = 0, RED_MAX = 1, RED_MIN = 2, RED_SUMSQ = 3, RED_ABSMAX = 4 };
 int reduce_scratch_floats();
 void reduce(DType dt, const void* x, int64_t n, int op, float scale, float* out, float* scratch, cudaStream_t s);
+// out[c] = scale * sum_k partial[k * cols + c] (+ out[c]); fp32, fixed order.
+void colsum_partials(const float* partial, int64_t chunks, int64_t cols, float scale, float* out, bool accumulate,
+                     cudaStream_t s);
 // scratch: colsum_scratch_floats(rows, cols) floats (may be null: single pass)
 int64_t colsum_scratch_floats(int64_t rows, int64_t cols);
 void colsum(DType dt, DType dt_out, const void* x, int64_t rows, int64_t cols, float scale, void* out, bool accumulate,
@@ -71,6 +74,11 @@ struct GemmArgs {
   // where mask <= 0.  Fuses the backward of a preceding ReLU into dX = dY W^T.
   const void* relu_mask = nullptr;
   int64_t ldm = 0, batch_stride_m = 0, batch2_stride_m = 0;
+  // Optional column sums of the output (before its rounding to C's dtype):
+  // per 32-row block, colsum[(m / 32) * N + n].  Needs gemm_tc_colsum_ok();
+  // colsum_partials() then adds the ceil(M / 32) rows.  Fuses a bias
+  // gradient db = sum_rows(dY) into the GEMM that produces dY.
+  float* colsum = nullptr;
 };
 void gemm_simt(DType in_dt, DType out_dt, const GemmArgs& a, cudaStream_t s);
 bool gemm_tc_supported(const GemmArgs& a);
@@ -93,6 +101,7 @@ void gemm_tc_set_wide(int mode);
 // The tiling the model picks for these operands: tile N (128/256/512), the
 // split-K factor, and whether the CTA-pair kernel runs.
 void gemm_tc_plan(DType out_dt, const GemmArgs& a, int max_ctas, int* bn, int* splits, int* pair);
+bool gemm_tc_colsum_ok(DType out_dt, const GemmArgs& a);
 void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int max_ctas = 0,
              float* workspace = nullptr, int64_t workspace_floats = 0);
 

@@ -62,6 +62,7 @@ struct TcParams {
   int i8;                  // 1: int8 x int8 -> int32 (kind::i8), K-major operands
   const float* row_scale;  // int8 dequantisation: per-row (A) and per-column (B) scales
   const float* col_scale;
+  float* colsum;           // per-32-row column sums of the output (staged fast path)
   int tma_c;               // 1: plain epilogue stores C through per-warp smem boxes + TMA;
                            // 2: same boxes, added into fp32 C (split-K partials reduced in L2)
 };
@@ -224,6 +225,9 @@ __device__ __forceinline__ void epi_store(const TcParams& p, const float* stg, i
     for (int k = 0; k < VEC; ++k) bv[k] = 0.f;
     if (p.bias) add_bias<VEC>(p.bias, p.bias_f32, n, valid, bv);
     const int mode = p.beta != 0.f ? 0 : (p.R ? 1 : 2);
+    float cs[VEC];
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) cs[k] = 0.f;
 #pragma unroll
     for (int ps = 0; ps < NP; ++ps) {
       const int rl = ps * RPP + rr;
@@ -248,6 +252,22 @@ __device__ __forceinline__ void epi_store(const TcParams& p, const float* stg, i
 #pragma unroll
       for (int k = 0; k < VEC; ++k) eo[k] = from_f32<T>(v[k]);
       *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.C) + cb + (int64_t)(row0 + rl) * p.ldc + n) = u;
+      if (p.colsum) {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) cs[k] += v[k];
+      }
+    }
+    if (p.colsum) {
+      // The lanes with the same column group (lane % LPR) hold the other rows.
+#pragma unroll
+      for (int off = LPR; off < 32; off <<= 1)
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) cs[k] += __shfl_xor_sync(0xffffffffu, cs[k], off);
+      if (rr == 0) {
+        float* dst = p.colsum + (int64_t)(row0 >> 5) * p.N + n;
+#pragma unroll
+        for (int k = 0; k < VEC; k += 4) *reinterpret_cast<float4*>(dst + k) = make_float4(cs[k], cs[k + 1], cs[k + 2], cs[k + 3]);
+      }
     }
     return;
   }
@@ -998,6 +1018,21 @@ bool split_red_ok(DType out_dt, const GemmArgs& a) {
 }
 }  // namespace
 
+// The column sums come from the staged epilogue's fast path, which must
+// then cover every chunk: exactly one auxiliary input (beta * C, residual or
+// ReLU mask) with 16-byte rows, M and N multiples of 32 (every lane of a
+// warp takes the fast path, so the lane shuffles are uniform), no
+// batching.
+bool gemm_tc_colsum_ok(DType out_dt, const GemmArgs& a) {
+  const int esz = out_dt == DType::F32 ? 4 : 2;
+  const int naux = (a.beta != 0.f) + (a.residual != nullptr) + (a.relu_mask != nullptr);
+  auto rows16 = [&](const void* p, int64_t ld) {
+    return p == nullptr || (al16(p) && (ld * esz) % 16 == 0);
+  };
+  return naux == 1 && a.batch == 1 && a.batch2 == 1 && a.M % 32 == 0 && a.N % 32 == 0 && al16(a.C) &&
+         (a.ldc * esz) % 16 == 0 && rows16(a.residual, a.ldr) && rows16(a.relu_mask, a.ldm);
+}
+
 bool gemm_tc_supported(const GemmArgs& a) {
   const bool a_k = (a.sak == 1), a_m = (a.sam == 1) && !a_k;
   const bool b_k = (a.sbk == 1), b_n = (a.sbn == 1) && !b_k;
@@ -1071,6 +1106,10 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
   bool pair = false;
   const bool red = split_red_ok(out_dt, a);
   choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits, pair, red, out_dt == DType::F32);
+  if (a.colsum != nullptr) {
+    DLVK_CHECK(gemm_tc_colsum_ok(out_dt, a), "gemm_tc: column sums need the staged fast-path layout");
+    splits = 1;  // the sums are taken over final outputs
+  }
   if (!red && (workspace == nullptr || workspace_floats < (int64_t)splits * a.M * a.N * a.batch * a.batch2))
     splits = 1;
   pair = pair && max_ctas != 1;
@@ -1131,6 +1170,7 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
   p.bias_f32 = (a.bias_dtype == (int)DType::F32);
   p.act = a.act;
   p.err = err;
+  p.colsum = a.colsum;
   p.splits = splits;
   p.kb_per_split = (int)(((a.K + BK - 1) / BK + splits - 1) / splits);
   p.split_stride = 0;
@@ -1215,7 +1255,7 @@ void gemm_tc_plan(DType out_dt, const GemmArgs& a, int max_ctas, int* bn, int* s
 }
 
 int64_t gemm_tc_workspace_floats(const GemmArgs& a, int max_ctas, DType out_dt) {
-  if (split_red_ok(out_dt, a)) return 0;
+  if (split_red_ok(out_dt, a) || a.colsum != nullptr) return 0;
   int BN = 256, splits = 1;
   bool pair = false;
   choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits, pair, false, out_dt == DType::F32);

@@ -94,6 +94,26 @@ __global__ void colsum_final_kernel(const float* __restrict__ partial, int chunk
   out[c] = from_f32<TO>(s);
 }
 
+// out[c] = scale * sum_k partial[k, c] (+ out[c]) for many chunks: 32 columns
+// per block, 8 lanes per column each summing every 8th chunk, then a fixed
+// tree (deterministic).
+__global__ void colsum_partials_kernel(const float* __restrict__ partial, int64_t chunks, int64_t cols, float scale,
+                                       float* __restrict__ out, bool accumulate) {
+  __shared__ float sm[8][33];
+  const int64_t c = blockIdx.x * 32 + threadIdx.x;
+  float acc = 0.f;
+  if (c < cols)
+    for (int64_t k = threadIdx.y; k < chunks; k += 8) acc += partial[k * cols + c];
+  sm[threadIdx.y][threadIdx.x] = acc;
+  __syncthreads();
+  if (threadIdx.y != 0 || c >= cols) return;
+  float s2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s2 += sm[i][threadIdx.x];
+  s2 *= scale;
+  out[c] = accumulate ? out[c] + s2 : s2;
+}
+
 // out[r] = scale * sum_c x[r, c]   (row sums, one warp per row)
 template <typename T>
 __global__ void rowsum_kernel(const T* __restrict__ x, int64_t rows, int64_t cols, float scale,
@@ -195,6 +215,13 @@ void colsum(DType dt, DType dt_out, const void* x, int64_t rows, int64_t cols, f
   else if (dt == DType::BF16 && dt_out == DType::BF16) DLVK_COLSUM(__nv_bfloat16, __nv_bfloat16);
   else throw std::runtime_error("dlvk::colsum: unsupported dtype");
 #undef DLVK_COLSUM
+}
+
+void colsum_partials(const float* partial, int64_t chunks, int64_t cols, float scale, float* out, bool accumulate,
+                     cudaStream_t s) {
+  colsum_partials_kernel<<<(unsigned)((cols + 31) / 32), dim3(32, 8), 0, s>>>(partial, chunks, cols, scale, out,
+                                                                            accumulate);
+  DLVK_POST_LAUNCH();
 }
 
 void rowsum(DType dt, const void* x, int64_t rows, int64_t cols, float scale, float* out, cudaStream_t s) {

@@ -168,21 +168,19 @@ def permute4(x: torch.Tensor, perm) -> torch.Tensor:
 
 # ---------------------------------------------------------------- GEMM
 def gemm(a: torch.Tensor, b: torch.Tensor, bias=None, act: int = ACT_NONE, alpha: float = 1.0, beta: float = 0.0,
-         out=None, out_dtype=None, residual=None, relu_mask=None) -> torch.Tensor:
+         out=None, out_dtype=None, residual=None, relu_mask=None, colsum_out=None, colsum_scale: float = 1.0,
+         colsum_accumulate: bool = False) -> torch.Tensor:
     """act(alpha * a @ b + beta * out + bias + residual), zeroed where
     relu_mask <= 0.  a: [M,K], [B,M,K] or [B,B2,M,K] (any strides), b
     likewise.  Transposes and head splits are views; the tensor-core path is
-    used whenever the layout allows it."""
+    used whenever the layout allows it.  With colsum_out (fp32 [N], 2-D
+    GEMMs) the column sums of the result, times colsum_scale, are written
+    (or added, colsum_accumulate) there as well: the bias gradient of a layer
+    whose output gradient this GEMM produces."""
     if native(a):
         return N().gemm(a, b, bias=bias, act=act, alpha=alpha, beta=beta, out=out, out_dtype=out_dtype,
-                        residual=residual, relu_mask=relu_mask)
-    if relu_mask is not None:
-        c = gemm(a, b, bias, act, alpha, beta, None, torch.float32, residual)
-        c = torch.where(relu_mask.float() > 0, c, torch.zeros_like(c))
-        if out is not None:
-            out.copy_(c)
-            return out
-        return c.to(out_dtype or a.dtype)
+                        residual=residual, relu_mask=relu_mask, colsum_out=colsum_out, colsum_scale=colsum_scale,
+                        colsum_accumulate=colsum_accumulate)
     c = alpha * torch.matmul(a.float(), b.float())
     if beta != 0.0 and out is not None:
         c = c + beta * out.float()
@@ -191,6 +189,14 @@ def gemm(a: torch.Tensor, b: torch.Tensor, bias=None, act: int = ACT_NONE, alpha
     if residual is not None:
         c = c + residual.float()
     c = _act_ref(c, act)
+    if relu_mask is not None:
+        c = torch.where(relu_mask.float() > 0, c, torch.zeros_like(c))
+    if colsum_out is not None:
+        s = c.reshape(-1, c.shape[-1]).sum(0) * colsum_scale
+        if colsum_accumulate:
+            colsum_out.add_(s)
+        else:
+            colsum_out.copy_(s)
     if out is not None:
         out.copy_(c)
         return out

@@ -10,12 +10,17 @@ Autograd only tracks activations.
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
 from . import core as K
 from . import nn as NN
 from .core import ACT_NONE, ACT_RELU, ACT_GELU
+
+# DLVK_FUSE_COLSUM=0: bias gradients by a separate column-sum pass instead of
+# the producing GEMM's epilogue.
+_FUSE_COLSUM = os.environ.get("DLVK_FUSE_COLSUM", "1") != "0"
 
 
 def _flat2(t: torch.Tensor) -> torch.Tensor:
@@ -366,9 +371,14 @@ class TransformerBlockFn(torch.autograd.Function):
         # FFN: y = f W2 + b2 + h
         wgrad(f2.weight, f.t(), g)
         bgrad(f2.bias, g)
-        df = K.gemm(g, f2.weight.value.t(), relu_mask=f)          # ReLU backward fused
+        # ReLU backward and the FF1 bias gradient (column sums) fused
+        if _FUSE_COLSUM:
+            df = K.gemm(g, f2.weight.value.t(), relu_mask=f, colsum_out=f1.bias.grad,
+                        colsum_accumulate=f1.bias.take_accumulate_flag())
+        else:
+            df = K.gemm(g, f2.weight.value.t(), relu_mask=f)
+            bgrad(f1.bias, df)
         wgrad(f1.weight, h2.t(), df)
-        bgrad(f1.bias, df)
         dh2 = K.gemm(df, f1.weight.value.t())
         acc = ln2.gamma.take_accumulate_flag()
         ln2.beta.take_accumulate_flag()

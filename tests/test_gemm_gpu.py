@@ -304,3 +304,25 @@ def test_gemm_tc_wide_pair_tile_splitk_batched_persistent():
         _wide(C, 1)
     torch.cuda.synchronize()
     assert C.read_device_error(True) == 0
+
+
+@pytest.mark.parametrize("M,N,K,out_dtype", [(512, 1024, 256, torch.bfloat16), (8192, 4096, 1024, torch.bfloat16),
+                                             (256, 384, 320, torch.float32), (200, 1000, 128, torch.bfloat16)])
+def test_gemm_tc_fused_colsum(M, N, K, out_dtype):
+    """Column sums of a ReLU-masked dX = dY W^T (the previous layer's bias
+    gradient), fused into the epilogue where M and N are multiples of 32 and a
+    separate pass otherwise; overwrite and accumulate."""
+    C = _C()
+    torch.manual_seed(9)
+    a = torch.randn(M, K, device="cuda").bfloat16()
+    b = torch.randn(N, K, device="cuda").bfloat16().t()
+    mask = torch.randn(M, N, device="cuda").to(out_dtype)
+    ref = torch.where(mask.float() > 0, a.float() @ b.float(), torch.zeros(M, N, device="cuda"))
+    cs = torch.full((N,), 5.0, device="cuda")
+    out = C.gemm(a, b, relu_mask=mask, out_dtype=out_dtype, force_path=1, colsum_out=cs, colsum_scale=0.5)
+    torch.cuda.synchronize()
+    assert C.read_device_error(True) == 0
+    _check(out, ref, 2e-2)
+    _check(cs, 0.5 * ref.sum(0), 4e-3)
+    C.gemm(a, b, relu_mask=mask, out_dtype=out_dtype, force_path=1, colsum_out=cs, colsum_accumulate=True)
+    _check(cs, 1.5 * ref.sum(0), 4e-3)
