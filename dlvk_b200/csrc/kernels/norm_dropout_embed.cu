@@ -734,11 +734,16 @@ __global__ void __launch_bounds__(256, 1) ln_bwd_ring_kernel(const __nv_bfloat16
   };
 #pragma unroll
   for (int k = 0; k < RING; ++k) issue(r0 + k * step, k);
-  float adg[NV][EPV], adb[NV][EPV];
+  // gr: this lane's gamma in registers (shared-memory reads at an 8-float
+  // lane stride would conflict 8 ways on every element).
+  float adg[NV][EPV], adb[NV][EPV], gr[NV][EPV];
 #pragma unroll
   for (int i = 0; i < NV; ++i)
 #pragma unroll
-    for (int k = 0; k < EPV; ++k) adg[i][k] = adb[i][k] = 0.f;
+    for (int k = 0; k < EPV; ++k) {
+      adg[i][k] = adb[i][k] = 0.f;
+      gr[i][k] = sgam[(lane + 32 * i) * EPV + k];
+    }
   const float invD = 1.f / D;
   int slot = 0;
   for (int64_t r = r0; r < rows; r += step) {
@@ -755,7 +760,7 @@ __global__ void __launch_bounds__(256, 1) ln_bwd_ring_kernel(const __nv_bfloat16
       for (int k = 0; k < EPV; ++k) {
         const float xh = (__bfloat162float(ex[k]) - mu) * rs;
         const float g = __bfloat162float(eg[k]);
-        const float gg = g * sgam[(lane + 32 * i) * EPV + k];
+        const float gg = g * gr[i][k];
         a += gg;
         bb += gg * xh;
         adg[i][k] += g * xh;
@@ -777,7 +782,7 @@ __global__ void __launch_bounds__(256, 1) ln_bwd_ring_kernel(const __nv_bfloat16
 #pragma unroll
       for (int k = 0; k < EPV; ++k) {
         const float xh = (__bfloat162float(ex[k]) - mu) * rs;
-        float v = rs * (__bfloat162float(eg[k]) * sgam[(lane + 32 * i) * EPV + k] - a - xh * bb);
+        float v = rs * (__bfloat162float(eg[k]) * gr[i][k] - a - xh * bb);
         if (RES) v += __bfloat162float(er[k]);
         eo[k] = __float2bfloat16_rn(v);
       }
