@@ -11,8 +11,11 @@
 // src/layers/activation.cpp:71-75, is only correct in this fused form).
 #include <type_traits>
 
+#include <cstdlib>
+
 #include "dlvk/common.h"
 #include "dlvk/kernels.h"
+#include "dlvk/sm100.h"
 
 namespace dlvk {
 namespace {
@@ -273,6 +276,116 @@ __global__ void __launch_bounds__(512, 2) softmax_ce_reg_kernel(const __nv_bfloa
   }
 }
 
+// Persistent form of softmax_ce_reg_kernel: each block walks the rows
+// blockIdx.x, + gridDim.x, ... and streams its next row into shared memory
+// with cp.async while it reduces the current one from registers, so the
+// memory system stays busy through the reductions and the gradient stores
+// (two blocks per SM, one 64 KB row buffer each at 32000 columns).  Same
+// arithmetic and results as softmax_ce_reg_kernel; dlogits may alias x (a
+// row is overwritten only after it has been read, and the prefetched row is
+// a different one).
+template <int NV>
+__global__ void __launch_bounds__(512, 2) softmax_ce_pipe_kernel(const __nv_bfloat16* x, const int* __restrict__ labels,
+                                                                 float* __restrict__ loss_rows,
+                                                                 __nv_bfloat16* dlogits, int64_t rows, int64_t cols,
+                                                                 float grad_scale) {
+  constexpr int THREADS = 512;
+  pdl_wait();
+  extern __shared__ uint4 srow[];
+  __shared__ float red[32];
+  const int nvec = (int)(cols / 8);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  auto prefetch = [&](int64_t row) {
+    if (row < rows) {
+      const uint4* src = reinterpret_cast<const uint4*>(x + row * cols);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int v = threadIdx.x + i * THREADS;
+        if (v < nvec) sm100::cp_async_16(sm100::smem_u32(srow + v), src + v, 16);
+      }
+    }
+    sm100::cp_async_commit();
+  };
+  int64_t r = blockIdx.x;
+  prefetch(r);
+  for (; r < rows; r += gridDim.x) {
+    sm100::cp_async_wait<0>();
+    __syncthreads();  // the row is in shared memory
+    uint4 raw[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int v = threadIdx.x + i * THREADS;
+      if (v < nvec) raw[i] = srow[v];
+    }
+    const int label = labels[r];
+    const float xl =
+        (label >= 0 && label < cols) ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(srow)[label]) : 0.f;
+    __syncthreads();  // every thread has read the buffer
+    prefetch(r + gridDim.x);
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int v = threadIdx.x + i * THREADS;
+      if (v < nvec) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __bfloat1622float2(h[k]);
+          mx = fmaxf(mx, fmaxf(f.x, f.y));
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[wid] = mx;
+    __syncthreads();
+    mx = lane < THREADS / 32 ? red[lane] : -INFINITY;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int v = threadIdx.x + i * THREADS;
+      if (v < nvec) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __bfloat1622float2(h[k]);
+          sum += __expf(f.x - mx) + __expf(f.y - mx);
+        }
+      }
+    }
+    sum = warp_sum(sum);
+    __syncthreads();  // every warp has read red[] (the maximum)
+    if (lane == 0) red[wid] = sum;
+    __syncthreads();
+    sum = lane < THREADS / 32 ? red[lane] : 0.f;
+    sum = warp_sum(sum);
+    const float inv = 1.f / sum;
+    if (threadIdx.x == 0 && loss_rows) loss_rows[r] = label < 0 ? 0.f : mx + logf(sum) - xl;
+    const float gs = label < 0 ? 0.f : grad_scale;
+    __nv_bfloat16* dr = dlogits + r * cols;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int v = threadIdx.x + i * THREADS;
+      if (v >= nvec) continue;
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
+      uint4 o;
+      __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int c = v * 8 + 2 * k;
+        const float2 f = __bfloat1622float2(h[k]);
+        const float g0 = (__expf(f.x - mx) * inv - (c == label ? 1.f : 0.f)) * gs;
+        const float g1 = (__expf(f.y - mx) * inv - (c + 1 == label ? 1.f : 0.f)) * gs;
+        oh[k] = __floats2bfloat162_rn(g0, g1);
+      }
+      reinterpret_cast<uint4*>(dr)[v] = o;
+    }
+  }
+  sm100::cp_async_wait<0>();
+}
+
 // Pointwise losses with a deterministic two-stage sum:
 //  MSE:  l = (p - t)^2,                      g = 2 (p - t) * gscale
 //  BCE:  l = -(t log p' + (1-t) log(1-p')),  p' = clamp(p, eps, 1-eps),
@@ -462,6 +575,27 @@ void launch_ce(const void* x, const int* labels, const float* probs, float* loss
       const int64_t per = (cols / 8 + 511) / 512;  // 16-byte vectors per thread
       const auto* xb = (const __nv_bfloat16*)x;
       auto* db = (__nv_bfloat16*)dlogits;
+      static const bool pipe = [] {
+        const char* e = std::getenv("DLVK_CE_PIPE");
+        return !(e && e[0] == '0');
+      }();
+      const int smem = (int)(cols * 2);
+      if (pipe && smem <= 100 * 1024) {
+        auto kern = per <= 2 ? softmax_ce_pipe_kernel<2>
+                             : (per <= 4 ? softmax_ce_pipe_kernel<4> : softmax_ce_pipe_kernel<8>);
+        static bool attr[3] = {false, false, false};
+        const int ai = per <= 2 ? 0 : (per <= 4 ? 1 : 2);
+        if (!attr[ai]) {  // one process-wide setting per instantiation (the largest row size allowed)
+          DLVK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
+          attr[ai] = true;
+        }
+        int sms = 0, dev = 0;
+        DLVK_CUDA_CHECK(cudaGetDevice(&dev));
+        DLVK_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        const unsigned grid = (unsigned)std::min<int64_t>(rows, 2 * (int64_t)sms);
+        launch_pdl(kern, dim3(grid), dim3(512), smem, s, xb, labels, loss_rows, db, rows, cols, grad_scale);
+        return;
+      }
       auto kern = per <= 2 ? softmax_ce_reg_kernel<2> : (per <= 4 ? softmax_ce_reg_kernel<4> : softmax_ce_reg_kernel<8>);
       launch_pdl(kern, dim3((unsigned)rows), dim3(512), 0, s, xb, labels, loss_rows, db, cols, grad_scale);
       return;

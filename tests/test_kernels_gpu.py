@@ -67,11 +67,12 @@ def test_softmax_ce(cols, dtype):
 
 
 @pytest.mark.parametrize("cols", [8000, 32000])
-def test_softmax_ce_vocab_inplace_ignored(cols):
-    """bf16 vocabulary-sized rows (register-resident kernel), gradient written
-    over the logits, one ignored row."""
+@pytest.mark.parametrize("rows", [19, 700])
+def test_softmax_ce_vocab_inplace_ignored(cols, rows):
+    """bf16 vocabulary-sized rows (register-resident kernels; with 700 rows
+    each persistent block walks several rows and prefetches the next),
+    gradient written over the logits, one ignored row."""
     C = _C()
-    rows = 19
     x = (torch.randn(rows, cols, device="cuda") * 3).bfloat16()
     lab = torch.randint(0, cols, (rows,), device="cuda", dtype=torch.int32)
     lab[3] = -1
