@@ -614,7 +614,10 @@ __global__ void __launch_bounds__(320, 1)
       tmem_ld32(tbase, r[0]);
       tmem_ld_wait();
       GEMM_STAMP(threadIdx.x == 64 && last_tile, 13);
-#pragma unroll
+      // Unrolled by two (the register double buffer needs the chunk parity at
+      // compile time), not fully: eight full copies of the chunk body for the
+      // 512-column tile make the epilogue's code large.
+#pragma unroll 2
       for (int i = 0; i < NCH; ++i) {
         if (i == 1) GEMM_STAMP(threadIdx.x == 64 && last_tile, 15);
         if (i + 1 < NCH) tmem_ld32(tbase + (uint32_t)((i + 1) * 32), r[(i + 1) & 1]);
@@ -950,8 +953,8 @@ void choose_tiling(const GemmArgs& a, int sms, int& BN, int& splits, bool& pair,
   // (the mainloop of the latter waits on L2 ~25% of the time), but its single
   // TMEM buffer leaves every tile's epilogue exposed.
   // Measured per-SM rates relative to the single-CTA tile: the wide tile
-  // gains with K (1.3 at K = 4096, 1.55 from K = 8192 on).
-  const double wide_eff = kbs >= 128 ? 1.55 : 1.3;
+  // gains with K (1.3 below K = 4096, 1.4 at 4096, 1.55 from 8192 on).
+  const double wide_eff = kbs >= 128 ? 1.55 : (kbs >= 64 ? 1.4 : 1.3);
   const Cand cands[] = {{true, 512, wide_eff}, {true, 256, 1.2}, {false, 256, 1.0}, {false, 128, 0.85}};
   for (const Cand& c : cands) {
     if (c.pair && !pair_ok) continue;
@@ -967,10 +970,10 @@ void choose_tiling(const GemmArgs& a, int sms, int& BN, int& splits, bool& pair,
       const int64_t waves = (units + slots - 1) / slots;
       const double unit_s = (double)tile_m * c.bn * BK * 2.0 * ((kbs + sp - 1) / sp) /
                             (sm_flops * (c.pair ? 2 : 1) * c.eff);
-      // Epilogue of one CTA's 128 x BN block (measured last-tile epilogue:
-      // ~5K cycles for 128 x 256 bf16, ~3x that for 128 x 512), exposed once
-      // at the end, or after every wave without a second accumulator buffer.
-      const double epi_s = 128.0 * c.bn * ((out_f32 || sp > 1) ? 4.0 : 2.0) / (c.bn == 512 ? 10e9 : 17e9);
+      // Epilogue of one CTA's 128 x BN block (measured: ~17 GB/s per CTA for
+      // 128 x 256, ~13.5 GB/s for 128 x 512), exposed once at the end, or
+      // after every wave without a second accumulator buffer.
+      const double epi_s = 128.0 * c.bn * ((out_f32 || sp > 1) ? 4.0 : 2.0) / (c.bn == 512 ? 13.5e9 : 17e9);
       double t = waves * unit_s + (c.bn == 512 ? waves : 1) * epi_s;
       if (sp > 1) {
         const double mn = (double)a.M * a.N * a.batch * a.batch2;
