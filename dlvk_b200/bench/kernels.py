@@ -26,7 +26,8 @@ def main():
     ap.add_argument("--vocab", type=int, default=32000)
     ap.add_argument("--params", type=int, default=185_000_000)
     ap.add_argument("--iters", type=int, default=20)
-    ap.add_argument("--only", default=None, choices=["bn"], help="bn: only the BatchNorm rows")
+    ap.add_argument("--only", default=None, choices=["bn", "ce"],
+                    help="bn: only the BatchNorm rows; ce: only softmax + cross-entropy")
     a = ap.parse_args()
     import dlvk_b200 as dl
     from dlvk_b200.models.params import Parameter, ParamStore
@@ -67,6 +68,14 @@ def main():
                time_fn(lambda: NN.batchnorm_bwd(bx, bg, bm, bs, bgam, bbet, dgb, dbb, False, True, 0.1, 3, 7, 5),
                        a.iters), 3 * n * 2)  # read x and dy, write dx
     if a.only == "bn":
+        for r in rows:
+            print(json.dumps(r), flush=True)
+        return
+    if a.only == "ce":
+        logits = torch.randn(R, V, device="cuda").bfloat16()
+        tgt = torch.randint(0, V, (R,), device="cuda", dtype=torch.int32)
+        report("softmax_ce(+grad in place)", time_fn(lambda: K.softmax_ce(logits, tgt, 1.0 / R, True, True), a.iters),
+               2 * R * V * 2)
         for r in rows:
             print(json.dumps(r), flush=True)
         return
