@@ -280,10 +280,12 @@ __global__ void __launch_bounds__(512, 2) softmax_ce_reg_kernel(const __nv_bfloa
 // blockIdx.x, + gridDim.x, ... and streams its next row into shared memory
 // with cp.async while it reduces the current one from registers, so the
 // memory system stays busy through the reductions and the gradient stores
-// (two blocks per SM, one 64 KB row buffer each at 32000 columns).  Same
-// arithmetic and results as softmax_ce_reg_kernel; dlogits may alias x (a
-// row is overwritten only after it has been read, and the prefetched row is
-// a different one).
+// (two blocks per SM, one 64 KB row buffer each at 32000 columns).  Unlike
+// softmax_ce_reg_kernel it computes each exponential once: the sum pass keeps
+// exp(x - max) in registers as bf16 in place of the logit, and the gradient
+// pass scales it (the label's gradient p - 1 stays in fp32 throughout).
+// dlogits may alias x (a row is overwritten only after it has been read, and
+// the prefetched row is a different one).
 template <int NV>
 __global__ void __launch_bounds__(512, 2) softmax_ce_pipe_kernel(const __nv_bfloat16* x, const int* __restrict__ labels,
                                                                  float* __restrict__ loss_rows,
@@ -342,16 +344,21 @@ __global__ void __launch_bounds__(512, 2) softmax_ce_pipe_kernel(const __nv_bflo
     mx = lane < THREADS / 32 ? red[lane] : -INFINITY;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    // The exponentials replace the logits in registers (as bf16), so the
+    // gradient pass needs none: non-label gradients carry one extra bf16
+    // rounding of p, the same size as the rounding of the stored gradient.
     float sum = 0.f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int v = threadIdx.x + i * THREADS;
       if (v < nvec) {
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw[i]);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const float2 f = __bfloat1622float2(h[k]);
-          sum += __expf(f.x - mx) + __expf(f.y - mx);
+          const float e0 = __expf(f.x - mx), e1 = __expf(f.y - mx);
+          sum += e0 + e1;
+          h[k] = __floats2bfloat162_rn(e0, e1);
         }
       }
     }
@@ -364,6 +371,8 @@ __global__ void __launch_bounds__(512, 2) softmax_ce_pipe_kernel(const __nv_bflo
     const float inv = 1.f / sum;
     if (threadIdx.x == 0 && loss_rows) loss_rows[r] = label < 0 ? 0.f : mx + logf(sum) - xl;
     const float gs = label < 0 ? 0.f : grad_scale;
+    const float gl = (__expf(xl - mx) * inv - 1.f) * gs;  // the label's gradient, from fp32 throughout
+    const float ginv = inv * gs;
     __nv_bfloat16* dr = dlogits + r * cols;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
@@ -375,9 +384,9 @@ __global__ void __launch_bounds__(512, 2) softmax_ce_pipe_kernel(const __nv_bflo
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const int c = v * 8 + 2 * k;
-        const float2 f = __bfloat1622float2(h[k]);
-        const float g0 = (__expf(f.x - mx) * inv - (c == label ? 1.f : 0.f)) * gs;
-        const float g1 = (__expf(f.y - mx) * inv - (c + 1 == label ? 1.f : 0.f)) * gs;
+        const float2 e = __bfloat1622float2(h[k]);
+        const float g0 = c == label ? gl : e.x * ginv;
+        const float g1 = c + 1 == label ? gl : e.y * ginv;
         oh[k] = __floats2bfloat162_rn(g0, g1);
       }
       reinterpret_cast<uint4*>(dr)[v] = o;

@@ -173,3 +173,24 @@ def test_grad_stats_and_clip():
     g[5] = float("inf")
     C.grad_stats(g, 1.0, 0.0, sumsq, flag, None, False, scratch)
     assert flag.item() == 1
+
+
+def test_softmax_ce_vocab_confident_label_gradient():
+    """Rows whose label dominates (p close to 1): the label's gradient p - 1 is
+    small and must stay accurate, so it is computed in fp32 from the logit and
+    not from the bf16-rounded probability."""
+    C = _C()
+    rows, cols = 300, 32000
+    x = torch.randn(rows, cols, device="cuda")
+    lab = torch.randint(0, cols, (rows,), device="cuda", dtype=torch.int32)
+    x[torch.arange(rows), lab.long()] += 20.0
+    x = x.bfloat16()
+    xf = x.float().requires_grad_(True)
+    torch.nn.functional.cross_entropy(xf, lab.long(), reduction="sum").backward()
+    _, dl = C.softmax_ce(x, lab, 1.0, in_place=False)
+    ref_l = xf.grad[torch.arange(rows), lab.long()]
+    got_l = dl.float()[torch.arange(rows), lab.long()]
+    # p - 1 is about -1e-4 here: rounding p to bf16 first would give 0
+    assert float(ref_l.abs().max()) < 1e-2
+    torch.testing.assert_close(got_l, ref_l, atol=1e-6, rtol=2e-2)
+    torch.testing.assert_close(dl.float(), xf.grad, atol=1e-3, rtol=2e-2)
