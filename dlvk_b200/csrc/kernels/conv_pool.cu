@@ -107,59 +107,84 @@ __global__ void __launch_bounds__(256) conv_dgrad_kernel(const T* __restrict__ g
 }
 
 // Weight/bias gradient partials: block (co, chunk) sums over the images of its
-// chunk and all output pixels; each thread keeps up to 32 weight partials in
-// registers (weights processed in groups of 32).  partial[chunk][co][Kel+1]
+// chunk and all output pixels; each thread keeps 32 weight partials in
+// registers (weights processed in groups of 32).  The group's input offsets
+// (ci, kh, kw) are decoded once into shared memory, so the pixel loop does
+// one bounds test, one load and one fma per weight.  partial[chunk][co][Kel+1]
 // (last slot = bias gradient).  Fixed reduction order => deterministic.
 template <typename T>
 __global__ void __launch_bounds__(256) conv_wgrad_partial_kernel(const T* __restrict__ x, const T* __restrict__ g,
                                                                  float* __restrict__ partial, ConvDesc d,
                                                                  int imgs_per_chunk) {
   __shared__ float red[8][33];
+  __shared__ int s_off[32], s_kh[32], s_kw[32];
   const int co = blockIdx.x, chunk = blockIdx.y;
   const int Kel = d.Cin * d.KH * d.KW;
   const int HWo = d.Ho * d.Wo;
+  const int64_t HW = (int64_t)d.H * d.W;
   const int n0 = chunk * imgs_per_chunk, n1 = min(d.N, n0 + imgs_per_chunk);
   const int64_t work = (int64_t)(n1 - n0) * HWo;
   float* out = partial + ((int64_t)chunk * d.Cout + co) * (Kel + 1);
-  for (int wg = 0; wg < Kel + 1; wg += 32) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  for (int wg = 0; wg < Kel; wg += 32) {
+    __syncthreads();  // the previous group's tables and red[] are no longer read
+    if (threadIdx.x < 32) {
+      const int wi = wg + threadIdx.x;
+      if (wi < Kel) {
+        const int ci = wi / (d.KH * d.KW);
+        const int r = wi - ci * d.KH * d.KW;
+        const int kh = r / d.KW, kw = r - kh * d.KW;
+        s_off[threadIdx.x] = (int)(ci * HW) + kh * d.W + kw;
+        s_kh[threadIdx.x] = kh;
+        s_kw[threadIdx.x] = kw;
+      } else {  // past the last weight: never in range
+        s_off[threadIdx.x] = 0;
+        s_kh[threadIdx.x] = -(1 << 28);
+        s_kw[threadIdx.x] = 0;
+      }
+    }
+    __syncthreads();
     float acc[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+    float bacc = 0.f;
     for (int64_t it = threadIdx.x; it < work; it += blockDim.x) {
       const int n = n0 + (int)(it / HWo);
       const int pix = (int)(it - (int64_t)(n - n0) * HWo);
       const int oh = pix / d.Wo, ow = pix - oh * d.Wo;
       const float gv = to_f32(g[((int64_t)n * d.Cout + co) * HWo + pix]);
       if (gv == 0.f) continue;
+      bacc += gv;
+      const int ih0 = oh * d.stride - d.pad, iw0 = ow * d.stride - d.pad;
+      const int64_t base = ((int64_t)n * d.Cin * d.H + ih0) * d.W + iw0;
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        const int wi = wg + j;
-        if (wi < Kel) {
-          const int ci = wi / (d.KH * d.KW);
-          const int r = wi - ci * d.KH * d.KW;
-          const int kh = r / d.KW, kw = r - kh * d.KW;
-          const int ih = oh * d.stride - d.pad + kh, iw = ow * d.stride - d.pad + kw;
-          if (ih >= 0 && ih < d.H && iw >= 0 && iw < d.W)
-            acc[j] = fmaf(gv, to_f32(x[(((int64_t)n * d.Cin + ci) * d.H + ih) * d.W + iw]), acc[j]);
-        } else if (wi == Kel) {
-          acc[j] += gv;
-        }
+        const int ih = ih0 + s_kh[j], iw = iw0 + s_kw[j];
+        if ((unsigned)ih < (unsigned)d.H && (unsigned)iw < (unsigned)d.W)
+          acc[j] = fmaf(gv, to_f32(x[base + s_off[j]]), acc[j]);
       }
     }
-    // Block reduction of the 32 partials: warp shuffle then across warps.
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    // Block reduction of the 32 partials (and, in the first group, the bias
+    // sum): warp shuffle then across warps.
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const float v = warp_sum(acc[j]);
       if (lane == j) red[wid][j] = v;
     }
-    __syncthreads();
-    if (threadIdx.x < 32) {
-      float s = 0.f;
-      for (int i = 0; i < (int)(blockDim.x >> 5); ++i) s += red[i][threadIdx.x];
-      if (wg + (int)threadIdx.x < Kel + 1) out[wg + threadIdx.x] = s;
+    if (wg == 0) {
+      const float v = warp_sum(bacc);
+      if (lane == 0) red[wid][32] = v;
     }
     __syncthreads();
+    if (threadIdx.x < 33) {
+      float sum = 0.f;
+      for (int i = 0; i < (int)(blockDim.x >> 5); ++i) sum += red[i][threadIdx.x];
+      if (threadIdx.x < 32) {
+        if (wg + (int)threadIdx.x < Kel) out[wg + threadIdx.x] = sum;
+      } else if (wg == 0) {
+        out[Kel] = sum;
+      }
+    }
   }
 }
 

@@ -31,8 +31,11 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs a) {
   const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // 16 x 16 threads
   float acc[4][4] = {};
-  for (int64_t k0 = 0; k0 < a.K; k0 += BK) {
-    // Load A tile (BM x BK) and B tile (BK x BN): 1024 elements each, 4 per thread.
+  // The next K slice is loaded into registers while the current one is
+  // multiplied out of shared memory, so each block pays the global-load
+  // latency once instead of once per slice (small GEMMs run few blocks).
+  float ra[4], rb[4];
+  auto load = [&](int64_t k0) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int e = threadIdx.x + i * 256;
@@ -40,13 +43,27 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs a) {
       int mm, kk;
       if (a.sak == 1) { kk = e % BK; mm = e / BK; } else { mm = e % BM; kk = e / BM; }
       const int64_t gm = m0 + mm, gk = k0 + kk;
-      As[kk][mm] = (gm < a.M && gk < a.K) ? to_f32(A[gm * a.sam + gk * a.sak]) : 0.f;
+      ra[i] = (gm < a.M && gk < a.K) ? to_f32(A[gm * a.sam + gk * a.sak]) : 0.f;
       int nn, kb;
       if (a.sbn == 1) { nn = e % BN; kb = e / BN; } else { kb = e % BK; nn = e / BK; }
       const int64_t gn = n0 + nn, gkb = k0 + kb;
-      Bs[kb][nn] = (gn < a.N && gkb < a.K) ? to_f32(B[gkb * a.sbk + gn * a.sbn]) : 0.f;
+      rb[i] = (gn < a.N && gkb < a.K) ? to_f32(B[gkb * a.sbk + gn * a.sbn]) : 0.f;
+    }
+  };
+  load(0);
+  for (int64_t k0 = 0; k0 < a.K; k0 += BK) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = threadIdx.x + i * 256;
+      int mm, kk;
+      if (a.sak == 1) { kk = e % BK; mm = e / BK; } else { mm = e % BM; kk = e / BM; }
+      As[kk][mm] = ra[i];
+      int nn, kb;
+      if (a.sbn == 1) { nn = e % BN; kb = e / BN; } else { kb = e % BK; nn = e / BK; }
+      Bs[kb][nn] = rb[i];
     }
     __syncthreads();
+    if (k0 + BK < a.K) load(k0 + BK);
 #pragma unroll
     for (int kk = 0; kk < BK; ++kk) {
       float av[4], bv[4];
