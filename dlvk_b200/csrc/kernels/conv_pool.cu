@@ -109,8 +109,8 @@ __global__ void __launch_bounds__(256) conv_dgrad_kernel(const T* __restrict__ g
 // Weight/bias gradient partials: block (co, chunk) sums over the images of its
 // chunk and all output pixels; each thread keeps 32 weight partials in
 // registers (weights processed in groups of 32).  The group's input offsets
-// (ci, kh, kw) are decoded once into shared memory, so the pixel loop does
-// one bounds test, one load and one fma per weight.  partial[chunk][co][Kel+1]
+// (ci, kh, kw) are decoded once (through shared memory into registers), so
+// the pixel loop does one bounds test, one load and one fma per weight.  partial[chunk][co][Kel+1]
 // (last slot = bias gradient).  Fixed reduction order => deterministic.
 template <typename T>
 __global__ void __launch_bounds__(256) conv_wgrad_partial_kernel(const T* __restrict__ x, const T* __restrict__ g,
@@ -139,14 +139,19 @@ __global__ void __launch_bounds__(256) conv_wgrad_partial_kernel(const T* __rest
         s_kw[threadIdx.x] = kw;
       } else {  // past the last weight: never in range
         s_off[threadIdx.x] = 0;
-        s_kh[threadIdx.x] = -(1 << 28);
+        s_kh[threadIdx.x] = -(1 << 14);
         s_kw[threadIdx.x] = 0;
       }
     }
     __syncthreads();
     float acc[32];
+    int toff[32], tkw[32];  // the table in registers: input offset, and kh << 16 | kw
 #pragma unroll
-    for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+    for (int j = 0; j < 32; ++j) {
+      acc[j] = 0.f;
+      toff[j] = s_off[j];
+      tkw[j] = (s_kh[j] << 16) | (s_kw[j] & 0xffff);
+    }
     float bacc = 0.f;
     for (int64_t it = threadIdx.x; it < work; it += blockDim.x) {
       const int n = n0 + (int)(it / HWo);
@@ -159,9 +164,9 @@ __global__ void __launch_bounds__(256) conv_wgrad_partial_kernel(const T* __rest
       const int64_t base = ((int64_t)n * d.Cin * d.H + ih0) * d.W + iw0;
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        const int ih = ih0 + s_kh[j], iw = iw0 + s_kw[j];
+        const int ih = ih0 + (tkw[j] >> 16), iw = iw0 + (short)(tkw[j] & 0xffff);
         if ((unsigned)ih < (unsigned)d.H && (unsigned)iw < (unsigned)d.W)
-          acc[j] = fmaf(gv, to_f32(x[base + s_off[j]]), acc[j]);
+          acc[j] = fmaf(gv, to_f32(x[base + toff[j]]), acc[j]);
       }
     }
     // Block reduction of the 32 partials (and, in the first group, the bias
