@@ -26,8 +26,8 @@ def main():
     ap.add_argument("--vocab", type=int, default=32000)
     ap.add_argument("--params", type=int, default=185_000_000)
     ap.add_argument("--iters", type=int, default=20)
-    ap.add_argument("--only", default=None, choices=["bn", "ce"],
-                    help="bn: only the BatchNorm rows; ce: only softmax + cross-entropy")
+    ap.add_argument("--only", default=None, choices=["bn", "ce", "ln"],
+                    help="bn: only the BatchNorm rows; ce: only softmax + cross-entropy; ln: only LayerNorm")
     a = ap.parse_args()
     import dlvk_b200 as dl
     from dlvk_b200.models.params import Parameter, ParamStore
@@ -85,6 +85,10 @@ def main():
                                           a.iters), 4 * R * D * 2 + R * 8)
     report("layernorm_bwd", time_fn(lambda: NN.layernorm_bwd(x, gamma, mean, rstd, dy, dg, db, False), a.iters),
            3 * R * D * 2 + R * 8)
+    if a.only == "ln":
+        for r in rows:
+            print(json.dumps(r), flush=True)
+        return
     logits = torch.randn(R, V, device="cuda").bfloat16()
     tgt = torch.randint(0, V, (R,), device="cuda", dtype=torch.int32)
     report("softmax_ce(+grad in place)", time_fn(lambda: K.softmax_ce(logits, tgt, 1.0 / R, True, True), a.iters),
