@@ -753,10 +753,12 @@ void flash_attention_fwd(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* ls
   const int E = H * FD;
   CUtensorMap tm = tmap::bf16_2d_sw128(qkv, (uint64_t)3 * E, (uint64_t)B * S, (uint64_t)3 * E, FT);
   FwdP p{out, lse, B, S, H, E, scale * 1.4426950408889634f, err};
-  static bool attr = false;
-  if (!attr) {
+  int adev = 0;
+  DLVK_CUDA_CHECK(cudaGetDevice(&adev));
+  static bool attr[64] = {};  // per device: the attribute belongs to each device's context
+  if (adev >= 64 || !attr[adev]) {
     DLVK_CUDA_CHECK(cudaFuncSetAttribute(flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM));
-    attr = true;
+    if (adev < 64) attr[adev] = true;
   }
   const int items = B * H * (S / FT);
   int grid = std::min(items, max_ctas > 0 ? max_ctas : tmap::sm_count());
@@ -792,10 +794,12 @@ void flash_attention_bwd(const __nv_bfloat16* qkv, const __nv_bfloat16* out, con
     if (r != CUDA_SUCCESS) throw std::runtime_error("dlvk: dq tensor map failed (" + std::to_string((int)r) + ")");
   }
   BwdP p{lse, delta, dqkv, B, S, H, E, scale * 1.4426950408889634f, scale, err};
-  static bool attr = false;
-  if (!attr) {
+  int adev = 0;
+  DLVK_CUDA_CHECK(cudaGetDevice(&adev));
+  static bool attr[64] = {};  // per device: the attribute belongs to each device's context
+  if (adev >= 64 || !attr[adev]) {
     DLVK_CUDA_CHECK(cudaFuncSetAttribute(flash_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM));
-    attr = true;
+    if (adev < 64) attr[adev] = true;
   }
   const int items = B * H * (S / FT);
   const int grid = std::min(items, max_ctas > 0 ? max_ctas : tmap::sm_count());

@@ -80,3 +80,35 @@ def test_attention_layer_uses_fused_path():
     assert ((dx1.float() - dx0.float()).norm() / dx0.float().norm()).item() < 3e-2
     for a, b in zip(lay.parameters(), twin.parameters()):
         assert ((a.grad - b.grad).norm() / b.grad.norm()).item() < 3e-2, a.name
+
+
+@pytest.mark.multigpu
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two CUDA devices")
+def test_kernels_on_two_devices_in_one_process():
+    """One process driving two GPUs: the kernels whose launchers raise the
+    dynamic shared-memory limit (fused attention, the persistent softmax-CE,
+    the tensor-core GEMM) must do so on each device before launching there."""
+    C = _ext.C()
+    B, S, H, D = 2, 256, 2, 64
+    scale = 1.0 / math.sqrt(D)
+    for dev in ("cuda:0", "cuda:1"):
+        with torch.cuda.device(dev):
+            g = torch.Generator().manual_seed(7)
+            qkv = torch.randn(B, S, 3 * H * D, generator=g).to(dev, torch.bfloat16)
+            out, lse = C.flash_attn_fwd(qkv, B, S, H, scale, 0)
+            x, o_ref, lse_ref = ref_attention(qkv.to("cuda:0"), B, S, H, D, scale)
+            err = (out.float().to("cuda:0") - o_ref.detach()).abs().max().item()
+            assert err < 2e-2 * max(1.0, o_ref.abs().max().item()), (dev, err)
+            dqkv = C.flash_attn_bwd(qkv, out, torch.ones_like(out), lse, B, S, H, scale, 0)
+            assert torch.isfinite(dqkv.float()).all()
+            logits = torch.randn(300, 32000, generator=g).to(dev, torch.bfloat16)
+            lab = torch.randint(0, 32000, (300,), generator=g, dtype=torch.int32).to(dev)
+            loss_rows, _ = C.softmax_ce(logits, lab, 1.0)
+            ref = torch.nn.functional.cross_entropy(logits.float(), lab.long(), reduction="none")
+            torch.testing.assert_close(loss_rows, ref, atol=0.05, rtol=1e-2)
+            a = torch.randn(512, 256, generator=g).to(dev, torch.bfloat16)
+            b = torch.randn(256, 1024, generator=g).to(dev, torch.bfloat16)
+            c = C.gemm(a, b, force_path=1)
+            assert (c.float() - a.float() @ b.float()).abs().max().item() < 2e-2 * (a.float() @ b.float()).abs().max().item()
+            torch.cuda.synchronize(dev)
+    assert C.read_device_error(True) == 0
