@@ -2,14 +2,16 @@
 #pragma once
 #include <torch/extension.h>
 
+#include "dlvk/aten_ops.h"
 #include "dlvk/common.h"
 
 namespace dlvk {
 namespace bind {
 
-DType to_dtype(const at::Tensor& t);
-void check_cuda(const at::Tensor& t, const char* name);
-cudaStream_t stream();
+// Tensor helpers of the ATen op layer (dlvk/aten_ops.h).
+using ::dlvk::aten::check_cuda;
+using ::dlvk::aten::stream;
+using ::dlvk::aten::to_dtype;
 
 void register_ops(py::module& m);
 void register_runtime(py::module& m);

@@ -49,6 +49,21 @@ void note_launch(uint64_t n = 1);
     if (!(cond)) throw std::runtime_error(std::string("dlvk: ") + (msg));        \
   } while (0)
 
+namespace dlvk {
+// Per-device host caches (kernel attributes, SM counts, error words) are
+// fixed arrays of kMaxDevices slots.  current_device_slot() returns the
+// current device's ordinal after checking that it fits, so no launcher
+// indexes one of those arrays out of bounds.
+constexpr int kMaxDevices = 64;
+inline int current_device_slot() {
+  int dev = 0;
+  DLVK_CUDA_CHECK(cudaGetDevice(&dev));
+  DLVK_CHECK(dev >= 0 && dev < kMaxDevices,
+             "device ordinal " + std::to_string(dev) + " is beyond the per-device cache size 64");
+  return dev;
+}
+}  // namespace dlvk
+
 // Launch bookkeeping: every launcher calls this right after its <<<>>>.
 #define DLVK_POST_LAUNCH()                                                       \
   do {                                                                           \

@@ -42,7 +42,10 @@ extern "C" {
 // out[c] = scale * sum_r x[r * cols + c] (+ out[c] if accumulate != 0).
 // x: device pointer, dtype 0 = float32, 1 = bfloat16, row-major [rows, cols];
 // out: device float32 [cols].  Enqueued on `stream`; returns a
-// DLVK_NOALLOC_* code.  Allocates no memory.
+// DLVK_NOALLOC_* code.  Allocates no memory.  DLVK_NOALLOC_CUDA_ERROR is
+// also returned, before anything is launched, when an earlier CUDA error is
+// already pending on the calling thread; in every error case `out` has not
+// been written by this call.
 int dlvk_colsum_noalloc(const void* x, int dtype, int64_t rows, int64_t cols, float scale, float* out,
                         int accumulate, cudaStream_t stream);
 

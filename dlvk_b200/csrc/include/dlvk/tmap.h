@@ -58,9 +58,8 @@ inline CUtensorMap bf16_2d_sw128(const void* base, uint64_t cols, uint64_t rows,
 }
 
 inline int sm_count() {
-  static int n[64] = {0};
-  int dev = 0;
-  DLVK_CUDA_CHECK(cudaGetDevice(&dev));
+  static int n[kMaxDevices] = {0};
+  const int dev = current_device_slot();
   if (n[dev] == 0) DLVK_CUDA_CHECK(cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev));
   return n[dev];
 }

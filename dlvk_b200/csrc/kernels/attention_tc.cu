@@ -689,37 +689,41 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
   }
 }
 
-// delta[b, h, q] = sum_d dO[b, q, h, d] * O[b, q, h, d]; one thread per
-// (b, q, h) row of 64 with 16-byte loads (consecutive threads read
-// consecutive rows).
+// delta[b, h, q] = sum_d dO[b, q, h, d] * O[b, q, h, d]: eight lanes per
+// (b, q, h) row of 64, one 16-byte vector of each operand per lane, reduced
+// with three shuffles.  A warp reads four consecutive rows (512 contiguous
+// bytes per operand per load instruction).
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
                                   float* __restrict__ delta, int B, int S, int H) {
   pdl_wait();
-  const int64_t total = (int64_t)B * S * H;
-  for (int64_t w = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; w < total; w += (int64_t)gridDim.x * blockDim.x) {
-    const uint4* a = reinterpret_cast<const uint4*>(o + w * FD);
-    const uint4* d = reinterpret_cast<const uint4*>(dout + w * FD);
-    uint4 av[8], dv[8];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      av[c] = a[c];
-      dv[c] = d[c];
-    }
+  const int64_t total = (int64_t)B * S * H * 8;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  // Warp-uniform trip count: lanes past the end compute zeros and store nothing.
+  for (int64_t base = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); base < total; base += stride) {
+    const int64_t t = base + (threadIdx.x & 31);
+    const bool on = t < total;
+    const int64_t w = t >> 3;
     float acc = 0.f;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const __nv_bfloat162* x = reinterpret_cast<const __nv_bfloat162*>(&av[c]);
-      const __nv_bfloat162* y = reinterpret_cast<const __nv_bfloat162*>(&dv[c]);
+    if (on) {
+      const uint4 av = reinterpret_cast<const uint4*>(o + w * FD)[t & 7];
+      const uint4 dv = reinterpret_cast<const uint4*>(dout + w * FD)[t & 7];
+      const __nv_bfloat162* x = reinterpret_cast<const __nv_bfloat162*>(&av);
+      const __nv_bfloat162* y = reinterpret_cast<const __nv_bfloat162*>(&dv);
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const float2 xf = __bfloat1622float2(x[k]), yf = __bfloat1622float2(y[k]);
         acc = fmaf(xf.x, yf.x, fmaf(xf.y, yf.y, acc));
       }
     }
-    const int h = (int)(w % H);
-    const int64_t bq = w / H;
-    const int q = (int)(bq % S), b = (int)(bq / S);
-    delta[((int64_t)b * H + h) * S + q] = acc;
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+    if (on && (t & 7) == 0) {
+      const int h = (int)(w % H);
+      const int64_t bq = w / H;
+      const int q = (int)(bq % S), b = (int)(bq / S);
+      delta[((int64_t)b * H + h) * S + q] = acc;
+    }
   }
 }
 
@@ -753,12 +757,11 @@ void flash_attention_fwd(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* ls
   const int E = H * FD;
   CUtensorMap tm = tmap::bf16_2d_sw128(qkv, (uint64_t)3 * E, (uint64_t)B * S, (uint64_t)3 * E, FT);
   FwdP p{out, lse, B, S, H, E, scale * 1.4426950408889634f, err};
-  int adev = 0;
-  DLVK_CUDA_CHECK(cudaGetDevice(&adev));
-  static bool attr[64] = {};  // per device: the attribute belongs to each device's context
-  if (adev >= 64 || !attr[adev]) {
+  const int adev = current_device_slot();
+  static bool attr[kMaxDevices] = {};  // per device: the attribute belongs to each device's context
+  if (!attr[adev]) {
     DLVK_CUDA_CHECK(cudaFuncSetAttribute(flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM));
-    if (adev < 64) attr[adev] = true;
+    attr[adev] = true;
   }
   const int items = B * H * (S / FT);
   int grid = std::min(items, max_ctas > 0 ? max_ctas : tmap::sm_count());
@@ -774,9 +777,9 @@ void flash_attention_bwd(const __nv_bfloat16* qkv, const __nv_bfloat16* out, con
   const int E = H * FD;
   const int64_t rows = (int64_t)B * S;
   {
-    const int64_t n = rows * H;
-    launch_pdl(attn_delta_kernel, dim3((unsigned)std::min<int64_t>((n + 255) / 256, 148 * 8)), dim3(256), 0, s, out,
-               dout, delta, B, S, H);
+    const int64_t n = rows * H * 8;
+    launch_pdl(attn_delta_kernel, dim3((unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)tmap::sm_count() * 16)),
+               dim3(256), 0, s, out, dout, delta, B, S, H);
     DLVK_POST_LAUNCH();
   }
   DLVK_CUDA_CHECK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * E, s));
@@ -794,12 +797,11 @@ void flash_attention_bwd(const __nv_bfloat16* qkv, const __nv_bfloat16* out, con
     if (r != CUDA_SUCCESS) throw std::runtime_error("dlvk: dq tensor map failed (" + std::to_string((int)r) + ")");
   }
   BwdP p{lse, delta, dqkv, B, S, H, E, scale * 1.4426950408889634f, scale, err};
-  int adev = 0;
-  DLVK_CUDA_CHECK(cudaGetDevice(&adev));
-  static bool attr[64] = {};  // per device: the attribute belongs to each device's context
-  if (adev >= 64 || !attr[adev]) {
+  const int adev = current_device_slot();
+  static bool attr[kMaxDevices] = {};  // per device: the attribute belongs to each device's context
+  if (!attr[adev]) {
     DLVK_CUDA_CHECK(cudaFuncSetAttribute(flash_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM));
-    if (adev < 64) attr[adev] = true;
+    attr[adev] = true;
   }
   const int items = B * H * (S / FT);
   const int grid = std::min(items, max_ctas > 0 ? max_ctas : tmap::sm_count());

@@ -82,6 +82,13 @@ extern "C" int dlvk_colsum_noalloc(const void* x, int dtype, int64_t rows, int64
     return DLVK_NOALLOC_BAD_ARG;
   if (cols > DLVK_NOALLOC_MAX_COLS) return DLVK_NOALLOC_TOO_LARGE;
   if (rows == 0 || cols == 0) return DLVK_NOALLOC_OK;
+  // An error that earlier, unrelated work left pending on this thread is
+  // reported before anything is queued (and left pending for the caller's
+  // own handling).  The launch checks below then see only this call's own
+  // launches, and the first kernel writes `out` only when it is the sole
+  // launch: a DLVK_NOALLOC_CUDA_ERROR return never follows a queued kernel
+  // that wrote `out`, so retrying with accumulate = 1 cannot add twice.
+  if (cudaPeekAtLastError() != cudaSuccess) return DLVK_NOALLOC_CUDA_ERROR;
   int err = DLVK_NOALLOC_OK;
   float* part = scratch_for_current_device(&err);
   if (part == nullptr) return err;

@@ -580,9 +580,8 @@ int g_conv_tc_override = -1;
 template <int BN>
 void launch_igemm(const CUtensorMap& tm, const IgemmParams& p, cudaStream_t s) {
   using C = IgCfg<BN>;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  DLVK_CUDA_CHECK(cudaGetDevice(&dev));
+  static bool attr_set[kMaxDevices] = {false};
+  const int dev = current_device_slot();
   if (!attr_set[dev]) {
     DLVK_CUDA_CHECK(cudaFuncSetAttribute(conv_igemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_set[dev] = true;
@@ -701,9 +700,8 @@ void conv2d_wgrad_tc(const __nv_bfloat16* x_nhwc, const __nv_bfloat16* dy_nhwc, 
   tmap::bind_context();
   // dY as a row-major [P, OC] matrix: 64 x 64 boxes, read M(OC)-major.
   const CUtensorMap tm = tmap::bf16_2d_sw128(dy_nhwc, (uint64_t)d.Cout, (uint64_t)p.P, (uint64_t)d.Cout, 64u);
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  DLVK_CUDA_CHECK(cudaGetDevice(&dev));
+  static bool attr_set[kMaxDevices] = {false};
+  const int dev = current_device_slot();
   if (!attr_set[dev]) {
     DLVK_CUDA_CHECK(cudaFuncSetAttribute(conv_wgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, WgCfg::SMEM));
     attr_set[dev] = true;

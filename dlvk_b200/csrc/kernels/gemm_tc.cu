@@ -817,9 +817,8 @@ CUtensorMap make_tmap(const void* base, uint64_t d0, uint64_t d1, uint64_t d2, u
 }
 
 int sm_count() {
-  static int n[64] = {0};
-  int dev = 0;
-  DLVK_CUDA_CHECK(cudaGetDevice(&dev));
+  static int n[kMaxDevices] = {0};
+  const int dev = current_device_slot();
   if (n[dev] == 0) DLVK_CUDA_CHECK(cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev));
   return n[dev];
 }
@@ -828,9 +827,8 @@ template <int BN>
 void launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const TcParams& p, int max_ctas,
                cudaStream_t s) {
   using C = Cfg<BN>;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  DLVK_CUDA_CHECK(cudaGetDevice(&dev));
+  static bool attr_set[kMaxDevices] = {false};
+  const int dev = current_device_slot();
   if (!attr_set[dev]) {
     DLVK_CUDA_CHECK(cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_set[dev] = true;
@@ -847,9 +845,8 @@ template <int BN>
 void launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const TcParams& p,
                     int max_ctas, cudaStream_t s) {
   using C = Cfg<BN, true>;
-  static int max_pairs[64] = {0};
-  int dev = 0;
-  DLVK_CUDA_CHECK(cudaGetDevice(&dev));
+  static int max_pairs[kMaxDevices] = {0};
+  const int dev = current_device_slot();
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;

@@ -592,13 +592,13 @@ void launch_ce(const void* x, const int* labels, const float* probs, float* loss
       if (pipe && smem <= 100 * 1024) {
         auto kern = per <= 2 ? softmax_ce_pipe_kernel<2>
                              : (per <= 4 ? softmax_ce_pipe_kernel<4> : softmax_ce_pipe_kernel<8>);
-        int sms = 0, dev = 0;
-        DLVK_CUDA_CHECK(cudaGetDevice(&dev));
-        static bool attr[64][3] = {};  // per device and instantiation (set to the largest row size allowed)
+        int sms = 0;
+        const int dev = current_device_slot();
+        static bool attr[kMaxDevices][3] = {};  // per device and instantiation (set to the largest row size allowed)
         const int ai = per <= 2 ? 0 : (per <= 4 ? 1 : 2);
-        if (dev >= 64 || !attr[dev][ai]) {
+        if (!attr[dev][ai]) {
           DLVK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
-          if (dev < 64) attr[dev][ai] = true;
+          attr[dev][ai] = true;
         }
         DLVK_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
         const unsigned grid = (unsigned)std::min<int64_t>(rows, 2 * (int64_t)sms);

@@ -14,7 +14,7 @@ namespace dlvk {
 namespace {
 std::atomic<uint64_t> g_launches{0};
 std::mutex g_err_mu;
-uint32_t* g_err_words[64] = {nullptr};
+uint32_t* g_err_words[kMaxDevices] = {nullptr};
 }  // namespace
 
 uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
@@ -36,8 +36,7 @@ void throw_cuda(cudaError_t e, const char* what, const char* file, int line) {
 }
 
 uint32_t* device_error_word() {
-  int dev = 0;
-  DLVK_CUDA_CHECK(cudaGetDevice(&dev));
+  const int dev = current_device_slot();
   std::lock_guard<std::mutex> lk(g_err_mu);
   if (g_err_words[dev] == nullptr) {
     void* p = nullptr;

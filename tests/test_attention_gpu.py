@@ -111,4 +111,5 @@ def test_kernels_on_two_devices_in_one_process():
             c = C.gemm(a, b, force_path=1)
             assert (c.float() - a.float() @ b.float()).abs().max().item() < 2e-2 * (a.float() @ b.float()).abs().max().item()
             torch.cuda.synchronize(dev)
-    assert C.read_device_error(True) == 0
+            # the error word is per device: read this device's, with it current
+            assert C.read_device_error(True) == 0, dev

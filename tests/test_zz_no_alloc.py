@@ -59,12 +59,17 @@ def test_noalloc_colsum_matches_regular_entry_point(dtype, rows, cols):
         assert torch.cuda.memory_stats()["allocation.all.allocated"] == before
         ref = mod.colsum(x, 0.5)
         torch.testing.assert_close(out, ref, rtol=1e-5, atol=1e-4)
+        # and against an independent fp64 sum, which shares no code with either
+        exact = (x.double().sum(0) * 0.5).float()
+        torch.testing.assert_close(out, exact, rtol=1e-5, atol=1e-3)
     # accumulate mode against the regular entry point's accumulate mode
-    acc_ref = torch.randn(cols, device="cuda")
-    acc = acc_ref.clone()
+    acc0 = torch.randn(cols, device="cuda")
+    acc_ref = acc0.clone()
+    acc = acc0.clone()
     assert _call(fn, xs[0], acc, 1.0, accumulate=True) == OK
     mod.colsum(xs[0], 1.0, out=acc_ref, accumulate=True)
     torch.testing.assert_close(acc, acc_ref, rtol=1e-5, atol=1e-4)
+    torch.testing.assert_close(acc, (acc0.double() + xs[0].double().sum(0)).float(), rtol=1e-5, atol=2e-3)
 
 
 def test_noalloc_colsum_rejects_too_many_columns():
