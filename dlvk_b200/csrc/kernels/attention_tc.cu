@@ -44,7 +44,6 @@ using namespace sm100;
 constexpr int FT = 128;                  // query / key tile
 constexpr int FD = 64;                   // head dim
 constexpr int TILE = FT * FD * 2;        // one bf16 [128 x 64] tile, 16 KB
-constexpr int KV_STAGES = 3;
 
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
   __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
@@ -104,45 +103,59 @@ struct FwdP {
   uint32_t* err;
 };
 
-// Shared memory: Q x2 | (K, V) x KV_STAGES | P (32 KB) | barriers.
-constexpr int FWD_SMEM = 2 * TILE + KV_STAGES * 2 * TILE + 2 * TILE + 256 + 1024;
+// Two softmax warpgroups ("streams" 0 and 1) work on independent items in
+// ping-pong: CTA c gives items c, c + 2g, ... to stream 0 and c + g,
+// c + 3g, ... to stream 1 (g = grid size).  Each stream has its own TMEM
+// score buffer S and output accumulator O, its own Q tile and its own P tile
+// in shared memory; the K / V ring, the TMA producer warp and the MMA warp
+// are shared.  While one stream normalises and stores its finished item, or
+// waits for its next scores, the other keeps the exponential unit busy.
+//
+// TMEM (512 columns): S0 0..127, S1 128..255, O0 256..319, O1 320..383.
+// Shared memory: Q x2 | (K, V) x FWD_KV_STAGES | P x2 (32 KB each) | barriers.
+constexpr int FWD_KV_STAGES = 4;
+constexpr int FWD_THREADS = 64 + 2 * 128;
+constexpr int FWD_SMEM = 2 * TILE + FWD_KV_STAGES * 2 * TILE + 2 * 2 * TILE + 256 + 1024;
 
-__global__ void __launch_bounds__(192, 1) flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, FwdP p) {
+__global__ void __launch_bounds__(FWD_THREADS, 1) flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, FwdP p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sKV = smem + 2 * TILE;
-  uint8_t* sP = sKV + KV_STAGES * 2 * TILE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * TILE);
-  uint64_t* q_full = bars;         // 2
-  uint64_t* q_empty = bars + 2;    // 2
-  uint64_t* kv_full = bars + 4;    // 3
-  uint64_t* kv_empty = bars + 7;   // 3
-  uint64_t* s_full = bars + 10;    // 2
-  uint64_t* s_empty = bars + 12;   // 2
-  uint64_t* p_full = bars + 14;
-  uint64_t* pv_done = bars + 15;
-  uint64_t* o_empty = bars + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  uint8_t* sQ = smem;                                   // stream t: sQ + t * TILE
+  uint8_t* sKV = smem + 2 * TILE;                       // stage k: K at k * 2 * TILE, V at + TILE
+  uint8_t* sP = sKV + FWD_KV_STAGES * 2 * TILE;         // stream t: sP + t * 2 * TILE
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * 2 * TILE);
+  uint64_t* q_full = bars;                              // [2] per stream
+  uint64_t* q_empty = bars + 2;                         // [2]
+  uint64_t* kv_full = bars + 4;                         // [FWD_KV_STAGES]
+  uint64_t* kv_empty = bars + 4 + FWD_KV_STAGES;        // [FWD_KV_STAGES]
+  uint64_t* s_full = bars + 4 + 2 * FWD_KV_STAGES;      // [2]
+  uint64_t* s_empty = s_full + 2;                       // [2], 4 warp arrivals
+  uint64_t* p_full = s_full + 4;                        // [2], 4 warp arrivals
+  uint64_t* pv_done = s_full + 6;                       // [2]
+  uint64_t* o_empty = s_full + 8;                       // [2], 4 warp arrivals
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 10);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nt = p.S / FT;
   const int items = p.B * p.H * nt;
+  const int g = (int)gridDim.x;
+  // Item of stream t in round r of this CTA (>= items: none).
+  auto item_of = [&](int r, int t) { return (int)blockIdx.x + (2 * r + t) * g; };
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&q_full[t], 1);
+      mbar_init(&q_empty[t], 1);
+      mbar_init(&s_full[t], 1);
+      mbar_init(&s_empty[t], 4);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&pv_done[t], 1);
+      mbar_init(&o_empty[t], 4);
     }
-    for (int i = 0; i < KV_STAGES; ++i) {
+    for (int i = 0; i < FWD_KV_STAGES; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
-    mbar_init(p_full, 4);
-    mbar_init(pv_done, 1);
-    mbar_init(o_empty, 4);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -152,216 +165,225 @@ __global__ void __launch_bounds__(192, 1) flash_fwd_kernel(const __grid_constant
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tbase = *tmem_slot;  // S0: cols 0..127, S1: 128..255, O: 256..319
+  const uint32_t tbase = *tmem_slot;
   pdl_wait();
 
   if (warp == 0) {
     if (lane == 0) {
       prefetch_tmap(&tm);
-      int it = 0;
       int kvs = 0;
       uint32_t kvph = 0;
-      for (int item = blockIdx.x; item < items; item += gridDim.x, ++it) {
-        const int qt = item % nt, bh = item / nt, h = bh % p.H, b = bh / p.H;
-        const int qs = it & 1;
-        if (!mbar_wait(&q_empty[qs], ((it >> 1) & 1) ^ 1u, p.err)) break;
-        mbar_arrive_expect_tx(&q_full[qs], TILE);
-        tma_load_2d(sQ + qs * TILE, &tm, &q_full[qs], h * FD, b * p.S + qt * FT);
-        bool ok = true;
-        for (int j = 0; j < nt; ++j) {
-          if (!mbar_wait(&kv_empty[kvs], kvph ^ 1u, p.err)) { ok = false; break; }
-          uint8_t* k = sKV + kvs * 2 * TILE;
-          mbar_arrive_expect_tx(&kv_full[kvs], 2 * TILE);
-          tma_load_2d(k, &tm, &kv_full[kvs], p.E + h * FD, b * p.S + j * FT);
-          tma_load_2d(k + TILE, &tm, &kv_full[kvs], 2 * p.E + h * FD, b * p.S + j * FT);
-          if (++kvs == KV_STAGES) {
-            kvs = 0;
-            kvph ^= 1u;
+      bool ok = true;
+      // Loads in the MMA warp's consumption order: round r, tile j, stream 0 then 1.
+      for (int r = 0; ok && item_of(r, 0) < items; ++r) {
+        for (int j = 0; ok && j < nt; ++j) {
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int item = item_of(r, t);
+            if (item >= items) continue;
+            const int qt = item % nt, bh = item / nt, h = bh % p.H, b = bh / p.H;
+            if (j == 0) {
+              if (!mbar_wait(&q_empty[t], (r & 1) ^ 1u, p.err)) { ok = false; break; }
+              mbar_arrive_expect_tx(&q_full[t], TILE);
+              tma_load_2d(sQ + t * TILE, &tm, &q_full[t], h * FD, b * p.S + qt * FT);
+            }
+            if (!mbar_wait(&kv_empty[kvs], kvph ^ 1u, p.err)) { ok = false; break; }
+            uint8_t* k = sKV + kvs * 2 * TILE;
+            mbar_arrive_expect_tx(&kv_full[kvs], 2 * TILE);
+            tma_load_2d(k, &tm, &kv_full[kvs], p.E + h * FD, b * p.S + j * FT);
+            tma_load_2d(k + TILE, &tm, &kv_full[kvs], 2 * p.E + h * FD, b * p.S + j * FT);
+            if (++kvs == FWD_KV_STAGES) {
+              kvs = 0;
+              kvph ^= 1u;
+            }
           }
         }
-        if (!ok) break;
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t id_s = make_idesc(1, 1, 1, false, false, 128, 128);
       const uint32_t id_o = make_idesc(1, 1, 1, false, true, 128, 64);
-      int it = 0, kvs = 0, sb = 0;
-      uint32_t kvph = 0, sph = 0, pph = 0, oph = 0;
+      int kvs = 0;
+      uint32_t kvph = 0;
+      // Per-stream MMA state (scalars, not arrays indexed by the stream, so
+      // it stays in registers).
+      struct St {
+        uint32_t sph, pph, oph;
+        int prev;  // K/V stage of the stream's previous tile
+      };
+      St st0{0, 0, 0, 0}, st1{0, 0, 0, 0};
       bool ok = true;
-      for (int item = blockIdx.x; item < items && ok; item += gridDim.x, ++it) {
-        const int qs = it & 1;
-        if (!mbar_wait(&q_full[qs], (it >> 1) & 1, p.err)) break;
-        const uint32_t qa = smem_u32(sQ + qs * TILE);
-        int prev = 0;
-        for (int j = 0; j <= nt; ++j) {
-          if (j < nt) {
-            if (!mbar_wait(&kv_full[kvs], kvph, p.err) || !mbar_wait(&s_empty[sb], sph ^ 1u, p.err)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t ka = smem_u32(sKV + kvs * 2 * TILE);
+      // Tile j's S for stream t, then the stream's previous tile's PV.
+      auto step = [&](int r, int j, int t, St& st) {
+        if (item_of(r, t) >= items) return true;
+        const uint32_t tS = tbase + (uint32_t)(t * 128), tO = tbase + 256u + (uint32_t)(t * 64);
+        if (j < nt) {
+          if (j == 0 && !mbar_wait(&q_full[t], r & 1, p.err)) return false;
+          if (!mbar_wait(&kv_full[kvs], kvph, p.err) || !mbar_wait(&s_empty[t], st.sph ^ 1u, p.err)) return false;
+          st.sph ^= 1u;
+          tc_fence_after();
+          const uint32_t qa = smem_u32(sQ + t * TILE), ka = smem_u32(sKV + kvs * 2 * TILE);
 #pragma unroll
-            for (int k = 0; k < FD / 16; ++k)
-              mma_f16(tbase + (uint32_t)(sb * 128), make_sw128_desc(qa + k * 32, 16, 1024),
-                      make_sw128_desc(ka + k * 32, 16, 1024), id_s, k ? 1u : 0u);
-            mma_commit(&s_full[sb]);
-            if (j == nt - 1) mma_commit(&q_empty[qs]);
+          for (int k = 0; k < FD / 16; ++k)
+            mma_f16(tS, make_sw128_desc(qa + k * 32, 16, 1024), make_sw128_desc(ka + k * 32, 16, 1024), id_s,
+                    k ? 1u : 0u);
+          mma_commit(&s_full[t]);
+          if (j == nt - 1) mma_commit(&q_empty[t]);
+        }
+        if (j > 0) {
+          if (j == 1) {
+            if (!mbar_wait(&o_empty[t], st.oph ^ 1u, p.err)) return false;
+            st.oph ^= 1u;
           }
-          if (j > 0) {
-            if (j == 1) {
-              if (!mbar_wait(o_empty, oph ^ 1u, p.err)) { ok = false; break; }
-              oph ^= 1u;
-            }
-            if (!mbar_wait(p_full, pph, p.err)) { ok = false; break; }
-            pph ^= 1u;
-            tc_fence_after();
-            const uint32_t va = smem_u32(sKV + prev * 2 * TILE + TILE);
-            const uint32_t pa = smem_u32(sP);
+          if (!mbar_wait(&p_full[t], st.pph, p.err)) return false;
+          st.pph ^= 1u;
+          tc_fence_after();
+          const uint32_t va = smem_u32(sKV + st.prev * 2 * TILE + TILE);
+          const uint32_t pa = smem_u32(sP + t * 2 * TILE);
 #pragma unroll
-            for (int k = 0; k < FT / 16; ++k)
-              mma_f16(tbase + 256, make_sw128_desc(pa + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024),
-                      make_sw128_desc(va + k * 2048, 16384, 1024), id_o, (j > 1 || k > 0) ? 1u : 0u);
-            mma_commit(&kv_empty[prev]);
-            mma_commit(pv_done);
-          }
-          if (j < nt) {
-            prev = kvs;
-            if (++kvs == KV_STAGES) {
-              kvs = 0;
-              kvph ^= 1u;
-            }
-            if (++sb == 2) {
-              sb = 0;
-              sph ^= 1u;
-            }
+          for (int k = 0; k < FT / 16; ++k)
+            mma_f16(tO, make_sw128_desc(pa + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024),
+                    make_sw128_desc(va + k * 2048, 16384, 1024), id_o, (j > 1 || k > 0) ? 1u : 0u);
+          mma_commit(&kv_empty[st.prev]);
+          mma_commit(&pv_done[t]);
+        }
+        if (j < nt) {
+          st.prev = kvs;
+          if (++kvs == FWD_KV_STAGES) {
+            kvs = 0;
+            kvph ^= 1u;
           }
         }
-      }
+        return true;
+      };
+      for (int r = 0; ok && item_of(r, 0) < items; ++r)
+        for (int j = 0; ok && j <= nt; ++j) ok = step(r, j, 0, st0) && step(r, j, 1, st1);
     }
   } else {
-    // Softmax warps: warp w reads TMEM lanes 32*(w%4) .. +31 (row = query).
+    // Softmax warps: stream t = (warp - 2) / 4; warp w reads TMEM lanes
+    // 32 * (w % 4) .. + 31 (row = query).
+    const int t = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    int sb = 0;
+    const uint32_t tS = tbase + lane_off + (uint32_t)(t * 128), tO = tbase + lane_off + 256u + (uint32_t)(t * 64);
+    uint8_t* prow = sP + t * 2 * TILE;
     uint32_t sph = 0, pvph = 0;
-    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+    for (int r = 0;; ++r) {
+      const int item = item_of(r, t);
+      if (item >= items) break;
       const int qt = item % nt, bh = item / nt, h = bh % p.H, b = bh / p.H;
       float m = -INFINITY, l = 0.f;
       bool ok = true;
       for (int j = 0; j < nt; ++j) {
-        const int tslot = (((item - (int)blockIdx.x) / (int)gridDim.x) * nt + j) * 8;
-        ATTN_TRACE(threadIdx.x == 64, tslot + 0);
-        if (!warp_wait(&s_full[sb], sph, p.err)) { ok = false; break; }
-        ATTN_TRACE(threadIdx.x == 64, tslot + 1);
+        if (!warp_wait(&s_full[t], sph, p.err)) { ok = false; break; }
+        sph ^= 1u;
         tc_fence_after();
-        uint32_t sr[4][32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(tbase + lane_off + (uint32_t)(sb * 128 + c * 32), sr[c]);
-        tmem_ld_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_empty[sb]);
-        ATTN_TRACE(threadIdx.x == 64, tslot + 2);
-        if (++sb == 2) {
-          sb = 0;
-          sph ^= 1u;
-        }
-        // Row max and (below) row sum as 8 independent partials: one thread
-        // owns the row, so a single 128-long dependency chain would leave the
-        // warp waiting on each step's latency.
+        // Pass 1: the row max over all 128 scores (8 independent partials:
+        // one thread owns a row).
         float mp[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) mp[k] = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int h2 = 0; h2 < 2; ++h2) {  // two halves of 64 columns
+          uint32_t sr[2][32];
+          tmem_ld32(tS + (uint32_t)(h2 * 64), sr[0]);
+          tmem_ld32(tS + (uint32_t)(h2 * 64 + 32), sr[1]);
+          tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(sr[c][i]));
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(sr[c][i]));
+        }
         float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
         mx *= p.c;
         const bool need = mx > m + 8.f;  // lazy rescale: keep the old reference max while it is within 2^8
         const float m_new = need ? mx : m;
         const float alpha = need ? hw_exp2(m - m_new) : 1.f;
-        // Exponentials first, into the S registers: this MUFU-heavy part
-        // overlaps the previous tile's PV product on the tensor cores; only
-        // the P write and the O rescale wait for that product.
-        float sp8[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) sp8[k] = 0.f;
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float e = hw_exp2(fmaf(__uint_as_float(sr[c][i]), p.c, -m_new));
-            sp8[i & 7] += e;
-            sr[c][i] = __float_as_uint(e);
-          }
-        ATTN_TRACE(threadIdx.x == 64, tslot + 3);
         if (j > 0) {
-          // PV of the previous tile must be done before O is rescaled or P rewritten.
-          if (!warp_wait(pv_done, pvph, p.err)) { ok = false; break; }
-          ATTN_TRACE(threadIdx.x == 64, tslot + 4);
+          // The previous tile's PV must be done before O is rescaled or P
+          // rewritten (it was queued right behind this tile's S).
+          if (!warp_wait(&pv_done[t], pvph, p.err)) { ok = false; break; }
           pvph ^= 1u;
           tc_fence_after();
           if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
               uint32_t o[32];
-              const uint32_t ta = tbase + lane_off + 256u + (uint32_t)(c * 32);
-              tmem_ld32(ta, o);
+              tmem_ld32(tO + (uint32_t)(c * 32), o);
               tmem_ld_wait();
 #pragma unroll
               for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-              tmem_st32(ta, o);
+              tmem_st32(tO + (uint32_t)(c * 32), o);
             }
             tmem_st_wait();
           }
         }
-        ATTN_TRACE(threadIdx.x == 64, tslot + 5);
+        // Pass 2: the scores again, 32 at a time, into exponentials written
+        // straight to P as bf16 (few live registers: a 320-thread block
+        // gives a thread 168); the row sum uses the fp32 values.
+        float sp8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) sp8[k] = 0.f;
+#pragma unroll 1  // one chunk's scores live at a time (unrolled, ptxas overlaps chunks and spills)
+        for (int c = 0; c < 4; ++c) {
+          uint32_t sc[32];
+          tmem_ld32(tS + (uint32_t)(c * 32), sc);
+          tmem_ld_wait();
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const float e0 = hw_exp2(fmaf(__uint_as_float(sc[i]), p.c, -m_new));
+            const float e1 = hw_exp2(fmaf(__uint_as_float(sc[i + 1]), p.c, -m_new));
+            sp8[i & 7] += e0;
+            sp8[(i + 1) & 7] += e1;
+            pk[i >> 1] = pack2(e0, e1);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(prow + sw_off(row, c * 4 + q)) =
+                make_uint4(pk[q * 4], pk[q * 4 + 1], pk[q * 4 + 2], pk[q * 4 + 3]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty[t]);
         l = l * alpha + (((sp8[0] + sp8[1]) + (sp8[2] + sp8[3])) + ((sp8[4] + sp8[5]) + (sp8[6] + sp8[7])));
         m = m_new;
-        uint8_t* prow = sP;
-#pragma unroll
-        for (int ch = 0; ch < 16; ++ch) {
-          const uint32_t* e = &sr[ch >> 2][(ch & 3) * 8];
-          uint4 v;
-          v.x = pack2(__uint_as_float(e[0]), __uint_as_float(e[1]));
-          v.y = pack2(__uint_as_float(e[2]), __uint_as_float(e[3]));
-          v.z = pack2(__uint_as_float(e[4]), __uint_as_float(e[5]));
-          v.w = pack2(__uint_as_float(e[6]), __uint_as_float(e[7]));
-          *reinterpret_cast<uint4*>(prow + sw_off(row, ch)) = v;
-        }
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(p_full);
-        ATTN_TRACE(threadIdx.x == 64, tslot + 6);
+        if (lane == 0) mbar_arrive(&p_full[t]);
       }
       if (!ok) break;
-      if (!warp_wait(pv_done, pvph, p.err)) break;
+      if (!warp_wait(&pv_done[t], pvph, p.err)) break;
       pvph ^= 1u;
       tc_fence_after();
-      uint32_t o0[32], o1[32];
-      tmem_ld32(tbase + lane_off + 256u, o0);
-      tmem_ld32(tbase + lane_off + 288u, o1);
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(o_empty);
+      // O row in two 32-column halves: normalise and store each (a thread
+      // writes its row's 128 bytes as eight 16-byte stores).
       const float inv = 1.f / l;
       const int64_t grow = (int64_t)b * p.S + (int64_t)qt * FT + row;
       uint4* dst = reinterpret_cast<uint4*>(p.out + grow * p.E + h * FD);
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint32_t* src = c < 4 ? &o0[c * 8] : &o1[(c - 4) * 8];
-        uint4 v;
-        v.x = pack2(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
-        v.y = pack2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
-        v.z = pack2(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
-        v.w = pack2(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
-        dst[c] = v;
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t o[32];
+        tmem_ld32(tO + (uint32_t)(hf * 32), o);
+        tmem_ld_wait();
+        if (hf == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&o_empty[t]);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t* src = &o[c * 8];
+          uint4 v;
+          v.x = pack2(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
+          v.y = pack2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
+          v.z = pack2(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
+          v.w = pack2(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
+          dst[hf * 4 + c] = v;
+        }
       }
       p.lse[((int64_t)b * p.H + h) * p.S + (int64_t)qt * FT + row] = m + log2f(l);
     }
@@ -765,7 +787,7 @@ void flash_attention_fwd(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* ls
   }
   const int items = B * H * (S / FT);
   int grid = std::min(items, max_ctas > 0 ? max_ctas : tmap::sm_count());
-  launch_pdl(flash_fwd_kernel, dim3(grid), dim3(192), FWD_SMEM, s, tm, p);
+  launch_pdl(flash_fwd_kernel, dim3(grid), dim3(FWD_THREADS), FWD_SMEM, s, tm, p);
   DLVK_POST_LAUNCH();
 }
 
