@@ -49,7 +49,11 @@ def main():
                     help="256 x 512 pair tile: 0 never, 1 when the tiling model picks it, 2 whenever it applies")
     ap.add_argument("--compare-single", action="store_true",
                     help="also time the single-CTA kernel (CTA-pair variant switched off)")
+    ap.add_argument("--fp32", action="store_true",
+                    help="fp32 operands: ours 3xTF32 and 1xTF32 against cuBLAS TF32 and cuBLAS fp32")
     args = ap.parse_args()
+    if args.fp32:
+        return fp32_main(args)
     C = _ext.C()
     C.gemm_set_wide(args.wide)
     shapes = DEFAULT
@@ -95,6 +99,46 @@ def main():
             ref = a.float() @ b.float()
             C.gemm(a, b, out=out, force_path=1)
             rec["max_rel_err"] = float((out.float() - ref).abs().max() / ref.abs().max())
+        print(json.dumps(rec), flush=True)
+
+
+def fp32_main(args):
+    """fp32 GEMMs: the tcgen05 kind::tf32 path (three passes with the 3xTF32
+    split, and one pass) against cuBLAS with TF32 allowed and with full fp32;
+    error against an fp64 product of the same operands."""
+    C = _ext.C()
+    shapes = [(8192, 4096, 4096, "k", "mn"), (4096, 4096, 4096, "k", "mn"), (1024, 4096, 8192, "mn", "mn")]
+    if args.shapes:
+        shapes = [tuple(int(v) if i < 3 else v for i, v in enumerate(s.split(","))) for s in args.shapes]
+    peak = measured_peaks()["bf16_tflops"]
+    old_mode = C.fp32_gemm_mode()
+    for (M, N, K, am, bm) in shapes:
+        a = torch.randn(M, K, device="cuda") if am == "k" else torch.randn(K, M, device="cuda").t()
+        b = torch.randn(K, N, device="cuda") if bm == "mn" else torch.randn(N, K, device="cuda").t()
+        out = torch.empty(M, N, device="cuda")
+        flops = 2.0 * M * N * K
+        ref = a.double() @ b.double()
+        rec = {"M": M, "N": N, "K": K, "a": am, "b": bm}
+        for name, mode in (("ours_3xtf32", 3), ("ours_tf32", 1)):
+            C.set_fp32_gemm_mode(mode)
+            t = time_fn(lambda: C.gemm(a, b, out=out, force_path=1), iters=args.iters)
+            rec[name + "_ms"] = round(t, 4)
+            rec[name + "_tflops"] = round(flops / t / 1e9, 1)
+            rec[name + "_rel_err"] = float((out.double() - ref).norm() / ref.norm())
+        C.set_fp32_gemm_mode(old_mode)
+        for name, tf in (("cublas_tf32", True), ("cublas_fp32", False)):
+            prev = torch.backends.cuda.matmul.allow_tf32
+            torch.backends.cuda.matmul.allow_tf32 = tf
+            try:
+                t = time_fn(lambda: torch.matmul(a, b, out=out), iters=args.iters)
+                rec[name + "_ms"] = round(t, 4)
+                rec[name + "_tflops"] = round(flops / t / 1e9, 1)
+                rec[name + "_rel_err"] = float((out.double() - ref).norm() / ref.norm())
+            finally:
+                torch.backends.cuda.matmul.allow_tf32 = prev
+        rec["ours_3xtf32_vs_cublas_fp32"] = round(rec["cublas_fp32_ms"] / rec["ours_3xtf32_ms"], 3)
+        rec["ours_tf32_vs_cublas_tf32"] = round(rec["cublas_tf32_ms"] / rec["ours_tf32_ms"], 3)
+        rec["bf16_peak_tflops_measured"] = peak
         print(json.dumps(rec), flush=True)
 
 

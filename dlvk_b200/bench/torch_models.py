@@ -48,7 +48,7 @@ class TorchTransformer(nn.Module):
 
 
 def wide_mlp():
-    layers = [nn.Linear(1024, 4096), nn.BatchNorm1d(4096), nn.ReLU(), nn.Dropout(0.1)]
+    layers = [nn.Linear(1024, 4096)]
     for _ in range(4):
         layers += [nn.Linear(4096, 4096), nn.BatchNorm1d(4096), nn.ReLU(), nn.Dropout(0.1)]
     layers += [nn.Linear(4096, 1000)]
@@ -71,7 +71,9 @@ def build_torch(name: str, local: int, rank: int):
     base = "cnn" if name.startswith("cnn") else name
     model = {"transformer": TorchTransformer, "wide_mlp": wide_mlp, "cnn": cnn, "mlp": mlp}[base]().to(dev)
     if zc.optimizer == "adam":
-        opt = torch.optim.Adam(model.parameters(), lr=1e-3, fused=True)
+        # capturable: the step counter stays on the device, so the whole
+        # training step can be captured into a CUDA graph
+        opt = torch.optim.Adam(model.parameters(), lr=1e-3, fused=True, capturable=True)
     else:
         opt = torch.optim.SGD(model.parameters(), lr=0.01, momentum=0.9, foreach=True)
     x, y = zoo.synthetic_batch(base, zc.batch, seed=1000 + rank, seq_len=zc.seq_len or 512)

@@ -4,6 +4,8 @@
 // the kernel supports them, and allocates outputs through PyTorch's caching
 // allocator (so the ops are CUDA-graph capturable).
 #include <ATen/ATen.h>
+#include <cstdlib>
+#include <string>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
@@ -221,6 +223,92 @@ std::vector<at::Tensor> pointwise_loss_op(const at::Tensor& p, const at::Tensor&
 // C = act(alpha * A @ B + beta * C + bias + residual).  A: [M,K], [b,M,K] or
 // [b,b2,M,K] (any strides; one unit stride per operand for the tensor-core
 // path); B likewise [.., K, N].  Transposes and head splits are views.
+// fp32 GEMMs on the tensor cores: DLVK_FP32_GEMM = 3xtf32 (default: the
+// product split into three TF32 products, error ~1e-6 relative, as fp32
+// SIMT), tf32 (one TF32 product, ~1e-3 relative) or simt (CUDA cores
+// only).  GEMMs below kTf32MinMacs multiply-adds stay on the SIMT kernel.
+constexpr double kTf32MinMacs = 67108864.0;  // 2^26
+
+namespace {
+int& fp32_mode_slot() {
+  static int mode = [] {
+    const char* e = std::getenv("DLVK_FP32_GEMM");
+    if (e == nullptr) return 3;
+    const std::string v(e);
+    return v == "simt" ? 0 : (v == "tf32" ? 1 : 3);
+  }();
+  return mode;
+}
+}  // namespace
+
+int fp32_gemm_mode() { return fp32_mode_slot(); }
+void set_fp32_gemm_mode(int mode) {
+  TORCH_CHECK(mode == 0 || mode == 1 || mode == 3, "dlvk: fp32 GEMM mode is 0 (simt), 1 (tf32) or 3 (3xtf32)");
+  fp32_mode_slot() = mode;
+}
+
+bool gemm_tf32_ok(const at::Tensor& A, const at::Tensor& B) {
+  if (A.scalar_type() != at::kFloat || B.scalar_type() != at::kFloat) return false;
+  if (A.dim() != B.dim() || A.dim() < 2 || A.dim() > 4) return false;
+  GemmArgs a = fill_args(A, B, A);
+  return gemm_tf32_tc_supported(a);
+}
+
+namespace {
+// hi / lo halves of an fp32 operand with the operand's own strides (a dense
+// view such as a transpose keeps its major-ness); other views are split
+// from a contiguous copy.
+std::pair<at::Tensor, at::Tensor> split_tf32(const at::Tensor& X) {
+  at::Tensor src = X.is_non_overlapping_and_dense() ? X : X.contiguous();
+  at::Tensor hi = at::empty_strided(src.sizes(), src.strides(), src.options());
+  at::Tensor lo = at::empty_strided(src.sizes(), src.strides(), src.options());
+  tf32_split(src.data_ptr<float>(), hi.data_ptr<float>(), lo.data_ptr<float>(), src.numel(), stream());
+  return {hi, lo};
+}
+
+void run_tf32(const GemmArgs& a, int max_ctas, const at::Tensor& like) {
+  const int64_t wsf = gemm_tc_workspace_floats(a, max_ctas, DType::F32, true);
+  at::Tensor ws = wsf > 0 ? at::empty({wsf}, like.options().dtype(at::kFloat)) : at::Tensor();
+  gemm_tf32_tc(DType::F32, a, stream(), device_error_word(), max_ctas, wsf > 0 ? ws.data_ptr<float>() : nullptr, wsf);
+}
+}  // namespace
+
+// C (fp32) = epilogue(alpha * A B + beta * C) with fp32 A, B on the tensor
+// cores.  three_pass: C = alpha Alo Bhi + beta C; C += alpha Ahi Blo;
+// C = epilogue(alpha Ahi Bhi + C) -- small terms first, the bias /
+// activation / residual / mask only on the last pass.
+void gemm_tf32_op(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const GemmArgs& args, bool three_pass,
+                  int max_ctas) {
+  if (!three_pass) {
+    run_tf32(args, max_ctas, C);
+    return;
+  }
+  auto sa = split_tf32(A);
+  auto sb = split_tf32(B);
+  GemmArgs lin = fill_args(sa.second, sb.first, C);
+  lin.alpha = args.alpha;
+  lin.beta = args.beta;
+  run_tf32(lin, max_ctas, C);
+  lin = fill_args(sa.first, sb.second, C);
+  lin.alpha = args.alpha;
+  lin.beta = 1.f;
+  run_tf32(lin, max_ctas, C);
+  GemmArgs last = args;
+  const GemmArgs hh = fill_args(sa.first, sb.first, C);
+  last.A = hh.A;
+  last.B = hh.B;
+  last.sam = hh.sam;
+  last.sak = hh.sak;
+  last.sbk = hh.sbk;
+  last.sbn = hh.sbn;
+  last.batch_stride_a = hh.batch_stride_a;
+  last.batch_stride_b = hh.batch_stride_b;
+  last.batch2_stride_a = hh.batch2_stride_a;
+  last.batch2_stride_b = hh.batch2_stride_b;
+  last.beta = 1.f;
+  run_tf32(last, max_ctas, C);
+}
+
 GemmArgs fill_args(const at::Tensor& A, const at::Tensor& B, const at::Tensor& C) {
   GemmArgs a;
   const int nd = A.dim();
@@ -332,7 +420,13 @@ at::Tensor gemm_op(const at::Tensor& A, const at::Tensor& B, c10::optional<at::T
       a.colsum = cs_part.data_ptr<float>();
     }
   }
-  if (use_tc) {
+  const int fmode = fp32_gemm_mode();
+  const bool tf32_path = A.scalar_type() == at::kFloat && C.scalar_type() == at::kFloat && fmode != 0 &&
+                         force_path != 2 && gemm_tf32_tc_supported(a) &&
+                         (force_path == 1 || (double)M * N * K * a.batch * a.batch2 >= kTf32MinMacs);
+  if (tf32_path) {
+    gemm_tf32_op(A, B, C, a, fmode == 3, (int)max_ctas);
+  } else if (use_tc) {
     TORCH_CHECK(tc_ok, "dlvk.gemm: tensor-core path requested but not applicable to these operands");
     const int64_t wsf = gemm_tc_workspace_floats(a, (int)max_ctas, to_dtype(C));
     at::Tensor ws = wsf > 0 ? at::empty({wsf}, A.options().dtype(at::kFloat)) : at::Tensor();

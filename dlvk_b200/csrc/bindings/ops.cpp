@@ -37,6 +37,9 @@ void register_ops(py::module& m) {
         py::arg("relu_mask") = py::none(), py::arg("colsum_out") = py::none(), py::arg("colsum_scale") = 1.0,
         py::arg("colsum_accumulate") = false);
   m.def("gemm_tc_ok", &gemm_tc_ok);
+  m.def("gemm_tf32_ok", &gemm_tf32_ok);
+  m.def("set_fp32_gemm_mode", &set_fp32_gemm_mode);
+  m.def("fp32_gemm_mode", &fp32_gemm_mode);
   m.def("optim_advance", &optim_advance_op);
   m.def("optim_update", &optim_update_op, py::arg("kind"), py::arg("hyper"), py::arg("p"), py::arg("grad"),
         py::arg("m") = py::none(), py::arg("v") = py::none(), py::arg("p_bf16") = py::none(),

@@ -34,6 +34,11 @@ std::vector<at::Tensor> softmax_ce_op(const at::Tensor& logits, const at::Tensor
 at::Tensor sum_scalar_op(const at::Tensor& v, double scale);
 std::vector<at::Tensor> pointwise_loss_op(const at::Tensor& p, const at::Tensor& t, int64_t kind, double loss_scale, double grad_scale, bool want_grad);
 GemmArgs fill_args(const at::Tensor& A, const at::Tensor& B, const at::Tensor& C);
+int fp32_gemm_mode();
+void set_fp32_gemm_mode(int mode);
+bool gemm_tf32_ok(const at::Tensor& A, const at::Tensor& B);
+void gemm_tf32_op(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const GemmArgs& args, bool three_pass,
+                  int max_ctas);
 at::Tensor gemm_op(const at::Tensor& A, const at::Tensor& B, c10::optional<at::Tensor> bias, int64_t act, double alpha, double beta, c10::optional<at::Tensor> out, c10::optional<at::ScalarType> out_dtype, int64_t force_path, int64_t max_ctas, c10::optional<at::Tensor> residual, c10::optional<at::Tensor> relu_mask, c10::optional<at::Tensor> colsum_out, double colsum_scale, bool colsum_accumulate);
 bool gemm_tc_ok(const at::Tensor& A, const at::Tensor& B);
 void optim_advance_op(const at::Tensor& hyper);

@@ -89,7 +89,8 @@ bool gemm_tc_supported(const GemmArgs& a);
 // reduce kernel applies the epilogue.  With a null/small workspace the GEMM
 // runs unsplit.  An fp32 C with a linear epilogue (alpha, beta 0 or 1) needs
 // no workspace: the partials are added into C by TMA reduces.
-int64_t gemm_tc_workspace_floats(const GemmArgs& a, int max_ctas = 0, DType out_dt = DType::BF16);
+int64_t gemm_tc_workspace_floats(const GemmArgs& a, int max_ctas = 0, DType out_dt = DType::BF16,
+                                 bool tf32 = false);
 // CTA-pair (tcgen05 cta_group::2, 256 x 256 tiles) variant for unsplit bf16
 // GEMMs with M >= 256; on by default (DLVK_GEMM_PAIR=0 turns it off).
 bool gemm_tc_pair_enabled();
@@ -104,6 +105,16 @@ void gemm_tc_plan(DType out_dt, const GemmArgs& a, int max_ctas, int* bn, int* s
 bool gemm_tc_colsum_ok(DType out_dt, const GemmArgs& a);
 void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int max_ctas = 0,
              float* workspace = nullptr, int64_t workspace_floats = 0);
+// fp32 operands on the tensor cores (tcgen05 kind::tf32: each product uses
+// the operands' top 19 bits, fp32 accumulation), single-CTA tiles; A / B
+// K-major or M/N-major like gemm_tc, row strides multiples of 4 elements.
+bool gemm_tf32_tc_supported(const GemmArgs& a);
+void gemm_tf32_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int max_ctas = 0,
+                  float* workspace = nullptr, int64_t workspace_floats = 0);
+// Splits fp32 x into hi = x rounded to tf32 and lo = x - hi, so that
+// A B ~= Ahi Bhi + Ahi Blo + Alo Bhi with every product exact in tf32 up to
+// the lo terms' own rounding (relative error ~2^-21): the 3xTF32 scheme.
+void tf32_split(const float* x, float* hi, float* lo, int64_t n, cudaStream_t s);
 
 // ---- int8 ----------------------------------------------------------------------
 // q[r, :] = round(x[r, :] / s[r]), s[r] = max|x[r, :]| / 127 (symmetric, per row).

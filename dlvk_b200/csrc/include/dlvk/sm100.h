@@ -246,6 +246,21 @@ __device__ __forceinline__ uint64_t make_sw128_desc(uint32_t smem_addr, uint32_t
   return d;
 }
 
+// UMMA shared-memory descriptor for an M/N-major 32-bit (tf32) operand in the
+// 128-byte swizzle with 32-byte atoms (layout type 1; TMA
+// SWIZZLE_128B_ATOM_32B): 128-byte rows along M/N, 4-row swizzle atoms along
+// K `sbo_bytes` apart, 128-byte M/N chunks `lbo_bytes` apart.  This is the
+// only layout tcgen05 accepts for M/N-major tf32 operands.
+__device__ __forceinline__ uint64_t make_sw128b32_desc(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;  // version = 1 (sm100)
+  d |= (uint64_t)1u << 61;  // SWIZZLE_128B_BASE32B
+  return d;
+}
+
 // Instruction descriptor.  fmt codes: kind::f16 A/B 0=f16 1=bf16 (tf32 = 2
 // under kind::tf32); kind::i8 A/B 0=u8 1=s8.  D fmt 1 = f32, 2 = s32.
 __host__ __device__ constexpr uint32_t make_idesc(uint32_t d_fmt, uint32_t a_fmt, uint32_t b_fmt, bool a_mn_major,

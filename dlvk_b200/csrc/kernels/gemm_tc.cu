@@ -60,6 +60,7 @@ struct TcParams {
   int kb_per_split;
   int64_t split_stride;  // elements between split slices of the workspace
   int i8;                  // 1: int8 x int8 -> int32 (kind::i8), K-major operands
+  int tf32;                // 1: fp32 operands, tf32 math, fp32 accumulate (kind::tf32); single-CTA tiles
   const float* row_scale;  // int8 dequantisation: per-row (A) and per-column (B) scales
   const float* col_scale;
   float* colsum;           // per-32-row column sums of the output (staged fast path)
@@ -331,7 +332,12 @@ __global__ void __launch_bounds__(320, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_per_split = p.tiles_m * p.tiles_n * p.batch;
   const int num_tiles = tiles_per_split * p.splits;  // work units
-  const int bke = p.i8 ? 2 * BK : BK;  // elements per 128-byte k-block
+  // elements per 128-byte k-block: 64 bf16, 128 int8 or 32 fp32 (tf32)
+  const int bke = p.i8 ? 2 * BK : (p.tf32 ? BK / 2 : BK);
+  // M/N-major operands come as boxes of one 128-byte swizzle row along M/N
+  // (64 bf16 or 32 fp32) by bke rows along K.
+  const int mn_box = p.tf32 ? 32 : 64;
+  const int mn_box_bytes = p.tf32 ? 4096 : 8192;
   const int num_kb = (p.K + bke - 1) / bke;
   // With PAIR the two CTAs of a cluster walk the same tiles; `rank` selects
   // the 128-row half of A / the BN/2-column half of B this CTA stages.
@@ -442,16 +448,14 @@ __global__ void __launch_bounds__(320, 1)
           if (!p.a_mn) {
             tma_load_4d(sA, &tmA, &full[stage], kb * bke, tm * BM, bi, bo);
           } else {
-#pragma unroll
-            for (int j = 0; j < BM / 64; ++j)
-              tma_load_4d(sA + j * 8192, &tmA, &full[stage], tm * BM + j * 64, kb * BK, bi, bo);
+            for (int j = 0; j < BM / mn_box; ++j)
+              tma_load_4d(sA + j * mn_box_bytes, &tmA, &full[stage], tm * BM + j * mn_box, kb * bke, bi, bo);
           }
           if (!p.b_mn) {
             tma_load_4d(sB, &tmB, &full[stage], kb * bke, tn * BN, bi, bo);
           } else {
-#pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              tma_load_4d(sB + j * 8192, &tmB, &full[stage], tn * BN + j * 64, kb * BK, bi, bo);
+            for (int j = 0; j < BN / mn_box; ++j)
+              tma_load_4d(sB + j * mn_box_bytes, &tmB, &full[stage], tn * BN + j * mn_box, kb * bke, bi, bo);
           }
           if (++stage == C::STAGES) {
             stage = 0;
@@ -521,7 +525,11 @@ __global__ void __launch_bounds__(320, 1)
       }
     } else if (lane == 0) {
       const uint32_t idesc = p.i8 ? make_idesc(2, 1, 1, false, false, BM, BN)
-                                  : make_idesc(1, 1, 1, p.a_mn != 0, p.b_mn != 0, BM, BN);
+                                  : (p.tf32 ? make_idesc(1, 2, 2, p.a_mn != 0, p.b_mn != 0, BM, BN)
+                                            : make_idesc(1, 1, 1, p.a_mn != 0, p.b_mn != 0, BM, BN));
+      // One MMA takes 32 bytes of K: a K-major operand advances 32 bytes per
+      // MMA, an M/N-major one K rows of 128 bytes (16 bf16 / 8 tf32 rows).
+      const uint32_t mn_step = p.tf32 ? 1024u : 2048u;
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -546,11 +554,15 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t bBase = aBase + C::A_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = p.a_mn ? make_sw128_desc(aBase + k * 2048, 8192, 1024)
+            // M/N-major tf32 operands use the 32-byte-atom swizzle (4-row atoms 512 bytes apart).
+            const uint64_t ad = p.a_mn ? (p.tf32 ? make_sw128b32_desc(aBase + k * mn_step, (uint32_t)mn_box_bytes, 512)
+                                                 : make_sw128_desc(aBase + k * mn_step, (uint32_t)mn_box_bytes, 1024))
                                        : make_sw128_desc(aBase + k * 32, 16, 1024);
-            const uint64_t bd = p.b_mn ? make_sw128_desc(bBase + k * 2048, 8192, 1024)
+            const uint64_t bd = p.b_mn ? (p.tf32 ? make_sw128b32_desc(bBase + k * mn_step, (uint32_t)mn_box_bytes, 512)
+                                                 : make_sw128_desc(bBase + k * mn_step, (uint32_t)mn_box_bytes, 1024))
                                        : make_sw128_desc(bBase + k * 32, 16, 1024);
             if (p.i8) mma_i8(d, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+            else if (p.tf32) mma_tf32(d, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
             else mma_f16(d, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           mma_commit(&empty[stage]);
@@ -798,19 +810,27 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 4-D bf16 tensor map: dims {d0 (contiguous), d1, inner batch, outer batch},
-// strides in elements, box {64, box1, 1, 1}, 128-byte swizzle, zero fill out
-// of bounds.
+// 4-D operand tensor map: dims {d0 (contiguous), d1, inner batch, outer
+// batch}, strides in elements, box {one 128-byte row, box1, 1, 1}, 128-byte
+// swizzle, zero fill out of bounds.
+// Operand element kinds of the tensor maps.
+enum class Elem { BF16, I8, F32 };
+
 CUtensorMap make_tmap(const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t d3, uint64_t s1, uint64_t s2,
-                      uint64_t s3, uint32_t box1, bool i8) {
+                      uint64_t s3, uint32_t box1, Elem el, bool mn_major = false) {
   CUtensorMap m;
   cuuint64_t dims[4] = {d0, d1, d2, d3};
-  const uint64_t esz = i8 ? 1 : 2;
+  const uint64_t esz = el == Elem::I8 ? 1 : (el == Elem::F32 ? 4 : 2);
   cuuint64_t strides[3] = {s1 * esz, s2 * esz, s3 * esz};
-  cuuint32_t box[4] = {i8 ? 128u : 64u, box1, 1, 1};
+  cuuint32_t box[4] = {(cuuint32_t)(128 / esz), box1, 1, 1};  // one 128-byte swizzle row
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = encode_fn()(&m, i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  const CUtensorMapDataType dt = el == Elem::I8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                                : (el == Elem::F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                                                   : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+  CUresult r = encode_fn()(&m, dt, 4, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           (el == Elem::F32 && mn_major) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                                         : CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw std::runtime_error("dlvk: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
   return m;
@@ -933,14 +953,14 @@ bool gemm_tc_wide_enabled() { return wide_flag() != 0; }
 // TMA reduce in L2 (plus a clear of C when beta = 0) instead of the workspace
 // round trip and the reduce launch.
 void choose_tiling(const GemmArgs& a, int sms, int& BN, int& splits, bool& pair, bool red = false,
-                   bool out_f32 = false) {
+                   bool out_f32 = false, bool single_cta = false) {
   const int64_t kbs = (a.K + BK - 1) / BK;
   const double sm_flops = 8.1e12;
   double best = 1e300;
   BN = 256;
   splits = 1;
   pair = false;
-  const bool pair_ok = gemm_tc_pair_enabled() && a.M >= 256 && sms >= 2;
+  const bool pair_ok = !single_cta && gemm_tc_pair_enabled() && a.M >= 256 && sms >= 2;
   struct Cand {
     bool pair;
     int bn;
@@ -1083,9 +1103,13 @@ CUtensorMap make_c_map(TcParams& p, int64_t M, int64_t N, bool reduce = false) {
 }
 }  // namespace
 
-void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int max_ctas, float* workspace,
-             int64_t workspace_floats) {
-  DLVK_CHECK(gemm_tc_supported(a), "gemm_tc: unsupported layout/alignment");
+namespace {
+// Shared host path of the bf16 and the tf32 GEMM.  TF32 runs on single-CTA
+// tiles (no CTA pairs): fp32 operands, 32-element k-blocks.
+void gemm_tc_impl(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int max_ctas, float* workspace,
+                  int64_t workspace_floats, bool tf32) {
+  const Elem el = tf32 ? Elem::F32 : Elem::BF16;
+  const int bke = tf32 ? BK / 2 : BK;
   if (a.M == 0 || a.N == 0) return;
   // The tensor-map encoder is a driver call and needs a current context on
   // this thread.  Threads that have only used the runtime through a "same
@@ -1105,7 +1129,7 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
   int BN = 256, splits = 1;
   bool pair = false;
   const bool red = split_red_ok(out_dt, a);
-  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits, pair, red, out_dt == DType::F32);
+  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits, pair, red, out_dt == DType::F32, tf32);
   if (a.colsum != nullptr) {
     DLVK_CHECK(gemm_tc_colsum_ok(out_dt, a), "gemm_tc: column sums need the staged fast-path layout");
     splits = 1;  // the sums are taken over final outputs
@@ -1119,20 +1143,20 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
   if (a_k) {
     const uint64_t d = (uint64_t)a.sam * (uint64_t)a.M;
     ta = make_tmap(a.A, a.K, a.M, a.batch2, a.batch, a.sam, pick(a.batch2, a.batch2_stride_a, d),
-                        pick(a.batch, a.batch_stride_a, d), BM, false);
+                        pick(a.batch, a.batch_stride_a, d), BM, el);
   } else {
     const uint64_t d = (uint64_t)a.sak * (uint64_t)a.K;
     ta = make_tmap(a.A, a.M, a.K, a.batch2, a.batch, a.sak, pick(a.batch2, a.batch2_stride_a, d),
-                        pick(a.batch, a.batch_stride_a, d), 64, false);
+                        pick(a.batch, a.batch_stride_a, d), (uint32_t)bke, el, true);
   }
   if (b_k) {
     const uint64_t d = (uint64_t)a.sbn * (uint64_t)a.N;
     tb = make_tmap(a.B, a.K, a.N, a.batch2, a.batch, a.sbn, pick(a.batch2, a.batch2_stride_b, d),
-                        pick(a.batch, a.batch_stride_b, d), pair ? 128 : BN, false);
+                        pick(a.batch, a.batch_stride_b, d), pair ? 128 : BN, el);
   } else {
     const uint64_t d = (uint64_t)a.sbk * (uint64_t)a.K;
     tb = make_tmap(a.B, a.N, a.K, a.batch2, a.batch, a.sbk, pick(a.batch2, a.batch2_stride_b, d),
-                        pick(a.batch, a.batch_stride_b, d), 64, false);
+                        pick(a.batch, a.batch_stride_b, d), (uint32_t)bke, el, true);
   }
   TcParams p{};
   p.M = (int)a.M;
@@ -1171,8 +1195,9 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
   p.act = a.act;
   p.err = err;
   p.colsum = a.colsum;
+  p.tf32 = tf32 ? 1 : 0;
   p.splits = splits;
-  p.kb_per_split = (int)(((a.K + BK - 1) / BK + splits - 1) / splits);
+  p.kb_per_split = (int)(((a.K + bke - 1) / bke + splits - 1) / splits);
   p.split_stride = 0;
   if (splits > 1 && red) {
     // Every split's epilogue adds alpha * partial into C with a TMA reduce;
@@ -1192,7 +1217,7 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
     p.beta = a.beta;
     splits = 1;
     p.splits = 1;
-    p.kb_per_split = (int)((a.K + BK - 1) / BK);
+    p.kb_per_split = (int)((a.K + bke - 1) / bke);
   }
   if (splits > 1) {
     // Partial accumulators go to the fp32 workspace; the reduce kernel
@@ -1228,6 +1253,64 @@ void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int
   else if (BN == 256) launch_tc<256>(ta, tb, tc, p, max_ctas, s);
   else launch_tc<128>(ta, tb, tc, p, max_ctas, s);
 }
+}  // namespace
+
+void gemm_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int max_ctas, float* workspace,
+             int64_t workspace_floats) {
+  DLVK_CHECK(gemm_tc_supported(a), "gemm_tc: unsupported layout/alignment");
+  gemm_tc_impl(out_dt, a, s, err, max_ctas, workspace, workspace_floats, false);
+}
+
+bool gemm_tf32_tc_supported(const GemmArgs& a) {
+  const bool a_k = (a.sak == 1), a_m = (a.sam == 1) && !a_k;
+  const bool b_k = (a.sbk == 1), b_n = (a.sbn == 1) && !b_k;
+  if (!(a_k || a_m) || !(b_k || b_n)) return false;
+  const int64_t lda = a_k ? a.sam : a.sak;
+  const int64_t ldb = b_k ? a.sbn : a.sbk;
+  if ((lda * 4) % 16 || (ldb * 4) % 16) return false;
+  if (a.batch > 1 && ((a.batch_stride_a * 4) % 16 || (a.batch_stride_b * 4) % 16)) return false;
+  if (a.batch2 > 1 && ((a.batch2_stride_a * 4) % 16 || (a.batch2_stride_b * 4) % 16)) return false;
+  if (a.batch * a.batch2 * ((a.M + 127) / 128) * ((a.N + 127) / 128) > (1LL << 31) - 1) return false;
+  if (!al16(a.A) || !al16(a.B)) return false;
+  if (a.M < 1 || a.N < 16 || a.K < 1) return false;
+  if (a.M > (1LL << 31) - 1 || a.N > (1LL << 31) - 1 || a.K > (1LL << 31) - 1) return false;
+  return true;
+}
+
+void gemm_tf32_tc(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int max_ctas, float* workspace,
+                  int64_t workspace_floats) {
+  DLVK_CHECK(gemm_tf32_tc_supported(a), "gemm_tf32_tc: unsupported layout/alignment");
+  gemm_tc_impl(out_dt, a, s, err, max_ctas, workspace, workspace_floats, true);
+}
+
+namespace {
+// hi = x rounded to tf32 (10 explicit mantissa bits; the low 13 bits zero),
+// lo = x - hi (exact in fp32).  Rounding is to nearest, ties away from zero,
+// done with integer arithmetic on the bit pattern; non-finite values pass
+// through in hi with lo = 0.
+__global__ void tf32_split_kernel(const float* __restrict__ x, float* __restrict__ hi, float* __restrict__ lo,
+                                  int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    const uint32_t u = __float_as_uint(v);
+    float h = v, l = 0.f;
+    if ((u & 0x7f800000u) != 0x7f800000u) {
+      const uint32_t r = (u + 0x1000u) & 0xffffe000u;  // add half an ulp of tf32, truncate
+      h = __uint_as_float(r);
+      l = v - h;
+    }
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+}  // namespace
+
+void tf32_split(const float* x, float* hi, float* lo, int64_t n, cudaStream_t s) {
+  if (n <= 0) return;
+  const int g = (int)std::min<int64_t>((n + 255) / 256, (int64_t)sm_count() * 8);
+  tf32_split_kernel<<<g, 256, 0, s>>>(x, hi, lo, n);
+  DLVK_POST_LAUNCH();
+}
 
 namespace {
 int& pair_flag() {
@@ -1254,11 +1337,11 @@ void gemm_tc_plan(DType out_dt, const GemmArgs& a, int max_ctas, int* bn, int* s
   *pair = (pr && max_ctas != 1) ? 1 : 0;
 }
 
-int64_t gemm_tc_workspace_floats(const GemmArgs& a, int max_ctas, DType out_dt) {
+int64_t gemm_tc_workspace_floats(const GemmArgs& a, int max_ctas, DType out_dt, bool tf32) {
   if (split_red_ok(out_dt, a) || a.colsum != nullptr) return 0;
   int BN = 256, splits = 1;
   bool pair = false;
-  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits, pair, false, out_dt == DType::F32);
+  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits, pair, false, out_dt == DType::F32, tf32);
   return splits > 1 ? (int64_t)splits * a.M * a.N * a.batch * a.batch2 : 0;
 }
 
@@ -1289,8 +1372,8 @@ void gemm_i8_tc(const int8_t* A, const int8_t* Bt, const float* row_scale, const
     }
   }
   const int BN = N >= 256 ? 256 : 128;
-  CUtensorMap ta = make_tmap(A, K, M, 1, 1, lda, lda * M, lda * M, BM, true);
-  CUtensorMap tb = make_tmap(Bt, K, N, 1, 1, ldb, ldb * N, ldb * N, BN, true);
+  CUtensorMap ta = make_tmap(A, K, M, 1, 1, lda, lda * M, lda * M, BM, Elem::I8);
+  CUtensorMap tb = make_tmap(Bt, K, N, 1, 1, ldb, ldb * N, ldb * N, BN, Elem::I8);
   TcParams p{};
   p.M = (int)M;
   p.N = (int)N;

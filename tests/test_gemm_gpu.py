@@ -31,7 +31,8 @@ def _check(out, ref, tol):
                                    (8192 // 4, 3072, 1024), (32, 128, 784), (129, 136, 72)])
 @pytest.mark.parametrize("a_t", [False, True])
 @pytest.mark.parametrize("b_t", [False, True])
-def test_gemm_tc_layouts(M, N, K, a_t, b_t):
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+def test_gemm_tc_layouts(M, N, K, a_t, b_t, out_dtype):
     C = _C()
     torch.manual_seed(0)
     dev = "cuda"
@@ -41,10 +42,78 @@ def test_gemm_tc_layouts(M, N, K, a_t, b_t):
     B = b.t().contiguous().t() if b_t else b  # K-major ([N,K] storage) when b_t
     if not C.gemm_tc_ok(A, B):
         pytest.skip("layout not eligible for the tensor-core path")
-    out = C.gemm(A, B, force_path=1)
+    out = C.gemm(A, B, force_path=1, out_dtype=out_dtype)
     torch.cuda.synchronize()
     assert C.read_device_error(True) == 0
-    _check(out, _ref(a, b), 2e-2)
+    # bf16 output: one rounding to 8 significant bits; fp32 output: only the
+    # fp32 accumulation order differs from the reference product
+    _check(out, _ref(a, b), 1e-2 if out_dtype == torch.bfloat16 else 1e-4)
+
+
+def _padded(rows, cols, transposed, dtype):
+    """A [rows, cols] operand whose row stride is padded to a multiple of 8
+    elements (16-byte aligned rows for TMA), stored row-major, or stored
+    transposed ([cols, rows(padded)]) and viewed back when `transposed`."""
+    if transposed:
+        st = torch.randn(cols, (rows + 7) // 8 * 8, device="cuda").to(dtype)
+        return st[:, :rows].t()
+    st = torch.randn(rows, (cols + 7) // 8 * 8, device="cuda").to(dtype)
+    return st[:, :cols]
+
+
+# Tile edges (128-row tiles, 128/256-column tiles, 64-deep k-blocks) +- 1.
+@pytest.mark.parametrize("M,N,K", [(127, 128, 64), (128, 129, 63), (129, 255, 65), (255, 256, 127),
+                                   (256, 257, 128), (257, 383, 129), (383, 384, 191), (385, 512, 257),
+                                   (1, 16, 1), (2, 17, 3)])
+@pytest.mark.parametrize("a_t", [False, True])
+def test_gemm_tc_tile_edges(M, N, K, a_t):
+    C = _C()
+    torch.manual_seed(M + N + K)
+    A = _padded(M, K, a_t, torch.bfloat16)
+    B = _padded(K, N, False, torch.bfloat16)
+    assert C.gemm_tc_ok(A, B)
+    out = C.gemm(A, B, out_dtype=torch.float32, force_path=1)
+    torch.cuda.synchronize()
+    assert C.read_device_error(True) == 0
+    _check(out, _ref(A, B), 1e-4)
+
+
+def _ref64(a, b):
+    return a.double() @ b.double()
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 384, 512), (300, 200, 100), (129, 136, 72), (1024, 1024, 4096),
+                                   (2048, 512, 1024)])
+@pytest.mark.parametrize("a_t", [False, True])
+@pytest.mark.parametrize("b_t", [False, True])
+def test_gemm_fp32_tensor_cores(M, N, K, a_t, b_t):
+    """fp32 operands on tcgen05 kind::tf32: 3xTF32 within 1e-5 of an fp64
+    product (fp32-class accuracy), one TF32 pass within 5e-3."""
+    C = _C()
+    torch.manual_seed(M * 7 + N + K)
+    A = _padded(M, K, a_t, torch.float32)
+    B = _padded(K, N, b_t, torch.float32)
+    assert C.gemm_tf32_ok(A, B)
+    ref = _ref64(A, B)
+    old = C.fp32_gemm_mode()
+    try:
+        for mode, tol in ((3, 1e-5), (1, 5e-3)):
+            C.set_fp32_gemm_mode(mode)
+            out = C.gemm(A, B, force_path=1)
+            torch.cuda.synchronize()
+            assert C.read_device_error(True) == 0
+            rel = ((out.double() - ref).norm() / ref.norm()).item()
+            assert rel < tol, (mode, rel)
+        # the full epilogue on the last 3xTF32 pass: alpha, beta, bias, ReLU
+        C.set_fp32_gemm_mode(3)
+        bias = torch.randn(N, device="cuda")
+        acc = torch.randn(M, N, device="cuda")
+        want = torch.relu(0.5 * ref + 1.0 * acc.double() + bias.double())
+        C.gemm(A, B, bias=bias, act=1, alpha=0.5, beta=1.0, out=acc, force_path=1)
+        rel = ((acc.double() - want).norm() / want.norm()).item()
+        assert rel < 1e-5, rel
+    finally:
+        C.set_fp32_gemm_mode(old)
 
 
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
