@@ -12,7 +12,13 @@ device (CUDA events around a CUDA graph of --iters steps, max over ranks):
   nccl   NCCL all-reduce followed by this framework's Adam kernel
 and reports bus bandwidth (2 (N-1)/N * bytes / t, the all-reduce convention)
 and the fused kernel's fraction of its roofline, max(bytes over NVLink per
-direction / 770 GB/s, local HBM bytes / measured HBM bandwidth), with
+direction / link bandwidth, local HBM bytes / measured HBM bandwidth).  The
+link bandwidth is measured first: every rank copies 1 GiB from its
+neighbour GPU at the same time (CUDA events, max over ranks), giving the
+per-direction peer-copy rate under load; --nvlink-gbs overrides it.  With
+NVLink multicast the two-shot sizes also time the NVLS form
+(multimem.ld_reduce / multimem.st), whose link bytes are G/N in and V out
+per rank for the reduce-scatter plus the multicast of V.  Byte counts:
   ll        NVLink 2 (N-1) * G;               HBM G + 2 (N-1) G + 24 n + V
   one-shot  NVLink (N-1) * G;                 HBM N*G + 24 n + V
   two-shot  NVLink (N-1)/N * (G + V);         HBM G + 24 n/N + V (pull),
@@ -37,9 +43,10 @@ def main():
     ap.add_argument("--min-kb", type=int, default=4)
     ap.add_argument("--max-mb", type=int, default=1024)
     ap.add_argument("--iters", type=int, default=10)
-    ap.add_argument("--nvlink-gbs", type=float, default=770.0)
+    ap.add_argument("--nvlink-gbs", type=float, default=0.0, help="0: measure the peer-copy rate")
     ap.add_argument("--pull-ctas", default="", help="comma list: also time the pull form at these grid sizes")
-    ap.add_argument("--algo", default=None, choices=["auto", "pull", "push"], help="two-shot form (DLVK_AR_ALGO)")
+    ap.add_argument("--algo", default=None, choices=["auto", "pull", "push", "nvls"],
+                    help="form (DLVK_AR_ALGO); auto: start-up calibration per size")
     ap.add_argument("--no-graph", dest="graph", action="store_false", help="time eager launches, not a CUDA graph")
     args = ap.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -54,6 +61,32 @@ def main():
 
     C = _ext.C()
     hbm = measured_peaks()["hbm_gbs"] * 1e9
+    link_gbs = args.nvlink_gbs
+    if link_gbs <= 0:
+        # every rank pulls 1 GiB from its neighbour at once (copy engines, NVLink)
+        peer = (local + 1) % torch.cuda.device_count()
+        src = torch.empty(1 << 28, dtype=torch.float32, device=f"cuda:{peer}")
+        dst = torch.empty(1 << 28, dtype=torch.float32, device=f"cuda:{local}")
+        for _ in range(3):
+            dst.copy_(src)
+        torch.cuda.synchronize(local)
+        torch.cuda.synchronize(peer)
+        dist.barrier()
+        s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(5):
+            dst.copy_(src)
+        e0.record()
+        torch.cuda.synchronize(local)
+        t = torch.tensor([s0.elapsed_time(e0) / 5 / 1e3], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        link_gbs = (1 << 30) / float(t.item()) / 1e9
+        del src, dst
+        torch.cuda.empty_cache()
+        if rank == 0:
+            print(json.dumps({"peer_copy_gbs_per_direction": round(link_gbs, 1), "bytes": 1 << 30,
+                              "method": "each rank copies 1 GiB from its neighbour GPU concurrently, "
+                                        "CUDA events, max over ranks"}), flush=True)
     dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float32
     nmax = args.max_mb * (1 << 20) // 4
     g = torch.Generator().manual_seed(rank)
@@ -111,7 +144,10 @@ def main():
 
         algo = fused.algorithm(0, n)
         tf = time_it(fused_step)
-        tpull = time_it(lambda: fused_step("pull")) if algo == "push" else None
+        tpull = time_it(lambda: fused_step("pull")) if algo in ("push", "nvls") else None
+        tnvls = None
+        if fused.nvls and algo == "pull" and n * 4 > fused.one_shot_bytes:
+            tnvls = time_it(lambda: fused_step("nvls"))
         toneshot = time_it(lambda: fused_step("one-shot")) if algo == "ll" else None
         tpull_ctas = {}
         if algo in ("push", "pull") and args.pull_ctas:
@@ -127,10 +163,13 @@ def main():
         elif algo == "one-shot":
             link = (world - 1) * gbytes
             local_b = world * gbytes + state + vbytes
+        elif algo == "nvls":  # switch reduces; each rank sends G/N... in total G out, V/N x N copies in
+            link = max(gbytes, (world - 1) / world * vbytes + gbytes / world)
+            local_b = gbytes + state / world + vbytes
         else:
             link = (world - 1) / world * (gbytes + vbytes)
             local_b = gbytes * (1 + (2 * (world - 1) / world if algo == "push" else 0)) + state / world + vbytes
-        roof = max(link / (args.nvlink_gbs * 1e9), local_b / hbm)
+        roof = max(link / (link_gbs * 1e9), local_b / hbm)
         bus = 2 * (world - 1) / world * gbytes
         if rank == 0:
             row = {"world": world, "bucket_bytes": gbytes, "param_dtype": args.dtype, "algo": algo,
@@ -140,8 +179,12 @@ def main():
                    "fused_roofline_us": round(roof * 1e6, 1),
                    "fused_frac_of_roofline": round(roof / tf, 3),
                    "speedup_vs_nccl_plus_adam": round(tn / tf, 3)}
+            row["link_gbs_per_direction"] = round(link_gbs, 1)
             if tpull is not None:
                 row["pull_us"] = round(tpull * 1e6, 1)
+            if tnvls is not None:
+                row["nvls_us"] = round(tnvls * 1e6, 1)
+                row["nvls_bus_gbs"] = round(bus / tnvls / 1e9, 1)
             if toneshot is not None:
                 row["pull_one_shot_us"] = round(toneshot * 1e6, 1)
             for c, t in tpull_ctas.items():
@@ -149,7 +192,8 @@ def main():
             print(json.dumps(row), flush=True)
     err = C.read_device_error(True)
     if rank == 0:
-        print(json.dumps({"device_error": int(err)}))
+        print(json.dumps({"device_error": int(err), "nvls": fused.nvls if fused.nvls else fused.nvls_reason,
+                          "calibration_us": (fused.calibration or {}).get("us")}))
     fused.close()
     dist.barrier()
     dist.destroy_process_group()

@@ -57,6 +57,42 @@ void fused_ar_op(std::shared_ptr<SymmetricBuffer> grads, std::shared_ptr<Symmetr
                             (int)ctas, stream());
 }
 
+// NVLS two-shot variant: `grads` and `values` carry NVLink-multicast
+// addresses (SymmetricBuffer views of multicast-bound memory).
+void fused_ar_nvls_op(std::shared_ptr<SymmetricBuffer> grads, std::shared_ptr<SymmetricBuffer> values,
+                      std::shared_ptr<SymmetricBuffer> flags, const at::Tensor& counters, int64_t bucket, int64_t start,
+                      int64_t end, const at::Tensor& master, c10::optional<at::Tensor> m, c10::optional<at::Tensor> v,
+                      const at::Tensor& hyper, int64_t kind, const at::Tensor& epoch, int64_t world, int64_t rank,
+                      bool values_are_master, int64_t value_code, int64_t ctas, double budget_s) {
+  c10::cuda::CUDAGuard g(master.device());
+  TORCH_CHECK(grads->multicast() != nullptr && values->multicast() != nullptr,
+              "NVLS all-reduce: the buffers have no multicast mapping");
+  FusedARArgs a;
+  a.world = (int)world;
+  a.rank = (int)rank;
+  a.peer_grads = const_cast<const void* const*>(grads->device_ptrs());
+  a.peer_values = values->device_ptrs();
+  a.peer_flags = reinterpret_cast<uint32_t* const*>(flags->device_ptrs());
+  a.my_flags = static_cast<uint32_t*>(flags->local());
+  a.cta_counter = reinterpret_cast<unsigned int*>(counters.data_ptr<int>()) + bucket;
+  a.start = start;
+  a.end = end;
+  a.bucket = (int)bucket;
+  a.master = master.data_ptr<float>();
+  a.m = m.has_value() ? m->data_ptr<float>() : nullptr;
+  a.v = v.has_value() ? v->data_ptr<float>() : nullptr;
+  a.hyper = reinterpret_cast<const OptimHyper*>(hyper.data_ptr());
+  a.kind = (int)kind;
+  a.scale = 1.f / (float)world;
+  a.epoch_ptr = epoch.data_ptr<int64_t>();
+  a.values_are_master = values_are_master ? 1 : 0;
+  a.err = device_error_word();
+  a.budget_ns = (uint64_t)(budget_s * 1e9);
+  a.mc_grads = grads->multicast();
+  a.mc_values = values->multicast();
+  fused_allreduce_optimizer_nvls(a, value_code == 0 ? DType::F32 : DType::BF16, (int)ctas, stream());
+}
+
 // Push two-shot variant: `recv` holds world-1 slots of recv_slot gradient
 // elements; `cflags` is the [PUSH_MAX_BUCKETS][PUSH_MAX_CHUNKS][world] table.
 void fused_ar_push_op(std::shared_ptr<SymmetricBuffer> grads, std::shared_ptr<SymmetricBuffer> values,
@@ -165,6 +201,9 @@ void register_comm(py::module& m) {
   auto c = m.def_submodule("comm", "NVLink peer-memory communication");
   py::class_<SymmetricBuffer, std::shared_ptr<SymmetricBuffer>>(c, "SymmetricBuffer")
       .def(py::init<int64_t, int>(), py::arg("bytes"), py::arg("device"))
+      .def(py::init<const std::vector<uint64_t>&, int, int64_t, int, uint64_t>(), py::arg("ptrs"), py::arg("rank"),
+           py::arg("bytes"), py::arg("device"), py::arg("multicast") = 0)
+      .def("multicast_ptr", [](const SymmetricBuffer& b) { return (int64_t)(uintptr_t)b.multicast(); })
       .def("handle", [](const SymmetricBuffer& b) { return py::bytes(b.handle()); })
       .def("open",
            [](SymmetricBuffer& b, const std::vector<py::bytes>& hs, int rank) {
@@ -188,6 +227,7 @@ void register_comm(py::module& m) {
   c.def("fused_allreduce_optimizer", &fused_ar_op);
   c.def("fused_allreduce_optimizer_push", &fused_ar_push_op);
   c.def("fused_allreduce_optimizer_ll", &fused_ar_ll_op);
+  c.def("fused_allreduce_optimizer_nvls", &fused_ar_nvls_op);
   c.attr("PUSH_MAX_BUCKETS") = PUSH_MAX_BUCKETS;
   c.attr("PUSH_MAX_CHUNKS") = PUSH_MAX_CHUNKS;
   c.def("p2p_allreduce", &p2p_allreduce_op);

@@ -50,6 +50,11 @@ struct FusedARArgs {
   const void* my_ll = nullptr;
   int64_t ll_off = 0;                       // element offset of this bucket inside a slot
   int64_t ll_cap = 0;                       // elements per slot
+  // NVLS two-shot (fused_allreduce_optimizer_nvls): NVLink-multicast
+  // addresses of the gradient and parameter buffers (the same flat layout as
+  // peer_grads / peer_values, every rank's memory bound to the object).
+  void* mc_grads = nullptr;
+  void* mc_values = nullptr;
 };
 
 // Chunk-flag table of the push two-shot kernel: [PUSH_MAX_BUCKETS]
@@ -80,11 +85,23 @@ void fused_allreduce_optimizer_ll(const FusedARArgs& a, DType value_dt, int ctas
 // recv_off, recv_slot, peer_cflags, my_cflags and cbucket must be set).
 void fused_allreduce_optimizer_push(const FusedARArgs& a, DType grad_dt, DType value_dt, cudaStream_t s);
 
+// NVLS two-shot: rank r's shard of the bucket is summed over all ranks by the
+// NVSwitch (multimem.ld_reduce on mc_grads, fp32 gradients), updated by the
+// optimizer on rank r, and the new parameters are written to every rank with
+// one multicast store each (multimem.st on mc_values).  Ready / done flags as
+// in fused_allreduce_optimizer.  Needs mc_grads and mc_values.
+void fused_allreduce_optimizer_nvls(const FusedARArgs& a, DType value_dt, int ctas, cudaStream_t s);
+
 // A device allocation that every rank of the node can address: cudaMalloc +
 // cudaIpcGetMemHandle here, cudaIpcOpenMemHandle of the peers' handles there.
 class SymmetricBuffer {
  public:
   SymmetricBuffer(int64_t bytes, int device);
+  // A non-owning view of memory another allocator made symmetric (for
+  // example PyTorch's symmetric memory): `ptrs[r]` is rank r's base address
+  // as mapped on this device, `multicast` the NVLink multicast address of
+  // the same buffer (0 if none).
+  SymmetricBuffer(const std::vector<uint64_t>& ptrs, int rank, int64_t bytes, int device, uint64_t multicast);
   ~SymmetricBuffer();
   SymmetricBuffer(const SymmetricBuffer&) = delete;
   SymmetricBuffer& operator=(const SymmetricBuffer&) = delete;
@@ -98,10 +115,13 @@ class SymmetricBuffer {
   void* const* device_ptrs() const { return dev_ptrs_; }
   const std::vector<void*>& host_ptrs() const { return ptrs_; }
   int device() const { return device_; }
+  void* multicast() const { return multicast_; }
 
  private:
   int64_t bytes_;
   int device_;
+  bool owned_ = true;
+  void* multicast_ = nullptr;
   void* local_ = nullptr;
   std::vector<void*> ptrs_;
   std::vector<bool> opened_;

@@ -256,6 +256,87 @@ void launch_fused(const FusedARArgs& a, int grid, cudaStream_t s) {
   }
 }
 
+// ---------------------------------------------------------------- NVLS
+// multimem operations on NVLink-multicast addresses: the NVSwitch reduces the
+// loads over every bound rank's memory and replicates the stores.
+__device__ __forceinline__ float4 multimem_ld_reduce_f32x4(const float* mc) {
+  float4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(mc)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void multimem_st_f32x4(float* mc, const float4& v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
+}
+// Four bf16 (8 bytes) stored as two 32-bit lanes: the store moves bits.
+__device__ __forceinline__ void multimem_st_bf16x4(__nv_bfloat16* mc, const float4& v) {
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+  asm volatile("multimem.st.relaxed.sys.global.v2.f32 [%0], {%1, %2};" ::"l"(mc),
+               "f"(__uint_as_float(*reinterpret_cast<const uint32_t*>(&lo))),
+               "f"(__uint_as_float(*reinterpret_cast<const uint32_t*>(&hi)))
+               : "memory");
+}
+// Orders this thread's accesses through one virtual alias of memory (the
+// unicast or the multicast mapping) against its accesses through the other.
+__device__ __forceinline__ void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
+
+template <typename TV, int U>
+__global__ void __launch_bounds__(128, 8) fused_nvls_ar_opt_kernel(FusedARArgs a) {
+  const uint32_t epoch = (uint32_t)(*a.epoch_ptr);
+  if (!ready_barrier(a, epoch)) return;
+  fence_proxy_alias();  // the peers' gradients were written through their unicast mappings
+  const OptimHyper h = *a.hyper;
+  const float gs = a.scale * h.grad_scale;
+  const int64_t n = a.end - a.start;
+  const int64_t shard = ((n + a.world - 1) / a.world + 63) / 64 * 64;
+  const int64_t lo = min(n, shard * a.rank), hi = min(n, lo + shard);
+  const int64_t base = a.start + lo;
+  const int64_t nvec = (hi - lo) / 4;
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const float* mg = reinterpret_cast<const float*>(a.mc_grads) + base;
+  float* mst = a.master + base;
+  float* mm = a.m ? a.m + base : nullptr;
+  float* vv = a.v ? a.v + base : nullptr;
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int64_t v0 = tid; v0 < nvec; v0 += stride * U) {
+    float4 g[U], w[U], m4[U], v4[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t vi = v0 + u * stride;
+      g[u] = vi < nvec ? multimem_ld_reduce_f32x4(mg + vi * 4) : z4;
+      w[u] = vi < nvec ? reinterpret_cast<const float4*>(mst)[vi] : z4;
+      m4[u] = (mm && vi < nvec) ? reinterpret_cast<const float4*>(mm)[vi] : z4;
+      v4[u] = (vv && vi < nvec) ? reinterpret_cast<const float4*>(vv)[vi] : z4;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t vi = v0 + u * stride;
+      if (vi >= nvec) continue;
+      opt_apply(a.kind, h, w[u].x, g[u].x * gs, m4[u].x, v4[u].x);
+      opt_apply(a.kind, h, w[u].y, g[u].y * gs, m4[u].y, v4[u].y);
+      opt_apply(a.kind, h, w[u].z, g[u].z * gs, m4[u].z, v4[u].z);
+      opt_apply(a.kind, h, w[u].w, g[u].w * gs, m4[u].w, v4[u].w);
+      if (mm) reinterpret_cast<float4*>(mm)[vi] = m4[u];
+      if (vv) reinterpret_cast<float4*>(vv)[vi] = v4[u];
+      if (a.values_are_master) {
+        // fp32 mode: the master is the compute copy and lives in the
+        // multicast buffer; one store reaches every rank (this one included).
+        multimem_st_f32x4(reinterpret_cast<float*>(a.mc_values) + base + vi * 4, w[u]);
+      } else {
+        reinterpret_cast<float4*>(mst)[vi] = w[u];
+        multimem_st_bf16x4(reinterpret_cast<__nv_bfloat16*>(a.mc_values) + base + vi * 4, w[u]);
+      }
+    }
+  }
+  fence_proxy_alias();  // peers will read the new parameters through their unicast mappings
+  done_barrier(a, epoch);
+}
+
 // Plain two-shot sum all-reduce of [start, end) of a symmetric buffer, in
 // place: reduce my shard over all ranks (rank order), store the sum into every
 // rank's buffer.  Same flag protocol as the fused kernel.
@@ -627,6 +708,18 @@ void fused_allreduce_optimizer_push(const FusedARArgs& a, DType grad_dt, DType v
   else if (grad_dt == DType::F32 && value_dt == DType::F32) launch_push<float, float>(a, grid, s);
   else if (grad_dt == DType::BF16 && value_dt == DType::BF16) launch_push<__nv_bfloat16, __nv_bfloat16>(a, grid, s);
   else throw std::runtime_error("push all-reduce: unsupported grad/value dtypes");
+  DLVK_POST_LAUNCH();
+}
+
+void fused_allreduce_optimizer_nvls(const FusedARArgs& a, DType value_dt, int ctas, cudaStream_t s) {
+  DLVK_CHECK(a.mc_grads != nullptr && a.mc_values != nullptr, "NVLS all-reduce: multicast addresses missing");
+  DLVK_CHECK(a.values_are_master == (value_dt == DType::F32 ? 1 : 0),
+             "NVLS all-reduce: fp32 values must be the master copy, bf16 values a mirror");
+  DLVK_CHECK((reinterpret_cast<uintptr_t>(a.mc_grads) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.mc_values) & 15) == 0,
+             "NVLS all-reduce: multicast addresses must be 16-byte aligned");
+  const int grid = std::max(1, ctas);
+  if (value_dt == DType::F32) fused_nvls_ar_opt_kernel<float, 2><<<grid, 128, 0, s>>>(a);
+  else fused_nvls_ar_opt_kernel<__nv_bfloat16, 2><<<grid, 128, 0, s>>>(a);
   DLVK_POST_LAUNCH();
 }
 

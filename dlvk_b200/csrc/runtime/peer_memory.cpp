@@ -23,11 +23,33 @@ SymmetricBuffer::SymmetricBuffer(int64_t bytes, int device) : bytes_(bytes), dev
   DLVK_CUDA_CHECK(cudaSetDevice(prev));
 }
 
+SymmetricBuffer::SymmetricBuffer(const std::vector<uint64_t>& ptrs, int rank, int64_t bytes, int device,
+                                 uint64_t multicast)
+    : bytes_(bytes), device_(device), owned_(false) {
+  DLVK_CHECK(rank >= 0 && rank < (int)ptrs.size(), "SymmetricBuffer: rank out of range");
+  multicast_ = reinterpret_cast<void*>(multicast);
+  local_ = reinterpret_cast<void*>(ptrs[rank]);
+  ptrs_.resize(ptrs.size());
+  for (size_t r = 0; r < ptrs.size(); ++r) ptrs_[r] = reinterpret_cast<void*>(ptrs[r]);
+  opened_.assign(ptrs.size(), false);
+  int prev = 0;
+  DLVK_CUDA_CHECK(cudaGetDevice(&prev));
+  DLVK_CUDA_CHECK(cudaSetDevice(device_));
+  DLVK_CUDA_CHECK(cudaMalloc(reinterpret_cast<void**>(&dev_ptrs_), sizeof(void*) * ptrs_.size()));
+  DLVK_CUDA_CHECK(cudaMemcpy(dev_ptrs_, ptrs_.data(), sizeof(void*) * ptrs_.size(), cudaMemcpyHostToDevice));
+  DLVK_CUDA_CHECK(cudaSetDevice(prev));
+}
+
 SymmetricBuffer::~SymmetricBuffer() {
   int prev = 0;
   if (cudaGetDevice(&prev) != cudaSuccess) return;
   cudaSetDevice(device_);
   cudaDeviceSynchronize();
+  if (!owned_) {  // the other allocator owns and unmaps the memory
+    if (dev_ptrs_) cudaFree(dev_ptrs_);
+    cudaSetDevice(prev);
+    return;
+  }
   for (size_t r = 0; r < ptrs_.size(); ++r)
     if (opened_[r] && ptrs_[r]) cudaIpcCloseMemHandle(ptrs_[r]);
   if (dev_ptrs_) cudaFree(dev_ptrs_);

@@ -55,6 +55,35 @@ def make_symmetric(nbytes: int, device: torch.device, group=None):
     return buf
 
 
+def make_symmetric_multicast(numel: int, dtype: torch.dtype, device: torch.device, group=None):
+    """Allocate `numel` elements through PyTorch's symmetric memory (which
+    binds every rank's allocation to one NVLink multicast object when the
+    node supports it) and wrap the per-rank and multicast addresses in a
+    non-owning SymmetricBuffer.  Returns (buffer, keep-alive objects) or
+    (None, reason) when symmetric memory or multicast is unavailable.
+    Collective."""
+    mc, reason = 0, "no NVLink multicast support on this node"
+    try:
+        import torch.distributed._symmetric_memory as symm_mem
+
+        t = symm_mem.empty(numel, dtype=dtype, device=device)
+        grp = group if group is not None else dist.group.WORLD
+        hdl = symm_mem.rendezvous(t, grp)
+        mc = int(getattr(hdl, "multicast_ptr", 0) or 0)
+        ptrs = [int(x) for x in hdl.buffer_ptrs]
+    except Exception as exc:  # noqa: BLE001 - any failure means: no NVLS here
+        mc, reason = 0, f"symmetric memory unavailable ({type(exc).__name__}: {str(exc)[:120]})"
+    # every rank votes (failures included) before any takes the multicast path
+    ok = torch.tensor([1 if mc else 0], dtype=torch.int32, device=device)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+    if not int(ok.item()):
+        return None, reason
+    t.zero_()
+    torch.cuda.synchronize(device)
+    buf = _ext.C().comm.SymmetricBuffer(ptrs, dist.get_rank(group), numel * t.element_size(), device.index, mc)
+    return buf, (t, hdl)
+
+
 class FusedAllReduceOptimizer:
     """Per-bucket fused gradient all-reduce + optimizer update.
 
@@ -100,14 +129,29 @@ class FusedAllReduceOptimizer:
         dev = store.device
         self.dev = dev
         n = store.numel
-        self.grad_buf = make_symmetric(n * 4, dev, group)
         self.bf16 = store.value is not store.master
-        if self.bf16:
-            self.value_buf = make_symmetric(n * 2, dev, group)
-            store.rebind(grad=self.grad_buf.tensor(0, n, 0), value=self.value_buf.tensor(1, n, 0))
-        else:
-            self.value_buf = make_symmetric(n * 4, dev, group)
-            store.rebind(grad=self.grad_buf.tensor(0, n, 0), master=self.value_buf.tensor(0, n, 0))
+        self.algo = algo or os.environ.get("DLVK_AR_ALGO", "auto")
+        if self.algo not in ("auto", "push", "pull", "nvls"):
+            raise ValueError(f"unknown all-reduce algorithm {self.algo!r}")
+        # NVLS: gradient and parameter buffers bound to NVLink multicast
+        # objects (PyTorch symmetric memory); otherwise cudaMalloc + IPC.
+        self.nvls = False
+        self.nvls_reason = "not requested"
+        self._keep = []
+        if world > 1 and self.algo in ("auto", "nvls") and os.environ.get("DLVK_AR_NVLS", "1") != "0":
+            g, kg = make_symmetric_multicast(n, torch.float32, dev, group)
+            v, kv = (make_symmetric_multicast(n, torch.bfloat16 if self.bf16 else torch.float32, dev, group)
+                     if g is not None else (None, kg))
+            if g is not None and v is not None:
+                self.grad_buf, self.value_buf, self._keep = g, v, [kg, kv]
+                self.nvls, self.nvls_reason = True, "multicast"
+            else:
+                self.nvls_reason = kv if g is not None else kg
+        if self.algo == "nvls" and not self.nvls:
+            raise RuntimeError(f"NVLS all-reduce requested but unavailable: {self.nvls_reason}")
+        if not self.nvls:
+            self.grad_buf = make_symmetric(n * 4, dev, group)
+            self.value_buf = make_symmetric(n * (2 if self.bf16 else 4), dev, group)
         self.flag_buf = make_symmetric(MAX_BUCKETS * 2 * world * 4, dev, group)
         self.counters = torch.zeros(MAX_BUCKETS, dtype=torch.int32, device=dev)
         self.epoch = torch.zeros(1, dtype=torch.int64, device=dev)
@@ -116,11 +160,9 @@ class FusedAllReduceOptimizer:
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
         self.ctas = ctas or int(os.environ.get("DLVK_AR_CTAS", str(6 * sms)))
         self.push_ctas = int(os.environ.get("DLVK_PUSH_CTAS", str(2 * sms)))
+        self.nvls_ctas = int(os.environ.get("DLVK_NVLS_CTAS", str(4 * sms)))
         self.st = optimizer.state(store)
         self._bucket_ids = {}
-        self.algo = algo or os.environ.get("DLVK_AR_ALGO", "auto")
-        if self.algo not in ("auto", "push", "pull"):
-            raise ValueError(f"unknown all-reduce algorithm {self.algo!r}")
         self._ll = {}  # (start, end) -> LL offset
         self._ll_used = 0
         self.ll = None
@@ -139,6 +181,17 @@ class FusedAllReduceOptimizer:
             self.recv = make_symmetric((world - 1) * self.recv_slot * 4, dev, group)
             self.cflags = make_symmetric(self.C.comm.PUSH_MAX_BUCKETS * self.C.comm.PUSH_MAX_CHUNKS * world * 4,
                                          dev, group)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group)
+        # Pick the form per bucket size from timings on this node (before
+        # the model's tensors move into the symmetric buffers).
+        self.calibration = None
+        if world > 1 and self.algo == "auto" and os.environ.get("DLVK_AR_CALIBRATE", "1") != "0":
+            self.calibration = self._calibrate()
+        if self.bf16:
+            store.rebind(grad=self.grad_buf.tensor(0, n, 0), value=self.value_buf.tensor(1, n, 0))
+        else:
+            store.rebind(grad=self.grad_buf.tensor(0, n, 0), master=self.value_buf.tensor(0, n, 0))
         torch.cuda.synchronize(dev)
         dist.barrier(group)
 
@@ -168,16 +221,78 @@ class FusedAllReduceOptimizer:
         return self._ll[key]
 
     def algorithm(self, start: int, end: int) -> str:
-        """The form the bucket [start, end) runs as: ll, one-shot, push or pull."""
-        if (end - start) * 4 <= self.one_shot_bytes or self.world == 1:
-            if self.world > 1 and self._ll_slot(start, end) is not None:
+        """The form the bucket [start, end) runs as: ll, one-shot, push, pull
+        or nvls.  With a start-up calibration the form measured fastest at
+        the nearest calibrated size is used (ll only while its buffer has
+        room)."""
+        n = end - start
+        if self.world == 1:
+            return "one-shot"
+        if self.calibration:
+            import math
+
+            best = min(self.calibration["best"], key=lambda e: abs(math.log(max(n, 1) / e[0])))[1]
+            if best == "ll":
+                return "ll" if self._ll_slot(start, end) is not None else "one-shot"
+            return best
+        if n * 4 <= self.one_shot_bytes:
+            if self._ll_slot(start, end) is not None:
                 return "ll"
             return "one-shot"
         if self.algo == "push":
             if self._push_slot(start, end) is not None:
                 return "push"
             raise RuntimeError("push all-reduce: receive buffer or flag table full")
+        if self.nvls and self.algo in ("auto", "nvls"):
+            return "nvls"
         return "pull"
+
+    def _calibrate(self) -> dict:
+        """Time every available form on bucket sizes from 256 KB to 64 MB
+        (gradients; the fresh symmetric buffers and scratch optimizer state,
+        so no model state is touched), max over ranks, and keep the fastest
+        per size.  Collective: every rank runs the same launches."""
+        n_all = self.store.numel
+        dev = self.dev
+        sizes = [s for s in (1 << 16, 1 << 18, 1 << 20, 1 << 22, 1 << 24) if s <= n_all] or [n_all // 64 * 64]
+        top = max(sizes)
+        master = torch.zeros(n_all, dtype=torch.float32, device=dev)
+        m = torch.zeros(top, dtype=torch.float32, device=dev) if self.st.m is not None else None
+        v = torch.zeros(top, dtype=torch.float32, device=dev) if self.st.v is not None else None
+        slot = MAX_BUCKETS - 1
+        table = []
+        for size in sizes:
+            forms = ["one-shot", "pull"] + (["nvls"] if self.nvls else [])
+            if self.ll is not None and size <= self.ll_cap:
+                forms.insert(0, "ll")
+            times = {}
+            for form in forms:
+                run = lambda: self._launch(form, 0, size, slot, master, m, v, None, ll_off=0)  # noqa: E731
+                for _ in range(2):
+                    self.begin_step()
+                    run()
+                evs = []
+                for _ in range(5):
+                    self.begin_step()
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record()
+                    run()
+                    b.record()
+                    evs.append((a, b))
+                torch.cuda.synchronize(dev)
+                t = sorted(x.elapsed_time(y) for x, y in evs)[2]
+                tt = torch.tensor([t], dtype=torch.float64, device=dev)
+                dist.all_reduce(tt, op=dist.ReduceOp.MAX, group=self.group)
+                times[form] = float(tt.item())
+            best = min(times, key=times.get)
+            table.append((size, best, {k: round(val * 1e3, 2) for k, val in times.items()}))
+        if self.C.read_device_error(True) != 0:
+            raise RuntimeError("all-reduce calibration: a peer wait timed out")
+        self.grad_buf.tensor(0, n_all, 0).zero_()
+        self.counters.zero_()
+        torch.cuda.synchronize(dev)
+        return {"best": [(sz, b) for sz, b, _ in table],
+                "us": {str(sz * 4): t for sz, _, t in table}}
 
     def begin_step(self) -> None:
         self.C.counter_add(self.epoch, 1)
@@ -185,9 +300,9 @@ class FusedAllReduceOptimizer:
     def reduce_update(self, start: int, end: int, algo: Optional[str] = None, ctas: Optional[int] = None) -> None:
         """Launch the fused all-reduce + update of [start, end) on the current
         stream.  `algo` = "pull" forces the pull two-shot form for a bucket
-        that would run push, "one-shot" the pull one-shot form for one that
-        would run ll, and `ctas` overrides the grid size (both for
-        comparisons)."""
+        that would run push or nvls, "one-shot" the pull one-shot form for
+        one that would run ll, "nvls" the multicast form (when available),
+        and `ctas` overrides the grid size (all for comparisons)."""
         key = (start, end)
         if key not in self._bucket_ids:
             if len(self._bucket_ids) >= MAX_BUCKETS:
@@ -195,30 +310,42 @@ class FusedAllReduceOptimizer:
             self._bucket_ids[key] = len(self._bucket_ids)
         b = self._bucket_ids[key]
         chosen = self.algorithm(start, end)
-        if algo == "pull" and chosen == "push":
+        if algo == "pull" and chosen in ("push", "nvls"):
             chosen = "pull"
         if algo == "one-shot" and chosen == "ll":
             chosen = "one-shot"
-        algo = chosen
+        if algo == "nvls" and self.nvls:
+            chosen = "nvls"
+        st = self.st
+        self._launch(chosen, start, end, b, self.store.master, st.m, st.v, ctas,
+                     ll_off=self._ll.get(key, 0), push=self._push.get(key))
+
+    def _launch(self, algo, start, end, slot, master, m, v, ctas, ll_off=0, push=None) -> None:
+        """One fused all-reduce + update of [start, end) in form `algo`, with
+        flag / counter slot `slot` and the given fp32 master and optimizer
+        state buffers (full-length, or bucket-length starting at `start`)."""
         st = self.st
         if algo == "ll":
             self.C.comm.fused_allreduce_optimizer_ll(
-                self.grad_buf, self.value_buf, self.ll, start, end, self._ll[key], self.ll_cap, self.store.master,
-                st.m, st.v, st.hyper, self.opt.kind, self.epoch, self.world, self.rank, not self.bf16,
+                self.grad_buf, self.value_buf, self.ll, start, end, ll_off, self.ll_cap, master,
+                m, v, st.hyper, self.opt.kind, self.epoch, self.world, self.rank, not self.bf16,
                 1 if self.bf16 else 0, ctas or self.ctas, BUDGET_S)
-            return
-        if algo == "push":
-            row, off = self._push[key]
+        elif algo == "push":
+            row, off = push
             self.C.comm.fused_allreduce_optimizer_push(
-                self.grad_buf, self.value_buf, self.flag_buf, self.recv, self.cflags, self.counters, b, row, start,
-                end, off, self.recv_slot, self.store.master, st.m, st.v, st.hyper, self.opt.kind, self.epoch,
+                self.grad_buf, self.value_buf, self.flag_buf, self.recv, self.cflags, self.counters, slot, row, start,
+                end, off, self.recv_slot, master, m, v, st.hyper, self.opt.kind, self.epoch,
                 self.world, self.rank, not self.bf16, 0, 1 if self.bf16 else 0, ctas or self.push_ctas, BUDGET_S)
-            return
-        one_shot = algo == "one-shot"
-        self.C.comm.fused_allreduce_optimizer(
-            self.grad_buf, self.value_buf, self.flag_buf, self.counters, b, start, end, self.store.master,
-            st.m, st.v, st.hyper, self.opt.kind, self.epoch, self.world, self.rank, one_shot, not self.bf16,
-            0, 1 if self.bf16 else 0, ctas or self.ctas, BUDGET_S)
+        elif algo == "nvls":
+            self.C.comm.fused_allreduce_optimizer_nvls(
+                self.grad_buf, self.value_buf, self.flag_buf, self.counters, slot, start, end, master, m, v,
+                st.hyper, self.opt.kind, self.epoch, self.world, self.rank, not self.bf16, 1 if self.bf16 else 0,
+                ctas or self.nvls_ctas, BUDGET_S)
+        else:
+            self.C.comm.fused_allreduce_optimizer(
+                self.grad_buf, self.value_buf, self.flag_buf, self.counters, slot, start, end, master,
+                m, v, st.hyper, self.opt.kind, self.epoch, self.world, self.rank, algo == "one-shot", not self.bf16,
+                0, 1 if self.bf16 else 0, ctas or self.ctas, BUDGET_S)
 
     def close(self) -> None:
         torch.cuda.synchronize(self.dev)

@@ -86,8 +86,15 @@ class DataParallel:
         return buckets
 
     def describe(self) -> dict:
-        return {"mode": self.mode, "buckets": len(self.buckets),
-                "bucket_mb": [round(b.numel * 4 / 2 ** 20, 2) for b in self.buckets]}
+        d = {"mode": self.mode, "buckets": len(self.buckets),
+             "bucket_mb": [round(b.numel * 4 / 2 ** 20, 2) for b in self.buckets]}
+        if self.fused is not None:
+            f = self.fused
+            d["forms"] = [f.algorithm(b.start, b.end) for b in self.buckets]
+            d["nvls"] = f.nvls if f.nvls else f.nvls_reason
+            if f.calibration:
+                d["calibration_us"] = f.calibration["us"]
+        return d
 
     # ------------------------------------------------------------ step protocol
     def begin_step(self) -> None:

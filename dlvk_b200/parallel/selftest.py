@@ -29,7 +29,8 @@ def main() -> int:
     ap.add_argument("--bucket-mb", type=float, default=0.05)
     ap.add_argument("--one-shot-bytes", type=int, default=None)
     ap.add_argument("--ll", type=int, default=1, help="0: small buckets use the pull one-shot form, not LL")
-    ap.add_argument("--algo", default=None, choices=["auto", "push", "pull"], help="two-shot form of the fused path")
+    ap.add_argument("--algo", default=None, choices=["auto", "push", "pull", "nvls"],
+                    help="form of the fused path (auto: calibrated per bucket size)")
     ap.add_argument("--cpu", action="store_true")
     ap.add_argument("--fail-rank", type=int, default=-1,
                     help="fault injection on the host: this rank exits between steps")
@@ -119,7 +120,8 @@ def main() -> int:
     mdiff = float((model.store.master - ref.store.master).abs().max())
     res = {"rank": rank, "world": world, "mode": args.mode, "model": args.model, "dtype": args.dtype,
            "max_param_diff": diff, "param_scale": scale, "master_diff": mdiff, "device_error": err_word,
-           "buckets": dp.describe()["buckets"], "ok": ok, "loss": float(loss)}
+           "buckets": dp.describe()["buckets"], "forms": dp.describe().get("forms"), "ok": ok,
+           "loss": float(loss)}
     print(json.dumps(res), flush=True)
     dp.close()
     dist.barrier()

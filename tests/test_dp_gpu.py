@@ -31,6 +31,30 @@ def test_fused_dp_matches_full_batch(model, dtype, oneshot, opt, algo):
     assert len(lines) == 2 and all(l["ok"] for l in lines), lines
 
 
+# Every fused form at 2, 4 and 8 ranks (the kernels are instantiated per
+# world size) against single-process full-batch training.  "nvls" needs
+# NVLink multicast; "auto" runs the start-up calibration and its choices.
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("model,dtype,oneshot,opt,algo", [("mlp", "fp32", 1 << 30, "adam", "auto"),
+                                                          ("mlp", "fp32", 1 << 30, "adam", "noll"),
+                                                          ("mlp", "fp32", 0, "adam", "pull"),
+                                                          ("mlp", "fp32", 0, "adam", "push"),
+                                                          ("mlp", "fp32", 0, "adam", "nvls"),
+                                                          ("transformer", "bf16", 0, "sgd", "nvls"),
+                                                          ("transformer", "bf16", 0, "sgd", "auto")])
+def test_fused_dp_forms_at_world(world, model, dtype, oneshot, opt, algo):
+    _need(world)
+    extra = ["--ll", "0"] if algo == "noll" else ["--algo", algo]
+    rc, lines, log = run_selftest(world, ["--mode", "fused", "--model", model, "--dtype", dtype,
+                                          "--one-shot-bytes", str(oneshot), "--opt", opt] + extra)
+    if algo == "nvls" and "NVLS all-reduce requested but unavailable" in log:
+        pytest.skip("no NVLink multicast on this node")
+    assert rc == 0, log[-4000:]
+    assert len(lines) == world and all(l["ok"] for l in lines), lines
+    if algo == "nvls":
+        assert all("nvls" in (l.get("forms") or []) for l in lines), lines
+
+
 def test_nccl_dp_matches_full_batch():
     _need(2)
     rc, lines, log = run_selftest(2, ["--mode", "nccl", "--model", "transformer", "--dtype", "bf16", "--opt", "sgd"])
