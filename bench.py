@@ -62,6 +62,8 @@ def parse():
     ap.add_argument("--no-graph", action="store_true",
                     help="eager step instead of a captured CUDA graph (both arms)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--timeline", action="store_true",
+                    help="N > 1, eager (--no-graph): record per-bucket all-reduce events of one extra step")
     ap.add_argument("--no-published", action="store_true",
                     help="skip the batch-1 MLP forward measured against the reference's published 3.772 ms")
     ap.add_argument("--allreduce", default="fused", choices=["fused", "nccl"],
@@ -256,6 +258,19 @@ def run_ours(args, rank, local, world):
            "dtype": zc.dtype, "data": "synthetic (shapes of the named config; random-init weights)",
            "config": metric_config(args, world, zc.batch, seq), "impl": "ours",
            "graph": not args.no_graph, "gpu_launches": int(launches), "e2e": e2e, "clocks": clock}
+    if dp is not None and args.timeline and args.no_graph:
+        dp.record_timeline(True)
+        step.run_staged()
+        torch.cuda.synchronize()
+        tl = dp.timeline()
+        dp.record_timeline(False)
+        # the latest time over ranks of every event
+        t = torch.tensor([e["ms"] for e in tl], dtype=torch.float64, device="cuda")
+        if world > 1:
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        for e, v in zip(tl, t.tolist()):
+            e["ms"] = round(v, 4)
+        out["timeline_ms_max_over_ranks"] = tl
     if dp is not None:
         out["config"]["allreduce"] = dp.describe()
         dp.close()

@@ -60,6 +60,7 @@ class DataParallel:
             for p in b.params:
                 self._bucket_of[id(p)] = b
                 p.on_grad_ready.append(self._on_grad_ready)
+        self._tl = None  # timeline records while enabled (eager steps only)
         self.fused = None
         if mode == "fused":
             from .comm import FusedAllReduceOptimizer
@@ -97,7 +98,33 @@ class DataParallel:
         return d
 
     # ------------------------------------------------------------ step protocol
+    # ------------------------------------------------------------ timeline
+    def record_timeline(self, on: bool = True) -> None:
+        """Record CUDA events per bucket (ready on the compute stream, start
+        and end on the comm stream) for the next eager steps; read them with
+        timeline().  Events cannot be recorded inside a CUDA-graph capture."""
+        self._tl = [] if on else None
+
+    def _ev(self, stream=None):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(stream)
+        return e
+
+    def timeline(self) -> list:
+        """Per bucket of the last recorded step: size, form and the ready /
+        start / end times (ms from the step's start on this rank)."""
+        if not self._tl:
+            return []
+        torch.cuda.synchronize(self.dev.device)
+        t0 = self._tl[0][1]
+        out = []
+        for kind, ev, b, form in self._tl[1:]:
+            out.append({"event": kind, "bucket": b, "form": form, "ms": round(t0.elapsed_time(ev), 4)})
+        return out
+
     def begin_step(self) -> None:
+        if self._tl is not None and self.dev.is_cuda:
+            self._tl = [("step_start", self._ev(), -1, None)]
         for b in self.buckets:
             b.pending = len(b.params)
         self.opt.advance(self.store)
@@ -123,9 +150,17 @@ class DataParallel:
             self._reduce_bucket(b)
             return
         cur = torch.cuda.current_stream()
+        tl = self._tl is not None and len(self._tl) > 0
+        form = self.fused.algorithm(b.start, b.end) if (tl and self.fused is not None) else self.mode
+        if tl:
+            self._tl.append(("ready", self._ev(cur), b.idx, form))
         self.comm_stream.wait_stream(cur)
         with torch.cuda.stream(self.comm_stream):
+            if tl:
+                self._tl.append(("start", self._ev(self.comm_stream), b.idx, form))
             self._reduce_bucket(b)
+            if tl:
+                self._tl.append(("end", self._ev(self.comm_stream), b.idx, form))
 
     def finish_step(self) -> None:
         # Buckets whose params got no gradient hook call (unused params) are
@@ -135,7 +170,11 @@ class DataParallel:
                 b.pending = 0
                 self._launch(b)
         if self.dev.is_cuda:
+            if self._tl:
+                self._tl.append(("backward_end", self._ev(), -1, None))
             torch.cuda.current_stream().wait_stream(self.comm_stream)
+            if self._tl:
+                self._tl.append(("step_end", self._ev(), -1, None))
 
     def consolidate(self) -> None:
         """Make every rank's fp32 master and optimizer state complete (two-shot
