@@ -110,6 +110,53 @@ class QuantizedDenseLayer(L.ModernLayer):
     __call__ = forward
 
 
+class QuantizedConv2DLayer(L.ModernLayer):
+    """Inference-only int8 convolution: im2col patches quantised per row
+    (dynamic, symmetric), weights per output channel, int32 accumulation in
+    the int8 GEMM (tcgen05 kind::i8 when the reduction length allows, which
+    the patch width is zero-padded to a multiple of 16 for) and an fp32
+    dequantisation + bias + ReLU epilogue; output NCHW."""
+
+    type_name = "QuantizedConv2D"
+
+    def __init__(self, conv: L.Conv2DLayer, act: int = K.ACT_NONE):
+        super().__init__()
+        W = conv.weight.master.detach()
+        self.cin, self.cout, self.k = conv.in_channels, conv.out_channels, conv.kernel_size
+        self.stride, self.padding = conv.stride, conv.padding
+        self.kdim = self.cin * self.k * self.k
+        self.kpad = (self.kdim + 15) // 16 * 16
+        w2 = torch.zeros(self.cout, self.kpad, device=W.device)
+        w2[:, :self.kdim] = W.reshape(self.cout, -1).float()
+        self.wq, self.w_scale = Q.quantize_rows(w2)
+        self.bias = conv.bias.master.detach().clone() if conv.bias is not None else None
+        self.act = act
+
+    def parameter_count(self) -> int:
+        return self.cout * self.kdim + (self.bias.numel() if self.bias is not None else 0)
+
+    def nbytes(self) -> int:
+        return self.wq.numel() + self.w_scale.numel() * 4 + (self.bias.numel() * 4 if self.bias is not None else 0)
+
+    def _forward(self, x):
+        n, _, h, w = x.shape
+        ho = (h + 2 * self.padding - self.k) // self.stride + 1
+        wo = (w + 2 * self.padding - self.k) // self.stride + 1
+        cols = torch.nn.functional.unfold(x.float(), self.k, padding=self.padding, stride=self.stride)
+        patches = cols.transpose(1, 2).reshape(n * ho * wo, self.kdim)
+        if self.kpad != self.kdim:
+            patches = torch.nn.functional.pad(patches, (0, self.kpad - self.kdim))
+        qx, sx = Q.quantize_rows(patches.contiguous())
+        y = Q.gemm_i8(qx, self.wq, sx, self.w_scale, self.bias, self.act, torch.float32)
+        return y.reshape(n, ho * wo, self.cout).transpose(1, 2).reshape(n, self.cout, ho, wo).contiguous()
+
+    def forward(self, x):
+        with torch.no_grad():
+            return self._forward(x)
+
+    __call__ = forward
+
+
 class _QuantizedSequential:
     """Inference-only model produced by quantize_model."""
 
@@ -131,7 +178,7 @@ class _QuantizedSequential:
         tot = 0
         for fn in self.steps:
             layer = getattr(fn, "__self__", None)
-            if isinstance(layer, QuantizedDenseLayer):
+            if isinstance(layer, (QuantizedDenseLayer, QuantizedConv2DLayer)):
                 tot += layer.nbytes()
             elif isinstance(layer, L.ModernLayer):
                 tot += sum(p.numel * 4 for p in layer.parameters())
@@ -150,7 +197,10 @@ class ModelOptimizer:
 
     # ------------------------------------------------------------ quantisation
     def quantize_model(self, model: Optional[Sequential] = None, config: QuantizationConfig = None):
-        """Returns an inference model whose Dense layers run in int8."""
+        """Returns an inference model whose Dense and Conv2D layers run in
+        int8 (per-output-channel weights, dynamic per-row activations; the
+        reference config's defaults, include/dlvk/optimization/
+        model_optimizer.h:40-47)."""
         model = model or self.model
         config = config or QuantizationConfig()
         if config.type != QuantizationType.INT8:
@@ -169,6 +219,12 @@ class ModelOptimizer:
                 q = QuantizedDenseLayer(cur, K.ACT_RELU if relu else K.ACT_NONE)
                 steps.append(q._forward)
                 i += 2 if relu else 1
+                continue
+            if isinstance(cur, L.Conv2DLayer):
+                relu = cur.relu or (isinstance(nxt, L.ActivationLayer) and nxt.activation == A.ReLU)
+                q = QuantizedConv2DLayer(cur, K.ACT_RELU if relu else K.ACT_NONE)
+                steps.append(q._forward)
+                i += 2 if (isinstance(nxt, L.ActivationLayer) and nxt.activation == A.ReLU) else 1
                 continue
             steps.append(cur._forward)
             i += 1
@@ -270,3 +326,146 @@ class ModelOptimizer:
                 model.forward(x)
             ms = (time.perf_counter() - t0) * 1e3 / iterations
         return {"latency_ms": ms, "throughput_samples_per_s": input_shape[0] / (ms / 1e3), "iterations": iterations}
+
+
+# ------------------------------------------------------------ architecture search
+@dataclass
+class SearchSpace:
+    """Candidate values per gene (include/dlvk/optimization/
+    model_optimizer.h:221-229)."""
+    layer_widths: List[int] = field(default_factory=lambda: [32, 64, 128, 256])
+    layer_depths: List[int] = field(default_factory=lambda: [1, 2, 3])
+    activation_functions: List[str] = field(default_factory=lambda: ["relu", "tanh", "sigmoid"])
+    dropout_rates: List[float] = field(default_factory=lambda: [0.0, 0.1, 0.3])
+
+
+@dataclass
+class SearchConfig:
+    """Genetic-search settings (model_optimizer.h:231-238) plus the model's
+    input / output sizes and a seed.  fitness_function(model) -> float,
+    higher is better."""
+    search_space: SearchSpace = field(default_factory=SearchSpace)
+    population_size: int = 20
+    num_generations: int = 50
+    mutation_rate: float = 0.1
+    crossover_rate: float = 0.7
+    fitness_function: Optional[object] = None
+    input_size: int = 784
+    output_size: int = 10
+    elite: int = 2
+    tournament: int = 3
+    seed: int = 0
+
+
+class NeuralArchitectureSearch:
+    """Evolutionary search over MLP architectures: a genome is a list of
+    hidden layers (width, activation, dropout) whose length is one of the
+    allowed depths; the phenotype is a Sequential of Dense layers with those
+    activations and dropouts and a Softmax output.  Each generation keeps the
+    `elite` best, then fills the population with children of tournament-
+    selected parents (one-point crossover with probability crossover_rate,
+    then per-gene mutation with probability mutation_rate, a depth change
+    included).  The reference declares this interface with a skeleton body
+    (src/optimization/model_optimizer.cpp:248-315)."""
+
+    def __init__(self, config: SearchConfig, device=None, dtype="fp32"):
+        import random
+
+        self.cfg = config
+        self.device = device
+        self.dtype = dtype
+        self.rng = random.Random(config.seed)
+        self.history = []  # (generation, best fitness, best genome)
+        self._cache = {}
+
+    # ---- genomes
+    def _gene(self):
+        sp = self.cfg.search_space
+        return (self.rng.choice(sp.layer_widths), self.rng.choice(sp.activation_functions),
+                self.rng.choice(sp.dropout_rates))
+
+    def generate_random_architecture(self):
+        depth = self.rng.choice(self.cfg.search_space.layer_depths)
+        return tuple(self._gene() for _ in range(depth))
+
+    def mutate_architecture(self, genome):
+        sp, p = self.cfg.search_space, self.cfg.mutation_rate
+        out = []
+        for w, a, d in genome:
+            if self.rng.random() < p:
+                w = self.rng.choice(sp.layer_widths)
+            if self.rng.random() < p:
+                a = self.rng.choice(sp.activation_functions)
+            if self.rng.random() < p:
+                d = self.rng.choice(sp.dropout_rates)
+            out.append((w, a, d))
+        if self.rng.random() < p:  # depth mutation: grow or shrink within the allowed depths
+            depth = self.rng.choice(sp.layer_depths)
+            while len(out) < depth:
+                out.append(self._gene())
+            out = out[:depth]
+        return tuple(out)
+
+    def crossover_architectures(self, g1, g2):
+        depths = self.cfg.search_space.layer_depths
+        cut1 = self.rng.randint(0, len(g1))
+        cut2 = self.rng.randint(0, len(g2))
+        child = list(g1[:cut1] + g2[cut2:])
+        if len(child) not in depths:  # keep the child inside the search space
+            depth = min(depths, key=lambda d: abs(d - len(child)))
+            while len(child) < depth:
+                child.append(self._gene())
+            child = child[:depth]
+        return tuple(child)
+
+    # ---- phenotype
+    def build(self, genome, seed: int = 0) -> Sequential:
+        m = Sequential(self.device, self.dtype, seed=seed)
+        prev = self.cfg.input_size
+        for w, a, d in genome:
+            m.add_dense(prev, w)
+            {"relu": m.add_relu, "tanh": m.add_tanh, "sigmoid": m.add_sigmoid}[a]()
+            if d > 0:
+                m.add_dropout(d)
+            prev = w
+        m.add_dense(prev, self.cfg.output_size)
+        m.add_softmax()
+        return m
+
+    def fitness(self, genome) -> float:
+        if genome not in self._cache:
+            fn = self.cfg.fitness_function
+            if fn is None:
+                raise ValueError("SearchConfig.fitness_function is required")
+            self._cache[genome] = float(fn(self.build(genome)))
+        return self._cache[genome]
+
+    def _select(self, pop, fits):
+        idx = [self.rng.randrange(len(pop)) for _ in range(max(1, self.cfg.tournament))]
+        return pop[max(idx, key=lambda i: fits[i])]
+
+    def search(self):
+        """Returns (best genome, best fitness); history per generation."""
+        c = self.cfg
+        pop = [self.generate_random_architecture() for _ in range(c.population_size)]
+        best, best_fit = None, -math.inf
+        for gen in range(c.num_generations):
+            fits = [self.fitness(g) for g in pop]
+            order = sorted(range(len(pop)), key=lambda i: fits[i], reverse=True)
+            if fits[order[0]] > best_fit:
+                best, best_fit = pop[order[0]], fits[order[0]]
+            self.history.append((gen, best_fit, best))
+            nxt = [pop[i] for i in order[:max(0, min(c.elite, len(pop)))]]
+            while len(nxt) < c.population_size:
+                p1, p2 = self._select(pop, fits), self._select(pop, fits)
+                child = self.crossover_architectures(p1, p2) if self.rng.random() < c.crossover_rate else p1
+                nxt.append(self.mutate_architecture(child))
+            pop = nxt
+        return best, best_fit
+
+    @staticmethod
+    def search_architecture(config: SearchConfig, device=None) -> Sequential:
+        """The reference's entry point: the best architecture found, built."""
+        nas = NeuralArchitectureSearch(config, device)
+        genome, _ = nas.search()
+        return nas.build(genome)
