@@ -26,6 +26,11 @@ import torch.distributed as dist
 from ..ops import core as K
 
 DEFAULT_BUCKET_MB = float(os.environ.get("DLVK_BUCKET_MB", "64"))
+# The parameters whose gradients become ready last (up to one bucket's worth,
+# params larger than a bucket excepted) go into smaller buckets, so that
+# most of them are reduced while the last layer's backward still runs
+# instead of after it (0 disables).
+TAIL_BUCKET_MB = float(os.environ.get("DLVK_TAIL_BUCKET_MB", "16"))
 
 
 class Bucket:
@@ -74,12 +79,26 @@ class DataParallel:
 
     def _make_buckets(self, bucket_mb: float) -> List[Bucket]:
         limit = int(bucket_mb * (1 << 20) / 4)
+        tail_limit = int(TAIL_BUCKET_MB * (1 << 20) / 4)
+        ranges = self.store.ranges()
+        tail, acc = set(), 0
+        if 0 < tail_limit < limit:
+            for p, s, e in reversed(ranges):  # flat order ends with the first layer: ready last
+                if e - s > limit:
+                    continue
+                if acc + (e - s) > limit:
+                    break
+                tail.add(id(p))
+                acc += e - s
         buckets, cur, start = [], [], 0
         end = 0
-        for p, s, e in self.store.ranges():
-            if cur and (e - start) > limit:
+        in_tail = False
+        for p, s, e in ranges:
+            lim = tail_limit if id(p) in tail else limit
+            if cur and ((e - start) > lim or (id(p) in tail) != in_tail):
                 buckets.append(Bucket(len(buckets), start, end, cur))
                 cur, start = [], s
+            in_tail = id(p) in tail
             cur.append(p)
             end = e
         if cur:
