@@ -195,6 +195,33 @@ void p2p_allreduce_op(std::shared_ptr<SymmetricBuffer> data, std::shared_ptr<Sym
   p2p_allreduce(a, dtype_code == 0 ? DType::F32 : DType::BF16, average, (int)ctas, stream());
 }
 
+// Broadcast / all-gather / reduce-scatter of the staging buffer `data`
+// into the local tensor `out` (mode 0 / 1 / 2; see p2p_collective).
+void p2p_collective_op(std::shared_ptr<SymmetricBuffer> data, std::shared_ptr<SymmetricBuffer> flags,
+                       const at::Tensor& counters, int64_t slot, const at::Tensor& out, int64_t numel, int64_t mode,
+                       int64_t root, const at::Tensor& epoch, int64_t world, int64_t rank, int64_t dtype_code,
+                       int64_t ctas, double budget_s) {
+  c10::cuda::CUDAGuard g(epoch.device());
+  const int64_t esz = dtype_code == 0 ? 4 : 2;
+  TORCH_CHECK(numel * esz <= data->bytes(), "p2p collective: staging buffer too small");
+  TORCH_CHECK(out.is_cuda() && out.is_contiguous(), "p2p collective: contiguous CUDA output");
+  const int64_t need = mode == 1 ? numel * world : (mode == 2 ? (numel + world - 1) / world : numel);
+  TORCH_CHECK(out.numel() >= need && out.element_size() == esz, "p2p collective: output too small or wrong dtype");
+  FusedARArgs a;
+  a.world = (int)world;
+  a.rank = (int)rank;
+  a.peer_grads = const_cast<const void* const*>(data->device_ptrs());
+  a.peer_flags = reinterpret_cast<uint32_t* const*>(flags->device_ptrs());
+  a.my_flags = static_cast<uint32_t*>(flags->local());
+  a.cta_counter = reinterpret_cast<unsigned int*>(counters.data_ptr<int>()) + slot;
+  a.bucket = (int)slot;
+  a.epoch_ptr = epoch.data_ptr<int64_t>();
+  a.err = device_error_word();
+  a.budget_ns = (uint64_t)(budget_s * 1e9);
+  p2p_collective(a, dtype_code == 0 ? DType::F32 : DType::BF16, (int)mode, (int)root, out.data_ptr(), numel,
+                 (int)ctas, stream());
+}
+
 }  // namespace
 
 void register_comm(py::module& m) {
@@ -231,6 +258,7 @@ void register_comm(py::module& m) {
   c.attr("PUSH_MAX_BUCKETS") = PUSH_MAX_BUCKETS;
   c.attr("PUSH_MAX_CHUNKS") = PUSH_MAX_CHUNKS;
   c.def("p2p_allreduce", &p2p_allreduce_op);
+  c.def("p2p_collective", &p2p_collective_op);
   c.def("wait_flag_probe", [](const at::Tensor& flag, int64_t epoch, double budget_s) {
     TORCH_CHECK(flag.is_cuda() && flag.scalar_type() == at::kInt && flag.numel() >= 1, "wait_flag_probe: int32 flag");
     c10::cuda::CUDAGuard g(flag.device());

@@ -75,6 +75,12 @@ void fused_allreduce_optimizer(const FusedARArgs& a, DType grad_dt, DType value_
 // Generic in-place sum (or mean) all-reduce of [start, end) of the symmetric
 // buffer whose per-rank bases are a.peer_grads.
 void p2p_allreduce(const FusedARArgs& a, DType dt, bool average, int ctas, cudaStream_t s);
+// Broadcast (mode 0, from `root`), all-gather (1: `out` holds world blocks of
+// numel) and reduce-scatter (2: `out` holds this rank's ceil(numel/world)
+// chunk of the rank-order sum) of the contributions every rank wrote at
+// offset 0 of its staging buffer (a.peer_grads), with ready / done flags.
+void p2p_collective(const FusedARArgs& a, DType dt, int mode, int root, void* out, int64_t numel, int ctas,
+                    cudaStream_t s);
 // One-shot low-latency variant for small buckets: every rank stores its
 // gradients, each fp32 value paired with the step epoch in one 8-byte word,
 // into every peer's LL buffer; receivers poll the words themselves (no

@@ -734,6 +734,64 @@ void p2p_allreduce(const FusedARArgs& a, DType dt, bool average, int ctas, cudaS
   DLVK_POST_LAUNCH();
 }
 
+// ---------------------------------------------------------------- collectives
+// Pull collectives over the staging symmetric buffer (`peer_grads` = every
+// rank's staging base): each rank has written its contribution at offset 0
+// of its own staging buffer before the launch; after the ready barrier every
+// rank reads what it needs straight from the peers' buffers (P2P loads) into
+// its local output; the done barrier then frees the staging buffers for
+// reuse.  Copies move 16-byte vectors with a byte tail; the reduce-scatter
+// sums in rank order (deterministic).
+namespace {
+enum CollMode : int { COLL_BROADCAST = 0, COLL_ALL_GATHER = 1, COLL_REDUCE_SCATTER = 2 };
+
+__device__ __forceinline__ void copy_bytes(uint8_t* dst, const uint8_t* src, int64_t nbytes, int64_t tid,
+                                           int64_t stride) {
+  const int64_t nv = nbytes / 16;
+  for (int64_t i = tid; i < nv; i += stride)
+    reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+  for (int64_t i = nv * 16 + tid; i < nbytes; i += stride) dst[i] = src[i];
+}
+
+template <typename T>
+__global__ void __launch_bounds__(128, 8) p2p_collective_kernel(FusedARArgs a, void* out, int64_t numel, int mode,
+                                                                int root) {
+  const uint32_t epoch = (uint32_t)(*a.epoch_ptr);
+  if (!ready_barrier(a, epoch)) return;
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if (mode == COLL_BROADCAST) {
+    if (a.rank != root)
+      copy_bytes(static_cast<uint8_t*>(out), static_cast<const uint8_t*>(a.peer_grads[root]),
+                 numel * (int64_t)sizeof(T), tid, stride);
+  } else if (mode == COLL_ALL_GATHER) {
+    const int64_t nb = numel * (int64_t)sizeof(T);
+    for (int r = 0; r < a.world; ++r)  // rank r's block, in place for every rank
+      copy_bytes(static_cast<uint8_t*>(out) + r * nb, static_cast<const uint8_t*>(a.peer_grads[r]), nb, tid, stride);
+  } else {
+    const int64_t chunk = (numel + a.world - 1) / a.world;
+    const int64_t lo = min(numel, chunk * a.rank), hi = min(numel, lo + chunk);
+    for (int64_t i = lo + tid; i < hi; i += stride) {
+      float acc = 0.f;
+      for (int r = 0; r < a.world; ++r) acc += to_f32(reinterpret_cast<const T*>(a.peer_grads[r])[i]);
+      static_cast<T*>(out)[i - lo] = from_f32<T>(acc);
+    }
+  }
+  done_barrier(a, epoch);
+}
+}  // namespace
+
+void p2p_collective(const FusedARArgs& a, DType dt, int mode, int root, void* out, int64_t numel, int ctas,
+                    cudaStream_t s) {
+  DLVK_CHECK(mode >= 0 && mode <= 2 && root >= 0 && root < a.world, "p2p collective: bad mode or root");
+  DLVK_CHECK((reinterpret_cast<uintptr_t>(out) & 15) == 0, "p2p collective: output must be 16-byte aligned");
+  const int grid = std::max(1, ctas);
+  if (dt == DType::F32) p2p_collective_kernel<float><<<grid, 128, 0, s>>>(a, out, numel, mode, root);
+  else if (dt == DType::BF16) p2p_collective_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(a, out, numel, mode, root);
+  else throw std::runtime_error("p2p collective: unsupported dtype");
+  DLVK_POST_LAUNCH();
+}
+
 namespace {
 // One block waiting on `flag` for `epoch` through the same bounded wait the
 // all-reduce kernels use; result[0] = 1 on success, 0 on timeout.

@@ -410,8 +410,13 @@ class NcclBackend(CommunicationBackend):
 
 
 class NvlinkBackend(CommunicationBackend):
-    """All-reduce through this framework's P2P kernel over a symmetric staging
-    buffer (sized on first use); other collectives through NCCL."""
+    """Every collective on this framework's P2P kernels over NVLink: the
+    caller's tensor is staged in a symmetric (IPC-mapped) buffer, ranks
+    announce it with ready flags and read each other's staging buffers
+    directly (all-reduce: two-shot, each rank sums its shard and stores it to
+    all; broadcast / all-gather: pull copies; reduce-scatter: each rank sums
+    its chunk in rank order), bounded flag waits throughout.  Tensors larger
+    than the staging buffer, or of other dtypes, go through NCCL."""
 
     def __init__(self, group=None, capacity_bytes: int = 256 << 20):
         self.group = group
@@ -449,11 +454,38 @@ class NvlinkBackend(CommunicationBackend):
             t.reshape(-1).copy_(view)
         return True
 
+    def _fits(self, t: torch.Tensor) -> bool:
+        return t.is_cuda and t.dtype in (torch.float32, torch.bfloat16) and t.numel() * t.element_size() <= self.capacity
+
+    def _collective(self, t: torch.Tensor, out: torch.Tensor, mode: int, root: int = 0) -> None:
+        view = self.buf.tensor(_codes(t.dtype), t.numel(), 0)
+        view.copy_(t.reshape(-1))
+        self.C.counter_add(self.epoch, 1)
+        self.C.comm.p2p_collective(self.buf, self.flags, self.counters, 1, out, t.numel(), mode, root, self.epoch,
+                                   self.world, self.rank, _codes(t.dtype), 64, BUDGET_S)
+
     def broadcast(self, tensor, root: int = 0) -> bool:
-        return self.nccl.broadcast(tensor, root)
+        if not self._fits(tensor):
+            return self.nccl.broadcast(tensor, root)
+        out = torch.empty(tensor.numel(), dtype=tensor.dtype, device=tensor.device)
+        self._collective(tensor.contiguous(), out, 0, root)
+        if self.rank != root:
+            tensor.copy_(out.reshape(tensor.shape))
+        return True
 
     def all_gather(self, tensor):
-        return self.nccl.all_gather(tensor)
+        if not self._fits(tensor):
+            return self.nccl.all_gather(tensor)
+        out = torch.empty(self.world * tensor.numel(), dtype=tensor.dtype, device=tensor.device)
+        self._collective(tensor.contiguous(), out, 1)
+        return [c.reshape(tensor.shape) for c in out.chunk(self.world)]
 
     def reduce_scatter(self, tensor):
-        return self.nccl.reduce_scatter(tensor)
+        """This rank's chunk of the sum over ranks (chunks as tensor.chunk(world))."""
+        if not self._fits(tensor) or tensor.shape[0] % self.world != 0:
+            return self.nccl.reduce_scatter(tensor)
+        t = tensor.contiguous()
+        chunk = t.numel() // self.world
+        out = torch.empty(chunk, dtype=t.dtype, device=t.device)
+        self._collective(t, out, 2)
+        return out.reshape((t.shape[0] // self.world,) + tuple(t.shape[1:]))

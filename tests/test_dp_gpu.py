@@ -79,3 +79,22 @@ def test_multi_gpu_trainer_api(extra):
     res = parse_objects(r.stdout)
     assert r.returncode == 0, (r.stdout + r.stderr)[-3000:]
     assert len(res) == 2 and all(o["ok"] for o in res), res
+
+
+def test_nvlink_backend_collectives_match_nccl():
+    """broadcast / all_gather / reduce_scatter / all_reduce on this
+    framework's P2P kernels against NCCL, 2 ranks."""
+    import os
+    import subprocess
+    import sys
+
+    from test_dp_cpu import ROOT, _port, parse_objects
+
+    _need(2)
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2", "--master-addr",
+           "127.0.0.1", f"--master-port={_port()}", "-m", "dlvk_b200.parallel.collectives_selftest"]
+    env = dict(os.environ, PYTHONPATH=ROOT + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=300, cwd=ROOT, env=env)
+    res = parse_objects(r.stdout)
+    assert r.returncode == 0, (r.stdout + r.stderr)[-3000:]
+    assert len(res) == 2 and all(o["ok"] for o in res), res
