@@ -49,6 +49,8 @@ def main():
                     help="256 x 512 pair tile: 0 never, 1 when the tiling model picks it, 2 whenever it applies")
     ap.add_argument("--compare-single", action="store_true",
                     help="also time the single-CTA kernel (CTA-pair variant switched off)")
+    ap.add_argument("--tilings", default="",
+                    help="semicolon list of bn,splits,pair to time besides the model's choice, e.g. '256,2,1;128,2,0'")
     ap.add_argument("--fp32", action="store_true",
                     help="fp32 operands: ours 3xTF32 and 1xTF32 against cuBLAS TF32 and cuBLAS fp32")
     args = ap.parse_args()
@@ -84,6 +86,17 @@ def main():
                "plan": list(C.gemm_plan(a, b, args.out_f32)),
                "ours_ms": round(t_ours, 4),
                "ours_tflops": round(flops / t_ours / 1e9, 1), "ours_frac_of_measured": round(flops / t_ours / 1e9 / peak, 3)}
+        for tl in [t for t in args.tilings.split(";") if t]:
+            bn, sp, pr = (int(v) for v in tl.split(","))
+            C.gemm_set_tiling(bn, sp, pr)
+            try:
+                tt = time_fn(lambda: C.gemm(a, b, out=out, force_path=1, **kw), iters=args.iters)
+                ref = a.float() @ b.float()
+                C.gemm(a, b, out=out, force_path=1, **kw)
+                ok = float((out.float() - ref).abs().max() / ref.abs().max()) < 2e-2
+            finally:
+                C.gemm_set_tiling(0, 0, -1)
+            rec[f"tiling_{bn}_{sp}_{pr}_ms"] = round(tt, 4) if ok else "wrong"
         if args.compare_single:
             C.gemm_set_pair(False)
             try:

@@ -46,6 +46,9 @@ void register_ops(py::module& m) {
         py::arg("extra_scale") = 1.0, py::arg("max_ctas") = 0);
   m.def("gemm_set_pair", [](bool on) { gemm_tc_set_pair(on); });
   m.def("gemm_set_wide", [](int64_t mode) { gemm_tc_set_wide((int)mode); });
+  m.def("gemm_set_tiling", [](int64_t bn, int64_t splits, int64_t pair) {
+    gemm_tc_set_tiling((int)bn, (int)splits, (int)pair);
+  }, py::arg("bn") = 0, py::arg("splits") = 0, py::arg("pair") = -1);
   m.def(
       "gemm_plan",
       [](const at::Tensor& A, const at::Tensor& B, bool out_f32, int64_t max_ctas) {

@@ -99,6 +99,9 @@ void gemm_tc_set_pair(bool on);
 // long-K GEMMs with few tiles.  Mode 0 never, 1 when the tiling model picks
 // it (default; DLVK_GEMM_WIDE sets the initial mode), 2 whenever it applies.
 void gemm_tc_set_wide(int mode);
+// Forces the tile N (128 / 256 / 512), split-K factor and CTA-pair use of
+// later GEMMs (0 / 0 / -1 restore the tiling model); for measurements.
+void gemm_tc_set_tiling(int bn, int splits, int pair);
 // The tiling the model picks for these operands: tile N (128/256/512), the
 // split-K factor, and whether the CTA-pair kernel runs.
 void gemm_tc_plan(DType out_dt, const GemmArgs& a, int max_ctas, int* bn, int* splits, int* pair);

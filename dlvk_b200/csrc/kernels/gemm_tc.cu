@@ -1104,6 +1104,21 @@ CUtensorMap make_c_map(TcParams& p, int64_t M, int64_t N, bool reduce = false) {
 }  // namespace
 
 namespace {
+// Tiling forced by gemm_tc_set_tiling (measurement only; 0 / -1 = the model's choice).
+struct TilingOverride {
+  int bn = 0, splits = 0, pair = -1;
+};
+TilingOverride& tiling_override() {
+  static TilingOverride t;
+  return t;
+}
+}  // namespace
+
+void gemm_tc_set_tiling(int bn, int splits, int pair) {
+  tiling_override() = TilingOverride{bn, splits, pair};
+}
+
+namespace {
 // Shared host path of the bf16 and the tf32 GEMM.  TF32 runs on single-CTA
 // tiles (no CTA pairs): fp32 operands, 32-element k-blocks.
 void gemm_tc_impl(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err, int max_ctas, float* workspace,
@@ -1130,6 +1145,12 @@ void gemm_tc_impl(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err
   bool pair = false;
   const bool red = split_red_ok(out_dt, a);
   choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits, pair, red, out_dt == DType::F32, tf32);
+  {
+    const TilingOverride& ov = tiling_override();
+    if (ov.pair >= 0) pair = ov.pair != 0 && !tf32 && a.M >= 256;
+    if (ov.bn > 0) BN = (ov.bn == 512 && !pair) ? 256 : ov.bn;
+    if (ov.splits > 0) splits = ov.splits;
+  }
   if (a.colsum != nullptr) {
     DLVK_CHECK(gemm_tc_colsum_ok(out_dt, a), "gemm_tc: column sums need the staged fast-path layout");
     splits = 1;  // the sums are taken over final outputs
