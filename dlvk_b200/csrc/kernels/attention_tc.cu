@@ -21,16 +21,24 @@
 //
 // Backward (flash_bwd_kernel): persistent CTAs walk (batch, head, 128-key
 // tile) items with K and V resident.  For each query tile the MMA warp
-// computes S^T = K Q^T and dP^T = V dO^T into TMEM; warps 2..5 (one key row
-// per thread) rebuild P^T = exp2(S^T c - lse) and dS^T = P^T (dP^T - delta)
-// into shared memory; the MMA warp then accumulates dV += P^T dO and
-// dK += dS^T Q in TMEM and computes dQ = dS K reading the same dS^T tile as
-// an MN-major operand.  The dQ tile goes through shared memory to the
-// global fp32 accumulator with TMA bulk reduce-add; dK / dV are written to
-// the fused gradient buffer [B, S, 3, H, 64] when the key tile is done.
+// computes S^T = K Q^T and dP^T = V dO^T into TMEM; warps 2..9 (two per
+// TMEM lane quarter, one key row per thread, half the queries each) rebuild
+// P^T = exp2(S^T c - lse) and dS^T = P^T (dP^T - delta) into shared memory;
+// the MMA warp then accumulates dV += P^T dO and dK += dS^T Q in TMEM and
+// computes dQ = dS K reading the same dS^T tile as an MN-major operand.
+// Software pipeline: the next query tile's S^T / dP^T are issued as soon as
+// the compute warps have read the current ones (before the current tile's
+// gradient MMAs), and dQ alternates between two TMEM buffers whose readout
+// happens one step late, so the gradient MMAs of step g run while the
+// compute warps reduce the dQ of step g-1.  The dQ tile goes through shared
+// memory to the global fp32 accumulator with TMA bulk reduce-add; dK / dV
+// are written to the fused gradient buffer [B, S, 3, H, 64] when the key
+// tile is done.
 //
 // Every mbarrier wait is bounded (mbar_wait: error word + early exit).
 #include <cuda.h>
+
+#include <cstdlib>
 
 #include "dlvk/common.h"
 #include "dlvk/kernels.h"
@@ -57,19 +65,23 @@ __device__ __forceinline__ uint32_t sw_off(int r, int c) {
   return (uint32_t)((c >> 3) * 16384 + (r >> 3) * 1024 + (r & 7) * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
 
-// Phase timestamps for kernel development: compiled in only with
-// DLVK_ATTN_TRACE defined (a standalone harness reads g_attn_trace).
-#ifdef DLVK_ATTN_TRACE
-__device__ unsigned long long g_attn_trace[8192];
-#define ATTN_TRACE(cond, slot)                                              \
-  do {                                                                      \
-    if ((cond) && blockIdx.x == 0 && (slot) < 8192) g_attn_trace[(slot)] = clock64(); \
-  } while (0)
-#else
-#define ATTN_TRACE(cond, slot) \
-  do {                         \
-  } while (0)
-#endif
+// 2^x on the FMA pipe, for x <= 128: Cody-Waite style reduction x = n + f,
+// f in [-0.5, 0.5], with n found by adding 1.5 * 2^23 (round to nearest
+// leaves n in the low mantissa bits), then a degree-3 polynomial for 2^f and
+// n added into the exponent field.  The coefficients are this file's own
+// least-squares fit of 2^f in relative error at Chebyshev nodes (max
+// relative error 7.8e-5, far below bf16's 2^-9 rounding of P).  Inputs are
+// clamped at -126 so the result stays a normal number; exp2(-126) is as good
+// as zero next to the row's largest term, 1.
+__device__ __forceinline__ float fma_exp2(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  float q = fmaf(0.05508868396282196f, f, 0.24260404706001282f);
+  q = fmaf(q, f, 0.6932762265205383f);
+  q = fmaf(q, f, 0.9999289512634277f);
+  return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
+}
 
 // 2^x with the hardware approximation (ex2.approx.ftz: flushes denormal
 // results to zero, which bf16 probabilities cannot represent anyway).
@@ -117,6 +129,10 @@ constexpr int FWD_KV_STAGES = 4;
 constexpr int FWD_THREADS = 64 + 2 * 128;
 constexpr int FWD_SMEM = 2 * TILE + FWD_KV_STAGES * 2 * TILE + 2 * 2 * TILE + 256 + 1024;
 
+// EMU: of every four pairs of scores, EMU pairs take their exponentials on the
+// FMA pipe (fma_exp2) and the rest on the MUFU unit (ex2.approx), which with
+// head dim 64 is the busiest pipe of the softmax.
+template <int EMU>
 __global__ void __launch_bounds__(FWD_THREADS, 1) flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, FwdP p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -280,74 +296,92 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) flash_fwd_kernel(const __grid_
         if (!warp_wait(&s_full[t], sph, p.err)) { ok = false; break; }
         sph ^= 1u;
         tc_fence_after();
-        // Pass 1: the row max over all 128 scores (8 independent partials:
-        // one thread owns a row).
+        // Three TMEM reads of the score row per tile: columns 0..63 for the
+        // max, columns 64..127 for the max and kept in registers for their
+        // exponentials, then columns 0..63 again (a thread has 168 registers
+        // in a 320-thread block, too few to hold all 128 scores).
         float mp[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) mp[k] = -INFINITY;
-#pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {  // two halves of 64 columns
-          uint32_t sr[2][32];
-          tmem_ld32(tS + (uint32_t)(h2 * 64), sr[0]);
-          tmem_ld32(tS + (uint32_t)(h2 * 64 + 32), sr[1]);
+        {
+          uint32_t sa[2][32];
+          tmem_ld32(tS, sa[0]);
+          tmem_ld32(tS + 32u, sa[1]);
           tmem_ld_wait();
 #pragma unroll
           for (int c = 0; c < 2; ++c)
 #pragma unroll
-            for (int i = 0; i < 32; ++i) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(sr[c][i]));
+            for (int i = 0; i < 32; ++i) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(sa[c][i]));
         }
+        if (j > 0) {
+          // The previous tile's PV must be done before P is rewritten or O
+          // rescaled (it was queued right behind this tile's S).
+          if (!warp_wait(&pv_done[t], pvph, p.err)) { ok = false; break; }
+          pvph ^= 1u;
+          tc_fence_after();
+        }
+        uint32_t sb[2][32];
+        tmem_ld32(tS + 64u, sb[0]);
+        tmem_ld32(tS + 96u, sb[1]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(sb[c][i]));
         float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
         mx *= p.c;
         const bool need = mx > m + 8.f;  // lazy rescale: keep the old reference max while it is within 2^8
         const float m_new = need ? mx : m;
         const float alpha = need ? hw_exp2(m - m_new) : 1.f;
-        if (j > 0) {
-          // The previous tile's PV must be done before O is rescaled or P
-          // rewritten (it was queued right behind this tile's S).
-          if (!warp_wait(&pv_done[t], pvph, p.err)) { ok = false; break; }
-          pvph ^= 1u;
-          tc_fence_after();
-          if (__any_sync(0xffffffffu, need)) {
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-              uint32_t o[32];
-              tmem_ld32(tO + (uint32_t)(c * 32), o);
-              tmem_ld_wait();
-#pragma unroll
-              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-              tmem_st32(tO + (uint32_t)(c * 32), o);
-            }
-            tmem_st_wait();
-          }
-        }
-        // Pass 2: the scores again, 32 at a time, into exponentials written
-        // straight to P as bf16 (few live registers: a 320-thread block
-        // gives a thread 168); the row sum uses the fp32 values.
+        // Exponentials straight to P as bf16; the row sum uses the fp32 values.
         float sp8[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) sp8[k] = 0.f;
-#pragma unroll 1  // one chunk's scores live at a time (unrolled, ptxas overlaps chunks and spills)
-        for (int c = 0; c < 4; ++c) {
-          uint32_t sc[32];
-          tmem_ld32(tS + (uint32_t)(c * 32), sc);
-          tmem_ld_wait();
+        auto emit = [&](const uint32_t (&sc)[32], int chunk) {  // 32 scores -> P chunk (4 x 16 bytes)
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
-            const float e0 = hw_exp2(fmaf(__uint_as_float(sc[i]), p.c, -m_new));
-            const float e1 = hw_exp2(fmaf(__uint_as_float(sc[i + 1]), p.c, -m_new));
+            const float x0 = fmaf(__uint_as_float(sc[i]), p.c, -m_new);
+            const float x1 = fmaf(__uint_as_float(sc[i + 1]), p.c, -m_new);
+            const bool emu = ((i >> 1) & 3) < EMU;
+            const float e0 = emu ? fma_exp2(x0) : hw_exp2(x0);
+            const float e1 = emu ? fma_exp2(x1) : hw_exp2(x1);
             sp8[i & 7] += e0;
             sp8[(i + 1) & 7] += e1;
             pk[i >> 1] = pack2(e0, e1);
           }
 #pragma unroll
           for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<uint4*>(prow + sw_off(row, c * 4 + q)) =
+            *reinterpret_cast<uint4*>(prow + sw_off(row, chunk * 4 + q)) =
                 make_uint4(pk[q * 4], pk[q * 4 + 1], pk[q * 4 + 2], pk[q * 4 + 3]);
+        };
+        emit(sb[0], 2);
+        emit(sb[1], 3);
+        asm volatile("" ::: "memory");  // keeps those P stores (and their math) ahead of the next TMEM read
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          uint32_t sc[32];
+          tmem_ld32(tS + (uint32_t)(c * 32), sc);
+          tmem_ld_wait();
+          if (c == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_empty[t]);  // the score buffer is read out
+          }
+          emit(sc, c);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_empty[t]);
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + (uint32_t)(c * 32), o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(tO + (uint32_t)(c * 32), o);
+          }
+          tmem_st_wait();
+        }
         l = l * alpha + (((sp8[0] + sp8[1]) + (sp8[2] + sp8[3])) + ((sp8[4] + sp8[5]) + (sp8[6] + sp8[7])));
         m = m_new;
         fence_proxy_async_smem();
@@ -446,11 +480,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
   uint64_t* st_full = bars + 6;
   uint64_t* ds_full = bars + 7;
   uint64_t* dq_full = bars + 8;
-  uint64_t* dq_free = bars + 9;
+  uint64_t* dq_free = bars + 14;  // 2: dQ TMEM buffer g & 1 read out
   uint64_t* kv_done = bars + 10;   // dK, dV accumulated for the item
   uint64_t* kv_read = bars + 11;   // dK, dV read out of TMEM
   uint64_t* cw_bar = bars + 12;    // compute-warp group barrier (one arrival per compute thread)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* st_free = bars + 13;   // S^T / dP^T read out of TMEM
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nt = p.S / FT;
@@ -466,10 +501,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
     mbar_init(st_full, 1);
     mbar_init(ds_full, BWD_COMPUTE_WARPS);
     mbar_init(dq_full, 1);
-    mbar_init(dq_free, BWD_COMPUTE_WARPS);
+    mbar_init(&dq_free[0], BWD_COMPUTE_WARPS);
+    mbar_init(&dq_free[1], BWD_COMPUTE_WARPS);
     mbar_init(kv_done, 1);
     mbar_init(kv_read, BWD_COMPUTE_WARPS);
     mbar_init(cw_bar, 32 * BWD_COMPUTE_WARPS);
+    mbar_init(st_free, BWD_COMPUTE_WARPS);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -479,7 +516,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  // TMEM: S^T 0..127, dP^T 128..255, dV 256..319, dK 320..383, dQ 384..447
+  // TMEM: S^T 0..127, dP^T 128..255, dV 256..319, dK 320..383, dQ of step g at 384 + 64 * (g & 1)
   const uint32_t tbase = *tmem_slot;
   pdl_wait();
 
@@ -514,35 +551,47 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
       const uint32_t id_st = make_idesc(1, 1, 1, false, false, 128, 128);  // S^T, dP^T: K-major A and B
       const uint32_t id_kv = make_idesc(1, 1, 1, false, true, 128, 64);    // dV, dK: K-major A, MN-major B
       const uint32_t id_q = make_idesc(1, 1, 1, true, true, 128, 64);      // dQ: MN-major A and B
-      int it = 0, qs = 0;
-      uint32_t qph = 0, dsph = 0, dqph = 0;
-      bool ok = true;
       const uint32_t ka = smem_u32(sK), va = smem_u32(sV), pta = smem_u32(sPT), dsa = smem_u32(sDS);
-      for (int item = blockIdx.x; item < items && ok; item += gridDim.x, ++it) {
-        if (!mbar_wait(kv_full, it & 1, p.err)) break;
-        if (!mbar_wait(kv_read, (it & 1) ^ 1u, p.err)) break;  // previous item's dK / dV read out
-        for (int i = 0; i < nt; ++i) {
-          ATTN_TRACE(true, 4096 + (it * nt + i) * 16 + 12);
-          if (!mbar_wait(&qd_full[qs], qph, p.err)) { ok = false; break; }
-          ATTN_TRACE(true, 4096 + (it * nt + i) * 16 + 13);
-          tc_fence_after();
-          const uint32_t qa = smem_u32(sQD + qs * 2 * TILE), doa = qa + TILE;
+      // Steps are numbered g across items; step g uses Q / dO stage g & 1.
+      // Step g+1's S^T / dP^T go out as soon as the compute warps have read
+      // step g's (st_free), ahead of step g's gradient MMAs, so the tensor
+      // cores run while the compute warps take the exponentials.
+      int64_t g = 0;
+      uint32_t stfph = 0, dsph = 0;
+      bool ok = true;
+      auto issue_scores = [&](int64_t gs) -> bool {
+        const int st = (int)(gs & 1);
+        if (!mbar_wait(&qd_full[st], (uint32_t)((gs >> 1) & 1), p.err)) return false;
+        if (gs > 0) {
+          if (!mbar_wait(st_free, stfph, p.err)) return false;  // step gs-1's scores read out of TMEM
+          stfph ^= 1u;
+        }
+        tc_fence_after();
+        const uint32_t qa = smem_u32(sQD + st * 2 * TILE), doa = qa + TILE;
 #pragma unroll
-          for (int k = 0; k < FD / 16; ++k) {
-            mma_f16(tbase, make_sw128_desc(ka + k * 32, 16, 1024), make_sw128_desc(qa + k * 32, 16, 1024), id_st,
-                    k ? 1u : 0u);
-            mma_f16(tbase + 128, make_sw128_desc(va + k * 32, 16, 1024), make_sw128_desc(doa + k * 32, 16, 1024),
-                    id_st, k ? 1u : 0u);
-          }
-          mma_commit(st_full);
-          ATTN_TRACE(true, 4096 + (it * nt + i) * 16 + 8);
+        for (int k = 0; k < FD / 16; ++k) {
+          mma_f16(tbase, make_sw128_desc(ka + k * 32, 16, 1024), make_sw128_desc(qa + k * 32, 16, 1024), id_st,
+                  k ? 1u : 0u);
+          mma_f16(tbase + 128, make_sw128_desc(va + k * 32, 16, 1024), make_sw128_desc(doa + k * 32, 16, 1024),
+                  id_st, k ? 1u : 0u);
+        }
+        mma_commit(st_full);
+        return true;
+      };
+      for (int item = blockIdx.x, it = 0; item < items && ok; item += gridDim.x, ++it) {
+        if (!mbar_wait(kv_full, it & 1, p.err)) break;
+        if (!issue_scores(g)) break;
+        for (int i = 0; i < nt; ++i, ++g) {
+          const int cur = (int)(g & 1);
+          if (i + 1 < nt && !issue_scores(g + 1)) { ok = false; break; }
           if (!mbar_wait(ds_full, dsph, p.err)) { ok = false; break; }
-          ATTN_TRACE(true, 4096 + (it * nt + i) * 16 + 9);
           dsph ^= 1u;
-          if (!mbar_wait(dq_free, dqph ^ 1u, p.err)) { ok = false; break; }
-          ATTN_TRACE(true, 4096 + (it * nt + i) * 16 + 10);
-          dqph ^= 1u;
+          if (i == 0 && !mbar_wait(kv_read, (it & 1) ^ 1u, p.err)) { ok = false; break; }  // previous dK / dV read
+          // dQ buffer g & 1 was read out two steps ago
+          if (!mbar_wait(&dq_free[cur], (uint32_t)((g >> 1) & 1) ^ 1u, p.err)) { ok = false; break; }
           tc_fence_after();
+          const uint32_t tdq = tbase + 384 + 64 * cur;
+          const uint32_t qa = smem_u32(sQD + cur * 2 * TILE), doa = qa + TILE;
 #pragma unroll
           for (int k = 0; k < FT / 16; ++k) {
             const uint32_t koff = (uint32_t)((k >> 2) * 16384 + (k & 3) * 32);
@@ -552,16 +601,11 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
             mma_f16(tbase + 320, make_sw128_desc(dsa + koff, 16, 1024), make_sw128_desc(qa + k * 2048, 16384, 1024),
                     id_kv, (i > 0 || k > 0) ? 1u : 0u);
             // dQ = dS K: A = dS^T tile read MN-major (M = queries in 64-wide chunks 16 KB apart), B = K MN-major
-            mma_f16(tbase + 384, make_sw128_desc(dsa + k * 2048, 16384, 1024),
+            mma_f16(tdq, make_sw128_desc(dsa + k * 2048, 16384, 1024),
                     make_sw128_desc(ka + k * 2048, 16384, 1024), id_q, k > 0 ? 1u : 0u);
           }
           mma_commit(dq_full);
-          ATTN_TRACE(true, 4096 + (it * nt + i) * 16 + 11);
-          mma_commit(&qd_empty[qs]);
-          if (++qs == 2) {
-            qs = 0;
-            qph ^= 1u;
-          }
+          mma_commit(&qd_empty[cur]);
         }
         if (!ok) break;
         mma_commit(kv_empty);
@@ -580,6 +624,47 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
     uint32_t stph = 0, dqph = 0, cwph = 0;
     int it = 0, ib = 0;
     bool ok = true;
+    // The dQ tile of step g leaves TMEM during step g+1, after that step's
+    // P^T / dS^T tiles are out: it sits in one of two TMEM buffers, so the
+    // gradient MMAs of step g+1 need not wait for it.  dq_x / dq_y are its
+    // coordinates in dQ.
+    bool dq_pending = false;
+    int dq_x = 0, dq_y = 0, dq_buf = 1;  // toggled to the step's buffer (g & 1) when it becomes pending
+    auto wait_dq = [&]() -> bool {  // the pending step's gradient MMAs are complete
+      if (!warp_wait(dq_full, dqph, p.err)) return false;
+      dqph ^= 1u;
+      tc_fence_after();
+      return true;
+    };
+    // TMEM -> registers -> this warp's 32 x 32 fp32 box of the swizzled
+    // staging tile -> TMA reduce-add issued by the warp's lane 0.  Each warp
+    // owns its box, so no cross-warp barrier is needed: lane 0 waits until
+    // its own previous reduce has read the box.
+    uint8_t* const dq_box = sDQ + hf * 16384 + quarter * 4096;
+    auto reduce_dq = [&]() {
+      uint32_t qv[32];
+      tmem_ld32(tbase + lane_off + 384u + (uint32_t)(64 * dq_buf + hf * 32), qv);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&dq_free[dq_buf]);
+        bulk_wait_read0();
+      }
+      __syncwarp();
+      uint8_t* base = dq_box + lane * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint4 v = make_uint4(qv[c * 4], qv[c * 4 + 1], qv[c * 4 + 2], qv[c * 4 + 3]);
+        *reinterpret_cast<uint4*>(base + ((c ^ (lane & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_reduce_add_2d(&tm_dq, dq_box, dq_x + hf * 32, dq_y + quarter * 32);
+        bulk_commit();
+      }
+    };
     // Each thread carries one lse (tid < 128) or delta (tid >= 128) value of
     // the next query tile, loaded one iteration ahead.
     auto fetch = [&](int item_, int i_) -> float {
@@ -592,86 +677,59 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
     for (int item = blockIdx.x; item < items && ok; item += gridDim.x, ++it) {
       const int kt = item % nt, bh = item / nt, h = bh % p.H, b = bh / p.H;
       for (int i = 0; i < nt; ++i, ib ^= 1) {
-        const int bslot = 4096 + (it * nt + i) * 16;
-        ATTN_TRACE(threadIdx.x == 64, bslot + 0);
         const float nxt = (i + 1 < nt) ? fetch(item, i + 1) : fetch(item + gridDim.x, 0);
         (tid < 128 ? sLse : sDel)[ib * 128 + (tid & 127)] = cur;
         cur = nxt;
         if (!group_sync(cw_bar, cwph, p.err)) { ok = false; break; }
-        ATTN_TRACE(threadIdx.x == 64, bslot + 1);
         if (!warp_wait(st_full, stph, p.err)) { ok = false; break; }
-        ATTN_TRACE(threadIdx.x == 64, bslot + 2);
         stph ^= 1u;
         tc_fence_after();
         const float* L = sLse + ib * 128;
         const float* Dl = sDel + ib * 128;
+        // sPT / sDS are free once the previous step's gradient MMAs are
+        // complete (its dQ commit); those ran while this CTA reduced the dQ
+        // of the step before.
+        if (dq_pending && !wait_dq()) { ok = false; break; }
 #pragma unroll 1
         for (int cq = 0; cq < 2; ++cq) {  // 32 query columns at a time, this warp's half
-          const int cb = hf * 2 + cq;
+          const int col = hf * 64 + cq * 32;
           uint32_t s[32], dp[32];
-          tmem_ld32(tbase + lane_off + (uint32_t)(cb * 32), s);
-          tmem_ld32(tbase + lane_off + 128u + (uint32_t)(cb * 32), dp);
+          tmem_ld32(tbase + lane_off + (uint32_t)col, s);
+          tmem_ld32(tbase + lane_off + 128u + (uint32_t)col, dp);
           tmem_ld_wait();
+          if (cq == 1) {  // scores read out: the next step's S^T / dP^T may overwrite them
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(st_free);
+          }
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {  // 8 queries per 16-byte chunk
-            float pt[8], ds[8];
-            // per-query lse / delta: two 16-byte broadcast loads each
-            const float4* L4 = reinterpret_cast<const float4*>(L + cb * 32 + q4 * 8);
-            const float4* D4 = reinterpret_cast<const float4*>(Dl + cb * 32 + q4 * 8);
-            const float4 la = L4[0], lb = L4[1], da = D4[0], db = D4[1];
-            const float lv[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
-            const float dv[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
+          for (int c8 = 0; c8 < 4; ++c8) {  // 8 queries per 16-byte chunk
+            uint32_t pk[4], dk[4];
 #pragma unroll
-            for (int i8 = 0; i8 < 8; ++i8) {
-              pt[i8] = hw_exp2(fmaf(__uint_as_float(s[q4 * 8 + i8]), p.c, -lv[i8]));
-              ds[i8] = pt[i8] * (__uint_as_float(dp[q4 * 8 + i8]) - dv[i8]);
+            for (int j = 0; j < 4; ++j) {
+              const int e = c8 * 8 + 2 * j;
+              // per-query lse / delta: 8-byte broadcast loads
+              const float2 lv = *reinterpret_cast<const float2*>(L + col + e);
+              const float2 dv = *reinterpret_cast<const float2*>(Dl + col + e);
+              const float p0 = hw_exp2(fmaf(__uint_as_float(s[e]), p.c, -lv.x));
+              const float p1 = hw_exp2(fmaf(__uint_as_float(s[e + 1]), p.c, -lv.y));
+              pk[j] = pack2(p0, p1);
+              dk[j] = pack2(p0 * (__uint_as_float(dp[e]) - dv.x), p1 * (__uint_as_float(dp[e + 1]) - dv.y));
             }
-            const int ch = cb * 4 + q4;
-            uint4 a4, d4;
-            a4.x = pack2(pt[0], pt[1]); a4.y = pack2(pt[2], pt[3]); a4.z = pack2(pt[4], pt[5]); a4.w = pack2(pt[6], pt[7]);
-            d4.x = pack2(ds[0], ds[1]); d4.y = pack2(ds[2], ds[3]); d4.z = pack2(ds[4], ds[5]); d4.w = pack2(ds[6], ds[7]);
-            *reinterpret_cast<uint4*>(sPT + sw_off(row, ch)) = a4;
-            *reinterpret_cast<uint4*>(sDS + sw_off(row, ch)) = d4;
+            const int ch = hf * 8 + cq * 4 + c8;
+            *reinterpret_cast<uint4*>(sPT + sw_off(row, ch)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            *reinterpret_cast<uint4*>(sDS + sw_off(row, ch)) = make_uint4(dk[0], dk[1], dk[2], dk[3]);
           }
         }
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(ds_full);
-        ATTN_TRACE(threadIdx.x == 64, bslot + 3);
-        // dQ tile (row = query): this warp's 32 columns -> swizzled fp32 staging
-        // sub-tile `hf` -> TMA reduce-add.
-        if (!warp_wait(dq_full, dqph, p.err)) { ok = false; break; }
-        ATTN_TRACE(threadIdx.x == 64, bslot + 4);
-        dqph ^= 1u;
-        tc_fence_after();
-        uint32_t qv[32];
-        tmem_ld32(tbase + lane_off + 384u + (uint32_t)(hf * 32), qv);
-        tmem_ld_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(dq_free);
-        ATTN_TRACE(threadIdx.x == 64, bslot + 5);
-        if (tid == 0) bulk_wait_read0();  // the previous reduce has read the staging buffer
-        if (!group_sync(cw_bar, cwph, p.err)) { ok = false; break; }
-        ATTN_TRACE(threadIdx.x == 64, bslot + 6);
-        {
-          uint8_t* base = sDQ + hf * 16384 + (row >> 3) * 1024 + (row & 7) * 128;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            uint4 v = make_uint4(qv[c * 4], qv[c * 4 + 1], qv[c * 4 + 2], qv[c * 4 + 3]);
-            *reinterpret_cast<uint4*>(base + ((c ^ (row & 7)) << 4)) = v;
-          }
-        }
-        fence_proxy_async_smem();
-        if (!group_sync(cw_bar, cwph, p.err)) { ok = false; break; }
-        ATTN_TRACE(threadIdx.x == 64, bslot + 7);
-        if (tid == 0) {
-          const int y = b * p.S + i * FT;
-          tma_reduce_add_2d(&tm_dq, sDQ, h * FD, y);
-          tma_reduce_add_2d(&tm_dq, sDQ + 16384, h * FD + 32, y);
-          bulk_commit();
-        }
+        if (dq_pending) reduce_dq();
+        dq_pending = true;
+        dq_buf ^= 1;
+        dq_x = h * FD;
+        dq_y = b * p.S + i * FT;
       }
       if (!ok) break;
       // dV (hf = 0) or dK (hf = 1, scaled) of this key tile -> the fused gradient buffer.
@@ -700,7 +758,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
       __syncwarp();
       if (lane == 0) mbar_arrive(kv_read);
     }
-    if (tid == 0) bulk_wait0();
+    if (ok && dq_pending && wait_dq()) reduce_dq();
+    if (lane == 0) bulk_wait0();
   }
   tc_fence_before();
   __syncthreads();
@@ -779,15 +838,21 @@ void flash_attention_fwd(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* ls
   const int E = H * FD;
   CUtensorMap tm = tmap::bf16_2d_sw128(qkv, (uint64_t)3 * E, (uint64_t)B * S, (uint64_t)3 * E, FT);
   FwdP p{out, lse, B, S, H, E, scale * 1.4426950408889634f, err};
+  static const int emu = [] {
+    const char* e = std::getenv("DLVK_ATTN_EXP2_FMA");  // pairs of four on the FMA pipe: 0, 1 or 2
+    const int v = e ? std::atoi(e) : 0;
+    return v < 0 ? 0 : (v > 2 ? 2 : v);
+  }();
+  auto kern = emu == 2 ? flash_fwd_kernel<2> : (emu == 1 ? flash_fwd_kernel<1> : flash_fwd_kernel<0>);
   const int adev = current_device_slot();
   static bool attr[kMaxDevices] = {};  // per device: the attribute belongs to each device's context
   if (!attr[adev]) {
-    DLVK_CUDA_CHECK(cudaFuncSetAttribute(flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM));
+    DLVK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM));
     attr[adev] = true;
   }
   const int items = B * H * (S / FT);
   int grid = std::min(items, max_ctas > 0 ? max_ctas : tmap::sm_count());
-  launch_pdl(flash_fwd_kernel, dim3(grid), dim3(FWD_THREADS), FWD_SMEM, s, tm, p);
+  launch_pdl(kern, dim3(grid), dim3(FWD_THREADS), FWD_SMEM, s, tm, p);
   DLVK_POST_LAUNCH();
 }
 
@@ -811,7 +876,7 @@ void flash_attention_bwd(const __nv_bfloat16* qkv, const __nv_bfloat16* out, con
   {
     cuuint64_t dims[2] = {(cuuint64_t)E, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)E * 4};
-    cuuint32_t box[2] = {32u, (cuuint32_t)FT};
+    cuuint32_t box[2] = {32u, 32u};  // one compute warp's 32 queries x 32 columns
     cuuint32_t estr[2] = {1, 1};
     CUresult r = tmap::encode_fn()(&tdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dq_acc, dims, strides, box, estr,
                                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
