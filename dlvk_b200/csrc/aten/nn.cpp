@@ -65,6 +65,26 @@ at::Tensor pack_conv_weights(const at::Tensor& w, const ConvDesc& d, bool dgrad)
 
 const __nv_bfloat16* bf(const at::Tensor& t) { return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr()); }
 
+// 1x1 filter, stride 1, no padding: in NCHW the convolution is a batched
+// GEMM over the tensors as they are (no NHWC copy, no im2col gather):
+//   forward  y[n] (Cout x HW) = W (Cout x Cin) . x[n] (Cin x HW), bias per row
+//   dgrad    dx[n] (Cin x HW) = W^T (Cin x Cout) . dy[n] (Cout x HW)
+//   wgrad    dW (Cout x Cin) = sum_n dy[n] (Cout x HW) . x[n]^T (HW x Cin)
+// with W shared by every image (zero batch stride).  Needs bf16 and rows
+// whose byte strides are multiples of 16 (channels and H*W multiples of 8).
+bool conv1x1_gemm_ok(const ConvDesc& d) {
+  const int64_t hw = (int64_t)d.H * d.W;
+  return d.KH == 1 && d.KW == 1 && d.stride == 1 && d.pad == 0 && d.Cin % 8 == 0 && d.Cout % 8 == 0 &&
+         hw % 8 == 0 && hw >= 16 && conv2d_tc_supported(DType::BF16, d);
+}
+
+void run_gemm_tc(DType out_dt, const GemmArgs& a, const at::Tensor& like) {
+  TORCH_CHECK(gemm_tc_supported(a), "dlvk.conv2d: 1x1 GEMM operands not tensor-core aligned");
+  const int64_t wsf = gemm_tc_workspace_floats(a, 0, out_dt);
+  at::Tensor ws = wsf > 0 ? at::empty({wsf}, like.options().dtype(at::kFloat)) : at::Tensor();
+  gemm_tc(out_dt, a, stream(), device_error_word(), 0, wsf > 0 ? ws.data_ptr<float>() : nullptr, wsf);
+}
+
 at::Tensor conv2d_fwd_op(const at::Tensor& x, const at::Tensor& w, c10::optional<at::Tensor> bias, int64_t stride,
                          int64_t pad, bool relu) {
   check_cuda(x, "x");
@@ -72,6 +92,29 @@ at::Tensor conv2d_fwd_op(const at::Tensor& x, const at::Tensor& w, c10::optional
   auto xc = x.contiguous(), wc = w.contiguous().to(x.scalar_type());
   auto d = conv_desc(xc, wc, stride, pad);
   auto y = at::empty({d.N, d.Cout, d.Ho, d.Wo}, xc.options());
+  if (xc.scalar_type() == at::kBFloat16 && conv1x1_gemm_ok(d)) {
+    const int64_t hw = (int64_t)d.H * d.W;
+    GemmArgs a;
+    a.A = wc.data_ptr();
+    a.B = xc.data_ptr();
+    a.C = y.data_ptr();
+    a.M = d.Cout;
+    a.N = hw;
+    a.K = d.Cin;
+    a.sam = d.Cin;
+    a.sak = 1;
+    a.sbk = hw;
+    a.sbn = 1;
+    a.ldc = hw;
+    a.batch = d.N;
+    a.batch_stride_a = 0;
+    a.batch_stride_b = (int64_t)d.Cin * hw;
+    a.batch_stride_c = (int64_t)d.Cout * hw;
+    a.row_bias = optf(bias);
+    a.act = relu ? ACT_RELU : ACT_NONE;
+    run_gemm_tc(DType::BF16, a, xc);
+    return y;
+  }
   if (conv2d_tc_supported(to_dtype(xc), d)) {
     auto xn = to_nhwc(xc);
     auto wp = pack_conv_weights(wc, d, false);
@@ -97,6 +140,32 @@ at::Tensor conv2d_dgrad_op(const at::Tensor& gy, const at::Tensor& w, std::vecto
     TORCH_CHECK(rsc.scalar_type() == gc.scalar_type() && rsc.numel() == dx.numel(), "dlvk.conv2d_dgrad: relu_src");
     rs = rsc.data_ptr();
   }
+  if (gc.scalar_type() == at::kBFloat16 && conv1x1_gemm_ok(d)) {
+    const int64_t hw = (int64_t)d.H * d.W;
+    GemmArgs a;
+    a.A = wc.data_ptr();  // W^T: [Cin x Cout] read M-major from W [Cout x Cin]
+    a.B = gc.data_ptr();
+    a.C = dx.data_ptr();
+    a.M = d.Cin;
+    a.N = hw;
+    a.K = d.Cout;
+    a.sam = 1;
+    a.sak = d.Cin;
+    a.sbk = hw;
+    a.sbn = 1;
+    a.ldc = hw;
+    a.batch = d.N;
+    a.batch_stride_a = 0;
+    a.batch_stride_b = (int64_t)d.Cout * hw;
+    a.batch_stride_c = (int64_t)d.Cin * hw;
+    if (rs) {
+      a.relu_mask = rs;
+      a.ldm = hw;
+      a.batch_stride_m = (int64_t)d.Cin * hw;
+    }
+    run_gemm_tc(DType::BF16, a, gc);
+    return dx;
+  }
   if (conv2d_tc_supported(to_dtype(gc), d)) {
     auto gn = to_nhwc(gc);
     auto wp = pack_conv_weights(wc, d, true);
@@ -114,6 +183,45 @@ void conv2d_wgrad_op(const at::Tensor& x, const at::Tensor& gy, const at::Tensor
   auto xc = x.contiguous(), gc = gy.contiguous().to(x.scalar_type());
   TORCH_CHECK(dw.scalar_type() == at::kFloat && dw.is_contiguous(), "dlvk.conv2d_wgrad: f32 contiguous dw");
   auto d = conv_desc(xc, dw, stride, pad);
+  if (xc.scalar_type() == at::kBFloat16 && conv1x1_gemm_ok(d)) {
+    TORCH_CHECK(gc.size(2) == d.Ho && gc.size(3) == d.Wo, "dlvk.conv2d_wgrad: grad shape");
+    const int64_t hw = (int64_t)d.H * d.W;
+    // Per-image products [N, Cout, Cin] in fp32, then summed over the images
+    // in image order (deterministic) into dW.
+    auto part = at::empty({d.N, d.Cout, d.Cin}, xc.options().dtype(at::kFloat));
+    GemmArgs a;
+    a.A = gc.data_ptr();
+    a.B = xc.data_ptr();  // x[n]^T: [HW x Cin] read K-major from x[n] [Cin x HW]
+    a.C = part.data_ptr();
+    a.M = d.Cout;
+    a.N = d.Cin;
+    a.K = hw;
+    a.sam = hw;
+    a.sak = 1;
+    a.sbk = 1;
+    a.sbn = hw;
+    a.ldc = d.Cin;
+    a.batch = d.N;
+    a.batch_stride_a = (int64_t)d.Cout * hw;
+    a.batch_stride_b = (int64_t)d.Cin * hw;
+    a.batch_stride_c = (int64_t)d.Cout * d.Cin;
+    run_gemm_tc(DType::F32, a, xc);
+    const int64_t cols = (int64_t)d.Cout * d.Cin;
+    const int64_t ns = colsum_scratch_floats(d.N, cols);
+    at::Tensor scr = ns > 0 ? at::empty({ns}, part.options()) : at::Tensor();
+    colsum(DType::F32, DType::F32, part.data_ptr(), d.N, cols, 1.f, dw.data_ptr<float>(), accumulate,
+           ns > 0 ? scr.data_ptr<float>() : nullptr, stream());
+    if (db.has_value()) {
+      // db[c] = sum over images and pixels of dy[n, c, :]: row sums, then a column sum over images.
+      auto rows = at::empty({(int64_t)d.N * d.Cout}, part.options());
+      rowsum(DType::BF16, gc.data_ptr(), (int64_t)d.N * d.Cout, hw, 1.f, rows.data_ptr<float>(), stream());
+      const int64_t ns2 = colsum_scratch_floats(d.N, d.Cout);
+      at::Tensor scr2 = ns2 > 0 ? at::empty({ns2}, part.options()) : at::Tensor();
+      colsum(DType::F32, DType::F32, rows.data_ptr(), d.N, d.Cout, 1.f, db->data_ptr<float>(), accumulate,
+             ns2 > 0 ? scr2.data_ptr<float>() : nullptr, stream());
+    }
+    return;
+  }
   if (conv2d_tc_supported(to_dtype(xc), d)) {
     TORCH_CHECK(gc.size(2) == d.Ho && gc.size(3) == d.Wo, "dlvk.conv2d_wgrad: grad shape");
     auto xn = to_nhwc(xc);

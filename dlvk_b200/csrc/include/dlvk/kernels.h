@@ -79,6 +79,11 @@ struct GemmArgs {
   // colsum_partials() then adds the ceil(M / 32) rows.  Fuses a bias
   // gradient db = sum_rows(dY) into the GEMM that produces dY.
   float* colsum = nullptr;
+  // Optional fp32 bias per output row (added with the column bias, before
+  // the activation): the per-channel bias of a convolution whose output
+  // rows are channels (1x1 convolution in NCHW as a batched GEMM).  Tensor-
+  // core path only.
+  const float* row_bias = nullptr;
 };
 void gemm_simt(DType in_dt, DType out_dt, const GemmArgs& a, cudaStream_t s);
 bool gemm_tc_supported(const GemmArgs& a);

@@ -107,6 +107,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs a) {
 
 void gemm_simt(DType in_dt, DType out_dt, const GemmArgs& a, cudaStream_t s) {
   if (a.M == 0 || a.N == 0) return;
+  DLVK_CHECK(a.row_bias == nullptr, "gemm_simt: per-row bias is a tensor-core-path option");
   dim3 grid((unsigned)((a.N + BN - 1) / BN), (unsigned)((a.M + BM - 1) / BM), (unsigned)(a.batch * a.batch2));
   if (in_dt == DType::F32 && out_dt == DType::F32)
     gemm_simt_kernel<float, float><<<grid, 256, 0, s>>>(a);

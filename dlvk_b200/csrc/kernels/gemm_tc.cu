@@ -66,6 +66,8 @@ struct TcParams {
   float* colsum;           // per-32-row column sums of the output (staged fast path)
   int tma_c;               // 1: plain epilogue stores C through per-warp smem boxes + TMA;
                            // 2: same boxes, added into fp32 C (split-K partials reduced in L2)
+  int a_bcast;             // 1: one A for every batch entry (its map has no batch extent)
+  const float* row_bias;   // fp32 bias per output row, or null
 };
 
 // PAIR: a 2-CTA cluster shares one 256 x BN tile (tcgen05 cta_group::2);
@@ -233,8 +235,9 @@ __device__ __forceinline__ void epi_store(const TcParams& p, const float* stg, i
     for (int ps = 0; ps < NP; ++ps) {
       const int rl = ps * RPP + rr;
       float v[VEC];
+      const float rbv = p.row_bias ? p.row_bias[row0 + rl] : 0.f;
 #pragma unroll
-      for (int k = 0; k < VEC; ++k) v[k] = stg[rl * 33 + cg * VEC + k] + bv[k];
+      for (int k = 0; k < VEC; ++k) v[k] = stg[rl * 33 + cg * VEC + k] + bv[k] + rbv;
       const T* e = reinterpret_cast<const T*>(&av[ps]);
       if (mode == 0) {
 #pragma unroll
@@ -288,6 +291,11 @@ __device__ __forceinline__ void epi_store(const TcParams& p, const float* stg, i
       for (int k = 0; k < VEC; ++k) v[k] += p.beta * o[k];
     }
     if (p.bias) add_bias<VEC>(p.bias, p.bias_f32, n, valid, v);
+    if (p.row_bias) {
+      const float rbv = p.row_bias[row];
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) v[k] += rbv;
+    }
     if (p.R) {
       float o[VEC];
       ld_vec<T, VEC>(p.R, rb + (int64_t)row * p.ldr + n, valid, p.r_vec, o);
@@ -388,6 +396,7 @@ __global__ void __launch_bounds__(320, 1)
         const int sp = t / tiles_per_split;
         tile_coords(t - sp * tiles_per_split, p, tm, tn, b);
         const int bo = b / p.batch2, bi = b - bo * p.batch2;
+        const int abo = p.a_bcast ? 0 : bo, abi = p.a_bcast ? 0 : bi;
         const int arow = tm * TILE_M + (int)rank * BM;
         // sub-block j of this CTA: columns tn*BN + j*MMA_N + rank*MMA_N/2 + [0, MMA_N/2)
         const int bcol = tn * BN + (int)rank * (C::MMA_N / 2);
@@ -403,10 +412,11 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);  // the leader's full barrier
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
           if (!p.a_mn) {
-            tma_load_4d_pair(sA, &tmA, fb, kb * BK, arow, bi, bo);
+            tma_load_4d_pair(sA, &tmA, fb, kb * BK, arow, abi, abo);
           } else {
 #pragma unroll
-            for (int j = 0; j < BM / 64; ++j) tma_load_4d_pair(sA + j * 8192, &tmA, fb, arow + j * 64, kb * BK, bi, bo);
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_4d_pair(sA + j * 8192, &tmA, fb, arow + j * 64, kb * BK, abi, abo);
           }
 #pragma unroll
           for (int sub = 0; sub < C::NSUB; ++sub) {
@@ -435,6 +445,7 @@ __global__ void __launch_bounds__(320, 1)
         const int sp = t / tiles_per_split;
         tile_coords(t - sp * tiles_per_split, p, tm, tn, b);
         const int bo = b / p.batch2, bi = b - bo * p.batch2;
+        const int abo = p.a_bcast ? 0 : bo, abi = p.a_bcast ? 0 : bi;
         const int kb0 = sp * p.kb_per_split, kb1 = min(num_kb, kb0 + p.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
           {
@@ -446,10 +457,10 @@ __global__ void __launch_bounds__(320, 1)
           uint8_t* sB = sA + C::A_BYTES;
           mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
           if (!p.a_mn) {
-            tma_load_4d(sA, &tmA, &full[stage], kb * bke, tm * BM, bi, bo);
+            tma_load_4d(sA, &tmA, &full[stage], kb * bke, tm * BM, abi, abo);
           } else {
             for (int j = 0; j < BM / mn_box; ++j)
-              tma_load_4d(sA + j * mn_box_bytes, &tmA, &full[stage], tm * BM + j * mn_box, kb * bke, bi, bo);
+              tma_load_4d(sA + j * mn_box_bytes, &tmA, &full[stage], tm * BM + j * mn_box, kb * bke, abi, abo);
           }
           if (!p.b_mn) {
             tma_load_4d(sB, &tmB, &full[stage], kb * bke, tn * BN, bi, bo);
@@ -656,7 +667,9 @@ __global__ void __launch_bounds__(320, 1)
           if (nbox < p.N) {
             float v[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[i & 1][j]) * p.alpha;
+            const float rbv = (p.row_bias && row0 + lane < p.M) ? p.row_bias[row0 + lane] : 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = fmaf(__uint_as_float(r[i & 1][j]), p.alpha, rbv);
             if (p.bias && n0 < p.N) add_bias<32>(p.bias, p.bias_f32, n0, min(32, p.N - n0), v);
             apply_act<32>(p.act, v);
             // Boxes start on 1024-byte boundaries (the swizzled box layout is
@@ -713,8 +726,9 @@ __global__ void __launch_bounds__(320, 1)
           const int row = row0 + lane;
           if (row < p.M && n0 < p.N) {
             float v[32];
+            const float rbv = p.row_bias ? p.row_bias[row] : 0.f;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[i & 1][j]) * p.alpha;
+            for (int j = 0; j < 32; ++j) v[j] = fmaf(__uint_as_float(r[i & 1][j]), p.alpha, rbv);
             if (p.i8) {
               // int32 accumulators -> real values: alpha * acc * row_scale * col_scale
               const float rs = p.alpha * p.row_scale[row];
@@ -918,6 +932,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
     if (a.bias)
       v += a.bias_dtype == (int)DType::F32 ? reinterpret_cast<const float*>(a.bias)[n]
                                            : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.bias)[n]);
+    if (a.row_bias) v += a.row_bias[m];
     if (a.residual)
       v += to_f32(reinterpret_cast<const T*>(a.residual)[bo * a.batch_stride_r + bi * a.batch2_stride_r + m * a.ldr + n]);
     if (a.act == ACT_RELU) v = fmaxf(v, 0.f);
@@ -1161,14 +1176,19 @@ void gemm_tc_impl(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err
   // Unused batch levels get a harmless stride (a multiple of 16 bytes).
   auto pick = [](int64_t cnt, int64_t stride, uint64_t dflt) { return cnt > 1 ? (uint64_t)stride : dflt; };
   CUtensorMap ta, tb;
+  // A shared by every batch entry (zero batch strides): its map covers one
+  // matrix and the producer reads it at batch coordinate 0.
+  const bool a_bcast = a.batch * a.batch2 > 1 && (a.batch == 1 || a.batch_stride_a == 0) &&
+                       (a.batch2 == 1 || a.batch2_stride_a == 0);
+  const uint64_t ab2 = a_bcast ? 1 : (uint64_t)a.batch2, ab = a_bcast ? 1 : (uint64_t)a.batch;
   if (a_k) {
     const uint64_t d = (uint64_t)a.sam * (uint64_t)a.M;
-    ta = make_tmap(a.A, a.K, a.M, a.batch2, a.batch, a.sam, pick(a.batch2, a.batch2_stride_a, d),
-                        pick(a.batch, a.batch_stride_a, d), BM, el);
+    ta = make_tmap(a.A, a.K, a.M, ab2, ab, a.sam, pick((int64_t)ab2, a.batch2_stride_a, d),
+                   pick((int64_t)ab, a.batch_stride_a, d), BM, el);
   } else {
     const uint64_t d = (uint64_t)a.sak * (uint64_t)a.K;
-    ta = make_tmap(a.A, a.M, a.K, a.batch2, a.batch, a.sak, pick(a.batch2, a.batch2_stride_a, d),
-                        pick(a.batch, a.batch_stride_a, d), (uint32_t)bke, el, true);
+    ta = make_tmap(a.A, a.M, a.K, ab2, ab, a.sak, pick((int64_t)ab2, a.batch2_stride_a, d),
+                   pick((int64_t)ab, a.batch_stride_a, d), (uint32_t)bke, el, true);
   }
   if (b_k) {
     const uint64_t d = (uint64_t)a.sbn * (uint64_t)a.N;
@@ -1213,6 +1233,8 @@ void gemm_tc_impl(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err
   p.beta = a.beta;
   p.bias = a.bias;
   p.bias_f32 = (a.bias_dtype == (int)DType::F32);
+  p.row_bias = a.row_bias;
+  p.a_bcast = a_bcast ? 1 : 0;
   p.act = a.act;
   p.err = err;
   p.colsum = a.colsum;
@@ -1254,6 +1276,7 @@ void gemm_tc_impl(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err
     p.alpha = 1.f;
     p.beta = 0.f;
     p.bias = nullptr;
+    p.row_bias = nullptr;
     p.R = nullptr;
     p.Mk = nullptr;
     p.act = ACT_NONE;

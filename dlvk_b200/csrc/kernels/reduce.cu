@@ -122,7 +122,29 @@ __global__ void rowsum_kernel(const T* __restrict__ x, int64_t rows, int64_t col
   const int lane = threadIdx.x & 31;
   if (r >= rows) return;
   float acc = 0.f;
-  for (int64_t c = lane; c < cols; c += 32) acc += to_f32(x[r * cols + c]);
+  const T* xr = x + r * cols;
+  constexpr int EPV = 16 / sizeof(T);
+  if (cols % EPV == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    // 16-byte vectors; each lane keeps two in flight
+    const uint4* v = reinterpret_cast<const uint4*>(xr);
+    const int64_t nv = cols / EPV;
+    int64_t i = lane;
+    for (; i + 32 < nv; i += 64) {
+      const uint4 a = v[i], b = v[i + 32];
+      const T* ea = reinterpret_cast<const T*>(&a);
+      const T* eb = reinterpret_cast<const T*>(&b);
+#pragma unroll
+      for (int k = 0; k < EPV; ++k) acc += to_f32(ea[k]) + to_f32(eb[k]);
+    }
+    for (; i < nv; i += 32) {
+      const uint4 a = v[i];
+      const T* ea = reinterpret_cast<const T*>(&a);
+#pragma unroll
+      for (int k = 0; k < EPV; ++k) acc += to_f32(ea[k]);
+    }
+  } else {
+    for (int64_t c = lane; c < cols; c += 32) acc += to_f32(xr[c]);
+  }
   acc = warp_sum(acc);
   if (lane == 0) out[r] = acc * scale;
 }

@@ -30,9 +30,12 @@ def tc_mode():
 
 
 # (N, Cin, H, W, Cout, k, stride, pad): 64/128/256-wide column tiles, ragged
-# pixel counts, strided and 1x1 filters, padding larger than one.
+# pixel counts, strided and 1x1 filters, padding larger than one.  The last
+# two are 1x1 convolutions whose pixel counts are multiples of 8: they run as
+# batched GEMMs over the NCHW tensors (ragged row tiles: 272 and 32 channels).
 SHAPES = [(4, 16, 12, 12, 32, 3, 1, 1), (2, 64, 17, 17, 128, 3, 2, 1), (2, 24, 9, 9, 200, 5, 1, 2),
-          (3, 128, 10, 7, 64, 1, 1, 0), (2, 32, 15, 15, 48, 3, 2, 0), (1, 16, 8, 8, 16, 7, 1, 3)]
+          (3, 128, 10, 7, 64, 1, 1, 0), (2, 32, 15, 15, 48, 3, 2, 0), (1, 16, 8, 8, 16, 7, 1, 3),
+          (2, 64, 8, 12, 96, 1, 1, 0), (3, 32, 16, 16, 272, 1, 1, 0)]
 
 
 @pytest.mark.parametrize("shape", SHAPES)
