@@ -272,20 +272,30 @@ __device__ __forceinline__ void multimem_st_f32x4(float* mc, const float4& v) {
                "f"(v.z), "f"(v.w)
                : "memory");
 }
-// Four bf16 (8 bytes) stored as two 32-bit lanes: the store moves bits.
-__device__ __forceinline__ void multimem_st_bf16x4(__nv_bfloat16* mc, const float4& v) {
-  const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
-  asm volatile("multimem.st.relaxed.sys.global.v2.f32 [%0], {%1, %2};" ::"l"(mc),
-               "f"(__uint_as_float(*reinterpret_cast<const uint32_t*>(&lo))),
-               "f"(__uint_as_float(*reinterpret_cast<const uint32_t*>(&hi)))
-               : "memory");
-}
 // Orders this thread's accesses through one virtual alias of memory (the
 // unicast or the multicast mapping) against its accesses through the other.
 __device__ __forceinline__ void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
 
+// Eight bf16 (16 bytes) stored as four 32-bit lanes: the store moves bits.
+__device__ __forceinline__ void multimem_st_bf16x8(__nv_bfloat16* mc, const float4& v0, const float4& v1) {
+  const __nv_bfloat162 a = __floats2bfloat162_rn(v0.x, v0.y), b = __floats2bfloat162_rn(v0.z, v0.w);
+  const __nv_bfloat162 c = __floats2bfloat162_rn(v1.x, v1.y), d = __floats2bfloat162_rn(v1.z, v1.w);
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc),
+               "f"(__uint_as_float(*reinterpret_cast<const uint32_t*>(&a))),
+               "f"(__uint_as_float(*reinterpret_cast<const uint32_t*>(&b))),
+               "f"(__uint_as_float(*reinterpret_cast<const uint32_t*>(&c))),
+               "f"(__uint_as_float(*reinterpret_cast<const uint32_t*>(&d)))
+               : "memory");
+}
+
+// NVLS two-shot: my shard's gradients summed by the switch (multimem
+// ld_reduce through the multicast mapping), the optimizer applied, and the
+// new parameters multicast to every rank with one store.  A thread handles
+// units of eight consecutive elements (two 16-byte reduce loads, one 16-byte
+// multicast store of bf16 parameters), U units in flight.  The range and the
+// shards are multiples of 8 elements (checked on the host).
 template <typename TV, int U>
-__global__ void __launch_bounds__(128, 8) fused_nvls_ar_opt_kernel(FusedARArgs a) {
+__global__ void __launch_bounds__(128, 4) fused_nvls_ar_opt_kernel(FusedARArgs a) {
   const uint32_t epoch = (uint32_t)(*a.epoch_ptr);
   if (!ready_barrier(a, epoch)) return;
   fence_proxy_alias();  // the peers' gradients were written through their unicast mappings
@@ -295,41 +305,52 @@ __global__ void __launch_bounds__(128, 8) fused_nvls_ar_opt_kernel(FusedARArgs a
   const int64_t shard = ((n + a.world - 1) / a.world + 63) / 64 * 64;
   const int64_t lo = min(n, shard * a.rank), hi = min(n, lo + shard);
   const int64_t base = a.start + lo;
-  const int64_t nvec = (hi - lo) / 4;
+  const int64_t nunit = (hi - lo) / 8;
   const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const float* mg = reinterpret_cast<const float*>(a.mc_grads) + base;
-  float* mst = a.master + base;
-  float* mm = a.m ? a.m + base : nullptr;
-  float* vv = a.v ? a.v + base : nullptr;
+  float4* mst = reinterpret_cast<float4*>(a.master + base);
+  float4* mm = a.m ? reinterpret_cast<float4*>(a.m + base) : nullptr;
+  float4* vv = a.v ? reinterpret_cast<float4*>(a.v + base) : nullptr;
   const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int64_t v0 = tid; v0 < nvec; v0 += stride * U) {
-    float4 g[U], w[U], m4[U], v4[U];
+  for (int64_t u0 = tid; u0 < nunit; u0 += stride * U) {
+    float4 g[U][2], w[U][2], m4[U][2], v4[U][2];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int64_t vi = v0 + u * stride;
-      g[u] = vi < nvec ? multimem_ld_reduce_f32x4(mg + vi * 4) : z4;
-      w[u] = vi < nvec ? reinterpret_cast<const float4*>(mst)[vi] : z4;
-      m4[u] = (mm && vi < nvec) ? reinterpret_cast<const float4*>(mm)[vi] : z4;
-      v4[u] = (vv && vi < nvec) ? reinterpret_cast<const float4*>(vv)[vi] : z4;
+      const int64_t ui = u0 + u * stride;
+      const bool on = ui < nunit;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int64_t q = ui * 2 + e;  // float4 index
+        g[u][e] = on ? multimem_ld_reduce_f32x4(mg + q * 4) : z4;
+        w[u][e] = on ? mst[q] : z4;
+        m4[u][e] = (mm && on) ? mm[q] : z4;
+        v4[u][e] = (vv && on) ? vv[q] : z4;
+      }
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int64_t vi = v0 + u * stride;
-      if (vi >= nvec) continue;
-      opt_apply(a.kind, h, w[u].x, g[u].x * gs, m4[u].x, v4[u].x);
-      opt_apply(a.kind, h, w[u].y, g[u].y * gs, m4[u].y, v4[u].y);
-      opt_apply(a.kind, h, w[u].z, g[u].z * gs, m4[u].z, v4[u].z);
-      opt_apply(a.kind, h, w[u].w, g[u].w * gs, m4[u].w, v4[u].w);
-      if (mm) reinterpret_cast<float4*>(mm)[vi] = m4[u];
-      if (vv) reinterpret_cast<float4*>(vv)[vi] = v4[u];
+      const int64_t ui = u0 + u * stride;
+      if (ui >= nunit) continue;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        opt_apply(a.kind, h, w[u][e].x, g[u][e].x * gs, m4[u][e].x, v4[u][e].x);
+        opt_apply(a.kind, h, w[u][e].y, g[u][e].y * gs, m4[u][e].y, v4[u][e].y);
+        opt_apply(a.kind, h, w[u][e].z, g[u][e].z * gs, m4[u][e].z, v4[u][e].z);
+        opt_apply(a.kind, h, w[u][e].w, g[u][e].w * gs, m4[u][e].w, v4[u][e].w);
+        if (mm) mm[ui * 2 + e] = m4[u][e];
+        if (vv) vv[ui * 2 + e] = v4[u][e];
+      }
       if (a.values_are_master) {
         // fp32 mode: the master is the compute copy and lives in the
         // multicast buffer; one store reaches every rank (this one included).
-        multimem_st_f32x4(reinterpret_cast<float*>(a.mc_values) + base + vi * 4, w[u]);
+        float* mv = reinterpret_cast<float*>(a.mc_values) + base + ui * 8;
+        multimem_st_f32x4(mv, w[u][0]);
+        multimem_st_f32x4(mv + 4, w[u][1]);
       } else {
-        reinterpret_cast<float4*>(mst)[vi] = w[u];
-        multimem_st_bf16x4(reinterpret_cast<__nv_bfloat16*>(a.mc_values) + base + vi * 4, w[u]);
+        mst[ui * 2] = w[u][0];
+        mst[ui * 2 + 1] = w[u][1];
+        multimem_st_bf16x8(reinterpret_cast<__nv_bfloat16*>(a.mc_values) + base + ui * 8, w[u][0], w[u][1]);
       }
     }
   }
@@ -717,6 +738,8 @@ void fused_allreduce_optimizer_nvls(const FusedARArgs& a, DType value_dt, int ct
              "NVLS all-reduce: fp32 values must be the master copy, bf16 values a mirror");
   DLVK_CHECK((reinterpret_cast<uintptr_t>(a.mc_grads) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.mc_values) & 15) == 0,
              "NVLS all-reduce: multicast addresses must be 16-byte aligned");
+  DLVK_CHECK(a.start % 64 == 0 && (a.end - a.start) % 64 == 0,
+             "NVLS all-reduce: the range must start and end on 64-element boundaries");
   const int grid = std::max(1, ctas);
   if (value_dt == DType::F32) fused_nvls_ar_opt_kernel<float, 2><<<grid, 128, 0, s>>>(a);
   else fused_nvls_ar_opt_kernel<__nv_bfloat16, 2><<<grid, 128, 0, s>>>(a);

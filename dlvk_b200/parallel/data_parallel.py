@@ -90,17 +90,19 @@ class DataParallel:
                     break
                 tail.add(id(p))
                 acc += e - s
+        # Buckets tile the flat store without gaps: each one ends where the
+        # next parameter starts, so it also covers the 64-element alignment
+        # padding after its last parameter (zero gradients, values that stay
+        # zero) and every bucket is a whole number of 64-element blocks.
         buckets, cur, start = [], [], 0
-        end = 0
         in_tail = False
         for p, s, e in ranges:
             lim = tail_limit if id(p) in tail else limit
             if cur and ((e - start) > lim or (id(p) in tail) != in_tail):
-                buckets.append(Bucket(len(buckets), start, end, cur))
+                buckets.append(Bucket(len(buckets), start, s, cur))
                 cur, start = [], s
             in_tail = id(p) in tail
             cur.append(p)
-            end = e
         if cur:
             buckets.append(Bucket(len(buckets), start, self.store.numel, cur))
         return buckets
