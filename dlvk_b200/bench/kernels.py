@@ -79,6 +79,20 @@ def main():
         for r in rows:
             print(json.dumps(r), flush=True)
         return
+    # Same-size anchors on the same box: a plain device copy of x (read 16 MB,
+    # write 16 MB) and PyTorch's own LayerNorm forward / backward.
+    yc = torch.empty_like(x)
+    report("[anchor] copy x -> y (torch)", time_fn(lambda: yc.copy_(x), a.iters), 2 * R * D * 2)
+    xt = x.detach().clone().requires_grad_(True)
+    gt = gamma.detach().bfloat16().requires_grad_(True)  # torch wants the input's dtype
+    bt = beta.detach().bfloat16().requires_grad_(True)
+    report("[anchor] layernorm_fwd (torch)",
+           time_fn(lambda: torch.nn.functional.layer_norm(x, (D,), gt.detach(), bt.detach(), 1e-5), a.iters),
+           2 * R * D * 2 + R * 8)
+    yt = torch.nn.functional.layer_norm(xt, (D,), gt, bt, 1e-5)
+    report("[anchor] layernorm_bwd (torch)",
+           time_fn(lambda: torch.autograd.grad(yt, (xt, gt, bt), dy, retain_graph=True), a.iters),
+           3 * R * D * 2 + R * 8)
     y, mean, rstd = NN.layernorm_fwd(x, gamma, beta, 1e-5)
     report("layernorm_fwd", time_fn(lambda: NN.layernorm_fwd(x, gamma, beta, 1e-5), a.iters), 2 * R * D * 2 + R * 8)
     report("layernorm_bwd+dres", time_fn(lambda: NN.layernorm_bwd(x, gamma, mean, rstd, dy, dg, db, False, dres),

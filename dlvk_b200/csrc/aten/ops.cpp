@@ -342,7 +342,8 @@ at::Tensor gemm_op(const at::Tensor& A, const at::Tensor& B, c10::optional<at::T
                    double alpha, double beta, c10::optional<at::Tensor> out, c10::optional<at::ScalarType> out_dtype,
                    int64_t force_path, int64_t max_ctas, c10::optional<at::Tensor> residual,
                    c10::optional<at::Tensor> relu_mask, c10::optional<at::Tensor> colsum_out,
-                   double colsum_scale, bool colsum_accumulate) {
+                   double colsum_scale, bool colsum_accumulate, c10::optional<at::Tensor> relu_bits_out,
+                   c10::optional<at::Tensor> relu_bits) {
   check_cuda(A, "A");
   check_cuda(B, "B");
   TORCH_CHECK(A.scalar_type() == B.scalar_type(), "dlvk.gemm: A and B must have the same dtype");
@@ -393,10 +394,28 @@ at::Tensor gemm_op(const at::Tensor& A, const at::Tensor& B, c10::optional<at::T
     if (nd >= 3) a.batch_stride_m = Mk.stride(0);
     if (nd == 4) a.batch2_stride_m = Mk.stride(1);
   }
+  // ReLU bitmask [M, ceil(N / 32)] int32 words (2-D GEMMs)
+  auto bits_arg = [&](const c10::optional<at::Tensor>& t, const char* what) -> at::Tensor {
+    if (!t.has_value()) return at::Tensor();
+    TORCH_CHECK(nd == 2, "dlvk.gemm: ", what, " needs a 2-D GEMM");
+    TORCH_CHECK(t->scalar_type() == at::kInt && t->dim() == 2 && t->size(0) == M && t->size(1) >= (N + 31) / 32 &&
+                    t->stride(1) == 1 && t->device() == C.device(),
+                "dlvk.gemm: ", what, " must be int32 [M, >= ceil(N / 32)] with unit column stride on C's device");
+    a.ldbits = t->stride(0);
+    return *t;
+  };
+  at::Tensor bits_o = bits_arg(relu_bits_out, "relu_bits_out");
+  at::Tensor bits_i = bits_arg(relu_bits, "relu_bits");
+  if (bits_o.defined()) a.relu_bits_out = reinterpret_cast<uint32_t*>(bits_o.data_ptr<int32_t>());
+  if (bits_i.defined()) a.relu_bits = reinterpret_cast<const uint32_t*>(bits_i.data_ptr<int32_t>());
+  TORCH_CHECK(!(bits_o.defined() && bits_i.defined()) || bits_o.stride(0) == bits_i.stride(0),
+              "dlvk.gemm: relu_bits_out and relu_bits with different row strides");
+
   a.act = (int)act;
   if (M == 0 || N == 0) return C;
   if (K == 0) {
     // Degenerate: C = act(beta*C + bias + residual).  Rare; do it with ATen.
+    TORCH_CHECK(!bits_o.defined() && !bits_i.defined(), "dlvk.gemm: ReLU bitmask with K = 0");
     if (beta == 0.0) C.zero_();
     else C.mul_(beta);
     if (bias.has_value()) C.add_(bc.to(C.scalar_type()));
@@ -433,6 +452,7 @@ at::Tensor gemm_op(const at::Tensor& A, const at::Tensor& B, c10::optional<at::T
     gemm_tc(to_dtype(C), a, stream(), device_error_word(), (int)max_ctas, wsf > 0 ? ws.data_ptr<float>() : nullptr,
             wsf);
   } else {
+    if (bits_o.defined()) bits_o.zero_();  // the SIMT kernel sets bits with atomic ORs
     gemm_simt(to_dtype(A), to_dtype(C), a, stream());
   }
   if (colsum_out.has_value()) {

@@ -35,7 +35,8 @@ void register_ops(py::module& m) {
         py::arg("alpha") = 1.0, py::arg("beta") = 0.0, py::arg("out") = py::none(), py::arg("out_dtype") = py::none(),
         py::arg("force_path") = 0, py::arg("max_ctas") = 0, py::arg("residual") = py::none(),
         py::arg("relu_mask") = py::none(), py::arg("colsum_out") = py::none(), py::arg("colsum_scale") = 1.0,
-        py::arg("colsum_accumulate") = false);
+        py::arg("colsum_accumulate") = false, py::arg("relu_bits_out") = py::none(),
+        py::arg("relu_bits") = py::none());
   m.def("gemm_tc_ok", &gemm_tc_ok);
   m.def("gemm_tf32_ok", &gemm_tf32_ok);
   m.def("set_fp32_gemm_mode", &set_fp32_gemm_mode);

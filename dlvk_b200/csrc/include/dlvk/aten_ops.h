@@ -39,7 +39,7 @@ void set_fp32_gemm_mode(int mode);
 bool gemm_tf32_ok(const at::Tensor& A, const at::Tensor& B);
 void gemm_tf32_op(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const GemmArgs& args, bool three_pass,
                   int max_ctas);
-at::Tensor gemm_op(const at::Tensor& A, const at::Tensor& B, c10::optional<at::Tensor> bias, int64_t act, double alpha, double beta, c10::optional<at::Tensor> out, c10::optional<at::ScalarType> out_dtype, int64_t force_path, int64_t max_ctas, c10::optional<at::Tensor> residual, c10::optional<at::Tensor> relu_mask, c10::optional<at::Tensor> colsum_out, double colsum_scale, bool colsum_accumulate);
+at::Tensor gemm_op(const at::Tensor& A, const at::Tensor& B, c10::optional<at::Tensor> bias, int64_t act, double alpha, double beta, c10::optional<at::Tensor> out, c10::optional<at::ScalarType> out_dtype, int64_t force_path, int64_t max_ctas, c10::optional<at::Tensor> residual, c10::optional<at::Tensor> relu_mask, c10::optional<at::Tensor> colsum_out, double colsum_scale, bool colsum_accumulate, c10::optional<at::Tensor> relu_bits_out = c10::nullopt, c10::optional<at::Tensor> relu_bits = c10::nullopt);
 bool gemm_tc_ok(const at::Tensor& A, const at::Tensor& B);
 void optim_advance_op(const at::Tensor& hyper);
 void optim_update_op(int64_t kind, const at::Tensor& hyper, const at::Tensor& p, const at::Tensor& grad, c10::optional<at::Tensor> m, c10::optional<at::Tensor> v, c10::optional<at::Tensor> p_bf16, double extra_scale, int64_t max_ctas);

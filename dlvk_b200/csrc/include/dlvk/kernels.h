@@ -84,6 +84,14 @@ struct GemmArgs {
   // rows are channels (1x1 convolution in NCHW as a batched GEMM).  Tensor-
   // core path only.
   const float* row_bias = nullptr;
+  // Optional ReLU bitmask, one bit per output element: bit n % 32 of word
+  // [m * ldbits + n / 32].  relu_bits_out is written by a forward GEMM (bit
+  // set where the output, after the activation, is > 0); relu_bits zeroes
+  // the output where the bit is clear -- the backward of that ReLU, reading
+  // 1/16 of the bytes of a bf16 mask.  2-D GEMMs only.
+  uint32_t* relu_bits_out = nullptr;
+  const uint32_t* relu_bits = nullptr;
+  int64_t ldbits = 0;
 };
 void gemm_simt(DType in_dt, DType out_dt, const GemmArgs& a, cudaStream_t s);
 bool gemm_tc_supported(const GemmArgs& a);

@@ -38,8 +38,6 @@
 // Every mbarrier wait is bounded (mbar_wait: error word + early exit).
 #include <cuda.h>
 
-#include <cstdlib>
-
 #include "dlvk/common.h"
 #include "dlvk/kernels.h"
 #include "dlvk/sm100.h"
@@ -63,24 +61,6 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 // [128 x 64] sub-tiles (the layout TMA SWIZZLE_128B produces).
 __device__ __forceinline__ uint32_t sw_off(int r, int c) {
   return (uint32_t)((c >> 3) * 16384 + (r >> 3) * 1024 + (r & 7) * 128 + (((c & 7) ^ (r & 7)) << 4));
-}
-
-// 2^x on the FMA pipe, for x <= 128: Cody-Waite style reduction x = n + f,
-// f in [-0.5, 0.5], with n found by adding 1.5 * 2^23 (round to nearest
-// leaves n in the low mantissa bits), then a degree-3 polynomial for 2^f and
-// n added into the exponent field.  The coefficients are this file's own
-// least-squares fit of 2^f in relative error at Chebyshev nodes (max
-// relative error 7.8e-5, far below bf16's 2^-9 rounding of P).  Inputs are
-// clamped at -126 so the result stays a normal number; exp2(-126) is as good
-// as zero next to the row's largest term, 1.
-__device__ __forceinline__ float fma_exp2(float x) {
-  x = fmaxf(x, -126.f);
-  const float t = x + 12582912.f;
-  const float f = x - (t - 12582912.f);
-  float q = fmaf(0.05508868396282196f, f, 0.24260404706001282f);
-  q = fmaf(q, f, 0.6932762265205383f);
-  q = fmaf(q, f, 0.9999289512634277f);
-  return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
 }
 
 // 2^x with the hardware approximation (ex2.approx.ftz: flushes denormal
@@ -129,10 +109,6 @@ constexpr int FWD_KV_STAGES = 4;
 constexpr int FWD_THREADS = 64 + 2 * 128;
 constexpr int FWD_SMEM = 2 * TILE + FWD_KV_STAGES * 2 * TILE + 2 * 2 * TILE + 256 + 1024;
 
-// EMU: of every four pairs of scores, EMU pairs take their exponentials on the
-// FMA pipe (fma_exp2) and the rest on the MUFU unit (ex2.approx), which with
-// head dim 64 is the busiest pipe of the softmax.
-template <int EMU>
 __global__ void __launch_bounds__(FWD_THREADS, 1) flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, FwdP p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -341,11 +317,8 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) flash_fwd_kernel(const __grid_
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
-            const float x0 = fmaf(__uint_as_float(sc[i]), p.c, -m_new);
-            const float x1 = fmaf(__uint_as_float(sc[i + 1]), p.c, -m_new);
-            const bool emu = ((i >> 1) & 3) < EMU;
-            const float e0 = emu ? fma_exp2(x0) : hw_exp2(x0);
-            const float e1 = emu ? fma_exp2(x1) : hw_exp2(x1);
+            const float e0 = hw_exp2(fmaf(__uint_as_float(sc[i]), p.c, -m_new));
+            const float e1 = hw_exp2(fmaf(__uint_as_float(sc[i + 1]), p.c, -m_new));
             sp8[i & 7] += e0;
             sp8[(i + 1) & 7] += e1;
             pk[i >> 1] = pack2(e0, e1);
@@ -838,12 +811,7 @@ void flash_attention_fwd(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* ls
   const int E = H * FD;
   CUtensorMap tm = tmap::bf16_2d_sw128(qkv, (uint64_t)3 * E, (uint64_t)B * S, (uint64_t)3 * E, FT);
   FwdP p{out, lse, B, S, H, E, scale * 1.4426950408889634f, err};
-  static const int emu = [] {
-    const char* e = std::getenv("DLVK_ATTN_EXP2_FMA");  // pairs of four on the FMA pipe: 0, 1 or 2
-    const int v = e ? std::atoi(e) : 0;
-    return v < 0 ? 0 : (v > 2 ? 2 : v);
-  }();
-  auto kern = emu == 2 ? flash_fwd_kernel<2> : (emu == 1 ? flash_fwd_kernel<1> : flash_fwd_kernel<0>);
+  auto kern = flash_fwd_kernel;
   const int adev = current_device_slot();
   static bool attr[kMaxDevices] = {};  // per device: the attribute belongs to each device's context
   if (!attr[adev]) {

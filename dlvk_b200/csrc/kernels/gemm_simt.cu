@@ -98,6 +98,9 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs a) {
       if (a.act == ACT_RELU) v = fmaxf(v, 0.f);
       else if (a.act == ACT_GELU) v = 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
       if (Mk && !(to_f32(Mk[gm * a.ldm + gn]) > 0.f)) v = 0.f;
+      if (a.relu_bits && !((a.relu_bits[gm * a.ldbits + (gn >> 5)] >> (gn & 31)) & 1u)) v = 0.f;
+      // the caller clears the bitmask before this path
+      if (a.relu_bits_out && v > 0.f) atomicOr(&a.relu_bits_out[gm * a.ldbits + (gn >> 5)], 1u << (gn & 31));
       *cp = from_f32<TC>(v);
     }
   }

@@ -68,6 +68,9 @@ struct TcParams {
                            // 2: same boxes, added into fp32 C (split-K partials reduced in L2)
   int a_bcast;             // 1: one A for every batch entry (its map has no batch extent)
   const float* row_bias;   // fp32 bias per output row, or null
+  uint32_t* bits_out;      // ReLU bitmask written (plain / TMA-store epilogues), or null
+  const uint32_t* bits_in; // ReLU bitmask applied (staged epilogue), or null
+  int64_t ldbits;          // 32-bit words per bitmask row
 };
 
 // PAIR: a 2-CTA cluster shares one 256 x BN tile (tcgen05 cta_group::2);
@@ -174,6 +177,16 @@ __device__ __forceinline__ void add_bias(const void* bias, bool f32, int n, int 
   }
 }
 
+// Word of the ReLU bitmask for one row's 32 columns [n0, n0 + 32): bit j set
+// where v[j] > 0 (after the activation); columns past N stay clear.
+__device__ __forceinline__ void store_bits(const TcParams& p, int row, int n0, const float* v) {
+  uint32_t w = 0;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) w |= (v[j] > 0.f ? 1u : 0u) << j;
+  if (p.N - n0 < 32) w &= (1u << (p.N - n0)) - 1u;
+  p.bits_out[(int64_t)row * p.ldbits + (n0 >> 5)] = w;
+}
+
 template <typename T> __device__ __forceinline__ float ld_elem(const void* p, int64_t i) {
   return to_f32(reinterpret_cast<const T*>(p)[i]);
 }
@@ -205,29 +218,54 @@ __device__ __forceinline__ void epi_store(const TcParams& p, const float* stg, i
   // Fast path: whole 16-byte vectors everywhere.  All global reads of the
   // chunk (beta*C, residual, mask) are issued before any is consumed, so the
   // chunk pays one memory latency instead of one per pass.
-  // Exactly one auxiliary input (beta*C, residual or mask) is prefetched.
+  // ReLU bitmask: lane l loads the chunk's word of row row0 + l; the lanes
+  // that handle a row take its bits with a shuffle.
+  uint32_t bw = 0;
+  if (p.bits_in) {
+    const int r = row0 + lane;
+    if (r < p.M && n0 < p.N) bw = p.bits_in[(int64_t)r * p.ldbits + (n0 >> 5)];
+  }
   const int naux = (p.beta != 0.f) + (p.R != nullptr) + (p.Mk != nullptr);
-  const bool fast = naux == 1 && valid == VEC && p.vec_ok && (!p.R || p.r_vec) && (!p.Mk || p.m_vec) &&
-                    row0 + 32 <= p.M;
+  // Exactly one auxiliary input (beta*C, residual or mask) is prefetched.
+  const bool fast = naux + (p.bits_in ? 1 : 0) == 1 && valid == VEC && p.vec_ok && (!p.R || p.r_vec) &&
+                    (!p.Mk || p.m_vec) && row0 + 32 <= p.M;
   if (fast) {
-    const T* abase;
-    int64_t aoff, ald;
-    if (p.beta != 0.f) {
-      abase = reinterpret_cast<const T*>(p.C); aoff = cb; ald = p.ldc;
-    } else if (p.R) {
-      abase = reinterpret_cast<const T*>(p.R); aoff = rb; ald = p.ldr;
-    } else {
-      abase = reinterpret_cast<const T*>(p.Mk); aoff = mb; ald = p.ldm;
-    }
     uint4 av[NP];
+    if (p.bits_in) {
+      // the bits as a 0 / 1 mask of this lane's VEC elements
 #pragma unroll
-    for (int ps = 0; ps < NP; ++ps)
-      av[ps] = *reinterpret_cast<const uint4*>(abase + aoff + (int64_t)(row0 + ps * RPP + rr) * ald + n);
+      for (int ps = 0; ps < NP; ++ps) {
+        const uint32_t mb = __shfl_sync(0xffffffffu, bw, ps * RPP + rr) >> (cg * VEC);
+        uint32_t w[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (VEC == 8) {  // two bf16 per word (1.0 = 0x3F80)
+            w[q] = (((mb >> (2 * q)) & 1u) ? 0x3F80u : 0u) | (((mb >> (2 * q + 1)) & 1u) ? 0x3F800000u : 0u);
+          } else {         // one fp32 per word
+            w[q] = ((mb >> q) & 1u) ? 0x3F800000u : 0u;
+          }
+        }
+        av[ps] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    } else {
+      const T* abase;
+      int64_t aoff, ald;
+      if (p.beta != 0.f) {
+        abase = reinterpret_cast<const T*>(p.C); aoff = cb; ald = p.ldc;
+      } else if (p.R) {
+        abase = reinterpret_cast<const T*>(p.R); aoff = rb; ald = p.ldr;
+      } else {
+        abase = reinterpret_cast<const T*>(p.Mk); aoff = mb; ald = p.ldm;
+      }
+#pragma unroll
+      for (int ps = 0; ps < NP; ++ps)
+        av[ps] = *reinterpret_cast<const uint4*>(abase + aoff + (int64_t)(row0 + ps * RPP + rr) * ald + n);
+    }
+    const int mode = p.beta != 0.f ? 0 : (p.R ? 1 : 2);
     float bv[VEC];
 #pragma unroll
     for (int k = 0; k < VEC; ++k) bv[k] = 0.f;
     if (p.bias) add_bias<VEC>(p.bias, p.bias_f32, n, valid, bv);
-    const int mode = p.beta != 0.f ? 0 : (p.R ? 1 : 2);
     float cs[VEC];
 #pragma unroll
     for (int k = 0; k < VEC; ++k) cs[k] = 0.f;
@@ -279,6 +317,7 @@ __device__ __forceinline__ void epi_store(const TcParams& p, const float* stg, i
   for (int pass = 0; pass < NP; ++pass) {
     const int rl = pass * RPP + rr;
     const int row = row0 + rl;
+    const uint32_t mbits = p.bits_in ? (__shfl_sync(0xffffffffu, bw, rl) >> (cg * VEC)) : ~0u;
     if (row >= p.M || valid == 0) continue;
     float v[VEC];
 #pragma unroll
@@ -309,6 +348,8 @@ __device__ __forceinline__ void epi_store(const TcParams& p, const float* stg, i
 #pragma unroll
       for (int k = 0; k < VEC; ++k) v[k] = o[k] > 0.f ? v[k] : 0.f;
     }
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) v[k] = ((mbits >> k) & 1u) ? v[k] : 0.f;
     T* dst = reinterpret_cast<T*>(p.C) + ci;
     if (p.vec_ok && valid == VEC) {
       uint4 u;
@@ -601,7 +642,7 @@ __global__ void __launch_bounds__(320, 1)
     const int q = warp & 3;
     const int half = ew >> 2;
     float* stg = epi + ew * (32 * 33);
-    const bool staged = (p.R != nullptr) || (p.Mk != nullptr) || (p.beta != 0.f);
+    const bool staged = (p.R != nullptr) || (p.Mk != nullptr) || (p.beta != 0.f) || (p.bits_in != nullptr);
     constexpr int NCH = BN / 64;  // 32-column chunks per warp
     int acc = 0, ecount = 0;
     uint32_t acc_phase = 0;
@@ -672,6 +713,7 @@ __global__ void __launch_bounds__(320, 1)
             for (int j = 0; j < 32; ++j) v[j] = fmaf(__uint_as_float(r[i & 1][j]), p.alpha, rbv);
             if (p.bias && n0 < p.N) add_bias<32>(p.bias, p.bias_f32, n0, min(32, p.N - n0), v);
             apply_act<32>(p.act, v);
+            if (p.bits_out && n0 < p.N && row0 + lane < p.M) store_bits(p, row0 + lane, n0, v);
             // Boxes start on 1024-byte boundaries (the swizzled box layout is
             // defined on aligned addresses).
             if (opens) {
@@ -743,6 +785,7 @@ __global__ void __launch_bounds__(320, 1)
             }
             if (p.bias) add_bias<32>(p.bias, p.bias_f32, n0, min(32, p.N - n0), v);
             apply_act<32>(p.act, v);
+            if (p.bits_out) store_bits(p, row, n0, v);
             const bool full = (n0 + 32 <= p.N) && p.vec_ok;
             if (p.out_f32) {
               float* dst = reinterpret_cast<float*>(p.C) + cb + (int64_t)row * p.ldc + n0;
@@ -941,6 +984,8 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
         !(to_f32(reinterpret_cast<const T*>(a.relu_mask)[bo * a.batch_stride_m + bi * a.batch2_stride_m + m * a.ldm + n]) >
           0.f))
       v = 0.f;
+    if (a.relu_bits && !((a.relu_bits[m * a.ldbits + (n >> 5)] >> (n & 31)) & 1u)) v = 0.f;
+
     *c = from_f32<T>(v);
   }
 }
@@ -1048,7 +1093,8 @@ bool split_red_enabled() {
 bool split_red_ok(DType out_dt, const GemmArgs& a) {
   return split_red_enabled() && tma_c_enabled() && out_dt == DType::F32 && a.batch == 1 && a.batch2 == 1 &&
          (a.beta == 0.f || a.beta == 1.f) && a.bias == nullptr && a.residual == nullptr &&
-         a.relu_mask == nullptr && a.act == ACT_NONE && al16(a.C) && (a.ldc * 4) % 16 == 0 &&
+         a.relu_mask == nullptr && a.relu_bits == nullptr && a.relu_bits_out == nullptr && a.act == ACT_NONE &&
+         al16(a.C) && (a.ldc * 4) % 16 == 0 &&
          a.ldc * 4 < (1LL << 40) && a.N % 4 == 0;
 }
 }  // namespace
@@ -1064,7 +1110,8 @@ bool gemm_tc_colsum_ok(DType out_dt, const GemmArgs& a) {
   auto rows16 = [&](const void* p, int64_t ld) {
     return p == nullptr || (al16(p) && (ld * esz) % 16 == 0);
   };
-  return naux == 1 && a.batch == 1 && a.batch2 == 1 && a.M % 32 == 0 && a.N % 32 == 0 && al16(a.C) &&
+  return (naux == 1 || (naux == 0 && a.relu_bits != nullptr)) && a.batch == 1 && a.batch2 == 1 && a.M % 32 == 0 &&
+         a.N % 32 == 0 && al16(a.C) &&
          (a.ldc * esz) % 16 == 0 && rows16(a.residual, a.ldr) && rows16(a.relu_mask, a.ldm);
 }
 
@@ -1170,6 +1217,13 @@ void gemm_tc_impl(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err
     DLVK_CHECK(gemm_tc_colsum_ok(out_dt, a), "gemm_tc: column sums need the staged fast-path layout");
     splits = 1;  // the sums are taken over final outputs
   }
+  if (a.relu_bits != nullptr || a.relu_bits_out != nullptr)
+    DLVK_CHECK(a.batch == 1 && a.batch2 == 1 && a.ldbits >= (a.N + 31) / 32, "gemm_tc: ReLU bitmask needs a 2-D GEMM");
+  if (a.relu_bits_out != nullptr) {
+    DLVK_CHECK(a.residual == nullptr && a.relu_mask == nullptr && a.relu_bits == nullptr && a.beta == 0.f,
+               "gemm_tc: the ReLU bitmask is written by plain epilogues only");
+    splits = 1;  // the bits are taken from final outputs
+  }
   if (!red && (workspace == nullptr || workspace_floats < (int64_t)splits * a.M * a.N * a.batch * a.batch2))
     splits = 1;
   pair = pair && max_ctas != 1;
@@ -1235,6 +1289,9 @@ void gemm_tc_impl(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err
   p.bias_f32 = (a.bias_dtype == (int)DType::F32);
   p.row_bias = a.row_bias;
   p.a_bcast = a_bcast ? 1 : 0;
+  p.bits_out = a.relu_bits_out;
+  p.bits_in = a.relu_bits;
+  p.ldbits = a.ldbits;
   p.act = a.act;
   p.err = err;
   p.colsum = a.colsum;
@@ -1277,6 +1334,7 @@ void gemm_tc_impl(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err
     p.beta = 0.f;
     p.bias = nullptr;
     p.row_bias = nullptr;
+    p.bits_in = nullptr;
     p.R = nullptr;
     p.Mk = nullptr;
     p.act = ACT_NONE;

@@ -167,20 +167,44 @@ def permute4(x: torch.Tensor, perm) -> torch.Tensor:
 
 
 # ---------------------------------------------------------------- GEMM
+def relu_bits_like(m: int, n: int, device) -> torch.Tensor:
+    """An int32 [m, ceil(n / 32)] buffer for a GEMM's ReLU bitmask."""
+    return torch.empty(m, (n + 31) // 32, dtype=torch.int32, device=device)
+
+
+def _pack_bits(pos: torch.Tensor, words: int) -> torch.Tensor:
+    """[m, n] bool -> [m, words] int32, bit j of word w = pos[:, 32 w + j]."""
+    m, n = pos.shape
+    pad = torch.zeros(m, words * 32, dtype=torch.int64, device=pos.device)
+    pad[:, :n] = pos.to(torch.int64)
+    shifts = torch.arange(32, dtype=torch.int64, device=pos.device)
+    w = (pad.reshape(m, words, 32) << shifts).sum(-1)
+    return torch.where(w >= 2 ** 31, w - 2 ** 32, w).to(torch.int32)
+
+
+def _unpack_bits(bits: torch.Tensor, n: int) -> torch.Tensor:
+    shifts = torch.arange(32, dtype=torch.int64, device=bits.device)
+    b = (bits.to(torch.int64) & 0xFFFFFFFF).unsqueeze(-1) >> shifts
+    return (b & 1).reshape(bits.shape[0], -1)[:, :n].bool()
+
+
 def gemm(a: torch.Tensor, b: torch.Tensor, bias=None, act: int = ACT_NONE, alpha: float = 1.0, beta: float = 0.0,
          out=None, out_dtype=None, residual=None, relu_mask=None, colsum_out=None, colsum_scale: float = 1.0,
-         colsum_accumulate: bool = False) -> torch.Tensor:
+         colsum_accumulate: bool = False, relu_bits_out=None, relu_bits=None) -> torch.Tensor:
     """act(alpha * a @ b + beta * out + bias + residual), zeroed where
     relu_mask <= 0.  a: [M,K], [B,M,K] or [B,B2,M,K] (any strides), b
     likewise.  Transposes and head splits are views; the tensor-core path is
     used whenever the layout allows it.  With colsum_out (fp32 [N], 2-D
     GEMMs) the column sums of the result, times colsum_scale, are written
     (or added, colsum_accumulate) there as well: the bias gradient of a layer
-    whose output gradient this GEMM produces."""
+    whose output gradient this GEMM produces.  relu_bits_out (int32
+    [M, ceil(N / 32)], relu_bits_like) receives one bit per output element,
+    set where the output is > 0; relu_bits zeroes the output where its bit is
+    clear (2-D GEMMs): a ReLU's backward from 1/16 of a bf16 mask's bytes."""
     if native(a):
         return N().gemm(a, b, bias=bias, act=act, alpha=alpha, beta=beta, out=out, out_dtype=out_dtype,
                         residual=residual, relu_mask=relu_mask, colsum_out=colsum_out, colsum_scale=colsum_scale,
-                        colsum_accumulate=colsum_accumulate)
+                        colsum_accumulate=colsum_accumulate, relu_bits_out=relu_bits_out, relu_bits=relu_bits)
     c = alpha * torch.matmul(a.float(), b.float())
     if beta != 0.0 and out is not None:
         c = c + beta * out.float()
@@ -191,6 +215,10 @@ def gemm(a: torch.Tensor, b: torch.Tensor, bias=None, act: int = ACT_NONE, alpha
     c = _act_ref(c, act)
     if relu_mask is not None:
         c = torch.where(relu_mask.float() > 0, c, torch.zeros_like(c))
+    if relu_bits is not None:
+        c = torch.where(_unpack_bits(relu_bits, c.shape[-1]), c, torch.zeros_like(c))
+    if relu_bits_out is not None:
+        relu_bits_out.copy_(_pack_bits(c > 0, relu_bits_out.shape[1]))
     if colsum_out is not None:
         s = c.reshape(-1, c.shape[-1]).sum(0) * colsum_scale
         if colsum_accumulate:

@@ -345,15 +345,17 @@ class TransformerBlockFn(torch.autograd.Function):
         a2 = _flat2(a)
         h = K.gemm(a2, at.w_o.value, residual=x2)
         h2, m2, r2 = NN.layernorm_fwd(h, ln2.gamma.master, ln2.beta.master, ln2.eps)
-        f = K.gemm(h2, f1.weight.value, bias=f1.bias.master, act=ACT_RELU)
+        # the ReLU's backward reads one bit per element instead of f
+        fbits = K.relu_bits_like(h2.shape[0], f1.weight.value.shape[1], h2.device)
+        f = K.gemm(h2, f1.weight.value, bias=f1.bias.master, act=ACT_RELU, relu_bits_out=fbits)
         y = K.gemm(f, f2.weight.value, bias=f2.bias.master, residual=h)
         ctx.blk, ctx.dims = blk, (B, S, H, D, scale)
-        ctx.save_for_backward(x2, h1, m1, r1, qkv, probs, a2, h, h2, m2, r2, f)
+        ctx.save_for_backward(x2, h1, m1, r1, qkv, probs, a2, h, h2, m2, r2, f, fbits)
         return y.reshape(B, S, E)
 
     @staticmethod
     def backward(ctx, gy):
-        x2, h1, m1, r1, qkv, probs, a2, h, h2, m2, r2, f = ctx.saved_tensors
+        x2, h1, m1, r1, qkv, probs, a2, h, h2, m2, r2, f, fbits = ctx.saved_tensors
         blk = ctx.blk
         B, S, H, D, scale = ctx.dims
         ln1, ln2, at, f1, f2 = blk.ln1, blk.ln2, blk.attn, blk.ff1, blk.ff2
@@ -373,10 +375,10 @@ class TransformerBlockFn(torch.autograd.Function):
         bgrad(f2.bias, g)
         # ReLU backward and the FF1 bias gradient (column sums) fused
         if _FUSE_COLSUM:
-            df = K.gemm(g, f2.weight.value.t(), relu_mask=f, colsum_out=f1.bias.grad,
+            df = K.gemm(g, f2.weight.value.t(), relu_bits=fbits, colsum_out=f1.bias.grad,
                         colsum_accumulate=f1.bias.take_accumulate_flag())
         else:
-            df = K.gemm(g, f2.weight.value.t(), relu_mask=f)
+            df = K.gemm(g, f2.weight.value.t(), relu_bits=fbits)
             bgrad(f1.bias, df)
         wgrad(f1.weight, h2.t(), df)
         dh2 = K.gemm(df, f1.weight.value.t())

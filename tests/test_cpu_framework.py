@@ -243,3 +243,22 @@ def test_tensor_facade_ops():
     assert float(r.data.abs().sum()) == 0.0
     d = t.divide(dl.Tensor([2, 3], device="cpu"))
     assert float(d.data[0, 0]) == 1e8
+
+
+def test_relu_bitmask_pack_roundtrip_cpu():
+    """The CPU restatement of the GEMM's ReLU bitmask: pack / unpack round trip
+    and the forward / backward pair against a plain mask."""
+    import torch
+    from dlvk_b200.ops import core as K
+
+    g = torch.Generator().manual_seed(3)
+    for m, n in ((5, 32), (7, 45), (3, 100)):
+        pos = torch.rand(m, n, generator=g) > 0.5
+        bits = K._pack_bits(pos, (n + 31) // 32)
+        assert bits.dtype == torch.int32 and bits.shape == (m, (n + 31) // 32)
+        assert torch.equal(K._unpack_bits(bits, n), pos)
+    a, b = torch.randn(6, 8, generator=g), torch.randn(8, 40, generator=g)
+    bits = K.relu_bits_like(6, 40, "cpu")
+    f = K.gemm(a, b, act=K.ACT_RELU, relu_bits_out=bits)
+    gy, w = torch.randn(6, 8, generator=g), torch.randn(40, 8, generator=g)
+    assert torch.allclose(K.gemm(gy, w.t(), relu_bits=bits), K.gemm(gy, w.t(), relu_mask=f))

@@ -395,3 +395,41 @@ def test_gemm_tc_fused_colsum(M, N, K, out_dtype):
     _check(cs, 0.5 * ref.sum(0), 4e-3)
     C.gemm(a, b, relu_mask=mask, out_dtype=out_dtype, force_path=1, colsum_out=cs, colsum_accumulate=True)
     _check(cs, 1.5 * ref.sum(0), 4e-3)
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 512, 256), (1024, 1024, 512), (300, 200, 100), (96, 1000, 64)])
+@pytest.mark.parametrize("force_path", [0, 2])  # 0: tensor cores where the layout allows, 2: SIMT
+def test_gemm_relu_bitmask(M, N, K, force_path):
+    """The forward GEMM writes one bit per output (> 0 after bias + ReLU); the
+    backward GEMM zeroes its output where the bit is clear, with the fused
+    column sums, and matches the same backward through a bf16 mask."""
+    from dlvk_b200.ops.core import _unpack_bits, relu_bits_like
+
+    C = _C()
+    g = torch.Generator(device="cuda").manual_seed(7)
+    a = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    b = (torch.randn(K, N, device="cuda", generator=g) * 0.1).bfloat16()
+    bias = torch.randn(N, device="cuda", generator=g) * 0.1
+    bits = relu_bits_like(M, N, "cuda")
+    f = C.gemm(a, b, bias=bias, act=1, force_path=force_path, relu_bits_out=bits)
+    ref = _ref(a, b, bias, act=1)
+    _check(f, ref, 1e-2)
+    pos = _unpack_bits(bits, N)
+    # bits agree with the reference wherever the output is not within rounding of zero
+    sure = (ref.abs() > 1e-3 * ref.abs().max())
+    assert torch.equal(pos[sure], (ref > 0)[sure])
+    # padding bits past N are clear
+    if N % 32:
+        tail = (bits[:, -1].to(torch.int64) & 0xFFFFFFFF) >> (N % 32)
+        assert int(tail.abs().sum()) == 0
+    # backward: dF = (G W^T) where the bit is set, plus the bias gradient (column sums)
+    gy = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.1).bfloat16()
+    cs = torch.zeros(N, device="cuda")
+    df = C.gemm(gy, w.t(), force_path=force_path, relu_bits=bits, colsum_out=cs)
+    dref = torch.where(pos, gy.float() @ w.float().t(), torch.zeros(M, N, device="cuda"))
+    _check(df, dref, 1e-2)
+    _check(cs, df.float().sum(0), 1e-2)
+    via_mask = C.gemm(gy, w.t(), force_path=force_path, relu_mask=f)
+    _check(df[sure], via_mask[sure].float(), 1e-2)
+    assert int(C.read_device_error(True)) == 0

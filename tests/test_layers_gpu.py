@@ -106,10 +106,11 @@ def test_batchnorm_relu_dropout(dtype, shape, p):
     close(dbt, 2 * db_c, tol * 2)
 
 
+@pytest.mark.parametrize("rows", [333, 5003])  # 5003: more rows than one pass of the grid's warps covers
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_layernorm(dtype):
+def test_layernorm(dtype, rows):
     C = _C()
-    x = torch.randn(333, 1024, device="cuda").to(dtype)
+    x = torch.randn(rows, 1024, device="cuda").to(dtype)
     gamma = torch.rand(1024, device="cuda") + 0.5
     beta = torch.randn(1024, device="cuda")
     y, mean, rstd = C.layernorm_fwd(x, gamma, beta, 1e-5)
