@@ -68,6 +68,7 @@ struct TcParams {
                            // 2: same boxes, added into fp32 C (split-K partials reduced in L2)
   int a_bcast;             // 1: one A for every batch entry (its map has no batch extent)
   const float* row_bias;   // fp32 bias per output row, or null
+  int sk;                  // 1: stream-K work split (fp32 C, partial tiles added by TMA reduces)
   uint32_t* bits_out;      // ReLU bitmask written (plain / TMA-store epilogues), or null
   const uint32_t* bits_in; // ReLU bitmask applied (staged epilogue), or null
   int64_t ldbits;          // 32-bit words per bitmask row
@@ -134,6 +135,48 @@ __device__ __forceinline__ void tile_coords(int t, const TcParams& p, int& tm, i
   const int rr = r - g * in_group;
   tm = first_m + rr % gsz;
   tn = rr / gsz;
+}
+
+// The units of work of one CTA (or CTA pair) c of n.
+//  - Tiles / split-K: unit t = (split, tile) for t = c, c + n, ...
+//  - Stream-K (p.sk): the tiles x k-blocks iteration space is cut into n
+//    equal contiguous ranges, one per CTA; the pieces of a range inside one
+//    tile are its units (at most a few per CTA), each added into the fp32
+//    output by the epilogue's TMA reduce, so no CTA idles in a last partial
+//    wave.
+// Producer, MMA issuer and epilogue each walk the same sequence.
+struct WorkIter {
+  int t;
+  int64_t cur, hi;
+};
+__device__ __forceinline__ void work_begin(const TcParams& p, int c, int n, int num_kb, int tiles, WorkIter& w) {
+  w.t = c;
+  const int64_t total = (int64_t)tiles * num_kb;
+  w.cur = total * c / n;
+  w.hi = total * (c + 1) / n;
+}
+__device__ __forceinline__ bool work_next(const TcParams& p, int n, int num_kb, int tiles_per_split, int num_tiles,
+                                          WorkIter& w, int& tm, int& tn, int& b, int& sp, int& kb0, int& kb1,
+                                          bool& last) {
+  if (p.sk) {
+    if (w.cur >= w.hi) return false;
+    const int tile = (int)(w.cur / num_kb);
+    kb0 = (int)(w.cur - (int64_t)tile * num_kb);
+    kb1 = (int)min((int64_t)num_kb, (int64_t)kb0 + (w.hi - w.cur));
+    w.cur += kb1 - kb0;
+    sp = 0;
+    tile_coords(tile, p, tm, tn, b);
+    last = w.cur >= w.hi;
+    return true;
+  }
+  if (w.t >= num_tiles) return false;
+  sp = w.t / tiles_per_split;
+  tile_coords(w.t - sp * tiles_per_split, p, tm, tn, b);
+  kb0 = sp * p.kb_per_split;
+  kb1 = min(num_kb, kb0 + p.kb_per_split);
+  last = w.t + n >= num_tiles;
+  w.t += n;
+  return true;
 }
 
 // Epilogue element loops below branch once per chunk, never per element: a
@@ -432,16 +475,16 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0 && PAIR) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int t = t0; t < num_tiles; t += tstep) {
-        int tm, tn, b;
-        const int sp = t / tiles_per_split;
-        tile_coords(t - sp * tiles_per_split, p, tm, tn, b);
+      WorkIter w;
+      work_begin(p, t0, tstep, num_kb, tiles_per_split, w);
+      int tm, tn, b, sp, kb0, kb1;
+      bool last;
+      while (work_next(p, tstep, num_kb, tiles_per_split, num_tiles, w, tm, tn, b, sp, kb0, kb1, last)) {
         const int bo = b / p.batch2, bi = b - bo * p.batch2;
         const int abo = p.a_bcast ? 0 : bo, abi = p.a_bcast ? 0 : bi;
         const int arow = tm * TILE_M + (int)rank * BM;
         // sub-block j of this CTA: columns tn*BN + j*MMA_N + rank*MMA_N/2 + [0, MMA_N/2)
         const int bcol = tn * BN + (int)rank * (C::MMA_N / 2);
-        const int kb0 = sp * p.kb_per_split, kb1 = min(num_kb, kb0 + p.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
           {
             GEMM_T0();
@@ -481,13 +524,13 @@ __global__ void __launch_bounds__(320, 1)
     } else if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-        int tm, tn, b;
-        const int sp = t / tiles_per_split;
-        tile_coords(t - sp * tiles_per_split, p, tm, tn, b);
+      WorkIter w;
+      work_begin(p, blockIdx.x, gridDim.x, num_kb, tiles_per_split, w);
+      int tm, tn, b, sp, kb0, kb1;
+      bool last;
+      while (work_next(p, gridDim.x, num_kb, tiles_per_split, num_tiles, w, tm, tn, b, sp, kb0, kb1, last)) {
         const int bo = b / p.batch2, bi = b - bo * p.batch2;
         const int abo = p.a_bcast ? 0 : bo, abi = p.a_bcast ? 0 : bi;
-        const int kb0 = sp * p.kb_per_split, kb1 = min(num_kb, kb0 + p.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
           {
             GEMM_T0();
@@ -527,7 +570,11 @@ __global__ void __launch_bounds__(320, 1)
         uint32_t phase = 0;
         int acc = 0;
         uint32_t acc_phase = 0;
-        for (int t = t0; t < num_tiles; t += tstep) {
+        WorkIter w;
+        work_begin(p, t0, tstep, num_kb, tiles_per_split, w);
+        int tm, tn, b, sp, kb0, kb1;
+        bool last;
+        while (work_next(p, tstep, num_kb, tiles_per_split, num_tiles, w, tm, tn, b, sp, kb0, kb1, last)) {
           {
             GEMM_T0();
             if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.err)) break;
@@ -536,8 +583,6 @@ __global__ void __launch_bounds__(320, 1)
           tc_fence_after();
           const uint32_t d = tmem_base + (uint32_t)(acc * BN);
           bool ok = true;
-          const int sp = t / tiles_per_split;
-          const int kb0 = sp * p.kb_per_split, kb1 = min(num_kb, kb0 + p.kb_per_split);
           for (int kb = kb0; kb < kb1; ++kb) {
             GEMM_T0();
             if (!mbar_wait(&full[stage], phase, p.err)) { ok = false; break; }
@@ -586,7 +631,11 @@ __global__ void __launch_bounds__(320, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      WorkIter w;
+      work_begin(p, blockIdx.x, gridDim.x, num_kb, tiles_per_split, w);
+      int tm, tn, b, sp, kb0, kb1;
+      bool last;
+      while (work_next(p, gridDim.x, num_kb, tiles_per_split, num_tiles, w, tm, tn, b, sp, kb0, kb1, last)) {
         {
           GEMM_T0();
           if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.err)) break;
@@ -595,8 +644,6 @@ __global__ void __launch_bounds__(320, 1)
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * BN);
         bool ok = true;
-        const int sp = t / tiles_per_split;
-        const int kb0 = sp * p.kb_per_split, kb1 = min(num_kb, kb0 + p.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
           GEMM_T0();
           if (!mbar_wait(&full[stage], phase, p.err)) { ok = false; break; }
@@ -652,11 +699,11 @@ __global__ void __launch_bounds__(320, 1)
     // and no load is left), so there each warp gets 1/8 of it and issues its
     // boxes without waiting.
     constexpr int WREG = (C::STAGES * C::STAGE_BYTES / 8) & ~1023;
-    for (int t = t0; t < num_tiles; t += tstep) {
-      int tm, tn, b;
-      const int sp = t / tiles_per_split;
-      tile_coords(t - sp * tiles_per_split, p, tm, tn, b);
-      const bool last_tile = t + tstep >= num_tiles;
+    WorkIter w;
+    work_begin(p, t0, tstep, num_kb, tiles_per_split, w);
+    int tm, tn, b, sp, kb0, kb1;
+    bool last_tile;
+    while (work_next(p, tstep, num_kb, tiles_per_split, num_tiles, w, tm, tn, b, sp, kb0, kb1, last_tile)) {
       int tcount = 0;  // boxes of this tile issued by this warp
 
       {
@@ -911,7 +958,8 @@ void launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& 
     attr_set[dev] = true;
   }
   const int tiles = p.tiles_m * p.tiles_n * p.batch * p.splits;
-  int grid = std::min(tiles, max_ctas > 0 ? max_ctas : sm_count());
+  const int slots = max_ctas > 0 ? max_ctas : sm_count();
+  int grid = p.sk ? slots : std::min(tiles, slots);  // stream-K: every CTA takes a share
   launch_pdl(gemm_tc_kernel<BN, false>, dim3(grid), dim3(320), C::SMEM, s, ta, tb, tc, p);
   DLVK_POST_LAUNCH();
 }
@@ -946,7 +994,7 @@ void launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensor
     max_pairs[dev] = std::max(1, n);
   }
   const int tiles = p.tiles_m * p.tiles_n * p.batch * p.splits;
-  int pairs = std::min(tiles, max_pairs[dev]);
+  int pairs = p.sk ? max_pairs[dev] : std::min(tiles, max_pairs[dev]);  // stream-K: every pair takes a share
   if (max_ctas > 0) pairs = std::max(1, std::min(pairs, max_ctas / 2));
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.numAttrs = 2;
@@ -1012,8 +1060,19 @@ bool gemm_tc_wide_enabled() { return wide_flag() != 0; }
 // With `red` (split_red_ok) the partials are added into C by the epilogue's
 // TMA reduce in L2 (plus a clear of C when beta = 0) instead of the workspace
 // round trip and the reduce launch.
+// DLVK_GEMM_STREAMK: 0 never, 1 when the tiling model picks it (default),
+// 2 whenever the output allows it (measurement).
+int streamk_mode() {
+  static const int m = [] {
+    const char* e = std::getenv("DLVK_GEMM_STREAMK");
+    return e ? std::atoi(e) : 1;
+  }();
+  return m;
+}
+
 void choose_tiling(const GemmArgs& a, int sms, int& BN, int& splits, bool& pair, bool red = false,
-                   bool out_f32 = false, bool single_cta = false) {
+                   bool out_f32 = false, bool single_cta = false, bool* sk = nullptr) {
+  if (sk) *sk = false;
   const int64_t kbs = (a.K + BK - 1) / BK;
   const double sm_flops = 8.1e12;
   double best = 1e300;
@@ -1062,6 +1121,27 @@ void choose_tiling(const GemmArgs& a, int sms, int& BN, int& splits, bool& pair,
         BN = c.bn;
         splits = sp;
         pair = c.pair;
+        if (sk) *sk = false;
+      }
+    }
+    // Stream-K (fp32 C with a linear epilogue): every slot gets the same
+    // number of k-blocks; a slot's pieces of about two tiles are added into C
+    // by TMA reduces (each slot's last epilogue is exposed), after a clear of
+    // C when beta = 0.
+    if (sk && red && c.bn != 512 && streamk_mode() != 0) {
+      const int64_t total = tiles * kbs;
+      const int64_t per = (total + slots - 1) / slots;
+      const double kb_s = (double)tile_m * c.bn * BK * 2.0 / (sm_flops * (c.pair ? 2 : 1) * c.eff);
+      const double mn = (double)a.M * a.N * a.batch * a.batch2;
+      const double t = per * kb_s + 2.0 * 128.0 * c.bn * 4.0 / 17e9 +
+                       (double)(tiles + slots) * tile_m * c.bn * 4.0 / 8e12 +
+                       (a.beta == 0.f ? mn * 4.0 / 5e12 + 2e-6 : 0.0);
+      if (t < best * 0.97 || (streamk_mode() == 2 && !*sk)) {
+        best = t;
+        BN = c.bn;
+        splits = 1;
+        pair = c.pair;
+        *sk = true;
       }
     }
   }
@@ -1204,15 +1284,22 @@ void gemm_tc_impl(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err
   const bool a_k = (a.sak == 1);
   const bool b_k = (a.sbk == 1);
   int BN = 256, splits = 1;
-  bool pair = false;
+  bool pair = false, sk = false;
   const bool red = split_red_ok(out_dt, a);
-  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits, pair, red, out_dt == DType::F32, tf32);
+  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, splits, pair, red, out_dt == DType::F32, tf32, &sk);
   {
     const TilingOverride& ov = tiling_override();
     if (ov.pair >= 0) pair = ov.pair != 0 && !tf32 && a.M >= 256;
     if (ov.bn > 0) BN = (ov.bn == 512 && !pair) ? 256 : ov.bn;
-    if (ov.splits > 0) splits = ov.splits;
+    if (ov.splits > 0) {
+      splits = ov.splits;
+      sk = false;
+    } else if (ov.splits == -1) {  // stream-K
+      splits = 1;
+      sk = red;
+    }
   }
+  if (BN == 512) sk = false;
   if (a.colsum != nullptr) {
     DLVK_CHECK(gemm_tc_colsum_ok(out_dt, a), "gemm_tc: column sums need the staged fast-path layout");
     splits = 1;  // the sums are taken over final outputs
@@ -1226,6 +1313,7 @@ void gemm_tc_impl(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err
   }
   if (!red && (workspace == nullptr || workspace_floats < (int64_t)splits * a.M * a.N * a.batch * a.batch2))
     splits = 1;
+  if (a.colsum != nullptr || a.relu_bits_out != nullptr || !red) sk = false;
   pair = pair && max_ctas != 1;
   // Unused batch levels get a harmless stride (a multiple of 16 bytes).
   auto pick = [](int64_t cnt, int64_t stride, uint64_t dflt) { return cnt > 1 ? (uint64_t)stride : dflt; };
@@ -1299,9 +1387,11 @@ void gemm_tc_impl(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err
   p.splits = splits;
   p.kb_per_split = (int)(((a.K + bke - 1) / bke + splits - 1) / splits);
   p.split_stride = 0;
-  if (splits > 1 && red) {
-    // Every split's epilogue adds alpha * partial into C with a TMA reduce;
-    // C starts from zero (beta = 0) or from its old value (beta = 1).
+  p.sk = sk ? 1 : 0;
+  if ((splits > 1 || sk) && red) {
+    // Every split's (stream-K unit's) epilogue adds alpha * partial into C
+    // with a TMA reduce; C starts from zero (beta = 0) or from its old value
+    // (beta = 1).
     p.beta = 0.f;  // the epilogue itself never reads C
     const CUtensorMap tc = make_c_map(p, a.M, a.N, true);
     if (p.tma_c == 2) {
@@ -1317,6 +1407,7 @@ void gemm_tc_impl(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err
     p.beta = a.beta;
     splits = 1;
     p.splits = 1;
+    p.sk = 0;
     p.kb_per_split = (int)((a.K + bke - 1) / bke);
   }
   if (splits > 1) {
@@ -1433,9 +1524,11 @@ void gemm_tc_set_wide(int mode) { wide_flag() = mode; }
 void gemm_tc_plan(DType out_dt, const GemmArgs& a, int max_ctas, int* bn, int* splits, int* pair) {
   int BN = 256, sp = 1;
   bool pr = false;
-  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, sp, pr, split_red_ok(out_dt, a), out_dt == DType::F32);
+  bool sk = false;
+  choose_tiling(a, max_ctas > 0 ? max_ctas : sm_count(), BN, sp, pr, split_red_ok(out_dt, a), out_dt == DType::F32,
+                false, &sk);
   *bn = BN;
-  *splits = sp;
+  *splits = sk ? -1 : sp;  // -1: stream-K
   *pair = (pr && max_ctas != 1) ? 1 : 0;
 }
 

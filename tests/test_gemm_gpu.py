@@ -433,3 +433,28 @@ def test_gemm_relu_bitmask(M, N, K, force_path):
     via_mask = C.gemm(gy, w.t(), force_path=force_path, relu_mask=f)
     _check(df[sure], via_mask[sure].float(), 1e-2)
     assert int(C.read_device_error(True)) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 1024, 8192), (1024, 3072, 4096), (300, 200, 1000), (512, 520, 2048)])
+@pytest.mark.parametrize("pair", [1, 0])
+@pytest.mark.parametrize("beta", [0.0, 1.0])
+def test_gemm_tc_stream_k(M, N, K, pair, beta):
+    """Stream-K (every CTA or pair takes an equal run of the tiles x k-blocks
+    space and adds its pieces into the fp32 output with TMA reduces), forced
+    through the tiling override, on weight-gradient layouts (both operands
+    M/N-major), against the fp32 product of the same operands."""
+    C = _C()
+    g = torch.Generator(device="cuda").manual_seed(11)
+    a = torch.randn(K, M, device="cuda", generator=g).bfloat16().t()
+    b = torch.randn(K, N, device="cuda", generator=g).bfloat16()
+    acc0 = torch.randn(M, N, device="cuda", generator=g)
+    out = acc0.clone()
+    try:
+        C.gemm_set_tiling(256, -1, pair)
+        C.gemm(a, b, beta=beta, out=out, force_path=1)
+    finally:
+        C.gemm_set_tiling(0, 0, -1)
+    ref = beta * acc0 + a.float() @ b.float()
+    err = (out - ref).abs().max().item()
+    assert err <= 1e-4 * ref.abs().max().item(), f"max err {err}"
+    assert int(C.read_device_error(True)) == 0
