@@ -220,6 +220,33 @@ __device__ __forceinline__ void add_bias(const void* bias, bool f32, int n, int 
   }
 }
 
+// Row-per-lane epilogues (lane = row row0 + lane, v = its 32 columns from
+// n0): zero v where the ReLU bitmask is clear, and rows past M entirely.
+__device__ __forceinline__ void mask_row_bits(const TcParams& p, int row, int n0, float* v) {
+  const uint32_t w = row < p.M ? p.bits_in[(int64_t)row * p.ldbits + (n0 >> 5)] : 0u;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = ((w >> j) & 1u) ? v[j] : 0.f;
+}
+
+// Column sums of a 32 x 32 chunk held one row per lane, by recursive
+// halving: at each of five steps a lane keeps half of its columns and adds
+// its partner's copies of them (16 + 8 + 4 + 2 + 1 shuffles), ending with
+// lane l holding column l.  Written to the per-32-row partials
+// colsum[(row0 / 32) * N + n].  Rows past M must be zero in v; v is consumed.
+__device__ __forceinline__ void colsum_chunk(const TcParams& p, int row0, int lane, int n0, float* v) {
+#pragma unroll
+  for (int h = 16; h >= 1; h >>= 1) {
+    const bool up = (lane & h) != 0;
+#pragma unroll
+    for (int j = 0; j < h; ++j) {
+      const float send = up ? v[j] : v[j + h];
+      const float keep = up ? v[j + h] : v[j];
+      v[j] = keep + __shfl_xor_sync(0xffffffffu, send, h);
+    }
+  }
+  if (n0 + lane < p.N) p.colsum[(int64_t)(row0 >> 5) * p.N + n0 + lane] = v[0];
+}
+
 // Word of the ReLU bitmask for one row's 32 columns [n0, n0 + 32): bit j set
 // where v[j] > 0 (after the activation); columns past N stay clear.
 __device__ __forceinline__ void store_bits(const TcParams& p, int row, int n0, const float* v) {
@@ -269,41 +296,24 @@ __device__ __forceinline__ void epi_store(const TcParams& p, const float* stg, i
     if (r < p.M && n0 < p.N) bw = p.bits_in[(int64_t)r * p.ldbits + (n0 >> 5)];
   }
   const int naux = (p.beta != 0.f) + (p.R != nullptr) + (p.Mk != nullptr);
-  // Exactly one auxiliary input (beta*C, residual or mask) is prefetched.
-  const bool fast = naux + (p.bits_in ? 1 : 0) == 1 && valid == VEC && p.vec_ok && (!p.R || p.r_vec) &&
+  // Exactly one auxiliary input (beta*C, residual or mask) is prefetched; a
+  // ReLU bitmask beside it takes the per-pass path below.
+  const bool fast = naux == 1 && !p.bits_in && valid == VEC && p.vec_ok && (!p.R || p.r_vec) &&
                     (!p.Mk || p.m_vec) && row0 + 32 <= p.M;
   if (fast) {
-    uint4 av[NP];
-    if (p.bits_in) {
-      // the bits as a 0 / 1 mask of this lane's VEC elements
-#pragma unroll
-      for (int ps = 0; ps < NP; ++ps) {
-        const uint32_t mb = __shfl_sync(0xffffffffu, bw, ps * RPP + rr) >> (cg * VEC);
-        uint32_t w[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          if (VEC == 8) {  // two bf16 per word (1.0 = 0x3F80)
-            w[q] = (((mb >> (2 * q)) & 1u) ? 0x3F80u : 0u) | (((mb >> (2 * q + 1)) & 1u) ? 0x3F800000u : 0u);
-          } else {         // one fp32 per word
-            w[q] = ((mb >> q) & 1u) ? 0x3F800000u : 0u;
-          }
-        }
-        av[ps] = make_uint4(w[0], w[1], w[2], w[3]);
-      }
+    const T* abase;
+    int64_t aoff, ald;
+    if (p.beta != 0.f) {
+      abase = reinterpret_cast<const T*>(p.C); aoff = cb; ald = p.ldc;
+    } else if (p.R) {
+      abase = reinterpret_cast<const T*>(p.R); aoff = rb; ald = p.ldr;
     } else {
-      const T* abase;
-      int64_t aoff, ald;
-      if (p.beta != 0.f) {
-        abase = reinterpret_cast<const T*>(p.C); aoff = cb; ald = p.ldc;
-      } else if (p.R) {
-        abase = reinterpret_cast<const T*>(p.R); aoff = rb; ald = p.ldr;
-      } else {
-        abase = reinterpret_cast<const T*>(p.Mk); aoff = mb; ald = p.ldm;
-      }
-#pragma unroll
-      for (int ps = 0; ps < NP; ++ps)
-        av[ps] = *reinterpret_cast<const uint4*>(abase + aoff + (int64_t)(row0 + ps * RPP + rr) * ald + n);
+      abase = reinterpret_cast<const T*>(p.Mk); aoff = mb; ald = p.ldm;
     }
+    uint4 av[NP];
+#pragma unroll
+    for (int ps = 0; ps < NP; ++ps)
+      av[ps] = *reinterpret_cast<const uint4*>(abase + aoff + (int64_t)(row0 + ps * RPP + rr) * ald + n);
     const int mode = p.beta != 0.f ? 0 : (p.R ? 1 : 2);
     float bv[VEC];
 #pragma unroll
@@ -689,7 +699,7 @@ __global__ void __launch_bounds__(320, 1)
     const int q = warp & 3;
     const int half = ew >> 2;
     float* stg = epi + ew * (32 * 33);
-    const bool staged = (p.R != nullptr) || (p.Mk != nullptr) || (p.beta != 0.f) || (p.bits_in != nullptr);
+    const bool staged = (p.R != nullptr) || (p.Mk != nullptr) || (p.beta != 0.f);
     constexpr int NCH = BN / 64;  // 32-column chunks per warp
     int acc = 0, ecount = 0;
     uint32_t acc_phase = 0;
@@ -760,6 +770,7 @@ __global__ void __launch_bounds__(320, 1)
             for (int j = 0; j < 32; ++j) v[j] = fmaf(__uint_as_float(r[i & 1][j]), p.alpha, rbv);
             if (p.bias && n0 < p.N) add_bias<32>(p.bias, p.bias_f32, n0, min(32, p.N - n0), v);
             apply_act<32>(p.act, v);
+            if (p.bits_in) mask_row_bits(p, row0 + lane, n0, v);
             if (p.bits_out && n0 < p.N && row0 + lane < p.M) store_bits(p, row0 + lane, n0, v);
             // Boxes start on 1024-byte boundaries (the swizzled box layout is
             // defined on aligned addresses).
@@ -799,6 +810,13 @@ __global__ void __launch_bounds__(320, 1)
                 st_shared_v4(a ^ (((a >> 7) & 7u) << 4), w[0], w[1], w[2], w[3]);
               }
             }
+            if (BN != 512 && p.colsum) {  // after the box write: consumes v (512-wide tiles: never, see host)
+              if (row0 + lane >= p.M) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = 0.f;
+              }
+              colsum_chunk(p, row0, lane, n0, v);
+            }
             if (!bf || (i & 1)) {
               fence_proxy_async_smem();
               __syncwarp();
@@ -832,6 +850,7 @@ __global__ void __launch_bounds__(320, 1)
             }
             if (p.bias) add_bias<32>(p.bias, p.bias_f32, n0, min(32, p.N - n0), v);
             apply_act<32>(p.act, v);
+            if (p.bits_in) mask_row_bits(p, row, n0, v);
             if (p.bits_out) store_bits(p, row, n0, v);
             const bool full = (n0 + 32 <= p.N) && p.vec_ok;
             if (p.out_f32) {
@@ -1190,7 +1209,8 @@ bool gemm_tc_colsum_ok(DType out_dt, const GemmArgs& a) {
   auto rows16 = [&](const void* p, int64_t ld) {
     return p == nullptr || (al16(p) && (ld * esz) % 16 == 0);
   };
-  return (naux == 1 || (naux == 0 && a.relu_bits != nullptr)) && a.batch == 1 && a.batch2 == 1 && a.M % 32 == 0 &&
+  // naux == 0: the TMA-store epilogue sums the columns in registers
+  return (naux == 1 || (naux == 0 && tma_c_enabled())) && a.batch == 1 && a.batch2 == 1 && a.M % 32 == 0 &&
          a.N % 32 == 0 && al16(a.C) &&
          (a.ldc * esz) % 16 == 0 && rows16(a.residual, a.ldr) && rows16(a.relu_mask, a.ldm);
 }
@@ -1303,6 +1323,9 @@ void gemm_tc_impl(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err
   if (a.colsum != nullptr) {
     DLVK_CHECK(gemm_tc_colsum_ok(out_dt, a), "gemm_tc: column sums need the staged fast-path layout");
     splits = 1;  // the sums are taken over final outputs
+    // without a staged input the TMA-store epilogue sums in registers, which
+    // the 512-wide tile's instantiation leaves out (register budget)
+    if (BN == 512 && a.beta == 0.f && a.residual == nullptr && a.relu_mask == nullptr) BN = 256;
   }
   if (a.relu_bits != nullptr || a.relu_bits_out != nullptr)
     DLVK_CHECK(a.batch == 1 && a.batch2 == 1 && a.ldbits >= (a.N + 31) / 32, "gemm_tc: ReLU bitmask needs a 2-D GEMM");
@@ -1441,6 +1464,8 @@ void gemm_tc_impl(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err
     return;
   }
   const CUtensorMap tc = make_c_map(p, a.M, a.N);
+  DLVK_CHECK(!(p.colsum && p.beta == 0.f && !p.R && !p.Mk && p.tma_c == 0),
+             "gemm_tc: column sums without a staged input need the TMA-store epilogue");
   if (pair && BN == 512) launch_tc_pair<512>(ta, tb, tc, p, max_ctas, s);
   else if (pair) launch_tc_pair<256>(ta, tb, tc, p, max_ctas, s);
   else if (BN == 256) launch_tc<256>(ta, tb, tc, p, max_ctas, s);

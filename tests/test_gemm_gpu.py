@@ -458,3 +458,23 @@ def test_gemm_tc_stream_k(M, N, K, pair, beta):
     err = (out - ref).abs().max().item()
     assert err <= 1e-4 * ref.abs().max().item(), f"max err {err}"
     assert int(C.read_device_error(True)) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 1024, 256), (8192, 1024, 512), (256, 4096, 128)])
+@pytest.mark.parametrize("bias", [False, True])
+def test_gemm_tc_colsum_in_registers(M, N, K, bias):
+    """Column sums fused into an epilogue with no staged input (summed over
+    each 32-row chunk in registers by shuffles), against the sums of the
+    GEMM's own output."""
+    C = _C()
+    g = torch.Generator(device="cuda").manual_seed(5)
+    a = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    b = (torch.randn(K, N, device="cuda", generator=g) * 0.1).bfloat16()
+    bv = torch.randn(N, device="cuda", generator=g) if bias else None
+    cs = torch.full((N,), 3.0, device="cuda")
+    out = C.gemm(a, b, bias=bv, out_dtype=torch.float32, colsum_out=cs, colsum_scale=0.5, colsum_accumulate=True)
+    _check(out, _ref(a, b, bv), 1e-3)
+    ref = 3.0 + 0.5 * out.sum(0)
+    err = (cs - ref).abs().max().item()
+    assert err <= 1e-4 * ref.abs().max().item() + 1e-3, f"max err {err}"
+    assert int(C.read_device_error(True)) == 0
