@@ -743,12 +743,13 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
   }
 }
 
-// delta[b, h, q] = sum_d dO[b, q, h, d] * O[b, q, h, d]: eight lanes per
+// delta[b, h, q] = sum_d dO[b, q, h, d] * O[b, q, h, d], and the row's 64
+// entries of the fp32 dQ accumulator cleared (no separate memset): eight lanes per
 // (b, q, h) row of 64, one 16-byte vector of each operand per lane, reduced
 // with three shuffles.  A warp reads four consecutive rows (512 contiguous
 // bytes per operand per load instruction).
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
-                                  float* __restrict__ delta, int B, int S, int H) {
+                                  float* __restrict__ delta, int B, int S, int H, float* __restrict__ dq_zero) {
   pdl_wait();
   const int64_t total = (int64_t)B * S * H * 8;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -768,6 +769,12 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __n
         const float2 xf = __bfloat1622float2(x[k]), yf = __bfloat1622float2(y[k]);
         acc = fmaf(xf.x, yf.x, fmaf(xf.y, yf.y, acc));
       }
+    }
+    if (on) {
+      // the same row of the fp32 dQ accumulator [B*S, H*64] starts at zero
+      float4* z = reinterpret_cast<float4*>(dq_zero + w * FD) + (t & 7) * 2;
+      z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+      z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     acc += __shfl_xor_sync(0xffffffffu, acc, 1);
     acc += __shfl_xor_sync(0xffffffffu, acc, 2);
@@ -834,10 +841,9 @@ void flash_attention_bwd(const __nv_bfloat16* qkv, const __nv_bfloat16* out, con
   {
     const int64_t n = rows * H * 8;
     launch_pdl(attn_delta_kernel, dim3((unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)tmap::sm_count() * 16)),
-               dim3(256), 0, s, out, dout, delta, B, S, H);
+               dim3(256), 0, s, out, dout, delta, B, S, H, dq_acc);
     DLVK_POST_LAUNCH();
   }
-  DLVK_CUDA_CHECK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * E, s));
   CUtensorMap tq = tmap::bf16_2d_sw128(qkv, (uint64_t)3 * E, (uint64_t)rows, (uint64_t)3 * E, FT);
   CUtensorMap td = tmap::bf16_2d_sw128(dout, (uint64_t)E, (uint64_t)rows, (uint64_t)E, FT);
   CUtensorMap tdq;
