@@ -247,6 +247,32 @@ __device__ __forceinline__ void colsum_chunk(const TcParams& p, int row0, int la
   if (n0 + lane < p.N) p.colsum[(int64_t)(row0 >> 5) * p.N + n0 + lane] = v[0];
 }
 
+// v[j] += R[row, n0 + j] (bf16, C's dtype) for a row-per-lane epilogue: the
+// lane reads its row's 32 consecutive elements as four 16-byte vectors.
+__device__ __forceinline__ void add_row_residual(const TcParams& p, int64_t rb, int row, int n0, float* v) {
+  if (row >= p.M || n0 >= p.N) return;
+  const int64_t off = rb + (int64_t)row * p.ldr + n0;
+  if (n0 + 32 <= p.N && p.r_vec) {
+    const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.R) + off);
+    uint4 u[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) u[q] = src[q];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[q]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(h[k]);
+        v[8 * q + 2 * k] += f.x;
+        v[8 * q + 2 * k + 1] += f.y;
+      }
+    }
+  } else {
+    for (int j = 0; j < 32 && n0 + j < p.N; ++j)
+      v[j] += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.R)[off + j]);
+  }
+}
+
 // Word of the ReLU bitmask for one row's 32 columns [n0, n0 + 32): bit j set
 // where v[j] > 0 (after the activation); columns past N stay clear.
 __device__ __forceinline__ void store_bits(const TcParams& p, int row, int n0, const float* v) {
@@ -699,7 +725,10 @@ __global__ void __launch_bounds__(320, 1)
     const int q = warp & 3;
     const int half = ew >> 2;
     float* stg = epi + ew * (32 * 33);
-    const bool staged = (p.R != nullptr) || (p.Mk != nullptr) || (p.beta != 0.f);
+    // A bf16 residual alone is added in registers; with beta or a mask (or
+    // an fp32 output) the chunk goes through the staged path, which handles
+    // all three.
+    const bool staged = (p.Mk != nullptr) || (p.beta != 0.f) || (p.R != nullptr && p.out_f32);
     constexpr int NCH = BN / 64;  // 32-column chunks per warp
     int acc = 0, ecount = 0;
     uint32_t acc_phase = 0;
@@ -769,6 +798,7 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = fmaf(__uint_as_float(r[i & 1][j]), p.alpha, rbv);
             if (p.bias && n0 < p.N) add_bias<32>(p.bias, p.bias_f32, n0, min(32, p.N - n0), v);
+            if (p.R) add_row_residual(p, rb, row0 + lane, n0, v);
             apply_act<32>(p.act, v);
             if (p.bits_in) mask_row_bits(p, row0 + lane, n0, v);
             if (p.bits_out && n0 < p.N && row0 + lane < p.M) store_bits(p, row0 + lane, n0, v);
@@ -849,6 +879,7 @@ __global__ void __launch_bounds__(320, 1)
               for (int j = 0; j < 32; ++j) v[j] *= cs[j];
             }
             if (p.bias) add_bias<32>(p.bias, p.bias_f32, n0, min(32, p.N - n0), v);
+            if (p.R) add_row_residual(p, rb, row, n0, v);
             apply_act<32>(p.act, v);
             if (p.bits_in) mask_row_bits(p, row, n0, v);
             if (p.bits_out) store_bits(p, row, n0, v);

@@ -435,7 +435,7 @@ def test_gemm_relu_bitmask(M, N, K, force_path):
     assert int(C.read_device_error(True)) == 0
 
 
-@pytest.mark.parametrize("M,N,K", [(1024, 1024, 8192), (1024, 3072, 4096), (300, 200, 1000), (512, 520, 2048)])
+@pytest.mark.parametrize("M,N,K", [(1024, 1024, 8192), (1024, 3072, 4096), (296, 200, 1000), (512, 520, 2048)])
 @pytest.mark.parametrize("pair", [1, 0])
 @pytest.mark.parametrize("beta", [0.0, 1.0])
 def test_gemm_tc_stream_k(M, N, K, pair, beta):
@@ -477,4 +477,23 @@ def test_gemm_tc_colsum_in_registers(M, N, K, bias):
     ref = 3.0 + 0.5 * out.sum(0)
     err = (cs - ref).abs().max().item()
     assert err <= 1e-4 * ref.abs().max().item() + 1e-3, f"max err {err}"
+    assert int(C.read_device_error(True)) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 1024, 256), (264, 200, 128), (8192, 1024, 1024)])
+@pytest.mark.parametrize("strided", [False, True])
+def test_gemm_tc_residual_in_registers(M, N, K, strided):
+    """bf16 residual added on the row-per-lane epilogue (contiguous rows read
+    as 16-byte vectors, or element by element for a ragged / strided one),
+    with bias and ReLU, against fp32 PyTorch."""
+    C = _C()
+    g = torch.Generator(device="cuda").manual_seed(9)
+    a = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    b = (torch.randn(K, N, device="cuda", generator=g) * 0.1).bfloat16()
+    bias = torch.randn(N, device="cuda", generator=g)
+    base = torch.randn(M, N + (3 if strided else 0), device="cuda", generator=g).bfloat16()
+    res = base[:, :N]
+    out = C.gemm(a, b, bias=bias, act=1, residual=res, force_path=1)
+    ref = torch.relu(a.float() @ b.float() + bias + res.float())
+    _check(out, ref, 1e-2)
     assert int(C.read_device_error(True)) == 0
