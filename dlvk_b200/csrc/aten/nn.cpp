@@ -349,7 +349,8 @@ std::vector<at::Tensor> layernorm_fwd_op(const at::Tensor& x, c10::optional<at::
 
 at::Tensor layernorm_bwd_op(const at::Tensor& x, c10::optional<at::Tensor> gamma, const at::Tensor& mean,
                             const at::Tensor& rstd, const at::Tensor& dy, c10::optional<at::Tensor> dgamma,
-                            c10::optional<at::Tensor> dbeta, bool accumulate, c10::optional<at::Tensor> dres) {
+                            c10::optional<at::Tensor> dbeta, bool accumulate, c10::optional<at::Tensor> dres,
+                            c10::optional<at::Tensor> dres_colsum, bool dres_colsum_accumulate) {
   check_cuda(x, "x");
   c10::cuda::CUDAGuard g(x.device());
   auto xc = x.contiguous(), dyc = dy.contiguous();
@@ -361,9 +362,12 @@ at::Tensor layernorm_bwd_op(const at::Tensor& x, c10::optional<at::Tensor> gamma
     drc = dres->contiguous();
     TORCH_CHECK(drc.scalar_type() == xc.scalar_type() && drc.numel() == xc.numel(), "dlvk.layernorm_bwd: dres");
   }
+  TORCH_CHECK(!dres_colsum.has_value() || (dres.has_value() && dres_colsum->numel() == D),
+              "dlvk.layernorm_bwd: dres_colsum needs dres and D elements");
   layernorm_bwd(to_dtype(xc), xc.data_ptr(), optf(gamma), mean.data_ptr<float>(), rstd.data_ptr<float>(),
                 dyc.data_ptr(), dx.data_ptr(), optfm(dgamma), optfm(dbeta), accumulate, R, (int)D,
-                scratch.data_ptr<float>(), stream(), dres.has_value() ? drc.data_ptr() : nullptr);
+                scratch.data_ptr<float>(), stream(), dres.has_value() ? drc.data_ptr() : nullptr,
+                optfm(dres_colsum), dres_colsum_accumulate);
   return dx;
 }
 

@@ -248,7 +248,7 @@ void register_nn(py::module& m) {
   m.def("layernorm_fwd", &layernorm_fwd_op, py::arg("x"), py::arg("gamma"), py::arg("beta"), py::arg("eps") = 1e-5);
   m.def("layernorm_bwd", &layernorm_bwd_op, py::arg("x"), py::arg("gamma"), py::arg("mean"), py::arg("rstd"),
         py::arg("dy"), py::arg("dgamma"), py::arg("dbeta"), py::arg("accumulate") = false,
-        py::arg("dres") = py::none());
+        py::arg("dres") = py::none(), py::arg("dres_colsum") = py::none(), py::arg("dres_colsum_accumulate") = false);
   m.def("dropout", &dropout_op, py::arg("x"), py::arg("p"), py::arg("stream_id") = 0, py::arg("seed") = 0,
         py::arg("step") = 0, py::arg("step_t") = py::none());
   m.def("embedding_fwd", &embedding_fwd_op);

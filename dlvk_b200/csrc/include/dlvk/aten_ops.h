@@ -63,7 +63,7 @@ at::Tensor avgpool_bwd_op(const at::Tensor& gy, int64_t H, int64_t W, int64_t k,
 std::vector<at::Tensor> batchnorm_fwd_op(const at::Tensor& x, c10::optional<at::Tensor> gamma, c10::optional<at::Tensor> beta, c10::optional<at::Tensor> run_mean, c10::optional<at::Tensor> run_var, double momentum, double eps, bool training, bool relu, double p, int64_t stream_id, int64_t seed, int64_t step, c10::optional<at::Tensor> step_t);
 at::Tensor batchnorm_bwd_op(const at::Tensor& x, const at::Tensor& dy, const at::Tensor& mean, const at::Tensor& rstd, c10::optional<at::Tensor> gamma, c10::optional<at::Tensor> beta, c10::optional<at::Tensor> dgamma, c10::optional<at::Tensor> dbeta, bool accumulate, bool relu, double p, int64_t stream_id, int64_t seed, int64_t step, c10::optional<at::Tensor> step_t);
 std::vector<at::Tensor> layernorm_fwd_op(const at::Tensor& x, c10::optional<at::Tensor> gamma, c10::optional<at::Tensor> beta, double eps);
-at::Tensor layernorm_bwd_op(const at::Tensor& x, c10::optional<at::Tensor> gamma, const at::Tensor& mean, const at::Tensor& rstd, const at::Tensor& dy, c10::optional<at::Tensor> dgamma, c10::optional<at::Tensor> dbeta, bool accumulate, c10::optional<at::Tensor> dres);
+at::Tensor layernorm_bwd_op(const at::Tensor& x, c10::optional<at::Tensor> gamma, const at::Tensor& mean, const at::Tensor& rstd, const at::Tensor& dy, c10::optional<at::Tensor> dgamma, c10::optional<at::Tensor> dbeta, bool accumulate, c10::optional<at::Tensor> dres, c10::optional<at::Tensor> dres_colsum = c10::nullopt, bool dres_colsum_accumulate = false);
 at::Tensor dropout_op(const at::Tensor& x, double p, int64_t stream_id, int64_t seed, int64_t step, c10::optional<at::Tensor> step_t);
 at::Tensor embedding_fwd_op(const at::Tensor& ids, const at::Tensor& table);
 void embedding_bwd_op(const at::Tensor& ids, const at::Tensor& dy, const at::Tensor& dtable);

@@ -245,9 +245,13 @@ int layernorm_bwd_blocks(int64_t rows);
 int64_t layernorm_bwd_scratch_floats(int64_t rows, int D);
 // dres (optional, same dtype/shape as dx): a residual-branch gradient added
 // to dx, fusing the sum of the two gradients of a pre-norm block input.
+// dres_colsum (optional, fp32 [D]): receives (or, with its accumulate flag,
+// adds) the column sums of dres -- the bias gradient of the biased GEMM whose
+// output gradient dres is.
 void layernorm_bwd(DType dt, const void* x, const float* gamma, const float* mean, const float* rstd, const void* dy,
                    void* dx, float* dgamma, float* dbeta, bool accumulate, int64_t rows, int D, float* scratch,
-                   cudaStream_t s, const void* dres = nullptr);
+                   cudaStream_t s, const void* dres = nullptr, float* dres_colsum = nullptr,
+                   bool dres_colsum_accumulate = false);
 void dropout(DType dt, const void* x, void* y, int64_t n, const DropoutDesc& dd, cudaStream_t s);
 void embedding_fwd(DType dt, const int32_t* ids, const void* table, void* out, int64_t n, int64_t V, int D,
                    cudaStream_t s);

@@ -786,7 +786,9 @@ __global__ void __launch_bounds__(256, 1) ln_bwd_ring_kernel(const __nv_bfloat16
                                                              __nv_bfloat16* __restrict__ dx, float* __restrict__ part,
                                                              int64_t rows, int D,
                                                              const __nv_bfloat16* __restrict__ dres) {
+  // part: [blocks][PD] partials, dgamma | dbeta (| column sums of dres)
   constexpr int EPV = 8, RING = 3, NT = RES ? 3 : 2, RV = NV * 32;  // 16-byte vectors per tensor row
+  constexpr int NP = RES ? 3 : 2;
   pdl_wait();
   extern __shared__ uint4 sring[];                                   // [8][RING][NT][RV]
   float* sgam = reinterpret_cast<float*>(sring + 8 * RING * NT * RV);
@@ -814,12 +816,14 @@ __global__ void __launch_bounds__(256, 1) ln_bwd_ring_kernel(const __nv_bfloat16
   for (int k = 0; k < RING; ++k) issue(r0 + k * step, k);
   // gr: this lane's gamma in registers (shared-memory reads at an 8-float
   // lane stride would conflict 8 ways on every element).
-  float adg[NV][EPV], adb[NV][EPV], gr[NV][EPV];
+  // adr: column sums of dres (the bias gradient of the layer whose output
+  // gradient dres is, when the block's residual sum ends in a biased GEMM).
+  float adg[NV][EPV], adb[NV][EPV], adr[NV][EPV], gr[NV][EPV];
 #pragma unroll
   for (int i = 0; i < NV; ++i)
 #pragma unroll
     for (int k = 0; k < EPV; ++k) {
-      adg[i][k] = adb[i][k] = 0.f;
+      adg[i][k] = adb[i][k] = adr[i][k] = 0.f;
       gr[i][k] = sgam[(lane + 32 * i) * EPV + k];
     }
   const float invD = 1.f / D;
@@ -861,7 +865,11 @@ __global__ void __launch_bounds__(256, 1) ln_bwd_ring_kernel(const __nv_bfloat16
       for (int k = 0; k < EPV; ++k) {
         const float xh = (__bfloat162float(ex[k]) - mu) * rs;
         float v = rs * (__bfloat162float(eg[k]) * gr[i][k] - a - xh * bb);
-        if (RES) v += __bfloat162float(er[k]);
+        if (RES) {
+          const float rv = __bfloat162float(er[k]);
+          v += rv;
+          adr[i][k] += rv;
+        }
         eo[k] = __float2bfloat16_rn(v);
       }
       reinterpret_cast<uint4*>(dx + r * D)[lane + 32 * i] = o;
@@ -871,8 +879,8 @@ __global__ void __launch_bounds__(256, 1) ln_bwd_ring_kernel(const __nv_bfloat16
   }
   sm100::cp_async_wait<0>();
   __syncthreads();
-  float* sp = reinterpret_cast<float*>(sring);  // the ring is free: [8][2*D] partials
-  float* mine = sp + (int64_t)w * 2 * D;
+  float* sp = reinterpret_cast<float*>(sring);  // the ring is free: [8][NP*D] partials
+  float* mine = sp + (int64_t)w * NP * D;
 #pragma unroll
   for (int i = 0; i < NV; ++i)
 #pragma unroll
@@ -880,42 +888,51 @@ __global__ void __launch_bounds__(256, 1) ln_bwd_ring_kernel(const __nv_bfloat16
       const int col = (lane + 32 * i) * EPV + k;
       mine[col] = adg[i][k];
       mine[D + col] = adb[i][k];
+      if (RES) mine[2 * D + col] = adr[i][k];
     }
   __syncthreads();
-  for (int d = threadIdx.x; d < 2 * D; d += blockDim.x) {
+  for (int d = threadIdx.x; d < NP * D; d += blockDim.x) {
     float acc = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc += sp[(int64_t)i * 2 * D + d];
-    part[(int64_t)blockIdx.x * 2 * D + d] = acc;
+    for (int i = 0; i < 8; ++i) acc += sp[(int64_t)i * NP * D + d];
+    part[(int64_t)blockIdx.x * NP * D + d] = acc;
   }
 }
 
 // Sums the per-block partials: block = 32 columns x 16 row groups, each
 // thread with four independent accumulators, combined in a fixed order
 // through shared memory.
+// np = 2 (dgamma, dbeta) or 3 (plus the column sums of the residual
+// gradient, into rsum with its own accumulate flag).
 __global__ void __launch_bounds__(512) ln_bwd_final_kernel(const float* __restrict__ part, int blocks, int D,
                                                            float* __restrict__ dgamma, float* __restrict__ dbeta,
-                                                           int accumulate) {
+                                                           int accumulate, int np, float* __restrict__ rsum,
+                                                           int rsum_accumulate) {
   pdl_wait();
   __shared__ float sm[16][33];
   const int d = blockIdx.x * 32 + threadIdx.x;
+  const int64_t pd = (int64_t)np * D;
   float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-  if (d < 2 * D) {
+  if (d < pd) {
     int b = threadIdx.y;
     for (; b + 48 < blocks; b += 64) {
-      s0 += part[(int64_t)b * 2 * D + d];
-      s1 += part[(int64_t)(b + 16) * 2 * D + d];
-      s2 += part[(int64_t)(b + 32) * 2 * D + d];
-      s3 += part[(int64_t)(b + 48) * 2 * D + d];
+      s0 += part[(int64_t)b * pd + d];
+      s1 += part[(int64_t)(b + 16) * pd + d];
+      s2 += part[(int64_t)(b + 32) * pd + d];
+      s3 += part[(int64_t)(b + 48) * pd + d];
     }
-    for (; b < blocks; b += 16) s0 += part[(int64_t)b * 2 * D + d];
+    for (; b < blocks; b += 16) s0 += part[(int64_t)b * pd + d];
   }
   sm[threadIdx.y][threadIdx.x] = (s0 + s1) + (s2 + s3);
   __syncthreads();
-  if (threadIdx.y != 0 || d >= 2 * D) return;
+  if (threadIdx.y != 0 || d >= pd) return;
   float s = 0.f;
 #pragma unroll
   for (int i = 0; i < 16; ++i) s += sm[i][threadIdx.x];
+  if (d >= 2 * D) {
+    if (rsum) rsum[d - 2 * D] = rsum_accumulate ? rsum[d - 2 * D] + s : s;
+    return;
+  }
   float* dst = d < D ? (dgamma ? dgamma + d : nullptr) : (dbeta ? dbeta + (d - D) : nullptr);
   if (dst) *dst = accumulate ? *dst + s : s;
 }
@@ -1108,20 +1125,32 @@ void layernorm_fwd(DType dt, const void* x, const float* gamma, const float* bet
 }
 
 int layernorm_bwd_blocks(int64_t rows) { return (int)std::max<int64_t>(1, std::min<int64_t>(148, (rows + 7) / 8)); }
-int64_t layernorm_bwd_scratch_floats(int64_t rows, int D) { return (int64_t)layernorm_bwd_blocks(rows) * 2 * D; }
+// Per-block partials (up to three D-wide rows each) and, after them, the
+// scratch of a column-sum pass over dres for the paths that do not fuse it.
+int64_t layernorm_bwd_scratch_floats(int64_t rows, int D) {
+  return (int64_t)layernorm_bwd_blocks(rows) * 3 * D + colsum_scratch_floats(rows, D);
+}
 
 void layernorm_bwd(DType dt, const void* x, const float* gamma, const float* mean, const float* rstd, const void* dy,
                    void* dx, float* dgamma, float* dbeta, bool accumulate, int64_t rows, int D, float* scratch,
-                   cudaStream_t s, const void* dres) {
+                   cudaStream_t s, const void* dres, float* dres_colsum, bool dres_colsum_accumulate) {
   const int blocks = layernorm_bwd_blocks(rows);
+  DLVK_CHECK(dres_colsum == nullptr || dres != nullptr, "layernorm_bwd: column sums of dres need dres");
+  // Paths without the fused sums: a column-sum pass over dres.
+  auto dres_sums = [&]() {
+    if (!dres_colsum) return;
+    float* cs = scratch + (int64_t)blocks * 3 * D;
+    colsum(dt, DType::F32, dres, rows, D, 1.f, dres_colsum, dres_colsum_accumulate,
+           colsum_scratch_floats(rows, D) > 0 ? cs : nullptr, s);
+  };
   if (dt == DType::BF16 && D % 256 == 0 && (D / 256 == 4 || D / 256 == 2 || D / 256 == 1)) {
     const bool al = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dy) |
                       reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(dres)) & 15) == 0;
     const int nv = D / 256;
     const int nt = dres ? 3 : 2;
-    const size_t ring = (size_t)8 * 3 * nt * nv * 32 * 16;  // reused for the [8][2D] fp32 partials
+    const size_t ring = (size_t)8 * 3 * nt * nv * 32 * 16;  // reused for the [8][2D or 3D] fp32 partials
     const size_t smem = ring + (size_t)D * 4;
-    if (al && ring >= (size_t)8 * 2 * D * 4 && smem <= 200 * 1024) {
+    if (al && ring >= (size_t)8 * (dres ? 3 : 2) * D * 4 && smem <= 200 * 1024) {
       auto launch = [&](auto kern) {
         DLVK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         launch_pdl(kern, dim3(blocks), dim3(256), smem, s, (const __nv_bfloat16*)x, gamma, mean, rstd,
@@ -1137,8 +1166,9 @@ void layernorm_bwd(DType dt, const void* x, const float* gamma, const float* mea
         else launch(ln_bwd_ring_kernel<1, false>);
       }
       DLVK_POST_LAUNCH();
-      launch_pdl(ln_bwd_final_kernel, dim3((2 * D + 31) / 32), dim3(32, 16), 0, s, (const float*)scratch, blocks, D,
-                 dgamma, dbeta, accumulate ? 1 : 0);
+      const int np = dres ? 3 : 2;
+      launch_pdl(ln_bwd_final_kernel, dim3((np * D + 31) / 32), dim3(32, 16), 0, s, (const float*)scratch, blocks, D,
+                 dgamma, dbeta, accumulate ? 1 : 0, np, dres_colsum, dres_colsum_accumulate ? 1 : 0);
       DLVK_POST_LAUNCH();
       return;
     }
@@ -1159,8 +1189,10 @@ void layernorm_bwd(DType dt, const void* x, const float* gamma, const float* mea
                                        (const T*)dres);
       });
       DLVK_POST_LAUNCH();
-      ln_bwd_final_kernel<<<(2 * D + 31) / 32, dim3(32, 16), 0, s>>>(scratch, blocks, D, dgamma, dbeta, accumulate ? 1 : 0);
+      ln_bwd_final_kernel<<<(2 * D + 31) / 32, dim3(32, 16), 0, s>>>(scratch, blocks, D, dgamma, dbeta, accumulate ? 1 : 0,
+                                                                    2, nullptr, 0);
       DLVK_POST_LAUNCH();
+      dres_sums();
       return;
     }
   }
@@ -1175,8 +1207,10 @@ void layernorm_bwd(DType dt, const void* x, const float* gamma, const float* mea
                                                       rows, D, (const T*)dres);
   });
   DLVK_POST_LAUNCH();
-  ln_bwd_final_kernel<<<(2 * D + 31) / 32, dim3(32, 16), 0, s>>>(scratch, blocks, D, dgamma, dbeta, accumulate ? 1 : 0);
+  ln_bwd_final_kernel<<<(2 * D + 31) / 32, dim3(32, 16), 0, s>>>(scratch, blocks, D, dgamma, dbeta, accumulate ? 1 : 0,
+                                                                2, nullptr, 0);
   DLVK_POST_LAUNCH();
+  dres_sums();
 }
 
 void dropout(DType dt, const void* x, void* y, int64_t n, const DropoutDesc& dd, cudaStream_t s) {

@@ -370,9 +370,9 @@ class TransformerBlockFn(torch.autograd.Function):
         def bgrad(p, grad):
             K.colsum(grad, out=p.grad, accumulate=p.take_accumulate_flag())
 
-        # FFN: y = f W2 + b2 + h
+        # FFN: y = f W2 + b2 + h (b2's gradient, the column sums of g, comes
+        # out of the LayerNorm backward below, which reads g as its residual)
         wgrad(f2.weight, f.t(), g)
-        bgrad(f2.bias, g)
         # ReLU backward and the FF1 bias gradient (column sums) fused
         if _FUSE_COLSUM:
             df = K.gemm(g, f2.weight.value.t(), relu_bits=fbits, colsum_out=f1.bias.grad,
@@ -384,7 +384,8 @@ class TransformerBlockFn(torch.autograd.Function):
         dh2 = K.gemm(df, f1.weight.value.t())
         acc = ln2.gamma.take_accumulate_flag()
         ln2.beta.take_accumulate_flag()
-        dh = NN.layernorm_bwd(h, ln2.gamma.master, m2, r2, dh2, ln2.gamma.grad, ln2.beta.grad, acc, dres=g)
+        dh = NN.layernorm_bwd(h, ln2.gamma.master, m2, r2, dh2, ln2.gamma.grad, ln2.beta.grad, acc, dres=g,
+                              dres_colsum=f2.bias.grad, dres_colsum_accumulate=f2.bias.take_accumulate_flag())
         # attention: h = a Wo + x
         wgrad(at.w_o, a2.t(), dh)
         da = K.gemm(dh, at.w_o.value.t())

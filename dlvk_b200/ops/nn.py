@@ -162,11 +162,19 @@ def layernorm_fwd(x, gamma, beta, eps: float):
     return y.to(x.dtype), mean.reshape(-1), rstd.reshape(-1)
 
 
-def layernorm_bwd(x, gamma, mean, rstd, dy, dgamma, dbeta, accumulate: bool, dres=None):
-    """dx (+ dres, the gradient of a residual branch sharing the input)."""
+def layernorm_bwd(x, gamma, mean, rstd, dy, dgamma, dbeta, accumulate: bool, dres=None, dres_colsum=None,
+                  dres_colsum_accumulate: bool = False):
+    """dx (+ dres, the gradient of a residual branch sharing the input).
+    dres_colsum (fp32 [D]) receives, or with dres_colsum_accumulate adds, the
+    column sums of dres: the bias gradient of the biased GEMM whose output
+    gradient dres is, taken in the same pass."""
     if native(x):
-        return N().layernorm_bwd(x, gamma, mean, rstd, dy, dgamma, dbeta, accumulate, dres)
+        return N().layernorm_bwd(x, gamma, mean, rstd, dy, dgamma, dbeta, accumulate, dres,
+                                 dres_colsum=dres_colsum, dres_colsum_accumulate=dres_colsum_accumulate)
     if dres is not None:
+        if dres_colsum is not None:
+            cs = dres.float().reshape(-1, dres.shape[-1]).sum(0)
+            dres_colsum.add_(cs) if dres_colsum_accumulate else dres_colsum.copy_(cs)
         out = layernorm_bwd(x, gamma, mean, rstd, dy, dgamma, dbeta, accumulate)
         return (out.float() + dres.float()).to(x.dtype)
     D = x.shape[-1]

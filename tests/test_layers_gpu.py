@@ -128,9 +128,11 @@ def test_layernorm(dtype, rows):
     close(dgam, gr.grad, tol * 2)
     close(dbet, br.grad, tol * 2)
     dres = torch.randn_like(yr).to(dtype)
-    dx2 = C.layernorm_bwd(x, gamma, mean, rstd, g, dgam, dbet, True, dres)
+    cs = torch.full((1024,), 2.0, device="cuda")
+    dx2 = C.layernorm_bwd(x, gamma, mean, rstd, g, dgam, dbet, True, dres, dres_colsum=cs, dres_colsum_accumulate=True)
     close(dx2, xr.grad + dres.float(), tol * 2)
     close(dgam, 2 * gr.grad, tol * 2)
+    close(cs, 2.0 + dres.float().sum(0), 1e-4)  # the residual gradient's column sums, fused
 
 
 def test_dropout_matches_cpu_oracle():
