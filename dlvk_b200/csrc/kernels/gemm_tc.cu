@@ -273,6 +273,32 @@ __device__ __forceinline__ void add_row_residual(const TcParams& p, int64_t rb, 
   }
 }
 
+// Zero v[j] where the bf16 mask Mk[row, n0 + j] <= 0 (row-per-lane
+// epilogue; the lane reads its row's 32 mask values as 16-byte vectors).
+__device__ __forceinline__ void mask_row_bf16(const TcParams& p, int64_t mb, int row, int n0, float* v) {
+  if (row >= p.M || n0 >= p.N) return;
+  const int64_t off = mb + (int64_t)row * p.ldm + n0;
+  if (n0 + 32 <= p.N && p.m_vec) {
+    const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.Mk) + off);
+    uint4 u[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) u[q] = src[q];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[q]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(h[k]);
+        v[8 * q + 2 * k] = f.x > 0.f ? v[8 * q + 2 * k] : 0.f;
+        v[8 * q + 2 * k + 1] = f.y > 0.f ? v[8 * q + 2 * k + 1] : 0.f;
+      }
+    }
+  } else {
+    for (int j = 0; j < 32 && n0 + j < p.N; ++j)
+      if (!(__bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.Mk)[off + j]) > 0.f)) v[j] = 0.f;
+  }
+}
+
 // Word of the ReLU bitmask for one row's 32 columns [n0, n0 + 32): bit j set
 // where v[j] > 0 (after the activation); columns past N stay clear.
 __device__ __forceinline__ void store_bits(const TcParams& p, int row, int n0, const float* v) {
@@ -725,10 +751,10 @@ __global__ void __launch_bounds__(320, 1)
     const int q = warp & 3;
     const int half = ew >> 2;
     float* stg = epi + ew * (32 * 33);
-    // A bf16 residual alone is added in registers; with beta or a mask (or
-    // an fp32 output) the chunk goes through the staged path, which handles
-    // all three.
-    const bool staged = (p.Mk != nullptr) || (p.beta != 0.f) || (p.R != nullptr && p.out_f32);
+    // A bf16 residual and a bf16 ReLU mask are applied in registers; with
+    // beta (or an fp32 output with either) the chunk goes through the staged
+    // path, which handles all three.
+    const bool staged = (p.beta != 0.f) || (p.out_f32 && (p.R != nullptr || p.Mk != nullptr));
     constexpr int NCH = BN / 64;  // 32-column chunks per warp
     int acc = 0, ecount = 0;
     uint32_t acc_phase = 0;
@@ -800,6 +826,7 @@ __global__ void __launch_bounds__(320, 1)
             if (p.bias && n0 < p.N) add_bias<32>(p.bias, p.bias_f32, n0, min(32, p.N - n0), v);
             if (p.R) add_row_residual(p, rb, row0 + lane, n0, v);
             apply_act<32>(p.act, v);
+            if (p.Mk) mask_row_bf16(p, mb, row0 + lane, n0, v);
             if (p.bits_in) mask_row_bits(p, row0 + lane, n0, v);
             if (p.bits_out && n0 < p.N && row0 + lane < p.M) store_bits(p, row0 + lane, n0, v);
             // Boxes start on 1024-byte boundaries (the swizzled box layout is
@@ -881,6 +908,7 @@ __global__ void __launch_bounds__(320, 1)
             if (p.bias) add_bias<32>(p.bias, p.bias_f32, n0, min(32, p.N - n0), v);
             if (p.R) add_row_residual(p, rb, row, n0, v);
             apply_act<32>(p.act, v);
+            if (p.Mk) mask_row_bf16(p, mb, row, n0, v);
             if (p.bits_in) mask_row_bits(p, row, n0, v);
             if (p.bits_out) store_bits(p, row, n0, v);
             const bool full = (n0 + 32 <= p.N) && p.vec_ok;
@@ -1240,8 +1268,11 @@ bool gemm_tc_colsum_ok(DType out_dt, const GemmArgs& a) {
   auto rows16 = [&](const void* p, int64_t ld) {
     return p == nullptr || (al16(p) && (ld * esz) % 16 == 0);
   };
-  // naux == 0: the TMA-store epilogue sums the columns in registers
-  return (naux == 1 || (naux == 0 && tma_c_enabled())) && a.batch == 1 && a.batch2 == 1 && a.M % 32 == 0 &&
+  // Staged epilogues (beta, or an fp32 output with a residual or mask) sum
+  // their transposed chunk on the fast path (exactly one such input); the
+  // others sum in registers on the TMA-store path.
+  const bool staged = a.beta != 0.f || (out_dt == DType::F32 && (a.residual != nullptr || a.relu_mask != nullptr));
+  return (staged ? naux == 1 : tma_c_enabled()) && a.batch == 1 && a.batch2 == 1 && a.M % 32 == 0 &&
          a.N % 32 == 0 && al16(a.C) &&
          (a.ldc * esz) % 16 == 0 && rows16(a.residual, a.ldr) && rows16(a.relu_mask, a.ldm);
 }
@@ -1356,7 +1387,8 @@ void gemm_tc_impl(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err
     splits = 1;  // the sums are taken over final outputs
     // without a staged input the TMA-store epilogue sums in registers, which
     // the 512-wide tile's instantiation leaves out (register budget)
-    if (BN == 512 && a.beta == 0.f && a.residual == nullptr && a.relu_mask == nullptr) BN = 256;
+    if (BN == 512 && a.beta == 0.f && !(out_dt == DType::F32 && (a.residual != nullptr || a.relu_mask != nullptr)))
+      BN = 256;
   }
   if (a.relu_bits != nullptr || a.relu_bits_out != nullptr)
     DLVK_CHECK(a.batch == 1 && a.batch2 == 1 && a.ldbits >= (a.N + 31) / 32, "gemm_tc: ReLU bitmask needs a 2-D GEMM");
@@ -1495,7 +1527,7 @@ void gemm_tc_impl(DType out_dt, const GemmArgs& a, cudaStream_t s, uint32_t* err
     return;
   }
   const CUtensorMap tc = make_c_map(p, a.M, a.N);
-  DLVK_CHECK(!(p.colsum && p.beta == 0.f && !p.R && !p.Mk && p.tma_c == 0),
+  DLVK_CHECK(!(p.colsum && p.beta == 0.f && !(p.out_f32 && (p.R || p.Mk)) && p.tma_c == 0),
              "gemm_tc: column sums without a staged input need the TMA-store epilogue");
   if (pair && BN == 512) launch_tc_pair<512>(ta, tb, tc, p, max_ctas, s);
   else if (pair) launch_tc_pair<256>(ta, tb, tc, p, max_ctas, s);

@@ -21,6 +21,9 @@ from .core import ACT_NONE, ACT_RELU, ACT_GELU
 # DLVK_FUSE_COLSUM=0: bias gradients by a separate column-sum pass instead of
 # the producing GEMM's epilogue.
 _FUSE_COLSUM = os.environ.get("DLVK_FUSE_COLSUM", "1") != "0"
+# The FFN's ReLU backward from a bitmask written by the forward GEMM (1), or
+# from the bf16 activation itself (0).
+_RELU_BITS = os.environ.get("DLVK_RELU_BITS", "1") != "0"
 
 
 def _flat2(t: torch.Tensor) -> torch.Tensor:
@@ -346,7 +349,7 @@ class TransformerBlockFn(torch.autograd.Function):
         h = K.gemm(a2, at.w_o.value, residual=x2)
         h2, m2, r2 = NN.layernorm_fwd(h, ln2.gamma.master, ln2.beta.master, ln2.eps)
         # the ReLU's backward reads one bit per element instead of f
-        fbits = K.relu_bits_like(h2.shape[0], f1.weight.value.shape[1], h2.device)
+        fbits = K.relu_bits_like(h2.shape[0], f1.weight.value.shape[1], h2.device) if _RELU_BITS else None
         f = K.gemm(h2, f1.weight.value, bias=f1.bias.master, act=ACT_RELU, relu_bits_out=fbits)
         y = K.gemm(f, f2.weight.value, bias=f2.bias.master, residual=h)
         ctx.blk, ctx.dims = blk, (B, S, H, D, scale)
@@ -374,11 +377,12 @@ class TransformerBlockFn(torch.autograd.Function):
         # out of the LayerNorm backward below, which reads g as its residual)
         wgrad(f2.weight, f.t(), g)
         # ReLU backward and the FF1 bias gradient (column sums) fused
+        mask = dict(relu_bits=fbits) if fbits is not None else dict(relu_mask=f)
         if _FUSE_COLSUM:
-            df = K.gemm(g, f2.weight.value.t(), relu_bits=fbits, colsum_out=f1.bias.grad,
-                        colsum_accumulate=f1.bias.take_accumulate_flag())
+            df = K.gemm(g, f2.weight.value.t(), colsum_out=f1.bias.grad,
+                        colsum_accumulate=f1.bias.take_accumulate_flag(), **mask)
         else:
-            df = K.gemm(g, f2.weight.value.t(), relu_bits=fbits)
+            df = K.gemm(g, f2.weight.value.t(), **mask)
             bgrad(f1.bias, df)
         wgrad(f1.weight, h2.t(), df)
         dh2 = K.gemm(df, f1.weight.value.t())
