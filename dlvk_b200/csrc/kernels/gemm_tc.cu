@@ -1303,7 +1303,10 @@ CUtensorMap make_c_map(TcParams& p, int64_t M, int64_t N, bool reduce = false) {
   CUtensorMap tc;
   std::memset(&tc, 0, sizeof(tc));
   p.tma_c = 0;
-  if (p.R != nullptr || p.Mk != nullptr || p.beta != 0.f || p.i8 || !p.vec_ok || !tma_c_enabled()) return tc;
+  // A bf16 residual or ReLU mask is applied in registers on this path; with
+  // an fp32 output either one (and beta) takes the staged epilogue instead.
+  if ((p.out_f32 && (p.R != nullptr || p.Mk != nullptr)) || p.beta != 0.f || p.i8 || !p.vec_ok || !tma_c_enabled())
+    return tc;
   const uint64_t esz = p.out_f32 ? 4 : 2;
   auto pick = [&](int64_t cnt, int64_t stride) -> uint64_t {
     return cnt > 1 ? (uint64_t)stride * esz : (uint64_t)M * (uint64_t)p.ldc * esz;
