@@ -9,14 +9,15 @@
 // [B, S, 3, H, 64] (bf16) through one 2-D TMA map over [B*S, 3*H*64].
 //
 // Forward (flash_fwd_kernel): persistent CTAs walk (batch, head, 128-query
-// tile) items.  Warp 0 issues TMA loads (Q double-buffered, K/V in a
-// 3-stage ring), warp 1 issues tcgen05.mma (S = Q K^T into one of two TMEM
-// score buffers; O += P V into a TMEM accumulator), warps 2..5 own one
-// query row per thread: they read the score row from TMEM, keep the online
-// max / sum in the log2 domain, rescale O in TMEM only when a row's max grew
-// by more than 2^8 (warp-uniform decision, since tcgen05.ld/st are
-// warp-collective), write P (bf16) into shared memory in the 128-byte
-// swizzled K-major layout the next MMA reads, and finally normalise O and
+// tile) items, two at a time (see the kernel).  Warp 0 issues TMA loads (Q
+// per stream, K/V in a 5-stage ring), warp 1 issues tcgen05.mma (S = Q K^T
+// into a TMEM score buffer per stream; O += P V into a TMEM accumulator,
+// with P read from TMEM), and the softmax warps own one query row per
+// thread: they load the whole score row from TMEM into registers (releasing
+// the score buffer at once), keep the online max / sum in the log2 domain,
+// rescale O in TMEM only when a row's max grew by more than 2^8
+// (warp-uniform decision, since tcgen05.ld/st are warp-collective), write P
+// as bf16 pairs into TMEM for the next MMA, and finally normalise O and
 // store it with the row's log-sum-exp (log2 units) for the backward pass.
 //
 // Backward (flash_bwd_kernel): persistent CTAs walk (batch, head, 128-key
@@ -26,14 +27,13 @@
 // P^T = exp2(S^T c - lse) and dS^T = P^T (dP^T - delta) into shared memory;
 // the MMA warp then accumulates dV += P^T dO and dK += dS^T Q in TMEM and
 // computes dQ = dS K reading the same dS^T tile as an MN-major operand.
-// Software pipeline: the next query tile's S^T / dP^T are issued as soon as
-// the compute warps have read the current ones (before the current tile's
-// gradient MMAs), and dQ alternates between two TMEM buffers whose readout
-// happens one step late, so the gradient MMAs of step g run while the
-// compute warps reduce the dQ of step g-1.  The dQ tile goes through shared
-// memory to the global fp32 accumulator with TMA bulk reduce-add; dK / dV
-// are written to the fused gradient buffer [B, S, 3, H, 64] when the key
-// tile is done.
+// Software pipeline: P^T / dS^T are double-buffered, so the compute warps
+// build step g+1's tiles while the tensor cores run step g's gradient MMAs;
+// the next query tile's S^T / dP^T are issued as soon as the compute warps
+// have read the current ones; dQ alternates between two TMEM buffers whose
+// readout happens one step late.  The dQ tile goes through shared memory to
+// the global fp32 accumulator with TMA bulk reduce-add; dK / dV are written
+// to the fused gradient buffer [B, S, 3, H, 64] when the key tile is done.
 //
 // Every mbarrier wait is bounded (mbar_wait: error word + early exit).
 #include <cuda.h>
@@ -78,15 +78,6 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32
   return __all_sync(0xffffffffu, ok);
 }
 
-// Bounded barrier among the 128 compute threads on an mbarrier of count 128
-// (bar.sync has no timeout; this gives up with the error word set).
-__device__ __forceinline__ bool group_sync(uint64_t* bar, uint32_t& phase, uint32_t* err) {
-  mbar_arrive(bar);
-  const bool ok = mbar_wait(bar, phase, err);
-  phase ^= 1u;
-  return __all_sync(0xffffffffu, ok);
-}
-
 struct FwdP {
   __nv_bfloat16* out;
   float* lse;
@@ -95,27 +86,42 @@ struct FwdP {
   uint32_t* err;
 };
 
+// D(tmem) (+)= A(tmem) * B(smem desc), kind::f16: A is read from tensor
+// memory (lane = row, two bf16 per 32-bit column, K-major), B from shared
+// memory.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Two softmax warpgroups ("streams" 0 and 1) work on independent items in
 // ping-pong: CTA c gives items c, c + 2g, ... to stream 0 and c + g,
 // c + 3g, ... to stream 1 (g = grid size).  Each stream has its own TMEM
-// score buffer S and output accumulator O, its own Q tile and its own P tile
-// in shared memory; the K / V ring, the TMA producer warp and the MMA warp
-// are shared.  While one stream normalises and stores its finished item, or
-// waits for its next scores, the other keeps the exponential unit busy.
+// score buffer S, probability tile P and output accumulator O, and its own
+// Q tile in shared memory; the K / V ring, the TMA producer warp and the MMA
+// warp are shared.  While one stream normalises and stores its finished
+// item, or waits for its next scores, the other keeps the exponential unit
+// busy.
 //
-// TMEM (512 columns): S0 0..127, S1 128..255, O0 256..319, O1 320..383.
-// Shared memory: Q x2 | (K, V) x FWD_KV_STAGES | P x2 (32 KB each) | barriers.
-constexpr int FWD_KV_STAGES = 4;
+// TMEM (512 columns): S0 0..127, S1 128..255, O0 256..319, O1 320..383,
+// P0 384..447, P1 448..511 (P as bf16 pairs: 128 keys in 64 columns).  The
+// PV product reads P straight from tensor memory.
+// Shared memory: Q x2 | (K, V) x FWD_KV_STAGES | barriers.
+constexpr int FWD_KV_STAGES = 5;
 constexpr int FWD_THREADS = 64 + 2 * 128;
-constexpr int FWD_SMEM = 2 * TILE + FWD_KV_STAGES * 2 * TILE + 2 * 2 * TILE + 256 + 1024;
+constexpr int FWD_SMEM = 2 * TILE + FWD_KV_STAGES * 2 * TILE + 256 + 1024;
 
 __global__ void __launch_bounds__(FWD_THREADS, 1) flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, FwdP p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                   // stream t: sQ + t * TILE
   uint8_t* sKV = smem + 2 * TILE;                       // stage k: K at k * 2 * TILE, V at + TILE
-  uint8_t* sP = sKV + FWD_KV_STAGES * 2 * TILE;         // stream t: sP + t * 2 * TILE
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * 2 * TILE);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + FWD_KV_STAGES * 2 * TILE);
   uint64_t* q_full = bars;                              // [2] per stream
   uint64_t* q_empty = bars + 2;                         // [2]
   uint64_t* kv_full = bars + 4;                         // [FWD_KV_STAGES]
@@ -210,6 +216,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) flash_fwd_kernel(const __grid_
       auto step = [&](int r, int j, int t, St& st) {
         if (item_of(r, t) >= items) return true;
         const uint32_t tS = tbase + (uint32_t)(t * 128), tO = tbase + 256u + (uint32_t)(t * 64);
+        const uint32_t tP = tbase + 384u + (uint32_t)(t * 64);
         if (j < nt) {
           if (j == 0 && !mbar_wait(&q_full[t], r & 1, p.err)) return false;
           if (!mbar_wait(&kv_full[kvs], kvph, p.err) || !mbar_wait(&s_empty[t], st.sph ^ 1u, p.err)) return false;
@@ -232,11 +239,12 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) flash_fwd_kernel(const __grid_
           st.pph ^= 1u;
           tc_fence_after();
           const uint32_t va = smem_u32(sKV + st.prev * 2 * TILE + TILE);
-          const uint32_t pa = smem_u32(sP + t * 2 * TILE);
+          // O += P V: A = P from TMEM (16 keys = 8 columns per MMA), B = V
+          // MN-major [keys x d].
 #pragma unroll
           for (int k = 0; k < FT / 16; ++k)
-            mma_f16(tO, make_sw128_desc(pa + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024),
-                    make_sw128_desc(va + k * 2048, 16384, 1024), id_o, (j > 1 || k > 0) ? 1u : 0u);
+            mma_f16_ts(tO, tP + (uint32_t)(k * 8), make_sw128_desc(va + k * 2048, 16384, 1024), id_o,
+                       (j > 1 || k > 0) ? 1u : 0u);
           mma_commit(&kv_empty[st.prev]);
           mma_commit(&pv_done[t]);
         }
@@ -260,7 +268,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) flash_fwd_kernel(const __grid_
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t tS = tbase + lane_off + (uint32_t)(t * 128), tO = tbase + lane_off + 256u + (uint32_t)(t * 64);
-    uint8_t* prow = sP + t * 2 * TILE;
+    const uint32_t tP = tbase + lane_off + 384u + (uint32_t)(t * 64);
     uint32_t sph = 0, pvph = 0;
     for (int r = 0;; ++r) {
       const int item = item_of(r, t);
@@ -272,76 +280,52 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) flash_fwd_kernel(const __grid_
         if (!warp_wait(&s_full[t], sph, p.err)) { ok = false; break; }
         sph ^= 1u;
         tc_fence_after();
-        // Three TMEM reads of the score row per tile: columns 0..63 for the
-        // max, columns 64..127 for the max and kept in registers for their
-        // exponentials, then columns 0..63 again (a thread has 168 registers
-        // in a 320-thread block, too few to hold all 128 scores).
+        // The whole score row (128 keys) in registers, so the score buffer
+        // is released right away for the stream's next tile.
+        uint32_t sc[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS + (uint32_t)(c * 32), sc[c]);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty[t]);
         float mp[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) mp[k] = -INFINITY;
-        {
-          uint32_t sa[2][32];
-          tmem_ld32(tS, sa[0]);
-          tmem_ld32(tS + 32u, sa[1]);
-          tmem_ld_wait();
 #pragma unroll
-          for (int c = 0; c < 2; ++c)
+        for (int c = 0; c < 4; ++c)
 #pragma unroll
-            for (int i = 0; i < 32; ++i) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(sa[c][i]));
-        }
-        if (j > 0) {
-          // The previous tile's PV must be done before P is rewritten or O
-          // rescaled (it was queued right behind this tile's S).
-          if (!warp_wait(&pv_done[t], pvph, p.err)) { ok = false; break; }
-          pvph ^= 1u;
-          tc_fence_after();
-        }
-        uint32_t sb[2][32];
-        tmem_ld32(tS + 64u, sb[0]);
-        tmem_ld32(tS + 96u, sb[1]);
-        tmem_ld_wait();
-#pragma unroll
-        for (int c = 0; c < 2; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(sb[c][i]));
+          for (int i = 0; i < 32; ++i) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(sc[c][i]));
         float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
         mx *= p.c;
         const bool need = mx > m + 8.f;  // lazy rescale: keep the old reference max while it is within 2^8
         const float m_new = need ? mx : m;
         const float alpha = need ? hw_exp2(m - m_new) : 1.f;
-        // Exponentials straight to P as bf16; the row sum uses the fp32 values.
+        if (j > 0) {
+          // The previous tile's PV must be done before P is rewritten or O
+          // rescaled.
+          if (!warp_wait(&pv_done[t], pvph, p.err)) { ok = false; break; }
+          pvph ^= 1u;
+          tc_fence_after();
+        }
+        // Exponentials straight to P (bf16 pairs in TMEM); the row sum uses
+        // the fp32 values.
         float sp8[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) sp8[k] = 0.f;
-        auto emit = [&](const uint32_t (&sc)[32], int chunk) {  // 32 scores -> P chunk (4 x 16 bytes)
-          uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const float e0 = hw_exp2(fmaf(__uint_as_float(sc[i]), p.c, -m_new));
-            const float e1 = hw_exp2(fmaf(__uint_as_float(sc[i + 1]), p.c, -m_new));
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 64; i += 2) {
+            const int c = 2 * hf + (i >> 5);
+            const float e0 = hw_exp2(fmaf(__uint_as_float(sc[c][i & 31]), p.c, -m_new));
+            const float e1 = hw_exp2(fmaf(__uint_as_float(sc[c][(i & 31) + 1]), p.c, -m_new));
             sp8[i & 7] += e0;
             sp8[(i + 1) & 7] += e1;
             pk[i >> 1] = pack2(e0, e1);
           }
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<uint4*>(prow + sw_off(row, chunk * 4 + q)) =
-                make_uint4(pk[q * 4], pk[q * 4 + 1], pk[q * 4 + 2], pk[q * 4 + 3]);
-        };
-        emit(sb[0], 2);
-        emit(sb[1], 3);
-        asm volatile("" ::: "memory");  // keeps those P stores (and their math) ahead of the next TMEM read
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          uint32_t sc[32];
-          tmem_ld32(tS + (uint32_t)(c * 32), sc);
-          tmem_ld_wait();
-          if (c == 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_empty[t]);  // the score buffer is read out
-          }
-          emit(sc, c);
+          tmem_st32(tP + (uint32_t)(hf * 32), pk);
         }
         if (j > 0 && __any_sync(0xffffffffu, need)) {
 #pragma unroll
@@ -353,11 +337,10 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) flash_fwd_kernel(const __grid_
             for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
             tmem_st32(tO + (uint32_t)(c * 32), o);
           }
-          tmem_st_wait();
         }
+        tmem_st_wait();
         l = l * alpha + (((sp8[0] + sp8[1]) + (sp8[2] + sp8[3])) + ((sp8[4] + sp8[5]) + (sp8[6] + sp8[7])));
         m = m_new;
-        fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[t]);
@@ -371,19 +354,18 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) flash_fwd_kernel(const __grid_
       const float inv = 1.f / l;
       const int64_t grow = (int64_t)b * p.S + (int64_t)qt * FT + row;
       uint4* dst = reinterpret_cast<uint4*>(p.out + grow * p.E + h * FD);
+      uint32_t o[2][32];
+      tmem_ld32(tO, o[0]);
+      tmem_ld32(tO + 32u, o[1]);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_empty[t]);
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
-        uint32_t o[32];
-        tmem_ld32(tO + (uint32_t)(hf * 32), o);
-        tmem_ld_wait();
-        if (hf == 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&o_empty[t]);
-        }
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          const uint32_t* src = &o[c * 8];
+          const uint32_t* src = &o[hf][c * 8];
           uint4 v;
           v.x = pack2(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
           v.y = pack2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
@@ -415,14 +397,30 @@ struct BwdP {
   uint32_t* err;
 };
 
-// Shared memory: K | V | (Q, dO) x2 | P^T (32 KB) | dS^T (32 KB) | dQ staging
-// (2 x 16 KB fp32, 128-byte swizzled) | lse x2 | delta x2 | barriers.
-constexpr int BWD_SMEM = 2 * TILE + 2 * 2 * TILE + 2 * TILE + 2 * TILE + 2 * TILE + 4 * 128 * 4 + 256 + 1024;
+// Shared memory: K | V | (Q, dO) x2 | P^T x2 (32 KB each) | dS^T x2 |
+// (lse, delta) x2 | barriers.  The producer copies each query tile's lse and
+// delta (128 floats each) into the stage of its Q / dO tiles, in the same
+// transaction.  P^T and dS^T are double-buffered (step g uses buffer
+// g & 1) so that the compute warps build step g+1's tiles while the tensor
+// cores run step g's gradient MMAs.  Step g's dQ tile is staged for its TMA
+// reduce-add in P^T buffer g & 1, which is free from the end of step g's
+// gradient MMAs until step g+2 writes its P^T there.
+constexpr int BWD_SMEM_USED = 14 * TILE + 4 * 128 * 4 + 256;
+constexpr int BWD_SMEM = 227 * 1024;  // the opt-in maximum; the kernel checks that the base alignment fits
+static_assert(BWD_SMEM_USED <= BWD_SMEM, "backward shared memory");
 
 __device__ __forceinline__ void tma_reduce_add_2d(const void* tmap, const void* src, int x, int y) {
   asm volatile(
       "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
       "r"(smem_u32(src)), "r"(x), "r"(y)
+      : "memory");
+}
+// Untiled bulk copy global -> this CTA's shared memory (16-byte aligned
+// addresses, size a multiple of 16), completion counted on `bar` in bytes.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
@@ -437,27 +435,31 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
                                                            const __grid_constant__ CUtensorMap tm_dq, BwdP p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // The layout needs all but 768 bytes of the allocation: a dynamic
+  // shared-memory base further than that from a 1024-byte boundary cannot
+  // hold it (the same decision in every thread, before any barrier).
+  if ((int)(smem - smem_raw) + BWD_SMEM_USED > BWD_SMEM) {
+    if (threadIdx.x == 0) atomicCAS(p.err, 0u, (uint32_t)DLVK_ERR_BAD_ARG);
+    return;
+  }
   uint8_t* sK = smem;
   uint8_t* sV = smem + TILE;
   uint8_t* sQD = smem + 2 * TILE;            // stage s: Q at s*2*TILE, dO at +TILE
-  uint8_t* sPT = smem + 6 * TILE;            // 32 KB
-  uint8_t* sDS = smem + 8 * TILE;            // 32 KB
-  uint8_t* sDQ = smem + 10 * TILE;           // 32 KB fp32 staging
-  float* sLse = reinterpret_cast<float*>(smem + 12 * TILE);   // [2][128]
-  float* sDel = sLse + 256;                                   // [2][128]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sDel + 256);
+  uint8_t* sPT = smem + 6 * TILE;            // buffer u at u*2*TILE (32 KB each)
+  uint8_t* sDS = smem + 10 * TILE;           // buffer u at u*2*TILE
+  float* sLD = reinterpret_cast<float*>(smem + 14 * TILE);    // stage s: lse at s*256, delta at s*256 + 128
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sLD + 512);
   uint64_t* kv_full = bars;
   uint64_t* kv_empty = bars + 1;
   uint64_t* qd_full = bars + 2;   // 2
   uint64_t* qd_empty = bars + 4;  // 2
   uint64_t* st_full = bars + 6;
-  uint64_t* ds_full = bars + 7;
-  uint64_t* dq_full = bars + 8;
-  uint64_t* dq_free = bars + 14;  // 2: dQ TMEM buffer g & 1 read out
-  uint64_t* kv_done = bars + 10;   // dK, dV accumulated for the item
-  uint64_t* kv_read = bars + 11;   // dK, dV read out of TMEM
-  uint64_t* cw_bar = bars + 12;    // compute-warp group barrier (one arrival per compute thread)
-  uint64_t* st_free = bars + 13;   // S^T / dP^T read out of TMEM
+  uint64_t* ds_full = bars + 7;   // 2: P^T / dS^T buffer u written
+  uint64_t* dq_full = bars + 9;   // 2: gradient MMAs of a step using dQ TMEM buffer u complete
+  uint64_t* dq_free = bars + 11;  // 2: dQ TMEM buffer u read out
+  uint64_t* kv_done = bars + 13;  // dK, dV accumulated for the item
+  uint64_t* kv_read = bars + 14;  // dK, dV read out of TMEM
+  uint64_t* st_free = bars + 15;  // S^T / dP^T read out of TMEM
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -470,15 +472,13 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
     for (int i = 0; i < 2; ++i) {
       mbar_init(&qd_full[i], 1);
       mbar_init(&qd_empty[i], 1);
+      mbar_init(&ds_full[i], BWD_COMPUTE_WARPS);
+      mbar_init(&dq_full[i], 1);
+      mbar_init(&dq_free[i], BWD_COMPUTE_WARPS);
     }
     mbar_init(st_full, 1);
-    mbar_init(ds_full, BWD_COMPUTE_WARPS);
-    mbar_init(dq_full, 1);
-    mbar_init(&dq_free[0], BWD_COMPUTE_WARPS);
-    mbar_init(&dq_free[1], BWD_COMPUTE_WARPS);
     mbar_init(kv_done, 1);
     mbar_init(kv_read, BWD_COMPUTE_WARPS);
-    mbar_init(cw_bar, 32 * BWD_COMPUTE_WARPS);
     mbar_init(st_free, BWD_COMPUTE_WARPS);
     fence_barrier_init();
   }
@@ -509,9 +509,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
         for (int i = 0; i < nt; ++i) {
           if (!mbar_wait(&qd_empty[qs], qph ^ 1u, p.err)) { ok = false; break; }
           uint8_t* d = sQD + qs * 2 * TILE;
-          mbar_arrive_expect_tx(&qd_full[qs], 2 * TILE);
+          const int64_t lo = ((int64_t)b * p.H + h) * p.S + (int64_t)i * FT;
+          mbar_arrive_expect_tx(&qd_full[qs], 2 * TILE + 2 * FT * 4);
           tma_load_2d(d, &tm_qkv, &qd_full[qs], h * FD, b * p.S + i * FT);
           tma_load_2d(d + TILE, &tm_do, &qd_full[qs], h * FD, b * p.S + i * FT);
+          bulk_load(sLD + qs * 256, p.lse + lo, FT * 4, &qd_full[qs]);
+          bulk_load(sLD + qs * 256 + 128, p.delta + lo, FT * 4, &qd_full[qs]);
           if (++qs == 2) {
             qs = 0;
             qph ^= 1u;
@@ -524,13 +527,13 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
       const uint32_t id_st = make_idesc(1, 1, 1, false, false, 128, 128);  // S^T, dP^T: K-major A and B
       const uint32_t id_kv = make_idesc(1, 1, 1, false, true, 128, 64);    // dV, dK: K-major A, MN-major B
       const uint32_t id_q = make_idesc(1, 1, 1, true, true, 128, 64);      // dQ: MN-major A and B
-      const uint32_t ka = smem_u32(sK), va = smem_u32(sV), pta = smem_u32(sPT), dsa = smem_u32(sDS);
-      // Steps are numbered g across items; step g uses Q / dO stage g & 1.
-      // Step g+1's S^T / dP^T go out as soon as the compute warps have read
-      // step g's (st_free), ahead of step g's gradient MMAs, so the tensor
-      // cores run while the compute warps take the exponentials.
+      const uint32_t ka = smem_u32(sK), va = smem_u32(sV);
+      // Steps are numbered g across items; step g uses Q / dO stage, P^T /
+      // dS^T buffer and dQ TMEM buffer g & 1.  Step g+1's S^T / dP^T go out
+      // as soon as the compute warps have read step g's (st_free), ahead of
+      // step g's gradient MMAs.
       int64_t g = 0;
-      uint32_t stfph = 0, dsph = 0;
+      uint32_t stfph = 0;
       bool ok = true;
       auto issue_scores = [&](int64_t gs) -> bool {
         const int st = (int)(gs & 1);
@@ -556,15 +559,16 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
         if (!issue_scores(g)) break;
         for (int i = 0; i < nt; ++i, ++g) {
           const int cur = (int)(g & 1);
+          const uint32_t par = (uint32_t)((g >> 1) & 1);
           if (i + 1 < nt && !issue_scores(g + 1)) { ok = false; break; }
-          if (!mbar_wait(ds_full, dsph, p.err)) { ok = false; break; }
-          dsph ^= 1u;
+          if (!mbar_wait(&ds_full[cur], par, p.err)) { ok = false; break; }
           if (i == 0 && !mbar_wait(kv_read, (it & 1) ^ 1u, p.err)) { ok = false; break; }  // previous dK / dV read
           // dQ buffer g & 1 was read out two steps ago
-          if (!mbar_wait(&dq_free[cur], (uint32_t)((g >> 1) & 1) ^ 1u, p.err)) { ok = false; break; }
+          if (!mbar_wait(&dq_free[cur], par ^ 1u, p.err)) { ok = false; break; }
           tc_fence_after();
           const uint32_t tdq = tbase + 384 + 64 * cur;
           const uint32_t qa = smem_u32(sQD + cur * 2 * TILE), doa = qa + TILE;
+          const uint32_t pta = smem_u32(sPT + cur * 2 * TILE), dsa = smem_u32(sDS + cur * 2 * TILE);
 #pragma unroll
           for (int k = 0; k < FT / 16; ++k) {
             const uint32_t koff = (uint32_t)((k >> 2) * 16384 + (k & 3) * 32);
@@ -577,7 +581,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
             mma_f16(tdq, make_sw128_desc(dsa + k * 2048, 16384, 1024),
                     make_sw128_desc(ka + k * 2048, 16384, 1024), id_q, k > 0 ? 1u : 0u);
           }
-          mma_commit(dq_full);
+          mma_commit(&dq_full[cur]);
           mma_commit(&qd_empty[cur]);
         }
         if (!ok) break;
@@ -592,40 +596,34 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
     const int quarter = warp & 3;
     const int hf = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
-    const int tid = threadIdx.x - 64;     // 0..255
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    uint32_t stph = 0, dqph = 0, cwph = 0;
-    int it = 0, ib = 0;
+    uint32_t stph = 0;
+    int it = 0;
+    int64_t g = 0;
     bool ok = true;
     // The dQ tile of step g leaves TMEM during step g+1, after that step's
-    // P^T / dS^T tiles are out: it sits in one of two TMEM buffers, so the
-    // gradient MMAs of step g+1 need not wait for it.  dq_x / dq_y are its
-    // coordinates in dQ.
+    // P^T / dS^T tiles are written: it sits in one of two TMEM buffers, so
+    // the gradient MMAs of step g+1 need not wait for it.  dq_x / dq_y are
+    // its coordinates in dQ.
     bool dq_pending = false;
-    int dq_x = 0, dq_y = 0, dq_buf = 1;  // toggled to the step's buffer (g & 1) when it becomes pending
-    auto wait_dq = [&]() -> bool {  // the pending step's gradient MMAs are complete
-      if (!warp_wait(dq_full, dqph, p.err)) return false;
-      dqph ^= 1u;
+    int dq_x = 0, dq_y = 0;
+    // Box of this warp inside a P^T buffer: the same 4 KB this warp writes
+    // its P^T rows into (rows 32 * quarter.., 16-byte chunks 8 * hf..).
+    const int box_off = hf * 16384 + quarter * 4096;
+    // Step gd's gradient MMAs complete -> dQ from TMEM -> registers -> this
+    // warp's 32 x 32 fp32 box (swizzled as the map expects) in P^T buffer
+    // gd & 1 -> TMA reduce-add issued by the warp's lane 0.
+    auto reduce_dq = [&](int64_t gd) -> bool {
+      const int u = (int)(gd & 1);
+      if (!warp_wait(&dq_full[u], (uint32_t)((gd >> 1) & 1), p.err)) return false;
       tc_fence_after();
-      return true;
-    };
-    // TMEM -> registers -> this warp's 32 x 32 fp32 box of the swizzled
-    // staging tile -> TMA reduce-add issued by the warp's lane 0.  Each warp
-    // owns its box, so no cross-warp barrier is needed: lane 0 waits until
-    // its own previous reduce has read the box.
-    uint8_t* const dq_box = sDQ + hf * 16384 + quarter * 4096;
-    auto reduce_dq = [&]() {
       uint32_t qv[32];
-      tmem_ld32(tbase + lane_off + 384u + (uint32_t)(64 * dq_buf + hf * 32), qv);
+      tmem_ld32(tbase + lane_off + 384u + (uint32_t)(64 * u + hf * 32), qv);
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&dq_free[dq_buf]);
-        bulk_wait_read0();
-      }
-      __syncwarp();
-      uint8_t* base = dq_box + lane * 128;
+      if (lane == 0) mbar_arrive(&dq_free[u]);
+      uint8_t* base = sPT + u * 2 * TILE + box_off + lane * 128;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         uint4 v = make_uint4(qv[c * 4], qv[c * 4 + 1], qv[c * 4 + 2], qv[c * 4 + 3]);
@@ -634,73 +632,70 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        tma_reduce_add_2d(&tm_dq, dq_box, dq_x + hf * 32, dq_y + quarter * 32);
+        tma_reduce_add_2d(&tm_dq, sPT + u * 2 * TILE + box_off, dq_x + hf * 32, dq_y + quarter * 32);
         bulk_commit();
       }
+      return true;
     };
-    // Each thread carries one lse (tid < 128) or delta (tid >= 128) value of
-    // the next query tile, loaded one iteration ahead.
-    auto fetch = [&](int item_, int i_) -> float {
-      if (item_ >= items) return 0.f;
-      const int bh_ = item_ / nt, h_ = bh_ % p.H, b_ = bh_ / p.H;
-      const int64_t base = ((int64_t)b_ * p.H + h_) * p.S + (int64_t)i_ * FT + (tid & 127);
-      return tid < 128 ? p.lse[base] : p.delta[base];
-    };
-    float cur = fetch(blockIdx.x, 0);
     for (int item = blockIdx.x; item < items && ok; item += gridDim.x, ++it) {
       const int kt = item % nt, bh = item / nt, h = bh % p.H, b = bh / p.H;
-      for (int i = 0; i < nt; ++i, ib ^= 1) {
-        const float nxt = (i + 1 < nt) ? fetch(item, i + 1) : fetch(item + gridDim.x, 0);
-        (tid < 128 ? sLse : sDel)[ib * 128 + (tid & 127)] = cur;
-        cur = nxt;
-        if (!group_sync(cw_bar, cwph, p.err)) { ok = false; break; }
+      for (int i = 0; i < nt; ++i, ++g) {
+        const int u = (int)(g & 1);
         if (!warp_wait(st_full, stph, p.err)) { ok = false; break; }
         stph ^= 1u;
+        // this step's lse / delta came with its Q / dO tiles (complete: the
+        // scores just computed read those tiles)
+        if (!warp_wait(&qd_full[u], (uint32_t)((g >> 1) & 1), p.err)) { ok = false; break; }
         tc_fence_after();
-        const float* L = sLse + ib * 128;
-        const float* Dl = sDel + ib * 128;
-        // sPT / sDS are free once the previous step's gradient MMAs are
-        // complete (its dQ commit); those ran while this CTA reduced the dQ
-        // of the step before.
-        if (dq_pending && !wait_dq()) { ok = false; break; }
-#pragma unroll 1
-        for (int cq = 0; cq < 2; ++cq) {  // 32 query columns at a time, this warp's half
-          const int col = hf * 64 + cq * 32;
-          uint32_t s[32], dp[32];
-          tmem_ld32(tbase + lane_off + (uint32_t)col, s);
-          tmem_ld32(tbase + lane_off + 128u + (uint32_t)col, dp);
-          tmem_ld_wait();
-          if (cq == 1) {  // scores read out: the next step's S^T / dP^T may overwrite them
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(st_free);
-          }
+        // All of this warp's scores at once (64 queries of S^T and dP^T), so
+        // the score buffer is released before any arithmetic.
+        uint32_t s[2][32], dp[2][32];
+        tmem_ld32(tbase + lane_off + (uint32_t)(hf * 64), s[0]);
+        tmem_ld32(tbase + lane_off + (uint32_t)(hf * 64 + 32), s[1]);
+        tmem_ld32(tbase + lane_off + 128u + (uint32_t)(hf * 64), dp[0]);
+        tmem_ld32(tbase + lane_off + 128u + (uint32_t)(hf * 64 + 32), dp[1]);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(st_free);  // the next step's S^T / dP^T may overwrite them
+        const float* L = sLD + u * 256 + hf * 64;
+        const float* Dl = L + 128;
+        // Buffer u was last read by step g-2's gradient MMAs (complete: its
+        // dQ was reduced during step g-1) and by the TMA reduce of step g-2's
+        // dQ box, which must have finished reading it.
+        uint8_t* const PT = sPT + u * 2 * TILE;
+        uint8_t* const DS = sDS + u * 2 * TILE;
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
 #pragma unroll
-          for (int c8 = 0; c8 < 4; ++c8) {  // 8 queries per 16-byte chunk
-            uint32_t pk[4], dk[4];
+        for (int c8 = 0; c8 < 8; ++c8) {  // 8 queries per 16-byte chunk
+          // per-query lse / delta: 16-byte broadcast loads
+          const float4 l0 = *reinterpret_cast<const float4*>(L + c8 * 8);
+          const float4 l1 = *reinterpret_cast<const float4*>(L + c8 * 8 + 4);
+          const float4 d0 = *reinterpret_cast<const float4*>(Dl + c8 * 8);
+          const float4 d1 = *reinterpret_cast<const float4*>(Dl + c8 * 8 + 4);
+          const float lv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+          const float dv[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+          uint32_t pk[4], dk[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int e = c8 * 8 + 2 * j;
-              // per-query lse / delta: 8-byte broadcast loads
-              const float2 lv = *reinterpret_cast<const float2*>(L + col + e);
-              const float2 dv = *reinterpret_cast<const float2*>(Dl + col + e);
-              const float p0 = hw_exp2(fmaf(__uint_as_float(s[e]), p.c, -lv.x));
-              const float p1 = hw_exp2(fmaf(__uint_as_float(s[e + 1]), p.c, -lv.y));
-              pk[j] = pack2(p0, p1);
-              dk[j] = pack2(p0 * (__uint_as_float(dp[e]) - dv.x), p1 * (__uint_as_float(dp[e + 1]) - dv.y));
-            }
-            const int ch = hf * 8 + cq * 4 + c8;
-            *reinterpret_cast<uint4*>(sPT + sw_off(row, ch)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            *reinterpret_cast<uint4*>(sDS + sw_off(row, ch)) = make_uint4(dk[0], dk[1], dk[2], dk[3]);
+          for (int j = 0; j < 4; ++j) {
+            const int e = c8 * 8 + 2 * j;
+            const float p0 = hw_exp2(fmaf(__uint_as_float(s[e >> 5][e & 31]), p.c, -lv[2 * j]));
+            const float p1 = hw_exp2(fmaf(__uint_as_float(s[e >> 5][(e + 1) & 31]), p.c, -lv[2 * j + 1]));
+            pk[j] = pack2(p0, p1);
+            dk[j] = pack2(p0 * (__uint_as_float(dp[e >> 5][e & 31]) - dv[2 * j]),
+                          p1 * (__uint_as_float(dp[e >> 5][(e + 1) & 31]) - dv[2 * j + 1]));
           }
+          const int ch = hf * 8 + c8;
+          *reinterpret_cast<uint4*>(PT + sw_off(row, ch)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          *reinterpret_cast<uint4*>(DS + sw_off(row, ch)) = make_uint4(dk[0], dk[1], dk[2], dk[3]);
         }
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(ds_full);
-        if (dq_pending) reduce_dq();
+        if (lane == 0) mbar_arrive(&ds_full[u]);
+        if (dq_pending && !reduce_dq(g - 1)) { ok = false; break; }
         dq_pending = true;
-        dq_buf ^= 1;
         dq_x = h * FD;
         dq_y = b * p.S + i * FT;
       }
@@ -731,7 +726,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
       __syncwarp();
       if (lane == 0) mbar_arrive(kv_read);
     }
-    if (ok && dq_pending && wait_dq()) reduce_dq();
+    if (ok && dq_pending) reduce_dq(g - 1);
     if (lane == 0) bulk_wait0();
   }
   tc_fence_before();
@@ -835,6 +830,9 @@ void flash_attention_bwd(const __nv_bfloat16* qkv, const __nv_bfloat16* out, con
                          const float* lse, float* delta, float* dq_acc, __nv_bfloat16* dqkv, int B, int S, int H,
                          float scale, cudaStream_t s, uint32_t* err, int max_ctas) {
   DLVK_CHECK(flash_attention_supported(B, S, H, FD, qkv), "flash_attention_bwd: unsupported shape");
+  // lse and delta rows are bulk-copied into shared memory (16-byte aligned)
+  DLVK_CHECK((reinterpret_cast<uintptr_t>(lse) & 15u) == 0 && (reinterpret_cast<uintptr_t>(delta) & 15u) == 0,
+             "flash_attention_bwd: lse and delta must be 16-byte aligned");
   tmap::bind_context();
   const int E = H * FD;
   const int64_t rows = (int64_t)B * S;
