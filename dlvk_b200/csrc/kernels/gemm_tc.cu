@@ -468,7 +468,11 @@ __device__ __forceinline__ void epi_store(const TcParams& p, const float* stg, i
   }
 }
 
-template <int BN, bool PAIR = false>
+// EPI = 1 compiles only the TMA-store epilogue (plain, bias, activation,
+// bf16 residual or mask, bitmask, column sums, reduce-add): a kernel with a
+// smaller instruction footprint for the common launches, whose epilogue
+// otherwise misses in the instruction cache.  EPI = 0 has every path.
+template <int BN, bool PAIR = false, int EPI = 0>
 __global__ void __launch_bounds__(320, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, TcParams p) {
@@ -798,7 +802,7 @@ __global__ void __launch_bounds__(320, 1)
         if (i == 1) GEMM_STAMP(threadIdx.x == 64 && last_tile, 15);
         if (i + 1 < NCH) tmem_ld32(tbase + (uint32_t)((i + 1) * 32), r[(i + 1) & 1]);
         const int n0 = tn * BN + (half * NCH + i) * 32;
-        if (staged) {
+        if (EPI == 0 && staged) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) stg[lane * 33 + j] = __uint_as_float(r[i & 1][j]) * p.alpha;
           __syncwarp();
@@ -807,7 +811,7 @@ __global__ void __launch_bounds__(320, 1)
             else epi_store<__nv_bfloat16, 8>(p, stg, row0, n0, lane, cb, rb, mb);
           }
           __syncwarp();
-        } else if (p.tma_c) {
+        } else if (EPI == 1 || p.tma_c) {
           // Row `lane` of this warp's box goes to smem and one lane stores the
           // box with TMA (rows >= M / columns >= N are clipped).  fp32: one
           // 32 x 32 box (128-byte rows) per chunk.  bf16: chunks i, i+1 fill
@@ -1025,28 +1029,42 @@ int sm_count() {
   return n[dev];
 }
 
-template <int BN>
-void launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const TcParams& p, int max_ctas,
-               cudaStream_t s) {
+// The epilogue paths a launch needs: 1 = TMA-store path only (its C map was
+// made and no input is staged through shared memory), 0 = all paths.
+int epi_kind(const TcParams& p) {
+  const bool staged = (p.beta != 0.f) || (p.out_f32 && (p.R != nullptr || p.Mk != nullptr));
+  return (p.tma_c != 0 && !staged) ? 1 : 0;
+}
+
+template <int BN, int EPI>
+void launch_tc_k(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const TcParams& p, int max_ctas,
+                 cudaStream_t s) {
   using C = Cfg<BN>;
   static bool attr_set[kMaxDevices] = {false};
   const int dev = current_device_slot();
   if (!attr_set[dev]) {
-    DLVK_CUDA_CHECK(cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    DLVK_CUDA_CHECK(
+        cudaFuncSetAttribute(gemm_tc_kernel<BN, false, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_set[dev] = true;
   }
   const int tiles = p.tiles_m * p.tiles_n * p.batch * p.splits;
   const int slots = max_ctas > 0 ? max_ctas : sm_count();
   int grid = p.sk ? slots : std::min(tiles, slots);  // stream-K: every CTA takes a share
-  launch_pdl(gemm_tc_kernel<BN, false>, dim3(grid), dim3(320), C::SMEM, s, ta, tb, tc, p);
+  launch_pdl(gemm_tc_kernel<BN, false, EPI>, dim3(grid), dim3(320), C::SMEM, s, ta, tb, tc, p);
   DLVK_POST_LAUNCH();
+}
+template <int BN>
+void launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const TcParams& p, int max_ctas,
+               cudaStream_t s) {
+  if (epi_kind(p) == 1) launch_tc_k<BN, 1>(ta, tb, tc, p, max_ctas, s);
+  else launch_tc_k<BN, 0>(ta, tb, tc, p, max_ctas, s);
 }
 
 // 2-CTA clusters sharing 256 x BN tiles (cta_group::2).  The persistent
 // grid is as many pairs as can be resident at once.
-template <int BN>
-void launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const TcParams& p,
-                    int max_ctas, cudaStream_t s) {
+template <int BN, int EPI>
+void launch_tc_pair_k(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const TcParams& p,
+                      int max_ctas, cudaStream_t s) {
   using C = Cfg<BN, true>;
   static int max_pairs[kMaxDevices] = {0};
   const int dev = current_device_slot();
@@ -1065,10 +1083,10 @@ void launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensor
   cfg.numAttrs = 1;  // occupancy query: cluster shape only
   if (max_pairs[dev] == 0) {
     DLVK_CUDA_CHECK(
-        cudaFuncSetAttribute(gemm_tc_kernel<BN, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        cudaFuncSetAttribute(gemm_tc_kernel<BN, true, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     cfg.gridDim = dim3(2 * 74, 1, 1);
     int n = 0;
-    DLVK_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<BN, true>, &cfg));
+    DLVK_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<BN, true, EPI>, &cfg));
     max_pairs[dev] = std::max(1, n);
   }
   const int tiles = p.tiles_m * p.tiles_n * p.batch * p.splits;
@@ -1076,8 +1094,14 @@ void launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensor
   if (max_ctas > 0) pairs = std::max(1, std::min(pairs, max_ctas / 2));
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.numAttrs = 2;
-  DLVK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, true>, ta, tb, tc, p));
+  DLVK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, true, EPI>, ta, tb, tc, p));
   DLVK_POST_LAUNCH();
+}
+template <int BN>
+void launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const TcParams& p,
+                    int max_ctas, cudaStream_t s) {
+  if (epi_kind(p) == 1) launch_tc_pair_k<BN, 1>(ta, tb, tc, p, max_ctas, s);
+  else launch_tc_pair_k<BN, 0>(ta, tb, tc, p, max_ctas, s);
 }
 
 inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
