@@ -471,7 +471,8 @@ __device__ __forceinline__ void epi_store(const TcParams& p, const float* stg, i
 // EPI = 1 compiles only the TMA-store epilogue (plain, bias, activation,
 // bf16 residual or mask, bitmask, column sums, reduce-add): a kernel with a
 // smaller instruction footprint for the common launches, whose epilogue
-// otherwise misses in the instruction cache.  EPI = 0 has every path.
+// otherwise misses in the instruction cache.  EPI = 2 is that path with
+// alpha, bias and activation only.  EPI = 0 has every path.
 template <int BN, bool PAIR = false, int EPI = 0>
 __global__ void __launch_bounds__(320, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -824,15 +825,15 @@ __global__ void __launch_bounds__(320, 1)
           if (nbox < p.N) {
             float v[32];
 #pragma unroll
-            const float rbv = (p.row_bias && row0 + lane < p.M) ? p.row_bias[row0 + lane] : 0.f;
+            const float rbv = (EPI != 2 && p.row_bias && row0 + lane < p.M) ? p.row_bias[row0 + lane] : 0.f;
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = fmaf(__uint_as_float(r[i & 1][j]), p.alpha, rbv);
             if (p.bias && n0 < p.N) add_bias<32>(p.bias, p.bias_f32, n0, min(32, p.N - n0), v);
-            if (p.R) add_row_residual(p, rb, row0 + lane, n0, v);
+            if (EPI != 2 && p.R) add_row_residual(p, rb, row0 + lane, n0, v);
             apply_act<32>(p.act, v);
-            if (p.Mk) mask_row_bf16(p, mb, row0 + lane, n0, v);
-            if (p.bits_in) mask_row_bits(p, row0 + lane, n0, v);
-            if (p.bits_out && n0 < p.N && row0 + lane < p.M) store_bits(p, row0 + lane, n0, v);
+            if (EPI != 2 && p.Mk) mask_row_bf16(p, mb, row0 + lane, n0, v);
+            if (EPI != 2 && p.bits_in) mask_row_bits(p, row0 + lane, n0, v);
+            if (EPI != 2 && p.bits_out && n0 < p.N && row0 + lane < p.M) store_bits(p, row0 + lane, n0, v);
             // Boxes start on 1024-byte boundaries (the swizzled box layout is
             // defined on aligned addresses).
             if (opens) {
@@ -871,7 +872,7 @@ __global__ void __launch_bounds__(320, 1)
                 st_shared_v4(a ^ (((a >> 7) & 7u) << 4), w[0], w[1], w[2], w[3]);
               }
             }
-            if (BN != 512 && p.colsum) {  // after the box write: consumes v (512-wide tiles: never, see host)
+            if (BN != 512 && EPI != 2 && p.colsum) {  // after the box write: consumes v (512-wide tiles: never, see host)
               if (row0 + lane >= p.M) {
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = 0.f;
@@ -1033,7 +1034,10 @@ int sm_count() {
 // made and no input is staged through shared memory), 0 = all paths.
 int epi_kind(const TcParams& p) {
   const bool staged = (p.beta != 0.f) || (p.out_f32 && (p.R != nullptr || p.Mk != nullptr));
-  return (p.tma_c != 0 && !staged) ? 1 : 0;
+  if (p.tma_c == 0 || staged) return 0;
+  const bool extras = p.R || p.Mk || p.bits_in || p.bits_out || p.colsum || p.row_bias;
+  static const bool plain_on = [] { const char* e = std::getenv("DLVK_GEMM_EPI2"); return !(e && e[0] == '0'); }();
+  return (extras || !plain_on) ? 1 : 2;
 }
 
 template <int BN, int EPI>
@@ -1056,7 +1060,9 @@ void launch_tc_k(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap
 template <int BN>
 void launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const TcParams& p, int max_ctas,
                cudaStream_t s) {
-  if (epi_kind(p) == 1) launch_tc_k<BN, 1>(ta, tb, tc, p, max_ctas, s);
+  const int k = epi_kind(p);
+  if (k == 2) launch_tc_k<BN, 2>(ta, tb, tc, p, max_ctas, s);
+  else if (k == 1) launch_tc_k<BN, 1>(ta, tb, tc, p, max_ctas, s);
   else launch_tc_k<BN, 0>(ta, tb, tc, p, max_ctas, s);
 }
 
@@ -1100,7 +1106,9 @@ void launch_tc_pair_k(const CUtensorMap& ta, const CUtensorMap& tb, const CUtens
 template <int BN>
 void launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const TcParams& p,
                     int max_ctas, cudaStream_t s) {
-  if (epi_kind(p) == 1) launch_tc_pair_k<BN, 1>(ta, tb, tc, p, max_ctas, s);
+  const int k = epi_kind(p);
+  if (k == 2) launch_tc_pair_k<BN, 2>(ta, tb, tc, p, max_ctas, s);
+  else if (k == 1) launch_tc_pair_k<BN, 1>(ta, tb, tc, p, max_ctas, s);
   else launch_tc_pair_k<BN, 0>(ta, tb, tc, p, max_ctas, s);
 }
 
