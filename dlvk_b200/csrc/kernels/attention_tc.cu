@@ -71,6 +71,14 @@ __device__ __forceinline__ float hw_exp2(float x) {
   return y;
 }
 
+// 2^(-x): the negation folds into the exponential's operand.
+__device__ __forceinline__ float hw_exp2_neg(float x) {
+  float y;
+  asm("{\n\t.reg .f32 t;\n\tneg.f32 t, %1;\n\tex2.approx.ftz.f32 %0, t;\n\t}" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float2 f2(uint32_t a, uint32_t b) { return make_float2(__uint_as_float(a), __uint_as_float(b)); }
+
 // Bounded wait whose outcome is the same in every lane of the warp (the
 // warp-collective tcgen05.ld / st that follow need all 32 lanes).
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
@@ -309,7 +317,8 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) flash_fwd_kernel(const __grid_
           tc_fence_after();
         }
         // Exponentials straight to P (bf16 pairs in TMEM); the row sum uses
-        // the fp32 values.
+        // the fp32 values.  (Packed fp32 pairs measured the same here and
+        // spill under the 168-register cap.)
         float sp8[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) sp8[k] = 0.f;
@@ -389,7 +398,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) flash_fwd_kernel(const __grid_
 // ---------------------------------------------------------------- backward
 struct BwdP {
   const float* lse;    // [B, H, S] log2 units
-  const float* delta;  // [B, H, S] rowsum(dO * O)
+  const float* delta;  // [B, H, S] -rowsum(dO * O)
   __nv_bfloat16* dqkv; // [B, S, 3E]
   int B, S, H, E;
   float c;             // scale * log2(e)
@@ -659,7 +668,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
         __syncwarp();
         if (lane == 0) mbar_arrive(st_free);  // the next step's S^T / dP^T may overwrite them
         const float* L = sLD + u * 256 + hf * 64;
-        const float* Dl = L + 128;
+        const float* Dl = L + 128;  // -delta
+        const float2 nc2 = make_float2(-p.c, -p.c);
         // Buffer u was last read by step g-2's gradient MMAs (complete: its
         // dQ was reduced during step g-1) and by the TMA reduce of step g-2's
         // dQ box, which must have finished reading it.
@@ -669,22 +679,25 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
         __syncwarp();
 #pragma unroll
         for (int c8 = 0; c8 < 8; ++c8) {  // 8 queries per 16-byte chunk
-          // per-query lse / delta: 16-byte broadcast loads
+          // per-query lse / -delta: 16-byte broadcast loads
           const float4 l0 = *reinterpret_cast<const float4*>(L + c8 * 8);
           const float4 l1 = *reinterpret_cast<const float4*>(L + c8 * 8 + 4);
           const float4 d0 = *reinterpret_cast<const float4*>(Dl + c8 * 8);
           const float4 d1 = *reinterpret_cast<const float4*>(Dl + c8 * 8 + 4);
-          const float lv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
-          const float dv[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+          const float2 lv[4] = {make_float2(l0.x, l0.y), make_float2(l0.z, l0.w), make_float2(l1.x, l1.y),
+                                make_float2(l1.z, l1.w)};
+          const float2 nd[4] = {make_float2(d0.x, d0.y), make_float2(d0.z, d0.w), make_float2(d1.x, d1.y),
+                                make_float2(d1.z, d1.w)};
           uint32_t pk[4], dk[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int e = c8 * 8 + 2 * j;
-            const float p0 = hw_exp2(fmaf(__uint_as_float(s[e >> 5][e & 31]), p.c, -lv[2 * j]));
-            const float p1 = hw_exp2(fmaf(__uint_as_float(s[e >> 5][(e + 1) & 31]), p.c, -lv[2 * j + 1]));
-            pk[j] = pack2(p0, p1);
-            dk[j] = pack2(p0 * (__uint_as_float(dp[e >> 5][e & 31]) - dv[2 * j]),
-                          p1 * (__uint_as_float(dp[e >> 5][(e + 1) & 31]) - dv[2 * j + 1]));
+            // p = 2^(S c - lse), dS = p (dP - delta), in packed fp32 pairs
+            const float2 x = __ffma2_rn(f2(s[e >> 5][e & 31], s[e >> 5][(e + 1) & 31]), nc2, lv[j]);
+            const float2 pp = make_float2(hw_exp2_neg(x.x), hw_exp2_neg(x.y));
+            const float2 ds = __fmul2_rn(pp, __fadd2_rn(f2(dp[e >> 5][e & 31], dp[e >> 5][(e + 1) & 31]), nd[j]));
+            pk[j] = pack2(pp.x, pp.y);
+            dk[j] = pack2(ds.x, ds.y);
           }
           const int ch = hf * 8 + c8;
           *reinterpret_cast<uint4*>(PT + sw_off(row, ch)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
@@ -738,7 +751,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) flash_bwd_kernel(const __grid_
   }
 }
 
-// delta[b, h, q] = sum_d dO[b, q, h, d] * O[b, q, h, d], and the row's 64
+// delta[b, h, q] = -sum_d dO[b, q, h, d] * O[b, q, h, d] (stored negated:
+// the backward kernel adds it to dP), and the row's 64
 // entries of the fp32 dQ accumulator cleared (no separate memset): eight lanes per
 // (b, q, h) row of 64, one 16-byte vector of each operand per lane, reduced
 // with three shuffles.  A warp reads four consecutive rows (512 contiguous
@@ -778,7 +792,7 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __n
       const int h = (int)(w % H);
       const int64_t bq = w / H;
       const int q = (int)(bq % S), b = (int)(bq / S);
-      delta[((int64_t)b * H + h) * S + q] = acc;
+      delta[((int64_t)b * H + h) * S + q] = -acc;
     }
   }
 }
