@@ -395,12 +395,13 @@ def run_torch(args, rank, local, world):
         opt.step()
         return loss
 
-    # The whole step (forward, backward, NCCL all-reduce through DDP for
-    # N > 1, optimizer) captured into one CUDA graph, so the comparison arm
-    # pays no eager launch overhead.  Falls back to eager if capture fails.
+    # One GPU: the whole step (forward, backward, optimizer) captured into
+    # one CUDA graph, so the comparison arm pays no eager launch overhead.
+    # N > 1 runs eager DDP: its NCCL reduction hooks do not capture, and a
+    # failed capture leaves the CUDA generator unusable for dropout.
     run = step
     graphed = False
-    if not args.no_graph:
+    if not args.no_graph and world == 1:
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):

@@ -14,6 +14,8 @@
 // keep iff u >= p.  The backward pass regenerates the same mask.  The step
 // comes from device memory (`step_ptr`) so a captured CUDA graph draws fresh
 // masks on every replay.
+#include <cstdlib>
+
 #include "dlvk/common.h"
 #include "dlvk/kernels.h"
 #include "dlvk/sm100.h"
@@ -899,6 +901,153 @@ __global__ void __launch_bounds__(256, 1) ln_bwd_ring_kernel(const __nv_bfloat16
   }
 }
 
+// Two warps per row for bf16 rows of 512 x NVH elements (D = 512 or 1024;
+// NVH = 1 or 2): warp 2p + h of a block owns columns [h D/2, (h+1) D/2) of the
+// rows of pair p, so a lane holds 16 dgamma / dbeta (/ dres column-sum)
+// accumulators instead of 32 and a block runs 16 warps.  Each warp streams
+// its half rows (x, dy and the residual gradient, with the row's mean and
+// rstd) through a 3-slot cp.async ring; the two halves of a row exchange
+// their partial sums through shared memory under a named barrier of the
+// pair's 64 threads (slot by row parity, so a write never races the
+// partner's read of the previous row).  Partials per block as in
+// ln_bwd_ring_kernel, so ln_bwd_final_kernel finishes both.
+__device__ __forceinline__ void named_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+template <int NVH, bool RES>
+__global__ void __launch_bounds__(512, 1) ln_bwd_pair_kernel(const __nv_bfloat16* __restrict__ x,
+                                                             const float* __restrict__ gamma,
+                                                             const float* __restrict__ mean,
+                                                             const float* __restrict__ rstd,
+                                                             const __nv_bfloat16* __restrict__ dy,
+                                                             __nv_bfloat16* __restrict__ dx, float* __restrict__ part,
+                                                             int64_t rows, int D,
+                                                             const __nv_bfloat16* __restrict__ dres) {
+  constexpr int EPV = 8, RING = 3, NT = RES ? 3 : 2, RV = NVH * 32;  // 16-byte vectors per tensor half row
+  constexpr int NP = RES ? 3 : 2;
+  constexpr int HALF = RV * EPV;  // columns per half row
+  pdl_wait();
+  extern __shared__ uint4 sring[];                                   // [16][RING][NT][RV]
+  float* sgam = reinterpret_cast<float*>(sring + 16 * RING * NT * RV);
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pr = w >> 1, hh = w & 1;
+  float* mystat = sgam + D + w * RING * 2;                            // [RING][mean, rstd]
+  float2* xch = reinterpret_cast<float2*>(sgam + D + 16 * RING * 2);  // [8 pairs][2 parities][2 halves]
+  for (int d = threadIdx.x; d < D; d += blockDim.x) sgam[d] = gamma ? gamma[d] : 1.f;
+  __syncthreads();
+  uint4* ring = sring + (size_t)w * RING * NT * RV;
+  const int64_t step = (int64_t)gridDim.x * 8;
+  const int64_t r0 = (int64_t)blockIdx.x * 8 + pr;
+  const int col0 = hh * HALF;
+  auto issue = [&](int64_t row, int slot) {
+    if (row < rows) {
+      uint4* b = ring + slot * NT * RV;
+      const int64_t base = row * D + col0;
+#pragma unroll
+      for (int i = 0; i < NVH; ++i) {
+        const int v = lane + 32 * i;
+        sm100::cp_async_16(sm100::smem_u32(b + v), reinterpret_cast<const uint4*>(x + base) + v, 16);
+        sm100::cp_async_16(sm100::smem_u32(b + RV + v), reinterpret_cast<const uint4*>(dy + base) + v, 16);
+        if (RES)
+          sm100::cp_async_16(sm100::smem_u32(b + 2 * RV + v), reinterpret_cast<const uint4*>(dres + base) + v, 16);
+      }
+      if (lane < 2)
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(sm100::smem_u32(mystat + slot * 2 + lane)),
+                     "l"((lane ? rstd : mean) + row)
+                     : "memory");
+    }
+    sm100::cp_async_commit();  // empty groups keep the count aligned
+  };
+#pragma unroll
+  for (int k = 0; k < RING; ++k) issue(r0 + k * step, k);
+  float adg[NVH][EPV], adb[NVH][EPV], adr[NVH][EPV], gr[NVH][EPV];
+#pragma unroll
+  for (int i = 0; i < NVH; ++i)
+#pragma unroll
+    for (int k = 0; k < EPV; ++k) {
+      adg[i][k] = adb[i][k] = adr[i][k] = 0.f;
+      gr[i][k] = sgam[col0 + (lane + 32 * i) * EPV + k];
+    }
+  const float invD = 1.f / D;
+  int slot = 0, par = 0;
+  for (int64_t r = r0; r < rows; r += step, par ^= 1) {
+    sm100::cp_async_wait<RING - 1>();
+    __syncwarp();  // lanes 0 and 1 copied the row's mean and rstd
+    const uint4* b = ring + slot * NT * RV;
+    const float mu = mystat[slot * 2], rs = mystat[slot * 2 + 1];
+    float a = 0.f, bb = 0.f;
+#pragma unroll
+    for (int i = 0; i < NVH; ++i) {
+      const uint4 ux = b[lane + 32 * i], ug = b[RV + lane + 32 * i];
+      const __nv_bfloat16* ex = reinterpret_cast<const __nv_bfloat16*>(&ux);
+      const __nv_bfloat16* eg = reinterpret_cast<const __nv_bfloat16*>(&ug);
+#pragma unroll
+      for (int k = 0; k < EPV; ++k) {
+        const float xh = (__bfloat162float(ex[k]) - mu) * rs;
+        const float g = __bfloat162float(eg[k]);
+        const float gg = g * gr[i][k];
+        a += gg;
+        bb += gg * xh;
+        adg[i][k] += g * xh;
+        adb[i][k] += g;
+      }
+    }
+    a = warp_sum(a);
+    bb = warp_sum(bb);
+    if (lane == 0) xch[(pr * 2 + par) * 2 + hh] = make_float2(a, bb);
+    named_sync(1 + pr, 64);
+    const float2 o = xch[(pr * 2 + par) * 2 + (hh ^ 1)];
+    a = (a + o.x) * invD;
+    bb = (bb + o.y) * invD;
+#pragma unroll
+    for (int i = 0; i < NVH; ++i) {
+      const uint4 ux = b[lane + 32 * i], ug = b[RV + lane + 32 * i];
+      uint4 ur = make_uint4(0, 0, 0, 0);
+      if (RES) ur = b[2 * RV + lane + 32 * i];
+      const __nv_bfloat16* ex = reinterpret_cast<const __nv_bfloat16*>(&ux);
+      const __nv_bfloat16* eg = reinterpret_cast<const __nv_bfloat16*>(&ug);
+      const __nv_bfloat16* er = reinterpret_cast<const __nv_bfloat16*>(&ur);
+      uint4 ov;
+      __nv_bfloat16* eo = reinterpret_cast<__nv_bfloat16*>(&ov);
+#pragma unroll
+      for (int k = 0; k < EPV; ++k) {
+        const float xh = (__bfloat162float(ex[k]) - mu) * rs;
+        float v = rs * (__bfloat162float(eg[k]) * gr[i][k] - a - xh * bb);
+        if (RES) {
+          const float rv = __bfloat162float(er[k]);
+          v += rv;
+          adr[i][k] += rv;
+        }
+        eo[k] = __float2bfloat16_rn(v);
+      }
+      reinterpret_cast<uint4*>(dx + r * D + col0)[lane + 32 * i] = ov;
+    }
+    issue(r + RING * step, slot);  // this lane has read its vectors of the slot
+    slot = slot + 1 == RING ? 0 : slot + 1;
+  }
+  sm100::cp_async_wait<0>();
+  __syncthreads();
+  float* sp = reinterpret_cast<float*>(sring);  // the ring is free: [16 warps][NP][HALF] partials
+  float* mine = sp + (int64_t)w * NP * HALF;
+#pragma unroll
+  for (int i = 0; i < NVH; ++i)
+#pragma unroll
+    for (int k = 0; k < EPV; ++k) {
+      const int col = (lane + 32 * i) * EPV + k;
+      mine[col] = adg[i][k];
+      mine[HALF + col] = adb[i][k];
+      if (RES) mine[2 * HALF + col] = adr[i][k];
+    }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < NP * D; idx += blockDim.x) {
+    const int np = idx / D, d = idx - np * D, h = d / HALF, dd = d - h * HALF;
+    float acc = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc += sp[((int64_t)(q * 2 + h) * NP + np) * HALF + dd];
+    part[(int64_t)blockIdx.x * NP * D + idx] = acc;
+  }
+}
+
 // Sums the per-block partials: block = 32 columns x 16 row groups, each
 // thread with four independent accumulators, combined in a fixed order
 // through shared memory.
@@ -1143,6 +1292,39 @@ void layernorm_bwd(DType dt, const void* x, const float* gamma, const float* mea
     colsum(dt, DType::F32, dres, rows, D, 1.f, dres_colsum, dres_colsum_accumulate,
            colsum_scratch_floats(rows, D) > 0 ? cs : nullptr, s);
   };
+  // Two warps per row (DLVK_LN_BWD_PAIR=0: one warp per row, the ring kernel below).
+  static const bool pair_on = [] {
+    const char* e = std::getenv("DLVK_LN_BWD_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  if (pair_on && dt == DType::BF16 && D % 512 == 0 && (D / 512 == 2 || D / 512 == 1)) {
+    const bool al = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dy) |
+                      reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(dres)) & 15) == 0;
+    const int nvh = D / 512;
+    const int nt = dres ? 3 : 2;
+    const size_t ring = (size_t)16 * 3 * nt * nvh * 32 * 16;  // reused for the [16][NP][D/2] fp32 partials
+    const size_t smem = ring + (size_t)D * 4 + 16 * 3 * 2 * 4 + 8 * 2 * 2 * 8;  // ring | gamma | row stats | exchange
+    if (al && ring >= (size_t)16 * (dres ? 3 : 2) * (D / 2) * 4 && smem <= 200 * 1024) {
+      auto launch = [&](auto kern) {
+        DLVK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        launch_pdl(kern, dim3(blocks), dim3(512), smem, s, (const __nv_bfloat16*)x, gamma, mean, rstd,
+                   (const __nv_bfloat16*)dy, (__nv_bfloat16*)dx, scratch, rows, D, (const __nv_bfloat16*)dres);
+      };
+      if (dres) {
+        if (nvh == 2) launch(ln_bwd_pair_kernel<2, true>);
+        else launch(ln_bwd_pair_kernel<1, true>);
+      } else {
+        if (nvh == 2) launch(ln_bwd_pair_kernel<2, false>);
+        else launch(ln_bwd_pair_kernel<1, false>);
+      }
+      DLVK_POST_LAUNCH();
+      const int np = dres ? 3 : 2;
+      launch_pdl(ln_bwd_final_kernel, dim3((np * D + 31) / 32), dim3(32, 16), 0, s, (const float*)scratch, blocks, D,
+                 dgamma, dbeta, accumulate ? 1 : 0, np, dres_colsum, dres_colsum_accumulate ? 1 : 0);
+      DLVK_POST_LAUNCH();
+      return;
+    }
+  }
   if (dt == DType::BF16 && D % 256 == 0 && (D / 256 == 4 || D / 256 == 2 || D / 256 == 1)) {
     const bool al = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dy) |
                       reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(dres)) & 15) == 0;

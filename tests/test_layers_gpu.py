@@ -108,27 +108,28 @@ def test_batchnorm_relu_dropout(dtype, shape, p):
 
 @pytest.mark.parametrize("rows", [333, 5003])  # 5003: more rows than one pass of the grid's warps covers
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_layernorm(dtype, rows):
+@pytest.mark.parametrize("D", [256, 512, 1024])  # bf16: one warp per row at 256, two warps per row at 512 / 1024
+def test_layernorm(dtype, rows, D):
     C = _C()
-    x = torch.randn(rows, 1024, device="cuda").to(dtype)
-    gamma = torch.rand(1024, device="cuda") + 0.5
-    beta = torch.randn(1024, device="cuda")
+    x = torch.randn(rows, D, device="cuda").to(dtype)
+    gamma = torch.rand(D, device="cuda") + 0.5
+    beta = torch.randn(D, device="cuda")
     y, mean, rstd = C.layernorm_fwd(x, gamma, beta, 1e-5)
     xr = x.float().clone().requires_grad_(True)
     gr = gamma.clone().requires_grad_(True)
     br = beta.clone().requires_grad_(True)
-    yr = F.layer_norm(xr, (1024,), gr, br, 1e-5)
+    yr = F.layer_norm(xr, (D,), gr, br, 1e-5)
     tol = 1e-4 if dtype == torch.float32 else 3e-2
     close(y, yr, tol)
     g = torch.randn_like(yr).to(dtype)
     yr.backward(g.float())
-    dgam, dbet = torch.zeros(1024, device="cuda"), torch.zeros(1024, device="cuda")
+    dgam, dbet = torch.zeros(D, device="cuda"), torch.zeros(D, device="cuda")
     dx = C.layernorm_bwd(x, gamma, mean, rstd, g, dgam, dbet, False)
     close(dx, xr.grad, tol * 2)
     close(dgam, gr.grad, tol * 2)
     close(dbet, br.grad, tol * 2)
     dres = torch.randn_like(yr).to(dtype)
-    cs = torch.full((1024,), 2.0, device="cuda")
+    cs = torch.full((D,), 2.0, device="cuda")
     dx2 = C.layernorm_bwd(x, gamma, mean, rstd, g, dgam, dbet, True, dres, dres_colsum=cs, dres_colsum_accumulate=True)
     close(dx2, xr.grad + dres.float(), tol * 2)
     close(dgam, 2 * gr.grad, tol * 2)
