@@ -1198,9 +1198,11 @@ void choose_tiling(const GemmArgs& a, int sms, int& BN, int& splits, bool& pair,
   // The 256 x 512 pair tile moves 25% fewer L2 bytes per FLOP than 256 x 256
   // (the mainloop of the latter waits on L2 ~25% of the time), but its single
   // TMEM buffer leaves every tile's epilogue exposed.
-  // Measured per-SM rates relative to the single-CTA tile: the wide tile
-  // gains with K (1.3 below K = 4096, 1.4 at 4096, 1.55 from 8192 on).
-  const double wide_eff = kbs >= 128 ? 1.55 : (kbs >= 64 ? 1.4 : 1.3);
+  // Measured per-SM rates relative to the single-CTA tile: the wide tile's
+  // mainloop runs ~1 090 cycles per 64-deep k-block (1.75x) below K = 8192
+  // (back-to-back timings of 8192 x 1024 x {1024, 3072, 4096} against the
+  // 256-wide pair tile), and 1.55x is kept from K = 8192 on.
+  const double wide_eff = kbs >= 128 ? 1.55 : 1.75;
   const Cand cands[] = {{true, 512, wide_eff}, {true, 256, 1.2}, {false, 256, 1.0}, {false, 128, 0.85}};
   for (const Cand& c : cands) {
     if (c.pair && !pair_ok) continue;
@@ -1217,9 +1219,9 @@ void choose_tiling(const GemmArgs& a, int sms, int& BN, int& splits, bool& pair,
       const double unit_s = (double)tile_m * c.bn * BK * 2.0 * ((kbs + sp - 1) / sp) /
                             (sm_flops * (c.pair ? 2 : 1) * c.eff);
       // Epilogue of one CTA's 128 x BN block (measured: ~17 GB/s per CTA for
-      // 128 x 256, ~13.5 GB/s for 128 x 512), exposed once at the end, or
+      // 128 x 256, ~18 GB/s for 128 x 512), exposed once at the end, or
       // after every wave without a second accumulator buffer.
-      const double epi_s = 128.0 * c.bn * ((out_f32 || sp > 1) ? 4.0 : 2.0) / (c.bn == 512 ? 13.5e9 : 17e9);
+      const double epi_s = 128.0 * c.bn * ((out_f32 || sp > 1) ? 4.0 : 2.0) / (c.bn == 512 ? 18e9 : 17e9);
       double t = waves * unit_s + (c.bn == 512 ? waves : 1) * epi_s;
       if (sp > 1) {
         const double mn = (double)a.M * a.N * a.batch * a.batch2;
