@@ -194,6 +194,93 @@ __global__ void __launch_bounds__(256) conv_wgrad_partial_kernel(const T* __rest
 }
 
 // Sum the chunk partials: dw[co, wi] (+)= sum_chunk partial[chunk][co][wi].
+// Weight gradient of a 3 x 3 convolution with few channels, one block per
+// chunk of images: each image's input planes and output gradient are staged
+// in shared memory (fp32), and thread t owns the (co, ci) channel pair
+// t % (Cout * Cin) over pixel group t / (Cout * Cin): it reads the gradient
+// once per pixel and accumulates all nine taps of that pair (and, for ci = 0,
+// the bias sum).  Groups are combined in shared memory in a fixed order; the
+// block writes its partial in conv_wgrad_partial_kernel's layout
+// [chunk][Cout][Cin * 9 + 1], so conv_wgrad_final_kernel finishes both.
+template <typename T>
+__global__ void __launch_bounds__(256) conv_wgrad_image_kernel(const T* __restrict__ x, const T* __restrict__ g,
+                                                               float* __restrict__ partial, ConvDesc d, int ipb) {
+  extern __shared__ float wsm[];
+  const int HW = d.H * d.W, HWo = d.Ho * d.Wo;
+  const int pairs = d.Cout * d.Cin;
+  const int G = max(1, (int)blockDim.x / pairs);  // pixel groups
+  const int Kel = d.Cin * 9;
+  float* sx = wsm;                       // [Cin][H][W]
+  float* sg = sx + d.Cin * HW;           // [Cout][Ho][Wo]
+  float* sred = sg + d.Cout * HWo;       // [G][pairs][10] group partials
+  const int n0 = blockIdx.x * ipb, n1 = min(d.N, n0 + ipb);
+  const int grp = threadIdx.x / pairs;
+  const int pr = threadIdx.x - grp * pairs;
+  const bool active = grp < G && pr < pairs;
+  const int co = active ? pr / d.Cin : 0, ci = active ? pr - co * d.Cin : 0;
+  float acc[10];
+#pragma unroll
+  for (int k = 0; k < 10; ++k) acc[k] = 0.f;
+  for (int n = n0; n < n1; ++n) {
+    __syncthreads();  // the previous image's planes are no longer read
+    const T* xn = x + (int64_t)n * d.Cin * HW;
+    const T* gn = g + (int64_t)n * d.Cout * HWo;
+    for (int i = threadIdx.x; i < d.Cin * HW; i += blockDim.x) sx[i] = to_f32(xn[i]);
+    for (int i = threadIdx.x; i < d.Cout * HWo; i += blockDim.x) sg[i] = to_f32(gn[i]);
+    __syncthreads();
+    if (!active) continue;
+    const float* gp = sg + co * HWo;
+    const float* xp = sx + ci * HW;
+    int oh = grp / d.Wo, ow = grp - oh * d.Wo;
+    for (int pix = grp; pix < HWo; pix += G) {
+      const float gv = gp[pix];
+      acc[9] += gv;
+      const int ih0 = oh * d.stride - d.pad, iw0 = ow * d.stride - d.pad;
+#pragma unroll
+      for (int kh = 0; kh < 3; ++kh) {
+        const int ih = ih0 + kh;
+        if ((unsigned)ih >= (unsigned)d.H) continue;
+#pragma unroll
+        for (int kw = 0; kw < 3; ++kw) {
+          const int iw = iw0 + kw;
+          if ((unsigned)iw < (unsigned)d.W) acc[kh * 3 + kw] = fmaf(gv, xp[ih * d.W + iw], acc[kh * 3 + kw]);
+        }
+      }
+      ow += G;
+      while (ow >= d.Wo) {
+        ow -= d.Wo;
+        ++oh;
+      }
+    }
+  }
+  __syncthreads();
+  if (active) {
+#pragma unroll
+    for (int k = 0; k < 10; ++k) sred[((int64_t)grp * pairs + pr) * 10 + k] = acc[k];
+  }
+  __syncthreads();
+  float* out = partial + (int64_t)blockIdx.x * d.Cout * (Kel + 1);
+  for (int i = threadIdx.x; i < pairs * 10; i += blockDim.x) {
+    const int q = i / 10, k = i - q * 10;
+    float sum = 0.f;
+    for (int gg = 0; gg < G; ++gg) sum += sred[((int64_t)gg * pairs + q) * 10 + k];
+    const int oc = q / d.Cin, ic = q - oc * d.Cin;
+    if (k < 9) out[oc * (Kel + 1) + ic * 9 + k] = sum;
+    else if (ic == 0) out[oc * (Kel + 1) + Kel] = sum;  // bias: counted once per output channel
+  }
+}
+
+// Shared memory of conv_wgrad_image_kernel, or 0 when the shape is not its case.
+size_t conv_wgrad_image_smem(const ConvDesc& d) {
+  if (d.KH != 3 || d.KW != 3) return 0;
+  const int pairs = d.Cout * d.Cin;
+  if (pairs > 256) return 0;
+  const int G = std::max(1, 256 / pairs);
+  const size_t floats = (size_t)d.Cin * d.H * d.W + (size_t)d.Cout * d.Ho * d.Wo + (size_t)G * pairs * 10;
+  const size_t bytes = floats * sizeof(float);
+  return bytes <= 96 * 1024 ? bytes : 0;
+}
+
 __global__ void conv_wgrad_final_kernel(const float* __restrict__ partial, int chunks, int Cout, int Kel,
                                         float* __restrict__ dw, float* __restrict__ db, int accumulate) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -363,7 +450,11 @@ void conv2d_dgrad(DType dt, const void* g, const void* w, void* dx, const void* 
   DLVK_POST_LAUNCH();
 }
 
-int conv2d_wgrad_chunks(const ConvDesc& d) { return std::max(1, std::min(d.N, 64)); }
+// One image per chunk on the staged 3 x 3 path (up to 1024 chunks), 64 chunks otherwise.
+int conv2d_wgrad_chunks(const ConvDesc& d) {
+  if (conv_wgrad_image_smem(d) > 0) return std::max(1, std::min(d.N, 1024));
+  return std::max(1, std::min(d.N, 64));
+}
 int64_t conv2d_wgrad_scratch_floats(const ConvDesc& d) {
   return (int64_t)conv2d_wgrad_chunks(d) * d.Cout * (d.Cin * d.KH * d.KW + 1);
 }
@@ -372,6 +463,24 @@ void conv2d_wgrad(DType dt, const void* x, const void* g, float* dw, float* db, 
                   float* scratch, cudaStream_t s) {
   const int chunks = conv2d_wgrad_chunks(d);
   const int per = (d.N + chunks - 1) / chunks;
+  const size_t ismem = conv_wgrad_image_smem(d);
+  if (ismem > 0 && (dt == DType::F32 || dt == DType::BF16)) {
+    auto launch = [&](auto kern, const auto* xp, const auto* gp) {
+      if (ismem > 48 * 1024)
+        DLVK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ismem));
+      kern<<<(unsigned)chunks, 256, ismem, s>>>(xp, gp, scratch, d, per);
+    };
+    if (dt == DType::F32)
+      launch(conv_wgrad_image_kernel<float>, (const float*)x, (const float*)g);
+    else
+      launch(conv_wgrad_image_kernel<__nv_bfloat16>, (const __nv_bfloat16*)x, (const __nv_bfloat16*)g);
+    DLVK_POST_LAUNCH();
+    const int Kel = d.Cin * d.KH * d.KW;
+    const int tot = d.Cout * (Kel + 1);
+    conv_wgrad_final_kernel<<<(tot + 255) / 256, 256, 0, s>>>(scratch, chunks, d.Cout, Kel, dw, db, accumulate ? 1 : 0);
+    DLVK_POST_LAUNCH();
+    return;
+  }
   dim3 grid((unsigned)d.Cout, (unsigned)chunks);
   if (dt == DType::F32)
     conv_wgrad_partial_kernel<float><<<grid, 256, 0, s>>>((const float*)x, (const float*)g, scratch, d, per);

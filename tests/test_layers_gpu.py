@@ -22,8 +22,15 @@ def close(a, b, tol):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("shape", [(4, 1, 28, 28, 8, 3, 1, 1), (3, 8, 14, 14, 16, 3, 1, 1), (2, 3, 9, 11, 5, 3, 2, 0)])
+@pytest.mark.parametrize("shape", [(4, 1, 28, 28, 8, 3, 1, 1), (3, 8, 14, 14, 16, 3, 1, 1), (2, 3, 9, 11, 5, 3, 2, 0),
+                                   (1300, 8, 14, 14, 16, 3, 1, 1)])  # more images than weight-gradient chunks
 def test_conv2d(dtype, shape):
+    # fp32 references without TF32 (cuDNN picks TF32 algorithms at large batch)
+    with torch.backends.cudnn.flags(enabled=True, benchmark=False, deterministic=False, allow_tf32=False):
+        _conv2d_case(dtype, shape)
+
+
+def _conv2d_case(dtype, shape):
     C = _C()
     N, Cin, H, W, Cout, k, s, p = shape
     x = torch.randn(N, Cin, H, W, device="cuda")
