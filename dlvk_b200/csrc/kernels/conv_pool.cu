@@ -225,7 +225,10 @@ __global__ void __launch_bounds__(256) conv_wgrad_image_kernel(const T* __restri
     __syncthreads();  // the previous image's planes are no longer read
     const T* xn = x + (int64_t)n * d.Cin * HW;
     const T* gn = g + (int64_t)n * d.Cout * HWo;
+    // unrolled so that several loads per thread are in flight
+#pragma unroll 8
     for (int i = threadIdx.x; i < d.Cin * HW; i += blockDim.x) sx[i] = to_f32(xn[i]);
+#pragma unroll 8
     for (int i = threadIdx.x; i < d.Cout * HWo; i += blockDim.x) sg[i] = to_f32(gn[i]);
     __syncthreads();
     if (!active) continue;
@@ -281,13 +284,23 @@ size_t conv_wgrad_image_smem(const ConvDesc& d) {
   return bytes <= 96 * 1024 ? bytes : 0;
 }
 
-__global__ void conv_wgrad_final_kernel(const float* __restrict__ partial, int chunks, int Cout, int Kel,
-                                        float* __restrict__ dw, float* __restrict__ db, int accumulate) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+// Sums the per-chunk partials: a block covers 32 entries with 8 threads per
+// entry, each summing every 8th chunk; the 8 are combined in a fixed order.
+__global__ void __launch_bounds__(256) conv_wgrad_final_kernel(const float* __restrict__ partial, int chunks, int Cout,
+                                                               int Kel, float* __restrict__ dw,
+                                                               float* __restrict__ db, int accumulate) {
+  __shared__ float red[8][33];
+  const int i = blockIdx.x * 32 + threadIdx.x;
   const int per = Kel + 1;
-  if (i >= Cout * per) return;
+  float sv = 0.f;
+  if (i < Cout * per)
+    for (int c = threadIdx.y; c < chunks; c += 8) sv += partial[(int64_t)c * Cout * per + i];
+  red[threadIdx.y][threadIdx.x] = sv;
+  __syncthreads();
+  if (threadIdx.y != 0 || i >= Cout * per) return;
   float s = 0.f;
-  for (int c = 0; c < chunks; ++c) s += partial[(int64_t)c * Cout * per + i];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) s += red[k][threadIdx.x];
   const int co = i / per, wi = i - co * per;
   if (wi < Kel) {
     float* p = dw + co * Kel + wi;
@@ -477,7 +490,7 @@ void conv2d_wgrad(DType dt, const void* x, const void* g, float* dw, float* db, 
     DLVK_POST_LAUNCH();
     const int Kel = d.Cin * d.KH * d.KW;
     const int tot = d.Cout * (Kel + 1);
-    conv_wgrad_final_kernel<<<(tot + 255) / 256, 256, 0, s>>>(scratch, chunks, d.Cout, Kel, dw, db, accumulate ? 1 : 0);
+    conv_wgrad_final_kernel<<<(tot + 31) / 32, dim3(32, 8), 0, s>>>(scratch, chunks, d.Cout, Kel, dw, db, accumulate ? 1 : 0);
     DLVK_POST_LAUNCH();
     return;
   }
@@ -492,7 +505,7 @@ void conv2d_wgrad(DType dt, const void* x, const void* g, float* dw, float* db, 
   DLVK_POST_LAUNCH();
   const int Kel = d.Cin * d.KH * d.KW;
   const int tot = d.Cout * (Kel + 1);
-  conv_wgrad_final_kernel<<<(tot + 255) / 256, 256, 0, s>>>(scratch, chunks, d.Cout, Kel, dw, db, accumulate ? 1 : 0);
+  conv_wgrad_final_kernel<<<(tot + 31) / 32, dim3(32, 8), 0, s>>>(scratch, chunks, d.Cout, Kel, dw, db, accumulate ? 1 : 0);
   DLVK_POST_LAUNCH();
 }
 
