@@ -106,6 +106,65 @@ __global__ void __launch_bounds__(256) conv_dgrad_kernel(const T* __restrict__ g
   dx[xi] = from_f32<T>(acc);
 }
 
+// Input gradient with the output gradient staged: one block per chunk of
+// images; each image's [Cout][Ho][Wo] gradient and the filter bank sit in
+// shared memory (fp32) and each thread computes input elements
+// threadIdx.x, + 256, ... of the image (all output channels and taps from
+// shared memory, so a warp reads one filter value per step and consecutive
+// gradient values).
+template <typename T>
+__global__ void __launch_bounds__(256) conv_dgrad_image_kernel(const T* __restrict__ g, const T* __restrict__ w,
+                                                               T* __restrict__ dx, const T* __restrict__ relu_src,
+                                                               ConvDesc d, int ipb) {
+  extern __shared__ float dsm[];
+  const int Kel = d.Cin * d.KH * d.KW;
+  const int HW = d.H * d.W, HWo = d.Ho * d.Wo;
+  float* sw = dsm;                  // [Cout][Kel]
+  float* sg = dsm + d.Cout * Kel;   // [Cout][Ho][Wo]
+  for (int i = threadIdx.x; i < d.Cout * Kel; i += blockDim.x) sw[i] = to_f32(w[i]);
+  const int n0 = blockIdx.x * ipb, n1 = min(d.N, n0 + ipb);
+  const int tot = d.Cin * HW;
+  for (int n = n0; n < n1; ++n) {
+    __syncthreads();  // the previous image's gradient is no longer read (and sw is written)
+    const T* gn = g + (int64_t)n * d.Cout * HWo;
+#pragma unroll 8
+    for (int i = threadIdx.x; i < d.Cout * HWo; i += blockDim.x) sg[i] = to_f32(gn[i]);
+    __syncthreads();
+    for (int e = threadIdx.x; e < tot; e += blockDim.x) {
+      const int ci = e / HW;
+      const int rem = e - ci * HW;
+      const int ih = rem / d.W, iw = rem - ih * d.W;
+      float acc = 0.f;
+      for (int kh = 0; kh < d.KH; ++kh) {
+        const int th = ih + d.pad - kh;
+        if (th < 0 || th % d.stride) continue;
+        const int oh = th / d.stride;
+        if (oh >= d.Ho) continue;
+        for (int kw = 0; kw < d.KW; ++kw) {
+          const int tw = iw + d.pad - kw;
+          if (tw < 0 || tw % d.stride) continue;
+          const int ow = tw / d.stride;
+          if (ow >= d.Wo) continue;
+          const float* gp = sg + oh * d.Wo + ow;
+          const float* wp = sw + (ci * d.KH + kh) * d.KW + kw;
+#pragma unroll 4
+          for (int co = 0; co < d.Cout; ++co) acc = fmaf(gp[co * HWo], wp[co * Kel], acc);
+        }
+      }
+      const int64_t xi = (int64_t)n * tot + e;
+      if (relu_src && !(to_f32(relu_src[xi]) > 0.f)) acc = 0.f;
+      dx[xi] = from_f32<T>(acc);
+    }
+  }
+}
+
+// Shared memory of conv_dgrad_image_kernel, or 0 when it does not apply.
+size_t conv_dgrad_image_smem(const ConvDesc& d) {
+  const size_t floats = (size_t)d.Cout * d.Cin * d.KH * d.KW + (size_t)d.Cout * d.Ho * d.Wo;
+  const size_t bytes = floats * sizeof(float);
+  return (d.Cin * d.H * d.W <= 16384 && bytes <= 96 * 1024) ? bytes : 0;
+}
+
 // Weight/bias gradient partials: block (co, chunk) sums over the images of its
 // chunk and all output pixels; each thread keeps 32 weight partials in
 // registers (weights processed in groups of 32).  The group's input offsets
@@ -444,6 +503,23 @@ void conv2d_dgrad(DType dt, const void* g, const void* w, void* dx, const void* 
                   cudaStream_t s) {
   const size_t smem = (size_t)d.Cout * d.Cin * d.KH * d.KW * sizeof(float);
   DLVK_CHECK(smem <= 200 * 1024, "conv2d_dgrad: filter bank too large for shared memory");
+  const size_t ismem = conv_dgrad_image_smem(d);
+  if (ismem > 0 && (dt == DType::F32 || dt == DType::BF16)) {
+    const int chunks = std::max(1, std::min(d.N, 1024));
+    const int per = (d.N + chunks - 1) / chunks;
+    auto launch = [&](auto kern, const auto* gp, const auto* wp, auto* dxp, const auto* rp) {
+      if (ismem > 48 * 1024)
+        DLVK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ismem));
+      kern<<<(unsigned)chunks, 256, ismem, s>>>(gp, wp, dxp, rp, d, per);
+    };
+    if (dt == DType::F32)
+      launch(conv_dgrad_image_kernel<float>, (const float*)g, (const float*)w, (float*)dx, (const float*)relu_src);
+    else
+      launch(conv_dgrad_image_kernel<__nv_bfloat16>, (const __nv_bfloat16*)g, (const __nv_bfloat16*)w,
+             (__nv_bfloat16*)dx, (const __nv_bfloat16*)relu_src);
+    DLVK_POST_LAUNCH();
+    return;
+  }
   const int64_t per_img = (int64_t)d.Cin * d.H * d.W;
   dim3 grid((unsigned)((per_img + 255) / 256), (unsigned)d.N);
   if (dt == DType::F32) {
