@@ -453,7 +453,9 @@ at::Tensor gemm_op(const at::Tensor& A, const at::Tensor& B, c10::optional<at::T
             wsf);
   } else {
     if (bits_o.defined()) bits_o.zero_();  // the SIMT kernel sets bits with atomic ORs
-    gemm_simt(to_dtype(A), to_dtype(C), a, stream());
+    const int64_t swf = gemm_simt_workspace_floats(a);
+    at::Tensor sws = swf > 0 ? at::empty({swf}, A.options().dtype(at::kFloat)) : at::Tensor();
+    gemm_simt(to_dtype(A), to_dtype(C), a, stream(), swf > 0 ? sws.data_ptr<float>() : nullptr, swf);
   }
   if (colsum_out.has_value()) {
     if (a.colsum != nullptr) {

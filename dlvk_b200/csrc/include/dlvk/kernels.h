@@ -93,7 +93,12 @@ struct GemmArgs {
   const uint32_t* relu_bits = nullptr;
   int64_t ldbits = 0;
 };
-void gemm_simt(DType in_dt, DType out_dt, const GemmArgs& a, cudaStream_t s);
+// SIMT GEMM.  With a workspace of gemm_simt_workspace_floats(a) floats, a
+// small 2-D GEMM with a plain epilogue splits K across blocks (fp32 partials,
+// then a finish kernel; deterministic).
+int64_t gemm_simt_workspace_floats(const GemmArgs& a);
+void gemm_simt(DType in_dt, DType out_dt, const GemmArgs& a, cudaStream_t s, float* ws = nullptr,
+               int64_t ws_floats = 0);
 bool gemm_tc_supported(const GemmArgs& a);
 // bf16 inputs, bf16 or f32 output, tcgen05 tensor cores.  `err` is the
 // device error word; `max_ctas` caps the persistent grid (0 = #SMs).

@@ -497,3 +497,24 @@ def test_gemm_tc_residual_in_registers(M, N, K, strided):
     ref = torch.relu(a.float() @ b.float() + bias + res.float())
     _check(out, ref, 1e-2)
     assert int(C.read_device_error(True)) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 47, 256), (256, 47, 2048), (32, 128, 784), (200, 10, 1000)])
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_gemm_simt_split_k(M, N, K, dt):
+    """Small GEMMs on the SIMT path split K across blocks (fp32 partials and a
+    finish kernel): plain, bias + ReLU, and accumulate into C."""
+    C = _C()
+    torch.manual_seed(M + K)
+    a = torch.randn(M, K, device="cuda").to(dt)
+    b = torch.randn(K, N, device="cuda").to(dt)
+    tol = 1e-4 if dt == torch.float32 else 1e-2
+    _check(C.gemm(a, b, force_path=2), _ref(a, b), tol)
+    bias = torch.randn(N, device="cuda")
+    _check(C.gemm(a, b, bias=bias, act=1, force_path=2), _ref(a, b, bias, act=1), tol)
+    acc = torch.randn(M, N, device="cuda")
+    ref = acc + a.float() @ b.float()
+    C.gemm(a, b, beta=1.0, out=acc, force_path=2)
+    _check(acc, ref, 1e-4)
+    torch.cuda.synchronize()
+    assert C.read_device_error(True) == 0
