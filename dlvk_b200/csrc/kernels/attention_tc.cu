@@ -216,57 +216,61 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) flash_fwd_kernel(const __grid_
       // it stays in registers).
       struct St {
         uint32_t sph, pph, oph;
-        int prev;  // K/V stage of the stream's previous tile
+        int prev;  // K/V stage of the stream's previous tile (its PV is pending)
+        int cur;   // K/V stage of the tile whose S was just issued
       };
-      St st0{0, 0, 0, 0}, st1{0, 0, 0, 0};
+      St st0{0, 0, 0, 0, 0}, st1{0, 0, 0, 0, 0};
       bool ok = true;
-      // Tile j's S for stream t, then the stream's previous tile's PV.
-      auto step = [&](int r, int j, int t, St& st) {
-        if (item_of(r, t) >= items) return true;
-        const uint32_t tS = tbase + (uint32_t)(t * 128), tO = tbase + 256u + (uint32_t)(t * 64);
-        const uint32_t tP = tbase + 384u + (uint32_t)(t * 64);
-        if (j < nt) {
-          if (j == 0 && !mbar_wait(&q_full[t], r & 1, p.err)) return false;
-          if (!mbar_wait(&kv_full[kvs], kvph, p.err) || !mbar_wait(&s_empty[t], st.sph ^ 1u, p.err)) return false;
-          st.sph ^= 1u;
-          tc_fence_after();
-          const uint32_t qa = smem_u32(sQ + t * TILE), ka = smem_u32(sKV + kvs * 2 * TILE);
+      // Round j: both streams' S for tile j, then both streams' PV for tile
+      // j - 1, so neither stream's scores wait behind the other's softmax.
+      auto stepS = [&](int r, int j, int t, St& st) {
+        if (item_of(r, t) >= items || j >= nt) return true;
+        const uint32_t tS = tbase + (uint32_t)(t * 128);
+        if (j == 0 && !mbar_wait(&q_full[t], r & 1, p.err)) return false;
+        if (!mbar_wait(&kv_full[kvs], kvph, p.err) || !mbar_wait(&s_empty[t], st.sph ^ 1u, p.err)) return false;
+        st.sph ^= 1u;
+        tc_fence_after();
+        const uint32_t qa = smem_u32(sQ + t * TILE), ka = smem_u32(sKV + kvs * 2 * TILE);
 #pragma unroll
-          for (int k = 0; k < FD / 16; ++k)
-            mma_f16(tS, make_sw128_desc(qa + k * 32, 16, 1024), make_sw128_desc(ka + k * 32, 16, 1024), id_s,
-                    k ? 1u : 0u);
-          mma_commit(&s_full[t]);
-          if (j == nt - 1) mma_commit(&q_empty[t]);
-        }
-        if (j > 0) {
-          if (j == 1) {
-            if (!mbar_wait(&o_empty[t], st.oph ^ 1u, p.err)) return false;
-            st.oph ^= 1u;
-          }
-          if (!mbar_wait(&p_full[t], st.pph, p.err)) return false;
-          st.pph ^= 1u;
-          tc_fence_after();
-          const uint32_t va = smem_u32(sKV + st.prev * 2 * TILE + TILE);
-          // O += P V: A = P from TMEM (16 keys = 8 columns per MMA), B = V
-          // MN-major [keys x d].
-#pragma unroll
-          for (int k = 0; k < FT / 16; ++k)
-            mma_f16_ts(tO, tP + (uint32_t)(k * 8), make_sw128_desc(va + k * 2048, 16384, 1024), id_o,
-                       (j > 1 || k > 0) ? 1u : 0u);
-          mma_commit(&kv_empty[st.prev]);
-          mma_commit(&pv_done[t]);
-        }
-        if (j < nt) {
-          st.prev = kvs;
-          if (++kvs == FWD_KV_STAGES) {
-            kvs = 0;
-            kvph ^= 1u;
-          }
+        for (int k = 0; k < FD / 16; ++k)
+          mma_f16(tS, make_sw128_desc(qa + k * 32, 16, 1024), make_sw128_desc(ka + k * 32, 16, 1024), id_s,
+                  k ? 1u : 0u);
+        mma_commit(&s_full[t]);
+        if (j == nt - 1) mma_commit(&q_empty[t]);
+        st.cur = kvs;
+        if (++kvs == FWD_KV_STAGES) {
+          kvs = 0;
+          kvph ^= 1u;
         }
         return true;
       };
+      auto stepPV = [&](int r, int j, int t, St& st) {
+        if (item_of(r, t) >= items || j == 0) return true;
+        const uint32_t tO = tbase + 256u + (uint32_t)(t * 64), tP = tbase + 384u + (uint32_t)(t * 64);
+        if (j == 1) {
+          if (!mbar_wait(&o_empty[t], st.oph ^ 1u, p.err)) return false;
+          st.oph ^= 1u;
+        }
+        if (!mbar_wait(&p_full[t], st.pph, p.err)) return false;
+        st.pph ^= 1u;
+        tc_fence_after();
+        const uint32_t va = smem_u32(sKV + st.prev * 2 * TILE + TILE);
+        // O += P V: A = P from TMEM (16 keys = 8 columns per MMA), B = V
+        // MN-major [keys x d].
+#pragma unroll
+        for (int k = 0; k < FT / 16; ++k)
+          mma_f16_ts(tO, tP + (uint32_t)(k * 8), make_sw128_desc(va + k * 2048, 16384, 1024), id_o,
+                     (j > 1 || k > 0) ? 1u : 0u);
+        mma_commit(&kv_empty[st.prev]);
+        mma_commit(&pv_done[t]);
+        return true;
+      };
       for (int r = 0; ok && item_of(r, 0) < items; ++r)
-        for (int j = 0; ok && j <= nt; ++j) ok = step(r, j, 0, st0) && step(r, j, 1, st1);
+        for (int j = 0; ok && j <= nt; ++j) {
+          ok = stepS(r, j, 0, st0) && stepS(r, j, 1, st1) && stepPV(r, j, 0, st0) && stepPV(r, j, 1, st1);
+          st0.prev = st0.cur;
+          st1.prev = st1.cur;
+        }
     }
   } else {
     // Softmax warps: stream t = (warp - 2) / 4; warp w reads TMEM lanes
