@@ -35,6 +35,8 @@ def make(M, N, K, am, bm):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--no-flush", action="store_true",
+                    help="back-to-back launches with L2 warm (as inside a training step), not L2 flushed before each")
     ap.add_argument("--shapes", nargs="*", default=None)
     ap.add_argument("--no-cublas", action="store_true")
     ap.add_argument("--check", action="store_true")
@@ -81,7 +83,7 @@ def main():
             kw["relu_mask"] = torch.randn(M, N, device="cuda").bfloat16()
         if args.beta:
             kw["beta"] = args.beta
-        t_ours = time_fn(lambda: C.gemm(a, b, out=out, force_path=1, **kw), iters=args.iters)
+        t_ours = time_fn(lambda: C.gemm(a, b, out=out, force_path=1, **kw), iters=args.iters, flush=not args.no_flush)
         rec = {"M": M, "N": N, "K": K, "a": am, "b": bm, "epilogue": sorted(kw), "out": str(out.dtype)[6:],
                "plan": list(C.gemm_plan(a, b, args.out_f32)),
                "ours_ms": round(t_ours, 4),
@@ -90,7 +92,7 @@ def main():
             bn, sp, pr = (int(v) for v in tl.split(","))
             C.gemm_set_tiling(bn, sp, pr)
             try:
-                tt = time_fn(lambda: C.gemm(a, b, out=out, force_path=1, **kw), iters=args.iters)
+                tt = time_fn(lambda: C.gemm(a, b, out=out, force_path=1, **kw), iters=args.iters, flush=not args.no_flush)
                 ref = a.float() @ b.float()
                 C.gemm(a, b, out=out, force_path=1, **kw)
                 ok = float((out.float() - ref).abs().max() / ref.abs().max()) < 2e-2
@@ -100,12 +102,12 @@ def main():
         if args.compare_single:
             C.gemm_set_pair(False)
             try:
-                t_1 = time_fn(lambda: C.gemm(a, b, out=out, force_path=1, **kw), iters=args.iters)
+                t_1 = time_fn(lambda: C.gemm(a, b, out=out, force_path=1, **kw), iters=args.iters, flush=not args.no_flush)
             finally:
                 C.gemm_set_pair(True)
             rec.update({"single_cta_ms": round(t_1, 4), "single_cta_tflops": round(flops / t_1 / 1e9, 1)})
         if not args.no_cublas:
-            t_cb = time_fn(lambda: torch.matmul(a, b, out=out_cb), iters=args.iters)
+            t_cb = time_fn(lambda: torch.matmul(a, b, out=out_cb), iters=args.iters, flush=not args.no_flush)
             rec.update({"cublas_ms": round(t_cb, 4), "cublas_tflops": round(flops / t_cb / 1e9, 1),
                         "speedup_vs_cublas": round(t_cb / t_ours, 3)})
         if args.check:
@@ -134,7 +136,7 @@ def fp32_main(args):
         rec = {"M": M, "N": N, "K": K, "a": am, "b": bm}
         for name, mode in (("ours_3xtf32", 3), ("ours_tf32", 1)):
             C.set_fp32_gemm_mode(mode)
-            t = time_fn(lambda: C.gemm(a, b, out=out, force_path=1), iters=args.iters)
+            t = time_fn(lambda: C.gemm(a, b, out=out, force_path=1), iters=args.iters, flush=not args.no_flush)
             rec[name + "_ms"] = round(t, 4)
             rec[name + "_tflops"] = round(flops / t / 1e9, 1)
             rec[name + "_rel_err"] = float((out.double() - ref).norm() / ref.norm())
@@ -143,7 +145,7 @@ def fp32_main(args):
             prev = torch.backends.cuda.matmul.allow_tf32
             torch.backends.cuda.matmul.allow_tf32 = tf
             try:
-                t = time_fn(lambda: torch.matmul(a, b, out=out), iters=args.iters)
+                t = time_fn(lambda: torch.matmul(a, b, out=out), iters=args.iters, flush=not args.no_flush)
                 rec[name + "_ms"] = round(t, 4)
                 rec[name + "_tflops"] = round(flops / t / 1e9, 1)
                 rec[name + "_rel_err"] = float((out.double() - ref).norm() / ref.norm())
