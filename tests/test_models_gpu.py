@@ -16,6 +16,23 @@ def close(a, b, tol):
     assert err <= tol * scale + 1e-7, f"max err {err}, scale {scale}"
 
 
+def _fp32_grad_check(builder, kw, x, y, opt, g_gpu, g_cpu_bf16, factor=2.0):
+    """Normwise check against an fp32 model of the same weights: the GPU bf16
+    gradients may be at most `factor` times as far from the fp32 gradients as
+    the CPU bf16 path's own are.  A kernel that drops a k-block, a tile edge
+    or a head moves the GPU far past that; bf16 rounding noise does not."""
+    m32 = builder(device="cpu", dtype="fp32", seed=0, **kw)
+    m32.build()
+    m32.train_step(x, y, dl.CrossEntropyLoss(), opt)
+    g32 = m32.store.grad.float()
+
+    def rel(g):
+        return ((g.float().cpu() - g32).norm() / g32.norm()).item()
+
+    e_gpu, e_cpu = rel(g_gpu), rel(g_cpu_bf16)
+    assert e_gpu <= factor * e_cpu + 1e-3, f"GPU bf16 grads {e_gpu:.4f} from fp32, CPU bf16 {e_cpu:.4f}"
+
+
 def _pair(builder, dtype_gpu, **kw):
     # The CPU reference path runs at the same storage precision, so bf16
     # rounding happens at the same points on both sides.
@@ -64,6 +81,7 @@ def test_wide_mlp_small_matches_cpu():
     lc, lg = _step_both(mc, mg, x, y, dl.SGD(0.01, 0.9), dl.SGD(0.01, 0.9))
     close(lg, lc, 5e-2)
     close(mg.store.grad, mc.store.grad, 1e-1)
+    _fp32_grad_check(zoo.wide_mlp, kw, x, y, dl.SGD(0.01, 0.9), mg.store.grad, mc.store.grad)
 
 
 def test_transformer_small_matches_cpu():
@@ -73,6 +91,7 @@ def test_transformer_small_matches_cpu():
     lc, lg = _step_both(mc, mg, x, y, dl.Adam(1e-3), dl.Adam(1e-3))
     close(lg, lc, 3e-2)
     close(mg.store.grad, mc.store.grad, 1e-1)
+    _fp32_grad_check(zoo.transformer, kw, x, y, dl.Adam(1e-3), mg.store.grad, mc.store.grad)
 
 
 def test_dlvk_roundtrip_gpu(tmp_path):
