@@ -276,6 +276,24 @@ __global__ void __launch_bounds__(512, 2) softmax_ce_reg_kernel(const __nv_bfloa
   }
 }
 
+constexpr float kLog2e = 1.4426950408889634f;
+
+// 2^x by the hardware approximation (ex2.approx.ftz).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// A bf16 pair (first element in the low half) as two floats: a bf16 is the
+// upper half of the fp32 of the same value.
+__device__ __forceinline__ float2 bf2_unpack(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+__device__ __forceinline__ uint32_t bf2_pack(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
 // Persistent form of softmax_ce_reg_kernel: each block walks the rows
 // blockIdx.x, + gridDim.x, ... and streams its next row into shared memory
 // with cp.async while it reduces the current one from registers, so the
@@ -324,19 +342,17 @@ __global__ void __launch_bounds__(512, 2) softmax_ce_pipe_kernel(const __nv_bflo
         (label >= 0 && label < cols) ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(srow)[label]) : 0.f;
     __syncthreads();  // every thread has read the buffer
     prefetch(r + gridDim.x);
-    float mx = -INFINITY;
+    // The row maximum on bf16 pairs (exact: a maximum needs no rounding).
+    __nv_bfloat162 m2 = __halves2bfloat162(__ushort_as_bfloat16(0xff80), __ushort_as_bfloat16(0xff80));
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int v = threadIdx.x + i * THREADS;
       if (v < nvec) {
         const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float2 f = __bfloat1622float2(h[k]);
-          mx = fmaxf(mx, fmaxf(f.x, f.y));
-        }
+        m2 = __hmax2(m2, __hmax2(__hmax2(h[0], h[1]), __hmax2(h[2], h[3])));
       }
     }
+    float mx = fmaxf(__low2float(m2), __high2float(m2));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if (lane == 0) red[wid] = mx;
@@ -347,22 +363,28 @@ __global__ void __launch_bounds__(512, 2) softmax_ce_pipe_kernel(const __nv_bflo
     // The exponentials replace the logits in registers (as bf16), so the
     // gradient pass needs none: non-label gradients carry one extra bf16
     // rounding of p, the same size as the rounding of the stored gradient.
-    float sum = 0.f;
+    // exp(x - max) = 2^((x - max) log2(e)), packed in pairs.  The difference
+    // comes first: it is exact near the maximum, where a fused
+    // x log2(e) - max log2(e) would leave the rounding error of max log2(e)
+    // (about 1e-6 at |max| = 20) in every term, and with it in p - 1 of a
+    // confident label.
+    const float2 l2e = make_float2(kLog2e, kLog2e), nm = make_float2(-mx, -mx);
+    float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int v = threadIdx.x + i * THREADS;
       if (v < nvec) {
-        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw[i]);
+        uint32_t* w = reinterpret_cast<uint32_t*>(&raw[i]);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const float2 f = __bfloat1622float2(h[k]);
-          const float e0 = __expf(f.x - mx), e1 = __expf(f.y - mx);
-          sum += e0 + e1;
-          h[k] = __floats2bfloat162_rn(e0, e1);
+          const float2 a = __fmul2_rn(__fadd2_rn(bf2_unpack(w[k]), nm), l2e);
+          const float2 e = make_float2(ex2_approx(a.x), ex2_approx(a.y));
+          s2 = __fadd2_rn(s2, e);
+          w[k] = bf2_pack(e.x, e.y);
         }
       }
     }
-    sum = warp_sum(sum);
+    float sum = warp_sum(s2.x + s2.y);
     __syncthreads();  // every warp has read red[] (the maximum)
     if (lane == 0) red[wid] = sum;
     __syncthreads();
@@ -372,25 +394,25 @@ __global__ void __launch_bounds__(512, 2) softmax_ce_pipe_kernel(const __nv_bflo
     if (threadIdx.x == 0 && loss_rows) loss_rows[r] = label < 0 ? 0.f : mx + logf(sum) - xl;
     const float gs = label < 0 ? 0.f : grad_scale;
     const float gl = (__expf(xl - mx) * inv - 1.f) * gs;  // the label's gradient, from fp32 throughout
-    const float ginv = inv * gs;
+    const float2 ginv = make_float2(inv * gs, inv * gs);
     __nv_bfloat16* dr = dlogits + r * cols;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int v = threadIdx.x + i * THREADS;
       if (v >= nvec) continue;
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
+      const uint32_t* w = reinterpret_cast<const uint32_t*>(&raw[i]);
       uint4 o;
-      __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+      uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const int c = v * 8 + 2 * k;
-        const float2 e = __bfloat1622float2(h[k]);
-        const float g0 = c == label ? gl : e.x * ginv;
-        const float g1 = c + 1 == label ? gl : e.y * ginv;
-        oh[k] = __floats2bfloat162_rn(g0, g1);
+        const float2 g = __fmul2_rn(bf2_unpack(w[k]), ginv);
+        ow[k] = bf2_pack(g.x, g.y);
       }
       reinterpret_cast<uint4*>(dr)[v] = o;
     }
+    // The label's gradient replaces its p * scale, written by the thread that
+    // stored the label's vector (a later store of the same thread).
+    if (label >= 0 && label < cols && (label / 8) % THREADS == (int)threadIdx.x) dr[label] = __float2bfloat16_rn(gl);
   }
   sm100::cp_async_wait<0>();
 }
