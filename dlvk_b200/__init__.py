@@ -20,7 +20,8 @@ from .models.sequential import Model, Sequential
 from .models.params import Parameter, ParamStore
 from .optim import (Optimizer, SGD, Adam, RMSprop, GradientClipping, LRScheduler, StepLRScheduler,
                     ExponentialLRScheduler, CosineAnnealingLRScheduler, LinearLRScheduler)
-from .losses import LossFunction, CrossEntropyLoss, MeanSquaredError, BinaryCrossEntropyLoss, MSELoss, BCELoss
+from .losses import (LossFunction, CrossEntropyLoss, MeanSquaredError, BinaryCrossEntropyLoss, MSELoss, BCELoss,
+                     LossOpsGPU)
 
 # The reference spells the device class VulkanDevice; this framework's device
 # runtime is CUDA.

@@ -9,6 +9,7 @@
 #include <cctype>
 #include <cmath>
 #include <sstream>
+#include <stdexcept>
 
 #include "dispatch.h"
 #include "dlvk/optimizers/optimizers.h"
@@ -375,5 +376,32 @@ Tensor FlattenLayer::forward(const Tensor& input) {
   return Tensor(input.data().reshape({input.data().size(0), -1}), input.device());
 }
 Tensor FlattenLayer::backward(const Tensor& g) { return Tensor(g.data().reshape(in_shape_), g.device()); }
+
+// ---------------------------------------------------------------- accessors
+std::vector<size_t> window_output_shape(const std::vector<size_t>& input_shape, size_t channels, size_t k,
+                                        size_t stride, size_t padding) {
+  const size_t r = input_shape.size();
+  if (r != 3 && r != 4) throw std::invalid_argument("window_output_shape: expected an NCHW or CHW shape");
+  if (stride == 0) throw std::invalid_argument("window_output_shape: stride 0");
+  std::vector<size_t> out = input_shape;
+  for (size_t d = r - 2; d < r; ++d) {
+    const size_t padded = input_shape[d] + 2 * padding;
+    if (padded < k) throw std::invalid_argument("window_output_shape: window larger than the padded input");
+    out[d] = (padded - k) / stride + 1;
+  }
+  if (channels) out[r - 3] = channels;
+  return out;
+}
+
+void BatchNormLayer::copy_into(at::Tensor& dst, const Tensor& src, const char* what) {
+  if (!src.defined() || src.data().numel() != dst.numel())
+    throw std::invalid_argument(std::string("BatchNorm ") + what + ": element count does not match");
+  dst.copy_(src.data().reshape(dst.sizes()));
+}
+
+void DropoutLayer::set_dropout_rate(float r) {
+  if (!(r >= 0.f && r < 1.f)) throw std::invalid_argument("dropout rate must be in [0, 1)");
+  rate = r;
+}
 
 }  // namespace dlvk

@@ -4,6 +4,7 @@
 // it uses the same device hyper-parameter block and optim.cu kernels.
 #include "dlvk/optimizers/optimizers.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 
@@ -19,7 +20,9 @@ struct Optimizer::State {
   Sequential* model = nullptr;
   at::Tensor m, v;        // flat fp32, parallel to the model's buffers
   at::Tensor hyper;       // device OptimHyper block (CUDA)
-  at::Tensor clip;        // device clip coefficient (1)
+  at::Tensor clip;        // clip coefficient (1); the CUDA update reads it through the hyper block
+  at::Tensor sumsq, scratch;  // norm-clipping work buffers (CUDA)
+  bool clip_set = false;      // clip holds a norm-clipping coefficient
   int64_t step = 0;       // host step count
 };
 
@@ -97,6 +100,49 @@ void Optimizer::set_learning_rate(double lr) {
   }
 }
 
+void Optimizer::set_grad_clip_norm(double max_norm) {
+  TORCH_CHECK(max_norm > 0.0, "dlvk: set_grad_clip_norm needs max_norm > 0");
+  clip_norm_ = max_norm;
+  use_clip_norm_ = true;
+}
+
+void Optimizer::set_grad_clip_value(double min_val, double max_val) {
+  TORCH_CHECK(min_val <= max_val, "dlvk: set_grad_clip_value: empty range");
+  clip_min_ = min_val;
+  clip_max_ = max_val;
+  use_clip_value_ = true;
+}
+
+void Optimizer::disable_grad_clipping() { use_clip_norm_ = use_clip_value_ = false; }
+
+// Value clamp, then the norm-clipping coefficient into st.clip: on CUDA by
+// the grad_stats kernel (sum of squares and coefficient stay on the device),
+// on CPU from the fp32 norm, as the Python package's Optimizer.prepare_grads.
+void Optimizer::prepare_grads(State& st, at::Tensor& grad) {
+  if (use_clip_value_) {
+    if (grad.is_cuda())
+      aten::unary_op(grad, UN_CLAMP, clip_min_, clip_max_, grad, c10::nullopt);
+    else
+      grad.clamp_(clip_min_, clip_max_);
+  }
+  if (!use_clip_norm_) {
+    if (st.clip_set) st.clip.fill_(1.0);  // clipping was switched off since the last step
+    st.clip_set = false;
+    return;
+  }
+  st.clip_set = true;
+  if (grad.is_cuda()) {
+    if (!st.sumsq.defined()) {
+      st.sumsq = at::zeros({1}, grad.options());
+      st.scratch = at::empty({(int64_t)grad_stats_scratch_floats()}, grad.options());
+    }
+    aten::grad_stats_op(grad, 1.0, clip_norm_, st.sumsq, c10::nullopt, st.clip, false, st.scratch, c10::nullopt);
+  } else {
+    const double norm = grad.norm().item<double>();
+    st.clip.fill_(std::min(1.0, clip_norm_ / (norm + 1e-6)));
+  }
+}
+
 void Optimizer::advance(State& st) {
   st.step += 1;
   if (st.hyper.defined()) aten::optim_advance_op(st.hyper);
@@ -108,6 +154,12 @@ void Optimizer::update_range(State& st, at::Tensor& master, at::Tensor& grad, in
   api::OptT m = st.m.defined() ? api::OptT(st.m.narrow(0, start, end - start)) : c10::nullopt;
   api::OptT v = st.v.defined() ? api::OptT(st.v.narrow(0, start, end - start)) : c10::nullopt;
   api::CpuHyper h{lr_, beta1_, beta2_, eps_, weight_decay_, momentum_, alpha_, bias_correction_, st.step};
+  if (!st.hyper.defined() && use_clip_norm_) {
+    // The CPU update has no clip pointer: scale a copy of the gradient.
+    at::Tensor gs = g * st.clip.item<float>();
+    api::optim_update(kind_, st.hyper, h, p, gs, m, v);
+    return;
+  }
   api::optim_update(kind_, st.hyper, h, p, g, m, v);
 }
 
@@ -115,6 +167,7 @@ void Optimizer::step(Sequential& model) {
   model.build();
   State& st = state(model);
   advance(st);
+  prepare_grads(st, model.grad());
   update_range(st, model.master(), model.grad(), 0, model.flat_numel());
 }
 
@@ -125,6 +178,7 @@ void Optimizer::update(ModernLayer* layer) {
   auto* model = static_cast<Sequential*>(const_cast<void*>(params[0]->store));
   State& st = state(*model);
   advance(st);
+  prepare_grads(st, model->grad());
   for (Parameter* p : params) update_range(st, model->master(), model->grad(), p->offset, p->offset + p->numel());
 }
 

@@ -16,6 +16,13 @@ namespace dlvk {
 
 enum class ActivationType { ReLU, Sigmoid, Tanh, Softmax };
 
+// Output shape of a k x k window with `stride` and `padding` over an
+// [N, C, H, W] or [C, H, W] input: (H + 2 padding - k) / stride + 1 per
+// spatial dimension; `channels` replaces C when nonzero.  Throws
+// std::invalid_argument for other ranks or a window that does not fit.
+std::vector<size_t> window_output_shape(const std::vector<size_t>& input_shape, size_t channels, size_t k,
+                                        size_t stride, size_t padding);
+
 class DenseLayer : public ModernLayer {
  public:
   DenseLayer(size_t input_size, size_t output_size, bool use_bias, at::Generator& gen);
@@ -30,6 +37,11 @@ class DenseLayer : public ModernLayer {
   // GEMM applies that ReLU's backward; defer_relu: this layer's own ReLU
   // backward is applied by its consumer.
   Tensor forward_fused(const Tensor& input, int act, bool mask_input, bool defer_relu);
+
+  // Accessors of the reference's dense_layer.h:31-32: views of the fp32
+  // masters (W [in, out]); an undefined Tensor when built without a bias.
+  Tensor get_weights() const { return Tensor(weight_->master); }
+  Tensor get_bias() const { return bias_ ? Tensor(bias_->master) : Tensor(); }
 
   size_t input_size, output_size;
 
@@ -51,6 +63,7 @@ class ActivationLayer : public ModernLayer {
   std::string type_name() const override;
   std::string config_json() const override;
   ActivationType activation() const { return type_; }
+  ActivationType get_activation_type() const { return type_; }
 
  private:
   ActivationType type_;
@@ -67,6 +80,17 @@ class Conv2DLayer : public ModernLayer {
   std::string type_name() const override { return "Conv2D"; }
   std::string config_json() const override;
   Tensor forward_fused(const Tensor& input, bool relu);
+
+  // Accessors of the reference's conv2d_layer.h:40-52 (W [out, in, k, k]).
+  Tensor get_weights() const { return Tensor(weight_->master); }
+  Tensor get_bias() const { return bias_ ? Tensor(bias_->master) : Tensor(); }
+  size_t get_in_channels() const { return in_channels; }
+  size_t get_out_channels() const { return out_channels; }
+  size_t get_kernel_height() const { return kernel_size; }
+  size_t get_kernel_width() const { return kernel_size; }
+  std::vector<size_t> compute_output_shape(const std::vector<size_t>& input_shape) const {
+    return window_output_shape(input_shape, out_channels, kernel_size, stride, padding);
+  }
 
   size_t in_channels, out_channels, kernel_size, stride, padding;
 
@@ -85,6 +109,12 @@ class MaxPool2DLayer : public ModernLayer {
   std::unique_ptr<ModernLayer> clone() const override;
   std::string type_name() const override { return "MaxPool2D"; }
   std::string config_json() const override;
+  // Accessors of the reference's pooling_layers.h:34-38 (square windows).
+  size_t get_pool_height() const { return pool_size; }
+  size_t get_pool_width() const { return pool_size; }
+  std::vector<size_t> compute_output_shape(const std::vector<size_t>& input_shape) const {
+    return window_output_shape(input_shape, 0, pool_size, stride, 0);
+  }
   size_t pool_size, stride;
 
  private:
@@ -100,6 +130,11 @@ class AvgPool2DLayer : public ModernLayer {
   std::unique_ptr<ModernLayer> clone() const override;
   std::string type_name() const override { return "AvgPool2D"; }
   std::string config_json() const override;
+  size_t get_pool_height() const { return pool_size; }
+  size_t get_pool_width() const { return pool_size; }
+  std::vector<size_t> compute_output_shape(const std::vector<size_t>& input_shape) const {
+    return window_output_shape(input_shape, 0, pool_size, stride, 0);
+  }
   size_t pool_size, stride;
 
  private:
@@ -117,6 +152,17 @@ class BatchNormLayer : public ModernLayer {
   std::unique_ptr<ModernLayer> clone() const override;
   std::string type_name() const override { return two_d_ ? "BatchNorm2D" : "BatchNorm1D"; }
   std::string config_json() const override;
+  // Accessors of the reference's batch_norm_layers.h:39-46.  The getters
+  // return views; the setters copy into the existing tensors, which stay
+  // the model's packed views.
+  Tensor get_gamma() const { return Tensor(gamma_->master); }
+  Tensor get_beta() const { return Tensor(beta_->master); }
+  Tensor get_running_mean() const { return Tensor(running_mean); }
+  Tensor get_running_var() const { return Tensor(running_var); }
+  void set_gamma(const Tensor& g) { copy_into(gamma_->master, g, "gamma"); }
+  void set_beta(const Tensor& b) { copy_into(beta_->master, b, "beta"); }
+  void set_running_mean(const Tensor& m) { copy_into(running_mean, m, "running_mean"); }
+  void set_running_var(const Tensor& v) { copy_into(running_var, v, "running_var"); }
   size_t num_features;
   double momentum, eps;
   at::Tensor running_mean, running_var;
@@ -125,6 +171,7 @@ class BatchNormLayer : public ModernLayer {
   std::vector<std::pair<std::string, at::Tensor*>> buffers() override;
 
  private:
+  static void copy_into(at::Tensor& dst, const Tensor& src, const char* what);
   bool two_d_;
   Parameter* gamma_ = nullptr;
   Parameter* beta_ = nullptr;
@@ -142,6 +189,9 @@ class DropoutLayer : public ModernLayer {
   std::unique_ptr<ModernLayer> clone() const override;
   std::string type_name() const override { return "Dropout"; }
   std::string config_json() const override;
+  float get_dropout_rate() const { return rate; }
+  // Throws std::invalid_argument outside [0, 1).
+  void set_dropout_rate(float r);
   float rate;
 
  private:

@@ -36,6 +36,15 @@ class Optimizer {
   void set_lr(double lr) { set_learning_rate(lr); }
   double get_lr() const { return lr_; }
 
+  // Gradient clipping (the reference's optimizers.h:41-45), applied by
+  // step() / update() before the update: by norm, the gradients are scaled
+  // by min(1, max_norm / ||g||) with the norm over the model's whole
+  // gradient buffer; by value, every element is clamped to [min, max]
+  // (in place, so the model's gradient buffer holds the clamped values).
+  void set_grad_clip_norm(double max_norm);
+  void set_grad_clip_value(double min_val, double max_val);
+  void disable_grad_clipping();
+
   // One update of every parameter of `model` (advances the step counter).
   void step(Sequential& model);
   // Reference interface: update one layer's parameters.
@@ -56,10 +65,13 @@ class Optimizer {
   const State* find_state(const Sequential& model) const;
   void advance(State& st);
   void update_range(State& st, at::Tensor& master, at::Tensor& grad, int64_t start, int64_t end);
+  void prepare_grads(State& st, at::Tensor& grad);
 
   int kind_;
   double lr_, beta1_, beta2_, eps_, momentum_, alpha_, weight_decay_;
   bool bias_correction_ = true;
+  bool use_clip_norm_ = false, use_clip_value_ = false;
+  double clip_norm_ = 0.0, clip_min_ = 0.0, clip_max_ = 0.0;
   std::map<const void*, std::unique_ptr<State>> states_;
 };
 

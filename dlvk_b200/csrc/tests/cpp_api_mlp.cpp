@@ -14,6 +14,7 @@
 #include <cmath>
 #include <cstdio>
 #include <fstream>
+#include <stdexcept>
 #include <string>
 
 #include "dlvk/dlvk.h"
@@ -118,6 +119,76 @@ int main(int argc, char** argv) {
     auto pred = trainer.predict(dlvk::Tensor(xs.narrow(0, 0, 10)));
     if (pred.shape() != std::vector<size_t>({10, 2})) return fail("predict shape");
     std::printf("trainer final loss %.4f acc %.3f\n", hist.back().loss, ev.accuracy);
+  }
+  // Reference accessor spellings: layer getters / setters, output shapes,
+  // optimizer clipping by value and by norm.
+  {
+    dlvk::Sequential m4(device, 5);
+    m4.add_conv2d(1, 4, 3, 1, 1);
+    m4.add_batchnorm2d(4);
+    m4.add_maxpool2d(2);
+    m4.add_flatten();
+    m4.add_dense(4 * 4 * 4, 3);
+    m4.add_dropout(0.25f);
+    m4.build();
+    auto* conv = dynamic_cast<dlvk::Conv2DLayer*>(&m4[0]);
+    auto* bn = dynamic_cast<dlvk::BatchNormLayer*>(&m4[1]);
+    auto* pool = dynamic_cast<dlvk::MaxPool2DLayer*>(&m4[2]);
+    auto* dense = dynamic_cast<dlvk::DenseLayer*>(&m4[4]);
+    auto* drop = dynamic_cast<dlvk::DropoutLayer*>(&m4[5]);
+    if (!conv || !bn || !pool || !dense || !drop) return fail("layer types");
+    if (conv->get_weights().shape() != std::vector<size_t>({4, 1, 3, 3}) || conv->get_in_channels() != 1 ||
+        conv->get_out_channels() != 4 || conv->get_kernel_height() != 3 || conv->get_kernel_width() != 3)
+      return fail("Conv2D accessors");
+    if (conv->compute_output_shape({2, 1, 8, 8}) != std::vector<size_t>({2, 4, 8, 8}) ||
+        pool->compute_output_shape({2, 4, 8, 8}) != std::vector<size_t>({2, 4, 4, 4}) ||
+        pool->get_pool_height() != 2 || pool->get_pool_width() != 2)
+      return fail("compute_output_shape");
+    bool threw = false;
+    try {
+      pool->compute_output_shape({1, 1});
+    } catch (const std::invalid_argument&) {
+      threw = true;
+    }
+    if (!threw) return fail("compute_output_shape accepted a 2-D shape");
+    if (drop->get_dropout_rate() != 0.25f) return fail("get_dropout_rate");
+    drop->set_dropout_rate(0.5f);
+    if (drop->get_dropout_rate() != 0.5f) return fail("set_dropout_rate");
+    bn->set_running_mean(dlvk::Tensor(at::full({4}, 0.5f)));
+    if (bn->get_running_mean().to_vector() != std::vector<float>(4, 0.5f)) return fail("BatchNorm running mean");
+    if (bn->get_gamma().to_vector() != std::vector<float>(4, 1.f)) return fail("BatchNorm gamma");
+    // get_weights() / get_bias() are views of the model's packed weights.
+    dense->get_weights().data().zero_();
+    dense->get_bias().data().fill_(2.f);
+    m4.set_training(false);
+    auto y4 = m4.forward(dlvk::Tensor(at::rand({2, 1, 8, 8}, g))).to_vector();
+    if (y4 != std::vector<float>(6, 2.f)) return fail("Dense get_weights is not a view");
+    auto* relu = dynamic_cast<dlvk::ActivationLayer*>(&model[1]);
+    if (!relu || relu->get_activation_type() != dlvk::ActivationType::ReLU) return fail("get_activation_type");
+
+    dlvk::Sequential m5(device, 6);
+    m5.add_dense(4, 2);
+    m5.build();
+    const int64_t n = m5.flat_numel();
+    at::Tensor gv = at::linspace(-3.0, 3.0, n).to(m5.master().device());
+    dlvk::SGD sgd(1.0);
+    sgd.set_grad_clip_value(-1.0, 0.5);
+    at::Tensor before = m5.master().clone();
+    m5.grad().copy_(gv);
+    sgd.step(m5);
+    if (!at::allclose(m5.master(), before - gv.clamp(-1.0, 0.5))) return fail("clip by value");
+    sgd.disable_grad_clipping();
+    sgd.set_grad_clip_norm(1.0);
+    before = m5.master().clone();
+    m5.grad().copy_(gv);
+    sgd.step(m5);
+    const float moved = (before - m5.master()).norm().item<float>();
+    if (std::fabs(moved - 1.f) > 1e-4f) return fail("clip by norm moved " + std::to_string(moved));
+    sgd.disable_grad_clipping();
+    before = m5.master().clone();
+    m5.grad().copy_(gv);
+    sgd.step(m5);
+    if (!at::allclose(m5.master(), before - gv)) return fail("disable_grad_clipping");
   }
   std::printf("OK\n");
   return 0;

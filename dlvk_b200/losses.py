@@ -117,3 +117,54 @@ class BinaryCrossEntropyLoss(LossFunction):
 # Reference spellings.
 MSELoss = MeanSquaredError
 BCELoss = BinaryCrossEntropyLoss
+
+
+class LossOpsGPU:
+    """The reference's per-op loss entry points (include/dlvk/loss/loss_ops_gpu.h:10-60)
+    over this library's loss kernels (softmax_loss.cu `pointwise_loss`;
+    cross-entropy on probabilities as CrossEntropyLoss).  Each method returns
+    its result tensor; the reference wrote it through an out-parameter and
+    returned a success flag.  The semantics are the reference's CPU ones:
+
+      mse_forward                    mean((p - t)^2)
+      mse_backward                   2 (p - t) / N
+      cross_entropy_forward          -sum t log(p + 1e-8) / B    (p: probabilities)
+      cross_entropy_backward         -t / (p + 1e-8) / B
+      binary_cross_entropy_forward   mean of -(t log p + (1 - t) log(1 - p)), p clamped to [eps, 1 - eps]
+      binary_cross_entropy_backward  (p - t) / (p (1 - p)) / N with the same clamp
+
+    The kernels clamp BCE probabilities at 1e-7; a larger `epsilon` clamps
+    the predictions first, a smaller one is rejected."""
+
+    def __init__(self, device=None):
+        self.device = device
+
+    def initialize(self) -> bool:
+        return True
+
+    def mse_forward(self, predictions, targets):
+        return MeanSquaredError().forward(predictions, targets)
+
+    def mse_backward(self, predictions, targets):
+        return MeanSquaredError().backward(predictions, targets)
+
+    def cross_entropy_forward(self, predictions, targets):
+        return CrossEntropyLoss().forward(predictions, targets)
+
+    def cross_entropy_backward(self, predictions, targets):
+        return CrossEntropyLoss().backward(predictions, targets)
+
+    @staticmethod
+    def _clamped(predictions, epsilon: float):
+        p = _unwrap(predictions)
+        if epsilon < 1e-7:
+            raise ValueError(f"epsilon {epsilon} is below the kernel's 1e-7 probability clamp")
+        if epsilon > 1e-7:
+            p = K.unary(p, K.UN_CLAMP, float(epsilon), 1.0 - float(epsilon))
+        return p
+
+    def binary_cross_entropy_forward(self, predictions, targets, epsilon: float = 1e-7):
+        return BinaryCrossEntropyLoss().forward(self._clamped(predictions, epsilon), targets)
+
+    def binary_cross_entropy_backward(self, predictions, targets, epsilon: float = 1e-7):
+        return BinaryCrossEntropyLoss().backward(self._clamped(predictions, epsilon), targets)

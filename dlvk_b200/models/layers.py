@@ -235,6 +235,23 @@ class ModernLayer:
         for s in stores.values():
             s.sync_value()
 
+    def is_training(self) -> bool:
+        return self.training
+
+    def _set_tensor(self, dst: torch.Tensor, src, what: str) -> None:
+        """Copy `src` (a tensor or array of dst's element count) into a
+        parameter master or a buffer in place, so a packed store keeps its
+        views, then refresh the compute-dtype mirrors."""
+        from ..tensor import Tensor as FacadeTensor
+
+        if isinstance(src, FacadeTensor):
+            src = src.data
+        src = torch.as_tensor(src)
+        if src.numel() != dst.numel():
+            raise ValueError(f"{self.type_name}.{what}: expected {dst.numel()} elements, got {src.numel()}")
+        dst.copy_(src.detach().reshape(dst.shape).to(dst.device, dst.dtype))
+        self._sync_values()
+
     def summary_line(self) -> str:
         info = self.get_layer_info()
         return f"{info.type:<24}{info.output_shape_str:<24}{info.parameter_count:>12}"
@@ -264,6 +281,22 @@ class DenseLayer(ModernLayer):
         self.activation = activation
         self._act = K.ACT_BY_NAME[activation]
 
+    # Accessors of include/dlvk/layers/dense_layer.h:31-32 (fp32 masters;
+    # W is [in, out]).  The setters copy in place.
+    def get_weights(self) -> torch.Tensor:
+        return self.weight.master
+
+    def get_bias(self) -> Optional[torch.Tensor]:
+        return self.bias.master if self.bias is not None else None
+
+    def set_weights(self, w) -> None:
+        self._set_tensor(self.weight.master, w, "weights")
+
+    def set_bias(self, b) -> None:
+        if self.bias is None:
+            raise ValueError("Dense layer built with use_bias=False has no bias")
+        self._set_tensor(self.bias.master, b, "bias")
+
     def _forward(self, x, act=None, residual=None, mask_input=False, defer_relu=False):
         a = self._act if act is None else act
         if x.dim() > 2 and x.shape[-1] != self.input_size:
@@ -290,6 +323,39 @@ class Conv2DLayer(ModernLayer):
         self.bias = self._param("bias", torch.zeros(self.out_channels), decay=False) if use_bias else None
         self.relu = activation == "relu"
 
+    # Accessors of include/dlvk/layers/conv2d_layer.h:40-52; W is
+    # [out_channels, in_channels, kernel, kernel].
+    def get_weights(self) -> torch.Tensor:
+        return self.weight.master
+
+    def get_bias(self) -> Optional[torch.Tensor]:
+        return self.bias.master if self.bias is not None else None
+
+    def set_weights(self, w) -> None:
+        self._set_tensor(self.weight.master, w, "weights")
+
+    def set_bias(self, b) -> None:
+        if self.bias is None:
+            raise ValueError("Conv2D layer built with use_bias=False has no bias")
+        self._set_tensor(self.bias.master, b, "bias")
+
+    def get_in_channels(self) -> int:
+        return self.in_channels
+
+    def get_out_channels(self) -> int:
+        return self.out_channels
+
+    def get_kernel_height(self) -> int:
+        return self.kernel_size
+
+    def get_kernel_width(self) -> int:
+        return self.kernel_size
+
+    def compute_output_shape(self, input_shape) -> List[int]:
+        """[N, C_out, H_out, W_out] for an [N, C_in, H, W] input (or the
+        [C_in, H, W] of one image)."""
+        return _window_out_shape(input_shape, self.out_channels, self.kernel_size, self.stride, self.padding)
+
     def _forward(self, x, relu=None):
         if x.dtype != self.compute_dtype:
             x = x.to(self.compute_dtype)
@@ -297,7 +363,36 @@ class Conv2DLayer(ModernLayer):
                                  self.relu if relu is None else relu)
 
 
-class MaxPool2DLayer(ModernLayer):
+def _window_out_shape(input_shape, channels: Optional[int], k: int, stride: int, pad: int) -> List[int]:
+    """Output shape of a k x k window op over NCHW (or CHW) input:
+    (H + 2 pad - k) // stride + 1 per spatial dimension."""
+    shape = [int(d) for d in input_shape]
+    if len(shape) not in (3, 4):
+        raise ValueError(f"expected an NCHW or CHW shape, got {shape}")
+    h, w = shape[-2:]
+    ho, wo = (h + 2 * pad - k) // stride + 1, (w + 2 * pad - k) // stride + 1
+    if ho <= 0 or wo <= 0:
+        raise ValueError(f"window {k} with stride {stride} and padding {pad} does not fit {h}x{w}")
+    return shape[:-3] + [shape[-3] if channels is None else channels, ho, wo]
+
+
+class _PoolBase(ModernLayer):
+    """Accessors of include/dlvk/layers/pooling_layers.h:34-38 (square
+    windows, so height and width are the same)."""
+
+    padding = 0
+
+    def get_pool_height(self) -> int:
+        return self.pool_size
+
+    def get_pool_width(self) -> int:
+        return self.pool_size
+
+    def compute_output_shape(self, input_shape) -> List[int]:
+        return _window_out_shape(input_shape, None, self.pool_size, self.stride, self.padding)
+
+
+class MaxPool2DLayer(_PoolBase):
     type_name = "MaxPool2D"
 
     def __init__(self, pool_size: int, stride: int = 0):
@@ -309,7 +404,7 @@ class MaxPool2DLayer(ModernLayer):
         return Fn.MaxPoolFn.apply(x, self.pool_size, self.stride)
 
 
-class AvgPool2DLayer(ModernLayer):
+class AvgPool2DLayer(_PoolBase):
     type_name = "AvgPool2D"
 
     def __init__(self, pool_size: int, stride: int = 0, padding: int = 0):
@@ -348,6 +443,36 @@ class _BatchNormBase(ModernLayer):
     def _buffers(self):
         return [("running_mean", self.running_mean), ("running_var", self.running_var)]
 
+    # Accessors of include/dlvk/layers/batch_norm_layers.h:39-46; the
+    # setters copy into the existing tensors (packed views stay valid).
+    def get_gamma(self) -> Optional[torch.Tensor]:
+        return self.gamma.master if self.gamma is not None else None
+
+    def get_beta(self) -> Optional[torch.Tensor]:
+        return self.beta.master if self.beta is not None else None
+
+    def get_running_mean(self) -> torch.Tensor:
+        return self.running_mean
+
+    def get_running_var(self) -> torch.Tensor:
+        return self.running_var
+
+    def set_gamma(self, g) -> None:
+        if self.gamma is None:
+            raise ValueError("BatchNorm built with affine=False has no gamma")
+        self._set_tensor(self.gamma.master, g, "gamma")
+
+    def set_beta(self, b) -> None:
+        if self.beta is None:
+            raise ValueError("BatchNorm built with affine=False has no beta")
+        self._set_tensor(self.beta.master, b, "beta")
+
+    def set_running_mean(self, m) -> None:
+        self._set_tensor(self.running_mean, m, "running_mean")
+
+    def set_running_var(self, v) -> None:
+        self._set_tensor(self.running_var, v, "running_var")
+
     def _forward(self, x, relu=False, p=0.0, stream=None):
         cfg = dict(momentum=self.momentum, eps=self.eps, training=self.training, relu=relu, p=p if self.training else 0.0,
                    stream=stream if stream is not None else self.dropout_stream, seed=self.device_ctx.seed,
@@ -373,6 +498,14 @@ class DropoutLayer(ModernLayer):
         self.rate = float(dropout_rate)
         self.stream = 0
 
+    def get_dropout_rate(self) -> float:
+        return self.rate
+
+    def set_dropout_rate(self, rate: float) -> None:
+        if not 0.0 <= float(rate) < 1.0:
+            raise ValueError(f"dropout rate must be in [0, 1), got {rate}")
+        self.rate = float(rate)
+
     def _on_bind(self):
         if not self.stream:
             self.stream = self.device_ctx.next_stream_id()
@@ -392,6 +525,9 @@ class ActivationLayer(ModernLayer):
             activation = ActivationType(activation.lower())
         self.activation = activation
         self.type_name = activation.name
+
+    def get_activation_type(self) -> ActivationType:
+        return self.activation
 
     def _forward(self, x):
         a = self.activation

@@ -59,7 +59,9 @@ class Optimizer:
         self.decoupled_wd = bool(decoupled_wd)
         self.clip_norm: Optional[float] = None
         self.clip_value: Optional[float] = None
+        self.clip_range: Optional[tuple] = None  # (min, max) from set_grad_clip_value
         self._states: Dict[int, _State] = {}
+        self._tensor_stores: Dict[tuple, "_TensorStore"] = {}
         self._scaler = None  # a GradientScaler attached to this optimizer's hyper blocks
 
     # ---------------------------------------------------------------- API
@@ -76,6 +78,73 @@ class Optimizer:
         """Clip by global norm (per optimizer step) and/or by value."""
         self.clip_norm = max_norm
         self.clip_value = clip_value
+        self.clip_range = None
+
+    # Reference spellings (include/dlvk/optimizers/optimizers.h:20-45).
+    def set_lr(self, lr: float) -> None:
+        self.set_learning_rate(lr)
+
+    def get_lr(self) -> float:
+        return self.lr
+
+    def set_grad_clip_norm(self, max_norm: float) -> None:
+        """Scale the gradients of each update by min(1, max_norm / ||g||)."""
+        self.clip_norm = float(max_norm)
+
+    def set_grad_clip_value(self, min_val: float, max_val: float) -> None:
+        """Clamp every gradient element to [min_val, max_val] before the update."""
+        if float(min_val) > float(max_val):
+            raise ValueError(f"clip range [{min_val}, {max_val}] is empty")
+        self.clip_value = None
+        self.clip_range = (float(min_val), float(max_val))
+
+    def disable_grad_clipping(self) -> None:
+        self.clip_norm = self.clip_value = self.clip_range = None
+
+    def _clip_bounds(self) -> Optional[tuple]:
+        if self.clip_range is not None:
+            return self.clip_range
+        if self.clip_value is not None:
+            return (-self.clip_value, self.clip_value)
+        return None
+
+    def zero_gradients(self) -> None:
+        """Zero the gradient buffers of every store and tensor this optimizer
+        has updated, and mark the packed parameters so the next backward
+        overwrites instead of accumulating."""
+        for st in self._states.values():
+            zero = getattr(st.store, "zero_grad", None)
+            if zero is not None:
+                zero(set_to_zero=True)
+            elif st.store.grad is not None:
+                st.store.grad.zero_()
+
+    def update_parameter(self, parameter: torch.Tensor, gradient: torch.Tensor) -> None:
+        """Apply one update of this optimizer's rule to a standalone tensor
+        in place (reference Optimizer::update_parameter,
+        include/dlvk/optimizers/optimizers.h:24-25).  The optimizer state
+        (momentum, m / v, step count) is kept per tensor storage, so
+        repeated calls on the same tensor continue one trajectory.  An
+        fp32 master copy is kept for a bf16 / fp16 tensor, which receives
+        the rounded result.  The gradient is not modified."""
+        from .tensor import Tensor as FacadeTensor
+
+        if isinstance(parameter, FacadeTensor):
+            parameter = parameter.data
+        if isinstance(gradient, FacadeTensor):
+            gradient = gradient.data
+        if not parameter.is_contiguous():
+            raise ValueError("update_parameter needs a contiguous parameter tensor")
+        if gradient.numel() != parameter.numel():
+            raise ValueError(f"gradient has {gradient.numel()} elements, parameter {parameter.numel()}")
+        key = (parameter.data_ptr(), parameter.numel(), parameter.dtype, str(parameter.device))
+        ts = self._tensor_stores.get(key)
+        if ts is None:
+            ts = _TensorStore(parameter)
+            self._tensor_stores[key] = ts
+        ts.grad = gradient.detach().reshape(-1).to(parameter.device, torch.float32, copy=True)
+        self.step(ts)
+        ts.grad = None
 
     def state(self, store) -> _State:
         st = self._states.get(id(store))
@@ -99,16 +168,17 @@ class Optimizer:
         """Global-norm clipping coefficient and value clipping (device side)."""
         st = self.state(store)
         scaled = self._scaler is not None and self._scaler.enabled
-        if scaled and self.clip_value is not None:
+        if scaled and self._clip_bounds() is not None:
             raise ValueError("value clipping is not defined on loss-scaled gradients; use clip_norm")
         if scaled:
             return  # the scaler computed the overflow flag and the clip coefficient
-        if self.clip_value is not None:
+        bounds = self._clip_bounds()
+        if bounds is not None:
             g = store.grad
             if st.cuda:
-                K.N().unary(g, K.UN_CLAMP, -self.clip_value, self.clip_value, out=g)
+                K.N().unary(g, K.UN_CLAMP, bounds[0], bounds[1], out=g)
             else:
-                g.clamp_(-self.clip_value, self.clip_value)
+                g.clamp_(bounds[0], bounds[1])
         if self.clip_norm is not None:
             if st.cuda:
                 if st.scratch is None:
@@ -212,6 +282,23 @@ class Optimizer:
             if self.bias_correction and st.step > 0:
                 set_field(st.hyper, "bc1", 1.0 / (1 - self.beta1 ** st.step))
                 set_field(st.hyper, "bc2", 1.0 / (1 - self.beta2 ** st.step))
+
+
+class _TensorStore:
+    """A one-tensor stand-in for a ParamStore, used by update_parameter:
+    `master` is the fp32 flat view being updated (the tensor itself when it
+    is fp32), `value` the caller's lower-precision tensor when there is one."""
+
+    def __init__(self, parameter: torch.Tensor):
+        self.device = parameter.device
+        self.numel = parameter.numel()
+        flat = parameter.detach().view(-1)
+        if parameter.dtype == torch.float32:
+            self.master = self.value = flat
+        else:
+            self.master = flat.float()
+            self.value = flat
+        self.grad = None
 
 
 class SGD(Optimizer):

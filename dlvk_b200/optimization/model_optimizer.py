@@ -301,6 +301,16 @@ class ModelOptimizer:
 
         return ModelExportManager().export_model(model, path, ModelFormat.ONNX, input_shape=input_shape)
 
+    @staticmethod
+    def import_from_onnx(path: str, device=None) -> Sequential:
+        """Rebuild a model from an ONNX file written by export_to_onnx
+        (architecture from the file's metadata, weights from its
+        initializers); reference include/dlvk/optimization/model_optimizer.h:149-152."""
+        from ..export import ModelExportManager, ModelFormat
+
+        model, _ = ModelExportManager().import_model(path, ModelFormat.ONNX, device)
+        return model
+
     # ------------------------------------------------------------ benchmarking
     def benchmark_model(self, model, input_shape, iterations: int = 50, warmup: int = 5, device=None) -> dict:
         """Device-timed latency (CUDA events) and throughput of model.forward."""

@@ -121,8 +121,9 @@ class FusedAllReduceOptimizer:
     def __init__(self, store, optimizer, world: int, rank: int, group=None,
                  one_shot_bytes: Optional[int] = None, ctas: Optional[int] = None, algo: Optional[str] = None,
                  recv_factor: Optional[float] = None):
-        if optimizer.clip_norm is not None:
-            raise ValueError("global-norm clipping is not supported with the fused all-reduce optimizer")
+        if optimizer.clip_norm is not None or optimizer._clip_bounds() is not None:
+            raise ValueError("gradient clipping (by norm or by value) is not supported with the fused all-reduce "
+                             "optimizer")
         self.C = _ext.C()
         self.store, self.opt = store, optimizer
         self.world, self.rank, self.group = world, rank, group

@@ -21,3 +21,9 @@ from . import persistence
 from .persistence import (CheckpointData, ModelCheckpointCallback, ModelSerializer, ModelVersioning,
                           SerializationFormat)
 from .persistence import ModelCheckpoint as CheckpointManager
+from .persistence import create_checkpoint_callback, create_versioning_system
+from types import SimpleNamespace as _NS
+
+# The reference's namespace persistence_factory (model_persistence.h:362-381).
+persistence_factory = _NS(create_checkpoint_callback=create_checkpoint_callback,
+                          create_versioning_system=create_versioning_system)

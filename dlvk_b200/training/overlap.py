@@ -37,7 +37,7 @@ class _Bucket:
 
 class OverlappedUpdate:
     def __init__(self, model, optimizer, bucket_mb: float = DEFAULT_BUCKET_MB, ctas: Optional[int] = None):
-        if optimizer.clip_norm is not None or getattr(optimizer, "clip_value", None) is not None:
+        if optimizer.clip_norm is not None or optimizer._clip_bounds() is not None:
             raise ValueError("gradient clipping needs every gradient before the first update")
         self.model = model.build()
         self.opt = optimizer

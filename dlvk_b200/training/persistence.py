@@ -133,10 +133,7 @@ class ModelSerializer:
 
             return ModelExportManager().export_model(model, filepath, ModelFormat.HDF5)
         if self.format is SerializationFormat.NUMPY_NPZ:
-            import numpy as np
-
-            np.savez(filepath, **{n: t.detach().float().cpu().numpy() for n, t in model.state_tensors()})
-            return True
+            return self.export_to_numpy(model, filepath)
         return self.save_binary(model, filepath, metadata)
 
     def load(self, filepath: str, device=None):
@@ -147,6 +144,78 @@ class ModelSerializer:
     @staticmethod
     def serialize_metadata(metadata: ModelMetadata) -> str:
         return json.dumps(asdict(metadata))
+
+    # Static entry points of include/dlvk/training/model_persistence.h:203-239.
+    @staticmethod
+    def save_model(model, filepath: str, format: SerializationFormat = SerializationFormat.DLVK_BINARY,
+                   metadata: Optional[ModelMetadata] = None) -> bool:
+        return ModelSerializer(format).save(model, filepath, metadata)
+
+    @staticmethod
+    def load_model(filepath: str, format: SerializationFormat = SerializationFormat.DLVK_BINARY, device=None):
+        return ModelSerializer(format).load(filepath, device)
+
+    @staticmethod
+    def save_weights(model, filepath: str, format: SerializationFormat = SerializationFormat.DLVK_BINARY) -> bool:
+        """Weights only, into an existing architecture's layout: `.dlvk`
+        binary, JSON (the same document save_json writes) or NumPy `.npz`."""
+        if format is SerializationFormat.NUMPY_NPZ:
+            return ModelSerializer.export_to_numpy(model, filepath)
+        if format is SerializationFormat.DLVK_JSON:
+            return ModelSerializer(format).save_json(model, filepath)
+        if format is not SerializationFormat.DLVK_BINARY:
+            raise ValueError(f"save_weights supports DLVK_BINARY, DLVK_JSON and NUMPY_NPZ, not {format.name}")
+        model.save_weights(filepath)
+        return True
+
+    @staticmethod
+    def load_weights(model, filepath: str, format: SerializationFormat = SerializationFormat.DLVK_BINARY) -> bool:
+        """Loads weights written by save_weights into `model` (same layer
+        list); every tensor's shape must match."""
+        model.build()
+        if format is SerializationFormat.DLVK_BINARY:
+            model.load_weights(filepath)
+            return True
+        if format is SerializationFormat.DLVK_JSON:
+            with open(filepath) as f:
+                w = json.load(f)["weights"]
+            src = {n: torch.tensor(e["data"], dtype=torch.float32).reshape(e["shape"]) for n, e in w.items()}
+        elif format is SerializationFormat.NUMPY_NPZ:
+            import numpy as np
+
+            with np.load(filepath) as z:
+                src = {n: torch.from_numpy(z[n].astype("float32")) for n in z.files}
+        else:
+            raise ValueError(f"load_weights supports DLVK_BINARY, DLVK_JSON and NUMPY_NPZ, not {format.name}")
+        for n, t in model.state_tensors():
+            if n not in src:
+                raise ValueError(f"{filepath}: no tensor named {n}")
+            if tuple(src[n].shape) != tuple(t.shape):
+                raise ValueError(f"{filepath}: {n} has shape {tuple(src[n].shape)}, the model {tuple(t.shape)}")
+            t.copy_(src[n].to(t.device, t.dtype))
+        model.store.sync_value()
+        return True
+
+    @staticmethod
+    def export_to_onnx(model, filepath: str, input_shapes=None) -> bool:
+        """ONNX graph with the weights as initializers; `input_shapes` is a
+        list with one input shape (the model has one input)."""
+        from ..export import ModelExportManager, ModelFormat
+
+        shape = list(input_shapes[0]) if input_shapes else None
+        return ModelExportManager().export_model(model, filepath, ModelFormat.ONNX, input_shape=shape)
+
+    @staticmethod
+    def export_to_numpy(model, filepath: str) -> bool:
+        """Every parameter and buffer as an fp32 array in one `.npz`, keyed
+        by the names state_tensors() gives."""
+        import numpy as np
+
+        model.build()
+        tmp = filepath + ".tmp.npz"
+        np.savez(tmp, **{n: t.detach().float().cpu().numpy() for n, t in model.state_tensors()})
+        os.replace(tmp, filepath)
+        return True
 
     # CheckpointData <-> file
     @staticmethod
@@ -361,3 +430,14 @@ class ModelCheckpointCallback(TrainingCallback):
 
     def get_checkpoint_manager(self) -> ModelCheckpoint:
         return self.manager
+
+
+# Factory functions of include/dlvk/training/model_persistence.h:362-381
+# (namespace persistence_factory).
+def create_checkpoint_callback(model, checkpoint_dir: str = "./checkpoints", model_name: str = "model",
+                               optimizer=None) -> ModelCheckpointCallback:
+    return ModelCheckpointCallback(model, checkpoint_dir, model_name, optimizer)
+
+
+def create_versioning_system(experiment_dir: str = "./experiments") -> ModelVersioning:
+    return ModelVersioning(experiment_dir)

@@ -45,7 +45,7 @@ class TrainStep:
         if overlap_update is None:
             overlap_update = os.environ.get("DLVK_OVERLAP_UPDATE", "0") != "0"
         if (dp is None and overlap_update and model.dev.is_cuda and scaler is None and regularizer is None
-                and getattr(optimizer, "clip_norm", None) is None and getattr(optimizer, "clip_value", None) is None):
+                and optimizer.clip_norm is None and optimizer._clip_bounds() is None):
             from .overlap import OverlappedUpdate
 
             dp = OverlappedUpdate(self.model, optimizer)

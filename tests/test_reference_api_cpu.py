@@ -1,0 +1,249 @@
+"""CPU tests of the reference's public accessor and helper spellings: layer
+get_/set_ accessors and output shapes, optimizer clipping setters,
+update_parameter and zero_gradients, ModelSerializer's static entry points,
+the persistence factory functions, ONNX import and LossOpsGPU.  Each result
+is checked against plain PyTorch math or a round trip."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+import dlvk_b200 as dl
+from dlvk_b200.models import layers as L
+from dlvk_b200.optimization.model_optimizer import ModelOptimizer
+from dlvk_b200.training import SerializationFormat, persistence_factory
+from dlvk_b200.training.persistence import ModelCheckpointCallback, ModelSerializer, ModelVersioning
+
+
+def _mlp(seed):
+    m = dl.Sequential("cpu", seed=seed)
+    m.add_dense(6, 5)
+    m.add_relu()
+    m.add_dense(5, 3)
+    m.add_softmax()
+    return m.build()
+
+
+def test_dense_get_set_weights_feed_the_forward():
+    m = _mlp(0)
+    d = m[0]
+    assert d.get_weights().shape == (6, 5) and d.get_bias().shape == (5,)
+    w = torch.randn(6, 5)
+    b = torch.randn(5)
+    d.set_weights(w)
+    d.set_bias(b)
+    assert torch.equal(d.get_weights(), w) and torch.equal(d.get_bias(), b)
+    # the packed store sees the new values (set_* copies in place)
+    assert torch.equal(m.store.master[d.weight.offset:d.weight.offset + 30].reshape(6, 5), w)
+    x = torch.randn(4, 6)
+    h = torch.relu(x @ w + b)
+    ref = torch.softmax(h @ m[2].get_weights() + m[2].get_bias(), -1)
+    torch.testing.assert_close(m.forward(x), ref, rtol=1e-5, atol=1e-6)
+    with pytest.raises(ValueError):
+        d.set_weights(torch.zeros(7))
+    nb = L.DenseLayer(3, 2, use_bias=False)
+    assert nb.get_bias() is None
+    with pytest.raises(ValueError):
+        nb.set_bias(torch.zeros(2))
+
+
+@pytest.mark.parametrize("k,s,p,hw", [(3, 1, 1, 8), (3, 2, 0, 9), (5, 2, 2, 11)])
+def test_conv_and_pool_output_shapes_match_forward(k, s, p, hw):
+    conv = L.Conv2DLayer(2, 4, k, s, p)
+    x = torch.randn(3, 2, hw, hw)
+    assert conv.compute_output_shape(list(x.shape)) == list(conv.forward(x).shape)
+    assert conv.compute_output_shape([2, hw, hw]) == list(conv.forward(x).shape)[1:]
+    assert (conv.get_in_channels(), conv.get_out_channels()) == (2, 4)
+    assert conv.get_kernel_height() == conv.get_kernel_width() == k
+    assert conv.get_weights().shape == (4, 2, k, k)
+    w, b = torch.randn(4, 2, k, k), torch.randn(4)
+    conv.set_weights(w)
+    conv.set_bias(b)
+    torch.testing.assert_close(conv.forward(x), F.conv2d(x, w, b, s, p), rtol=1e-5, atol=1e-5)
+    for pool in (L.MaxPool2DLayer(2, 2), L.AvgPool2DLayer(3, 2, 1)):
+        assert pool.compute_output_shape(list(x.shape)) == list(pool.forward(x).shape)
+        assert pool.get_pool_height() == pool.get_pool_width() == pool.pool_size
+    with pytest.raises(ValueError):
+        L.MaxPool2DLayer(4, 4).compute_output_shape([1, 1, 2, 2])
+
+
+def test_batchnorm_accessors_drive_eval_forward():
+    bn = L.BatchNorm1DLayer(4)
+    g, b = torch.rand(4) + 0.5, torch.randn(4)
+    rm, rv = torch.randn(4), torch.rand(4) + 0.1
+    bn.set_gamma(g)
+    bn.set_beta(b)
+    bn.set_running_mean(rm)
+    bn.set_running_var(rv)
+    for get, want in ((bn.get_gamma, g), (bn.get_beta, b), (bn.get_running_mean, rm), (bn.get_running_var, rv)):
+        assert torch.equal(get(), want)
+    bn.set_training(False)
+    assert not bn.is_training()
+    x = torch.randn(8, 4)
+    torch.testing.assert_close(bn.forward(x), (x - rm) / torch.sqrt(rv + bn.eps) * g + b, rtol=1e-5, atol=1e-5)
+    with pytest.raises(ValueError):
+        L.BatchNorm1DLayer(4, affine=False).set_gamma(g)
+
+
+def test_dropout_and_activation_accessors():
+    d = L.DropoutLayer(0.25)
+    assert d.get_dropout_rate() == 0.25
+    d.set_dropout_rate(0.5)
+    assert d.get_dropout_rate() == 0.5
+    with pytest.raises(ValueError):
+        d.set_dropout_rate(1.0)
+    d.set_dropout_rate(0.0)
+    x = torch.randn(64)
+    assert torch.equal(d.forward(x), x)
+    assert L.ActivationLayer("tanh").get_activation_type() == L.ActivationType.Tanh
+
+
+def _sgd_ref(p, grads, lr, mu):
+    p, v = p.clone(), torch.zeros_like(p)
+    for g in grads:
+        v = mu * v + g
+        p = p - lr * v
+    return p
+
+
+def test_update_parameter_keeps_per_tensor_state():
+    torch.manual_seed(0)
+    p0 = torch.randn(10)
+    grads = [torch.randn(10) for _ in range(3)]
+    p = p0.clone()
+    opt = dl.SGD(0.1, 0.9)
+    for g in grads:
+        g_before = g.clone()
+        opt.update_parameter(p, g)
+        assert torch.equal(g, g_before)  # the caller's gradient is not clipped or scaled in place
+    torch.testing.assert_close(p, _sgd_ref(p0, grads, 0.1, 0.9), rtol=1e-6, atol=1e-7)
+
+    # Adam with bias correction against torch.optim.Adam
+    q = torch.nn.Parameter(p0.clone())
+    ref = torch.optim.Adam([q], lr=1e-2, betas=(0.9, 0.999), eps=1e-8)
+    mine = p0.clone()
+    adam = dl.Adam(1e-2)
+    for g in grads:
+        q.grad = g.clone()
+        ref.step()
+        adam.update_parameter(mine, g)
+    torch.testing.assert_close(mine, q.detach(), rtol=1e-5, atol=1e-6)
+
+
+def test_update_parameter_bf16_tensor_keeps_fp32_master():
+    p0 = torch.randn(32)
+    p = p0.bfloat16()
+    opt = dl.SGD(1e-3)
+    g = torch.full((32,), 1.0)
+    for _ in range(4):
+        opt.update_parameter(p, g)
+    # four steps of 1e-3 accumulate in the fp32 master before rounding
+    torch.testing.assert_close(p.float(), (p0.bfloat16().float() - 4e-3).bfloat16().float(), rtol=0, atol=0)
+
+
+def test_gradient_clipping_setters():
+    g = torch.tensor([-3.0, -0.5, 0.25, 2.0])
+    p = torch.zeros(4)
+    opt = dl.SGD(1.0)
+    opt.set_grad_clip_value(-1.0, 0.5)
+    opt.update_parameter(p, g)
+    torch.testing.assert_close(p, -g.clamp(-1.0, 0.5))
+    with pytest.raises(ValueError):
+        opt.set_grad_clip_value(1.0, -1.0)
+    opt.disable_grad_clipping()
+    opt.set_grad_clip_norm(1.0)
+    p = torch.zeros(4)
+    opt.update_parameter(p, g)
+    torch.testing.assert_close(p.norm(), torch.tensor(1.0), rtol=1e-4, atol=1e-5)
+    opt.disable_grad_clipping()
+    p = torch.zeros(4)
+    opt.update_parameter(p, g)
+    torch.testing.assert_close(p, -g)
+    opt.set_lr(0.5)
+    assert opt.get_lr() == 0.5 == opt.get_learning_rate()
+
+
+def test_zero_gradients_clears_the_store():
+    m = _mlp(1)
+    opt = dl.SGD(0.1)
+    m.train_step(torch.randn(4, 6), torch.tensor([0, 1, 2, 0], dtype=torch.int32), dl.CrossEntropyLoss(), opt)
+    assert m.store.grad.abs().sum() > 0
+    opt.zero_gradients()
+    assert m.store.grad.abs().sum() == 0
+
+
+@pytest.mark.parametrize("fmt", [SerializationFormat.DLVK_BINARY, SerializationFormat.DLVK_JSON,
+                                 SerializationFormat.NUMPY_NPZ])
+def test_serializer_save_and_load_weights(tmp_path, fmt):
+    src, dst = _mlp(2), _mlp(3)
+    assert not torch.equal(src.store.master, dst.store.master)
+    path = str(tmp_path / "w.bin")
+    assert ModelSerializer.save_weights(src, path, fmt)
+    assert ModelSerializer.load_weights(dst, path, fmt)
+    assert torch.equal(src.store.master, dst.store.master)
+    x = torch.randn(3, 6)
+    assert torch.equal(src.forward(x), dst.forward(x))
+
+
+def test_serializer_save_and_load_model(tmp_path):
+    src = _mlp(4)
+    x = torch.randn(3, 6)
+    for fmt, name in ((SerializationFormat.DLVK_BINARY, "m.dlvk"), (SerializationFormat.DLVK_JSON, "m.json")):
+        path = str(tmp_path / name)
+        assert ModelSerializer.save_model(src, path, fmt)
+        back = ModelSerializer.load_model(path, fmt, device="cpu")
+        assert torch.equal(back.forward(x), src.forward(x))
+
+
+def test_export_to_numpy_and_onnx_round_trip(tmp_path):
+    import numpy as np
+
+    m = _mlp(5)
+    npz = str(tmp_path / "w.npz")
+    assert ModelSerializer.export_to_numpy(m, npz)
+    with np.load(npz) as z:
+        names = [n for n, _ in m.state_tensors()]
+        assert sorted(z.files) == sorted(names)
+        for n, t in m.state_tensors():
+            assert np.array_equal(z[n], t.numpy())
+    onnx = str(tmp_path / "m.onnx")
+    assert ModelSerializer.export_to_onnx(m, onnx, [[1, 6]])
+    back = ModelOptimizer.import_from_onnx(onnx, device="cpu")
+    x = torch.randn(2, 6)
+    torch.testing.assert_close(back.forward(x), m.forward(x), rtol=0, atol=0)
+
+
+def test_persistence_factory(tmp_path):
+    m = _mlp(6)
+    cb = persistence_factory.create_checkpoint_callback(m, str(tmp_path / "ck"), "net")
+    assert isinstance(cb, ModelCheckpointCallback)
+    assert cb.get_checkpoint_manager().model_name == "net"
+    vs = persistence_factory.create_versioning_system(str(tmp_path / "exp"))
+    assert isinstance(vs, ModelVersioning)
+
+
+def test_loss_ops_gpu_entry_points_match_torch():
+    torch.manual_seed(1)
+    ops = dl.LossOpsGPU()
+    assert ops.initialize()
+    p = torch.rand(8, 5) * 0.98 + 0.01
+    t = torch.rand(8, 5)
+    torch.testing.assert_close(ops.mse_forward(p, t), F.mse_loss(p, t), rtol=1e-5, atol=1e-7)
+    torch.testing.assert_close(ops.mse_backward(p, t), 2 * (p - t) / p.numel(), rtol=1e-5, atol=1e-7)
+    probs = torch.softmax(torch.randn(8, 5), -1)
+    onehot = F.one_hot(torch.randint(0, 5, (8,)), 5).float()
+    torch.testing.assert_close(ops.cross_entropy_forward(probs, onehot),
+                               -(onehot * torch.log(probs + 1e-8)).sum() / 8, rtol=1e-5, atol=1e-7)
+    torch.testing.assert_close(ops.cross_entropy_backward(probs, onehot), -onehot / (probs + 1e-8) / 8,
+                               rtol=1e-5, atol=1e-7)
+    tb = (torch.rand(8, 5) > 0.5).float()
+    pe = torch.tensor([[0.0, 1e-4, 0.5, 1.0 - 1e-4, 1.0]])
+    te = torch.tensor([[0.0, 1.0, 1.0, 0.0, 1.0]])
+    for pp, tt in ((p, tb), (pe, te)):
+        for eps in (1e-7, 1e-3):
+            pc = pp.clamp(eps, 1 - eps)
+            torch.testing.assert_close(ops.binary_cross_entropy_forward(pp, tt, eps),
+                                       F.binary_cross_entropy(pc, tt), rtol=1e-4, atol=1e-6)
+            torch.testing.assert_close(ops.binary_cross_entropy_backward(pp, tt, eps),
+                                       (pc - tt) / (pc * (1 - pc)) / pp.numel(), rtol=1e-4, atol=1e-6)
+    with pytest.raises(ValueError):
+        ops.binary_cross_entropy_forward(p, tb, 1e-9)
