@@ -7,12 +7,17 @@ Implemented here:
   config's defaults), dynamic symmetric int8 activations per row, int32
   accumulation on the tensor cores (tcgen05 kind::i8) and an fp32
   dequantisation + bias + ReLU epilogue;
-* prune_model: global or per-layer magnitude pruning (masks kept so the
-  sparsity survives further training steps);
+* prune_model: the reference's four PruningStrategy values
+  (model_optimizer.h:30-35): magnitude (global or per layer), structured
+  (whole output neurons / channels by L2 norm), gradual (cubic sparsity
+  schedule, prune_step) and lottery ticket (magnitude masks, survivors
+  rewound to the remembered initial weights); masks are kept so the
+  sparsity survives further training steps;
 * distill_model: soft-target training of a student against a teacher;
 * optimize_for_inference: evaluation mode + batch-norm folding is left to the
   layers; returns the model ready for a captured graph;
-* benchmark_model: device-timed latency / throughput with CUDA events.
+* benchmark_model: device-timed latency / throughput with CUDA events, per
+  batch size when `batch_sizes` is given (BenchmarkResults).
 """
 from __future__ import annotations
 
@@ -46,12 +51,43 @@ class QuantizationConfig:
     calibration_data: Optional[torch.Tensor] = None
 
 
+class PruningStrategy(enum.Enum):
+    MAGNITUDE = 0
+    STRUCTURED = 1
+    GRADUAL = 2
+    LOTTERY_TICKET = 3
+
+
 @dataclass
 class PruningConfig:
+    """Fields of include/dlvk/optimization/model_optimizer.h:51-58.
+    `sparsity` is the reference's sparsity_ratio; `structured=True` selects
+    PruningStrategy.STRUCTURED.  `pruned_layers` / `skip_layers` name layers
+    by index ("3" or "layers.3") or type name ("Dense"); an empty
+    `pruned_layers` means every layer with a weight matrix or filter bank."""
+
     sparsity: float = 0.5
     structured: bool = False
     global_pruning: bool = True
     fine_tune_epochs: int = 0
+    strategy: PruningStrategy = PruningStrategy.MAGNITUDE
+    pruned_layers: List[str] = field(default_factory=list)
+    skip_layers: List[str] = field(default_factory=list)
+    gradual_pruning: bool = False
+    pruning_frequency: int = 100
+
+
+@dataclass
+class BenchmarkResults:
+    """model_optimizer.h:173-178.  average_gpu_utilization is the device-busy
+    share (CUDA-event time over host wall time) of the timed loop, in
+    percent; 0 on CPU.  peak_memory_usage is the caching allocator's peak
+    in bytes during the runs (0 on CPU)."""
+
+    latency_per_batch_size: dict = field(default_factory=dict)     # batch -> ms
+    throughput_per_batch_size: dict = field(default_factory=dict)  # batch -> samples/s
+    peak_memory_usage: int = 0
+    average_gpu_utilization: float = 0.0
 
 
 @dataclass
@@ -194,6 +230,7 @@ class ModelOptimizer:
         self.model = model
         self.stats = OptimizationStats()
         self._masks = {}
+        self._initial = None
 
     # ------------------------------------------------------------ quantisation
     def quantize_model(self, model: Optional[Sequential] = None, config: QuantizationConfig = None):
@@ -235,36 +272,125 @@ class ModelOptimizer:
         return qm
 
     # ------------------------------------------------------------ pruning
-    def prune_model(self, model: Optional[Sequential] = None, config: PruningConfig = None) -> float:
-        """Magnitude pruning of weight matrices; returns the achieved sparsity."""
+    @staticmethod
+    def _selected(i: int, layer, config: PruningConfig) -> bool:
+        names = {str(i), f"layers.{i}", layer.type_name.lower()}
+        if any(n.lower() in names for n in config.skip_layers):
+            return False
+        return not config.pruned_layers or any(n.lower() in names for n in config.pruned_layers)
+
+    def _prunable(self, model: Sequential, config: PruningConfig):
+        """(weight, bias) parameter pairs of the selected layers: every
+        parameter with two or more dimensions, with its layer's 1-D bias
+        when the layer has exactly one weight (Dense, Conv2D)."""
+        out = []
+        for i, layer in enumerate(model.layers()):
+            if not self._selected(i, layer, config):
+                continue
+            ps = layer.parameters()
+            ws = [p for p in ps if len(p.shape) >= 2]
+            bias = getattr(layer, "bias", None) if len(ws) == 1 else None
+            out.extend((w, bias if isinstance(bias, type(w)) else None) for w in ws)
+        return out
+
+    @staticmethod
+    def _kth(a: torch.Tensor, frac: float) -> torch.Tensor:
+        """Threshold below or at which a fraction `frac` of `a` lies."""
+        k = int(frac * a.numel())
+        return a.kthvalue(k).values if k > 0 else a.min() - 1
+
+    def remember_initial_weights(self, model: Sequential) -> None:
+        """Snapshot the weights a lottery-ticket pruning rewinds to (call
+        right after building the model, before training)."""
+        model.build()
+        self._initial = {id(p): p.master.detach().clone() for p in model.parameters()}
+
+    def prune_model(self, model: Optional[Sequential] = None, config: PruningConfig = None,
+                    sparsity: Optional[float] = None) -> float:
+        """Prunes the selected layers' weights to `sparsity` (default
+        config.sparsity) and returns the achieved fraction of zeros over the
+        pruned tensors.
+
+        MAGNITUDE / GRADUAL: the smallest |w| are zeroed, over all selected
+        tensors at once (global_pruning) or per tensor.  A one-shot call
+        with GRADUAL prunes to the full target; prune_step follows the
+        schedule.
+        STRUCTURED: per layer, the output units (Dense columns of W [in, out],
+        Conv2D filters of W [out, in, k, k]) with the smallest L2 norm are
+        zeroed together with their bias; at least one unit stays.
+        LOTTERY_TICKET: magnitude masks as MAGNITUDE, then every weight is
+        rewound to its remembered initial value (remember_initial_weights)
+        and the mask applied."""
         model = model or self.model
         config = config or PruningConfig()
+        target = float(config.sparsity if sparsity is None else sparsity)
+        if not 0.0 <= target < 1.0:
+            raise ValueError(f"sparsity must be in [0, 1), got {target}")
+        strategy = PruningStrategy.STRUCTURED if config.structured else config.strategy
+        if strategy is PruningStrategy.LOTTERY_TICKET and self._initial is None:
+            raise ValueError("lottery-ticket pruning needs remember_initial_weights(model) before training")
         model.build()
-        weights = [p for p in model.parameters() if len(p.shape) >= 2]
-        if not weights:
+        pairs = self._prunable(model, config)
+        if not pairs:
             return 0.0
-        if config.global_pruning:
-            allw = torch.cat([p.master.detach().abs().reshape(-1) for p in weights])
-            k = int(config.sparsity * allw.numel())
-            thr = allw.kthvalue(max(k, 1)).values if k > 0 else allw.min() - 1
-            thrs = [thr] * len(weights)
+        masks = {}
+        if strategy is PruningStrategy.STRUCTURED:
+            for w, b in pairs:
+                wt = w.master.detach()
+                unit_norm = wt.norm(dim=0) if wt.dim() == 2 else wt.reshape(wt.shape[0], -1).norm(dim=1)
+                drop = min(int(target * unit_norm.numel()), unit_norm.numel() - 1)
+                keep = torch.ones_like(unit_norm, dtype=torch.bool)
+                if drop > 0:
+                    keep[unit_norm.argsort()[:drop]] = False
+                masks[id(w)] = (keep.reshape(1, -1) if wt.dim() == 2 else
+                                keep.reshape(-1, *([1] * (wt.dim() - 1)))).expand_as(wt).clone()
+                if b is not None:
+                    masks[id(b)] = keep.clone()
+        elif config.global_pruning:
+            allw = torch.cat([w.master.detach().abs().reshape(-1) for w, _ in pairs])
+            thr = self._kth(allw, target)
+            for w, _ in pairs:
+                masks[id(w)] = w.master.detach().abs() > thr
         else:
-            thrs = []
-            for p in weights:
-                a = p.master.detach().abs().reshape(-1)
-                k = int(config.sparsity * a.numel())
-                thrs.append(a.kthvalue(max(k, 1)).values if k > 0 else a.min() - 1)
-        zeros = 0
-        total = 0
-        for p, t in zip(weights, thrs):
-            mask = p.master.detach().abs() > t
+            for w, _ in pairs:
+                masks[id(w)] = w.master.detach().abs() > self._kth(w.master.detach().abs().reshape(-1), target)
+        by_id = {id(p): p for w, b in pairs for p in (w, b) if p is not None}
+        for pid, mask in masks.items():
+            p = by_id[pid]
+            if strategy is PruningStrategy.LOTTERY_TICKET:
+                p.master.copy_(self._initial[pid].to(p.master.device))
             p.master.mul_(mask)
-            self._masks[id(p)] = mask
-            zeros += int((~mask).sum())
-            total += mask.numel()
+            self._masks[pid] = mask
+        if strategy is PruningStrategy.LOTTERY_TICKET:
+            # The rest of the model (biases, norms) rewinds too.
+            for p in model.parameters():
+                if id(p) not in masks and id(p) in self._initial:
+                    p.master.copy_(self._initial[id(p)].to(p.master.device))
         model.store.sync_value()
+        zeros = sum(int((~masks[id(w)]).sum()) for w, _ in pairs)
+        total = sum(w.numel for w, _ in pairs)
         self.stats.sparsity = zeros / max(total, 1)
         return self.stats.sparsity
+
+    @staticmethod
+    def gradual_sparsity(step: int, total_steps: int, final_sparsity: float) -> float:
+        """Cubic schedule of Zhu and Gupta, "To prune, or not to prune"
+        (2017): s_t = s_f (1 - (1 - t / T)^3), reaching s_f at t = T."""
+        f = min(max(step / max(total_steps, 1), 0.0), 1.0)
+        return final_sparsity * (1.0 - (1.0 - f) ** 3)
+
+    def prune_step(self, model: Sequential, step: int, total_steps: int, config: PruningConfig = None) -> float:
+        """Gradual pruning inside a training loop: every
+        `config.pruning_frequency` steps the selected weights are pruned to
+        the schedule's sparsity; on the other steps the masks are
+        re-applied.  Returns the sparsity target in force."""
+        config = config or PruningConfig(strategy=PruningStrategy.GRADUAL, gradual_pruning=True)
+        target = self.gradual_sparsity(step, total_steps, config.sparsity)
+        if step % max(config.pruning_frequency, 1) == 0 or step >= total_steps:
+            self.prune_model(model, config, sparsity=target)
+        else:
+            self.apply_masks(model)
+        return target
 
     def apply_masks(self, model: Sequential) -> None:
         """Re-apply pruning masks (call after optimizer steps while fine-tuning)."""
@@ -312,30 +438,60 @@ class ModelOptimizer:
         return model
 
     # ------------------------------------------------------------ benchmarking
-    def benchmark_model(self, model, input_shape, iterations: int = 50, warmup: int = 5, device=None) -> dict:
-        """Device-timed latency (CUDA events) and throughput of model.forward."""
+    def benchmark_model(self, model, input_shape, iterations: int = 50, warmup: int = 5, device=None,
+                        batch_sizes=None):
+        """Latency and throughput of model.forward, timed with CUDA events on
+        the GPU (wall clock on CPU).
+
+        Without `batch_sizes`, `input_shape` includes the batch dimension and
+        a dict {latency_ms, throughput_samples_per_s, iterations} is
+        returned.  With `batch_sizes` (the reference's form,
+        model_optimizer.h:166-185), `input_shape` is one sample's shape and a
+        BenchmarkResults with one entry per batch size is returned."""
         dev = torch.device(device) if device else (model.dev.device if hasattr(model, "dev") else
                                                    torch.device("cuda" if torch.cuda.is_available() else "cpu"))
-        x = torch.rand(*input_shape, device=dev)
         if hasattr(model, "set_training"):
             model.set_training(False)
+        if batch_sizes is None:
+            ms, _ = self._time_forward(model, torch.rand(*input_shape, device=dev), iterations, warmup)
+            return {"latency_ms": ms, "throughput_samples_per_s": input_shape[0] / (ms / 1e3),
+                    "iterations": iterations}
+        res = BenchmarkResults()
+        if dev.type == "cuda":
+            torch.cuda.reset_peak_memory_stats(dev)
+        busy = wall = 0.0
+        for b in batch_sizes:
+            ms, wall_ms = self._time_forward(model, torch.rand(int(b), *input_shape, device=dev), iterations, warmup)
+            res.latency_per_batch_size[int(b)] = ms
+            res.throughput_per_batch_size[int(b)] = int(b) / (ms / 1e3)
+            busy += ms * iterations
+            wall += wall_ms
+        if dev.type == "cuda":
+            res.peak_memory_usage = int(torch.cuda.max_memory_allocated(dev))
+            res.average_gpu_utilization = 100.0 * min(busy / max(wall, 1e-9), 1.0)
+        return res
+
+    @staticmethod
+    def _time_forward(model, x, iterations: int, warmup: int):
+        """(ms per forward, wall ms of the whole timed loop)."""
         for _ in range(warmup):
             model.forward(x)
-        if dev.type == "cuda":
-            torch.cuda.synchronize(dev)
+        if x.is_cuda:
+            torch.cuda.synchronize(x.device)
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0 = time.perf_counter()
             s.record()
             for _ in range(iterations):
                 model.forward(x)
             e.record()
             e.synchronize()
-            ms = s.elapsed_time(e) / iterations
-        else:
-            t0 = time.perf_counter()
-            for _ in range(iterations):
-                model.forward(x)
-            ms = (time.perf_counter() - t0) * 1e3 / iterations
-        return {"latency_ms": ms, "throughput_samples_per_s": input_shape[0] / (ms / 1e3), "iterations": iterations}
+            wall = (time.perf_counter() - t0) * 1e3
+            return s.elapsed_time(e) / iterations, wall
+        t0 = time.perf_counter()
+        for _ in range(iterations):
+            model.forward(x)
+        wall = (time.perf_counter() - t0) * 1e3
+        return wall / iterations, wall
 
 
 # ------------------------------------------------------------ architecture search

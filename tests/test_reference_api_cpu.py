@@ -1,8 +1,9 @@
 """CPU tests of the reference's public accessor and helper spellings: layer
 get_/set_ accessors and output shapes, optimizer clipping setters,
 update_parameter and zero_gradients, ModelSerializer's static entry points,
-the persistence factory functions, ONNX import and LossOpsGPU.  Each result
-is checked against plain PyTorch math or a round trip."""
+the persistence factory functions, ONNX import, LossOpsGPU, the four
+pruning strategies and the per-batch-size benchmark.  Each result is checked
+against plain PyTorch math or a round trip."""
 import pytest
 import torch
 import torch.nn.functional as F
@@ -247,3 +248,111 @@ def test_loss_ops_gpu_entry_points_match_torch():
                                        (pc - tt) / (pc * (1 - pc)) / pp.numel(), rtol=1e-4, atol=1e-6)
     with pytest.raises(ValueError):
         ops.binary_cross_entropy_forward(p, tb, 1e-9)
+
+
+# ---------------------------------------------------------------- pruning strategies
+from dlvk_b200.optimization import BenchmarkResults, PruningConfig, PruningStrategy  # noqa: E402
+
+
+def _prune_net(seed=0):
+    m = dl.Sequential("cpu", seed=seed)
+    m.add_conv2d(1, 8, 3, 1, 1)
+    m.add_relu()
+    m.add_flatten()
+    m.add_dense(8 * 6 * 6, 16)
+    m.add_relu()
+    m.add_dense(16, 4)
+    return m.build()
+
+
+def test_magnitude_pruning_global_and_per_layer():
+    for global_pruning in (True, False):
+        m = _prune_net()
+        ws = [p.master.clone() for p in m.parameters() if len(p.shape) >= 2]
+        opt = ModelOptimizer()
+        got = opt.prune_model(m, PruningConfig(sparsity=0.5, global_pruning=global_pruning))
+        pruned = [p.master for p in m.parameters() if len(p.shape) >= 2]
+        total = sum(w.numel() for w in ws)
+        zeros = sum(int((w == 0).sum()) for w in pruned)
+        assert got == pytest.approx(zeros / total)
+        assert 0.49 <= got <= 0.51
+        if global_pruning:
+            thr = torch.cat([w.abs().reshape(-1) for w in ws]).kthvalue(int(0.5 * total)).values
+            for w0, w in zip(ws, pruned):
+                assert torch.equal(w, w0 * (w0.abs() > thr))
+        else:
+            for w0, w in zip(ws, pruned):
+                assert 0.45 <= float((w == 0).float().mean()) <= 0.55
+        # masks hold across a training step
+        m.train_step(torch.randn(4, 1, 6, 6), torch.tensor([0, 1, 2, 3], dtype=torch.int32),
+                     dl.CrossEntropyLoss(), dl.SGD(0.1))
+        opt.apply_masks(m)
+        assert sum(int((p.master == 0).sum()) for p in m.parameters() if len(p.shape) >= 2) >= zeros
+
+
+def test_structured_pruning_zeroes_whole_units():
+    m = _prune_net(1)
+    conv, d1 = m[0], m[3]
+    cn = conv.get_weights().reshape(8, -1).norm(dim=1)
+    dn = d1.get_weights().norm(dim=0)
+    conv.set_bias(torch.ones(8))
+    d1.set_bias(torch.ones(16))
+    ModelOptimizer().prune_model(m, PruningConfig(sparsity=0.5, strategy=PruningStrategy.STRUCTURED,
+                                                   pruned_layers=["0", "Dense"], skip_layers=["layers.5"]))
+    dead_c = conv.get_weights().reshape(8, -1).abs().sum(1) == 0
+    assert torch.equal(dead_c, torch.isin(torch.arange(8), cn.argsort()[:4]))
+    assert torch.equal(conv.get_bias() == 0, dead_c)
+    dead_d = d1.get_weights().abs().sum(0) == 0
+    assert torch.equal(dead_d, torch.isin(torch.arange(16), dn.argsort()[:8]))
+    assert torch.equal(d1.get_bias() == 0, dead_d)
+    assert int((m[5].get_weights() == 0).sum()) == 0  # skipped layer untouched
+
+
+def test_gradual_schedule_and_prune_step():
+    assert ModelOptimizer.gradual_sparsity(0, 100, 0.8) == 0.0
+    assert ModelOptimizer.gradual_sparsity(100, 100, 0.8) == pytest.approx(0.8)
+    assert ModelOptimizer.gradual_sparsity(50, 100, 0.8) == pytest.approx(0.8 * (1 - 0.5 ** 3))
+    m = _prune_net(2)
+    opt = ModelOptimizer()
+    cfg = PruningConfig(sparsity=0.6, strategy=PruningStrategy.GRADUAL, gradual_pruning=True, pruning_frequency=5)
+    last = -1.0
+    for step in range(0, 21):
+        opt.prune_step(m, step, 20, cfg)
+        s = opt.stats.sparsity
+        assert s >= last - 1e-9
+        last = s
+    assert last == pytest.approx(0.6, abs=0.01)
+
+
+def test_lottery_ticket_rewinds_survivors():
+    m = _prune_net(3)
+    opt = ModelOptimizer()
+    with pytest.raises(ValueError):
+        opt.prune_model(m, PruningConfig(strategy=PruningStrategy.LOTTERY_TICKET))
+    opt.remember_initial_weights(m)
+    init = {id(p): p.master.clone() for p in m.parameters()}
+    sgd = dl.SGD(0.5)
+    for _ in range(3):
+        m.train_step(torch.randn(8, 1, 6, 6), torch.randint(0, 4, (8,), dtype=torch.int32),
+                     dl.CrossEntropyLoss(), sgd)
+    trained = {id(p): p.master.clone() for p in m.parameters()}
+    opt.prune_model(m, PruningConfig(sparsity=0.5, strategy=PruningStrategy.LOTTERY_TICKET))
+    for p in m.parameters():
+        if len(p.shape) >= 2:
+            keep = trained[id(p)].abs() > 0
+            alive = p.master != 0
+            assert torch.equal(p.master[alive], init[id(p)][alive])
+            assert int(alive.sum()) <= int(keep.sum())
+        else:
+            assert torch.equal(p.master, init[id(p)])
+
+
+def test_benchmark_model_per_batch_size():
+    m = _mlp(7)
+    r = ModelOptimizer().benchmark_model(m, [6], iterations=3, warmup=1, device="cpu", batch_sizes=[1, 4])
+    assert isinstance(r, BenchmarkResults)
+    assert sorted(r.latency_per_batch_size) == [1, 4]
+    for b, ms in r.latency_per_batch_size.items():
+        assert ms > 0 and r.throughput_per_batch_size[b] == pytest.approx(b / (ms / 1e3))
+    d = ModelOptimizer().benchmark_model(m, [4, 6], iterations=2, warmup=1, device="cpu")
+    assert d["latency_ms"] > 0
