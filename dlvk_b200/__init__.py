@@ -27,7 +27,7 @@ from .losses import (LossFunction, CrossEntropyLoss, MeanSquaredError, BinaryCro
 # runtime is CUDA.
 VulkanDevice = CudaDevice
 
-from .models.layers import (RNNLayer, LSTMLayer, GRULayer, BidirectionalRNN, BiLSTM, BiGRU, BiRNN)
+from .models.layers import (RNNLayer, LSTMLayer, GRULayer, BidirectionalRNN, BiLSTM, BiGRU, BiRNN, ConvLayer)
 from .models.builder import model_from_architecture, load_model_file
 from .training import (TrainStep, ModelTrainer, Trainer, create_trainer, TrainingMetrics, TrainingCallback,
                        ProgressCallback, ModelCheckpoint, EarlyStopping, EarlyStoppingCallback, ReduceLROnPlateau,

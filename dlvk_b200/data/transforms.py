@@ -663,3 +663,8 @@ class PreprocessingPipelineBuilder:
 
     def build(self) -> PreprocessingPipeline:
         return self.p
+
+
+# The reference's factory::SimpleBuilder (include/dlvk/data/transforms_clean.h:172-184):
+# resize / random_horizontal_flip / random_crop / normalize / build.
+SimpleBuilder = PreprocessingPipelineBuilder

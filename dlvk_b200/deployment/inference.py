@@ -55,6 +55,9 @@ class Config:
     serving: ServingConfig = field(default_factory=ServingConfig)
 
 
+Config.Serving = ServingConfig  # the reference's nested Config::Serving (inference_deployment.h:21-27)
+
+
 class _Request:
     __slots__ = ("x", "n", "future", "callback", "t0")
 

@@ -893,3 +893,14 @@ BatchNorm1DLayerAdapter = BatchNorm1DLayer
 BatchNorm2DLayerAdapter = BatchNorm2DLayer
 DropoutLayerAdapter = DropoutLayer
 Layer = ModernLayer
+
+
+class ConvLayer(Conv2DLayer):
+    """The legacy layer of include/dlvk/layers/layer.h:22-38 (declared there,
+    never defined): a stride-1, unpadded Conv2D.  The reference's trailing
+    device argument is accepted and used for placement."""
+
+    def __init__(self, in_channels: int, out_channels: int, kernel_size: int, device=None):
+        super().__init__(in_channels, out_channels, kernel_size, 1, 0)
+        if device is not None:
+            self.to(getattr(device, "device", device))

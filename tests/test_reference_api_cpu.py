@@ -356,3 +356,18 @@ def test_benchmark_model_per_batch_size():
         assert ms > 0 and r.throughput_per_batch_size[b] == pytest.approx(b / (ms / 1e3))
     d = ModelOptimizer().benchmark_model(m, [4, 6], iterations=2, warmup=1, device="cpu")
     assert d["latency_ms"] > 0
+
+
+def test_legacy_names():
+    from dlvk_b200.data.transforms import PreprocessingPipeline, SimpleBuilder
+    from dlvk_b200.deployment.inference import Config
+
+    conv = dl.ConvLayer(2, 3, 3)
+    x = torch.randn(1, 2, 5, 5)
+    assert list(conv.forward(x).shape) == [1, 3, 3, 3]
+    torch.testing.assert_close(conv.forward(x), F.conv2d(x, conv.get_weights(), conv.get_bias()),
+                               rtol=1e-5, atol=1e-5)
+    p = SimpleBuilder().resize(8, 8).random_horizontal_flip(0.5).normalize([0.5], [0.5]).build()
+    assert isinstance(p, PreprocessingPipeline)
+    assert tuple(p.process(torch.rand(2, 1, 4, 4)).shape) == (2, 1, 8, 8)
+    assert Config.Serving().timeout_ms == Config().serving.timeout_ms == 1000
