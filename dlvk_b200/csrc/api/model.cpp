@@ -55,6 +55,19 @@ void Sequential::add(std::unique_ptr<ModernLayer> layer) {
   plan_.clear();
 }
 
+std::unique_ptr<Sequential> Sequential::clone() const {
+  auto c = std::make_unique<Sequential>(device_, seed_);
+  for (const auto& l : layers_) {
+    if (const auto* d = dynamic_cast<const DropoutLayer*>(l.get()))
+      c->add(std::make_unique<DropoutLayer>(d->rate, ++c->dropout_sites_, &c->seed_, &c->step_));
+    else
+      c->add(l->clone());
+  }
+  c->step_ = step_;
+  c->set_training(training_);
+  return c;
+}
+
 void Sequential::add_dense(size_t in, size_t out, bool use_bias) {
   add(std::make_unique<DenseLayer>(in, out, use_bias, gen_));
 }

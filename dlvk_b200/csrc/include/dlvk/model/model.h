@@ -48,6 +48,12 @@ class Sequential : public Model {
   Sequential(const Sequential&) = delete;
   Sequential& operator=(const Sequential&) = delete;
 
+  // Deep copy (the reference's Sequential::clone, model.h:39-46): same
+  // device, seed, step count and training flag, copies of every layer's
+  // weights and buffers; dropout layers draw from the copy's own stream
+  // state, so the copy's next masks equal the original's.
+  std::unique_ptr<Sequential> clone() const;
+
   void add(std::unique_ptr<ModernLayer> layer);
   void add_layer(std::unique_ptr<ModernLayer> layer) { add(std::move(layer)); }
   void add_dense(size_t input_size, size_t output_size, bool use_bias = true);

@@ -161,8 +161,14 @@ int main(int argc, char** argv) {
     dense->get_weights().data().zero_();
     dense->get_bias().data().fill_(2.f);
     m4.set_training(false);
-    auto y4 = m4.forward(dlvk::Tensor(at::rand({2, 1, 8, 8}, g))).to_vector();
+    at::Tensor x4 = at::rand({2, 1, 8, 8}, g);
+    auto y4 = m4.forward(dlvk::Tensor(x4)).to_vector();
     if (y4 != std::vector<float>(6, 2.f)) return fail("Dense get_weights is not a view");
+    // clone(): an independent deep copy
+    auto c4 = m4.clone();
+    dense->get_bias().data().fill_(3.f);
+    if (c4->forward(dlvk::Tensor(x4)).to_vector() != std::vector<float>(6, 2.f)) return fail("clone shares weights");
+    if (c4->size() != m4.size() || c4->parameter_count() != m4.parameter_count()) return fail("clone layers");
     auto* relu = dynamic_cast<dlvk::ActivationLayer*>(&model[1]);
     if (!relu || relu->get_activation_type() != dlvk::ActivationType::ReLU) return fail("get_activation_type");
 
