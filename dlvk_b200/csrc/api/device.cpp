@@ -46,6 +46,43 @@ std::string CudaDevice::name() const {
   return p.name;
 }
 
+namespace {
+bool props(int index, cudaDeviceProp* p) {
+  if (index < 0) return false;
+  if (cudaGetDeviceProperties(p, index) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return true;
+}
+}  // namespace
+
+std::string CudaDevice::get_device_type_string() const {
+  cudaDeviceProp p;
+  if (!props(index_, &p)) return "cpu";
+  return "CUDA GPU sm_" + std::to_string(p.major) + std::to_string(p.minor) + ", " +
+         std::to_string(p.multiProcessorCount) + " SMs";
+}
+
+std::string CudaDevice::get_vulkan_version_string() const {
+  int v = 0;
+  if (cudaRuntimeGetVersion(&v) != cudaSuccess) {
+    cudaGetLastError();
+    return "CUDA";
+  }
+  return "CUDA " + std::to_string(v / 1000) + "." + std::to_string((v % 1000) / 10);
+}
+
+uint32_t CudaDevice::get_max_workgroup_size() const {
+  cudaDeviceProp p;
+  return props(index_, &p) ? (uint32_t)p.maxThreadsPerBlock : 0u;
+}
+
+uint64_t CudaDevice::get_total_device_memory() const {
+  cudaDeviceProp p;
+  return props(index_, &p) ? (uint64_t)p.totalGlobalMem : 0u;
+}
+
 std::shared_ptr<CudaDevice> CudaDevice::cpu() {
   static std::shared_ptr<CudaDevice> dev = [] {
     auto d = std::make_shared<CudaDevice>(-1);

@@ -9,6 +9,7 @@
 #pragma once
 #include <c10/core/Device.h>
 
+#include <cstdint>
 #include <memory>
 #include <string>
 
@@ -28,6 +29,21 @@ class CudaDevice {
   int index() const { return index_; }
   c10::Device device() const;
   std::string name() const;
+
+  // Device-info getters of the reference's vulkan_device.h:64-70, answered
+  // from cudaGetDeviceProperties (the CPU device answers "cpu" / zeros):
+  // get_device_type_string: "CUDA GPU sm_<major><minor>, <n> SMs" or "cpu";
+  // get_vulkan_version_string: the CUDA runtime version ("CUDA 12.9");
+  // get_max_workgroup_size: max threads per block;
+  // get_max_memory_allocation / get_total_device_memory: total global memory
+  // in bytes; get_memory_heap_count: 1 (one global memory).
+  std::string get_device_name() const { return name(); }
+  std::string get_device_type_string() const;
+  std::string get_vulkan_version_string() const;
+  uint32_t get_max_workgroup_size() const;
+  uint64_t get_max_memory_allocation() const { return get_total_device_memory(); }
+  uint32_t get_memory_heap_count() const { return is_cuda() ? 1u : 0u; }
+  uint64_t get_total_device_memory() const;
 
   // Shared CPU device (for tests and CPU-only programs).
   static std::shared_ptr<CudaDevice> cpu();

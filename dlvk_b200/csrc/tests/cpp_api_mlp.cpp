@@ -37,6 +37,11 @@ int main(int argc, char** argv) {
   at::set_num_threads(1);
   auto device = mode == "cuda" ? std::make_shared<dlvk::CudaDevice>(0) : dlvk::CudaDevice::cpu();
   if (!device->initialize()) return fail("no CUDA device");
+  std::printf("device %s (%s, %s, %llu bytes)\n", device->get_device_name().c_str(),
+              device->get_device_type_string().c_str(), device->get_vulkan_version_string().c_str(),
+              (unsigned long long)device->get_total_device_memory());
+  if (device->is_cuda() && (device->get_max_workgroup_size() == 0 || device->get_total_device_memory() == 0))
+    return fail("device getters");
 
   // README example: batch-1 forward of a freshly built model.
   {

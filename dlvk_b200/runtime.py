@@ -80,6 +80,29 @@ class CudaDevice:
     def get_sm_count(self) -> int:
         return torch.cuda.get_device_properties(self.device).multi_processor_count if self.is_cuda else 0
 
+    def get_device_type_string(self) -> str:
+        if not self.is_cuda:
+            return "cpu"
+        pr = torch.cuda.get_device_properties(self.device)
+        return f"CUDA GPU sm_{pr.major}{pr.minor}, {pr.multi_processor_count} SMs"
+
+    def get_vulkan_version_string(self) -> str:
+        """The CUDA runtime version (the reference reported its Vulkan API version)."""
+        return f"CUDA {torch.version.cuda}" if self.is_cuda else "cpu"
+
+    def get_max_workgroup_size(self) -> int:
+        """Max threads per block (1024 on every GPU this library targets)."""
+        return 1024 if self.is_cuda else 0
+
+    def get_total_device_memory(self) -> int:
+        return int(torch.cuda.get_device_properties(self.device).total_memory) if self.is_cuda else 0
+
+    def get_max_memory_allocation(self) -> int:
+        return self.get_total_device_memory()
+
+    def get_memory_heap_count(self) -> int:
+        return 1 if self.is_cuda else 0
+
     def get_memory_info(self):
         """(free_bytes, total_bytes)."""
         if self.is_cuda:

@@ -371,3 +371,12 @@ def test_legacy_names():
     assert isinstance(p, PreprocessingPipeline)
     assert tuple(p.process(torch.rand(2, 1, 4, 4)).shape) == (2, 1, 8, 8)
     assert Config.Serving().timeout_ms == Config().serving.timeout_ms == 1000
+
+
+def test_device_getters_on_cpu():
+    from dlvk_b200.runtime import CudaDevice
+
+    d = CudaDevice("cpu")
+    assert d.get_device_name() == d.get_device_type_string() == "cpu"
+    assert d.get_total_device_memory() == d.get_max_memory_allocation() == 0
+    assert d.get_memory_heap_count() == 0 and d.get_max_workgroup_size() == 0
