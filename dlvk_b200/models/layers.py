@@ -238,6 +238,16 @@ class ModernLayer:
     def is_training(self) -> bool:
         return self.training
 
+    def update_weights(self, learning_rate: float) -> None:
+        """The legacy Layer::update_weights (reference src/layers/dense_layer.cpp:68):
+        one plain SGD step p -= learning_rate * grad on this layer's packed
+        parameters, through the optimizer kernel on a GPU."""
+        ps = [p for p in self.parameters() if p.store is not None]
+        if ps:
+            from ..optim import SGD
+
+            SGD(learning_rate).update_parameters(ps)
+
     def _set_tensor(self, dst: torch.Tensor, src, what: str) -> None:
         """Copy `src` (a tensor or array of dst's element count) into a
         parameter master or a buffer in place, so a packed store keeps its

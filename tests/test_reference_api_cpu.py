@@ -380,3 +380,15 @@ def test_device_getters_on_cpu():
     assert d.get_device_name() == d.get_device_type_string() == "cpu"
     assert d.get_total_device_memory() == d.get_max_memory_allocation() == 0
     assert d.get_memory_heap_count() == 0 and d.get_max_workgroup_size() == 0
+
+
+def test_legacy_update_weights_is_plain_sgd():
+    m = _mlp(8)
+    m.train_step(torch.randn(4, 6), torch.tensor([0, 1, 2, 0], dtype=torch.int32), dl.CrossEntropyLoss(),
+                 dl.SGD(0.0))
+    d = m[0]
+    w0, g = d.get_weights().clone(), d.weight.grad.clone()
+    other = m[2].get_weights().clone()
+    d.update_weights(0.5)
+    torch.testing.assert_close(d.get_weights(), w0 - 0.5 * g)
+    assert torch.equal(m[2].get_weights(), other)  # only this layer moves
