@@ -40,7 +40,7 @@ import time
 
 import torch
 
-BASELINE_MS_BATCH1_FWD = 3.772  # published MLP forward (batch 1) of the reference
+PUBLISHED_MS_BATCH1_FWD = 3.772  # published MLP forward (batch 1) of the reference
 
 REFERENCE_UNAVAILABLE = (
     "reference is a C++/Vulkan-compute project with no Python package: offline pip install fails "
@@ -362,8 +362,8 @@ def run_mlp_fwd_b1(args, rank, local, world):
     return {"metric": "MLP 784-128-10 softmax forward latency, batch 1 (device-timed, max/ranks)",
             "value": round(ms, 5), "unit": "ms", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms, 5), "higher_is_better": False, "scaling": "weak",
-            "vs_baseline": round(ms / BASELINE_MS_BATCH1_FWD, 5), "published_ms": BASELINE_MS_BATCH1_FWD,
-            "speedup_vs_published": round(BASELINE_MS_BATCH1_FWD / ms, 1),
+            "vs_baseline": round(ms / PUBLISHED_MS_BATCH1_FWD, 5), "published_ms": PUBLISHED_MS_BATCH1_FWD,
+            "speedup_vs_published": round(PUBLISHED_MS_BATCH1_FWD / ms, 1),
             "captured_graph_ms": round(gms, 5) if gms is not None else None,
             "dtype": "fp32", "data": "synthetic x ~ U[0,1) of shape [1, 784]; random-init weights (seed 0)",
             "config": {"model": "mlp 784-128-10 + softmax (reference README example)", "global_batch": world,
